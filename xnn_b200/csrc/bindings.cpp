@@ -1,0 +1,394 @@
+// Python bindings of the xnn_b200 native kernels (CUDA for sm_100a, C++/OpenMP on the CPU).
+// Every op checks shapes, dtypes and devices and launches on the current CUDA stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cmath>
+#include <vector>
+
+#include "neighbor_impl.h"
+
+// ---- CUDA launchers (defined in the .cu files) -------------------------------------------
+template <typename T>
+cudaError_t edge_geom_fwd(int64_t, int, const T*, int, const T*, T, T, int, T*, T*, cudaStream_t);
+template <typename T>
+cudaError_t edge_geom_bwd(int64_t, int, const T*, int, const T*, T, T, int, const T*, const T*, T*, cudaStream_t);
+template <typename T>
+cudaError_t edge_geom_jvp(int64_t, int, const T*, int, const T*, T, T, int, const T*, T*, T*, cudaStream_t);
+template <typename T>
+cudaError_t conv_gather(int, int, int, const int64_t*, const int*, const int64_t*, int, const T* const*,
+                        const T* const*, const T* const*, T*, cudaStream_t);
+template <typename T>
+cudaError_t conv_edge(int, int, int, const int64_t*, const int*, const int64_t*, const T*, int,
+                      const T* const*, const T* const*, int, const T* const*, const T* const*, T*, T*,
+                      cudaStream_t);
+template <typename T>
+cudaError_t conv_scatter(int, int, int, const int64_t*, const int64_t*, const int*, const T*, int,
+                         const T* const*, const T* const*, T*, cudaStream_t);
+template <typename T>
+cudaError_t symcon_fwd(int, int, int, int, const T*, const int64_t*, const T*, T*, cudaStream_t);
+template <typename T>
+cudaError_t symcon_bwd(int, int, int, int, const T*, const int64_t*, const T*, const T*, T*, T*, cudaStream_t);
+template <typename T>
+cudaError_t symcon_bwd2(int, int, int, int, const T*, const int64_t*, const T*, const T*, const T*,
+                        const T*, T*, T*, T*, cudaStream_t);
+int symcon_num_invariants(int lmax, int corr);
+cudaError_t nb_count_cuda(const NbParams& p, int64_t* counts, cudaStream_t s);
+cudaError_t nb_write_cuda(const NbParams& p, const int64_t* offsets, int64_t* src, int64_t* dst,
+                          int64_t* shifts, cudaStream_t s);
+
+namespace {
+
+#define XNN_CUDA_OK(expr)                                                               \
+  do {                                                                                  \
+    cudaError_t _e = (expr);                                                            \
+    TORCH_CHECK(_e == cudaSuccess, "xnn_b200 kernel launch failed: ", cudaGetErrorString(_e)); \
+  } while (0)
+
+void check_cuda(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+template <typename T>
+const T* ptr_or_null(const c10::optional<torch::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr<T>() : nullptr;
+}
+
+// ---- neighbour list ------------------------------------------------------------------
+std::vector<torch::Tensor> neighbor_list(torch::Tensor pos, torch::Tensor cell, std::vector<int64_t> reps,
+                                         std::vector<int64_t> pbc, double cutoff, bool self_interaction) {
+  TORCH_CHECK(pos.dim() == 2 && pos.size(1) == 3 && pos.scalar_type() == torch::kFloat64,
+              "pos must be (N, 3) float64");
+  pos = pos.contiguous();
+  const int64_t N = pos.size(0);
+  auto lopt = torch::TensorOptions().dtype(torch::kInt64).device(pos.device());
+  if (N == 0) {
+    auto z = torch::zeros({0}, lopt);
+    return {z, z.clone(), torch::zeros({0, 3}, lopt)};
+  }
+  const bool periodic = pbc[0] || pbc[1] || pbc[2];
+  torch::Tensor cellc = cell.to(torch::kCPU, torch::kFloat64).contiguous();
+  torch::Tensor p = pos;
+  double cm[9];
+  if (!periodic) {
+    // open boundaries: an orthorhombic box around the atoms
+    auto lo = std::get<0>(pos.min(0));
+    auto hi = std::get<0>(pos.max(0));
+    p = pos - lo;
+    auto ext = (hi - lo).to(torch::kCPU);
+    for (int a = 0; a < 9; ++a) cm[a] = 0.0;
+    for (int a = 0; a < 3; ++a) cm[4 * a] = std::max(ext[a].item<double>(), 1e-6) * (1.0 + 1e-9) + 1e-9;
+  } else {
+    for (int a = 0; a < 9; ++a) cm[a] = cellc.data_ptr<double>()[a];
+  }
+  // plane spacings and cell counts
+  double h[3];
+  {
+    auto c = torch::from_blob(cm, {3, 3}, torch::kFloat64).clone();
+    const double vol = std::abs(torch::det(c).item<double>());
+    for (int a = 0; a < 3; ++a) {
+      auto b = c[(a + 1) % 3];
+      auto d = c[(a + 2) % 3];
+      const double area = torch::linalg_cross(b, d).norm().item<double>();
+      h[a] = vol / area;
+    }
+  }
+  int64_t nc[3], k[3];
+  for (int a = 0; a < 3; ++a) {
+    nc[a] = std::max<int64_t>(1, (int64_t)std::floor(h[a] / cutoff));
+  }
+  // keep the grid no finer than about one cell per atom
+  while ((double)nc[0] * nc[1] * nc[2] > 2.0 * (double)N + 64.0) {
+    int amax = 0;
+    for (int a = 1; a < 3; ++a) if (nc[a] > nc[amax]) amax = a;
+    nc[amax] = std::max<int64_t>(1, nc[amax] / 2);
+  }
+  for (int a = 0; a < 3; ++a) {
+    k[a] = (int64_t)std::ceil(cutoff / (h[a] / (double)nc[a]) - 1e-12);
+    if (k[a] < 1) k[a] = 1;
+    if (!pbc[a] && periodic) {
+      // an open axis of a partly periodic cell: the box of the cell holds the atoms
+    }
+  }
+  auto cellt = torch::from_blob(cm, {3, 3}, torch::kFloat64).clone().to(pos.device());
+  auto frac = torch::matmul(p, torch::linalg_inv(cellt));
+  auto ncell_t = torch::tensor({nc[0], nc[1], nc[2]}, lopt);
+  auto ci = torch::floor(frac * ncell_t.to(torch::kFloat64)).to(torch::kInt64);
+  ci = torch::clamp(ci, torch::zeros_like(ncell_t), ncell_t - 1);
+  auto lin = (ci.select(1, 0) * nc[1] + ci.select(1, 1)) * nc[2] + ci.select(1, 2);
+  auto sorted = std::get<1>(torch::sort(lin, /*stable=*/true, 0, false));
+  const int64_t ncells = nc[0] * nc[1] * nc[2];
+  auto counts_c = torch::bincount(lin, {}, ncells);
+  auto cell_start = torch::zeros({ncells + 1}, lopt);
+  cell_start.narrow(0, 1, ncells).copy_(torch::cumsum(counts_c, 0));
+
+  NbParams prm;
+  prm.pos = p.data_ptr<double>();
+  for (int a = 0; a < 9; ++a) prm.cell[a] = cm[a];
+  for (int a = 0; a < 3; ++a) { prm.ncell[a] = nc[a]; prm.k[a] = k[a]; prm.pbc[a] = pbc[a] ? 1 : 0; }
+  lin = lin.contiguous();
+  sorted = sorted.contiguous();
+  prm.atom_cell = lin.data_ptr<int64_t>();
+  prm.sorted = sorted.data_ptr<int64_t>();
+  prm.cell_start = cell_start.data_ptr<int64_t>();
+  prm.cutoff2 = cutoff * cutoff;
+  prm.self_interaction = self_interaction ? 1 : 0;
+  prm.N = N;
+
+  auto counts = torch::empty({N}, lopt);
+  if (pos.is_cuda()) {
+    c10::cuda::CUDAGuard g(pos.device());
+    auto st = at::cuda::getCurrentCUDAStream();
+    XNN_CUDA_OK(nb_count_cuda(prm, counts.data_ptr<int64_t>(), st));
+  } else {
+    int64_t* cp = counts.data_ptr<int64_t>();
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t i = 0; i < N; ++i) {
+      int64_t n = 0;
+      nb_visit(prm, i, [&](int64_t, int64_t, int64_t, int64_t) { ++n; });
+      cp[i] = n;
+    }
+  }
+  auto offsets = torch::cumsum(counts, 0) - counts;
+  const int64_t E = counts.sum().item<int64_t>();
+  auto src = torch::empty({E}, lopt);
+  auto dst = torch::empty({E}, lopt);
+  auto shifts = torch::empty({E, 3}, lopt);
+  if (E > 0) {
+    offsets = offsets.contiguous();
+    if (pos.is_cuda()) {
+      c10::cuda::CUDAGuard g(pos.device());
+      auto st = at::cuda::getCurrentCUDAStream();
+      XNN_CUDA_OK(nb_write_cuda(prm, offsets.data_ptr<int64_t>(), src.data_ptr<int64_t>(),
+                                dst.data_ptr<int64_t>(), shifts.data_ptr<int64_t>(), st));
+    } else {
+      const int64_t* op = offsets.data_ptr<int64_t>();
+      int64_t* sp = src.data_ptr<int64_t>();
+      int64_t* dp = dst.data_ptr<int64_t>();
+      int64_t* hp = shifts.data_ptr<int64_t>();
+#pragma omp parallel for schedule(dynamic, 64)
+      for (int64_t i = 0; i < N; ++i) {
+        int64_t o = op[i];
+        nb_visit(prm, i, [&](int64_t j, int64_t s0, int64_t s1, int64_t s2) {
+          sp[o] = j; dp[o] = i;
+          hp[3 * o] = -s0; hp[3 * o + 1] = -s1; hp[3 * o + 2] = -s2;
+          ++o;
+        });
+      }
+    }
+  }
+  return {src, dst, shifts};
+}
+
+// ---- edge geometry ---------------------------------------------------------------------
+std::vector<torch::Tensor> edge_geometry_fwd(torch::Tensor vec, int64_t lmax, torch::Tensor freqs, double norm,
+                                             double rc, int64_t p) {
+  check_cuda(vec, "vec");
+  check_cuda(freqs, "freqs");
+  TORCH_CHECK(vec.dim() == 2 && vec.size(1) == 3, "vec must be (E, 3)");
+  TORCH_CHECK(freqs.scalar_type() == vec.scalar_type(), "freqs dtype");
+  c10::cuda::CUDAGuard g(vec.device());
+  const int64_t E = vec.size(0);
+  const int nrbf = (int)freqs.numel();
+  const int D = (int)((lmax + 1) * (lmax + 1));
+  auto Y = torch::empty({E, D}, vec.options());
+  auto R = torch::empty({E, nrbf}, vec.options());
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(vec.scalar_type(), "edge_geometry_fwd", [&] {
+    XNN_CUDA_OK(edge_geom_fwd<scalar_t>(E, (int)lmax, vec.data_ptr<scalar_t>(), nrbf, freqs.data_ptr<scalar_t>(),
+                                        (scalar_t)norm, (scalar_t)rc, (int)p, Y.data_ptr<scalar_t>(),
+                                        R.data_ptr<scalar_t>(), st));
+  });
+  return {Y, R};
+}
+
+torch::Tensor edge_geometry_bwd(torch::Tensor vec, int64_t lmax, torch::Tensor freqs, double norm, double rc,
+                                int64_t p, c10::optional<torch::Tensor> gY, c10::optional<torch::Tensor> gR) {
+  check_cuda(vec, "vec");
+  c10::cuda::CUDAGuard g(vec.device());
+  if (gY.has_value() && gY->defined()) check_cuda(*gY, "gY");
+  if (gR.has_value() && gR->defined()) check_cuda(*gR, "gR");
+  const int64_t E = vec.size(0);
+  auto gvec = torch::empty_like(vec);
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(vec.scalar_type(), "edge_geometry_bwd", [&] {
+    XNN_CUDA_OK(edge_geom_bwd<scalar_t>(E, (int)lmax, vec.data_ptr<scalar_t>(), (int)freqs.numel(),
+                                        freqs.data_ptr<scalar_t>(), (scalar_t)norm, (scalar_t)rc, (int)p,
+                                        ptr_or_null<scalar_t>(gY), ptr_or_null<scalar_t>(gR),
+                                        gvec.data_ptr<scalar_t>(), st));
+  });
+  return gvec;
+}
+
+std::vector<torch::Tensor> edge_geometry_jvp(torch::Tensor vec, int64_t lmax, torch::Tensor freqs, double norm,
+                                             double rc, int64_t p, torch::Tensor w, bool want_Y, bool want_R) {
+  check_cuda(vec, "vec");
+  check_cuda(w, "w");
+  c10::cuda::CUDAGuard g(vec.device());
+  const int64_t E = vec.size(0);
+  const int nrbf = (int)freqs.numel();
+  const int D = (int)((lmax + 1) * (lmax + 1));
+  torch::Tensor dY = want_Y ? torch::empty({E, D}, vec.options()) : torch::Tensor();
+  torch::Tensor dR = want_R ? torch::empty({E, nrbf}, vec.options()) : torch::Tensor();
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(vec.scalar_type(), "edge_geometry_jvp", [&] {
+    XNN_CUDA_OK(edge_geom_jvp<scalar_t>(E, (int)lmax, vec.data_ptr<scalar_t>(), nrbf, freqs.data_ptr<scalar_t>(),
+                                        (scalar_t)norm, (scalar_t)rc, (int)p, w.data_ptr<scalar_t>(),
+                                        want_Y ? dY.data_ptr<scalar_t>() : nullptr,
+                                        want_R ? dR.data_ptr<scalar_t>() : nullptr, st));
+  });
+  return {dY, dR};
+}
+
+// ---- convolution ------------------------------------------------------------------------
+template <typename T>
+std::vector<const T*> ptrs(const std::vector<torch::Tensor>& v, const char* name) {
+  std::vector<const T*> out;
+  for (auto& t : v) {
+    check_cuda(t, name);
+    out.push_back(t.data_ptr<T>());
+  }
+  return out;
+}
+
+torch::Tensor conv_gather_op(int64_t N, int64_t C, int64_t P, torch::Tensor dst_ptr, torch::Tensor src,
+                             c10::optional<torch::Tensor> perm, std::vector<torch::Tensor> xs,
+                             std::vector<torch::Tensor> Rs, std::vector<torch::Tensor> Ys) {
+  TORCH_CHECK(xs.size() == Rs.size() && Rs.size() == Ys.size() && !xs.empty() && xs.size() <= 3,
+              "conv_gather takes 1-3 (x, R, Y) terms");
+  check_cuda(dst_ptr, "dst_ptr");
+  check_cuda(src, "src");
+  c10::cuda::CUDAGuard g(src.device());
+  const int64_t D = P * P;
+  auto A = torch::empty({D, N, C}, xs[0].options());
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(xs[0].scalar_type(), "conv_gather", [&] {
+    auto px = ptrs<scalar_t>(xs, "x");
+    auto pR = ptrs<scalar_t>(Rs, "R");
+    auto pY = ptrs<scalar_t>(Ys, "Y");
+    XNN_CUDA_OK(conv_gather<scalar_t>((int)N, (int)C, (int)P, dst_ptr.data_ptr<int64_t>(), src.data_ptr<int>(),
+                                      perm.has_value() && perm->defined() ? perm->data_ptr<int64_t>() : nullptr,
+                                      (int)xs.size(), px.data(), pR.data(), pY.data(), A.data_ptr<scalar_t>(), st));
+  });
+  return A;
+}
+
+std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t E, torch::Tensor dst_ptr,
+                                        torch::Tensor src, c10::optional<torch::Tensor> perm, torch::Tensor G,
+                                        std::vector<torch::Tensor> xR, std::vector<torch::Tensor> YR,
+                                        std::vector<torch::Tensor> xY, std::vector<torch::Tensor> RY) {
+  TORCH_CHECK(xR.size() == YR.size() && xR.size() <= 2, "conv_edge: 0-2 (x, Y) terms for gR");
+  TORCH_CHECK(xY.size() == RY.size() && xY.size() <= 2, "conv_edge: 0-2 (x, R) terms for gY");
+  check_cuda(G, "G");
+  c10::cuda::CUDAGuard g(G.device());
+  const int64_t D = P * P;
+  const int64_t cpl = std::min<int64_t>(4, std::max<int64_t>(1, (C + 31) / 32));
+  const bool split = (C + 32 * cpl - 1) / (32 * cpl) > 1;
+  torch::Tensor gR = xR.empty() ? torch::Tensor() : torch::empty({E, P, C}, G.options());
+  torch::Tensor gY = xY.empty() ? torch::Tensor()
+                                : (split ? torch::zeros({E, D}, G.options()) : torch::empty({E, D}, G.options()));
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(G.scalar_type(), "conv_edge", [&] {
+    auto pxR = ptrs<scalar_t>(xR, "x");
+    auto pYR = ptrs<scalar_t>(YR, "Y");
+    auto pxY = ptrs<scalar_t>(xY, "x");
+    auto pRY = ptrs<scalar_t>(RY, "R");
+    XNN_CUDA_OK(conv_edge<scalar_t>((int)N, (int)C, (int)P, dst_ptr.data_ptr<int64_t>(), src.data_ptr<int>(),
+                                    perm.has_value() && perm->defined() ? perm->data_ptr<int64_t>() : nullptr,
+                                    G.data_ptr<scalar_t>(), (int)xR.size(), pxR.data(), pYR.data(),
+                                    (int)xY.size(), pxY.data(), pRY.data(),
+                                    gR.defined() ? gR.data_ptr<scalar_t>() : nullptr,
+                                    gY.defined() ? gY.data_ptr<scalar_t>() : nullptr, st));
+  });
+  return {gR, gY};
+}
+
+torch::Tensor conv_scatter_op(int64_t N, int64_t C, int64_t P, torch::Tensor src_ptr, torch::Tensor src_perm,
+                              torch::Tensor dst, torch::Tensor G, std::vector<torch::Tensor> Rs,
+                              std::vector<torch::Tensor> Ys) {
+  TORCH_CHECK(Rs.size() == Ys.size() && !Rs.empty() && Rs.size() <= 2, "conv_scatter: 1-2 (R, Y) terms");
+  check_cuda(G, "G");
+  c10::cuda::CUDAGuard g(G.device());
+  auto gx = torch::empty({N, C}, G.options());
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(G.scalar_type(), "conv_scatter", [&] {
+    auto pR = ptrs<scalar_t>(Rs, "R");
+    auto pY = ptrs<scalar_t>(Ys, "Y");
+    XNN_CUDA_OK(conv_scatter<scalar_t>((int)N, (int)C, (int)P, src_ptr.data_ptr<int64_t>(),
+                                       src_perm.data_ptr<int64_t>(), dst.data_ptr<int>(), G.data_ptr<scalar_t>(),
+                                       (int)Rs.size(), pR.data(), pY.data(), gx.data_ptr<scalar_t>(), st));
+  });
+  return gx;
+}
+
+// ---- symmetric contraction --------------------------------------------------------------------
+torch::Tensor symcon_fwd_op(torch::Tensor A, torch::Tensor z, torch::Tensor W, int64_t lmax, int64_t corr) {
+  check_cuda(A, "A"); check_cuda(z, "z"); check_cuda(W, "W");
+  c10::cuda::CUDAGuard g(A.device());
+  const int64_t N = A.size(1), C = A.size(2);
+  TORCH_CHECK(W.size(1) == symcon_num_invariants((int)lmax, (int)corr) && W.size(2) == C, "W shape");
+  auto out = torch::empty({N, C}, A.options());
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(A.scalar_type(), "symcon_fwd", [&] {
+    XNN_CUDA_OK(symcon_fwd<scalar_t>((int)N, (int)C, (int)lmax, (int)corr, A.data_ptr<scalar_t>(),
+                                     z.data_ptr<int64_t>(), W.data_ptr<scalar_t>(), out.data_ptr<scalar_t>(), st));
+  });
+  return out;
+}
+
+std::vector<torch::Tensor> symcon_bwd_op(torch::Tensor A, torch::Tensor z, torch::Tensor W, torch::Tensor gout,
+                                         int64_t lmax, int64_t corr, bool want_gA, bool want_gW) {
+  check_cuda(A, "A"); check_cuda(gout, "g");
+  c10::cuda::CUDAGuard g(A.device());
+  const int64_t N = A.size(1), C = A.size(2), K = W.size(1);
+  torch::Tensor gA = want_gA ? torch::empty_like(A) : torch::Tensor();
+  torch::Tensor gWa = want_gW ? torch::empty({N, K, C}, A.options()) : torch::Tensor();
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(A.scalar_type(), "symcon_bwd", [&] {
+    XNN_CUDA_OK(symcon_bwd<scalar_t>((int)N, (int)C, (int)lmax, (int)corr, A.data_ptr<scalar_t>(),
+                                     z.data_ptr<int64_t>(), W.data_ptr<scalar_t>(), gout.data_ptr<scalar_t>(),
+                                     want_gA ? gA.data_ptr<scalar_t>() : nullptr,
+                                     want_gW ? gWa.data_ptr<scalar_t>() : nullptr, st));
+  });
+  return {gA, gWa};
+}
+
+std::vector<torch::Tensor> symcon_bwd2_op(torch::Tensor A, torch::Tensor z, torch::Tensor W, torch::Tensor gout,
+                                          c10::optional<torch::Tensor> uA, c10::optional<torch::Tensor> uWa,
+                                          int64_t lmax, int64_t corr, bool want_g, bool want_A, bool want_W) {
+  check_cuda(A, "A");
+  c10::cuda::CUDAGuard g(A.device());
+  const int64_t N = A.size(1), C = A.size(2), K = W.size(1);
+  torch::Tensor cg = want_g ? torch::empty({N, C}, A.options()) : torch::Tensor();
+  torch::Tensor cA = want_A ? torch::empty_like(A) : torch::Tensor();
+  torch::Tensor cW = want_W ? torch::empty({N, K, C}, A.options()) : torch::Tensor();
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(A.scalar_type(), "symcon_bwd2", [&] {
+    XNN_CUDA_OK(symcon_bwd2<scalar_t>((int)N, (int)C, (int)lmax, (int)corr, A.data_ptr<scalar_t>(),
+                                      z.data_ptr<int64_t>(), W.data_ptr<scalar_t>(), gout.data_ptr<scalar_t>(),
+                                      ptr_or_null<scalar_t>(uA), ptr_or_null<scalar_t>(uWa),
+                                      want_g ? cg.data_ptr<scalar_t>() : nullptr,
+                                      want_A ? cA.data_ptr<scalar_t>() : nullptr,
+                                      want_W ? cW.data_ptr<scalar_t>() : nullptr, st));
+  });
+  return {cg, cA, cW};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.attr("HAS_CUDA") = true;
+  m.def("neighbor_list", &neighbor_list, "cell-list neighbour search (CUDA or OpenMP)");
+  m.def("edge_geometry_fwd", &edge_geometry_fwd);
+  m.def("edge_geometry_bwd", &edge_geometry_bwd);
+  m.def("edge_geometry_jvp", &edge_geometry_jvp);
+  m.def("conv_gather", &conv_gather_op);
+  m.def("conv_edge", &conv_edge_op);
+  m.def("conv_scatter", &conv_scatter_op);
+  m.def("symcon_fwd", &symcon_fwd_op);
+  m.def("symcon_bwd", &symcon_bwd_op);
+  m.def("symcon_bwd2", &symcon_bwd2_op);
+  m.def("symcon_num_invariants", &symcon_num_invariants);
+}

@@ -1,0 +1,330 @@
+// The equivariant convolution of MACE/NequIP with scalar node features, as the partial
+// derivatives of one 4-linear form over the edges e = (s -> d):
+//
+//   Phi(G, x, R, Y) = sum_e sum_c sum_{l,m} G[lm, d, c] * R[e, l, c] * x[s, c] * Y[e, lm]
+//
+//   A  = dPhi/dG : A[lm, d, c]  = sum_{e into d} R[e,l,c] x[s,c] Y[e,lm]      (message pass)
+//   gx = dPhi/dx : gx[s, c]     = sum_{e out of s} sum_lm G[lm,d,c] R[e,l,c] Y[e,lm]
+//   gR = dPhi/dR : gR[e, l, c]  = x[s,c] sum_m G[lm,d,c] Y[e,lm]
+//   gY = dPhi/dY : gY[e, lm]    = sum_c G[lm,d,c] R[e,l,c] x[s,c]
+//
+// Because Phi is linear in each argument, every derivative of every order is again one
+// of these four contractions with some arguments replaced by cotangents; the kernels
+// take up to three (gather) or two (edge / scatter) argument sets and add their terms,
+// which is exactly what the first and second backward of a force loss need.
+//
+// Layouts: x (N, C); R (E, P, C); Y (E, P*P); G and A (P*P, N, C) component-major, so the
+// per-degree channel mixing that follows is one plain matrix product per degree.
+// Mapping: one warp per atom, lanes over channels (CPL channels per lane), receivers
+// through the CSR of edges grouped by receiver, senders through a permutation grouped
+// by sender: every sum is a register accumulation, deterministic and atomic-free
+// (except gY when the channels are split over several warps, C > 128).
+#include "common.cuh"
+
+template <typename T>
+struct GatherTerms {  // per term: x, R, Y
+  const T* x[3];
+  const T* R[3];
+  const T* Y[3];
+  int n;
+};
+
+template <typename T>
+struct PairTerms {  // per term: two operands (meaning depends on the kernel)
+  const T* a[2];
+  const T* b[2];
+  int n;
+};
+
+template <typename T, int P, int CPL>
+__global__ void __launch_bounds__(128) conv_gather_kernel(
+    int N, int C, const int64_t* __restrict__ dst_ptr, const int* __restrict__ src,
+    const int64_t* __restrict__ perm, GatherTerms<T> t, T* __restrict__ A) {
+  constexpr int D = P * P;
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= N) return;
+  const int cbase = blockIdx.y * 32 * CPL;
+  T acc[CPL][D];
+#pragma unroll
+  for (int q = 0; q < CPL; ++q)
+#pragma unroll
+    for (int d = 0; d < D; ++d) acc[q][d] = T(0);
+  const int64_t j0 = dst_ptr[i], j1 = dst_ptr[i + 1];
+  for (int64_t j = j0; j < j1; ++j) {
+    const int64_t e = perm ? perm[j] : j;
+    const int64_t s = src[e];
+#pragma unroll
+    for (int tt = 0; tt < 3; ++tt) {
+      if (tt < t.n) {
+        T y[D];
+#pragma unroll
+        for (int d = 0; d < D; ++d) y[d] = __ldg(t.Y[tt] + e * D + d);
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+          const int c = cbase + lane + 32 * q;
+          if (c < C) {
+            const T xv = __ldg(t.x[tt] + s * C + c);
+#pragma unroll
+            for (int l = 0; l < P; ++l) {
+              const T r = __ldg(t.R[tt] + (e * P + l) * C + c) * xv;
+#pragma unroll
+              for (int m = 0; m < 2 * l + 1; ++m) acc[q][l * l + m] += r * y[l * l + m];
+            }
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) {
+    const int c = cbase + lane + 32 * q;
+    if (c < C) {
+#pragma unroll
+      for (int d = 0; d < D; ++d) A[((int64_t)d * N + i) * C + c] = acc[q][d];
+    }
+  }
+}
+
+// gR (terms a = x, b = Y) and gY (terms a = x, b = R) of the edges into each receiver;
+// G of the receiver is read once into registers.
+template <typename T, int P, int CPL>
+__global__ void __launch_bounds__(128) conv_edge_kernel(
+    int N, int C, const int64_t* __restrict__ dst_ptr, const int* __restrict__ src,
+    const int64_t* __restrict__ perm, const T* __restrict__ G, PairTerms<T> tR, PairTerms<T> tY,
+    T* __restrict__ gR, T* __restrict__ gY, int atomic_gY) {
+  constexpr int D = P * P;
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (i >= N) return;
+  const int cbase = blockIdx.y * 32 * CPL;
+  T g[CPL][D];
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) {
+    const int c = cbase + lane + 32 * q;
+#pragma unroll
+    for (int d = 0; d < D; ++d) g[q][d] = c < C ? __ldg(G + ((int64_t)d * N + i) * C + c) : T(0);
+  }
+  const int64_t j0 = dst_ptr[i], j1 = dst_ptr[i + 1];
+  for (int64_t j = j0; j < j1; ++j) {
+    const int64_t e = perm ? perm[j] : j;
+    const int64_t s = src[e];
+    if (tR.n > 0) {
+      T out[CPL][P];
+#pragma unroll
+      for (int q = 0; q < CPL; ++q)
+#pragma unroll
+        for (int l = 0; l < P; ++l) out[q][l] = T(0);
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) {
+        if (tt < tR.n) {
+          T y[D];
+#pragma unroll
+          for (int d = 0; d < D; ++d) y[d] = __ldg(tR.b[tt] + e * D + d);
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            const int c = cbase + lane + 32 * q;
+            if (c < C) {
+              const T xv = __ldg(tR.a[tt] + s * C + c);
+#pragma unroll
+              for (int l = 0; l < P; ++l) {
+                T sm = T(0);
+#pragma unroll
+                for (int m = 0; m < 2 * l + 1; ++m) sm += g[q][l * l + m] * y[l * l + m];
+                out[q][l] += xv * sm;
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < CPL; ++q) {
+        const int c = cbase + lane + 32 * q;
+        if (c < C) {
+#pragma unroll
+          for (int l = 0; l < P; ++l) gR[(e * P + l) * C + c] = out[q][l];
+        }
+      }
+    }
+    if (tY.n > 0) {
+      T v[16];
+#pragma unroll
+      for (int d = 0; d < 16; ++d) v[d] = T(0);
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) {
+        if (tt < tY.n) {
+#pragma unroll
+          for (int q = 0; q < CPL; ++q) {
+            const int c = cbase + lane + 32 * q;
+            if (c < C) {
+              const T xv = __ldg(tY.a[tt] + s * C + c);
+#pragma unroll
+              for (int l = 0; l < P; ++l) {
+                const T r = __ldg(tY.b[tt] + (e * P + l) * C + c) * xv;
+#pragma unroll
+                for (int m = 0; m < 2 * l + 1; ++m) v[l * l + m] += g[q][l * l + m] * r;
+              }
+            }
+          }
+        }
+      }
+      reduce16(v, lane);
+      const int idx = reduce16_index(lane);
+      if ((lane & 1) == 0 && idx < D) {
+        if (atomic_gY) atomicAdd(gY + e * D + idx, v[0]);
+        else gY[e * D + idx] = v[0];
+      }
+    }
+  }
+}
+
+// gx of every sender (terms a = R, b = Y), edges through the sender permutation.
+template <typename T, int P, int CPL>
+__global__ void __launch_bounds__(128) conv_scatter_kernel(
+    int N, int C, const int64_t* __restrict__ src_ptr, const int64_t* __restrict__ src_perm,
+    const int* __restrict__ dst, const T* __restrict__ G, PairTerms<T> t, T* __restrict__ gx) {
+  constexpr int D = P * P;
+  const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (s >= N) return;
+  const int cbase = blockIdx.y * 32 * CPL;
+  T acc[CPL];
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) acc[q] = T(0);
+  const int64_t j0 = src_ptr[s], j1 = src_ptr[s + 1];
+  for (int64_t j = j0; j < j1; ++j) {
+    const int64_t e = src_perm[j];
+    const int64_t d = dst[e];
+    T gd[CPL][D];
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c = cbase + lane + 32 * q;
+#pragma unroll
+      for (int k = 0; k < D; ++k) gd[q][k] = c < C ? __ldg(G + ((int64_t)k * N + d) * C + c) : T(0);
+    }
+#pragma unroll
+    for (int tt = 0; tt < 2; ++tt) {
+      if (tt < t.n) {
+        T y[D];
+#pragma unroll
+        for (int k = 0; k < D; ++k) y[k] = __ldg(t.b[tt] + e * D + k);
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+          const int c = cbase + lane + 32 * q;
+          if (c < C) {
+#pragma unroll
+            for (int l = 0; l < P; ++l) {
+              T sm = T(0);
+#pragma unroll
+              for (int m = 0; m < 2 * l + 1; ++m) sm += gd[q][l * l + m] * y[l * l + m];
+              acc[q] += __ldg(t.a[tt] + (e * P + l) * C + c) * sm;
+            }
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) {
+    const int c = cbase + lane + 32 * q;
+    if (c < C) gx[(int64_t)s * C + c] = acc[q];
+  }
+}
+
+namespace {
+inline int cpl_for(int C) {
+  const int c = (C + 31) / 32;
+  return c > 4 ? 4 : (c < 1 ? 1 : c);
+}
+}  // namespace
+
+#define XNN_P_CPL_SWITCH(P, CPL, ...)                                        \
+  switch (P * 8 + CPL) {                                                     \
+    case 9: { constexpr int PP = 1, QQ = 1; __VA_ARGS__; } break;            \
+    case 10: { constexpr int PP = 1, QQ = 2; __VA_ARGS__; } break;           \
+    case 11: { constexpr int PP = 1, QQ = 3; __VA_ARGS__; } break;           \
+    case 12: { constexpr int PP = 1, QQ = 4; __VA_ARGS__; } break;           \
+    case 17: { constexpr int PP = 2, QQ = 1; __VA_ARGS__; } break;           \
+    case 18: { constexpr int PP = 2, QQ = 2; __VA_ARGS__; } break;           \
+    case 19: { constexpr int PP = 2, QQ = 3; __VA_ARGS__; } break;           \
+    case 20: { constexpr int PP = 2, QQ = 4; __VA_ARGS__; } break;           \
+    case 25: { constexpr int PP = 3, QQ = 1; __VA_ARGS__; } break;           \
+    case 26: { constexpr int PP = 3, QQ = 2; __VA_ARGS__; } break;           \
+    case 27: { constexpr int PP = 3, QQ = 3; __VA_ARGS__; } break;           \
+    case 28: { constexpr int PP = 3, QQ = 4; __VA_ARGS__; } break;           \
+    case 33: { constexpr int PP = 4, QQ = 1; __VA_ARGS__; } break;           \
+    case 34: { constexpr int PP = 4, QQ = 2; __VA_ARGS__; } break;           \
+    case 35: { constexpr int PP = 4, QQ = 3; __VA_ARGS__; } break;           \
+    case 36: { constexpr int PP = 4, QQ = 4; __VA_ARGS__; } break;           \
+    default: return cudaErrorInvalidValue;                                   \
+  }
+
+template <typename T>
+cudaError_t conv_gather(int N, int C, int P, const int64_t* dst_ptr, const int* src, const int64_t* perm,
+                        int nterms, const T* const* x, const T* const* R, const T* const* Y, T* A,
+                        cudaStream_t stream) {
+  if (N == 0) return cudaSuccess;
+  if (nterms < 1 || nterms > 3) return cudaErrorInvalidValue;
+  GatherTerms<T> t;
+  t.n = nterms;
+  for (int k = 0; k < 3; ++k) {
+    t.x[k] = k < nterms ? x[k] : nullptr;
+    t.R[k] = k < nterms ? R[k] : nullptr;
+    t.Y[k] = k < nterms ? Y[k] : nullptr;
+  }
+  const int cpl = cpl_for(C);
+  dim3 grid((N + 3) / 4, (C + 32 * cpl - 1) / (32 * cpl));
+  XNN_P_CPL_SWITCH(P, cpl, conv_gather_kernel<T, PP, QQ><<<grid, 128, 0, stream>>>(N, C, dst_ptr, src, perm, t, A));
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t conv_edge(int N, int C, int P, const int64_t* dst_ptr, const int* src, const int64_t* perm,
+                      const T* G, int nR, const T* const* xR, const T* const* YR, int nY,
+                      const T* const* xY, const T* const* RY, T* gR, T* gY, cudaStream_t stream) {
+  if (N == 0) return cudaSuccess;
+  if (nR < 0 || nR > 2 || nY < 0 || nY > 2) return cudaErrorInvalidValue;
+  PairTerms<T> tR, tY;
+  tR.n = nR; tY.n = nY;
+  for (int k = 0; k < 2; ++k) {
+    tR.a[k] = k < nR ? xR[k] : nullptr; tR.b[k] = k < nR ? YR[k] : nullptr;
+    tY.a[k] = k < nY ? xY[k] : nullptr; tY.b[k] = k < nY ? RY[k] : nullptr;
+  }
+  const int cpl = cpl_for(C);
+  const int gy = (C + 32 * cpl - 1) / (32 * cpl);
+  dim3 grid((N + 3) / 4, gy);
+  const int atomic_gY = gy > 1 ? 1 : 0;
+  XNN_P_CPL_SWITCH(P, cpl, conv_edge_kernel<T, PP, QQ><<<grid, 128, 0, stream>>>(N, C, dst_ptr, src, perm, G, tR, tY, gR, gY, atomic_gY));
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t conv_scatter(int N, int C, int P, const int64_t* src_ptr, const int64_t* src_perm,
+                         const int* dst, const T* G, int nterms, const T* const* R,
+                         const T* const* Y, T* gx, cudaStream_t stream) {
+  if (N == 0) return cudaSuccess;
+  if (nterms < 1 || nterms > 2) return cudaErrorInvalidValue;
+  PairTerms<T> t;
+  t.n = nterms;
+  for (int k = 0; k < 2; ++k) {
+    t.a[k] = k < nterms ? R[k] : nullptr;
+    t.b[k] = k < nterms ? Y[k] : nullptr;
+  }
+  const int cpl = cpl_for(C);
+  dim3 grid((N + 3) / 4, (C + 32 * cpl - 1) / (32 * cpl));
+  XNN_P_CPL_SWITCH(P, cpl, conv_scatter_kernel<T, PP, QQ><<<grid, 128, 0, stream>>>(N, C, src_ptr, src_perm, dst, G, t, gx));
+  return cudaGetLastError();
+}
+
+#define XNN_INST(T)                                                                                  \
+  template cudaError_t conv_gather<T>(int, int, int, const int64_t*, const int*, const int64_t*, int, \
+                                      const T* const*, const T* const*, const T* const*, T*,          \
+                                      cudaStream_t);                                                  \
+  template cudaError_t conv_edge<T>(int, int, int, const int64_t*, const int*, const int64_t*,       \
+                                    const T*, int, const T* const*, const T* const*, int,            \
+                                    const T* const*, const T* const*, T*, T*, cudaStream_t);         \
+  template cudaError_t conv_scatter<T>(int, int, int, const int64_t*, const int64_t*, const int*,    \
+                                       const T*, int, const T* const*, const T* const*, T*,          \
+                                       cudaStream_t);
+XNN_INST(float)
+XNN_INST(double)

@@ -1,0 +1,2 @@
+"""Imports every model family so that their ``@register_model`` decorators run."""
+from . import mace  # noqa: F401

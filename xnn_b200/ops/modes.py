@@ -1,0 +1,43 @@
+"""Which derivatives the fused ops may skip, scoped to one pass of autograd.
+
+A force-loss training step differentiates twice. In the force pass
+(``autograd.grad(E, pos)``) no parameter gradient is used, and in the parameter pass
+(``loss.backward(inputs=params)``) no cotangent of a purely geometric input (the edge
+vectors and their features) is used. The fused ops read these flags and skip that work;
+a caller that needs full derivatives (Hessians, vibrations) simply does not set them.
+"""
+from __future__ import annotations
+
+import contextlib
+import threading
+
+
+class _Modes(threading.local):
+    def __init__(self):
+        self.force_pass = False
+        self.params_only = False
+
+
+MODES = _Modes()
+
+
+@contextlib.contextmanager
+def force_pass(enabled: bool = True):
+    """Within: parameter gradients of the fused ops are not formed."""
+    prev = MODES.force_pass
+    MODES.force_pass = enabled
+    try:
+        yield
+    finally:
+        MODES.force_pass = prev
+
+
+@contextlib.contextmanager
+def params_only(enabled: bool = True):
+    """Within: cotangents of geometric inputs (edge vectors, their features) are not formed."""
+    prev = MODES.params_only
+    MODES.params_only = enabled
+    try:
+        yield
+    finally:
+        MODES.params_only = prev
