@@ -1,0 +1,262 @@
+"""Headline benchmark: MACE (OFF23-small-shaped) data-parallel training throughput, structures/s.
+
+Config 2 of the benchmark plan: MACE with 2 interactions, 96x0e hidden channels, max_L 0,
+correlation 3, max_ell 3, 8 Bessel functions, r_max 4.5 A, float32, random init; per GPU a
+batch of 64 seeded synthetic molecules of 10-60 atoms ({H,C,N,O,F,S,Cl} at 50/30/8/8/2/1/1 %,
+0.1 atoms/A^3, 0.9 A minimum separation) with float64 Morse labels; energy + force loss.
+One process per GPU (torchrun), NCCL; weak scaling (64 structures per GPU per step).
+
+Device timing: W untimed warm-up steps, then K steps each bracketed by CUDA events on the
+launching stream, with a 256 MB write (larger than the 126 MB L2) between steps to flush
+L2; barrier + synchronize on both sides; the max over ranks is reported. The e2e figure runs
+the same steps through ``Trainer.train_step`` on batches in pinned host memory (host-to-device
+copy of every step's inputs) and reads each step's loss back to the host.
+
+``--impl reference`` runs the reference package installed under ``baseline/_ref`` through
+its own API, or prints why it cannot.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="xnn_b200", choices=["xnn_b200", "reference"])
+    ap.add_argument("--batch", type=int, default=64, help="structures per GPU per step")
+    ap.add_argument("--pool", type=int, default=8, help="distinct batches per rank, cycled")
+    ap.add_argument("--no-graph", action="store_true", help="eager steps instead of one CUDA graph")
+    ap.add_argument("--grad-sync", default="nccl", choices=["nccl", "p2p"])
+    ap.add_argument("--dtype", default="float32")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU's SM clock and throttle reasons while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for s in self.samples for n, v in zip(names, s[3:7]) if "Active" in v and "Not" not in v})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def reference_arm(args):
+    """Run the unmodified reference through its own API, or say why it cannot run."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    reason = None
+    if not os.path.isdir(os.path.join(ref, "xnn")):
+        reason = "reference not installed under baseline/_ref"
+    else:
+        sys.path.insert(0, ref)
+        try:
+            import xnn.gnn.models.mace  # noqa: F401
+        except ModuleNotFoundError as exc:
+            reason = (f"the reference MACE imports {exc.name!r}, which is not installed and not in the "
+                      "offline wheelhouse (no network); the reference cannot build the benchmarked model")
+        except Exception as exc:  # pragma: no cover
+            reason = f"reference import failed: {exc!r}"
+    if reason is None:
+        reason = "reference MACE importable but its arm is not wired"
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    sys.path.insert(0, ROOT)
+    import torch
+    import torch.distributed as dist
+
+    from xnn_b200.config import from_dict
+    from xnn_b200.data import AtomicDataset, synthetic
+    from xnn_b200.parallel import distributed as D
+    from xnn_b200.train import Trainer
+
+    world = D.env_world()
+    rank = D.env_rank()
+    dtype = getattr(torch, args.dtype)
+    torch.set_default_dtype(dtype)
+    B = args.batch
+    # synthetic data: a pool of distinct batches per rank, cycled through the steps
+    mols = synthetic.organic_molecules(B * args.pool, seed=1000 + rank)
+    ds = AtomicDataset(mols, 4.5, precompute=True)
+    graphs = [ds[i] for i in range(len(ds))]
+    n_edges = sum(g.num_edges for g in graphs)
+    n_atoms = sum(g.num_nodes for g in graphs)
+    avg_nb = n_edges / n_atoms
+    cfg = from_dict({
+        "model": {"name": "mace", "cutoff": 4.5, "n_features": 96, "n_interactions": 2, "n_rbf": 8,
+                  "extra": {"species": [1, 6, 7, 8, 9, 16, 17], "max_ell": 3, "max_L": 0,
+                            "correlation": 3, "avg_num_neighbors": avg_nb}},
+        "optim": {"lr": 1e-3, "energy_weight": 1.0, "force_weight": 10.0, "epochs": 1,
+                  "scheduler": "none"},
+        "data": {"batch_size": B, "val_fraction": 0.0},
+        "trainer": {"cuda_graph": not args.no_graph, "grad_sync": args.grad_sync, "loggers": []},
+        "device": "cuda", "seed": 1234, "output_dir": os.path.join(ROOT, "gpurun_out", "bench_run"),
+    })
+    trainer = Trainer(cfg, ds, val=[], test=[])
+    dev = trainer.device
+    # fixed-capacity padded batches in pinned host memory
+    cap = trainer.capacity_for([ds], B)
+    if world > 1:
+        t = torch.tensor(cap, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        cap = tuple(int(x) for x in t.tolist())
+    padder = trainer.make_padder(*cap)
+    from xnn_b200.data import collate
+    host_batches = []
+    for k in range(args.pool):
+        gs = graphs[k * B:(k + 1) * B]
+        host_batches.append(padder(gs) if not args.no_graph else collate(gs).pin_memory())
+    in_bytes = [sum(v.numel() * v.element_size() for v in vars(b).values() if isinstance(v, torch.Tensor))
+                for b in host_batches]
+    dev_batches = [b.to(dev) for b in host_batches]
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def step(i, batch):
+        return trainer.train_step(batch)
+
+    # warm-up (the first step captures the graph)
+    for i in range(max(3, args.warmup)):
+        loss, _ = step(i, dev_batches[i % args.pool])
+    torch.cuda.synchronize(dev)
+    finite = bool(torch.isfinite(loss).item())
+
+    # launch count of this repository's kernels in one step (eager step under the profiler, untimed)
+    launches = None
+    try:
+        from torch.profiler import ProfilerActivity, profile
+        trainer.use_graphs, saved = False, trainer.use_graphs
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            trainer._train_step_impl(dev_batches[0])
+            torch.cuda.synchronize(dev)
+        trainer.use_graphs = saved
+        names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+        ours = [n for n in names if any(k in n for k in ("conv_gather", "conv_edge", "conv_scatter",
+                                                          "symcon_", "edge_geom_", "p2p_allreduce",
+                                                          "radial_mlp", "nb_count", "nb_write"))]
+        launches = len(ours)
+        all_kernels = len(names)
+    except Exception as exc:  # pragma: no cover
+        all_kernels = None
+        print(f"launch count unavailable: {exc}", file=sys.stderr)
+
+    # device-timed region
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            starts[i].record()
+            step(i, dev_batches[i % args.pool])
+            stops[i].record()
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = sum(a.elapsed_time(b) for a, b in zip(starts, stops)) / args.steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * B / (ms_max / 1e3)
+
+    # end to end through the public step: pinned host batch in, loss out, every step
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        loss, _ = trainer.train_step(host_batches[i % args.pool])
+        _ = float(loss.item())
+    torch.cuda.synchronize(dev)
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e = world * B * args.steps / float(te.item())
+
+    trainer.close()
+    if rank == 0:
+        line = {
+            "metric": "MACE train structures/s", "value": round(value, 2), "unit": "structures/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_max, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32" if dtype == torch.float32 else str(dtype),
+            "data": "synthetic (seeded organic molecules, 10-60 atoms, float64 Morse labels); random-init weights",
+            "config": {"model": "MACE OFF23-small-shaped: 2 interactions, 96x0e, max_ell 3, max_L 0, "
+                                "correlation 3, 8 Bessel, r_max 4.5 A",
+                       "global_batch": world * B, "seq_len": None, "atoms_per_structure": "10-60",
+                       "parallelism": f"dp{world}", "grad_sync": args.grad_sync,
+                       "cuda_graph": not args.no_graph,
+                       "l2": "flushed between timed steps (256 MB write)",
+                       "avg_atoms_per_batch": round(n_atoms / args.pool, 1),
+                       "avg_edges_per_batch": round(n_edges / args.pool, 1)},
+            "clocks": clocks.summary(),
+            "e2e": {"value": round(e2e, 2), "unit": "structures/s",
+                    "h2d_bytes_per_step": int(sum(in_bytes) / len(in_bytes)), "d2h_bytes_per_step": 8},
+            "gpu_launches": None if launches is None else launches * args.steps,
+            "gpu_launches_per_step": {"xnn_b200_kernels": launches, "all_kernels": all_kernels},
+            "loss_finite": finite,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,114 @@
+"""CUDA kernels against the PyTorch formulas of the same ops: values, first and second derivatives."""
+import pytest
+import torch
+
+from xnn_b200 import _ext
+from xnn_b200.data import collate, structure_to_graph, synthetic
+from xnn_b200.ops import mace_ops as K
+
+pytestmark = pytest.mark.gpu
+
+
+def _graph(n=6, cutoff=4.5, seed=0):
+    mols = synthetic.organic_molecules(n, seed=seed, labels=False)
+    return collate([structure_to_graph(s, cutoff) for s in mols])
+
+
+def _check_derivs(fn_fast, fn_ref, inputs, rtol, atol, second=True):
+    ins_f = [x.detach().clone().requires_grad_(True) for x in inputs]
+    ins_r = [x.detach().clone().requires_grad_(True) for x in inputs]
+    out_f = fn_fast(*ins_f)
+    out_r = fn_ref(*ins_r)
+    out_f = out_f if isinstance(out_f, tuple) else (out_f,)
+    out_r = out_r if isinstance(out_r, tuple) else (out_r,)
+    for a, b in zip(out_f, out_r):
+        torch.testing.assert_close(a, b, rtol=rtol, atol=atol)
+    cots = [torch.randn_like(o) for o in out_r]
+    gf = torch.autograd.grad(out_f, ins_f, cots, create_graph=True, allow_unused=True)
+    gr = torch.autograd.grad(out_r, ins_r, cots, create_graph=True, allow_unused=True)
+    for a, b in zip(gf, gr):
+        if b is None:
+            continue
+        torch.testing.assert_close(a, b, rtol=rtol, atol=atol)
+    if not second:
+        return
+    vs = [torch.randn_like(g) if g is not None else None for g in gr]
+    sf = sum((g * v).sum() for g, v in zip(gf, vs) if g is not None)
+    sr = sum((g * v).sum() for g, v in zip(gr, vs) if g is not None)
+    hf = torch.autograd.grad(sf, ins_f, allow_unused=True)
+    hr = torch.autograd.grad(sr, ins_r, allow_unused=True)
+    for a, b in zip(hf, hr):
+        if b is None:
+            continue
+        assert a is not None
+        torch.testing.assert_close(a, b, rtol=rtol, atol=atol)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_ext():
+    if not _ext.cuda_available():
+        pytest.fail(f"native extension not loaded: {_ext.error()}")
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-9), (torch.float32, 2e-4)])
+@pytest.mark.parametrize("lmax", [1, 2, 3])
+def test_edge_geometry(dtype, tol, lmax):
+    g = _graph()
+    vec = g.edge_vectors().to("cuda", dtype)
+    freqs = (torch.pi * torch.arange(1, 9, dtype=dtype, device="cuda"))
+    cfg = (lmax, freqs, (2 / 4.5) ** 0.5, 4.5, 5)
+    _check_derivs(lambda v: K.edge_geometry(v, *cfg), lambda v: K.edge_features_torch(v, *cfg), [vec], tol, tol)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-9), (torch.float32, 5e-4)])
+@pytest.mark.parametrize("P,C", [(4, 96), (3, 40), (2, 16), (4, 160)])
+def test_conv(dtype, tol, P, C):
+    g = _graph()
+    dev = "cuda"
+    ei = g.edge_index.to(dev)
+    N, E = g.num_nodes, g.num_edges
+    plan = K.EdgePlan.build(ei, N)
+    x = torch.randn(N, C, dtype=dtype, device=dev)
+    R = torch.randn(E, P, C, dtype=dtype, device=dev)
+    Y = torch.randn(E, P * P, dtype=dtype, device=dev)
+    _check_derivs(lambda a, b, c: K.conv(a, b, c, plan), lambda a, b, c: K.conv_torch(a, b, c, plan),
+                  [x, R, Y], tol, tol)
+
+
+def test_conv_unsorted_edges():
+    g = _graph()
+    dev = "cuda"
+    perm = torch.randperm(g.num_edges)
+    ei = g.edge_index[:, perm].to(dev)
+    N, E, P, C = g.num_nodes, g.num_edges, 4, 32
+    plan = K.EdgePlan.build(ei, N)
+    assert plan.dst_perm is not None
+    x = torch.randn(N, C, dtype=torch.float64, device=dev)
+    R = torch.randn(E, P, C, dtype=torch.float64, device=dev)
+    Y = torch.randn(E, P * P, dtype=torch.float64, device=dev)
+    _check_derivs(lambda a, b, c: K.conv(a, b, c, plan), lambda a, b, c: K.conv_torch(a, b, c, plan),
+                  [x, R, Y], 1e-9, 1e-9)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-9), (torch.float32, 5e-4)])
+@pytest.mark.parametrize("lmax,corr", [(3, 3), (2, 3), (1, 2), (3, 1)])
+def test_symmetric_contraction(dtype, tol, lmax, corr):
+    dev = "cuda"
+    N, C, n_el = 300, 40, 5
+    D = (lmax + 1) ** 2
+    Kn = K.num_invariants(lmax, corr)
+    A = 0.5 * torch.randn(D, N, C, dtype=dtype, device=dev)
+    W = torch.randn(n_el, Kn, C, dtype=dtype, device=dev)
+    z = torch.randint(0, n_el, (N,), device=dev)
+    _check_derivs(lambda a, w: K.symmetric_contraction(a, w, z, lmax, corr),
+                  lambda a, w: K.symmetric_contraction_torch(a, w, z, lmax, corr), [A, W], tol, tol)
+
+
+def test_neighbor_list_cuda_matches_cpu():
+    from xnn_b200.data.neighborlist import build_neighbor_list
+    for s in synthetic.triclinic_crystals(2, seed=5, labels=False) + [synthetic.water_box(6000)]:
+        a = build_neighbor_list(s["pos"], 5.0, s["cell"], s["pbc"], engine="native")
+        b = build_neighbor_list(s["pos"].cuda(), 5.0, s["cell"].cuda(), s["pbc"], engine="native")
+        ka = torch.unique(torch.cat([a[0].T, a[1]], 1), dim=0)
+        kb = torch.unique(torch.cat([b[0].T.cpu(), b[1].cpu()], 1), dim=0)
+        assert torch.equal(ka, kb)

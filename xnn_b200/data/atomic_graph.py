@@ -54,6 +54,9 @@ class AtomicGraph:
     stress_weight: Optional[Tensor] = None
     atom_force_weight: Optional[Tensor] = None
     compute_dtype: Optional[torch.dtype] = None
+    # "dst" when the edges are grouped by receiver in increasing order (what the
+    # neighbour lists produce and collate keeps); lets the fused kernels skip a sort
+    edge_order: Optional[str] = None
 
     # --- sizes -------------------------------------------------------------------
     @property
@@ -112,7 +115,7 @@ class AtomicGraph:
                   edge_index=new_node[self.edge_index[:, edge_keep]],
                   cell_shifts=self.cell_shifts[edge_keep],
                   batch=new_graph[self.batch[node_keep]], n_atoms=self.n_atoms[keep],
-                  compute_dtype=self.compute_dtype)
+                  compute_dtype=self.compute_dtype, edge_order=self.edge_order)
         for f in fields(self):
             if f.name in kw:
                 continue

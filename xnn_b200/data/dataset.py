@@ -54,7 +54,7 @@ def structure_to_graph(s: Dict, cutoff: float, device=None, max_neighbors: Optio
                     batch=torch.zeros(n, dtype=torch.long, device=device),
                     n_atoms=torch.tensor([n], dtype=torch.long, device=device),
                     cell=None if cell is None else cell[None],
-                    pbc=None if pbc is None else pbc[None])
+                    pbc=None if pbc is None else pbc[None], edge_order="dst")
     if "energy" in s and s["energy"] is not None:
         g.energy = torch.as_tensor([float(s["energy"])], dtype=torch.float64, device=device)
     if "forces" in s and s["forces"] is not None:
@@ -101,7 +101,8 @@ def collate(graphs: Sequence[AtomicGraph]) -> AtomicGraph:
     out = dict(pos=pos, atomic_numbers=torch.cat([g.atomic_numbers for g in graphs]),
                edge_index=edge_index, cell_shifts=torch.cat([g.cell_shifts for g in graphs]),
                batch=batch, n_atoms=torch.cat([g.n_atoms for g in graphs]),
-               compute_dtype=graphs[0].compute_dtype)
+               compute_dtype=graphs[0].compute_dtype,
+               edge_order="dst" if all(g.edge_order == "dst" for g in graphs) else None)
     if any(g.cell is not None for g in graphs):
         out["cell"] = torch.cat([g.cell if g.cell is not None else
                                  pos.new_zeros(g.num_graphs, 3, 3) for g in graphs])
@@ -111,7 +112,7 @@ def collate(graphs: Sequence[AtomicGraph]) -> AtomicGraph:
     skip = set(out) | {"cell", "pbc"} | set(_MASKED.values())
     for f in fields(AtomicGraph):
         name = f.name
-        if name in skip or name == "compute_dtype":
+        if name in skip or name in ("compute_dtype", "edge_order"):
             continue
         vals = [getattr(g, name) for g in graphs]
         if all(v is None for v in vals):

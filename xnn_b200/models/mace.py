@@ -420,7 +420,10 @@ class MACE(GNNPotential):
 
     def forward(self, data: AtomicGraph) -> dict:
         edge_vec = data.edge_vectors()
-        plan = getattr(data, "_edge_plan", None)
+        plan = None
+        if data.edge_order == "dst" and self._fast_active(edge_vec):
+            from ..ops.mace_ops import EdgePlan
+            plan = EdgePlan.build(data.edge_index, data.num_nodes, assume_dst_sorted=True)
         feats, node_energy = self.node_features_energy(data.atomic_numbers, data.edge_index,
                                                        edge_vec, plan)
         return {"node_energy": node_energy, "energy": self.aggregate_energy(node_energy, data),

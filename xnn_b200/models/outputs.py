@@ -15,6 +15,7 @@ import torch
 from torch import Tensor, nn
 
 from ..data import AtomicGraph
+from ..ops.modes import force_pass
 from ..ops.scatter import cell_volume
 
 
@@ -68,9 +69,11 @@ class ForceStressOutput(nn.Module):
             need.append("strain")
         g = {k: None for k in need}
         if inputs and energy.requires_grad:
-            grads = torch.autograd.grad([energy], inputs, grad_outputs=[torch.ones_like(energy)],
-                                        create_graph=create_graph, retain_graph=create_graph,
-                                        allow_unused=True)
+            # only position / strain derivatives are asked for: the fused ops skip the rest
+            with force_pass():
+                grads = torch.autograd.grad([energy], inputs, grad_outputs=[torch.ones_like(energy)],
+                                            create_graph=create_graph, retain_graph=create_graph,
+                                            allow_unused=True)
             g = dict(zip(need, grads))
         if self.compute_forces and not direct:
             out["forces"] = -g["pos"] if g.get("pos") is not None else torch.zeros_like(data.pos)

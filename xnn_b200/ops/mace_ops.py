@@ -64,13 +64,15 @@ class EdgePlan:
         src, dst = edge_index[0], edge_index[1]
         E = int(src.shape[0])
         dev = src.device
-        counts = torch.bincount(dst, minlength=n_nodes)
+        # counts by index_add (no host synchronisation: capturable in a CUDA graph)
+        one = torch.ones(E, dtype=torch.int64, device=dev)
+        counts = torch.zeros(n_nodes, dtype=torch.int64, device=dev).index_add_(0, dst, one)
         dst_ptr = torch.zeros(n_nodes + 1, dtype=torch.int64, device=dev)
         dst_ptr[1:] = torch.cumsum(counts, 0)
         if assume_dst_sorted is None:
             assume_dst_sorted = bool((dst[1:] >= dst[:-1]).all()) if E > 1 else True
         dst_perm = None if assume_dst_sorted else torch.argsort(dst, stable=True)
-        scounts = torch.bincount(src, minlength=n_nodes)
+        scounts = torch.zeros(n_nodes, dtype=torch.int64, device=dev).index_add_(0, src, one)
         src_ptr = torch.zeros(n_nodes + 1, dtype=torch.int64, device=dev)
         src_ptr[1:] = torch.cumsum(scounts, 0)
         src_perm = torch.argsort(src, stable=True)
