@@ -21,11 +21,11 @@ cudaError_t conv_gather(int, int, int, const int64_t*, const int*, const int64_t
                         const T* const*, const T* const*, T*, cudaStream_t);
 template <typename T>
 cudaError_t conv_edge(int, int, int, const int64_t*, const int*, const int64_t*, const T*, int,
-                      const T* const*, const T* const*, int, const T* const*, const T* const*, T*, T*,
+                      const T* const*, const T* const*, T* const*, int, const T* const*, const T* const*, T*, T*,
                       cudaStream_t);
 template <typename T>
-cudaError_t conv_scatter(int, int, int, const int64_t*, const int64_t*, const int*, const T*, int,
-                         const T* const*, const T* const*, T*, cudaStream_t);
+cudaError_t conv_scatter(int, int, int, const int64_t*, const int64_t*, int, const T* const*, const T* const*,
+                         T*, cudaStream_t);
 template <typename T>
 cudaError_t symcon_fwd(int, int, int, int, const T*, const int64_t*, const T*, T*, cudaStream_t);
 template <typename T>
@@ -275,50 +275,65 @@ torch::Tensor conv_gather_op(int64_t N, int64_t C, int64_t P, torch::Tensor dst_
   return A;
 }
 
+// Returns [gR, gY, T_0, T_1] (undefined where not requested). Ys: 0-2 Y terms; xs: per Y term
+// an x for gR or an undefined tensor; want_T: per Y term whether T_t is written; want_gR.
 std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t E, torch::Tensor dst_ptr,
                                         torch::Tensor src, c10::optional<torch::Tensor> perm, torch::Tensor G,
-                                        std::vector<torch::Tensor> xR, std::vector<torch::Tensor> YR,
+                                        std::vector<torch::Tensor> Ys, std::vector<c10::optional<torch::Tensor>> xs,
+                                        std::vector<bool> want_T, bool want_gR,
                                         std::vector<torch::Tensor> xY, std::vector<torch::Tensor> RY) {
-  TORCH_CHECK(xR.size() == YR.size() && xR.size() <= 2, "conv_edge: 0-2 (x, Y) terms for gR");
+  TORCH_CHECK(Ys.size() == xs.size() && Ys.size() == want_T.size() && Ys.size() <= 2,
+              "conv_edge: 0-2 Y terms with matching x / want_T");
   TORCH_CHECK(xY.size() == RY.size() && xY.size() <= 2, "conv_edge: 0-2 (x, R) terms for gY");
   check_cuda(G, "G");
   c10::cuda::CUDAGuard g(G.device());
   const int64_t D = P * P;
   const int64_t cpl = std::min<int64_t>(4, std::max<int64_t>(1, (C + 31) / 32));
   const bool split = (C + 32 * cpl - 1) / (32 * cpl) > 1;
-  torch::Tensor gR = xR.empty() ? torch::Tensor() : torch::empty({E, P, C}, G.options());
+  torch::Tensor gR = (want_gR && !Ys.empty()) ? torch::empty({E, P, C}, G.options()) : torch::Tensor();
   torch::Tensor gY = xY.empty() ? torch::Tensor()
                                 : (split ? torch::zeros({E, D}, G.options()) : torch::empty({E, D}, G.options()));
+  std::vector<torch::Tensor> Ts(2);
+  for (size_t k = 0; k < Ys.size(); ++k)
+    if (want_T[k]) Ts[k] = torch::empty({E, P, C}, G.options());
   auto st = at::cuda::getCurrentCUDAStream();
   AT_DISPATCH_FLOATING_TYPES(G.scalar_type(), "conv_edge", [&] {
-    auto pxR = ptrs<scalar_t>(xR, "x");
-    auto pYR = ptrs<scalar_t>(YR, "Y");
+    auto pY = ptrs<scalar_t>(Ys, "Y");
+    std::vector<const scalar_t*> px;
+    std::vector<scalar_t*> pT;
+    for (size_t k = 0; k < Ys.size(); ++k) {
+      if (xs[k].has_value() && xs[k]->defined()) {
+        check_cuda(*xs[k], "x");
+        px.push_back(xs[k]->data_ptr<scalar_t>());
+      } else {
+        px.push_back(nullptr);
+      }
+      pT.push_back(Ts[k].defined() ? Ts[k].data_ptr<scalar_t>() : nullptr);
+    }
     auto pxY = ptrs<scalar_t>(xY, "x");
     auto pRY = ptrs<scalar_t>(RY, "R");
     XNN_CUDA_OK(conv_edge<scalar_t>((int)N, (int)C, (int)P, dst_ptr.data_ptr<int64_t>(), src.data_ptr<int>(),
                                     perm.has_value() && perm->defined() ? perm->data_ptr<int64_t>() : nullptr,
-                                    G.data_ptr<scalar_t>(), (int)xR.size(), pxR.data(), pYR.data(),
+                                    G.data_ptr<scalar_t>(), (int)Ys.size(), pY.data(), px.data(), pT.data(),
                                     (int)xY.size(), pxY.data(), pRY.data(),
                                     gR.defined() ? gR.data_ptr<scalar_t>() : nullptr,
                                     gY.defined() ? gY.data_ptr<scalar_t>() : nullptr, st));
   });
-  return {gR, gY};
+  return {gR, gY, Ts[0], Ts[1]};
 }
 
 torch::Tensor conv_scatter_op(int64_t N, int64_t C, int64_t P, torch::Tensor src_ptr, torch::Tensor src_perm,
-                              torch::Tensor dst, torch::Tensor G, std::vector<torch::Tensor> Rs,
-                              std::vector<torch::Tensor> Ys) {
-  TORCH_CHECK(Rs.size() == Ys.size() && !Rs.empty() && Rs.size() <= 2, "conv_scatter: 1-2 (R, Y) terms");
-  check_cuda(G, "G");
-  c10::cuda::CUDAGuard g(G.device());
-  auto gx = torch::empty({N, C}, G.options());
+                              std::vector<torch::Tensor> as, std::vector<torch::Tensor> bs) {
+  TORCH_CHECK(as.size() == bs.size() && !as.empty() && as.size() <= 2, "conv_scatter: 1-2 (a, b) terms");
+  c10::cuda::CUDAGuard g(as[0].device());
+  auto gx = torch::empty({N, C}, as[0].options());
   auto st = at::cuda::getCurrentCUDAStream();
-  AT_DISPATCH_FLOATING_TYPES(G.scalar_type(), "conv_scatter", [&] {
-    auto pR = ptrs<scalar_t>(Rs, "R");
-    auto pY = ptrs<scalar_t>(Ys, "Y");
+  AT_DISPATCH_FLOATING_TYPES(as[0].scalar_type(), "conv_scatter", [&] {
+    auto pa = ptrs<scalar_t>(as, "a");
+    auto pb = ptrs<scalar_t>(bs, "b");
     XNN_CUDA_OK(conv_scatter<scalar_t>((int)N, (int)C, (int)P, src_ptr.data_ptr<int64_t>(),
-                                       src_perm.data_ptr<int64_t>(), dst.data_ptr<int>(), G.data_ptr<scalar_t>(),
-                                       (int)Rs.size(), pR.data(), pY.data(), gx.data_ptr<scalar_t>(), st));
+                                       src_perm.data_ptr<int64_t>(), (int)as.size(), pa.data(), pb.data(),
+                                       gx.data_ptr<scalar_t>(), st));
   });
   return gx;
 }
@@ -378,7 +393,10 @@ std::vector<torch::Tensor> symcon_bwd2_op(torch::Tensor A, torch::Tensor z, torc
 
 }  // namespace
 
+void register_comm(pybind11::module& m);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  register_comm(m);
   m.attr("HAS_CUDA") = true;
   m.def("neighbor_list", &neighbor_list, "cell-list neighbour search (CUDA or OpenMP)");
   m.def("edge_geometry_fwd", &edge_geometry_fwd);

@@ -15,10 +15,11 @@
 //
 // Layouts: x (N, C); R (E, P, C); Y (E, P*P); G and A (P*P, N, C) component-major, so the
 // per-degree channel mixing that follows is one plain matrix product per degree.
-// Mapping: one warp per atom, lanes over channels (CPL channels per lane), receivers
-// through the CSR of edges grouped by receiver, senders through a permutation grouped
-// by sender: every sum is a register accumulation, deterministic and atomic-free
-// (except gY when the channels are split over several warps, C > 128).
+// Mapping: one block of four warps per atom, the warps splitting the atom's edges and lanes
+// over channels (CPL channels per lane); receivers through the CSR of edges grouped by
+// receiver, senders through a permutation grouped by sender. Every sum accumulates in
+// registers and meets the other warps' in shared memory in a fixed order: deterministic and
+// atomic-free (except gY when the channels are split over several blocks, C > 128).
 #include "common.cuh"
 
 template <typename T>
@@ -36,14 +37,16 @@ struct PairTerms {  // per term: two operands (meaning depends on the kernel)
   int n;
 };
 
-template <typename T, int P, int CPL>
-__global__ void __launch_bounds__(128) conv_gather_kernel(
+// One block of WPA warps per receiver; warp w takes the receiver's edges j0+w, j0+w+WPA, ...
+// and the warps' partial sums meet in shared memory (fixed order: deterministic).
+template <typename T, int P, int CPL, int WPA>
+__global__ void __launch_bounds__(32 * WPA) conv_gather_kernel(
     int N, int C, const int64_t* __restrict__ dst_ptr, const int* __restrict__ src,
     const int64_t* __restrict__ perm, GatherTerms<T> t, T* __restrict__ A) {
   constexpr int D = P * P;
-  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int i = blockIdx.x;
+  const int w = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (i >= N) return;
   const int cbase = blockIdx.y * 32 * CPL;
   T acc[CPL][D];
 #pragma unroll
@@ -51,7 +54,7 @@ __global__ void __launch_bounds__(128) conv_gather_kernel(
 #pragma unroll
     for (int d = 0; d < D; ++d) acc[q][d] = T(0);
   const int64_t j0 = dst_ptr[i], j1 = dst_ptr[i + 1];
-  for (int64_t j = j0; j < j1; ++j) {
+  for (int64_t j = j0 + w; j < j1; j += WPA) {
     const int64_t e = perm ? perm[j] : j;
     const int64_t s = src[e];
 #pragma unroll
@@ -76,6 +79,25 @@ __global__ void __launch_bounds__(128) conv_gather_kernel(
       }
     }
   }
+  // reduce over the warps: shared [WPA-1][D][32*CPL]
+  extern __shared__ unsigned char smem_raw[];
+  T* red = reinterpret_cast<T*>(smem_raw);
+  if (WPA > 1) {
+    if (w > 0) {
+#pragma unroll
+      for (int q = 0; q < CPL; ++q)
+#pragma unroll
+        for (int d = 0; d < D; ++d) red[((w - 1) * D + d) * 32 * CPL + q * 32 + lane] = acc[q][d];
+    }
+    __syncthreads();
+    if (w != 0) return;
+#pragma unroll
+    for (int ww = 1; ww < WPA; ++ww)
+#pragma unroll
+      for (int q = 0; q < CPL; ++q)
+#pragma unroll
+        for (int d = 0; d < D; ++d) acc[q][d] += red[((ww - 1) * D + d) * 32 * CPL + q * 32 + lane];
+  }
 #pragma unroll
   for (int q = 0; q < CPL; ++q) {
     const int c = cbase + lane + 32 * q;
@@ -86,17 +108,29 @@ __global__ void __launch_bounds__(128) conv_gather_kernel(
   }
 }
 
-// gR (terms a = x, b = Y) and gY (terms a = x, b = R) of the edges into each receiver;
-// G of the receiver is read once into registers.
-template <typename T, int P, int CPL>
-__global__ void __launch_bounds__(128) conv_edge_kernel(
+// Per edge into each receiver (G of the receiver read once into registers):
+//   T_t[e, l, c] = sum_m G[lm, d, c] * Y_t[e, lm]              (written when tT.out[t])
+//   gR[e, l, c]  = sum_t x_t[s, c] * T_t[e, l, c]             (terms with x_t given)
+//   gY[e, lm]    = sum_c G[lm, d, c] * sum_t R_t[e, l, c] x_t[s, c]
+// T is the sender-independent half of dPhi/dx and dPhi/dR: the sender sums of dPhi/dx are
+// then a streaming product of T with R (conv_scatter_kernel).
+template <typename T>
+struct EdgeTerms {
+  const T* Y[2];   // (E, D) per term
+  const T* x[2];   // (N, C) per term, or null (no gR contribution)
+  T* Tout[2];      // (E, P, C) per term, or null
+  int n;
+};
+
+template <typename T, int P, int CPL, int WPA>
+__global__ void __launch_bounds__(32 * WPA) conv_edge_kernel(
     int N, int C, const int64_t* __restrict__ dst_ptr, const int* __restrict__ src,
-    const int64_t* __restrict__ perm, const T* __restrict__ G, PairTerms<T> tR, PairTerms<T> tY,
+    const int64_t* __restrict__ perm, const T* __restrict__ G, EdgeTerms<T> tE, PairTerms<T> tY,
     T* __restrict__ gR, T* __restrict__ gY, int atomic_gY) {
   constexpr int D = P * P;
-  const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int i = blockIdx.x;
+  const int w = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (i >= N) return;
   const int cbase = blockIdx.y * 32 * CPL;
   T g[CPL][D];
 #pragma unroll
@@ -106,10 +140,10 @@ __global__ void __launch_bounds__(128) conv_edge_kernel(
     for (int d = 0; d < D; ++d) g[q][d] = c < C ? __ldg(G + ((int64_t)d * N + i) * C + c) : T(0);
   }
   const int64_t j0 = dst_ptr[i], j1 = dst_ptr[i + 1];
-  for (int64_t j = j0; j < j1; ++j) {
+  for (int64_t j = j0 + w; j < j1; j += WPA) {
     const int64_t e = perm ? perm[j] : j;
     const int64_t s = src[e];
-    if (tR.n > 0) {
+    if (tE.n > 0) {
       T out[CPL][P];
 #pragma unroll
       for (int q = 0; q < CPL; ++q)
@@ -117,32 +151,35 @@ __global__ void __launch_bounds__(128) conv_edge_kernel(
         for (int l = 0; l < P; ++l) out[q][l] = T(0);
 #pragma unroll
       for (int tt = 0; tt < 2; ++tt) {
-        if (tt < tR.n) {
+        if (tt < tE.n) {
           T y[D];
 #pragma unroll
-          for (int d = 0; d < D; ++d) y[d] = __ldg(tR.b[tt] + e * D + d);
+          for (int d = 0; d < D; ++d) y[d] = __ldg(tE.Y[tt] + e * D + d);
 #pragma unroll
           for (int q = 0; q < CPL; ++q) {
             const int c = cbase + lane + 32 * q;
             if (c < C) {
-              const T xv = __ldg(tR.a[tt] + s * C + c);
+              const T xv = tE.x[tt] ? __ldg(tE.x[tt] + s * C + c) : T(0);
 #pragma unroll
               for (int l = 0; l < P; ++l) {
                 T sm = T(0);
 #pragma unroll
                 for (int m = 0; m < 2 * l + 1; ++m) sm += g[q][l * l + m] * y[l * l + m];
+                if (tE.Tout[tt]) tE.Tout[tt][(e * P + l) * C + c] = sm;
                 out[q][l] += xv * sm;
               }
             }
           }
         }
       }
+      if (gR != nullptr) {
 #pragma unroll
-      for (int q = 0; q < CPL; ++q) {
-        const int c = cbase + lane + 32 * q;
-        if (c < C) {
+        for (int q = 0; q < CPL; ++q) {
+          const int c = cbase + lane + 32 * q;
+          if (c < C) {
 #pragma unroll
-          for (int l = 0; l < P; ++l) gR[(e * P + l) * C + c] = out[q][l];
+            for (int l = 0; l < P; ++l) gR[(e * P + l) * C + c] = out[q][l];
+          }
         }
       }
     }
@@ -178,60 +215,56 @@ __global__ void __launch_bounds__(128) conv_edge_kernel(
   }
 }
 
-// gx of every sender (terms a = R, b = Y), edges through the sender permutation.
-template <typename T, int P, int CPL>
-__global__ void __launch_bounds__(128) conv_scatter_kernel(
+// gx[s, c] = sum over the edges out of s of sum_l sum_t a_t[e, l, c] * b_t[e, l, c]
+// (a_t, b_t both (E, P, C): R and T of conv_edge_kernel); streaming, edges via the sender permutation.
+template <typename T, int P, int CPL, int WPA>
+__global__ void __launch_bounds__(32 * WPA) conv_scatter_kernel(
     int N, int C, const int64_t* __restrict__ src_ptr, const int64_t* __restrict__ src_perm,
-    const int* __restrict__ dst, const T* __restrict__ G, PairTerms<T> t, T* __restrict__ gx) {
-  constexpr int D = P * P;
-  const int s = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    PairTerms<T> t, T* __restrict__ gx) {
+  const int s = blockIdx.x;
+  const int w = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  if (s >= N) return;
   const int cbase = blockIdx.y * 32 * CPL;
   T acc[CPL];
 #pragma unroll
   for (int q = 0; q < CPL; ++q) acc[q] = T(0);
   const int64_t j0 = src_ptr[s], j1 = src_ptr[s + 1];
-  for (int64_t j = j0; j < j1; ++j) {
+  for (int64_t j = j0 + w; j < j1; j += WPA) {
     const int64_t e = src_perm[j];
-    const int64_t d = dst[e];
-    T gd[CPL][D];
-#pragma unroll
-    for (int q = 0; q < CPL; ++q) {
-      const int c = cbase + lane + 32 * q;
-#pragma unroll
-      for (int k = 0; k < D; ++k) gd[q][k] = c < C ? __ldg(G + ((int64_t)k * N + d) * C + c) : T(0);
-    }
 #pragma unroll
     for (int tt = 0; tt < 2; ++tt) {
       if (tt < t.n) {
-        T y[D];
-#pragma unroll
-        for (int k = 0; k < D; ++k) y[k] = __ldg(t.b[tt] + e * D + k);
 #pragma unroll
         for (int q = 0; q < CPL; ++q) {
           const int c = cbase + lane + 32 * q;
           if (c < C) {
 #pragma unroll
             for (int l = 0; l < P; ++l) {
-              T sm = T(0);
-#pragma unroll
-              for (int m = 0; m < 2 * l + 1; ++m) sm += gd[q][l * l + m] * y[l * l + m];
-              acc[q] += __ldg(t.a[tt] + (e * P + l) * C + c) * sm;
+              const int64_t o = (e * P + l) * C + c;
+              acc[q] += __ldg(t.a[tt] + o) * __ldg(t.b[tt] + o);
             }
           }
         }
       }
     }
   }
+  __shared__ T red[WPA][32 * CPL];
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) red[w][q * 32 + lane] = acc[q];
+  __syncthreads();
+  if (w != 0) return;
 #pragma unroll
   for (int q = 0; q < CPL; ++q) {
+    T v = red[0][q * 32 + lane];
+#pragma unroll
+    for (int ww = 1; ww < WPA; ++ww) v += red[ww][q * 32 + lane];
     const int c = cbase + lane + 32 * q;
-    if (c < C) gx[(int64_t)s * C + c] = acc[q];
+    if (c < C) gx[(int64_t)s * C + c] = v;
   }
 }
 
 namespace {
+constexpr int kWPA = 4;  // warps per atom
 inline int cpl_for(int C) {
   const int c = (C + 31) / 32;
   return c > 4 ? 4 : (c < 1 ? 1 : c);
@@ -273,46 +306,48 @@ cudaError_t conv_gather(int N, int C, int P, const int64_t* dst_ptr, const int* 
     t.Y[k] = k < nterms ? Y[k] : nullptr;
   }
   const int cpl = cpl_for(C);
-  dim3 grid((N + 3) / 4, (C + 32 * cpl - 1) / (32 * cpl));
-  XNN_P_CPL_SWITCH(P, cpl, conv_gather_kernel<T, PP, QQ><<<grid, 128, 0, stream>>>(N, C, dst_ptr, src, perm, t, A));
+  dim3 grid(N, (C + 32 * cpl - 1) / (32 * cpl));
+  const size_t smem = (size_t)(kWPA - 1) * P * P * 32 * cpl * sizeof(T);
+  XNN_P_CPL_SWITCH(P, cpl, conv_gather_kernel<T, PP, QQ, kWPA><<<grid, 32 * kWPA, smem, stream>>>(N, C, dst_ptr, src, perm, t, A));
   return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t conv_edge(int N, int C, int P, const int64_t* dst_ptr, const int* src, const int64_t* perm,
-                      const T* G, int nR, const T* const* xR, const T* const* YR, int nY,
-                      const T* const* xY, const T* const* RY, T* gR, T* gY, cudaStream_t stream) {
+                      const T* G, int nE, const T* const* Ys, const T* const* xs, T* const* Touts,
+                      int nY, const T* const* xY, const T* const* RY, T* gR, T* gY, cudaStream_t stream) {
   if (N == 0) return cudaSuccess;
-  if (nR < 0 || nR > 2 || nY < 0 || nY > 2) return cudaErrorInvalidValue;
-  PairTerms<T> tR, tY;
-  tR.n = nR; tY.n = nY;
+  if (nE < 0 || nE > 2 || nY < 0 || nY > 2) return cudaErrorInvalidValue;
+  EdgeTerms<T> tE;
+  PairTerms<T> tY;
+  tE.n = nE; tY.n = nY;
   for (int k = 0; k < 2; ++k) {
-    tR.a[k] = k < nR ? xR[k] : nullptr; tR.b[k] = k < nR ? YR[k] : nullptr;
+    tE.Y[k] = k < nE ? Ys[k] : nullptr; tE.x[k] = k < nE ? xs[k] : nullptr;
+    tE.Tout[k] = k < nE ? Touts[k] : nullptr;
     tY.a[k] = k < nY ? xY[k] : nullptr; tY.b[k] = k < nY ? RY[k] : nullptr;
   }
   const int cpl = cpl_for(C);
   const int gy = (C + 32 * cpl - 1) / (32 * cpl);
-  dim3 grid((N + 3) / 4, gy);
+  dim3 grid(N, gy);
   const int atomic_gY = gy > 1 ? 1 : 0;
-  XNN_P_CPL_SWITCH(P, cpl, conv_edge_kernel<T, PP, QQ><<<grid, 128, 0, stream>>>(N, C, dst_ptr, src, perm, G, tR, tY, gR, gY, atomic_gY));
+  XNN_P_CPL_SWITCH(P, cpl, conv_edge_kernel<T, PP, QQ, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, dst_ptr, src, perm, G, tE, tY, gR, gY, atomic_gY));
   return cudaGetLastError();
 }
 
 template <typename T>
-cudaError_t conv_scatter(int N, int C, int P, const int64_t* src_ptr, const int64_t* src_perm,
-                         const int* dst, const T* G, int nterms, const T* const* R,
-                         const T* const* Y, T* gx, cudaStream_t stream) {
+cudaError_t conv_scatter(int N, int C, int P, const int64_t* src_ptr, const int64_t* src_perm, int nterms,
+                         const T* const* a, const T* const* b, T* gx, cudaStream_t stream) {
   if (N == 0) return cudaSuccess;
   if (nterms < 1 || nterms > 2) return cudaErrorInvalidValue;
   PairTerms<T> t;
   t.n = nterms;
   for (int k = 0; k < 2; ++k) {
-    t.a[k] = k < nterms ? R[k] : nullptr;
-    t.b[k] = k < nterms ? Y[k] : nullptr;
+    t.a[k] = k < nterms ? a[k] : nullptr;
+    t.b[k] = k < nterms ? b[k] : nullptr;
   }
   const int cpl = cpl_for(C);
-  dim3 grid((N + 3) / 4, (C + 32 * cpl - 1) / (32 * cpl));
-  XNN_P_CPL_SWITCH(P, cpl, conv_scatter_kernel<T, PP, QQ><<<grid, 128, 0, stream>>>(N, C, src_ptr, src_perm, dst, G, t, gx));
+  dim3 grid(N, (C + 32 * cpl - 1) / (32 * cpl));
+  XNN_P_CPL_SWITCH(P, cpl, conv_scatter_kernel<T, PP, QQ, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, src_ptr, src_perm, t, gx));
   return cudaGetLastError();
 }
 
@@ -321,10 +356,9 @@ cudaError_t conv_scatter(int N, int C, int P, const int64_t* src_ptr, const int6
                                       const T* const*, const T* const*, const T* const*, T*,          \
                                       cudaStream_t);                                                  \
   template cudaError_t conv_edge<T>(int, int, int, const int64_t*, const int*, const int64_t*,       \
-                                    const T*, int, const T* const*, const T* const*, int,            \
-                                    const T* const*, const T* const*, T*, T*, cudaStream_t);         \
-  template cudaError_t conv_scatter<T>(int, int, int, const int64_t*, const int64_t*, const int*,    \
-                                       const T*, int, const T* const*, const T* const*, T*,          \
-                                       cudaStream_t);
+                                    const T*, int, const T* const*, const T* const*, T* const*, int,  \
+                                    const T* const*, const T* const*, T*, T*, cudaStream_t);          \
+  template cudaError_t conv_scatter<T>(int, int, int, const int64_t*, const int64_t*, int,           \
+                                       const T* const*, const T* const*, T*, cudaStream_t);
 XNN_INST(float)
 XNN_INST(double)

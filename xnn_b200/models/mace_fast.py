@@ -22,6 +22,7 @@ from torch import Tensor
 from torch.nn import functional as F
 
 from ..ops import mace_ops as K
+from ..ops.radial import radial_network
 from ..ops.scatter import refresh_ghosts
 
 
@@ -69,7 +70,18 @@ def radial_mlp(net, rad: Tensor, col_scale: Optional[Tensor] = None) -> Tensor:
 
 
 def _conv_path_scale(blk, like: Tensor) -> Tensor:
-    """Per output column of the radial net, the tensor product's path coefficient ``w * CG(0,l,l)``."""
+    """Per output column of the radial net, the tensor product's path coefficient ``w * CG(0,l,l)``.
+
+    Cached per device and dtype on the block (built outside any CUDA-graph capture).
+    """
+    cache = blk.__dict__.setdefault("_fast_consts", {})
+    key = ("path_scale", like.device, like.dtype)
+    if key not in cache:
+        cache[key] = _conv_path_scale_build(blk).to(like)
+    return cache[key]
+
+
+def _conv_path_scale_build(blk) -> Tensor:
     from ..o3 import wigner_3j
     tp = blk.conv_tp
     C = tp.irreps_in1[0].mul
@@ -78,7 +90,7 @@ def _conv_path_scale(blk, like: Tensor) -> Tensor:
         l = tp.irreps_in2[ins.i_in2].ir.l
         cg = float(wigner_3j(0, l, l, dtype=torch.float64)[0, 0, 0]) * (2 * l + 1) ** 0.5
         scales.append(torch.full((C,), ins.path_weight * cg / (2 * l + 1) ** 0.5, dtype=torch.float64))
-    return torch.cat(scales).to(like)
+    return torch.cat(scales)
 
 
 def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor, edge_vec: Tensor,
@@ -91,7 +103,8 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
     ef = model.edge_feat
     lmax = model.max_ell
     P = lmax + 1
-    Y, rad = K.edge_geometry(edge_vec, lmax, ef.rbf.freqs, ef.rbf.norm, ef.cutoff, ef.envelope.p)
+    Y, _ = K.edge_geometry(edge_vec, lmax, ef.rbf.freqs, ef.rbf.norm, ef.cutoff, ef.envelope.p)
+    r = torch.linalg.norm(edge_vec, dim=-1)
     n_el = len(model.species)
     C = model.num_features
     emb = model.node_embedding
@@ -103,7 +116,8 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
             h = refresh_ghosts(h)
         sc = species_linear(h, z, _species_weights(blk.skip_tp, n_el)) if blk.residual else None
         h_up = h @ _linear_blocks(blk.linear_up)[0]
-        R = radial_mlp(blk.conv_tp_weights, rad, _conv_path_scale(blk, rad)).view(-1, P, C)
+        R = radial_network(r, blk.conv_tp_weights, _conv_path_scale(blk, r), ef.rbf.freqs, ef.rbf.norm,
+                           ef.cutoff, ef.envelope.p).view(-1, P, C)
         A = K.conv(h_up, R, Y, plan)                                   # (D, N, C)
         mats = _linear_blocks(blk.linear)
         parts = []

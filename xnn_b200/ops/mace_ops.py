@@ -205,27 +205,25 @@ class _Conv(Function):
 class _ConvVJP(Function):
     @staticmethod
     def forward(ctx, G, x, R, Y, plan, need):
+        # T1[e, l, c] = sum_m G[lm, d, c] Y[e, lm]: gR = x[s] * T1, gx = sum_{e out of s} sum_l R * T1;
+        # kept for the second derivative
         nx, nR, nY = need
         N, C, P = plan.n_nodes, x.shape[1], R.shape[1]
         G = G.contiguous()
-        gx = gR = gY = None
         K = _C()
-        if nx:
-            gx = K.conv_scatter(N, C, P, plan.src_ptr, plan.src_perm, plan.dst32, G, [R], [Y])
-        if nR or nY:
-            gR, gY = K.conv_edge(N, C, P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm, G,
-                                 [x] if nR else [], [Y] if nR else [], [x] if nY else [], [R] if nY else [])
-            gR = gR if nR else None
-            gY = gY if nY else None
-        ctx.save_for_backward(G, x, R, Y)
+        gR, gY, T1, _ = K.conv_edge(N, C, P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm, G,
+                                    [Y], [x if nR else None], [True], bool(nR),
+                                    [x] if nY else [], [R] if nY else [])
+        gx = K.conv_scatter(N, C, P, plan.src_ptr, plan.src_perm, [R], [T1]) if nx else None
+        ctx.save_for_backward(G, x, R, Y, T1)
         ctx.plan = plan
         ctx.set_materialize_grads(False)
-        return gx, gR, gY
+        return gx, (gR if nR else None), (gY if nY else None)
 
     @staticmethod
     @once_differentiable
     def backward(ctx, ux, uR, uY):
-        G, x, R, Y = ctx.saved_tensors
+        G, x, R, Y, T1 = ctx.saved_tensors
         plan = ctx.plan
         N, C, P = plan.n_nodes, x.shape[1], R.shape[1]
         K = _C()
@@ -243,28 +241,33 @@ class _ConvVJP(Function):
                     xs.append(tx); Rs.append(tR); Ys.append(tY)
             if xs:
                 cG = K.conv_gather(N, C, P, plan.dst_ptr, plan.src32, plan.dst_perm, xs, Rs, Ys)
+        # edge terms: (Y, ux) gives ux*T1 to cot_R; (uY, x) gives x*T2 to cot_R and T2 for cot_x
+        Ys, xs, wT = [], [], []
+        if nR and ux is not None:
+            Ys.append(Y); xs.append(ux); wT.append(False)
+        if uY is not None and (nR or nx):
+            Ys.append(uY); xs.append(x if nR else None); wT.append(bool(nx))
+        xY, RY = [], []
+        if nY:
+            for tx, tR in ((ux, R), (x, uR)):
+                if tx is not None and tR is not None:
+                    xY.append(tx); RY.append(tR)
+        T2 = None
+        if Ys or xY:
+            a, b, t0, t1 = K.conv_edge(N, C, P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm, G,
+                                       Ys, xs, wT, bool(nR) and any(v is not None for v in xs), xY, RY)
+            cR = a if (nR and any(v is not None for v in xs)) else None
+            cY = b if xY else None
+            if uY is not None and nx:
+                T2 = t1 if len(Ys) == 2 else t0
         if nx:
-            Rs, Ys = [], []
-            for tR, tY in ((uR, Y), (R, uY)):
-                if tR is not None and tY is not None:
-                    Rs.append(tR); Ys.append(tY)
-            if Rs:
-                cx = K.conv_scatter(N, C, P, plan.src_ptr, plan.src_perm, plan.dst32, G, Rs, Ys)
-        if nR or nY:
-            xR, YR, xY, RY = [], [], [], []
-            if nR:
-                for tx, tY in ((ux, Y), (x, uY)):
-                    if tx is not None and tY is not None:
-                        xR.append(tx); YR.append(tY)
-            if nY:
-                for tx, tR in ((ux, R), (x, uR)):
-                    if tx is not None and tR is not None:
-                        xY.append(tx); RY.append(tR)
-            if xR or xY:
-                a, b = K.conv_edge(N, C, P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm, G,
-                                   xR, YR, xY, RY)
-                cR = a if xR else None
-                cY = b if xY else None
+            As, Bs = [], []
+            if uR is not None:
+                As.append(uR); Bs.append(T1)
+            if T2 is not None:
+                As.append(R); Bs.append(T2)
+            if As:
+                cx = K.conv_scatter(N, C, P, plan.src_ptr, plan.src_perm, As, Bs)
         return cG, cx, cR, cY, None, None
 
 

@@ -5,14 +5,18 @@ A force-loss training step differentiates twice. In the force pass
 (``loss.backward(inputs=params)``) no cotangent of a purely geometric input (the edge
 vectors and their features) is used. The fused ops read these flags and skip that work;
 a caller that needs full derivatives (Hessians, vibrations) simply does not set them.
+
+The flags are process-wide, not thread-local: PyTorch runs the backward functions of CUDA
+tensors on its own autograd worker thread, which would not see a thread-local value set by
+the caller. A flag is only set around a synchronous autograd call, so within a process the
+backward that reads it is the one its caller started.
 """
 from __future__ import annotations
 
 import contextlib
-import threading
 
 
-class _Modes(threading.local):
+class _Modes:
     def __init__(self):
         self.force_pass = False
         self.params_only = False

@@ -1,0 +1,208 @@
+"""The per-edge radial network of MACE / NequIP, differentiated forward-mode along the edge length.
+
+The network ``R(r) = MLP(rad(r))`` depends on the edge vector only through its length ``r``
+(``rad`` is the enveloped Bessel basis). The forward pass therefore carries the tangent
+``dR/dr`` next to ``R``: primal and tangent rows are stacked, so every layer is one matrix
+product over ``2E`` rows, and the activation couples the halves
+(``h = c f(a)``, ``h' = c f'(a) a'``). Consequences for a force-loss step:
+
+* force pass: ``dE/dr = sum_j gR[e, j] dR/dr[e, j]`` -- no matrix product at all;
+* parameter pass: the energy term is one reverse sweep over the primal rows; the force term is
+  one reverse sweep of the stacked network with cotangent ``u_r gR`` on the tangent rows, whose
+  activation derivative brings in ``f''``.
+
+Weights are the e3nn-layout ``layer{k}.weight`` parameters; the per-layer normalisation
+factors and constants are applied inside (``FullyConnectedNet.folded``), the per-column
+scale of the last layer carries the tensor-product path coefficients.
+The matrix products run on :mod:`xnn_b200.ops.gemm` (tcgen05 on sm_100a when available).
+"""
+from __future__ import annotations
+
+import math
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+from torch import Tensor
+from torch.autograd import Function
+from torch.autograd.function import once_differentiable
+
+from .modes import MODES
+
+
+def _silu_d(a: Tensor):
+    s = torch.sigmoid(a)
+    f = a * s
+    f1 = s * (1.0 + a * (1.0 - s))
+    f2 = s * (1.0 - s) * (2.0 + a * (1.0 - 2.0 * s))
+    return f, f1, f2
+
+
+def bessel_envelope(r: Tensor, freqs: Tensor, norm: float, rc: float, p: int) -> Tuple[Tensor, Tensor]:
+    """``rad (E, n)`` and ``d rad / dr`` of ``norm sin(f r / rc) / r * env(r / rc)``."""
+    rcl = r.clamp(min=1e-8)[:, None]
+    w = freqs / rc
+    s, c = torch.sin(w * rcl), torch.cos(w * rcl)
+    b = norm * s / rcl
+    db = norm * (w * c / rcl - s / (rcl * rcl))
+    x = (r / rc)[:, None]
+    a0, a1, a2 = -(p + 1) * (p + 2) / 2.0, p * (p + 2.0), -p * (p + 1) / 2.0
+    xp = x ** p
+    env = 1.0 + xp * (a0 + x * (a1 + a2 * x))
+    denv = (xp / x.clamp(min=1e-30)) * (p * a0 + x * ((p + 1) * a1 + (p + 2) * a2 * x)) / rc
+    inside = (r < rc)[:, None].to(r.dtype)
+    return b * env * inside, (db * env + b * denv) * inside
+
+
+class RadialSpec:
+    """Constants of one folded e3nn MLP: factor and activation constant per layer, column scale."""
+
+    def __init__(self, net, col_scale: Optional[Tensor], freqs: Tensor, norm: float, rc: float, p: int):
+        layers = net.folded()
+        for _, _, act, _ in layers[:-1]:
+            if act is not torch.nn.functional.silu:
+                raise NotImplementedError("the fused radial network supports SiLU hidden layers")
+        if layers[-1][2] is not None:
+            raise NotImplementedError("the fused radial network has a linear output layer")
+        self.factors = [float(f) for _, f, _, _ in layers]
+        self.consts = [float(c) for _, _, _, c in layers[:-1]]
+        self.col_scale = col_scale
+        self.freqs, self.norm, self.rc, self.p = freqs, float(norm), float(rc), int(p)
+
+
+def _eff(Ws: Sequence[Tensor], spec: RadialSpec) -> List[Tensor]:
+    out = [W * f for W, f in zip(Ws, spec.factors)]
+    if spec.col_scale is not None:
+        out[-1] = out[-1] * spec.col_scale
+    return out
+
+
+def _forward(r: Tensor, We: List[Tensor], spec: RadialSpec):
+    E = r.shape[0]
+    rad, drad = bessel_envelope(r, spec.freqs.to(r.dtype), spec.norm, spec.rc, spec.p)
+    H = torch.cat([rad, drad], 0)
+    acts = []
+    for k in range(len(We) - 1):
+        A = H @ We[k]
+        a, ad = A[:E], A[E:]
+        f, f1, _ = _silu_d(a)
+        c = spec.consts[k]
+        H = torch.cat([c * f, c * f1 * ad], 0)
+        acts.append(A)
+    out = H @ We[-1]
+    return out[:E], out[E:], acts, rad, drad
+
+
+def _reverse(r: Tensor, We: List[Tensor], spec: RadialSpec, acts: List[Tensor], rad: Tensor, drad: Tensor,
+             dR: Optional[Tensor], dRd: Optional[Tensor]) -> List[Tensor]:
+    """Gradients of the effective weights for cotangents ``dR`` (primal rows) and ``dRd`` (tangent rows)."""
+    E = r.shape[0]
+    z = None
+    if dR is None:
+        dR = torch.zeros_like(dRd)
+    if dRd is None:
+        dRd = torch.zeros_like(dR)
+    # hidden outputs per layer, stacked
+    Hs = [torch.cat([rad, drad], 0)]
+    for k, A in enumerate(acts):
+        a, ad = A[:E], A[E:]
+        f, f1, _ = _silu_d(a)
+        c = spec.consts[k]
+        Hs.append(torch.cat([c * f, c * f1 * ad], 0))
+    D = torch.cat([dR, dRd], 0)                   # cotangent of the stacked output
+    grads = [None] * len(We)
+    grads[-1] = Hs[-1].t() @ D
+    dH = D @ We[-1].t()
+    for k in range(len(acts) - 1, -1, -1):
+        A = acts[k]
+        a, ad = A[:E], A[E:]
+        _, f1, f2 = _silu_d(a)
+        c = spec.consts[k]
+        dh, dhd = dH[:E], dH[E:]
+        da = c * (dh * f1 + dhd * f2 * ad)
+        dad = c * dhd * f1
+        DA = torch.cat([da, dad], 0)
+        grads[k] = Hs[k].t() @ DA
+        if k > 0:
+            dH = DA @ We[k].t()
+    return grads
+
+
+def _raw_grads(gE: List[Tensor], spec: RadialSpec) -> List[Tensor]:
+    out = [g * f for g, f in zip(gE, spec.factors)]
+    if spec.col_scale is not None:
+        out[-1] = out[-1] * spec.col_scale
+    return out
+
+
+class _Radial(Function):
+    @staticmethod
+    def forward(ctx, r, spec, *Ws):
+        We = _eff(Ws, spec)
+        R, Rd, acts, rad, drad = _forward(r, We, spec)
+        ctx.spec = spec
+        ctx.save_for_backward(r, Rd, rad, drad, *acts, *Ws)
+        ctx.n_acts = len(acts)
+        return R
+
+    @staticmethod
+    def backward(ctx, gR):
+        saved = ctx.saved_tensors
+        r, Rd, rad, drad = saved[:4]
+        acts = list(saved[4:4 + ctx.n_acts])
+        Ws = list(saved[4 + ctx.n_acts:])
+        spec = ctx.spec
+        g_r = None
+        if ctx.needs_input_grad[0] and not MODES.params_only:
+            g_r = _RadialVJP.apply(gR, r, Rd, rad, drad, spec, len(acts), *acts, *Ws)
+        gW = [None] * len(Ws)
+        if any(ctx.needs_input_grad[2:]) and not MODES.force_pass:
+            with torch.no_grad():
+                We = _eff(Ws, spec)
+                gE = _reverse(r, We, spec, acts, rad, drad, gR, None)
+                gW = _raw_grads(gE, spec)
+        return (g_r, None, *gW)
+
+
+class _RadialVJP(Function):
+    """``g_r[e] = sum_j gR[e, j] dR/dr[e, j]`` and its derivatives."""
+
+    @staticmethod
+    def forward(ctx, gR, r, Rd, rad, drad, spec, n_acts, *rest):
+        acts = rest[:n_acts]
+        Ws = rest[n_acts:]
+        ctx.spec, ctx.n_acts = spec, n_acts
+        ctx.save_for_backward(gR, r, Rd, rad, drad, *acts, *Ws)
+        return (gR * Rd).sum(-1)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, u):
+        saved = ctx.saved_tensors
+        gR, r, Rd, rad, drad = saved[:5]
+        acts = list(saved[5:5 + ctx.n_acts])
+        Ws = list(saved[5 + ctx.n_acts:])
+        spec = ctx.spec
+        n_in = 7 + len(acts)
+        cot_gR = u[:, None] * Rd if ctx.needs_input_grad[0] else None
+        gW = [None] * len(Ws)
+        if any(ctx.needs_input_grad[n_in:]):
+            We = _eff(Ws, spec)
+            gE = _reverse(r, We, spec, acts, rad, drad, None, u[:, None] * gR)
+            gW = _raw_grads(gE, spec)
+        cot_r = None
+        if ctx.needs_input_grad[1] and not MODES.params_only:
+            # d/dr of sum gR dR/dr: second derivative along r, by autograd on the formulas
+            with torch.enable_grad():
+                rr = r.detach().requires_grad_(True)
+                We = _eff([w.detach() for w in Ws], spec)
+                _, Rd2, _, _, _ = _forward(rr, We, spec)
+                (cot_r,) = torch.autograd.grad((gR * Rd2).sum(-1), rr, u)
+        return (cot_gR, cot_r, None, None, None, None, None) + (None,) * len(acts) + tuple(gW)
+
+
+def radial_network(r: Tensor, net, col_scale: Optional[Tensor], freqs: Tensor, norm: float, rc: float,
+                   p: int) -> Tensor:
+    """``R (E, n_out)`` of the enveloped-Bessel MLP at edge lengths ``r (E,)`` (see module notes)."""
+    spec = RadialSpec(net, col_scale, freqs, norm, rc, p)
+    Ws = [layer.weight for layer in net]
+    return _Radial.apply(r, spec, *Ws)

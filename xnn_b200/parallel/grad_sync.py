@@ -35,12 +35,6 @@ class GradSync:
         # pad to a multiple of 64 elements (256-byte aligned slices per rank)
         align = 64 * max(1, self.world)
         self.padded = (self.numel + align - 1) // align * align
-        self.flat = torch.zeros(self.padded, dtype=self.dtype, device=dev)
-        off = 0
-        for p in self.params:
-            n = p.numel()
-            p.grad = self.flat[off:off + n].view_as(p)
-            off += n
         if backend == "auto":
             backend = "nccl"
         if self.world == 1:
@@ -50,6 +44,14 @@ class GradSync:
         if backend == "p2p":
             from .p2p_allreduce import P2PAllReduce
             self._p2p = P2PAllReduce(self.padded, self.dtype, dev)
+            self.flat = self._p2p.buffer          # the gradients live in peer-mapped memory
+        else:
+            self.flat = torch.zeros(self.padded, dtype=self.dtype, device=dev)
+        off = 0
+        for p in self.params:
+            n = p.numel()
+            p.grad = self.flat[off:off + n].view_as(p)
+            off += n
 
     def rebind(self) -> None:
         """Point every ``.grad`` at the flat buffer again (after something replaced it)."""
