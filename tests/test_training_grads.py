@@ -21,9 +21,11 @@ def _loss_grads(model, batch, flags: bool):
     return loss.detach(), g
 
 
-@pytest.mark.parametrize("device", ["cpu"] + (["cuda"] if torch.cuda.is_available() else []))
-def test_force_loss_gradients_match_reference(device):
-    torch.set_default_dtype(torch.float64)
+@pytest.mark.parametrize("device,dtype,tol", [("cpu", torch.float64, 1e-8),
+                                              pytest.param("cuda", torch.float64, 1e-8, marks=pytest.mark.gpu),
+                                              pytest.param("cuda", torch.float32, 2e-3, marks=pytest.mark.gpu)])
+def test_force_loss_gradients_match_reference(device, dtype, tol):
+    torch.set_default_dtype(dtype)
     try:
         torch.manual_seed(1)
         m = MACE(species=[1, 6, 7, 8, 9, 16, 17], cutoff=4.5, num_channels=8, n_rbf=8, num_interactions=2,
@@ -33,11 +35,12 @@ def test_force_loss_gradients_match_reference(device):
         l1, g1 = _loss_grads(m, b, flags=False)
         m.use_fast = True
         l2, g2 = _loss_grads(m, b, flags=True)
-        torch.testing.assert_close(l1, l2, rtol=1e-10, atol=1e-12)
+        torch.testing.assert_close(l1, l2, rtol=tol, atol=tol * 1e-2)
         for a, c in zip(g1, g2):
             if a is None:
                 assert c is None or c.abs().max() == 0
                 continue
-            torch.testing.assert_close(a, c, rtol=1e-8, atol=1e-10)
+            scale = float(a.abs().max()) + 1e-30
+            assert float((a - c).abs().max()) <= tol * scale + 1e-12
     finally:
         torch.set_default_dtype(torch.float32)

@@ -86,11 +86,139 @@ void p2p_allreduce_op(std::vector<int64_t> bufs, std::vector<int64_t> flags, tor
 
 }  // namespace
 
+void register_gemm(pybind11::module& m);
+void register_radial(pybind11::module& m);
+
 void register_comm(pybind11::module& m) {
+  register_gemm(m);
+  register_radial(m);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
   m.def("mapped_status", &mapped_status);
   m.def("p2p_allreduce", &p2p_allreduce_op);
   m.def("p2p_flag_words", []() { return (int64_t)p2p_flag_words(); });
+}
+
+// ---- tensor-core GEMM ---------------------------------------------------------------------
+cudaError_t gemm_tf32x3(int M, int N, int K, const float* X, int ldx, const float* W, int64_t sk, int64_t sn,
+                        float* Bpack, float* Y, int ldy, const float* col_scale, int* status, long long spin_limit,
+                        cudaStream_t s);
+size_t gemm_rows_pack_floats(int K, int N);
+
+torch::Tensor gemm_tf32x3_op(torch::Tensor X, torch::Tensor W, c10::optional<torch::Tensor> col_scale,
+                             torch::Tensor status, int64_t spin_limit) {
+  TORCH_CHECK(X.is_cuda() && W.is_cuda() && X.scalar_type() == torch::kFloat32 &&
+              W.scalar_type() == torch::kFloat32, "gemm_tf32x3: float32 CUDA operands");
+  TORCH_CHECK(X.dim() == 2 && W.dim() == 2 && X.size(1) == W.size(0), "gemm_tf32x3: shapes");
+  TORCH_CHECK(X.stride(1) == 1, "gemm_tf32x3: X rows must be contiguous");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32, "status: int32 CUDA");
+  c10::cuda::CUDAGuard g(X.device());
+  const int64_t M = X.size(0), K = X.size(1), N = W.size(1);
+  auto Y = torch::empty({M, N}, X.options());
+  auto Bpack = torch::empty({(int64_t)gemm_rows_pack_floats((int)K, (int)N)}, X.options());
+  const float* cs = nullptr;
+  torch::Tensor csc;
+  if (col_scale.has_value() && col_scale->defined()) {
+    csc = col_scale->contiguous();
+    TORCH_CHECK(csc.numel() == N, "col_scale size");
+    cs = csc.data_ptr<float>();
+  }
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaError_t e = gemm_tf32x3((int)M, (int)N, (int)K, X.data_ptr<float>(), (int)X.stride(0), W.data_ptr<float>(),
+                              W.stride(0), W.stride(1), Bpack.data_ptr<float>(), Y.data_ptr<float>(), (int)N, cs,
+                              status.data_ptr<int>(), (long long)spin_limit, st);
+  TORCH_CHECK(e == cudaSuccess, "gemm_tf32x3 failed: ", cudaGetErrorString(e));
+  return Y;
+}
+
+void register_gemm(pybind11::module& m) { m.def("gemm_tf32x3", &gemm_tf32x3_op); }
+
+// ---- reduction GEMM and the radial network's elementwise stages -------------------------------
+cudaError_t gemm_reduce_tf32x3(int M, int K1, int N, const float* X, int ldx, const float* D, int ldd,
+                               int rows_per_cta, float* partial, float* out, float scale, int* status,
+                               long long spin_limit, cudaStream_t s);
+int gemm_reduce_ctas(int M, int rows_per_cta);
+template <typename T>
+cudaError_t radial_basis(int64_t E, int n, const T* r, const T* freqs, T norm, T rc, int p, T* out, cudaStream_t s);
+template <typename T>
+cudaError_t radial_act(int64_t E, int H, const T* A, T c, T* out, cudaStream_t s);
+template <typename T>
+cudaError_t radial_dact(int64_t E, int H, const T* A, const T* dH, T c, int primal_only, T* DA, T* Hout,
+                        cudaStream_t s);
+
+namespace {
+
+torch::Tensor gemm_reduce_op(torch::Tensor X, torch::Tensor D, int64_t rows_per_cta, double scale,
+                             torch::Tensor status, int64_t spin_limit) {
+  TORCH_CHECK(X.is_cuda() && D.is_cuda() && X.scalar_type() == torch::kFloat32 && D.scalar_type() == torch::kFloat32,
+              "gemm_reduce: float32 CUDA operands");
+  TORCH_CHECK(X.dim() == 2 && D.dim() == 2 && X.size(0) == D.size(0), "gemm_reduce: shapes");
+  TORCH_CHECK(X.stride(1) == 1 && D.stride(1) == 1, "gemm_reduce: rows must be contiguous");
+  c10::cuda::CUDAGuard g(X.device());
+  const int64_t M = X.size(0), K1 = X.size(1), N = D.size(1);
+  auto out = torch::empty({K1, N}, X.options());
+  const int ctas = gemm_reduce_ctas((int)M, (int)rows_per_cta);
+  auto partial = torch::empty({std::max(ctas, 1), K1, N}, X.options());
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaError_t e = gemm_reduce_tf32x3((int)M, (int)K1, (int)N, X.data_ptr<float>(), (int)X.stride(0),
+                                     D.data_ptr<float>(), (int)D.stride(0), (int)rows_per_cta,
+                                     partial.data_ptr<float>(), out.data_ptr<float>(), (float)scale,
+                                     status.data_ptr<int>(), (long long)spin_limit, st);
+  TORCH_CHECK(e == cudaSuccess, "gemm_reduce failed: ", cudaGetErrorString(e));
+  return out;
+}
+
+torch::Tensor radial_basis_op(torch::Tensor r, torch::Tensor freqs, double norm, double rc, int64_t p) {
+  TORCH_CHECK(r.is_cuda() && r.is_contiguous() && freqs.is_cuda(), "radial_basis: CUDA tensors");
+  c10::cuda::CUDAGuard g(r.device());
+  const int64_t E = r.size(0), n = freqs.numel();
+  auto out = torch::empty({2 * E, n}, r.options());
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(r.scalar_type(), "radial_basis", [&] {
+    auto fr = freqs.to(r.scalar_type()).contiguous();
+    TORCH_CHECK(radial_basis<scalar_t>(E, (int)n, r.data_ptr<scalar_t>(), fr.data_ptr<scalar_t>(), (scalar_t)norm,
+                                       (scalar_t)rc, (int)p, out.data_ptr<scalar_t>(), st) == cudaSuccess,
+                "radial_basis launch");
+  });
+  return out;
+}
+
+torch::Tensor radial_act_op(torch::Tensor A, double c) {
+  TORCH_CHECK(A.is_cuda() && A.is_contiguous() && A.size(0) % 2 == 0, "radial_act: stacked CUDA rows");
+  c10::cuda::CUDAGuard g(A.device());
+  const int64_t E = A.size(0) / 2, H = A.size(1);
+  auto out = torch::empty_like(A);
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(A.scalar_type(), "radial_act", [&] {
+    TORCH_CHECK(radial_act<scalar_t>(E, (int)H, A.data_ptr<scalar_t>(), (scalar_t)c, out.data_ptr<scalar_t>(), st)
+                == cudaSuccess, "radial_act launch");
+  });
+  return out;
+}
+
+std::vector<torch::Tensor> radial_dact_op(torch::Tensor A, torch::Tensor dH, double c, bool primal_only,
+                                          bool want_H) {
+  TORCH_CHECK(A.is_cuda() && A.is_contiguous() && dH.is_contiguous(), "radial_dact: contiguous CUDA");
+  c10::cuda::CUDAGuard g(A.device());
+  const int64_t E = A.size(0) / 2, H = A.size(1);
+  auto DA = primal_only ? torch::empty({E, H}, A.options()) : torch::empty_like(A);
+  torch::Tensor Ho = want_H ? (primal_only ? torch::empty({E, H}, A.options()) : torch::empty_like(A)) : torch::Tensor();
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(A.scalar_type(), "radial_dact", [&] {
+    TORCH_CHECK(radial_dact<scalar_t>(E, (int)H, A.data_ptr<scalar_t>(), dH.data_ptr<scalar_t>(), (scalar_t)c,
+                                      primal_only ? 1 : 0, DA.data_ptr<scalar_t>(),
+                                      want_H ? Ho.data_ptr<scalar_t>() : nullptr, st) == cudaSuccess,
+                "radial_dact launch");
+  });
+  return {DA, Ho};
+}
+
+}  // namespace
+
+void register_radial(pybind11::module& m) {
+  m.def("gemm_reduce_tf32x3", &gemm_reduce_op);
+  m.def("radial_basis", &radial_basis_op);
+  m.def("radial_act", &radial_act_op);
+  m.def("radial_dact", &radial_dact_op);
 }
