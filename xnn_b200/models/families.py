@@ -1,2 +1,2 @@
 """Imports every model family so that their ``@register_model`` decorators run."""
-from . import mace  # noqa: F401
+from . import mace, nequip, tensornet  # noqa: F401

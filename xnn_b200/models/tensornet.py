@@ -1,0 +1,295 @@
+"""TensorNet (Simeon & De Fabritiis 2023): Cartesian rank-2 tensor message passing.
+
+Per atom the features are ``F`` 3x3 tensors ``X = I 1 + A + S`` (scalar, skew, traceless
+symmetric parts). Layout and parameter names follow the reference
+(``src/xnn/gnn/models/tensornet.py:79-847``): the embedding builds ``X`` from the neighbour
+directions weighted by a pair embedding of both species and three radial projections; each
+interaction normalises ``X``, mixes its parts, sums messages ``f_ij (I_j, A_j, S_j)`` (self
+pairs included), forms ``C = YM + MY`` (O(3)) or ``2 YM`` (SO(3)), mixes again and updates
+``X <- X + dX + dX^2``; the readout takes ``(|I|^2, |A|^2, |S|^2)`` through a LayerNorm and a
+linear layer, then an MLP. Edge vectors are ``pos[i] - pos[j]`` (receiver minus sender).
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+from torch import Tensor, nn
+
+from ..data import AtomicGraph
+from ..nn import CosineCutoff, make_radial_basis
+from ..ops.scatter import refresh_ghosts, scatter_sum
+from .base import InteratomicPotential
+from .registry import register_model
+
+_READOUTS = ("mlp", "gated")
+_GROUPS = ("O(3)", "SO(3)")
+
+
+def make_activation(name: str) -> nn.Module:
+    return {"silu": nn.SiLU, "tanh": nn.Tanh, "relu": nn.ReLU, "gelu": nn.GELU,
+            "ssp": nn.Softplus}[name]()
+
+
+def skew_tensor(v: Tensor) -> Tensor:
+    """``(N, 3, F)`` axial vectors to ``(N, 3, 3, F)`` skew matrices."""
+    z = torch.zeros_like(v[:, 0])
+    x, y, w = v[:, 0], v[:, 1], v[:, 2]
+    return torch.stack([z, -w, y, w, z, -x, -y, x, z], 1).reshape(v.shape[0], 3, 3, v.shape[2])
+
+
+def axial_vector(t: Tensor) -> Tensor:
+    return 0.5 * torch.stack([t[:, 2, 1] - t[:, 1, 2], t[:, 0, 2] - t[:, 2, 0], t[:, 1, 0] - t[:, 0, 1]], 1)
+
+
+def decompose(t: Tensor) -> Tuple[Tensor, Tensor, Tensor]:
+    skew = 0.5 * (t - t.transpose(1, 2))
+    scalar = t.diagonal(dim1=1, dim2=2).mean(-1)
+    eye = torch.eye(3, dtype=t.dtype, device=t.device)
+    sym = t - skew - scalar[:, None, None, :] * eye[None, :, :, None]
+    return scalar, skew, sym
+
+
+def compose(scalar: Tensor, skew: Tensor, sym: Tensor) -> Tensor:
+    eye = torch.eye(3, dtype=skew.dtype, device=skew.device)
+    return scalar[:, None, None, :] * eye[None, :, :, None] + skew + sym
+
+
+def frobenius(t: Tensor) -> Tensor:
+    return (t * t).sum(dim=(1, 2))
+
+
+def tensor_matmul(a: Tensor, b: Tensor) -> Tensor:
+    return (a.unsqueeze(3) * b.unsqueeze(1)).sum(2)
+
+
+class GatedMLP(nn.Module):
+    def __init__(self, sizes, activation: str):
+        super().__init__()
+        self.layers = nn.ModuleList([nn.Linear(a, b) for a, b in zip(sizes[:-1], sizes[1:])])
+        self.gates = nn.ModuleList([nn.Linear(a, b) for a, b in zip(sizes[:-1], sizes[1:])])
+        self.act = make_activation(activation)
+
+    def forward(self, x: Tensor) -> Tensor:
+        for i, (l, g) in enumerate(zip(self.layers, self.gates)):
+            last = i == len(self.layers) - 1
+            h = l(x) if last else self.act(l(x))
+            x = h * torch.sigmoid(g(x))
+        return x
+
+
+class TensorEmbedding(nn.Module):
+    def __init__(self, n_features: int, n_rbf: int, n_elements: int, activation: str):
+        super().__init__()
+        self.n_features = n_features
+        self.distance_proj1 = nn.Linear(n_rbf, n_features)
+        self.distance_proj2 = nn.Linear(n_rbf, n_features)
+        self.distance_proj3 = nn.Linear(n_rbf, n_features)
+        self.emb = nn.Embedding(n_elements, n_features)
+        self.emb2 = nn.Linear(2 * n_features, n_features)
+        self.act = make_activation(activation)
+        self.linears_tensor = nn.ModuleList([nn.Linear(n_features, n_features, bias=False) for _ in range(3)])
+        self.linears_scalar = nn.ModuleList([nn.Linear(n_features, 2 * n_features),
+                                             nn.Linear(2 * n_features, 3 * n_features)])
+        self.init_norm = nn.LayerNorm(n_features)
+
+    def forward(self, z: Tensor, src: Tensor, dst: Tensor, cut: Tensor, unit: Tensor, rbf: Tensor) -> Tensor:
+        n = z.shape[0]
+        emb = self.emb(z)
+        pair = self.emb2(torch.cat([emb.index_select(0, dst), emb.index_select(0, src)], -1))
+        w = cut.unsqueeze(-1) * pair
+        scalar = scatter_sum(w * self.distance_proj1(rbf), dst, n)
+        vector = scatter_sum((w * self.distance_proj2(rbf)).unsqueeze(1) * unit.unsqueeze(-1), dst, n)
+        outer = unit.unsqueeze(2) * unit.unsqueeze(1)
+        full = scatter_sum((w * self.distance_proj3(rbf))[:, None, None, :] * outer.unsqueeze(-1), dst, n)
+        skew = skew_tensor(vector)
+        eye = torch.eye(3, dtype=full.dtype, device=full.device)
+        sym = full - full.diagonal(dim1=1, dim2=2).mean(-1)[:, None, None, :] * eye[None, :, :, None]
+        norm = self.init_norm(frobenius(compose(scalar, skew, sym)))
+        for lin in self.linears_scalar:
+            norm = self.act(lin(norm))
+        norm = norm.reshape(n, 3, self.n_features)
+        scalar = self.linears_tensor[0](scalar) * norm[:, 0]
+        skew = _mix(self.linears_tensor[1], skew) * norm[:, 1, None, None, :]
+        sym = _mix(self.linears_tensor[2], sym) * norm[:, 2, None, None, :]
+        return compose(scalar, skew, sym)
+
+
+def _mix(lin: nn.Linear, t: Tensor) -> Tensor:
+    """A channel-mixing linear map on ``(N, 3, 3, F)`` tensors (acts on the last axis)."""
+    return lin(t)
+
+
+class Interaction(nn.Module):
+    def __init__(self, n_features: int, n_rbf: int, activation: str, o3: bool):
+        super().__init__()
+        self.n_features = n_features
+        self.o3 = o3
+        self.act = make_activation(activation)
+        self.linears_scalar = nn.ModuleList([nn.Linear(n_rbf, n_features), nn.Linear(n_features, 2 * n_features),
+                                             nn.Linear(2 * n_features, 3 * n_features)])
+        self.linears_tensor = nn.ModuleList([nn.Linear(n_features, n_features, bias=False) for _ in range(6)])
+
+    def forward(self, X: Tensor, src: Tensor, dst: Tensor, cut: Tensor, rbf: Tensor, q: Tensor) -> Tensor:
+        n, F = X.shape[0], self.n_features
+        f = rbf
+        for lin in self.linears_scalar:
+            f = self.act(lin(f))
+        filters = (f * cut.unsqueeze(-1)).reshape(-1, 3, F)
+        X = X / (frobenius(X) + 1.0)[:, None, None, :]
+        scalar, skew, sym = decompose(X)
+        scalar = self.linears_tensor[0](scalar)
+        skew = self.linears_tensor[1](skew)
+        sym = self.linears_tensor[2](sym)
+        Y = compose(scalar, skew, sym)
+        vector = axial_vector(skew)
+        m_scalar = scatter_sum(filters[:, 0] * scalar.index_select(0, src), dst, n)
+        m_vector = scatter_sum(filters[:, 1].unsqueeze(1) * vector.index_select(0, src), dst, n)
+        m_sym = scatter_sum(filters[:, 2][:, None, None, :] * sym.index_select(0, src), dst, n)
+        msg = compose(m_scalar, skew_tensor(m_vector), m_sym)
+        cs = (1.0 + 0.1 * q)[:, None, None, None]
+        C = cs * (tensor_matmul(Y, msg) + tensor_matmul(msg, Y)) if self.o3 else 2.0 * tensor_matmul(Y, msg)
+        scalar, skew, sym = decompose(C)
+        norm = frobenius(C) + 1.0
+        scalar = self.linears_tensor[3](scalar / norm)
+        skew = self.linears_tensor[4](skew / norm[:, None, None, :])
+        sym = self.linears_tensor[5](sym / norm[:, None, None, :])
+        dX = compose(scalar, skew, sym)
+        return X + dX + cs * tensor_matmul(dX, dX)
+
+
+@register_model("tensornet")
+class TensorNet(InteratomicPotential):
+    head_modules = ("readout", "atom_ref")
+    refreshes_ghosts = True
+    readout_extra_inputs = 0
+
+    def __init__(self, n_features: int = 128, n_interactions: int = 2, n_rbf: int = 32, cutoff: float = 4.5,
+                 radial_basis: str = "expnorm", trainable_rbf: bool = False, activation: str = "silu",
+                 equivariance_group: str = "O(3)", n_elements: int = 128, energy_shift: float = 0.0,
+                 energy_scale: float = 1.0, species=None, atomic_energies=None, readout: str = "mlp",
+                 readout_hidden=None, self_pairs: bool = True, rbf_max: Optional[float] = None,
+                 gamma: Optional[float] = None):
+        super().__init__()
+        if readout not in _READOUTS:
+            raise ValueError(f"readout must be one of {_READOUTS}")
+        if equivariance_group not in _GROUPS:
+            raise ValueError(f"equivariance_group must be one of {_GROUPS}")
+        self.cutoff = float(cutoff)
+        if species is not None:
+            self.species = [int(z) for z in species]
+        self.n_features = n_features
+        self.node_feature_dim = n_features
+        self.n_interactions = n_interactions
+        self.equivariance_group = equivariance_group
+        span = float(rbf_max) if rbf_max is not None and radial_basis == "gaussian" else cutoff
+        self.rbf = make_radial_basis(radial_basis, n_rbf, span, trainable_rbf, gamma=gamma)
+        self.cutoff_fn = CosineCutoff(cutoff)
+        self.tensor_embedding = TensorEmbedding(n_features, n_rbf, n_elements, activation)
+        self.layers = nn.ModuleList([Interaction(n_features, n_rbf, activation, equivariance_group == "O(3)")
+                                     for _ in range(n_interactions)])
+        self.out_norm = nn.LayerNorm(3 * n_features)
+        self.linear = nn.Linear(3 * n_features, n_features)
+        self.act = make_activation(activation)
+        self.self_pairs = bool(self_pairs)
+        self.activate_features = readout == "mlp"
+        n_in = n_features + self.readout_extra_inputs
+        if readout_hidden is None:
+            readout_hidden = (n_features // 2,) if readout == "mlp" else (n_in, n_features, n_features)
+        sizes = [n_in, *[int(h) for h in readout_hidden], 1]
+        if readout == "mlp":
+            mods = []
+            for a, b in zip(sizes[:-1], sizes[1:]):
+                mods += [nn.Linear(a, b), make_activation(activation)]
+            self.readout = nn.Sequential(*mods[:-1])
+        else:
+            self.readout = GatedMLP(sizes, activation)
+        for mod in self.readout.modules():
+            if isinstance(mod, nn.Linear):
+                nn.init.xavier_uniform_(mod.weight)
+                nn.init.zeros_(mod.bias)
+        self.register_buffer("energy_scale", torch.tensor(float(energy_scale)))
+        self.register_buffer("energy_shift", torch.tensor(float(energy_shift)))
+        self.atom_ref = nn.Embedding(n_elements, 1)
+        nn.init.zeros_(self.atom_ref.weight)
+        if atomic_energies is not None:
+            if species is None:
+                raise ValueError("species is required to map atomic_energies")
+            self.set_atomic_energies(species, atomic_energies)
+
+    def set_atomic_energies(self, species, values) -> None:
+        with torch.no_grad():
+            self.atom_ref.weight[torch.as_tensor(list(species)), 0] = torch.as_tensor(
+                values, dtype=self.atom_ref.weight.dtype)
+
+    def set_energy_scale_shift(self, scale: float, shift: float) -> None:
+        self.energy_scale.fill_(float(scale))
+        self.energy_shift.fill_(float(shift))
+
+    def receptive_field(self) -> float:
+        return max(1, self.n_interactions) * self.cutoff
+
+    def tensors(self, atomic_numbers: Tensor, edge_index: Tensor, edge_vec: Tensor, total_charge: Tensor) -> Tensor:
+        r = torch.linalg.norm(edge_vec, dim=-1)
+        unit = edge_vec / r.clamp(min=1e-12).unsqueeze(-1)
+        src, dst = edge_index[0], edge_index[1]
+        if self.self_pairs:
+            n = atomic_numbers.shape[0]
+            loops = torch.arange(n, dtype=edge_index.dtype, device=edge_index.device)
+            src = torch.cat([src, loops])
+            dst = torch.cat([dst, loops])
+            r = torch.cat([r, r.new_zeros((n,))])
+            unit = torch.cat([unit, unit.new_zeros((n, 3))])
+        cut = self.cutoff_fn(r)
+        rbf = self.rbf(r)
+        X = self.tensor_embedding(atomic_numbers, src, dst, cut, unit, rbf)
+        for layer in self.layers:
+            X = layer(refresh_ghosts(X), src, dst, cut, rbf, total_charge)
+        return X
+
+    def _features(self, X: Tensor) -> Tensor:
+        scalar, skew, sym = decompose(X)
+        x = torch.cat([3.0 * scalar * scalar, frobenius(skew), frobenius(sym)], -1)
+        x = self.linear(self.out_norm(x))
+        return self.act(x) if self.activate_features else x
+
+    def _energy(self, x: Tensor, atomic_numbers: Tensor) -> Tensor:
+        return (self.energy_scale * self.readout(x).squeeze(-1) + self.energy_shift
+                + self.atom_ref(atomic_numbers).squeeze(-1))
+
+    def node_features_energy(self, atomic_numbers: Tensor, edge_index: Tensor, edge_vec: Tensor):
+        q = torch.zeros(atomic_numbers.shape[0], dtype=edge_vec.dtype, device=edge_vec.device)
+        x = self._features(self.tensors(atomic_numbers, edge_index, edge_vec, q))
+        return x, self._energy(x, atomic_numbers)
+
+    def node_energy(self, atomic_numbers, edge_index, edge_vec):
+        return self.node_features_energy(atomic_numbers, edge_index, edge_vec)[1]
+
+    def forward(self, data: AtomicGraph) -> dict:
+        vec = data.edge_vectors()
+        q = data.total_charge
+        qa = (q.index_select(0, data.batch).to(vec.dtype) if q is not None
+              else torch.zeros(data.num_nodes, dtype=vec.dtype, device=vec.device))
+        x = self._features(self.tensors(data.atomic_numbers, data.edge_index, vec, qa))
+        ne = self._energy(x, data.atomic_numbers)
+        return {"node_energy": ne, "energy": self.aggregate_energy(ne, data), "node_features": x}
+
+    @classmethod
+    def from_config(cls, cfg) -> "TensorNet":
+        from ..config.coerce import coerce_per_species, coerce_species
+        extra = dict(cfg.extra or {})
+        species = coerce_species(extra.get("species")) if extra.get("species") is not None else None
+        return cls(n_features=cfg.n_features, n_interactions=cfg.n_interactions, n_rbf=cfg.n_rbf,
+                   cutoff=cfg.cutoff, radial_basis=str(extra.get("radial_basis", "expnorm")),
+                   trainable_rbf=bool(extra.get("trainable_rbf", False)),
+                   activation=str(extra.get("activation", "silu")),
+                   equivariance_group=str(extra.get("equivariance_group", "O(3)")),
+                   n_elements=int(extra.get("n_elements", 128)),
+                   energy_shift=float(extra.get("energy_shift", 0.0)),
+                   energy_scale=float(extra.get("energy_scale", 1.0)), species=species,
+                   atomic_energies=coerce_per_species(extra.get("atomic_energies"), species or [],
+                                                      "atomic_energies"),
+                   readout=str(extra.get("readout", "mlp")), readout_hidden=extra.get("readout_hidden"),
+                   self_pairs=bool(extra.get("self_pairs", True)),
+                   rbf_max=None if extra.get("rbf_max") is None else float(extra["rbf_max"]),
+                   gamma=None if extra.get("gamma") is None else float(extra["gamma"]))
