@@ -29,6 +29,12 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
 
+# name fragments of the kernels compiled into xnn_b200/_C.so
+OUR_KERNELS = ("conv_gather", "conv_edge", "conv_scatter", "symcon_", "edge_geom_", "p2p_allreduce",
+               "gemm_pack_kernel", "gemm_rows_kernel", "gemm_reduce_kernel", "sum_partials_kernel",
+               "radial_basis_kernel", "radial_act_kernel", "radial_dact_kernel", "nb_count", "nb_write")
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -183,9 +189,7 @@ def main():
             torch.cuda.synchronize(dev)
         trainer.use_graphs = saved
         names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
-        ours = [n for n in names if any(k in n for k in ("conv_gather", "conv_edge", "conv_scatter",
-                                                          "symcon_", "edge_geom_", "p2p_allreduce",
-                                                          "radial_mlp", "nb_count", "nb_write"))]
+        ours = [n for n in names if any(k in n for k in OUR_KERNELS)]
         launches = len(ours)
         all_kernels = len(names)
     except Exception as exc:  # pragma: no cover

@@ -1,0 +1,147 @@
+"""Micro-benchmarks of the hot CUDA kernels on a config-4-shaped water box.
+
+Each op is timed with CUDA events on the current stream after warm-up; between timed launches a
+buffer larger than L2 is overwritten so every launch reads its operands from HBM. The printed
+line gives the duration, the algorithmic bytes moved (the operands each kernel must read and the
+results it must write, once) and the achieved fraction of a reference bandwidth.
+
+    python -m xnn_b200.utils.kernel_bench --atoms 20000 --ops conv_gather,gemm_reduce
+
+The same command with ``--iters 1 --warmup 1`` is a small case for a profiler capture.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from typing import Callable, Dict, List
+
+import torch
+
+from .. import _ext
+from ..data import synthetic
+from ..data.neighborlist import build_neighbor_list
+from ..ops import gemm
+from ..ops import mace_ops as K
+
+L2_FLUSH_BYTES = 256 << 20
+
+
+def peaks() -> Dict[str, float]:
+    """Measured HBM bandwidth (GB/s) from MEASURED_PEAKS.json at the repository root, else 6650."""
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def time_op(fn: Callable[[], object], iters: int, warmup: int) -> float:
+    """Median milliseconds of ``fn`` over ``iters`` launches, L2 flushed before each."""
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    for _ in range(warmup):
+        fn()
+    times: List[float] = []
+    for _ in range(iters):
+        flush.fill_(1.0)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def water_case(n_atoms: int, cutoff: float = 4.5, C: int = 96, P: int = 4, seed: int = 0):
+    s = synthetic.water_box(n_atoms, seed=seed)
+    dev = torch.device("cuda")
+    pos, cell = s["pos"].to(dev), s["cell"].to(dev)
+    ei, shifts = build_neighbor_list(pos, cutoff, cell, s["pbc"], engine="native")
+    order = torch.argsort(ei[1], stable=True)
+    ei, shifts = ei[:, order], shifts[order]
+    vec = (pos[ei[1]] - pos[ei[0]] + shifts.to(pos.dtype) @ cell).float()
+    N, E = pos.shape[0], ei.shape[1]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    return {
+        "pos": pos, "cell": cell, "pbc": s["pbc"], "cutoff": cutoff, "ei": ei, "vec": vec, "N": N, "E": E,
+        "plan": K.EdgePlan.build(ei, N, assume_dst_sorted=True),
+        "x": torch.randn(N, C, device=dev, generator=g),
+        "R": torch.randn(E, P, C, device=dev, generator=g),
+        "Y": torch.randn(E, P * P, device=dev, generator=g),
+        "G": torch.randn(P * P, N, C, device=dev, generator=g),
+        "C": C, "P": P,
+    }
+
+
+def build_ops(case) -> Dict[str, tuple]:
+    """name -> (callable, algorithmic bytes)."""
+    C, P, N, E = case["C"], case["P"], case["N"], case["E"]
+    plan, x, R, Y, G = case["plan"], case["x"], case["R"], case["Y"], case["G"]
+    ops = _ext.ops()
+    f = 4
+    T1 = torch.randn(E, P, C, device="cuda")
+    out: Dict[str, tuple] = {}
+    out["conv_gather"] = (lambda: ops.conv_gather(N, C, P, plan.dst_ptr, plan.src32, plan.dst_perm, [x], [R], [Y]),
+                          f * (E * P * C + E * P * P + N * C + P * P * N * C))
+    out["conv_edge"] = (lambda: ops.conv_edge(N, C, P, E, plan.dst_ptr, plan.src32, plan.dst_perm, G, [Y], [x],
+                                              [True], True, [], []),
+                        f * (P * P * N * C + E * P * P + N * C + 2 * E * P * C))
+    out["conv_scatter"] = (lambda: ops.conv_scatter(N, C, P, plan.src_ptr, plan.src_perm, [R], [T1]),
+                           f * (2 * E * P * C + N * C))
+    H = 64
+    Hr = torch.randn(2 * E, H, device="cuda")
+    W2 = torch.randn(H, P * C, device="cuda")
+    out["gemm_rows_64x384"] = (lambda: gemm.mm_raw(Hr[:E], W2), f * (E * H + E * P * C + H * P * C))
+    Wh = torch.randn(H, H, device="cuda")
+    out["gemm_rows_64x64"] = (lambda: gemm.mm_raw(Hr, Wh), f * (2 * E * H * 2 + H * H))
+    D = torch.randn(E, P * C, device="cuda")
+    out["gemm_reduce_64x384"] = (lambda: gemm.mm_t_raw(Hr[:E], D), f * (E * H + E * P * C))
+    Dh = torch.randn(2 * E, H, device="cuda")
+    out["gemm_reduce_64x64"] = (lambda: gemm.mm_t_raw(Hr, Dh), f * (2 * E * H * 2))
+    vec = case["vec"]
+    freqs = torch.pi * torch.arange(1, 9, dtype=torch.float32, device="cuda")
+    out["edge_geometry"] = (lambda: K.edge_geometry(vec, 3, freqs, (2 / 4.5) ** 0.5, 4.5, 5),
+                            f * (3 * E + 16 * E + 8 * E))
+    D16 = 16
+    A = 0.5 * torch.randn(D16, N, C, device="cuda")
+    Ws = torch.randn(2, K.num_invariants(3, 3), C, device="cuda")
+    z = torch.randint(0, 2, (N,), device="cuda")
+    out["symcon_fwd"] = (lambda: K.symmetric_contraction(A, Ws, z, 3, 3), f * (D16 * N * C + N * C))
+    pos, cell, pbc, rc = case["pos"], case["cell"], case["pbc"], case["cutoff"]
+    out["neighbor_list"] = (lambda: build_neighbor_list(pos, rc, cell, pbc, engine="native"),
+                            8 * 3 * N + E * (2 * 8 + 3 * 8))
+    return out
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--atoms", type=int, default=20000)
+    ap.add_argument("--ops", default="all")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args(argv)
+    if not _ext.cuda_available():
+        raise SystemExit(f"native extension not loaded: {_ext.error()}")
+    case = water_case(args.atoms)
+    ops = build_ops(case)
+    names = list(ops) if args.ops == "all" else args.ops.split(",")
+    pk = peaks()
+    with torch.no_grad():
+        for name in names:
+            fn, nbytes = ops[name]
+            ms = time_op(fn, args.iters, args.warmup)
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            print(json.dumps({"op": name, "atoms": case["N"], "edges": case["E"], "ms": round(ms, 4),
+                              "alg_bytes": int(nbytes), "gb_s": round(gbs, 1),
+                              f"frac_hbm_{pk['source']}": round(gbs / pk["hbm_gbs"], 3)}), flush=True)
+
+
+if __name__ == "__main__":
+    main()
