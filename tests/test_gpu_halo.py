@@ -1,0 +1,115 @@
+"""Fused peer-memory ghost exchange, every rank played by one cooperative launch on one GPU,
+against the exchange written with plain indexing; DomainParallel on the GPU against a plain
+evaluation."""
+import pytest
+import torch
+
+from xnn_b200 import _ext
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_ext():
+    if not _ext.cuda_available():
+        pytest.fail(f"native extension not loaded: {_ext.error()}")
+
+
+def _fake_plans(world, n_atoms, seed):
+    """Owners, ghost lists grouped by owner, and the send lists / offsets they imply."""
+    g = torch.Generator().manual_seed(seed)
+    owner = torch.randint(0, world, (n_atoms,), generator=g)
+    owned = [torch.nonzero(owner == r).flatten() for r in range(world)]
+    ghosts = []
+    for r in range(world):
+        pick = torch.nonzero(torch.rand(n_atoms, generator=g) < 0.3).flatten()
+        pick = pick[torch.sort(owner[pick], stable=True).indices]     # grouped by owner (own images too)
+        ghosts.append(pick)
+    recv = [[int((owner[ghosts[r]] == p).sum()) for p in range(world)] for r in range(world)]
+    send = [[recv[p][s] for p in range(world)] for s in range(world)]
+    send_rows, remote, remote_send = [], [], []
+    for s in range(world):
+        rows = []
+        for p in range(world):
+            req = ghosts[p][owner[ghosts[p]] == s]
+            rows.append(torch.searchsorted(owned[s], req))
+        send_rows.append(torch.cat(rows))
+        remote.append([sum(recv[p][:s]) for p in range(world)])
+        remote_send.append([sum(send[p][:s]) for p in range(world)])
+    return owner, owned, ghosts, recv, send, send_rows, remote, remote_send
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("width,dtype", [(96, torch.float32), (3, torch.float64), (3, torch.float32)])
+def test_emulated_exchange_both_directions(world, width, dtype):
+    from xnn_b200.parallel.halo import PeerHaloExchange
+    dev = torch.device("cuda")
+    ex = PeerHaloExchange(dev, nblocks=8, emulate_world=world, timeout_s=5.0)
+    try:
+        for rep in range(3):                      # consecutive exchanges alternate buffer halves
+            owner, owned, ghosts, recv, send, send_rows, remote, remote_send = _fake_plans(world, 500, rep)
+            values = torch.randn(500, width, dtype=dtype)
+            xs = [values[o].to(dev) for o in owned]
+            rb = width * values.element_size()
+            most = max(max(len(g) for g in ghosts), max(len(s) for s in send_rows))
+            ex.reserve(most * rb)
+            outs = [torch.full((len(ghosts[r]), width), float("nan"), dtype=dtype, device=dev) for r in range(world)]
+            ex.launch(xs, [s.to(dev) for s in send_rows], send, remote, outs, rb)
+            ex.check()
+            for r in range(world):
+                torch.testing.assert_close(outs[r].cpu(), values[ghosts[r]], rtol=0, atol=0)
+            # adjoint: ghost gradients back to their owners, accumulated into the owned rows
+            gs = [torch.randn(len(ghosts[r]), width, dtype=dtype, device=dev) for r in range(world)]
+            backs = [torch.zeros(len(send_rows[s]), width, dtype=dtype, device=dev) for s in range(world)]
+            ex.launch(gs, [None] * world, recv, remote_send, backs, rb)
+            ex.check()
+            want = torch.zeros(500, width, dtype=torch.float64)
+            for r in range(world):
+                want.index_add_(0, ghosts[r], gs[r].cpu().double())
+            for s in range(world):
+                got = torch.zeros(len(owned[s]), width, dtype=torch.float64)
+                got.index_add_(0, send_rows[s], backs[s].cpu().double())
+                torch.testing.assert_close(got, want[owned[s]], rtol=1e-12, atol=1e-12)
+    finally:
+        ex.close()
+
+
+def test_exchange_timeout_reports_status():
+    """A peer that never signals: the bounded wait gives up and the status word says so."""
+    from xnn_b200.parallel.halo import PeerHaloExchange
+    dev = torch.device("cuda")
+    ex = PeerHaloExchange(dev, nblocks=2, emulate_world=2, timeout_s=0.2)
+    try:
+        ex.reserve(1 << 16)
+        x = torch.randn(4, 8, device=dev)
+        out = torch.zeros(2, 8, device=dev)
+        # rank 1 plays with a launch of its own blocks, but rank 0's counters are read as if an
+        # extra exchange had been expected: bump rank 0's epochs so its target is out of reach
+        ex.epochs[0] += 5
+        ex.launch([x, x], [torch.tensor([0, 1], device=dev), torch.tensor([2, 3], device=dev)],
+                  [[0, 2], [2, 0]], [[0, 0], [0, 0]], [out, out.clone()], 32)
+        with pytest.raises(RuntimeError, match="did not arrive"):
+            ex.check()
+    finally:
+        ex.close()
+
+
+def test_domain_parallel_gpu_matches_plain():
+    from xnn_b200.data import structure_to_graph, synthetic
+    from xnn_b200.models import ForceStressOutput
+    from xnn_b200.models.mace import MACE
+    from xnn_b200.parallel.domain import DomainParallel
+    torch.manual_seed(0)
+    m = MACE(species=[1, 8], cutoff=4.5, num_channels=32, n_rbf=8, num_interactions=2, max_ell=3,
+             correlation=3, avg_num_neighbors=30.0).cuda().eval()
+    s = synthetic.water_box(3000, seed=1)
+    g = structure_to_graph(s, 4.5).to("cuda")
+    ref = ForceStressOutput(m)(g.clone())
+    dp = DomainParallel(m, skin=0.5)
+    out = dp(g)
+    torch.testing.assert_close(out["energy"].float(), ref["energy"].reshape(1).float(), rtol=1e-5, atol=1e-3)
+    torch.testing.assert_close(out["forces"], ref["forces"], rtol=1e-3, atol=1e-4)
+    m.edge_chunk = 20000
+    out2 = dp(g)
+    torch.testing.assert_close(out2["energy"], out["energy"], rtol=1e-6, atol=1e-4)
+    torch.testing.assert_close(out2["forces"], out["forces"], rtol=1e-4, atol=1e-5)

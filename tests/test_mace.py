@@ -142,3 +142,14 @@ def test_state_dict_layout_and_config():
         assert k in keys
     assert m.products[0].symmetric_contractions.contractions[0].U_matrix_3.shape == (16, 16, 16, 23)
     assert math.isclose(m.receptive_field(), 9.0)
+
+
+def test_edge_chunks_match_single_pass():
+    m = _model().set_use_fast(True).eval()
+    f = ForceStressOutput(m)
+    b = _batch(4, seed=2)
+    o1 = f(b.clone())
+    m.edge_chunk = 37
+    o2 = f(b.clone())
+    torch.testing.assert_close(o1["energy"], o2["energy"], rtol=1e-12, atol=1e-12)
+    torch.testing.assert_close(o1["forces"], o2["forces"], rtol=1e-11, atol=1e-11)

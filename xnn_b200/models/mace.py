@@ -347,6 +347,9 @@ class MACE(GNNPotential):
                 self.readouts.append(NonLinearReadout(hidden_out, MLP_irreps, gate_fn) if last
                                      else LinearReadout(hid))
         self.use_fast = "auto"
+        #: in evaluation, run the fused path's edge work in receiver chunks of at most this many
+        #: edges under activation checkpointing (``None``: one pass over all edges)
+        self.edge_chunk = None
         self.__dict__["_fast_cache"] = None
 
     # --- fast-path selection -----------------------------------------------------

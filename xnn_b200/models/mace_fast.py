@@ -20,6 +20,7 @@ from typing import List, Optional, Tuple
 import torch
 from torch import Tensor
 from torch.nn import functional as F
+from torch.utils.checkpoint import checkpoint
 
 from ..ops import mace_ops as K
 from ..ops.radial import radial_network
@@ -93,6 +94,40 @@ def _conv_path_scale_build(blk) -> Tensor:
     return torch.cat(scales)
 
 
+def _messages(h_up: Tensor, r: Tensor, Y: Tensor, plan: K.EdgePlan, blk, ef, P: int, C: int) -> Tensor:
+    """Radial network and message pass of one interaction over the edges of ``plan``."""
+    R = radial_network(r, blk.conv_tp_weights, _conv_path_scale(blk, r), ef.rbf.freqs, ef.rbf.norm,
+                       ef.cutoff, ef.envelope.p).view(-1, P, C)
+    return K.conv(h_up, R, Y, plan)
+
+
+def _edge_chunks(plan: K.EdgePlan, edge_index: Tensor, max_edges: Optional[int]):
+    """Receiver-contiguous edge chunks of at most ``max_edges`` edges (``None``: no chunking).
+
+    With edges sorted by receiver, a chunk is the edge range of a range of receivers, so its
+    messages fill a contiguous block of node rows. Each chunk's radial network and message pass
+    run under activation checkpointing: the per-edge tensors of one chunk are alive at a time,
+    which bounds the memory of a force evaluation on millions of edges.
+    """
+    if max_edges is None or plan.n_edges <= max_edges or plan.dst_perm is not None:
+        return None
+    ptr = plan.dst_ptr.cpu()
+    bounds, n0 = [], 0
+    N = plan.n_nodes
+    while n0 < N:
+        limit = int(ptr[n0]) + max_edges
+        n1 = int(torch.searchsorted(ptr, torch.tensor(limit), right=True)) - 1
+        n1 = min(max(n1, n0 + 1), N)
+        bounds.append((n0, n1))
+        n0 = n1
+    out = []
+    for n0, n1 in bounds:
+        e0, e1 = int(ptr[n0]), int(ptr[n1])
+        ei = torch.stack([edge_index[0, e0:e1], edge_index[1, e0:e1] - n0])
+        out.append(((e0, e1), K.EdgePlan.build(ei, n1 - n0, assume_dst_sorted=True, n_src=N)))
+    return out
+
+
 def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor, edge_vec: Tensor,
                               plan: Optional[K.EdgePlan] = None) -> Tuple[Tensor, Tensor]:
     N = atomic_numbers.shape[0]
@@ -105,6 +140,8 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
     P = lmax + 1
     Y, _ = K.edge_geometry(edge_vec, lmax, ef.rbf.freqs, ef.rbf.norm, ef.cutoff, ef.envelope.p)
     r = torch.linalg.norm(edge_vec, dim=-1)
+    chunks = _edge_chunks(plan, edge_index, getattr(model, "edge_chunk", None)) \
+        if not model.training else None
     n_el = len(model.species)
     C = model.num_features
     emb = model.node_embedding
@@ -116,9 +153,11 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
             h = refresh_ghosts(h)
         sc = species_linear(h, z, _species_weights(blk.skip_tp, n_el)) if blk.residual else None
         h_up = h @ _linear_blocks(blk.linear_up)[0]
-        R = radial_network(r, blk.conv_tp_weights, _conv_path_scale(blk, r), ef.rbf.freqs, ef.rbf.norm,
-                           ef.cutoff, ef.envelope.p).view(-1, P, C)
-        A = K.conv(h_up, R, Y, plan)                                   # (D, N, C)
+        if chunks is None:
+            A = _messages(h_up, r, Y, plan, blk, ef, P, C)               # (D, N, C)
+        else:
+            A = torch.cat([checkpoint(_messages, h_up, r[e0:e1], Y[e0:e1], sub, blk, ef, P, C,
+                                      use_reentrant=False) for (e0, e1), sub in chunks], dim=1)
         mats = _linear_blocks(blk.linear)
         parts = []
         for l in range(P):

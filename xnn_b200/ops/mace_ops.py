@@ -58,9 +58,16 @@ class EdgePlan:
     dst_perm: Optional[Tensor]
     src_ptr: Tensor
     src_perm: Tensor
+    #: number of sender rows when senders and receivers differ (an edge chunk); -1: ``n_nodes``
+    n_src: int = -1
+
+    @property
+    def n_senders(self) -> int:
+        return self.n_src if self.n_src >= 0 else self.n_nodes
 
     @staticmethod
-    def build(edge_index: Tensor, n_nodes: int, assume_dst_sorted: Optional[bool] = None) -> "EdgePlan":
+    def build(edge_index: Tensor, n_nodes: int, assume_dst_sorted: Optional[bool] = None,
+              n_src: Optional[int] = None) -> "EdgePlan":
         src, dst = edge_index[0], edge_index[1]
         E = int(src.shape[0])
         dev = src.device
@@ -72,12 +79,13 @@ class EdgePlan:
         if assume_dst_sorted is None:
             assume_dst_sorted = bool((dst[1:] >= dst[:-1]).all()) if E > 1 else True
         dst_perm = None if assume_dst_sorted else torch.argsort(dst, stable=True)
-        scounts = torch.zeros(n_nodes, dtype=torch.int64, device=dev).index_add_(0, src, one)
-        src_ptr = torch.zeros(n_nodes + 1, dtype=torch.int64, device=dev)
+        ns = n_nodes if n_src is None else int(n_src)
+        scounts = torch.zeros(ns, dtype=torch.int64, device=dev).index_add_(0, src, one)
+        src_ptr = torch.zeros(ns + 1, dtype=torch.int64, device=dev)
         src_ptr[1:] = torch.cumsum(scounts, 0)
         src_perm = torch.argsort(src, stable=True)
         return EdgePlan(n_nodes, E, src.to(torch.int32).contiguous(), dst.to(torch.int32).contiguous(),
-                        src, dst, dst_ptr, dst_perm, src_ptr, src_perm)
+                        src, dst, dst_ptr, dst_perm, src_ptr, src_perm, -1 if n_src is None else ns)
 
 
 # --------------------------------------------------------------------------- edge geometry
@@ -214,7 +222,7 @@ class _ConvVJP(Function):
         gR, gY, T1, _ = K.conv_edge(N, C, P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm, G,
                                     [Y], [x if nR else None], [True], bool(nR),
                                     [x] if nY else [], [R] if nY else [])
-        gx = K.conv_scatter(N, C, P, plan.src_ptr, plan.src_perm, [R], [T1]) if nx else None
+        gx = K.conv_scatter(plan.n_senders, C, P, plan.src_ptr, plan.src_perm, [R], [T1]) if nx else None
         ctx.save_for_backward(G, x, R, Y, T1)
         ctx.plan = plan
         ctx.set_materialize_grads(False)
@@ -267,7 +275,7 @@ class _ConvVJP(Function):
             if T2 is not None:
                 As.append(R); Bs.append(T2)
             if As:
-                cx = K.conv_scatter(N, C, P, plan.src_ptr, plan.src_perm, As, Bs)
+                cx = K.conv_scatter(plan.n_senders, C, P, plan.src_ptr, plan.src_perm, As, Bs)
         return cG, cx, cR, cY, None, None
 
 

@@ -31,6 +31,7 @@ from torch.autograd import Function
 
 from ..data.atomic_graph import AtomicGraph
 from ..data.neighborlist import build_neighbor_list
+from ..ops.modes import force_pass
 from ..ops.scatter import domain_hooks, structure_sum
 
 #: added to the ghost shell and the neighbour-list reach so rounding never drops an atom on an edge
@@ -131,8 +132,12 @@ class DomainPlan:
     order: Tensor
     need: float
     skin: float
-    #: offset of this process's rows inside every receiver's ghost list (peer-memory exchange)
+    #: peer-memory exchange: first row of this process's rows in every receiver's ghost list,
+    #: first row of its ghosts in every owner's send list, and the largest ghost or send count
+    #: of any process (sizes the shared receive buffers)
     remote_offsets: Optional[list] = None
+    remote_send_offsets: Optional[list] = None
+    max_rows: int = 0
 
     @property
     def n_owned(self) -> int:
@@ -340,15 +345,20 @@ class DomainParallel(nn.Module):
             recv_counts = recv_counts_t.tolist()
             requested = ghosts.new_empty(int(sum(send_counts)))
             dist.all_to_all_single(requested, ghosts, send_counts, recv_counts, group=self.group)
-            # where this process's rows start inside every receiver's ghost list
-            starts = torch.cumsum(recv_counts_t, 0) - recv_counts_t
+            # where this process's rows start inside every receiver's ghost list, and where its
+            # ghosts start inside every owner's send list
+            starts = torch.stack([torch.cumsum(recv_counts_t, 0) - recv_counts_t,
+                                  torch.cumsum(send_counts_t, 0) - send_counts_t], 1).contiguous()
             remote = torch.empty_like(starts)
             dist.all_to_all_single(remote, starts, group=self.group)
-            remote_offsets = remote.tolist()
+            remote_offsets, remote_send_offsets = remote[:, 0].tolist(), remote[:, 1].tolist()
+            most = torch.tensor([max(len(ghosts), len(requested))], dtype=torch.long, device=device)
+            dist.all_reduce(most, op=dist.ReduceOp.MAX, group=self.group)
+            max_rows = int(most[0])
         else:
             send_counts, requested = recv_counts_t.tolist(), ghosts
             recv_counts = recv_counts_t.tolist()
-            remote_offsets = [0]
+            remote_offsets, remote_send_offsets, max_rows = [0], [0], len(ghosts)
         send_rows = torch.searchsorted(owned, requested)
         if len(requested) and not (len(owned) and bool(
                 (owned[send_rows.clamp(max=len(owned) - 1)] == requested).all())):
@@ -394,7 +404,7 @@ class DomainParallel(nn.Module):
             cell_shifts=cell_shifts.to(device), pbc=pbc, atomic_numbers=atomic_numbers,
             total_charge=total_charge, spin_multiplicity=spin_multiplicity, reference=reference,
             cell=cell, counts=counts, order=order, need=self.need, skin=self.skin,
-            remote_offsets=remote_offsets)
+            remote_offsets=remote_offsets, remote_send_offsets=remote_send_offsets, max_rows=max_rows)
 
     def _cell(self, plan: DomainPlan, cell: Optional[Tensor]) -> Optional[Tensor]:
         if plan.cell is None:
@@ -526,13 +536,17 @@ class DomainParallel(nn.Module):
         inputs = [p] + ([strain] if strain is not None else [])
         grads = [None] * len(inputs)
         if energy.requires_grad:
-            grads = list(torch.autograd.grad([energy], inputs, allow_unused=True))
+            # only position / strain derivatives: the fused ops skip their weight gradients
+            with force_pass():
+                grads = list(torch.autograd.grad([energy], inputs, allow_unused=True))
         g_pos = grads[0] if grads[0] is not None else torch.zeros_like(p)
         g_strain = (grads[1] if strain is not None and grads[1] is not None
                     else torch.zeros((3, 3), dtype=torch.float64, device=device))
         total = torch.cat([energy.detach().reshape(1), g_strain.to(torch.float64).reshape(9)])
         if plan.world > 1:
             dist.all_reduce(total, group=self.group)
+        if self._exchanger is not None:
+            self._exchanger.check()
         result = {"energy": total[:1], "forces": -g_pos.to(dtype)}
         if strain is not None:
             result["stress"] = (total[1:10].view(1, 3, 3) / volume).to(dtype)
