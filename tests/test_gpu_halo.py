@@ -113,3 +113,41 @@ def test_domain_parallel_gpu_matches_plain():
     out2 = dp(g)
     torch.testing.assert_close(out2["energy"], out["energy"], rtol=1e-6, atol=1e-4)
     torch.testing.assert_close(out2["forces"], out["forces"], rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_domain_parallel_two_gpus_p2p_matches_collective(tmp_path):
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    script = tmp_path / "dd.py"
+    script.write_text(
+        "import sys, torch\n"
+        f"sys.path.insert(0, {root!r})\n"
+        "from xnn_b200.parallel import distributed as D\n"
+        "from xnn_b200.data import synthetic, structure_to_graph\n"
+        "from xnn_b200.models.mace import MACE\n"
+        "from xnn_b200.parallel.domain import DomainParallel\n"
+        "dev = D.init_process_group('cuda', timeout_s=60)\n"
+        "torch.manual_seed(0)\n"
+        "m = MACE(species=[1, 8], cutoff=4.5, num_channels=32, n_rbf=8, num_interactions=2, max_ell=3,\n"
+        "         correlation=3, avg_num_neighbors=30.0).to(dev).eval()\n"
+        "g = structure_to_graph(synthetic.water_box(6000, seed=2), 4.5).to(dev)\n"
+        "outs = {}\n"
+        "for ex in ('collective', 'p2p'):\n"
+        "    dp = DomainParallel(m, skin=0.5, exchange=ex)\n"
+        "    for rep in range(2):\n"
+        "        outs[ex] = dp(g)\n"
+        "    dp.close()\n"
+        "a, b = outs['collective'], outs['p2p']\n"
+        "assert torch.allclose(a['energy'], b['energy'], rtol=1e-9, atol=1e-9), (a['energy'], b['energy'])\n"
+        "assert torch.allclose(a['forces'], b['forces'], rtol=1e-6, atol=1e-6)\n"
+        "assert torch.allclose(a['stress'], b['stress'], rtol=1e-6, atol=1e-7)\n"
+        "D.destroy_process_group()\n"
+        "print('ok')\n")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "10", "240", sys.executable, "-m", "torch.distributed.run", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", "29519", str(script)]
+    out = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert out.returncode == 0, out.stdout + out.stderr

@@ -23,6 +23,7 @@ from torch.nn import functional as F
 from torch.utils.checkpoint import checkpoint
 
 from ..ops import mace_ops as K
+from ..ops.lean_conv import lean_radial_conv
 from ..ops.radial import radial_network
 from ..ops.scatter import refresh_ghosts
 
@@ -105,9 +106,10 @@ def _edge_chunks(plan: K.EdgePlan, edge_index: Tensor, max_edges: Optional[int])
     """Receiver-contiguous edge chunks of at most ``max_edges`` edges (``None``: no chunking).
 
     With edges sorted by receiver, a chunk is the edge range of a range of receivers, so its
-    messages fill a contiguous block of node rows. Each chunk's radial network and message pass
-    run under activation checkpointing: the per-edge tensors of one chunk are alive at a time,
-    which bounds the memory of a force evaluation on millions of edges.
+    messages fill a contiguous block of node rows. On CUDA the chunks go to
+    :func:`~xnn_b200.ops.lean_conv.lean_radial_conv` (per-edge tensors of one chunk alive at a
+    time, recomputed in the backward); on the CPU each chunk runs under activation checkpointing.
+    Returns ``[((e0, e1), (n0, n1), plan_of_chunk), ...]``.
     """
     if max_edges is None or plan.n_edges <= max_edges or plan.dst_perm is not None:
         return None
@@ -124,7 +126,7 @@ def _edge_chunks(plan: K.EdgePlan, edge_index: Tensor, max_edges: Optional[int])
     for n0, n1 in bounds:
         e0, e1 = int(ptr[n0]), int(ptr[n1])
         ei = torch.stack([edge_index[0, e0:e1], edge_index[1, e0:e1] - n0])
-        out.append(((e0, e1), K.EdgePlan.build(ei, n1 - n0, assume_dst_sorted=True, n_src=N)))
+        out.append(((e0, e1), (n0, n1), K.EdgePlan.build(ei, n1 - n0, assume_dst_sorted=True, n_src=N)))
     return out
 
 
@@ -155,9 +157,12 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
         h_up = h @ _linear_blocks(blk.linear_up)[0]
         if chunks is None:
             A = _messages(h_up, r, Y, plan, blk, ef, P, C)               # (D, N, C)
+        elif h_up.is_cuda:
+            A = lean_radial_conv(h_up, r, Y, chunks, blk.conv_tp_weights, _conv_path_scale(blk, r),
+                                 ef.rbf.freqs, ef.rbf.norm, ef.cutoff, ef.envelope.p, P)
         else:
             A = torch.cat([checkpoint(_messages, h_up, r[e0:e1], Y[e0:e1], sub, blk, ef, P, C,
-                                      use_reentrant=False) for (e0, e1), sub in chunks], dim=1)
+                                      use_reentrant=False) for (e0, e1), _, sub in chunks], dim=1)
         mats = _linear_blocks(blk.linear)
         parts = []
         for l in range(P):

@@ -1,0 +1,97 @@
+"""Radial network + message pass for force evaluation on millions of edges, in bounded memory.
+
+``A[lm, d, c] = sum_{e: s->d} R(r_e)[l, c] x[s, c] Y[e, lm]`` evaluated over receiver-contiguous
+edge chunks; the per-edge tensors of the radial network (``R``, its tangent ``dR/dr`` and the
+hidden activations, several kB per edge) exist for one chunk at a time and are never saved.
+The backward recomputes ``R`` and ``dR/dr`` chunk by chunk (the forward-mode network of
+:mod:`xnn_b200.ops.radial`) and forms, per chunk, the edge cotangents ``g_r = sum gR dR/dr`` and
+``gY`` and the sender cotangent ``gx``. Saved state is ``x``, ``r`` and ``Y``: O(E) floats
+instead of O(E * P * C).
+
+First derivatives only (forces, stress, MD); parameter gradients are not formed, so training
+uses the ordinary path. CUDA only.
+"""
+from __future__ import annotations
+
+from typing import List, Sequence, Tuple
+
+import torch
+from torch import Tensor
+from torch.autograd import Function
+from torch.autograd.function import once_differentiable
+from torch.nn import functional as F
+
+from .. import _ext
+from . import gemm
+from .mace_ops import EdgePlan
+from .radial import RadialSpec, _eff, _forward
+
+
+def _primal(r: Tensor, We: List[Tensor], spec: RadialSpec) -> Tensor:
+    """``R`` only (no tangent rows): basis, hidden SiLU layers, output layer."""
+    E = r.shape[0]
+    H = _ext.ops().radial_basis(r.contiguous(), spec.freqs.to(r.device), spec.norm, spec.rc, spec.p)[:E]
+    for k in range(len(We) - 1):
+        H = F.silu(gemm.mm_raw(H.contiguous(), We[k]))
+        if spec.consts[k] != 1.0:
+            H = H * spec.consts[k]
+    return gemm.mm_raw(H.contiguous(), We[-1])
+
+
+Chunk = Tuple[Tuple[int, int], Tuple[int, int], EdgePlan]
+
+
+class _LeanRadialConv(Function):
+    @staticmethod
+    def forward(ctx, x: Tensor, r: Tensor, Y: Tensor, chunks: Sequence[Chunk], spec: RadialSpec, P: int,
+                *Ws: Tensor) -> Tensor:
+        C = x.shape[1]
+        N = chunks[-1][1][1]
+        K = _ext.ops()
+        We = _eff(Ws, spec)
+        A = x.new_empty((P * P, N, C))
+        xc = x.contiguous()
+        for (e0, e1), (n0, n1), sub in chunks:
+            R = _primal(r[e0:e1], We, spec).view(-1, P, C)
+            A[:, n0:n1] = K.conv_gather(n1 - n0, C, P, sub.dst_ptr, sub.src32, None, [xc], [R],
+                                        [Y[e0:e1].contiguous()])
+        ctx.chunks, ctx.spec, ctx.P = chunks, spec, P
+        ctx.save_for_backward(x, r, Y, *Ws)
+        return A
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx, G: Tensor):
+        x, r, Y = ctx.saved_tensors[:3]
+        Ws = ctx.saved_tensors[3:]
+        P, spec = ctx.P, ctx.spec
+        N_src, C = x.shape
+        K = _ext.ops()
+        We = _eff(Ws, spec)
+        xc = x.contiguous()
+        gx = torch.zeros_like(xc) if ctx.needs_input_grad[0] else None
+        g_r = torch.empty_like(r) if ctx.needs_input_grad[1] else None
+        gY = torch.empty_like(Y) if ctx.needs_input_grad[2] else None
+        for (e0, e1), (n0, n1), sub in ctx.chunks:
+            R, Rd, _, _ = _forward(r[e0:e1], We, spec)
+            R, Rd = R.view(-1, P, C), Rd.view(-1, P, C)
+            Gc = G[:, n0:n1].contiguous()
+            Yc = Y[e0:e1].contiguous()
+            want_y = gY is not None
+            gR, gYc, T1, _ = K.conv_edge(n1 - n0, C, P, e1 - e0, sub.dst_ptr, sub.src32, None, Gc, [Yc], [xc],
+                                         [gx is not None], True, [xc] if want_y else [], [R] if want_y else [])
+            if g_r is not None:
+                g_r[e0:e1] = (gR * Rd).sum((1, 2))
+            if want_y:
+                gY[e0:e1] = gYc
+            if gx is not None:
+                gx += K.conv_scatter(N_src, C, P, sub.src_ptr, sub.src_perm, [R], [T1])
+        return (gx, g_r, gY, None, None, None) + (None,) * len(Ws)
+
+
+def lean_radial_conv(x: Tensor, r: Tensor, Y: Tensor, chunks: Sequence[Chunk], net, col_scale: Tensor,
+                     freqs: Tensor, norm: float, rc: float, p: int, P: int) -> Tensor:
+    """``A (P*P, N, C)`` of the MACE message pass with the radial network ``net`` (see module notes)."""
+    spec = RadialSpec(net, col_scale, freqs, norm, rc, p)
+    Ws = [layer.weight for layer in net]
+    return _LeanRadialConv.apply(x, r, Y, chunks, spec, P, *Ws)
