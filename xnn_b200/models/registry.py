@@ -71,8 +71,23 @@ def prepare_model(cfg) -> nn.Module:
         spec = extra["long_range"] if isinstance(extra["long_range"], dict) else {}
         model = LatentEwald(model, **spec)
     if extra.get("dispersion"):
-        from .dispersion import DispersionCorrection
-        spec = extra["dispersion"]
-        spec = {"method": spec} if isinstance(spec, str) else dict(spec)
-        model = DispersionCorrection(model, **spec)
+        model = add_dispersion(model, extra["dispersion"])
     return model
+
+
+def add_dispersion(model, spec):
+    """Wrap ``model`` (or ``None``: pure dispersion) in a D3 / D4 correction.
+
+    ``spec`` is ``{"name": "d3" | "d4", **options}``, a bare name, or ``True`` (D4 defaults), as
+    the reference's ``add_dispersion`` (``src/xnn/common/models/registry.py:438``)."""
+    if isinstance(spec, str):
+        spec = {"name": spec}
+    opts = dict(spec) if isinstance(spec, dict) else {}
+    name = str(opts.pop("name", "d4")).lower()
+    if name == "d3":
+        from .d3 import D3_KEYS, D3Dispersion
+        return D3Dispersion(model, **{k: v for k, v in opts.items() if k in D3_KEYS})
+    if name == "d4":
+        from .d4 import D4Dispersion
+        return D4Dispersion(model, **opts)
+    raise KeyError(f"unknown dispersion model {name!r} (use 'd3' or 'd4')")
