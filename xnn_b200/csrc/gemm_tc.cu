@@ -20,6 +20,7 @@
 // Every wait is bounded: on a timeout the kernel records an error in `status`, stops issuing,
 // waits (bounded) for the MMAs it issued, frees its TMEM and returns.
 #include <algorithm>
+#include <cstdlib>
 
 #include "tc_common.cuh"
 
@@ -216,10 +217,25 @@ cudaError_t launch_rows(int M, int N, int K, const float* X, int ldx, const floa
 
 }  // namespace
 
+size_t gemm_ws_pack_floats(int K, int N);
+// XNN_B200_GEMM_WS=0 selects the staged kernel (comparison runs)
+static bool gemm_ws_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("XNN_B200_GEMM_WS");
+    on = (v != nullptr && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+cudaError_t gemm_tf32x3_ws(int M, int N, int K, const float* X, int ldx, const float* W, int64_t sk, int64_t sn,
+                           float* Bpack, float* Y, int ldy, const float* col_scale, int* status, long long spin_limit,
+                           cudaStream_t s);
+
+// workspace for the packed W of either kernel
 size_t gemm_rows_pack_floats(int K, int N) {
   const int KC = N <= 192 ? 32 : 16;
   const int n_chunks = (K + KC - 1) / KC;
-  return (size_t)n_chunks * 2 * KC * N;
+  return std::max((size_t)n_chunks * 2 * KC * N, gemm_ws_pack_floats(K, N));
 }
 
 cudaError_t gemm_tf32x3(int M, int N, int K, const float* X, int ldx, const float* W, int64_t sk, int64_t sn,
@@ -232,6 +248,12 @@ cudaError_t gemm_tf32x3(int M, int N, int K, const float* X, int ldx, const floa
   if (ldy % 4 != 0 || (reinterpret_cast<uintptr_t>(Y) & 15) != 0 || (reinterpret_cast<uintptr_t>(X) & 15) != 0 ||
       (reinterpret_cast<uintptr_t>(Bpack) & 15) != 0)
     return cudaErrorInvalidValue;
+  // the warp-specialized TMA kernel first; the staged kernel for what it does not cover
+  if (gemm_ws_enabled()) {
+    cudaError_t e = gemm_tf32x3_ws(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, s);
+    if (e != cudaErrorNotSupported) return e;
+    cudaGetLastError();
+  }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

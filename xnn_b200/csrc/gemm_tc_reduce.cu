@@ -10,6 +10,8 @@
 // the MMAs of chunk g. Each CTA writes its partial (K1, N)
 // block to a workspace and a second kernel sums the partials in a fixed order
 // (deterministic). The workspace is scratch memory of ctas * K1 * N floats owned by the caller.
+#include <cstdlib>
+
 #include "tc_common.cuh"
 
 namespace {
@@ -180,6 +182,20 @@ cudaError_t launch_reduce(int M, int K1, int N, const float* X, int ldx, const f
 
 int gemm_reduce_ctas(int M, int rows_per_cta) { return (M + rows_per_cta - 1) / rows_per_cta; }
 
+cudaError_t gemm_reduce_tf32x3_ws(int M, int K1, int N, const float* X, int ldx, const float* D, int ldd,
+                                  float* partial, size_t partial_floats, float* out, float scale, int* status,
+                                  long long spin_limit, cudaStream_t s);
+
+// XNN_B200_GEMM_WS=0 selects the staged kernel (comparison runs)
+static bool reduce_ws_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("XNN_B200_GEMM_WS");
+    on = (v != nullptr && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 cudaError_t gemm_reduce_tf32x3(int M, int K1, int N, const float* X, int ldx, const float* D, int ldd,
                                int rows_per_cta, float* partial, float* out, float scale, int* status,
                                long long spin_limit, cudaStream_t s) {
@@ -192,6 +208,13 @@ cudaError_t gemm_reduce_tf32x3(int M, int K1, int N, const float* X, int ldx, co
   const int64_t nout = (int64_t)K1 * N;
   if (M == 0) return cudaMemsetAsync(out, 0, nout * sizeof(float), s);
   const int ctas = gemm_reduce_ctas(M, rows_per_cta);
+  if (reduce_ws_enabled()) {
+    // the warp-specialized TMA kernel when its partials fit the workspace sized for this call
+    cudaError_t e = gemm_reduce_tf32x3_ws(M, K1, N, X, ldx, D, ldd, partial, (size_t)ctas * K1 * N, out, scale,
+                                          status, spin_limit, s);
+    if (e != cudaErrorNotSupported) return e;
+    cudaGetLastError();
+  }
   cudaError_t e = N <= 128 ? launch_reduce<32>(M, K1, N, X, ldx, D, ldd, rows_per_cta, partial, status, spin_limit, ctas, s)
                            : launch_reduce<16>(M, K1, N, X, ldx, D, ldd, rows_per_cta, partial, status, spin_limit, ctas, s);
   if (e != cudaSuccess) return e;

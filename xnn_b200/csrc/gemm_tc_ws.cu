@@ -1,0 +1,400 @@
+// Row GEMM Y[M, N] = (X[M, K] @ W[K, N]) * col_scale on tcgen05, warp-specialized and fed by TMA
+// (3xTF32, FP32 accuracy; K <= 512, N <= 512 and a multiple of 16).
+//
+// One persistent CTA per SM, 8 warps with fixed roles:
+//   warp 0      producer: per pipeline step, one 2D TMA tile load of X (128 rows x KC, swizzled
+//               to the row width) and one 1D bulk copy of the packed W chunk, both completing on
+//               the stage's `full` mbarrier;
+//   warps 2-3   converter: rewrite the swizzled row-major X tile into the canonical K-major
+//               layout as TF32 hi and lo halves (x = hi + lo), fence to the async proxy and arrive
+//               on `conv`;
+//   warp 1      MMA issuer (one lane): hi*hi + hi*lo + lo*hi tcgen05.mma (kind::tf32, M = 128,
+//               N = NS <= 256) into one of two TMEM accumulators, commits to the stage's `empty`
+//               barrier and, after the unit's last chunk, to the accumulator's `full` barrier;
+//   warps 4-7   epilogue: tcgen05.ld of the accumulator (warp 4 + q owns TMEM lanes 32q..32q+31),
+//               column scale, swizzled staging in shared memory and 2D TMA stores of 32 x 16 tiles;
+//               arrive on the accumulator's `empty` barrier so the next unit can reuse it.
+// A unit of work is (row tile, column half): N > 256 is split into two halves of NS = N / 2
+// columns so that two accumulators (double buffering) fit in the 512 TMEM columns. The stages of
+// the X/W ring and the two accumulators let loads, conversion, MMAs and stores of consecutive
+// units overlap.
+//
+// Every wait is bounded (`spin_limit` polls); a role that gives up records code 4 in `status` and
+// raises a shared abort flag that makes the other roles leave their loops; the MMA warp then waits
+// (bounded) for its issued MMAs before TMEM is freed. Loads never use cluster multicast.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "tc_common.cuh"
+
+namespace {
+
+constexpr int WS_STAGES = 2;
+constexpr int WS_THREADS = 256;
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      :: "r"(tc::smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(tc::smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];"
+               :: "l"(map), "r"(x), "r"(y), "r"(tc::smem_u32(src)) : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(tc::smem_u32(bar)) : "memory");
+}
+
+// bounded wait that also gives up when another role raised the abort flag
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, long long limit,
+                                              volatile int* abort_flag, int* status) {
+  long long n = 0;
+  while (!tc::mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (++n > limit) {
+      *abort_flag = 1;
+      atomicExch(status, 4);
+      return false;
+    }
+    __nanosleep(20);
+  }
+  return true;
+}
+
+// W packed per (column half h, K chunk c): [hi | lo], each NS x KC in the canonical K-major layout
+template <int KC>
+__global__ void gemm_ws_pack_kernel(int K, int N, int NS, const float* __restrict__ W, int64_t sk, int64_t sn,
+                                    float* __restrict__ out) {
+  const int n_chunks = (K + KC - 1) / KC;
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t tot = (int64_t)n_chunks * KC * N;
+  if (idx >= tot) return;
+  const int n = (int)(idx % N);
+  const int kl = (int)((idx / N) % KC);
+  const int c = (int)(idx / ((int64_t)N * KC));
+  const int k = c * KC + kl;
+  const int h = n / NS, nl = n % NS;
+  const float w = k < K ? W[k * sk + n * sn] : 0.f;
+  float hi, lo;
+  tc::split_tf32(w, hi, lo);
+  const uint32_t off = ((uint32_t)(nl >> 3) * (KC / 4) * 128u + (uint32_t)(kl >> 2) * 128u + (uint32_t)(nl & 7) * 16u +
+                        (uint32_t)(kl & 3) * 4u) / 4;
+  float* base = out + ((int64_t)h * n_chunks + c) * 2 * NS * KC;
+  base[off] = hi;
+  base[(int64_t)NS * KC + off] = lo;
+}
+
+template <int KC>
+struct WsLayout {
+  static constexpr uint32_t A_BYTES = 128 * KC * 4;
+  static constexpr uint32_t SW_MASK = KC == 32 ? 7 : (KC == 16 ? 3 : 1);   // 128 / 64 / 32-byte swizzle
+  uint32_t w_bytes;        // one stage of W: hi + lo
+  uint32_t stage_bytes;    // raw + hi + lo + W, rounded to 1024
+  uint32_t stage0;         // offset of stage 0
+  uint32_t staging;        // epilogue staging: 4 warps x 2 buffers x 2 KB
+  uint32_t bars;
+  uint32_t total;
+  __host__ __device__ WsLayout(int NS) {
+    w_bytes = (uint32_t)NS * KC * 4 * 2;
+    stage_bytes = (3 * A_BYTES + w_bytes + 1023) / 1024 * 1024;
+    stage0 = 0;
+    staging = WS_STAGES * stage_bytes;
+    bars = staging + 4 * 2 * 2048;
+    total = bars + 256;
+  }
+};
+
+template <int KC>
+__global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
+    const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapY, int M, int N, int K,
+    int NS, const float* __restrict__ Bpack, const float* __restrict__ col_scale, int* status,
+    long long spin_limit, int tmem_cols, uint32_t acc_stride) {
+  using namespace tc;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // align the dynamic buffer to 1024 bytes (swizzle atoms)
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const WsLayout<KC> L(NS);
+  constexpr uint32_t A_BYTES = WsLayout<KC>::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* conv = full + WS_STAGES;
+  uint64_t* empty = conv + WS_STAGES;
+  uint64_t* accf = empty + WS_STAGES;
+  uint64_t* acce = accf + 2;
+  uint64_t* fin = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_chunks = (K + KC - 1) / KC;
+  const int n_sub = N / NS;
+  const int tiles = (M + 127) / 128;
+  const int units = tiles * n_sub;
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(tmem_slot)), "r"(tmem_cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (tid == 32) {
+    for (int s = 0; s < WS_STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(conv + s, 64);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf + b, 1);
+      mbar_init(acce + b, 128);
+    }
+    mbar_init(fin, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t W_BYTES = L.w_bytes;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      long long it = 0;
+      int last_s = -1;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        const int tile = u / n_sub, h = u % n_sub;
+        for (int c = 0; c < n_chunks; ++c, ++it) {
+          const int s = (int)(it % WS_STAGES);
+          if (it >= WS_STAGES &&
+              !wait_or_abort(empty + s, (uint32_t)(((it / WS_STAGES) - 1) & 1), spin_limit, abort_flag, status))
+            break;
+          unsigned char* st = smem + L.stage0 + (uint32_t)s * L.stage_bytes;
+          mbar_arrive_expect_tx(full + s, A_BYTES + W_BYTES);
+          tma_load_2d(st, &mapA, c * KC, tile * 128, full + s);
+          bulk_g2s(st + 3 * A_BYTES, Bpack + ((int64_t)h * n_chunks + c) * 2 * NS * KC, W_BYTES, full + s);
+          last_s = s;
+        }
+      }
+      // after an abort, let the last copies land before the CTA leaves
+      if (*abort_flag && last_s >= 0) mbar_wait(full + last_s, (uint32_t)(((it - 1) / WS_STAGES) & 1), spin_limit);
+    }
+  } else if (warp == 2 || warp == 3) {
+    // ---------------------------------------------------------------- converter
+    const int ct = tid - 64;           // 0..63
+    long long it = 0;
+    bool go = true;
+    for (int u = blockIdx.x; u < units && go; u += gridDim.x) {
+      for (int c = 0; c < n_chunks; ++c, ++it) {
+        const int s = (int)(it % WS_STAGES);
+        if (!wait_or_abort(full + s, (uint32_t)((it / WS_STAGES) & 1), spin_limit, abort_flag, status)) {
+          go = false;
+          break;
+        }
+        unsigned char* st = smem + L.stage0 + (uint32_t)s * L.stage_bytes;
+        const unsigned char* raw = st;
+        unsigned char* hi = st + A_BYTES;
+        unsigned char* lo = st + 2 * A_BYTES;
+        // flat index i of 16-byte chunks in canonical order: ((row_group * KC/4) + k4) * 8 + r8
+        for (int i = ct; i < 128 * KC / 4; i += 64) {
+          const int r8 = i & 7;
+          const int k4 = (i >> 3) % (KC / 4);
+          const int rg = (i >> 3) / (KC / 4);
+          const uint32_t lin = (uint32_t)(rg * 8 + r8) * (KC * 4) + (uint32_t)k4 * 16;
+          const uint32_t phys = lin ^ (((lin >> 7) & WsLayout<KC>::SW_MASK) << 4);
+          const float4 x = *reinterpret_cast<const float4*>(raw + phys);
+          float4 h4, l4;
+          split4(x, h4, l4);
+          *reinterpret_cast<float4*>(hi + (uint32_t)i * 16) = h4;
+          *reinterpret_cast<float4*>(lo + (uint32_t)i * 16) = l4;
+        }
+        fence_async_smem();
+        mbar_arrive(conv + s);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_tf32(NS, 0, 0);
+      const uint32_t lbo = 128, sbo = (KC / 4) * 128;
+      long long it = 0, uidx = 0;
+      bool go = true;
+      for (int u = blockIdx.x; u < units && go; u += gridDim.x, ++uidx) {
+        const int b = (int)(uidx & 1);
+        if (uidx >= 2 && !wait_or_abort(acce + b, (uint32_t)(((uidx >> 1) - 1) & 1), spin_limit, abort_flag, status))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)b * acc_stride;
+        for (int c = 0; c < n_chunks; ++c, ++it) {
+          const int s = (int)(it % WS_STAGES);
+          if (!wait_or_abort(conv + s, (uint32_t)((it / WS_STAGES) & 1), spin_limit, abort_flag, status)) {
+            go = false;
+            break;
+          }
+          tc_fence_after();
+          const unsigned char* st = smem + L.stage0 + (uint32_t)s * L.stage_bytes;
+          const uint32_t ah = smem_u32(st + A_BYTES), al = smem_u32(st + 2 * A_BYTES);
+          const uint32_t bh = smem_u32(st + 3 * A_BYTES), bl = bh + W_BYTES / 2;
+#pragma unroll
+          for (int k = 0; k < KC / 8; ++k) {
+            const uint32_t off = (uint32_t)k * 256u;
+            const uint32_t acc = (c > 0 || k > 0) ? 1u : 0u;
+            mma_tf32(d, make_desc2(ah + off, lbo, sbo), make_desc2(bh + off, lbo, sbo), idesc, acc);
+            mma_tf32(d, make_desc2(ah + off, lbo, sbo), make_desc2(bl + off, lbo, sbo), idesc, 1u);
+            mma_tf32(d, make_desc2(al + off, lbo, sbo), make_desc2(bh + off, lbo, sbo), idesc, 1u);
+          }
+          commit_to(empty + s);
+        }
+        if (go) commit_to(accf + b);
+      }
+      // all issued MMAs complete before TMEM is released
+      commit_to(fin);
+      mbar_wait(fin, 0, spin_limit);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 4..7)
+    const int q = warp - 4;            // TMEM lane quarter
+    unsigned char* stage_buf = smem + L.staging + (uint32_t)q * 2 * 2048;
+    long long uidx = 0;
+    int nst = 0;                       // stores issued by this warp
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++uidx) {
+      const int b = (int)(uidx & 1);
+      if (!wait_or_abort(accf + b, (uint32_t)((uidx >> 1) & 1), spin_limit, abort_flag, status)) break;
+      tc_fence_after();
+      const int tile = u / n_sub, h = u % n_sub;
+      const uint32_t lane_base = tmem + (uint32_t)b * acc_stride + ((uint32_t)(q * 32) << 16);
+      for (int c0 = 0; c0 < NS; c0 += 16, ++nst) {
+        float v[16];
+        tmem_ld16(lane_base + (uint32_t)c0, v);
+        if (col_scale) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] *= __ldg(col_scale + h * NS + c0 + j);
+        }
+        unsigned char* sb = stage_buf + (uint32_t)(nst & 1) * 2048;
+        if (nst >= 2) {
+          if (lane == 0) bulk_wait_read1();       // the store that last read this buffer is done
+          __syncwarp();
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t lin = (uint32_t)lane * 64u + (uint32_t)j * 16u;
+          const uint32_t phys = lin ^ (((lin >> 7) & 3u) << 4);
+          *reinterpret_cast<float4*>(sb + phys) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&mapY, sb, h * NS + c0, tile * 128 + q * 32);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acce + b);
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(tmem_cols));
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+bool encode_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t row_bytes, uint32_t box_c,
+               uint32_t box_r, CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_c, box_r};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int KC>
+cudaError_t launch_ws(int M, int N, int K, const float* X, int ldx, const float* W, int64_t sk, int64_t sn,
+                      float* Bpack, float* Y, int ldy, const float* col_scale, int* status, long long spin_limit,
+                      int sms, cudaStream_t s) {
+  const int NS = N <= 256 ? N : N / 2;
+  const CUtensorMapSwizzle swA = KC == 32 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                          : (KC == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  CUtensorMap mapA, mapY;
+  if (!encode_2d(&mapA, X, (uint64_t)K, (uint64_t)M, (uint64_t)ldx * 4, KC, 128, swA)) return cudaErrorNotSupported;
+  if (!encode_2d(&mapY, Y, (uint64_t)N, (uint64_t)M, (uint64_t)ldy * 4, 16, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+    return cudaErrorNotSupported;
+  const int n_chunks = (K + KC - 1) / KC;
+  const int64_t tot = (int64_t)n_chunks * KC * N;
+  gemm_ws_pack_kernel<KC><<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(K, N, NS, W, sk, sn, Bpack);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const WsLayout<KC> L(NS);
+  const size_t smem = L.total + 1024;       // + alignment slack
+  if (smem > 227 * 1024) return cudaErrorNotSupported;
+  e = cudaFuncSetAttribute(gemm_ws_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const uint32_t acc_stride = NS <= 128 ? 128u : 256u;
+  const int tmem_cols = (int)(2 * acc_stride);
+  const int units = ((M + 127) / 128) * (N / NS);
+  const int grid = std::min(units, sms);
+  gemm_ws_kernel<KC><<<grid, WS_THREADS, smem, s>>>(mapA, mapY, M, N, K, NS, Bpack, col_scale, status, spin_limit,
+                                                    tmem_cols, acc_stride);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// K chunk: the whole K when it is small, 32 unless the column half is wide (shared memory)
+int gemm_ws_kc(int K, int N) {
+  const int NS = N <= 256 ? N : N / 2;
+  if (K <= 8) return 8;
+  if (K <= 16 || NS > 192) return 16;
+  return 32;
+}
+
+size_t gemm_ws_pack_floats(int K, int N) {
+  const int KC = gemm_ws_kc(K, N);
+  return (size_t)((K + KC - 1) / KC) * 2 * KC * N;
+}
+
+// cudaErrorNotSupported: shape or layout outside this kernel's scope (the caller falls back)
+cudaError_t gemm_tf32x3_ws(int M, int N, int K, const float* X, int ldx, const float* W, int64_t sk, int64_t sn,
+                           float* Bpack, float* Y, int ldy, const float* col_scale, int* status, long long spin_limit,
+                           cudaStream_t s) {
+  if (M == 0) return cudaSuccess;
+  if (N < 16 || N > 512 || N % 16 != 0 || K < 1 || K > 512) return cudaErrorNotSupported;
+  const int NS = N <= 256 ? N : N / 2;
+  if (NS % 16 != 0 || NS * (N / NS) != N) return cudaErrorNotSupported;
+  if (ldx % 4 != 0 || ldy % 4 != 0 || (reinterpret_cast<uintptr_t>(X) & 15) || (reinterpret_cast<uintptr_t>(Y) & 15) ||
+      (reinterpret_cast<uintptr_t>(Bpack) & 15))
+    return cudaErrorNotSupported;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  switch (gemm_ws_kc(K, N)) {
+    case 8: return launch_ws<8>(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, sms, s);
+    case 16: return launch_ws<16>(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, sms, s);
+    default: return launch_ws<32>(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, sms, s);
+  }
+}
