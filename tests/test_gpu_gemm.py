@@ -44,3 +44,25 @@ def test_tf32x3_reduce_accuracy(M, K1, N):
     ref = X.double().t() @ D.double()
     err = (G.double() - ref).abs().max() / ref.abs().max()
     assert err < 1e-5, float(err)
+
+
+@pytest.mark.parametrize("M,K,N", [(21570, 96, 96), (30000, 96, 672), (17000, 64, 16)])
+def test_matmul_autograd_two_orders(M, K, N):
+    """The differentiable tensor-core product against float64 autograd, first and second order."""
+    from xnn_b200.ops import gemm
+    g = torch.Generator(device="cuda").manual_seed(1)
+    X = torch.randn(M, K, device="cuda", generator=g, requires_grad=True)
+    W = torch.randn(K, N, device="cuda", generator=g, requires_grad=True) / K ** 0.5
+    V = torch.randn(M, N, device="cuda", generator=g)
+    Y = gemm.matmul(X, W)
+    Xd, Wd = X.detach().double().requires_grad_(True), W.detach().double().requires_grad_(True)
+    Yd = Xd @ Wd
+    torch.testing.assert_close(Y.double(), Yd, rtol=1e-5, atol=1e-5)
+    gX, gW = torch.autograd.grad((Y * V).sum(), (X, W), create_graph=True)
+    gXd, gWd = torch.autograd.grad((Yd * V.double()).sum(), (Xd, Wd), create_graph=True)
+    torch.testing.assert_close(gX.double(), gXd, rtol=1e-5, atol=1e-4)
+    torch.testing.assert_close(gW.double(), gWd, rtol=1e-5, atol=1e-3)
+    U = torch.randn_like(gX)
+    h, = torch.autograd.grad((gX * U).sum(), W)
+    hd, = torch.autograd.grad((gXd * U.double()).sum(), Wd)
+    torch.testing.assert_close(h.double(), hd, rtol=1e-5, atol=1e-3)

@@ -22,7 +22,7 @@ cudaError_t conv_gather(int, int, int, const int64_t*, const int*, const int64_t
 template <typename T>
 cudaError_t conv_edge(int, int, int, const int64_t*, const int*, const int64_t*, const T*, int,
                       const T* const*, const T* const*, T* const*, int, const T* const*, const T* const*, T*, T*,
-                      cudaStream_t);
+                      const T*, T*, cudaStream_t);
 template <typename T>
 cudaError_t conv_scatter(int, int, int, const int64_t*, const int64_t*, int, const T* const*, const T* const*,
                          T*, cudaStream_t);
@@ -281,7 +281,9 @@ std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t
                                         torch::Tensor src, c10::optional<torch::Tensor> perm, torch::Tensor G,
                                         std::vector<torch::Tensor> Ys, std::vector<c10::optional<torch::Tensor>> xs,
                                         std::vector<bool> want_T, bool want_gR,
-                                        std::vector<torch::Tensor> xY, std::vector<torch::Tensor> RY) {
+                                        std::vector<torch::Tensor> xY, std::vector<torch::Tensor> RY,
+                                        c10::optional<torch::Tensor> Rd) {
+  // with Rd (E, P, C): the first output is g_r[e] = sum_{l,c} gR[e,l,c] Rd[e,l,c] (E,) instead of gR
   TORCH_CHECK(Ys.size() == xs.size() && Ys.size() == want_T.size() && Ys.size() <= 2,
               "conv_edge: 0-2 Y terms with matching x / want_T");
   TORCH_CHECK(xY.size() == RY.size() && xY.size() <= 2, "conv_edge: 0-2 (x, R) terms for gY");
@@ -290,7 +292,12 @@ std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t
   const int64_t D = P * P;
   const int64_t cpl = std::min<int64_t>(4, std::max<int64_t>(1, (C + 31) / 32));
   const bool split = (C + 32 * cpl - 1) / (32 * cpl) > 1;
-  torch::Tensor gR = (want_gR && !Ys.empty()) ? torch::empty({E, P, C}, G.options()) : torch::Tensor();
+  const bool contract = Rd.has_value() && Rd->defined();
+  if (contract) check_cuda(*Rd, "Rd");
+  torch::Tensor gR = (want_gR && !Ys.empty() && !contract) ? torch::empty({E, P, C}, G.options()) : torch::Tensor();
+  torch::Tensor g_r = (want_gR && !Ys.empty() && contract)
+                          ? (split ? torch::zeros({E}, G.options()) : torch::empty({E}, G.options()))
+                          : torch::Tensor();
   torch::Tensor gY = xY.empty() ? torch::Tensor()
                                 : (split ? torch::zeros({E, D}, G.options()) : torch::empty({E, D}, G.options()));
   std::vector<torch::Tensor> Ts(2);
@@ -317,9 +324,11 @@ std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t
                                     G.data_ptr<scalar_t>(), (int)Ys.size(), pY.data(), px.data(), pT.data(),
                                     (int)xY.size(), pxY.data(), pRY.data(),
                                     gR.defined() ? gR.data_ptr<scalar_t>() : nullptr,
-                                    gY.defined() ? gY.data_ptr<scalar_t>() : nullptr, st));
+                                    gY.defined() ? gY.data_ptr<scalar_t>() : nullptr,
+                                    contract ? Rd->data_ptr<scalar_t>() : nullptr,
+                                    g_r.defined() ? g_r.data_ptr<scalar_t>() : nullptr, st));
   });
-  return {gR, gY, Ts[0], Ts[1]};
+  return {contract ? g_r : gR, gY, Ts[0], Ts[1]};
 }
 
 torch::Tensor conv_scatter_op(int64_t N, int64_t C, int64_t P, torch::Tensor src_ptr, torch::Tensor src_perm,
@@ -403,7 +412,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("edge_geometry_bwd", &edge_geometry_bwd);
   m.def("edge_geometry_jvp", &edge_geometry_jvp);
   m.def("conv_gather", &conv_gather_op);
-  m.def("conv_edge", &conv_edge_op);
+  m.def("conv_edge", &conv_edge_op, pybind11::arg("N"), pybind11::arg("C"), pybind11::arg("P"), pybind11::arg("E"),
+        pybind11::arg("dst_ptr"), pybind11::arg("src"), pybind11::arg("perm"), pybind11::arg("G"), pybind11::arg("Ys"),
+        pybind11::arg("xs"), pybind11::arg("want_T"), pybind11::arg("want_gR"), pybind11::arg("xY"),
+        pybind11::arg("RY"), pybind11::arg("Rd") = pybind11::none());
   m.def("conv_scatter", &conv_scatter_op);
   m.def("symcon_fwd", &symcon_fwd_op);
   m.def("symcon_bwd", &symcon_bwd_op);

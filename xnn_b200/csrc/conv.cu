@@ -126,7 +126,7 @@ template <typename T, int P, int CPL, int WPA>
 __global__ void __launch_bounds__(32 * WPA) conv_edge_kernel(
     int N, int C, const int64_t* __restrict__ dst_ptr, const int* __restrict__ src,
     const int64_t* __restrict__ perm, const T* __restrict__ G, EdgeTerms<T> tE, PairTerms<T> tY,
-    T* __restrict__ gR, T* __restrict__ gY, int atomic_gY) {
+    T* __restrict__ gR, T* __restrict__ gY, int atomic_gY, const T* __restrict__ Rd, T* __restrict__ g_r) {
   constexpr int D = P * P;
   const int i = blockIdx.x;
   const int w = threadIdx.x >> 5;
@@ -180,6 +180,23 @@ __global__ void __launch_bounds__(32 * WPA) conv_edge_kernel(
 #pragma unroll
             for (int l = 0; l < P; ++l) gR[(e * P + l) * C + c] = out[q][l];
           }
+        }
+      } else if (Rd != nullptr) {
+        // contracted with the tangent dR/dr of the radial network: one scalar per edge
+        T acc = T(0);
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+          const int c = cbase + lane + 32 * q;
+          if (c < C) {
+#pragma unroll
+            for (int l = 0; l < P; ++l) acc += out[q][l] * __ldg(Rd + (e * P + l) * C + c);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+          if (atomic_gY) atomicAdd(g_r + e, acc);
+          else g_r[e] = acc;
         }
       }
     }
@@ -315,7 +332,8 @@ cudaError_t conv_gather(int N, int C, int P, const int64_t* dst_ptr, const int* 
 template <typename T>
 cudaError_t conv_edge(int N, int C, int P, const int64_t* dst_ptr, const int* src, const int64_t* perm,
                       const T* G, int nE, const T* const* Ys, const T* const* xs, T* const* Touts,
-                      int nY, const T* const* xY, const T* const* RY, T* gR, T* gY, cudaStream_t stream) {
+                      int nY, const T* const* xY, const T* const* RY, T* gR, T* gY, const T* Rd, T* g_r,
+                      cudaStream_t stream) {
   if (N == 0) return cudaSuccess;
   if (nE < 0 || nE > 2 || nY < 0 || nY > 2) return cudaErrorInvalidValue;
   EdgeTerms<T> tE;
@@ -330,7 +348,7 @@ cudaError_t conv_edge(int N, int C, int P, const int64_t* dst_ptr, const int* sr
   const int gy = (C + 32 * cpl - 1) / (32 * cpl);
   dim3 grid(N, gy);
   const int atomic_gY = gy > 1 ? 1 : 0;
-  XNN_P_CPL_SWITCH(P, cpl, conv_edge_kernel<T, PP, QQ, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, dst_ptr, src, perm, G, tE, tY, gR, gY, atomic_gY));
+  XNN_P_CPL_SWITCH(P, cpl, conv_edge_kernel<T, PP, QQ, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, dst_ptr, src, perm, G, tE, tY, gR, gY, atomic_gY, Rd, g_r));
   return cudaGetLastError();
 }
 
@@ -357,7 +375,7 @@ cudaError_t conv_scatter(int N, int C, int P, const int64_t* src_ptr, const int6
                                       cudaStream_t);                                                  \
   template cudaError_t conv_edge<T>(int, int, int, const int64_t*, const int*, const int64_t*,       \
                                     const T*, int, const T* const*, const T* const*, T* const*, int,  \
-                                    const T* const*, const T* const*, T*, T*, cudaStream_t);          \
+                                    const T* const*, const T* const*, T*, T*, const T*, T*, cudaStream_t);          \
   template cudaError_t conv_scatter<T>(int, int, int, const int64_t*, const int64_t*, int,           \
                                        const T* const*, const T* const*, T*, cudaStream_t);
 XNN_INST(float)

@@ -22,6 +22,7 @@ from torch import Tensor
 from torch.nn import functional as F
 from torch.utils.checkpoint import checkpoint
 
+from ..ops import gemm
 from ..ops import mace_ops as K
 from ..ops.lean_conv import lean_radial_conv
 from ..ops.radial import radial_network
@@ -49,7 +50,7 @@ def _species_weights(tp, n_el: int, block: int = 0) -> Tensor:
 def species_linear(h: Tensor, z: Tensor, Wz: Tensor) -> Tensor:
     """``out[i] = h[i] @ Wz[z_i]`` for ``h (..., N, C_in)`` and ``Wz (n_el, C_in, C_out)``."""
     n_el, c_in, c_out = Wz.shape
-    full = h @ Wz.permute(1, 0, 2).reshape(c_in, n_el * c_out)      # (..., N, n_el*C_out)
+    full = gemm.matmul(h, Wz.permute(1, 0, 2).reshape(c_in, n_el * c_out))   # (..., N, n_el*C_out)
     full = full.view(*h.shape[:-1], n_el, c_out)
     idx = z.view(*([1] * (h.dim() - 2)), -1, 1, 1).expand(*h.shape[:-1], 1, c_out)
     return full.gather(-2, idx).squeeze(-2)
@@ -154,7 +155,7 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
         if t > 0:
             h = refresh_ghosts(h)
         sc = species_linear(h, z, _species_weights(blk.skip_tp, n_el)) if blk.residual else None
-        h_up = h @ _linear_blocks(blk.linear_up)[0]
+        h_up = gemm.matmul(h, _linear_blocks(blk.linear_up)[0])
         if chunks is None:
             A = _messages(h_up, r, Y, plan, blk, ef, P, C)               # (D, N, C)
         elif h_up.is_cuda:
@@ -167,7 +168,7 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
         parts = []
         for l in range(P):
             blk_l = A[l * l:(l + 1) * (l + 1)]
-            parts.append(blk_l @ (mats[l] / blk.avg_num_neighbors))
+            parts.append(gemm.matmul(blk_l, mats[l] / blk.avg_num_neighbors))
         A2 = torch.cat(parts, 0) if P > 1 else parts[0]
         if not blk.residual:
             outs = []
@@ -177,7 +178,7 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
         sym = prod.symmetric_contractions.contractions[0]
         W = torch.cat(list(sym.weights), dim=1)                         # (n_el, K, C)
         B = K.symmetric_contraction(A2, W, z, lmax, sym.correlation)
-        h = B @ _linear_blocks(prod.linear)[0]
+        h = gemm.matmul(B, _linear_blocks(prod.linear)[0])
         if prod.use_sc and sc is not None:
             h = h + sc
         inter = inter + readout(h).squeeze(-1)

@@ -1,8 +1,10 @@
 """Matrix products of the hot paths on the sm_100a tensor cores (``csrc/gemm_tc.cu``).
 
-:func:`matmul` computes ``X @ W`` (optionally times a per-column scale) for float32 CUDA
-operands with a tcgen05 kernel accumulating in TMEM, using the 3xTF32 split so the result
-keeps float32 accuracy; it is differentiable (the backward products run through it as well).
+:func:`matmul` computes ``X @ W`` for float32 CUDA operands with a tcgen05 kernel accumulating
+in TMEM, using the 3xTF32 split so the result keeps float32 accuracy; it is differentiable to
+any order (its backward products run through :func:`matmul` / :func:`matmul_t` again).
+:func:`mm_raw` / :func:`mm_t_raw` are the same products without autograd (with an optional
+per-column scale).
 Other dtypes, devices or shapes fall back to ``torch.mm``. ``XNN_B200_TC_GEMM=0`` disables
 the tensor-core path.
 """
@@ -13,6 +15,7 @@ from typing import Dict, Optional
 
 import torch
 from torch import Tensor
+from torch.autograd import Function
 
 from .. import _ext
 
@@ -81,3 +84,80 @@ def mm_t_raw(X: Tensor, D: Tensor) -> Tensor:
     if reduce_supported(X, D):
         return _ext.ops().gemm_reduce_tf32x3(X, D, rows_per_cta(X.shape[0]), 1.0, _status(X.device), SPIN_LIMIT)
     return X.t() @ D
+
+
+# --------------------------------------------------------------------------- differentiable products
+class _MM(Function):
+    """``X @ W`` on the tensor cores; its derivatives are products of the same two kinds, so it
+    differentiates to any order (force training takes second derivatives through node linears)."""
+
+    @staticmethod
+    def forward(ctx, X: Tensor, W: Tensor) -> Tensor:
+        ctx.save_for_backward(X, W)
+        return mm_raw(X.contiguous(), W)
+
+    @staticmethod
+    def backward(ctx, G: Tensor):
+        X, W = ctx.saved_tensors
+        gX = matmul(G, W.t()) if ctx.needs_input_grad[0] else None
+        gW = matmul_t(X, G) if ctx.needs_input_grad[1] else None
+        return gX, gW
+
+
+class _MMT(Function):
+    """``X^T @ D`` (a reduction over the rows) on the tensor cores."""
+
+    @staticmethod
+    def forward(ctx, X: Tensor, D: Tensor) -> Tensor:
+        ctx.save_for_backward(X, D)
+        return mm_t_raw(X.contiguous(), D.contiguous())
+
+    @staticmethod
+    def backward(ctx, G: Tensor):
+        X, D = ctx.saved_tensors
+        gX = matmul(D, G.t()) if ctx.needs_input_grad[0] else None
+        gD = matmul(X, G) if ctx.needs_input_grad[1] else None
+        return gX, gD
+
+
+def _column_block(N: int) -> int:
+    """Largest multiple of 16 up to 256 dividing ``N`` (0: none)."""
+    for c in range(256, 15, -16):
+        if N % c == 0:
+            return c
+    return 0
+
+
+#: below this many rows the library GEMM wins: a 128-row tile per CTA leaves most SMs idle
+MIN_ROWS = int(os.environ.get("XNN_B200_TC_MIN_ROWS", "16384"))
+
+
+def _tc_ok(X: Tensor, W: Tensor) -> bool:
+    rows = X.numel() // max(X.shape[-1], 1) if X.dim() else 0
+    return (enabled() and X.is_cuda and X.dtype == torch.float32 and W.dtype == torch.float32
+            and rows >= MIN_ROWS and _ext.cuda_available())
+
+
+def matmul(X: Tensor, W: Tensor) -> Tensor:
+    """``X @ W`` for ``X (..., K)``, ``W (K, N)``: tensor cores for float32 CUDA operands
+    (columns in blocks when ``N > 512``), ``torch.matmul`` otherwise."""
+    if not _tc_ok(X, W) or X.shape[-1] == 0:
+        return X @ W
+    lead = X.shape[:-1]
+    X2 = X.reshape(-1, X.shape[-1])
+    N = W.shape[1]
+    if 16 <= N <= 512 and N % 16 == 0:
+        Y = _MM.apply(X2, W)
+    else:
+        c = _column_block(N)
+        if c == 0:
+            return X @ W
+        Y = torch.cat([_MM.apply(X2, W[:, j:j + c]) for j in range(0, N, c)], dim=1)
+    return Y.reshape(*lead, N)
+
+
+def matmul_t(X: Tensor, D: Tensor) -> Tensor:
+    """``X^T @ D`` summed over the rows of ``X (M, K1)`` and ``D (M, N)``."""
+    if not _tc_ok(X, D) or not reduce_supported(X.contiguous(), D.contiguous()):
+        return X.t() @ D
+    return _MMT.apply(X, D)

@@ -78,10 +78,12 @@ class _LeanRadialConv(Function):
             Gc = G[:, n0:n1].contiguous()
             Yc = Y[e0:e1].contiguous()
             want_y = gY is not None
-            gR, gYc, T1, _ = K.conv_edge(n1 - n0, C, P, e1 - e0, sub.dst_ptr, sub.src32, None, Gc, [Yc], [xc],
-                                         [gx is not None], True, [xc] if want_y else [], [R] if want_y else [])
+            # the edge kernel contracts gR with dR/dr itself: g_r without the (E, P, C) gR tensor
+            g_rc, gYc, T1, _ = K.conv_edge(n1 - n0, C, P, e1 - e0, sub.dst_ptr, sub.src32, None, Gc, [Yc], [xc],
+                                           [gx is not None], g_r is not None, [xc] if want_y else [],
+                                           [R] if want_y else [], Rd.contiguous())
             if g_r is not None:
-                g_r[e0:e1] = (gR * Rd).sum((1, 2))
+                g_r[e0:e1] = g_rc
             if want_y:
                 gY[e0:e1] = gYc
             if gx is not None:
