@@ -225,7 +225,7 @@ def main():
     trainer = Trainer(cfg, ds, val=[], test=[])
     dev = trainer.device
     # fixed-capacity padded batches in pinned host memory
-    cap = trainer.capacity_for([ds], B)
+    cap = trainer.capacity_for_batches([graphs[k * B:(k + 1) * B] for k in range(args.pool)])
     if world > 1:
         t = torch.tensor(cap, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -211,6 +211,22 @@ class Trainer:
         e = sum(es)
         return int(n * (1 + h)) + 2, int(e * (1 + h)) + 1, batch_size + 1
 
+    def capacity_for_batches(self, batches, headroom: Optional[float] = None):
+        """Padding capacities covering the given batches (lists of graphs, or collated graphs).
+
+        Sizing the captured step to the batches a run actually draws (instead of the worst case
+        of any ``batch_size`` structures) keeps the padded work close to the real work."""
+        h = self.cfg.trainer.graph_headroom if headroom is None else headroom
+        n = e = g = 0
+        for b in batches:
+            if isinstance(b, (list, tuple)):
+                n = max(n, sum(x.num_nodes for x in b))
+                e = max(e, sum(x.num_edges for x in b))
+                g = max(g, len(b))
+            else:
+                n, e, g = max(n, b.num_nodes), max(e, b.num_edges), max(g, b.num_graphs)
+        return int(n * (1 + h)) + 2, int(e * (1 + h)) + 1, g + 1
+
     def make_padder(self, max_atoms: int, max_edges: int, max_graphs: int) -> PaddedCollate:
         self._padder = PaddedCollate(max_atoms, max_edges, max_graphs, self.cfg.model.cutoff,
                                      pin_memory=self.device.type == "cuda")
