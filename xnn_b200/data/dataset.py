@@ -40,6 +40,8 @@ def structure_to_graph(s: Dict, cutoff: float, device=None, max_neighbors: Optio
     if cell is not None:
         cell = t(cell, pos.dtype).reshape(3, 3)
         pbc = torch.ones(3, dtype=torch.bool) if pbc is None else torch.as_tensor(pbc, dtype=torch.bool)
+    else:
+        pbc = None
     edge_index, shifts = build_neighbor_list(pos, cutoff, cell, pbc, engine=engine)
     if max_neighbors is not None:
         from .neighborlist import nearest_edges
