@@ -14,6 +14,29 @@ def free_port() -> int:
     return port
 
 
+def _to_plain(x):
+    """Tensors to numpy (pickled by value: no shared-memory handles that die with the child)."""
+    import torch
+    if isinstance(x, torch.Tensor):
+        return ("__tensor__", x.detach().cpu().numpy())
+    if isinstance(x, dict):
+        return {k: _to_plain(v) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return type(x)(_to_plain(v) for v in x)
+    return x
+
+
+def _from_plain(x):
+    import torch
+    if isinstance(x, tuple) and len(x) == 2 and x[0] == "__tensor__":
+        return torch.from_numpy(x[1])
+    if isinstance(x, dict):
+        return {k: _from_plain(v) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return type(x)(_from_plain(v) for v in x)
+    return x
+
+
 def _entry(rank, world, port, fn, args, queue):
     import torch
     import torch.distributed as dist
@@ -24,7 +47,7 @@ def _entry(rank, world, port, fn, args, queue):
         dist.init_process_group("gloo", rank=rank, world_size=world,
                                 timeout=__import__("datetime").timedelta(seconds=120))
         out = fn(rank, world, *args)
-        queue.put((rank, "ok", out))
+        queue.put((rank, "ok", _to_plain(out)))
     except Exception:  # pragma: no cover - reported by the parent
         queue.put((rank, "error", traceback.format_exc()))
     finally:
@@ -46,7 +69,7 @@ def run_ranks(fn, world: int, *args, timeout: float = 600.0):
             rank, status, out = queue.get(timeout=timeout)
             if status != "ok":
                 raise RuntimeError(f"rank {rank} failed:\n{out}")
-            results[rank] = out
+            results[rank] = _from_plain(out)
     finally:
         for p in procs:
             p.join(timeout=30)
