@@ -11,6 +11,8 @@
 //   3. waits until every rank's counter reached epoch * gridDim.x (every CTA of every peer of
 //      this exchange has stored its rows), with a bounded wait;
 //   4. unpacks: copies its own half (n_out rows, grouped by source) to the output array.
+// Without a row list (a plain all-to-all of contiguous segments) every thread of the grid copies
+// 16-byte units of each destination's segment.
 // Counters only grow, so they need no reset; the halves alternate so that a peer already in
 // the next exchange never overwrites rows still being unpacked (it could only reach the
 // exchange after that once this rank's next signal arrived, i.e. after this unpack).
@@ -46,6 +48,19 @@ __device__ __forceinline__ void copy_row(char* dst, const char* src, int64_t nby
   for (int k = lane; k < n; k += 32) d[k] = __ldcg(s + k);
 }
 
+// a contiguous byte range copied by every thread of the grid (16-byte units when aligned)
+__device__ __forceinline__ void copy_span(char* dst, const char* src, int64_t nbytes, int64_t tid, int64_t nthreads) {
+  if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | (uintptr_t)nbytes) & 15) == 0) {
+    const int4* s = reinterpret_cast<const int4*>(src);
+    int4* d = reinterpret_cast<int4*>(dst);
+    for (int64_t k = tid; k < nbytes / 16; k += nthreads) d[k] = __ldcg(s + k);
+  } else {
+    const int* s = reinterpret_cast<const int*>(src);
+    int* d = reinterpret_cast<int*>(dst);
+    for (int64_t k = tid; k < nbytes / 4; k += nthreads) d[k] = __ldcg(s + k);
+  }
+}
+
 __global__ void __launch_bounds__(256) halo_exchange_kernel(HaloArgs a) {
   const int rank = a.emulate ? (int)blockIdx.y : a.rank;
   const HaloRankArgs& R = a.r[a.emulate ? blockIdx.y : 0];
@@ -57,16 +72,25 @@ __global__ void __launch_bounds__(256) halo_exchange_kernel(HaloArgs a) {
   const bool vec16 = (a.row_bytes & 15) == 0;
   __shared__ int abort_flag;
 
-  // 1. pack and store into the destinations' buffers
-  for (int64_t i = (int64_t)b * warps + warp; i < R.n_send; i += (int64_t)gridDim.x * warps) {
-    int d = 0;
-    while (d < a.world - 1 && i >= R.seg_end[d]) ++d;
-    const int64_t begin = d == 0 ? 0 : R.seg_end[d - 1];
-    char* dst = R.buf[d][half] + (R.remote_off[d] + (i - begin)) * a.row_bytes;
-    const int64_t row = R.rows != nullptr ? R.rows[i] : i;
-    const char* src = R.src + row * a.row_bytes;
-    if (vec16) copy_row<int4>(dst, src, a.row_bytes, lane);
-    else copy_row<int>(dst, src, a.row_bytes, lane);
+  const int64_t gtid = (int64_t)b * blockDim.x + threadIdx.x, gthreads = (int64_t)gridDim.x * blockDim.x;
+  // 1. pack and store into the destinations' buffers: gathered rows one warp per row, or, without
+  //    a row list, each destination's contiguous segment by all threads
+  if (R.rows != nullptr) {
+    for (int64_t i = (int64_t)b * warps + warp; i < R.n_send; i += (int64_t)gridDim.x * warps) {
+      int d = 0;
+      while (d < a.world - 1 && i >= R.seg_end[d]) ++d;
+      const int64_t begin = d == 0 ? 0 : R.seg_end[d - 1];
+      char* dst = R.buf[d][half] + (R.remote_off[d] + (i - begin)) * a.row_bytes;
+      const char* src = R.src + R.rows[i] * a.row_bytes;
+      if (vec16) copy_row<int4>(dst, src, a.row_bytes, lane);
+      else copy_row<int>(dst, src, a.row_bytes, lane);
+    }
+  } else {
+    for (int d = 0; d < a.world; ++d) {
+      const int64_t begin = d == 0 ? 0 : R.seg_end[d - 1];
+      copy_span(R.buf[d][half] + R.remote_off[d] * a.row_bytes, R.src + begin * a.row_bytes,
+                (R.seg_end[d] - begin) * a.row_bytes, gtid, gthreads);
+    }
   }
   __syncthreads();
 
@@ -93,12 +117,8 @@ __global__ void __launch_bounds__(256) halo_exchange_kernel(HaloArgs a) {
   __syncthreads();
   if (abort_flag) return;
 
-  // 4. unpack this rank's half
-  const char* in = R.buf[rank][half];
-  for (int64_t i = (int64_t)b * warps + warp; i < R.n_out; i += (int64_t)gridDim.x * warps) {
-    if (vec16) copy_row<int4>(R.out + i * a.row_bytes, in + i * a.row_bytes, a.row_bytes, lane);
-    else copy_row<int>(R.out + i * a.row_bytes, in + i * a.row_bytes, a.row_bytes, lane);
-  }
+  // 4. unpack this rank's half (one contiguous range)
+  copy_span(R.out, R.buf[rank][half], R.n_out * a.row_bytes, gtid, gthreads);
 }
 
 }  // namespace

@@ -1,0 +1,409 @@
+"""Polarizable multipole electrostatics with smooth particle-mesh Ewald (AMOEBA-style).
+
+Sites carry charges ``q``, dipoles ``d`` (e A) and traceless quadrupoles ``Q`` (e A^2) in the
+global frame, and isotropic polarizabilities ``alpha_pol`` (A^3). The electrostatic energy of a
+periodic set of multipoles (eV) is the Ewald sum
+
+    E = E_real + E_recip + E_self (+ the neutralising-background term of a net charge),
+
+where the interaction of two sites is the operator ``L_i L_j g(|r_j - r_i|)`` with
+``L = q + d . grad + (1/3) Q : grad grad`` acting on each site's own position, ``g`` the
+erfc-screened Coulomb kernel in real space (cutoff ``rc``) and the Gaussian-smoothed rest in
+reciprocal space. Pairs of one molecule (``molecule`` ids) are excluded from every interaction;
+their reciprocal-space share is removed with the ``erf`` kernel.
+
+Reciprocal space is smooth PME (Essmann et al., J. Chem. Phys. 103, 8577 (1995)): the operator
+``L`` is applied to the order-``p`` cardinal B-spline weights of each site (first and second
+spline derivatives, mapped to Cartesian axes by the reciprocal cell), spread on a ``K1 x K2 x
+K3`` mesh, transformed by a real FFT and weighted by ``exp(-pi^2 m^2 / a^2) / (pi V m^2) B(m)``
+with the Euler exponential-spline moduli ``B``. Forces and fields follow by differentiation.
+
+Induced dipoles minimise ``U(mu) = E(q, d + mu, Q) + sum |mu_i|^2 / (2 alpha_i)``; the stationary
+point solves ``(alpha^-1 - T) mu = F_perm`` by preconditioned conjugate gradients (Jacobi),
+``T mu`` being the field of the dipoles ``mu`` (one spread, FFT and back-interpolation per
+iteration). At convergence the forces are ``-dU/dr`` at fixed ``mu`` (stationarity).
+
+Real-space pair terms follow the B_n formalism (B_0 = g, B_n = -(1/r) dB_{n-1}/dr) with the
+five contraction terms of the Tinker multipole code family; the Ewald self terms of charges,
+dipoles and quadrupoles are included. Everything is differentiable tensor code (CUDA or CPU);
+the mesh can be split over processes as z-slabs (:mod:`xnn_b200.ffnn.slab_fft`).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+from torch import Tensor, nn
+
+#: Coulomb constant (eV A / e^2) and one Debye in e A
+KE = 14.399645478425668
+DEBYE = 0.20819433622621843
+#: two sites of one molecule closer than this (A) interact only through the molecule's exclusion
+MOLECULE_REACH = 3.0
+
+
+# ----------------------------------------------------------------------------- B-splines
+def _spline_padded(t: Tensor, n: int, p: int) -> Tensor:
+    """``M_n(t + j)`` for ``j = 0..p-1`` (zero for ``j >= n``), ``(..., p)``."""
+    w = [t, 1.0 - t]
+    for m in range(3, n + 1):
+        new = []
+        for j in range(m):
+            v = torch.zeros_like(t)
+            if j < m - 1:
+                v = v + (t + j) / (m - 1) * w[j]
+            if j >= 1:
+                v = v + (m - t - j) / (m - 1) * w[j - 1]
+            new.append(v)
+        w = new
+    w = w + [torch.zeros_like(t)] * (p - len(w))
+    return torch.stack(w[:p], -1)
+
+
+def bspline_derivs(t: Tensor, p: int) -> Tuple[Tensor, Tensor, Tensor]:
+    """``M_p``, ``M_p'`` and ``M_p''`` at ``t + j`` (``j = 0..p-1``), each ``(..., p)``; the site
+    spreads onto grid points ``floor(u) - j``."""
+    m0 = _spline_padded(t, p, p)
+    a1 = _spline_padded(t, p - 1, p)
+    a2 = _spline_padded(t, p - 2, p)
+    sh = lambda a, k: torch.cat([torch.zeros_like(a[..., :k]), a[..., :p - k]], -1)  # noqa: E731
+    m1 = a1 - sh(a1, 1)
+    m2 = a2 - 2.0 * sh(a2, 1) + sh(a2, 2)
+    return m0, m1, m2
+
+
+def bspline_moduli(K: int, p: int, dtype, device) -> Tensor:
+    """``|b(m)|^2`` of the Euler exponential spline for the ``K`` FFT frequencies."""
+    mk = _spline_padded(torch.zeros((), dtype=torch.float64), p, p)        # M_p(j), j = 0..p-1
+    coef = mk[1:p]                                                          # M_p(1..p-1)
+    m = torch.arange(K, dtype=torch.float64)
+    k = torch.arange(0, p - 1, dtype=torch.float64)
+    ang = 2.0 * math.pi * m[:, None] * k[None, :] / K
+    re = (coef[None, :] * torch.cos(ang)).sum(1)
+    im = (coef[None, :] * torch.sin(ang)).sum(1)
+    den = re * re + im * im
+    bad = den < 1e-10
+    if bool(bad.any()):
+        idx = torch.nonzero(bad).flatten()
+        for i in idx.tolist():
+            den[i] = 0.5 * (den[(i - 1) % K] + den[(i + 1) % K])
+    return (1.0 / den).to(dtype=dtype, device=device)
+
+
+def _freq(K: int, device) -> Tensor:
+    return torch.fft.fftfreq(K, d=1.0 / K, device=device)
+
+
+# ----------------------------------------------------------------------------- reciprocal
+def spline_stencil(pos: Tensor, cell: Tensor, mesh: List[int], p: int):
+    """Per site: base grid index ``floor(u)`` ``(n, 3)`` and per-axis spline values / first /
+    second derivatives ``(n, 3, p)``, plus ``G (3, 3)`` with ``du_a / dr_b = G[b, a]``."""
+    inv = torch.linalg.inv(cell)
+    K = torch.tensor(mesh, dtype=pos.dtype, device=pos.device)
+    u = (pos @ inv) * K
+    base = torch.floor(u.detach())
+    t = u - base
+    m0, m1, m2 = bspline_derivs(t, p)
+    G = inv * K[None, :]
+    return base.long(), m0, m1, m2, G
+
+
+def spread(pos: Tensor, cell: Tensor, q: Optional[Tensor], d: Optional[Tensor], Q: Optional[Tensor],
+           mesh: List[int], p: int, z_range: Optional[Tuple[int, int]] = None) -> Tensor:
+    """Mesh of ``sum_i L_i W_i`` (``(K1, K2, K3)``; with ``z_range`` only planes ``[z0, z1)``
+    of the third axis, ``(K1, K2, z1 - z0)``)."""
+    n = pos.shape[0]
+    K1, K2, K3 = mesh
+    base, m0, m1, m2, G = spline_stencil(pos, cell, mesh, p)
+    # multipoles in scaled-fractional coordinates: d_u = G^T d, Q_u = G^T Q G
+    coef0 = q if q is not None else pos.new_zeros(n)
+    du = d @ G if d is not None else None
+    Qu = G.t() @ Q @ G if Q is not None else None
+    j = torch.arange(p, device=pos.device)
+    ix = (base[:, 0, None] - j[None, :]) % K1
+    iy = (base[:, 1, None] - j[None, :]) % K2
+    iz = (base[:, 2, None] - j[None, :]) % K3
+    a0, b0, c0 = m0[:, 0], m0[:, 1], m0[:, 2]
+    a1, b1, c1 = m1[:, 0], m1[:, 1], m1[:, 2]
+    val = coef0[:, None, None, None] * a0[:, :, None, None] * b0[:, None, :, None] * c0[:, None, None, :]
+    if du is not None:
+        val = val + du[:, 0, None, None, None] * a1[:, :, None, None] * b0[:, None, :, None] * c0[:, None, None, :]
+        val = val + du[:, 1, None, None, None] * a0[:, :, None, None] * b1[:, None, :, None] * c0[:, None, None, :]
+        val = val + du[:, 2, None, None, None] * a0[:, :, None, None] * b0[:, None, :, None] * c1[:, None, None, :]
+    if Qu is not None:
+        a2, b2, c2 = m2[:, 0], m2[:, 1], m2[:, 2]
+        fa = [a0, a1, a2]
+        fb = [b0, b1, b2]
+        fc = [c0, c1, c2]
+        for x in range(3):
+            for y in range(3):
+                order = [0, 0, 0]
+                order[x] += 1
+                order[y] += 1
+                w = Qu[:, x, y] / 3.0
+                val = val + w[:, None, None, None] * fa[order[0]][:, :, None, None] * \
+                    fb[order[1]][:, None, :, None] * fc[order[2]][:, None, None, :]
+    flat_xy = (ix[:, :, None] * K2 + iy[:, None, :])                       # (n, p, p)
+    if z_range is None:
+        idx = flat_xy[:, :, :, None] * K3 + iz[:, None, None, :]
+        grid = pos.new_zeros(K1 * K2 * K3).index_add_(0, idx.reshape(-1), val.reshape(-1))
+        return grid.view(K1, K2, K3)
+    z0, z1 = z_range
+    nz = z1 - z0
+    keep = (iz >= z0) & (iz < z1)
+    idx = flat_xy[:, :, :, None] * nz + (iz - z0).clamp(0, max(nz - 1, 0))[:, None, None, :]
+    val = val * keep[:, None, None, :].to(val.dtype)
+    grid = pos.new_zeros(K1 * K2 * nz).index_add_(0, idx.reshape(-1), val.reshape(-1))
+    return grid.view(K1, K2, nz)
+
+
+def influence(cell: Tensor, mesh: List[int], alpha: float, p: int, dtype, device) -> Tensor:
+    """``exp(-pi^2 m^2 / alpha^2) / (pi V m^2) B(m)`` on the rfft half-spectrum ``(K1, K2, K3//2+1)``,
+    zero at ``m = 0`` and doubled where the half spectrum stands for two conjugate terms."""
+    K1, K2, K3 = mesh
+    rec = torch.linalg.inv(cell).t().to(torch.float64)                      # rows: reciprocal vectors
+    f1, f2 = _freq(K1, device).double(), _freq(K2, device).double()
+    f3 = torch.arange(K3 // 2 + 1, device=device, dtype=torch.float64)
+    m = (f1[:, None, None, None] * rec[0] + f2[None, :, None, None] * rec[1] + f3[None, None, :, None] * rec[2])
+    m2 = (m * m).sum(-1)
+    vol = torch.det(cell.to(torch.float64)).abs()
+    B = (bspline_moduli(K1, p, torch.float64, device)[:, None, None] * bspline_moduli(K2, p, torch.float64, device)[
+        None, :, None] * bspline_moduli(K3, p, torch.float64, device)[None, None, :K3 // 2 + 1])
+    with torch.no_grad():
+        safe = torch.where(m2 > 0, m2, torch.ones_like(m2))
+    val = torch.exp(-math.pi ** 2 * m2 / alpha ** 2) / (math.pi * vol * safe) * B
+    val = torch.where(m2 > 0, val, torch.zeros_like(val))
+    w = torch.full((K3 // 2 + 1,), 2.0, dtype=torch.float64, device=device)
+    w[0] = 1.0
+    if K3 % 2 == 0:
+        w[-1] = 1.0
+    return (val * w[None, None, :]).to(dtype)
+
+
+def recip_energy(grid: Tensor, infl: Tensor) -> Tensor:
+    """``(1/2) sum_m infl(m) |F(Q)(m)|^2`` (Coulomb units) of a full mesh."""
+    F = torch.fft.rfftn(grid)
+    return 0.5 * (infl * (F.real * F.real + F.imag * F.imag)).sum()
+
+
+# ----------------------------------------------------------------------------- real space
+def _bn(r: Tensor, alpha: float, kind: str, nmax: int = 4) -> List[Tensor]:
+    """``B_0..B_nmax`` of ``erfc(a r)/r`` (``kind="erfc"``) or ``-erf(a r)/r`` (``"neg_erf"``)."""
+    r2 = r * r
+    if kind == "erfc":
+        b = [torch.erfc(alpha * r) / r]
+        ex = torch.exp(-alpha * alpha * r2)
+        f = 1.0 / (alpha * math.sqrt(math.pi))
+        for n in range(1, nmax + 1):
+            f = f * 2.0 * alpha * alpha
+            b.append(((2 * n - 1) * b[-1] + f * ex) / r2)
+        return b
+    c = _bn(r, alpha, "erfc", nmax)
+    inv = [1.0 / r]
+    for n in range(1, nmax + 1):
+        inv.append((2 * n - 1) * inv[-1] / r2)
+    return [ci - vi for ci, vi in zip(c, inv)]          # erfc/r - 1/r = -erf/r
+
+
+def pair_energy(v: Tensor, qi, di, Qi, qj, dj, Qj, B: List[Tensor]) -> Tensor:
+    """``L_i L_j g`` per pair with ``v = r_j - r_i`` and ``B_n`` of ``g`` (Tinker-scaled Q' = Q/3)."""
+    Qi3, Qj3 = Qi / 3.0, Qj / 3.0
+    dri, drk = (di * v).sum(-1), (dj * v).sum(-1)
+    qir = (Qi3 @ v[..., None]).squeeze(-1)
+    qkr = (Qj3 @ v[..., None]).squeeze(-1)
+    qrri, qrrk = (qir * v).sum(-1), (qkr * v).sum(-1)
+    qrrik = (qir * qkr).sum(-1)
+    qik = (Qi3 * Qj3).sum((-1, -2))
+    dik = (di * dj).sum(-1)
+    diqkr = (di * qkr).sum(-1)
+    dkqir = (dj * qir).sum(-1)
+    t1 = qi * qj
+    t2 = qj * dri - qi * drk + dik
+    t3 = qi * qrrk + qj * qrri - dri * drk + 2.0 * (dkqir - diqkr + qik)
+    t4 = dri * qrrk - drk * qrri - 4.0 * qrrik
+    t5 = qrri * qrrk
+    return t1 * B[0] + t2 * B[1] + t3 * B[2] + t4 * B[3] + t5 * B[4]
+
+
+def real_energy(pos: Tensor, cell: Tensor, i: Tensor, j: Tensor, shift: Tensor, excluded: Tensor,
+                q: Tensor, d: Tensor, Q: Tensor, alpha: float, chunk: int = 1 << 21) -> Tensor:
+    """Sum over unique pairs ``(i, j, shift)`` (``v = pos[j] - pos[i] + shift @ cell``); excluded
+    pairs contribute ``-erf`` (their reciprocal share removed)."""
+    e = pos.new_zeros(())
+    for s in range(0, i.shape[0], chunk):
+        a, b = i[s:s + chunk], j[s:s + chunk]
+        v = pos[b] - pos[a] + shift[s:s + chunk].to(pos.dtype) @ cell
+        r = torch.linalg.norm(v, dim=-1)
+        ex = excluded[s:s + chunk]
+        Bc = _bn(r, alpha, "erfc")
+        Be = _bn(r, alpha, "neg_erf")
+        B = [torch.where(ex, y, x) for x, y in zip(Bc, Be)]
+        e = e + pair_energy(v, q[a], d[a], Q[a], q[b], d[b], Q[b], B).sum()
+    return e
+
+
+def self_energy(q: Tensor, d: Tensor, Q: Tensor, alpha: float) -> Tensor:
+    a2 = 2.0 * alpha * alpha
+    Q3 = Q / 3.0
+    return -(alpha / math.sqrt(math.pi)) * ((q * q).sum() + a2 * ((d * d).sum() / 3.0 + 2.0 * a2 * (Q3 * Q3).sum() / 5.0))
+
+
+def background_energy(q: Tensor, cell: Tensor, alpha: float) -> Tensor:
+    vol = torch.det(cell).abs()
+    return -math.pi * q.sum() ** 2 / (2.0 * vol * alpha * alpha)
+
+
+# ----------------------------------------------------------------------------- pair list
+def multipole_pairs(pos: Tensor, cell: Tensor, cutoff: float, molecule: Optional[Tensor]):
+    """Unique pairs within ``cutoff`` (``i < j`` or ``i == j`` in a nonzero image counted once),
+    their shifts, and which pairs belong to one molecule (excluded)."""
+    from ..data.neighborlist import build_neighbor_list
+    ei, sh = build_neighbor_list(pos.detach().double(), cutoff, cell.detach().double(),
+                                 torch.ones(3, dtype=torch.bool))
+    src, dst = ei[0], ei[1]
+    # edge vector pos[dst] - pos[src] + sh @ cell; keep each unordered pair once
+    key = (src < dst) | ((src == dst) & ((sh[:, 0] > 0) | ((sh[:, 0] == 0) & ((sh[:, 1] > 0) | (
+        (sh[:, 1] == 0) & (sh[:, 2] > 0))))))
+    i, j, s = src[key], dst[key], sh[key]
+    if molecule is None:
+        excluded = torch.zeros_like(i, dtype=torch.bool)
+    else:
+        # the pairs of one molecule (its minimal image: molecules are far smaller than the box)
+        p64, c64 = pos.detach().double(), cell.detach().double()
+        r = torch.linalg.norm(p64[j.to(pos.device)] - p64[i.to(pos.device)] + s.to(pos.device).double() @ c64, dim=-1)
+        m = molecule.to(pos.device)
+        excluded = (m[i.to(pos.device)] == m[j.to(pos.device)]) & (r < MOLECULE_REACH)
+    return i.to(pos.device), j.to(pos.device), s.to(pos.device), excluded.to(pos.device)
+
+
+# ----------------------------------------------------------------------------- module
+@dataclass
+class EwaldSetup:
+    alpha: float = 0.4
+    cutoff: float = 7.0
+    mesh: Tuple[int, int, int] = (128, 128, 128)
+    order: int = 5
+    fft_dtype: torch.dtype = torch.float32
+
+
+class PolarizableMultipoles(nn.Module):
+    """Energy, forces and induced dipoles of a periodic polarizable multipole system."""
+
+    def __init__(self, setup: EwaldSetup = EwaldSetup(), tol_debye: float = 1e-5, max_iter: int = 100,
+                 mesh_backend=None, group=None):
+        """``mesh_backend``: a :class:`~xnn_b200.ffnn.slab_fft.SlabFFT` to split the mesh over the
+        processes of ``group`` (the real-space pairs are split too, and fields, energies and
+        forces summed); ``None`` evaluates everything here."""
+        super().__init__()
+        self.setup = setup
+        self.tol = float(tol_debye) * DEBYE
+        self.max_iter = int(max_iter)
+        self.mesh_backend = mesh_backend
+        self.group = group
+        dist_on = mesh_backend is not None and torch.distributed.is_available() and torch.distributed.is_initialized()
+        self.world = torch.distributed.get_world_size(group) if dist_on else 1
+        self.rank = torch.distributed.get_rank(group) if dist_on else 0
+        self._infl = None
+
+    def _sum(self, t: Tensor) -> Tensor:
+        if self.world > 1:
+            t = t.contiguous()
+            torch.distributed.all_reduce(t, group=self.group)
+        return t
+
+    def pairs(self, pos, cell, molecule):
+        i, j, s, ex = multipole_pairs(pos, cell, self.setup.cutoff, molecule)
+        if self.world > 1:
+            sl = slice(self.rank, None, self.world)
+            i, j, s, ex = i[sl], j[sl], s[sl], ex[sl]
+        return i, j, s, ex
+
+    def _influence(self, cell: Tensor) -> Tensor:
+        s = self.setup
+        key = (tuple(cell.detach().reshape(-1).tolist()), cell.device)
+        if self._infl is None or self._infl[0] != key:
+            self._infl = (key, influence(cell.detach(), list(s.mesh), s.alpha, s.order, s.fft_dtype, cell.device))
+        return self._infl[1]
+
+    def recip(self, pos, cell, q, d, Q) -> Tensor:
+        s = self.setup
+        if self.mesh_backend is not None:
+            return self.mesh_backend.energy(pos, cell, q, d, Q, s)
+        grid = spread(pos, cell, q, d, Q, list(s.mesh), s.order).to(s.fft_dtype)
+        return recip_energy(grid, self._influence(cell)).to(pos.dtype)
+
+    def electrostatic(self, pos, cell, pairs, q, d, Q) -> Tensor:
+        """Ewald energy in eV (Coulomb constant applied)."""
+        s = self.setup
+        i, j, sh, ex = pairs
+        e = self.recip(pos, cell, q, d, Q) + real_energy(pos, cell, i, j, sh, ex, q, d, Q, s.alpha)
+        if self.rank == 0:
+            e = e + self_energy(q, d, Q, s.alpha) + background_energy(q, cell, s.alpha)
+        return KE * e           # this process's share when the work is split
+
+    def field(self, pos, cell, pairs, q, d, Q) -> Tensor:
+        """Electric field ``-dE/d(mu)`` at every site (eV / (e A) units), ``(n, 3)``."""
+        mu = torch.zeros_like(d, requires_grad=True)
+        with torch.enable_grad():
+            e = self.electrostatic(pos.detach(), cell.detach(), pairs, q.detach(), d.detach() + mu, Q.detach())
+            (g,) = torch.autograd.grad(e, mu)
+        return -self._sum(g)
+
+    def dipole_field(self, pos, cell, pairs, v) -> Tensor:
+        """``T v``: field at every site from dipoles ``v`` alone."""
+        n = v.shape[0]
+        z3 = v.new_zeros(n, 3, 3)
+        vv = v.detach().clone().requires_grad_(True)
+        with torch.enable_grad():
+            e = self.electrostatic(pos.detach(), cell.detach(), pairs, v.new_zeros(n), vv, z3)
+            (g,) = torch.autograd.grad(e, vv)
+        return -self._sum(g)
+
+    def induce(self, pos, cell, pairs, q, d, Q, pol, mu0: Optional[Tensor] = None):
+        """Induced dipoles by Jacobi-preconditioned CG on ``(alpha^-1 - T) mu = F_perm``."""
+        F = self.field(pos, cell, pairs, q, d, Q) / KE        # fields in e / A^2 (Coulomb units)
+        inv_a = 1.0 / pol[:, None]
+
+        def A(v):
+            return inv_a * v - self.dipole_field(pos, cell, pairs, v) / KE
+
+        mu = pol[:, None] * F if mu0 is None else mu0.detach().clone()
+        r = F - A(mu)
+        z = pol[:, None] * r
+        p_ = z.clone()
+        rz = (r * z).sum()
+        it = 0
+        for it in range(1, self.max_iter + 1):
+            Ap = A(p_)
+            step = rz / (p_ * Ap).sum()
+            mu = mu + step * p_
+            r = r - step * Ap
+            z = pol[:, None] * r
+            err = torch.sqrt(((pol[:, None] * r) ** 2).sum(-1).mean())
+            if float(err) < self.tol:
+                break
+            rz_new = (r * z).sum()
+            p_ = z + (rz_new / rz) * p_
+            rz = rz_new
+        return mu.detach(), it, float(err)
+
+    def forward(self, pos: Tensor, cell: Tensor, q: Tensor, d: Tensor, Q: Tensor, pol: Tensor,
+                molecule: Optional[Tensor] = None, compute_forces: bool = True,
+                mu0: Optional[Tensor] = None) -> Dict[str, Tensor]:
+        pairs = self.pairs(pos, cell, molecule)
+        mu, iters, err = self.induce(pos, cell, pairs, q, d, Q, pol, mu0)
+        p = pos.detach().requires_grad_(compute_forces)
+        with torch.enable_grad():
+            e_total = self.electrostatic(p, cell, pairs, q, d + mu, Q)
+            if self.rank == 0:
+                e_total = e_total + KE * 0.5 * ((mu * mu).sum(-1) / pol).sum()
+            out = {"energy": self._sum(e_total.detach().reshape(1))[0], "induced_dipoles": mu,
+                   "iterations": torch.tensor(iters), "residual_debye": torch.tensor(err / DEBYE)}
+            if compute_forces:
+                (g,) = torch.autograd.grad(e_total, p)
+                out["forces"] = -self._sum(g)
+        if self.mesh_backend is not None and hasattr(self.mesh_backend, "check"):
+            self.mesh_backend.check()
+        return out
