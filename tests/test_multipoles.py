@@ -101,7 +101,7 @@ def test_forces_match_finite_differences_and_induction_converges():
     assert float(out["residual_debye"]) < 1e-9
     # induced dipoles solve mu = alpha (F_perm + T mu)
     pairs = M.multipole_pairs(pos, cell, 5.2, mol)
-    F = mod.field(pos, cell, pairs, q, d + out["induced_dipoles"], Q) / M.KE
+    F = mod.field(pos, cell, pairs, q, d + out["induced_dipoles"], Q, pol=pol) / M.KE
     torch.testing.assert_close(out["induced_dipoles"], pol[:, None] * F, rtol=1e-7, atol=1e-9)
     eps = 1e-5
     for k in (0, 5, 11):

@@ -18,8 +18,11 @@ spline derivatives, mapped to Cartesian axes by the reciprocal cell), spread on 
 K3`` mesh, transformed by a real FFT and weighted by ``exp(-pi^2 m^2 / a^2) / (pi V m^2) B(m)``
 with the Euler exponential-spline moduli ``B``. Forces and fields follow by differentiation.
 
-Induced dipoles minimise ``U(mu) = E(q, d + mu, Q) + sum |mu_i|^2 / (2 alpha_i)``; the stationary
-point solves ``(alpha^-1 - T) mu = F_perm`` by preconditioned conjugate gradients (Jacobi),
+Induced dipoles minimise ``U(mu) = E(q, d + mu, Q) + sum |mu_i|^2 / (2 alpha_i)``, where every
+interaction involving ``mu`` uses Thole-damped real-space kernels (``a = 0.39``, ``u = r /
+(alpha_i alpha_j)^(1/6)``, as AMOEBA damps induction) and the permanent multipoles interact
+undamped; the stationary point solves ``(alpha^-1 - T) mu = F_perm`` by preconditioned
+conjugate gradients (Jacobi),
 ``T mu`` being the field of the dipoles ``mu`` (one spread, FFT and back-interpolation per
 iteration). At convergence the forces are ``-dU/dr`` at fixed ``mu`` (stationarity).
 
@@ -227,10 +230,25 @@ def pair_energy(v: Tensor, qi, di, Qi, qj, dj, Qj, B: List[Tensor]) -> Tensor:
     return t1 * B[0] + t2 * B[1] + t3 * B[2] + t4 * B[3] + t5 * B[4]
 
 
+def thole_damp(B: List[Tensor], r: Tensor, au3: Tensor) -> List[Tensor]:
+    """Thole-damped ``B_1..B_3`` (``au3 = a (r / (alpha_i alpha_j)^(1/6))^3``): the bare ``1/r^n``
+    parts scaled by ``lambda_3, lambda_5, lambda_7`` (AMOEBA's damping of induction)."""
+    ex = torch.exp(-au3)
+    l3 = 1.0 - ex
+    l5 = 1.0 - (1.0 + au3) * ex
+    l7 = 1.0 - (1.0 + au3 + 0.6 * au3 * au3) * ex
+    r2 = r * r
+    r3 = r2 * r
+    return [B[0], B[1] - (1.0 - l3) / r3, B[2] - 3.0 * (1.0 - l5) / (r3 * r2),
+            B[3] - 15.0 * (1.0 - l7) / (r3 * r2 * r2), B[4]]
+
+
 def real_energy(pos: Tensor, cell: Tensor, i: Tensor, j: Tensor, shift: Tensor, excluded: Tensor,
-                q: Tensor, d: Tensor, Q: Tensor, alpha: float, chunk: int = 1 << 21) -> Tensor:
+                q: Tensor, d: Tensor, Q: Tensor, alpha: float, chunk: int = 1 << 21,
+                pol: Optional[Tensor] = None, thole: Optional[float] = None) -> Tensor:
     """Sum over unique pairs ``(i, j, shift)`` (``v = pos[j] - pos[i] + shift @ cell``); excluded
-    pairs contribute ``-erf`` (their reciprocal share removed)."""
+    pairs contribute ``-erf`` (their reciprocal share removed); with ``thole`` the dipole,
+    dipole-dipole and dipole-quadrupole kernels are Thole-damped."""
     e = pos.new_zeros(())
     for s in range(0, i.shape[0], chunk):
         a, b = i[s:s + chunk], j[s:s + chunk]
@@ -238,6 +256,9 @@ def real_energy(pos: Tensor, cell: Tensor, i: Tensor, j: Tensor, shift: Tensor, 
         r = torch.linalg.norm(v, dim=-1)
         ex = excluded[s:s + chunk]
         Bc = _bn(r, alpha, "erfc")
+        if thole is not None:
+            u = r / (pol[a] * pol[b]) ** (1.0 / 6.0)
+            Bc = thole_damp(Bc, r, thole * u * u * u)
         Be = _bn(r, alpha, "neg_erf")
         B = [torch.where(ex, y, x) for x, y in zip(Bc, Be)]
         e = e + pair_energy(v, q[a], d[a], Q[a], q[b], d[b], Q[b], B).sum()
@@ -292,7 +313,7 @@ class PolarizableMultipoles(nn.Module):
     """Energy, forces and induced dipoles of a periodic polarizable multipole system."""
 
     def __init__(self, setup: EwaldSetup = EwaldSetup(), tol_debye: float = 1e-5, max_iter: int = 100,
-                 mesh_backend=None, group=None):
+                 mesh_backend=None, group=None, thole: Optional[float] = 0.39):
         """``mesh_backend``: a :class:`~xnn_b200.ffnn.slab_fft.SlabFFT` to split the mesh over the
         processes of ``group`` (the real-space pairs are split too, and fields, energies and
         forces summed); ``None`` evaluates everything here."""
@@ -302,6 +323,7 @@ class PolarizableMultipoles(nn.Module):
         self.max_iter = int(max_iter)
         self.mesh_backend = mesh_backend
         self.group = group
+        self.thole = None if thole is None else float(thole)
         dist_on = mesh_backend is not None and torch.distributed.is_available() and torch.distributed.is_initialized()
         self.world = torch.distributed.get_world_size(group) if dist_on else 1
         self.rank = torch.distributed.get_rank(group) if dist_on else 0
@@ -334,40 +356,58 @@ class PolarizableMultipoles(nn.Module):
         grid = spread(pos, cell, q, d, Q, list(s.mesh), s.order).to(s.fft_dtype)
         return recip_energy(grid, self._influence(cell)).to(pos.dtype)
 
-    def electrostatic(self, pos, cell, pairs, q, d, Q) -> Tensor:
-        """Ewald energy in eV (Coulomb constant applied)."""
+    def electrostatic(self, pos, cell, pairs, q, d, Q, pol: Optional[Tensor] = None) -> Tensor:
+        """Ewald energy in eV (Coulomb constant applied); with ``pol`` the real-space kernels are
+        Thole-damped (the induction energy surface)."""
         s = self.setup
         i, j, sh, ex = pairs
-        e = self.recip(pos, cell, q, d, Q) + real_energy(pos, cell, i, j, sh, ex, q, d, Q, s.alpha)
+        th = self.thole if pol is not None else None
+        e = self.recip(pos, cell, q, d, Q) + real_energy(pos, cell, i, j, sh, ex, q, d, Q, s.alpha, pol=pol, thole=th)
         if self.rank == 0:
             e = e + self_energy(q, d, Q, s.alpha) + background_energy(q, cell, s.alpha)
         return KE * e           # this process's share when the work is split
 
-    def field(self, pos, cell, pairs, q, d, Q) -> Tensor:
-        """Electric field ``-dE/d(mu)`` at every site (eV / (e A) units), ``(n, 3)``."""
+    def polarizable_energy(self, pos, cell, pairs, q, d, Q, pol, mu) -> Tensor:
+        """``U(mu)``: permanent multipoles interact undamped, everything involving the induced
+        dipoles through the Thole-damped kernels, plus ``sum |mu|^2 / (2 alpha)``."""
+        s = self.setup
+        i, j, sh, ex = pairs
+        u = self.electrostatic(pos, cell, pairs, q, d + mu, Q, pol=pol if self.thole is not None else None)
+        if self.thole is not None:
+            u = u + KE * (real_energy(pos, cell, i, j, sh, ex, q, d, Q, s.alpha)
+                          - real_energy(pos, cell, i, j, sh, ex, q, d, Q, s.alpha, pol=pol, thole=self.thole))
+        if self.rank == 0:
+            u = u + KE * 0.5 * ((mu * mu).sum(-1) / pol).sum()
+        return u
+
+    def field(self, pos, cell, pairs, q, d, Q, pol: Optional[Tensor] = None) -> Tensor:
+        """Electric field ``-dE/d(mu)`` at every site (eV / (e A) units), ``(n, 3)``; Thole-damped
+        when ``pol`` is given."""
         mu = torch.zeros_like(d, requires_grad=True)
         with torch.enable_grad():
-            e = self.electrostatic(pos.detach(), cell.detach(), pairs, q.detach(), d.detach() + mu, Q.detach())
+            e = self.electrostatic(pos.detach(), cell.detach(), pairs, q.detach(), d.detach() + mu, Q.detach(),
+                                   pol=pol)
             (g,) = torch.autograd.grad(e, mu)
         return -self._sum(g)
 
-    def dipole_field(self, pos, cell, pairs, v) -> Tensor:
+    def dipole_field(self, pos, cell, pairs, v, pol: Optional[Tensor] = None) -> Tensor:
         """``T v``: field at every site from dipoles ``v`` alone."""
         n = v.shape[0]
         z3 = v.new_zeros(n, 3, 3)
         vv = v.detach().clone().requires_grad_(True)
         with torch.enable_grad():
-            e = self.electrostatic(pos.detach(), cell.detach(), pairs, v.new_zeros(n), vv, z3)
+            e = self.electrostatic(pos.detach(), cell.detach(), pairs, v.new_zeros(n), vv, z3, pol=pol)
             (g,) = torch.autograd.grad(e, vv)
         return -self._sum(g)
 
     def induce(self, pos, cell, pairs, q, d, Q, pol, mu0: Optional[Tensor] = None):
         """Induced dipoles by Jacobi-preconditioned CG on ``(alpha^-1 - T) mu = F_perm``."""
-        F = self.field(pos, cell, pairs, q, d, Q) / KE        # fields in e / A^2 (Coulomb units)
+        damp = pol if self.thole is not None else None
+        F = self.field(pos, cell, pairs, q, d, Q, pol=damp) / KE        # fields in e / A^2 (Coulomb units)
         inv_a = 1.0 / pol[:, None]
 
         def A(v):
-            return inv_a * v - self.dipole_field(pos, cell, pairs, v) / KE
+            return inv_a * v - self.dipole_field(pos, cell, pairs, v, pol=damp) / KE
 
         mu = pol[:, None] * F if mu0 is None else mu0.detach().clone()
         r = F - A(mu)
@@ -396,9 +436,7 @@ class PolarizableMultipoles(nn.Module):
         mu, iters, err = self.induce(pos, cell, pairs, q, d, Q, pol, mu0)
         p = pos.detach().requires_grad_(compute_forces)
         with torch.enable_grad():
-            e_total = self.electrostatic(p, cell, pairs, q, d + mu, Q)
-            if self.rank == 0:
-                e_total = e_total + KE * 0.5 * ((mu * mu).sum(-1) / pol).sum()
+            e_total = self.polarizable_energy(p, cell, pairs, q, d, Q, pol, mu)
             out = {"energy": self._sum(e_total.detach().reshape(1))[0], "induced_dipoles": mu,
                    "iterations": torch.tensor(iters), "residual_debye": torch.tensor(err / DEBYE)}
             if compute_forces:
