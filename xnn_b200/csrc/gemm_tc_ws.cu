@@ -1,7 +1,7 @@
 // Row GEMM Y[M, N] = (X[M, K] @ W[K, N]) * col_scale on tcgen05, warp-specialized and fed by TMA
 // (3xTF32, FP32 accuracy; K <= 512, N <= 512 and a multiple of 16).
 //
-// One persistent CTA per SM, 8 warps with fixed roles:
+// One persistent CTA per SM, 12 warps with fixed roles:
 //   warp 0      producer: per pipeline step, one 2D TMA tile load of X (128 rows x KC, swizzled
 //               to the row width) and one 1D bulk copy of the packed W chunk, both completing on
 //               the stage's `full` mbarrier;
@@ -11,13 +11,16 @@
 //   warp 1      MMA issuer (one lane): hi*hi + hi*lo + lo*hi tcgen05.mma (kind::tf32, M = 128,
 //               N = NS <= 256) into one of two TMEM accumulators, commits to the stage's `empty`
 //               barrier and, after the unit's last chunk, to the accumulator's `full` barrier;
-//   warps 4-7   epilogue: tcgen05.ld of the accumulator (warp 4 + q owns TMEM lanes 32q..32q+31),
-//               column scale, swizzled staging in shared memory and 2D TMA stores of 32 x 16 tiles;
-//               arrive on the accumulator's `empty` barrier so the next unit can reuse it.
+//   warps 4-11  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes 32 (w % 4) ..; the
+//               two warps of a lane quarter split the columns), column scale, swizzled staging in
+//               shared memory and 2D TMA stores of 32 x 16 tiles; arrive on the accumulator's
+//               `empty` barrier so the next unit can reuse it.
 // A unit of work is (row tile, column half): N > 256 is split into two halves of NS = N / 2
-// columns so that two accumulators (double buffering) fit in the 512 TMEM columns. The stages of
-// the X/W ring and the two accumulators let loads, conversion, MMAs and stores of consecutive
-// units overlap.
+// columns so that two accumulators (double buffering) fit in the 512 TMEM columns. When the
+// packed W of one column half fits in shared memory next to the stages, each CTA keeps one half
+// resident (loaded once) and walks row tiles; otherwise W is streamed with each X chunk. The
+// stages of the ring and the two accumulators let loads, conversion, MMAs and stores of
+// consecutive units overlap.
 //
 // Every wait is bounded (`spin_limit` polls); a role that gives up records code 4 in `status` and
 // raises a shared abort flag that makes the other roles leave their loops; the MMA warp then waits
@@ -32,7 +35,7 @@
 namespace {
 
 constexpr int WS_STAGES = 2;
-constexpr int WS_THREADS = 256;
+constexpr int WS_THREADS = 384;
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -96,32 +99,53 @@ template <int KC>
 struct WsLayout {
   static constexpr uint32_t A_BYTES = 128 * KC * 4;
   static constexpr uint32_t SW_MASK = KC == 32 ? 7 : (KC == 16 ? 3 : 1);   // 128 / 64 / 32-byte swizzle
-  uint32_t w_bytes;        // one stage of W: hi + lo
-  uint32_t stage_bytes;    // raw + hi + lo + W, rounded to 1024
+  uint32_t w_bytes;        // one K chunk of W: hi + lo
+  uint32_t stage_bytes;    // raw + hi + lo (+ W when streamed), rounded to 1024
   uint32_t stage0;         // offset of stage 0
-  uint32_t staging;        // epilogue staging: 4 warps x 2 buffers x 2 KB
+  uint32_t wres;           // resident W (every K chunk of one column half)
+  uint32_t staging;        // epilogue staging: 8 warps x 2 buffers x 2 KB
   uint32_t bars;
   uint32_t total;
-  __host__ __device__ WsLayout(int NS) {
+  __host__ __device__ WsLayout(int NS, int n_chunks, int resident) {
     w_bytes = (uint32_t)NS * KC * 4 * 2;
-    stage_bytes = (3 * A_BYTES + w_bytes + 1023) / 1024 * 1024;
+    stage_bytes = (3 * A_BYTES + (resident ? 0u : w_bytes) + 1023) / 1024 * 1024;
     stage0 = 0;
-    staging = WS_STAGES * stage_bytes;
-    bars = staging + 4 * 2 * 2048;
+    wres = WS_STAGES * stage_bytes;
+    staging = wres + (resident ? (uint32_t)n_chunks * w_bytes : 0u);
+    staging = (staging + 1023) / 1024 * 1024;
+    bars = staging + 8 * 2 * 2048;
     total = bars + 256;
   }
 };
+
+// the k-th unit of this CTA: streamed W walks (tile, half) units round-robin; resident W keeps
+// one column half per CTA (gridDim.x a multiple of n_sub) and walks its tiles
+__device__ __forceinline__ bool unit_at(long long k, int resident, int n_sub, int tiles, int& tile, int& h) {
+  if (resident) {
+    h = (int)(blockIdx.x % n_sub);
+    const long long t = (long long)(blockIdx.x / n_sub) + k * (long long)(gridDim.x / n_sub);
+    if (t >= tiles) return false;
+    tile = (int)t;
+    return true;
+  }
+  const long long u = (long long)blockIdx.x + k * (long long)gridDim.x;
+  if (u >= (long long)tiles * n_sub) return false;
+  tile = (int)(u / n_sub);
+  h = (int)(u % n_sub);
+  return true;
+}
 
 template <int KC>
 __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
     const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapY, int M, int N, int K,
     int NS, const float* __restrict__ Bpack, const float* __restrict__ col_scale, int* status,
-    long long spin_limit, int tmem_cols, uint32_t acc_stride) {
+    long long spin_limit, int tmem_cols, uint32_t acc_stride, int resident) {
   using namespace tc;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // align the dynamic buffer to 1024 bytes (swizzle atoms)
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  const WsLayout<KC> L(NS);
+  const int n_chunks = (K + KC - 1) / KC;
+  const WsLayout<KC> L(NS, n_chunks, resident);
   constexpr uint32_t A_BYTES = WsLayout<KC>::A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* conv = full + WS_STAGES;
@@ -129,14 +153,13 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
   uint64_t* accf = empty + WS_STAGES;
   uint64_t* acce = accf + 2;
   uint64_t* fin = acce + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+  uint64_t* wfull = fin + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wfull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_chunks = (K + KC - 1) / KC;
   const int n_sub = N / NS;
   const int tiles = (M + 127) / 128;
-  const int units = tiles * n_sub;
 
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -151,9 +174,10 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf + b, 1);
-      mbar_init(acce + b, 128);
+      mbar_init(acce + b, 256);
     }
     mbar_init(fin, 1);
+    mbar_init(wfull, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -168,20 +192,30 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
     if (lane == 0) {
       long long it = 0;
       int last_s = -1;
-      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
-        const int tile = u / n_sub, h = u % n_sub;
+      int tile, h;
+      if (resident) {
+        // this CTA's column half of W, every K chunk, once
+        h = (int)(blockIdx.x % n_sub);
+        mbar_arrive_expect_tx(wfull, (uint32_t)n_chunks * W_BYTES);
+        for (int c = 0; c < n_chunks; ++c)
+          bulk_g2s(smem + L.wres + (uint32_t)c * W_BYTES, Bpack + ((int64_t)h * n_chunks + c) * 2 * NS * KC, W_BYTES,
+                   wfull);
+      }
+      for (long long k = 0; unit_at(k, resident, n_sub, tiles, tile, h) && !*abort_flag; ++k) {
         for (int c = 0; c < n_chunks; ++c, ++it) {
           const int s = (int)(it % WS_STAGES);
           if (it >= WS_STAGES &&
               !wait_or_abort(empty + s, (uint32_t)(((it / WS_STAGES) - 1) & 1), spin_limit, abort_flag, status))
             break;
           unsigned char* st = smem + L.stage0 + (uint32_t)s * L.stage_bytes;
-          mbar_arrive_expect_tx(full + s, A_BYTES + W_BYTES);
+          mbar_arrive_expect_tx(full + s, A_BYTES + (resident ? 0u : W_BYTES));
           tma_load_2d(st, &mapA, c * KC, tile * 128, full + s);
-          bulk_g2s(st + 3 * A_BYTES, Bpack + ((int64_t)h * n_chunks + c) * 2 * NS * KC, W_BYTES, full + s);
+          if (!resident)
+            bulk_g2s(st + 3 * A_BYTES, Bpack + ((int64_t)h * n_chunks + c) * 2 * NS * KC, W_BYTES, full + s);
           last_s = s;
         }
       }
+      if (resident && *abort_flag) mbar_wait(wfull, 0, spin_limit);
       // after an abort, let the last copies land before the CTA leaves
       if (*abort_flag && last_s >= 0) mbar_wait(full + last_s, (uint32_t)(((it - 1) / WS_STAGES) & 1), spin_limit);
     }
@@ -190,7 +224,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
     const int ct = tid - 64;           // 0..63
     long long it = 0;
     bool go = true;
-    for (int u = blockIdx.x; u < units && go; u += gridDim.x) {
+    int tile, h;
+    for (long long k = 0; go && unit_at(k, resident, n_sub, tiles, tile, h); ++k) {
       for (int c = 0; c < n_chunks; ++c, ++it) {
         const int s = (int)(it % WS_STAGES);
         if (!wait_or_abort(full + s, (uint32_t)((it / WS_STAGES) & 1), spin_limit, abort_flag, status)) {
@@ -224,8 +259,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
       const uint32_t idesc = make_idesc_tf32(NS, 0, 0);
       const uint32_t lbo = 128, sbo = (KC / 4) * 128;
       long long it = 0, uidx = 0;
-      bool go = true;
-      for (int u = blockIdx.x; u < units && go; u += gridDim.x, ++uidx) {
+      bool go = !resident || wait_or_abort(wfull, 0, spin_limit, abort_flag, status);
+      int tile, h;
+      for (; go && unit_at(uidx, resident, n_sub, tiles, tile, h); ++uidx) {
         const int b = (int)(uidx & 1);
         if (uidx >= 2 && !wait_or_abort(acce + b, (uint32_t)(((uidx >> 1) - 1) & 1), spin_limit, abort_flag, status))
           break;
@@ -240,7 +276,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
           tc_fence_after();
           const unsigned char* st = smem + L.stage0 + (uint32_t)s * L.stage_bytes;
           const uint32_t ah = smem_u32(st + A_BYTES), al = smem_u32(st + 2 * A_BYTES);
-          const uint32_t bh = smem_u32(st + 3 * A_BYTES), bl = bh + W_BYTES / 2;
+          const uint32_t bh = resident ? smem_u32(smem + L.wres + (uint32_t)c * W_BYTES) : smem_u32(st + 3 * A_BYTES);
+          const uint32_t bl = bh + W_BYTES / 2;
 #pragma unroll
           for (int k = 0; k < KC / 8; ++k) {
             const uint32_t off = (uint32_t)k * 256u;
@@ -258,18 +295,21 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
       mbar_wait(fin, 0, spin_limit);
     }
   } else {
-    // ---------------------------------------------------------------- epilogue (warps 4..7)
-    const int q = warp - 4;            // TMEM lane quarter
-    unsigned char* stage_buf = smem + L.staging + (uint32_t)q * 2 * 2048;
+    // ---------------------------------------------------------------- epilogue (warps 4..11)
+    const int q = warp & 3;            // TMEM lane quarter (tcgen05.ld reaches lanes 32 (warp % 4) ..)
+    const int part = (warp - 4) >> 2;  // which half of the unit's columns this warp drains
+    const int cw = (NS / 2) % 16 == 0 ? NS / 2 : (part == 0 ? NS : 0);
+    const int cbeg = (NS / 2) % 16 == 0 ? part * (NS / 2) : 0;
+    unsigned char* stage_buf = smem + L.staging + (uint32_t)(warp - 4) * 2 * 2048;
     long long uidx = 0;
     int nst = 0;                       // stores issued by this warp
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++uidx) {
+    int tile, h;
+    for (; unit_at(uidx, resident, n_sub, tiles, tile, h); ++uidx) {
       const int b = (int)(uidx & 1);
       if (!wait_or_abort(accf + b, (uint32_t)((uidx >> 1) & 1), spin_limit, abort_flag, status)) break;
       tc_fence_after();
-      const int tile = u / n_sub, h = u % n_sub;
       const uint32_t lane_base = tmem + (uint32_t)b * acc_stride + ((uint32_t)(q * 32) << 16);
-      for (int c0 = 0; c0 < NS; c0 += 16, ++nst) {
+      for (int c0 = cbeg; c0 < cbeg + cw; c0 += 16, ++nst) {
         float v[16];
         tmem_ld16(lane_base + (uint32_t)c0, v);
         if (col_scale) {
@@ -349,17 +389,23 @@ cudaError_t launch_ws(int M, int N, int K, const float* X, int ldx, const float*
   gemm_ws_pack_kernel<KC><<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(K, N, NS, W, sk, sn, Bpack);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  const WsLayout<KC> L(NS);
-  const size_t smem = L.total + 1024;       // + alignment slack
+  // W resident in shared memory (loaded once per CTA) when it fits, else streamed per K chunk
+  const int n_sub = N / NS;
+  const int tiles = (M + 127) / 128;
+  int resident = 1;
+  size_t smem = WsLayout<KC>(NS, n_chunks, 1).total + 1024;       // + alignment slack
+  if (smem > 227 * 1024 || sms < n_sub) {
+    resident = 0;
+    smem = WsLayout<KC>(NS, n_chunks, 0).total + 1024;
+  }
   if (smem > 227 * 1024) return cudaErrorNotSupported;
   e = cudaFuncSetAttribute(gemm_ws_kernel<KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const uint32_t acc_stride = NS <= 128 ? 128u : 256u;
   const int tmem_cols = (int)(2 * acc_stride);
-  const int units = ((M + 127) / 128) * (N / NS);
-  const int grid = std::min(units, sms);
+  const int grid = resident ? std::min(tiles, sms / n_sub) * n_sub : std::min(tiles * n_sub, sms);
   gemm_ws_kernel<KC><<<grid, WS_THREADS, smem, s>>>(mapA, mapY, M, N, K, NS, Bpack, col_scale, status, spin_limit,
-                                                    tmem_cols, acc_stride);
+                                                    tmem_cols, acc_stride, resident);
   return cudaGetLastError();
 }
 
