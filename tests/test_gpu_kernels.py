@@ -112,3 +112,16 @@ def test_neighbor_list_cuda_matches_cpu():
         ka = torch.unique(torch.cat([a[0].T, a[1]], 1), dim=0)
         kb = torch.unique(torch.cat([b[0].T.cpu(), b[1].cpu()], 1), dim=0)
         assert torch.equal(ka, kb)
+
+
+def test_schnet_cfconv_kernel_matches_torch_path():
+    from xnn_b200.models import ForceStressOutput
+    from xnn_b200.models.schnet import SchNet
+    torch.manual_seed(0)
+    m = SchNet(n_features=64, n_interactions=3, n_rbf=20, cutoff=5.0).cuda().double()
+    g = _graph(n=8, cutoff=5.0).to("cuda")
+    g.pos = g.pos.double()
+    o_fast = ForceStressOutput(m.set_use_fast(True))(g.clone())
+    o_ref = ForceStressOutput(m.set_use_fast(False))(g.clone())
+    torch.testing.assert_close(o_fast["energy"], o_ref["energy"], rtol=1e-10, atol=1e-10)
+    torch.testing.assert_close(o_fast["forces"], o_ref["forces"], rtol=1e-9, atol=1e-10)

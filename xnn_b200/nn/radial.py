@@ -12,16 +12,17 @@ class GaussianRBF(nn.Module):
     """``exp(-gamma (r - mu_k)^2)`` with ``n_rbf`` centres evenly spaced on ``[start, cutoff]``."""
 
     def __init__(self, n_rbf: int = 50, cutoff: float = 5.0, start: float = 0.0,
-                 gamma: Optional[float] = None, trainable: bool = False):
+                 gamma: Optional[float] = None, trainable: bool = False, endpoint: bool = True):
         super().__init__()
-        centers = torch.linspace(start, cutoff, n_rbf)
-        width = (cutoff - start) / max(n_rbf - 1, 1)
-        g = torch.tensor(gamma if gamma is not None else 0.5 / width ** 2)
+        centers = torch.linspace(start, cutoff, n_rbf) if endpoint else torch.linspace(start, cutoff, n_rbf + 1)[:n_rbf]
+        width = float(centers[1] - centers[0]) if n_rbf > 1 else 1.0
+        g = float(gamma) if gamma is not None else 0.5 / width ** 2
         if trainable:
-            self.centers, self.gamma = nn.Parameter(centers), nn.Parameter(g)
+            self.centers, self.gamma = nn.Parameter(centers), nn.Parameter(torch.tensor(g))
         else:
+            # a plain float (the state dict holds only the centres, as the reference's)
             self.register_buffer("centers", centers)
-            self.register_buffer("gamma", g)
+            self.gamma = g
 
     def forward(self, r: Tensor) -> Tensor:
         return torch.exp(-self.gamma * (r[..., None] - self.centers) ** 2)
