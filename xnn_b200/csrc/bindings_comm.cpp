@@ -89,11 +89,13 @@ void p2p_allreduce_op(std::vector<int64_t> bufs, std::vector<int64_t> flags, tor
 void register_gemm(pybind11::module& m);
 void register_radial(pybind11::module& m);
 void register_halo(pybind11::module& m);
+void register_ffnn(pybind11::module& m);
 
 void register_comm(pybind11::module& m) {
   register_gemm(m);
   register_radial(m);
   register_halo(m);
+  register_ffnn(m);
   m.def("ipc_alloc", &ipc_alloc);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);

@@ -122,8 +122,9 @@ def spread(pos: Tensor, cell: Tensor, q: Optional[Tensor], d: Optional[Tensor], 
     base, m0, m1, m2, G = spline_stencil(pos, cell, mesh, p)
     # multipoles in scaled-fractional coordinates: d_u = G^T d, Q_u = G^T Q G
     coef0 = q if q is not None else pos.new_zeros(n)
-    du = d @ G if d is not None else None
-    Qu = G.t() @ Q @ G if Q is not None else None
+    du = (d[:, :, None] * G[None]).sum(1) if d is not None else None
+    Qu = ((G[None, :, :, None, None] * Q[:, :, None, :, None] * G[None, None, None, :, :]).sum((1, 3))
+          if Q is not None else None)                                       # G^T Q G per site
     j = torch.arange(p, device=pos.device)
     ix = (base[:, 0, None] - j[None, :]) % K1
     iy = (base[:, 1, None] - j[None, :]) % K2
@@ -214,8 +215,9 @@ def pair_energy(v: Tensor, qi, di, Qi, qj, dj, Qj, B: List[Tensor]) -> Tensor:
     """``L_i L_j g`` per pair with ``v = r_j - r_i`` and ``B_n`` of ``g`` (Tinker-scaled Q' = Q/3)."""
     Qi3, Qj3 = Qi / 3.0, Qj / 3.0
     dri, drk = (di * v).sum(-1), (dj * v).sum(-1)
-    qir = (Qi3 @ v[..., None]).squeeze(-1)
-    qkr = (Qj3 @ v[..., None]).squeeze(-1)
+    # 3x3 products written out elementwise (batched tiny matmuls are slow library calls)
+    qir = (Qi3 * v[..., None, :]).sum(-1)
+    qkr = (Qj3 * v[..., None, :]).sum(-1)
     qrri, qrrk = (qir * v).sum(-1), (qkr * v).sum(-1)
     qrrik = (qir * qkr).sum(-1)
     qik = (Qi3 * Qj3).sum((-1, -2))
@@ -228,6 +230,17 @@ def pair_energy(v: Tensor, qi, di, Qi, qj, dj, Qj, B: List[Tensor]) -> Tensor:
     t4 = dri * qrrk - drk * qrri - 4.0 * qrrik
     t5 = qrri * qrrk
     return t1 * B[0] + t2 * B[1] + t3 * B[2] + t4 * B[3] + t5 * B[4]
+
+
+def _kernel_ok() -> bool:
+    from .. import _ext
+    return _ext.cuda_available() and hasattr(_ext.ops(), "mp_real")
+
+
+def _shift_vec(shift: Tensor, cell: Tensor) -> Tensor:
+    """``shift @ cell`` for integer shifts (three scaled rows, no library matmul)."""
+    sf = shift.to(cell.dtype)
+    return sf[:, 0:1] * cell[0] + sf[:, 1:2] * cell[1] + sf[:, 2:3] * cell[2]
 
 
 def thole_damp(B: List[Tensor], r: Tensor, au3: Tensor) -> List[Tensor]:
@@ -243,16 +256,43 @@ def thole_damp(B: List[Tensor], r: Tensor, au3: Tensor) -> List[Tensor]:
             B[3] - 15.0 * (1.0 - l7) / (r3 * r2 * r2), B[4]]
 
 
+class _RealKernel(torch.autograd.Function):
+    """Real-space pair sum on the CUDA kernel (``csrc/multipole_real.cu``); first derivatives
+    with respect to positions and dipoles (forces and fields)."""
+
+    @staticmethod
+    def forward(ctx, pos, d, cell, q, Q, pol, i, j, shift, excluded, alpha, thole):
+        from .. import _ext
+        e, gp, gd = _ext.ops().mp_real(pos.contiguous(), cell.contiguous(), q.contiguous(), d.contiguous(),
+                                       Q.contiguous(), pol.contiguous(), i.contiguous(), j.contiguous(),
+                                       shift.contiguous(), excluded.contiguous(), float(alpha),
+                                       float(thole) if thole is not None else -1.0,
+                                       ctx.needs_input_grad[0], ctx.needs_input_grad[1])
+        ctx.save_for_backward(gp if ctx.needs_input_grad[0] else None, gd if ctx.needs_input_grad[1] else None)
+        return e[0]
+
+    @staticmethod
+    def backward(ctx, g):
+        gp, gd = ctx.saved_tensors
+        return (None if gp is None else g * gp, None if gd is None else g * gd) + (None,) * 10
+
+
 def real_energy(pos: Tensor, cell: Tensor, i: Tensor, j: Tensor, shift: Tensor, excluded: Tensor,
                 q: Tensor, d: Tensor, Q: Tensor, alpha: float, chunk: int = 1 << 21,
                 pol: Optional[Tensor] = None, thole: Optional[float] = None) -> Tensor:
     """Sum over unique pairs ``(i, j, shift)`` (``v = pos[j] - pos[i] + shift @ cell``); excluded
     pairs contribute ``-erf`` (their reciprocal share removed); with ``thole`` the dipole,
-    dipole-dipole and dipole-quadrupole kernels are Thole-damped."""
+    dipole-dipole and dipole-quadrupole kernels are Thole-damped. On CUDA (float64) the pair
+    kernel evaluates it (differentiable in positions and dipoles)."""
+    if pos.is_cuda and pos.dtype == torch.float64 and _kernel_ok():
+        if (q.requires_grad or Q.requires_grad or cell.requires_grad) and torch.is_grad_enabled():
+            raise NotImplementedError("the real-space pair kernel differentiates positions and dipoles only")
+        pw = pol if pol is not None else torch.ones_like(q)
+        return _RealKernel.apply(pos, d, cell, q, Q.reshape(-1, 9), pw, i, j, shift, excluded, alpha, thole)
     e = pos.new_zeros(())
     for s in range(0, i.shape[0], chunk):
         a, b = i[s:s + chunk], j[s:s + chunk]
-        v = pos[b] - pos[a] + shift[s:s + chunk].to(pos.dtype) @ cell
+        v = pos[b] - pos[a] + _shift_vec(shift[s:s + chunk], cell)
         r = torch.linalg.norm(v, dim=-1)
         ex = excluded[s:s + chunk]
         Bc = _bn(r, alpha, "erfc")
