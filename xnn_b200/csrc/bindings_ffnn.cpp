@@ -10,6 +10,12 @@ cudaError_t mp_real_launch(int64_t n_pairs, const double* pos, const double* cel
                            const bool* excl, double alpha, double thole, double* energy, double* gpos, double* gd,
                            cudaStream_t s);
 
+cudaError_t pme_spread_launch(int64_t n, int p, const double* pos, const double* G, int K1, int K2, int K3, int z0,
+                              int nz, const double* q, const double* d, const double* Q, float* grid, cudaStream_t s);
+cudaError_t pme_gather_launch(int64_t n, int p, const double* pos, const double* G, int K1, int K2, int K3, int z0,
+                              int nz, const double* q, const double* d, const double* Q, const float* phi, double* gd,
+                              double* gpos, cudaStream_t s);
+
 namespace {
 
 void need(const torch::Tensor& t, torch::ScalarType st, const char* name) {
@@ -42,6 +48,49 @@ std::vector<torch::Tensor> mp_real_op(torch::Tensor pos, torch::Tensor cell, tor
   return {e, gp, gd};
 }
 
+const double* opt(const c10::optional<torch::Tensor>& t, const char* name) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  need(*t, torch::kFloat64, name);
+  return t->data_ptr<double>();
+}
+
+// mesh planes [z0, z0 + nz) of the spread multipoles, float32 (K1, K2, nz)
+torch::Tensor pme_spread_op(torch::Tensor pos, torch::Tensor G, std::vector<int64_t> mesh, int64_t p, int64_t z0,
+                            int64_t nz, c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> d,
+                            c10::optional<torch::Tensor> Q) {
+  need(pos, torch::kFloat64, "pos"); need(G, torch::kFloat64, "G");
+  TORCH_CHECK(mesh.size() == 3, "pme_spread: 3 mesh sizes");
+  c10::cuda::CUDAGuard g(pos.device());
+  auto grid = torch::zeros({mesh[0], mesh[1], nz}, pos.options().dtype(torch::kFloat32));
+  cudaError_t err = pme_spread_launch(pos.size(0), (int)p, pos.data_ptr<double>(), G.data_ptr<double>(), (int)mesh[0],
+                                      (int)mesh[1], (int)mesh[2], (int)z0, (int)nz, opt(q, "q"), opt(d, "d"),
+                                      opt(Q, "Q"), grid.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(err == cudaSuccess, "pme_spread launch failed: ", cudaGetErrorString(err));
+  return grid;
+}
+
+// adjoint: dE/dd and dE/dpos of the spread for the mesh potential phi (float32 (K1, K2, nz))
+std::vector<torch::Tensor> pme_gather_op(torch::Tensor pos, torch::Tensor G, std::vector<int64_t> mesh, int64_t p,
+                                         int64_t z0, int64_t nz, c10::optional<torch::Tensor> q,
+                                         c10::optional<torch::Tensor> d, c10::optional<torch::Tensor> Q,
+                                         torch::Tensor phi, bool want_gd, bool want_gpos) {
+  need(pos, torch::kFloat64, "pos"); need(G, torch::kFloat64, "G"); need(phi, torch::kFloat32, "phi");
+  c10::cuda::CUDAGuard g(pos.device());
+  const int64_t n = pos.size(0);
+  auto gd = want_gd ? torch::zeros({n, 3}, pos.options()) : torch::Tensor();
+  auto gp = want_gpos ? torch::zeros({n, 3}, pos.options()) : torch::Tensor();
+  cudaError_t err = pme_gather_launch(n, (int)p, pos.data_ptr<double>(), G.data_ptr<double>(), (int)mesh[0],
+                                      (int)mesh[1], (int)mesh[2], (int)z0, (int)nz, opt(q, "q"), opt(d, "d"),
+                                      opt(Q, "Q"), phi.data_ptr<float>(), want_gd ? gd.data_ptr<double>() : nullptr,
+                                      want_gpos ? gp.data_ptr<double>() : nullptr, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(err == cudaSuccess, "pme_gather launch failed: ", cudaGetErrorString(err));
+  return {gd, gp};
+}
+
 }  // namespace
 
-void register_ffnn(pybind11::module& m) { m.def("mp_real", &mp_real_op); }
+void register_ffnn(pybind11::module& m) {
+  m.def("mp_real", &mp_real_op);
+  m.def("pme_spread", &pme_spread_op);
+  m.def("pme_gather", &pme_gather_op);
+}

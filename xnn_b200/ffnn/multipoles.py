@@ -113,11 +113,42 @@ def spline_stencil(pos: Tensor, cell: Tensor, mesh: List[int], p: int):
     return base.long(), m0, m1, m2, G
 
 
+class _SpreadKernel(torch.autograd.Function):
+    """Spreading on the CUDA kernel (``csrc/pme_spread.cu``) into a float32 mesh; the backward
+    is the gather kernel (fields and forces). Differentiable in positions and dipoles."""
+
+    @staticmethod
+    def forward(ctx, pos, d, cell, q, Q, mesh, p, z0, nz):
+        from .. import _ext
+        K = torch.tensor(mesh, dtype=torch.float64, device=pos.device)
+        G = (torch.linalg.inv(cell.detach().double()) * K[None, :]).contiguous()
+        args = (pos.detach().contiguous(), G, list(mesh), int(p), int(z0), int(nz),
+                None if q is None else q.detach().contiguous(), None if d is None else d.detach().contiguous(),
+                None if Q is None else Q.detach().reshape(-1, 9).contiguous())
+        ctx.args = args
+        return _ext.ops().pme_spread(*args)
+
+    @staticmethod
+    def backward(ctx, phi):
+        from .. import _ext
+        want_p, want_d = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        gd, gp = _ext.ops().pme_gather(*ctx.args, phi.float().contiguous(), bool(want_d), bool(want_p))
+        return (gp if want_p else None, gd if want_d else None) + (None,) * 7
+
+
 def spread(pos: Tensor, cell: Tensor, q: Optional[Tensor], d: Optional[Tensor], Q: Optional[Tensor],
-           mesh: List[int], p: int, z_range: Optional[Tuple[int, int]] = None) -> Tensor:
+           mesh: List[int], p: int, z_range: Optional[Tuple[int, int]] = None,
+           out_dtype: Optional[torch.dtype] = None) -> Tensor:
     """Mesh of ``sum_i L_i W_i`` (``(K1, K2, K3)``; with ``z_range`` only planes ``[z0, z1)``
-    of the third axis, ``(K1, K2, z1 - z0)``)."""
+    of the third axis, ``(K1, K2, z1 - z0)``). For a float32 mesh of float64 CUDA sites the
+    spreading kernel runs (its adjoint differentiates positions and dipoles)."""
     n = pos.shape[0]
+    if (out_dtype == torch.float32 and pos.is_cuda and pos.dtype == torch.float64 and p <= 8 and _kernel_ok()
+            and hasattr(__import__("xnn_b200._ext", fromlist=["ops"]).ops(), "pme_spread")):
+        if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (q, Q, cell)):
+            raise NotImplementedError("the spreading kernel differentiates positions and dipoles only")
+        z0, z1 = z_range if z_range is not None else (0, mesh[2])
+        return _SpreadKernel.apply(pos, d, cell, q, Q, list(mesh), p, z0, z1 - z0)
     K1, K2, K3 = mesh
     base, m0, m1, m2, G = spline_stencil(pos, cell, mesh, p)
     # multipoles in scaled-fractional coordinates: d_u = G^T d, Q_u = G^T Q G
@@ -393,7 +424,7 @@ class PolarizableMultipoles(nn.Module):
         s = self.setup
         if self.mesh_backend is not None:
             return self.mesh_backend.energy(pos, cell, q, d, Q, s)
-        grid = spread(pos, cell, q, d, Q, list(s.mesh), s.order).to(s.fft_dtype)
+        grid = spread(pos, cell, q, d, Q, list(s.mesh), s.order, out_dtype=s.fft_dtype).to(s.fft_dtype)
         return recip_energy(grid, self._influence(cell)).to(pos.dtype)
 
     def electrostatic(self, pos, cell, pairs, q, d, Q, pol: Optional[Tensor] = None) -> Tensor:

@@ -182,7 +182,8 @@ class SlabFFT:
             pos, q = pos.index_select(0, keep), q.index_select(0, keep) if q is not None else None
             d = d.index_select(0, keep) if d is not None else None
             Q = Q.index_select(0, keep) if Q is not None else None
-        planes = spread(pos, cell, q, d, Q, self.mesh, p, z_range=(z0, z1)).to(setup.fft_dtype)
+        planes = spread(pos, cell, q, d, Q, self.mesh, p, z_range=(z0, z1), out_dtype=setup.fft_dtype).to(
+            setup.fft_dtype)
         F = torch.fft.rfft(planes, dim=0)                 # (K1//2+1, K2, nz)
         F = torch.fft.fft(F, dim=1)
         F = _Transpose.apply(F, self)                      # (nkx_r, K2, K3)
