@@ -63,7 +63,7 @@ def test_d3_matches_reference(kind, damping, s9):
     b = theirs.evaluate(*args(pos))
     torch.testing.assert_close(a["node_energy"], b["node_energy"], rtol=1e-9, atol=1e-11)
     torch.testing.assert_close(a["coordination_numbers"], b["coordination_numbers"], rtol=1e-11, atol=1e-12)
-    fa, = torch.autograd.grad(a["node_energy"].sum(), pos)
+    fa, = torch.autograd.grad(a["node_energy"].sum(), pos, retain_graph=True)
     fb, = torch.autograd.grad(b["node_energy"].sum(), pos)
     torch.testing.assert_close(fa, fb, rtol=1e-8, atol=1e-11)
 
@@ -147,3 +147,26 @@ def test_latent_ewald_wrapper():
     gm.pos[k, 0] -= eps
     fd = -(les(gp)["energy"] - les(gm)["energy"]) / (2 * eps)
     torch.testing.assert_close(o["forces"][k, 0], fd[0], rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("s9", [0.0, 1.0])
+def test_d4_matches_reference_for_molecules(s9):
+    ref_d4 = _reference("xnn.common.models.d4")
+    from xnn_b200.data import collate
+    from xnn_b200.models.d4 import DFTD4
+    mols = synthetic.organic_molecules(2, seed=6, labels=False)
+    b = collate([structure_to_graph(s, 14.0) for s in mols])
+    opts = dict(s9=s9, cutoff_pair=14.0, cutoff_triple=10.0, cutoff_cn=10.0, cutoff_eeq_cn=10.0)
+    mine, theirs = DFTD4(**opts), ref_d4.DFTD4(regime="dense", **opts)
+    pos = b.pos.clone().requires_grad_(True)
+    vec = pos[b.edge_index[1]] - pos[b.edge_index[0]]
+    args = (b.atomic_numbers, pos, b.edge_index, vec, b.batch, 2, torch.zeros(2, 3, 3),
+            torch.zeros(2, 3, dtype=torch.bool), torch.tensor([0.0, 1.0]))
+    a = mine.evaluate(*args)
+    r = theirs.evaluate(*args)
+    for k in ("charges", "coordination_numbers", "polarizabilities"):
+        torch.testing.assert_close(a[k], r[k], rtol=1e-10, atol=1e-12)
+    torch.testing.assert_close(a["node_energy"], r["node_energy"], rtol=1e-9, atol=1e-11)
+    fa, = torch.autograd.grad(a["node_energy"].sum(), pos, retain_graph=True)
+    fr, = torch.autograd.grad(r["node_energy"].sum(), pos)
+    torch.testing.assert_close(fa, fr, rtol=1e-8, atol=1e-11)

@@ -1,0 +1,227 @@
+"""Grimme D4 dispersion: EEQ partial charges, charge-scaled dynamic polarizabilities, C6 by
+Casimir-Polder integration, BJ-damped two-body and ATM three-body energies.
+
+Written from Caldeweyher et al., J. Chem. Phys. 150, 154122 (2019), with the conventions of the
+reference's ``src/xnn/common/models/d4.py`` (``DFTD4`` at ``:266``) so the numbers agree: the
+error-function coordination number (k0 = 7.5, 4/3-scaled covalent radii) weighted by the
+electronegativity factor (k1..k3), the softly capped EEQ coordination number, the EEQ solve with
+the Gaussian-charge Coulomb matrix and the total-charge constraint, the N^s Gaussian weights
+(beta2 = 6) with the highest-CN fallback, the charge scaling zeta of the reference
+polarizabilities (ga = 3, gc = 2), the 23-point Casimir-Polder trapezoid grid, and the ATM term
+from neutral (q = 0) polarizabilities. Reference data: the published D4 tables
+(``d4_reference.npz``, see :mod:`xnn_b200.models.dispersion`).
+
+Built: the dense regime for isolated structures (molecules; a batch of them). Not built: the
+periodic Ewald EEQ, the large-system iterative EEQ and the tail correction (a periodic structure
+raises ``NotImplementedError``).
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict
+
+import numpy as np
+import torch
+from torch import Tensor, nn
+
+from ..ops.scatter import scatter_sum, structure_sum
+from .dispersion import (BOHR, HARTREE, DispersionCorrection, evaluate_on_graph, gaussian_reference_weights,
+                         load_tables, options_from_extra, switching_function, three_body_energy)
+from .registry import register_model
+
+KCN, K4, K5, K6 = 7.5, 4.10451, 19.08857, 2.0 * 11.28174 ** 2
+EEQ_CN_MAX, EEQ_CN_REG = 8.0, 1.0e-14
+MAX_Z = 103
+CUTOFF_PAIR_AU, CUTOFF_TRIPLE_AU, CUTOFF_CN_AU, CUTOFF_EEQ_CN_AU = 60.0, 40.0, 30.0, 25.0
+FREQ = [0.000001, 0.05, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 1.0, 1.2, 1.4, 1.6, 1.8, 2.0, 2.5, 3.0, 4.0,
+        5.0, 7.5, 10.0]
+CP_WEIGHTS = [0.5 * ((FREQ[k] - FREQ[k - 1] if k > 0 else 0.0) + (FREQ[k + 1] - FREQ[k] if k < len(FREQ) - 1 else 0.0))
+              for k in range(len(FREQ))]
+
+
+def _zeta(a: float, c, qref, qmod):
+    """Charge scaling exp(a (1 - exp(c (1 - qref / qmod)))), exp(a) for negative qmod."""
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        s = np.exp(a * (1.0 - np.exp(c * (1.0 - qref / qmod))))
+    return np.where(qmod < 0.0, np.exp(a), s)
+
+
+class DFTD4(nn.Module):
+    def __init__(self, s6: float = 1.0, s8: float = 1.20065498, a1: float = 0.40085597, a2: float = 5.02928789,
+                 s9: float = 1.0, alp: float = 16.0, ga: float = 3.0, gc: float = 2.0, wf: float = 6.0,
+                 cutoff_pair: float = CUTOFF_PAIR_AU * BOHR, cutoff_triple: float = CUTOFF_TRIPLE_AU * BOHR,
+                 cutoff_cn: float = CUTOFF_CN_AU * BOHR, cutoff_eeq_cn: float = CUTOFF_EEQ_CN_AU * BOHR,
+                 switch_width_pair: float = 0.0, switch_width_triple: float = 0.0, trainable: bool = False,
+                 reference_charges: str = "eeq", **unused):
+        super().__init__()
+        self.ga, self.gc, self.wf, self.alp = float(ga), float(gc), float(wf), float(alp)
+        self.cutoff_pair, self.cutoff_triple = float(cutoff_pair), float(cutoff_triple)
+        self.cutoff_cn, self.cutoff_eeq_cn = float(cutoff_cn), float(cutoff_eeq_cn)
+        self.cutoff = max(self.cutoff_pair, self.cutoff_triple, self.cutoff_cn, self.cutoff_eeq_cn)
+        self.switch_width_pair, self.switch_width_triple = float(switch_width_pair), float(switch_width_triple)
+        self.n_features = 3
+        dt = torch.get_default_dtype()
+        for name, v in [("s6", s6), ("s8", s8), ("a1", a1), ("a2", a2), ("s9", s9)]:
+            t = torch.tensor(float(v), dtype=dt)
+            if trainable:
+                setattr(self, name, nn.Parameter(t))
+            else:
+                self.register_buffer(name, t)
+        ref = load_tables("d4_reference.npz")
+        if reference_charges not in ("eeq", "gfn2"):
+            raise ValueError("reference_charges must be 'eeq' or 'gfn2'")
+        if reference_charges == "gfn2":
+            ref = dict(ref, refq=ref["refq_gfn2"], refh=ref["refh_gfn2"])
+        buf = lambda n, a, d=dt: self.register_buffer(n, torch.tensor(a, dtype=d), persistent=False)  # noqa: E731
+        buf("rcov", 4.0 / 3.0 * ref["covalent_radius_aa"] / BOHR)
+        buf("en", ref["pauling_en"])
+        buf("zeff", ref["zeff"])
+        buf("hardness", ref["hardness"])
+        zz = np.arange(ref["r4r2_raw"].shape[0], dtype=np.float64)
+        buf("r4r2", np.sqrt(0.5 * ref["r4r2_raw"] * np.sqrt(zz)))
+        for k in ("eeq_chi", "eeq_eta", "eeq_kcnchi", "eeq_rad"):
+            buf(k, np.nan_to_num(ref[k], nan=0.0))
+        buf("nref", ref["nref"], torch.long)
+        buf("ngw", ref["ngw"], torch.long)
+        self.max_ngw = int(ref["ngw"].max())
+        buf("refcn", ref["refcn"])
+        buf("refq", ref["refq"])
+        buf("refalpha", self._reference_polarizabilities(ref))
+        buf("cp_weights", CP_WEIGHTS)
+
+    def _reference_polarizabilities(self, ref) -> np.ndarray:
+        """``alpha_A,ref(i w)`` (23, 7, Z): the reference molecule's TD-DFT polarizability minus
+        its charge-scaled secondary systems, times the reference's scale, clamped at zero."""
+        sys = ref["refsys"]
+        present = sys > 0
+        idx = np.where(present, sys, 0)
+        zx = ref["zeff"][idx]
+        hx = ref["hardness"][idx] * self.gc
+        scale = _zeta(self.ga, hx, zx, ref["refh"] + zx)
+        aiw_x = ref["sscale"][idx] * ref["secaiw"][:, idx] * scale
+        alpha = ref["ascale"] * (ref["alphaiw"] - ref["hcount"] * aiw_x)
+        return np.where(present, np.maximum(alpha, 0.0), 0.0)
+
+    # ------------------------------------------------------------------ pieces (atomic units)
+    def coordination_numbers(self, z, edge_index, r, n):
+        src, dst = edge_index[0], edge_index[1]
+        zi, zj = z[dst], z[src]
+        rc = self.rcov[zi] + self.rcov[zj]
+        count = 0.5 * (1.0 + torch.erf(-KCN * (r - rc) / rc))
+        enf = K4 * torch.exp(-((self.en[zi] - self.en[zj]).abs() + K5) ** 2 / K6)
+        cn_d4 = scatter_sum(torch.where(r <= self.cutoff_cn / BOHR, enf * count, torch.zeros_like(count)), dst, n)
+        raw = scatter_sum(torch.where(r <= self.cutoff_eeq_cn / BOHR, count, torch.zeros_like(count)), dst, n)
+        cn_eeq = math.log(1.0 + math.exp(EEQ_CN_MAX)) - torch.log(1.0 + torch.exp(EEQ_CN_MAX - raw))
+        return cn_d4, cn_eeq
+
+    def eeq_charges(self, z, pos, cn_eeq, total_charge) -> Tensor:
+        """EEQ charges of one isolated structure (positions in bohr)."""
+        n = pos.shape[0]
+        rad2 = self.eeq_rad[z] ** 2
+        gamma = torch.rsqrt(rad2[:, None] + rad2[None, :])
+        eye = torch.eye(n, dtype=torch.bool, device=pos.device)
+        dvec = pos[None, :, :] - pos[:, None, :]
+        r2 = (dvec * dvec).sum(-1)
+        r = torch.sqrt(torch.where(eye, torch.ones_like(r2), r2))
+        A = torch.where(eye, torch.zeros_like(r), torch.erf(gamma * r) / r)
+        A = A + torch.diag(self.eeq_eta[z] + math.sqrt(2.0 / math.pi) / self.eeq_rad[z])
+        x = -self.eeq_chi[z] + self.eeq_kcnchi[z] * cn_eeq / torch.sqrt(cn_eeq + EEQ_CN_REG)
+        ones = torch.ones((n, 1), dtype=pos.dtype, device=pos.device)
+        zero = torch.zeros((1, 1), dtype=pos.dtype, device=pos.device)
+        full = torch.cat([torch.cat([A, ones], 1), torch.cat([ones.t(), zero], 1)], 0)
+        rhs = torch.cat([x, total_charge.reshape(1).to(pos.dtype)])[:, None]
+        return torch.linalg.solve(full, rhs)[:n, 0]
+
+    def gaussian_weights(self, z, cn):
+        refcn = self.refcn[:, z].t()
+        ngw = self.ngw[:, z].t()
+        valid = torch.arange(refcn.shape[1], device=z.device)[None, :] < self.nref[z][:, None]
+        eps = 1.0842021724855044e-19 if cn.dtype == torch.float32 else 1.4916681462400413e-154
+        return gaussian_reference_weights(cn, refcn, valid, self.wf, ngw, eps)
+
+    def charge_scaling(self, z, q):
+        zi = self.zeff[z][:, None]
+        gi = (self.hardness[z] * self.gc)[:, None]
+        qmod = q[:, None] + zi
+        qref = self.refq[:, z].t() + zi
+        neg = qmod < 0.0
+        safe = torch.where(neg, torch.ones_like(qmod), qmod)
+        s = torch.exp(self.ga * (1.0 - torch.exp(gi * (1.0 - qref / safe))))
+        return torch.where(neg, torch.full_like(qmod, math.exp(self.ga)), s)
+
+    def dynamic_polarizabilities(self, z, weights):
+        return torch.einsum("nr,krn->nk", weights, self.refalpha[:, :, z])
+
+    def two_body_energy(self, z, edge_index, r, alpha_iw, n):
+        src, dst = edge_index[0], edge_index[1]
+        c6 = (3.0 / math.pi) * (alpha_iw[dst] * alpha_iw[src] * self.cp_weights).sum(-1)
+        zi, zj = z[dst], z[src]
+        rr = 3.0 * self.r4r2[zi] * self.r4r2[zj]
+        r0 = self.a1 * torch.sqrt(rr) + self.a2
+        r2 = r * r
+        t6 = 1.0 / (r2 ** 3 + r0 ** 6)
+        t8 = 1.0 / (r2 ** 4 + r0 ** 8)
+        sw = switching_function(r, self.cutoff_pair / BOHR, self.switch_width_pair / BOHR)
+        return scatter_sum(-0.5 * c6 * sw * (self.s6 * t6 + self.s8 * rr * t8), dst, n)
+
+    def pair_radius_table(self) -> Tensor:
+        return self.a1 * torch.sqrt(3.0 * self.r4r2[:, None] * self.r4r2[None, :]) + self.a2
+
+    # ------------------------------------------------------------------ evaluation
+    def evaluate(self, atomic_numbers: Tensor, pos: Tensor, edge_index: Tensor, edge_vec: Tensor, batch: Tensor,
+                 num_graphs: int, cell: Tensor, pbc: Tensor, total_charge: Tensor) -> Dict[str, Tensor]:
+        z = atomic_numbers
+        n = z.shape[0]
+        if bool((z > MAX_Z).any()) or bool((z < 1).any()):
+            raise ValueError("D4 with EEQ charges supports atomic numbers 1..103")
+        periodic = pbc.any(-1) & (cell.abs().sum((-1, -2)) > 1e-8)
+        if bool(periodic.any()):
+            raise NotImplementedError("D4 for periodic structures (Ewald EEQ) is not built; use D3")
+        pos_au = pos / BOHR
+        vec = edge_vec / BOHR
+        r = torch.linalg.norm(vec, dim=-1)
+        cn_d4, cn_eeq = self.coordination_numbers(z, edge_index, r, n)
+        q = torch.zeros_like(cn_d4)
+        for b in range(num_graphs):
+            m = torch.nonzero(batch == b).squeeze(1)
+            q = q.index_put((m,), self.eeq_charges(z[m], pos_au[m], cn_eeq[m], total_charge[b]))
+        alpha_iw = self.dynamic_polarizabilities(z, self.gaussian_weights(z, cn_d4) * self.charge_scaling(z, q))
+        in_pair = r <= self.cutoff_pair / BOHR
+        e2 = self.two_body_energy(z, edge_index[:, in_pair], r[in_pair], alpha_iw, n)
+        e3 = torch.zeros_like(e2)
+        if bool(self.s9 != 0.0):
+            w0 = self.gaussian_weights(z, cn_d4) * self.charge_scaling(z, torch.zeros_like(q))
+            a0 = self.dynamic_polarizabilities(z, w0)
+            c6_0 = (3.0 / math.pi) * (a0 * self.cp_weights) @ a0.t()
+            m3 = r <= self.cutoff_triple / BOHR
+            e3 = three_body_energy(z, edge_index[:, m3], vec[m3], r[m3], c6_0, self.pair_radius_table(), self.s9,
+                                   self.alp / 3.0, self.cutoff_triple / BOHR, self.switch_width_triple / BOHR, n)
+        return {"node_energy": (e2 + e3) * HARTREE,
+                "energy_2body": structure_sum(e2, batch, num_graphs) * HARTREE,
+                "energy_3body": structure_sum(e3, batch, num_graphs) * HARTREE,
+                "coordination_numbers": cn_d4, "charges": q, "polarizabilities": alpha_iw[:, 0],
+                "dynamic_polarizabilities": alpha_iw,
+                "node_features": torch.stack([cn_d4, q, alpha_iw[:, 0]], 1)}
+
+    def forward(self, data) -> Dict[str, Tensor]:
+        return evaluate_on_graph(self, data)
+
+
+D4_KEYS = ("s6", "s8", "a1", "a2", "s9", "alp", "ga", "gc", "wf", "cutoff_pair", "cutoff_triple", "cutoff_cn",
+           "cutoff_eeq_cn", "switch_width_pair", "switch_width_triple", "trainable", "reference_charges")
+
+
+@register_model("d4")
+class D4Dispersion(DispersionCorrection):
+    """D4 as a potential: standalone, or added to ``model`` (``model.extra["dispersion"]``)."""
+
+    def __init__(self, model=None, **d4_options):
+        super().__init__(DFTD4(**{k: v for k, v in d4_options.items() if k in D4_KEYS}), model)
+
+    @property
+    def d4(self) -> DFTD4:
+        return self.term
+
+    @classmethod
+    def from_config(cls, cfg) -> "D4Dispersion":
+        return cls(**options_from_extra(dict(getattr(cfg, "extra", {}) or {}), D4_KEYS))
