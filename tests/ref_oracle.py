@@ -1,0 +1,67 @@
+"""The reference framework (installed under ``baseline/_ref``) as an oracle: load its module, copy
+a batch into its graph type and compare energies / forces / stress of the same state dict."""
+import importlib
+import os
+import sys
+import warnings
+
+import pytest
+import torch
+
+from xnn_b200.data import collate, structure_to_graph, synthetic
+from xnn_b200.models import ForceStressOutput
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "baseline", "_ref")
+
+
+def ref_module(name):
+    if not os.path.isdir(os.path.join(REF, "xnn")):
+        pytest.skip("reference framework not installed under baseline/_ref")
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    with warnings.catch_warnings():
+        warnings.simplefilter("ignore")
+        return importlib.import_module(name)
+
+
+def batch(periodic=False, cutoff=5.0, n=3, species=None, seed=2):
+    if periodic:
+        ss = synthetic.triclinic_crystals(2, seed=5, labels=False)
+        for s in ss:
+            s["atomic_numbers"] = torch.full_like(s["atomic_numbers"], 8)
+    else:
+        ss = synthetic.organic_molecules(n, seed=seed, labels=False)
+    if species is not None:
+        for s in ss:
+            z = s["atomic_numbers"]
+            s["atomic_numbers"] = torch.as_tensor(species)[torch.arange(len(z)) % len(species)]
+    return collate([structure_to_graph(s, cutoff) for s in ss])
+
+
+def ref_graph(b, **extra):
+    ad = ref_module("xnn.common.data")
+    return ad.AtomicGraph(pos=b.pos.clone(), atomic_numbers=b.atomic_numbers, edge_index=b.edge_index,
+                          cell_shifts=b.cell_shifts, batch=b.batch, n_atoms=b.n_atoms, cell=b.cell, pbc=b.pbc,
+                          **extra)
+
+
+def load_same_weights(mine, ref):
+    missing, unexpected = mine.load_state_dict(ref.state_dict(), strict=False)
+    assert not missing and not unexpected, (missing, unexpected)
+
+
+def compare(mine, ref, b, periodic=False, rtol=1e-10, atol=1e-11, keys=(), **extra):
+    outs = ref_module("xnn.common.models.outputs")
+    o_ref = outs.ForceStressOutput(ref, compute_stress=periodic)(ref_graph(b, **extra))
+    g = b.clone()
+    for k, v in extra.items():
+        setattr(g, k, v)
+    o = ForceStressOutput(mine, compute_stress=periodic)(g)
+    torch.testing.assert_close(o["energy"], o_ref["energy"], rtol=rtol, atol=atol)
+    torch.testing.assert_close(o["forces"], o_ref["forces"], rtol=rtol, atol=atol)
+    if periodic:
+        torch.testing.assert_close(o["stress"], o_ref["stress"], rtol=rtol, atol=atol)
+    for k in keys:
+        torch.testing.assert_close(o[k], o_ref[k], rtol=rtol, atol=atol)
+    return o, o_ref

@@ -18,17 +18,13 @@ from torch import Tensor, nn
 
 from ..data import AtomicGraph
 from ..nn import CosineCutoff, make_radial_basis
+from ..nn.blocks import GatedMLP, make_activation
 from ..ops.scatter import refresh_ghosts, scatter_sum
 from .base import InteratomicPotential
 from .registry import register_model
 
 _READOUTS = ("mlp", "gated")
 _GROUPS = ("O(3)", "SO(3)")
-
-
-def make_activation(name: str) -> nn.Module:
-    return {"silu": nn.SiLU, "tanh": nn.Tanh, "relu": nn.ReLU, "gelu": nn.GELU,
-            "ssp": nn.Softplus}[name]()
 
 
 def skew_tensor(v: Tensor) -> Tensor:
@@ -61,21 +57,6 @@ def frobenius(t: Tensor) -> Tensor:
 
 def tensor_matmul(a: Tensor, b: Tensor) -> Tensor:
     return (a.unsqueeze(3) * b.unsqueeze(1)).sum(2)
-
-
-class GatedMLP(nn.Module):
-    def __init__(self, sizes, activation: str):
-        super().__init__()
-        self.layers = nn.ModuleList([nn.Linear(a, b) for a, b in zip(sizes[:-1], sizes[1:])])
-        self.gates = nn.ModuleList([nn.Linear(a, b) for a, b in zip(sizes[:-1], sizes[1:])])
-        self.act = make_activation(activation)
-
-    def forward(self, x: Tensor) -> Tensor:
-        for i, (l, g) in enumerate(zip(self.layers, self.gates)):
-            last = i == len(self.layers) - 1
-            h = l(x) if last else self.act(l(x))
-            x = h * torch.sigmoid(g(x))
-        return x
 
 
 class TensorEmbedding(nn.Module):
