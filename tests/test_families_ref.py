@@ -41,3 +41,40 @@ def test_qet(hardness, periodic):
     b = batch(periodic)
     extra = {"total_charge": torch.tensor([1.0, -1.0] + ([0.0] if not periodic else []))}
     compare(mine, ref, b, periodic, keys=("charges",), **extra)
+
+
+def _properties(mine, ref, b, train, **extra):
+    from ref_oracle import ref_graph
+    mine.train(train)
+    ref.train(train)
+    g = b.clone()
+    for k, v in extra.items():
+        setattr(g, k, v)
+    o, o_ref = mine(g), ref(ref_graph(b, **extra))
+    torch.testing.assert_close(o["properties"], o_ref["properties"], rtol=1e-10, atol=1e-11)
+    torch.testing.assert_close(o["structure_features"], o_ref["structure_features"], rtol=1e-10, atol=1e-11)
+
+
+@pytest.mark.parametrize("train", [False, True])
+@pytest.mark.parametrize("classification", [False, True])
+def test_cgcnn(train, classification):
+    from xnn_b200.models.cgcnn import CGCNN
+    mine, ref = _pair("xnn.gnn.models.cgcnn", "CGCNN", CGCNN, n_features=8, n_interactions=2, n_rbf=12,
+                      cutoff=5.0, max_neighbors=6, atom_features="onehot", classification=classification,
+                      dropout=0.0)
+    with torch.no_grad():   # non-trivial batch-norm statistics and affine parameters
+        for mod in list(ref.modules()):
+            if isinstance(mod, torch.nn.BatchNorm1d):
+                mod.running_mean.uniform_(-0.5, 0.5); mod.running_var.uniform_(0.5, 2.0)
+                mod.weight.uniform_(0.5, 1.5); mod.bias.uniform_(-0.3, 0.3)
+    load_same_weights(mine, ref)
+    _properties(mine, ref, batch(False, cutoff=5.0), train)
+
+
+@pytest.mark.parametrize("states", [None, 3])
+def test_megnet(states):
+    from xnn_b200.models.megnet import MEGNet
+    mine, ref = _pair("xnn.gnn.models.megnet", "MEGNet", MEGNet, n_features=8, n_interactions=2, n_rbf=10,
+                      cutoff=4.0, n_state_types=states)
+    extra = {"state": torch.tensor([0, 2, 1])} if states else {}
+    _properties(mine, ref, batch(False, cutoff=4.0), False, **extra)

@@ -40,7 +40,8 @@ def structure_sum(values: Tensor, batch: Tensor, num_graphs: int) -> Tensor:
 def segment_softmax(logits: Tensor, index: Tensor, n: int) -> Tensor:
     """Softmax of ``logits`` within the groups given by ``index`` (``n`` groups)."""
     shape = (n,) + tuple(logits.shape[1:])
-    mx = logits.new_full(shape, float("-inf")).index_reduce(0, index, logits, "amax", include_self=True)
+    idx = index.view((-1,) + (1,) * (logits.dim() - 1)).expand_as(logits)
+    mx = logits.new_full(shape, float("-inf")).scatter_reduce(0, idx, logits, "amax", include_self=True)
     e = torch.exp(logits - mx.index_select(0, index))
     s = scatter_sum(e, index, n)
     return e / s.index_select(0, index).clamp_min(1e-30)
