@@ -78,3 +78,16 @@ def test_megnet(states):
                       cutoff=4.0, n_state_types=states)
     extra = {"state": torch.tensor([0, 2, 1])} if states else {}
     _properties(mine, ref, batch(False, cutoff=4.0), False, **extra)
+
+
+@pytest.mark.parametrize("preset", ["ani1x", "ani2x", "ani1"])
+def test_ani(preset):
+    from xnn_b200.models.ani import ANI
+    mod = ref_module("xnn.dnn.models.ani")
+    torch.manual_seed(0)
+    ref = getattr(mod.ANI, preset)().double()
+    mine = getattr(ANI, preset)().double()
+    load_same_weights(mine, ref)
+    sp = [1, 6, 7, 8, 16, 9, 17] if preset == "ani2x" else [1, 6, 7, 8]
+    compare(mine, ref, batch(False, cutoff=mine.cutoff, species=sp), rtol=1e-9, atol=1e-9)
+    compare(mine, ref, batch(True, cutoff=mine.cutoff), True, rtol=1e-9, atol=1e-9)

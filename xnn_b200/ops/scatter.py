@@ -68,6 +68,23 @@ def build_triplets(edge_index: Tensor, n_nodes: int):
     return e1[keep], e2[keep]
 
 
+def build_center_pairs(dst: Tensor, n_nodes: int):
+    """All unordered pairs of distinct edges sharing a receiver, as ``(first, second)`` edge
+    indices with ``first`` before ``second`` in the receiver's (stable) edge order."""
+    order = torch.argsort(dst, stable=True)
+    counts = torch.bincount(dst, minlength=n_nodes)
+    starts = torch.cumsum(counts, 0) - counts
+    d = dst.index_select(0, order)
+    local = torch.arange(order.numel(), device=dst.device) - starts.index_select(0, d)
+    partners = counts.index_select(0, d) - 1 - local               # later edges of the same receiver
+    first = torch.repeat_interleave(order, partners)
+    base = torch.repeat_interleave(torch.arange(order.numel(), device=dst.device), partners)
+    k = torch.arange(first.numel(), device=dst.device) - torch.repeat_interleave(
+        torch.cumsum(partners, 0) - partners, partners)
+    second = order.index_select(0, base + 1 + k)
+    return first, second
+
+
 # --- domain-decomposition hooks --------------------------------------------------------
 def active_domain():
     return getattr(_DOMAIN, "plan", None)
