@@ -91,3 +91,58 @@ def test_ani(preset):
     sp = [1, 6, 7, 8, 16, 9, 17] if preset == "ani2x" else [1, 6, 7, 8]
     compare(mine, ref, batch(False, cutoff=mine.cutoff, species=sp), rtol=1e-9, atol=1e-9)
     compare(mine, ref, batch(True, cutoff=mine.cutoff), True, rtol=1e-9, atol=1e-9)
+
+
+_CUTS = [{"kind": "cosine", "r_cut": 5.0}, {"kind": "tanh", "r_cut": 4.0, "r_inner": 0.5},
+         {"kind": "polynomial", "r_cut": 4.5, "exponent": 3}]
+
+
+def _functions(species):
+    f = []
+    for zc in species:
+        for zn in species:
+            f.append({"element": zc, "type": 2, "neighbors": [zn], "eta": 0.3, "rs": 1.0, "cutoff": 1})
+            f.append({"element": zc, "type": 1, "neighbors": [zn], "n_features": 2, "cutoff": 2})
+        for a in species:
+            for b in species:
+                if a <= b:
+                    f.append({"element": zc, "type": 3, "neighbors": [a, b], "eta": 0.02, "lambda": -1.0,
+                              "zeta": 2.0})
+                    f.append({"element": zc, "type": 9, "neighbors": [b, a], "eta": 0.01, "lambda": 1.0,
+                              "zeta": 4.0, "cutoff": 1})
+                    f.append({"element": zc, "type": 8, "neighbors": [a, b], "eta": 0.001, "theta_s": 100.0})
+    return f
+
+
+@pytest.mark.parametrize("generation,periodic", [(2, False), (2, True), (3, False), (4, False), (4, True)])
+def test_hdnnp(generation, periodic):
+    from xnn_b200.featurizers.acsf import AtomCenteredSymmetryFunctions
+    from xnn_b200.models.hdnnp import HDNNP
+    sp = [6, 8] if not periodic else [8]
+    refm = ref_module("xnn.dnn.models.hdnnp")
+    reff = ref_module("xnn.dnn.featurizers.acsf")
+    torch.manual_seed(0)
+    kw = dict(generation=generation, hidden=(6, 5), atomic_energies=[-1.0 * z for z in sp],
+              screening={"kind": "cosine", "r_cut": 3.0} if generation >= 3 else None)
+    ref = refm.HDNNP(sp, reff.AtomCenteredSymmetryFunctions(sp, _CUTS, _functions(sp), mode="center_scale"),
+                     **kw).double()
+    mine = HDNNP(sp, AtomCenteredSymmetryFunctions(sp, _CUTS, _functions(sp), mode="center_scale"), **kw).double()
+    b = batch(periodic, cutoff=5.0, species=sp)
+    with torch.no_grad():
+        ref.featurizer.stat_min.uniform_(-0.1, 0.1); ref.featurizer.stat_max.uniform_(1.0, 2.0)
+        ref.featurizer.stat_avg.uniform_(0.0, 0.5)
+    load_same_weights(mine, ref)
+    keys = ("charges",) if generation >= 3 else ()
+    extra = {"total_charge": torch.tensor([1.0, 0.0] + ([] if periodic else [-1.0]))} if generation >= 3 else {}
+    compare(mine, ref, b, periodic, rtol=1e-9, atol=1e-9, keys=keys, **extra)
+
+
+@pytest.mark.parametrize("symmetrize", [False, True])
+def test_nnp1g(symmetrize):
+    from xnn_b200.data import collate, structure_to_graph
+    from xnn_b200.models.hdnnp import NNP1G
+    mine, ref = _pair("xnn.dnn.models.hdnnp", "NNP1G", NNP1G, species=[8, 1, 1], hidden=(7,),
+                      coordinates="exponential", symmetrize=symmetrize)
+    torch.manual_seed(3)
+    ss = [{"pos": torch.randn(3, 3), "atomic_numbers": torch.tensor([8, 1, 1])} for _ in range(2)]
+    compare(mine, ref, collate([structure_to_graph(s, 1.0) for s in ss]), rtol=1e-10, atol=1e-10)
