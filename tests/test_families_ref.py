@@ -146,3 +146,19 @@ def test_nnp1g(symmetrize):
     torch.manual_seed(3)
     ss = [{"pos": torch.randn(3, 3), "atomic_numbers": torch.tensor([8, 1, 1])} for _ in range(2)]
     compare(mine, ref, collate([structure_to_graph(s, 1.0) for s in ss]), rtol=1e-10, atol=1e-10)
+
+
+@pytest.mark.parametrize("lr_cutoff,dispersion", [(None, False), (8.0, False), (None, True), (8.0, True)])
+def test_physnet(lr_cutoff, dispersion):
+    from xnn_b200.models.physnet import PhysNet
+    mine, ref = _pair("xnn.dnn.models.physnet", "PhysNet", PhysNet, cutoff=5.0, lr_cutoff=lr_cutoff, n_features=8,
+                      n_rbf=6, num_blocks=2, use_dispersion=dispersion)
+    with torch.no_grad():   # the zero-initialised heads would hide most of the network
+        for name, p in ref.named_parameters():
+            if "k2f" in name or "output_blocks" in name:
+                p.uniform_(-0.3, 0.3)
+    load_same_weights(mine, ref)
+    tol = 1e-6 if dispersion else 1e-10   # float32-rounded D3 radii in the reference's legacy tables
+    b = batch(False, cutoff=lr_cutoff or 5.0)
+    compare(mine, ref, b, rtol=tol, atol=tol, keys=("charges", "nh_loss"),
+            total_charge=torch.tensor([1.0, 0.0, -2.0]))
