@@ -162,3 +162,11 @@ def test_physnet(lr_cutoff, dispersion):
     b = batch(False, cutoff=lr_cutoff or 5.0)
     compare(mine, ref, b, rtol=tol, atol=tol, keys=("charges", "nh_loss"),
             total_charge=torch.tensor([1.0, 0.0, -2.0]))
+
+
+@pytest.mark.parametrize("charge_model", ["recursive", "qeq"])
+def test_qrnn(charge_model):
+    from xnn_b200.models.qrnn import QRNN
+    mine, ref = _pair("xnn.dnn.models.qrnn", "QRNN", QRNN, hidden=(8, 6), charge_model=charge_model)
+    b = batch(False, cutoff=mine.cutoff, species=[1, 6, 7, 8, 16, 17])
+    compare(mine, ref, b, rtol=1e-9, atol=1e-9, keys=("charges",), total_charge=torch.tensor([1.0, 0.0, -1.0]))
