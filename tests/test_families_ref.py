@@ -170,3 +170,33 @@ def test_qrnn(charge_model):
     mine, ref = _pair("xnn.dnn.models.qrnn", "QRNN", QRNN, hidden=(8, 6), charge_model=charge_model)
     b = batch(False, cutoff=mine.cutoff, species=[1, 6, 7, 8, 16, 17])
     compare(mine, ref, b, rtol=1e-9, atol=1e-9, keys=("charges",), total_charge=torch.tensor([1.0, 0.0, -1.0]))
+
+
+@pytest.mark.parametrize("energy_constraint,symmetric", [(False, False), (True, False), (False, True)])
+def test_sgdml_fit_and_predict(energy_constraint, symmetric):
+    """Both frameworks fit the same training set; the fitted models agree on new structures."""
+    from xnn_b200.data import collate, structure_to_graph
+    from xnn_b200.models.sgdml import SGDML
+    refm = ref_module("xnn.krnn.models.sgdml")
+    z = torch.tensor([8, 1, 1, 6])
+    torch.manual_seed(4)
+    base = torch.tensor([[0.0, 0.0, 0.0], [0.95, 0.1, 0.0], [-0.3, 0.9, 0.1], [0.2, -0.4, 1.4]])
+
+    def structs(k):
+        out = []
+        for _ in range(k):
+            p = base + 0.05 * torch.randn(4, 3)
+            d = torch.cdist(p, p) + torch.eye(4)
+            e = (1.0 / d).triu(1).sum()
+            f = -torch.autograd.functional.jacobian(lambda q: (1.0 / (torch.cdist(q, q) + torch.eye(4))).triu(1).sum(), p)
+            out.append({"pos": p, "atomic_numbers": z, "energy": e.reshape(1), "forces": f})
+        return [structure_to_graph(s, 1.0) for s in out]
+
+    train, test = structs(6), structs(3)
+    perms = [[0, 1, 2, 3], [0, 2, 1, 3]] if symmetric else None
+    mine = SGDML([8, 1, 1, 6], sigma=2.0, use_symmetries=False)
+    ref = refm.SGDML([8, 1, 1, 6], sigma=2.0, use_symmetries=False)
+    mine.fit(train, energy_constraint=energy_constraint, perms=perms)
+    ref.fit(train, energy_constraint=energy_constraint, perms=perms, solver="analytic")
+    b = collate(test)
+    compare(mine, ref, b, rtol=1e-7, atol=1e-8)
