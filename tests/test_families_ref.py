@@ -200,3 +200,20 @@ def test_sgdml_fit_and_predict(energy_constraint, symmetric):
     ref.fit(train, energy_constraint=energy_constraint, perms=perms, solver="analytic")
     b = collate(test)
     compare(mine, ref, b, rtol=1e-7, atol=1e-8)
+
+
+@pytest.mark.parametrize("coulomb,channels,periodic", [("simple", 1, False), ("simple", 2, False), ("dsf", 1, True),
+                                                      ("ewald", 1, True), (None, 1, False)])
+def test_aimnet2(coulomb, channels, periodic):
+    from xnn_b200.models.aimnet2 import AIMNet2
+    sp = [1, 6, 7, 8] if not periodic else [8]
+    kw = dict(species=sp, cutoff=4.0, n_features=4, n_rbf=6, hidden=[[12, 10], [12, 10], [12, 10, 8]],
+              n_vector_combinations=3, aim_size=8, readout_hidden=(6,), charge_channels=channels, coulomb=coulomb,
+              lr_cutoff=6.0, atomic_energies=[-0.5 * z for z in sp])
+    mine, ref = _pair("xnn.gnn.models.aimnet2", "AIMNet2", AIMNet2, **kw)
+    b = batch(periodic, cutoff=mine.cutoff, species=sp if not periodic else None)
+    tq = torch.tensor([1.0, 0.0] + ([] if periodic else [-1.0]))
+    extra = {"total_charge": tq}
+    if channels == 2:
+        extra["spin_multiplicity"] = torch.tensor([2.0, 1.0, 2.0])
+    compare(mine, ref, b, periodic, rtol=1e-9, atol=1e-9, keys=("charges",), **extra)
