@@ -217,3 +217,13 @@ def test_aimnet2(coulomb, channels, periodic):
     if channels == 2:
         extra["spin_multiplicity"] = torch.tensor([2.0, 1.0, 2.0])
     compare(mine, ref, b, periodic, rtol=1e-9, atol=1e-9, keys=("charges",), **extra)
+
+
+@pytest.mark.parametrize("max_nu,passes,receiver", [(2, 1, False), (3, 2, True), (4, 1, False)])
+def test_cace(max_nu, passes, receiver):
+    from xnn_b200.models.cace import CACE
+    mine, ref = _pair("xnn.gnn.models.cace", "CACE", CACE, species=[1, 6, 7, 8], cutoff=4.5, n_atom_basis=2,
+                      n_rbf=4, max_l=3, max_nu=max_nu, num_message_passing=passes, embed_receiver_nodes=receiver,
+                      readout_hidden=[8], atomic_energies=[-0.5, -1.0, -1.5, -2.0])
+    compare(mine, ref, batch(False, cutoff=4.5, species=[1, 6, 7, 8]), rtol=1e-9, atol=1e-9)
+    compare(mine, ref, batch(True, cutoff=4.5, species=[8]), True, rtol=1e-9, atol=1e-9)
