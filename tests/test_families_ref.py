@@ -227,3 +227,16 @@ def test_cace(max_nu, passes, receiver):
                       readout_hidden=[8], atomic_energies=[-0.5, -1.0, -1.5, -2.0])
     compare(mine, ref, batch(False, cutoff=4.5, species=[1, 6, 7, 8]), rtol=1e-9, atol=1e-9)
     compare(mine, ref, batch(True, cutoff=4.5, species=[8]), True, rtol=1e-9, atol=1e-9)
+
+
+@pytest.mark.parametrize("cls_name,gate,ref_basis", [("DimeNet", "kj", False), ("DimeNet", "ji", True),
+                                                     ("DimeNetPP", "kj", False), ("DimeNetPP", "ji", False)])
+def test_dimenet(cls_name, gate, ref_basis):
+    from xnn_b200.models import dimenet as M
+    kw = dict(n_features=8, n_interactions=2, n_rbf=4, n_spherical=3, cutoff=4.5, radial_gate=gate,
+              reference_basis=ref_basis, n_output_layers=1, species=[1, 6, 7, 8], atomic_energies=[-1.0, -2, -3, -4])
+    kw.update(dict(n_bilinear=3) if cls_name == "DimeNet" else dict(n_triplet_features=6, n_basis_features=3,
+                                                                     n_output_features=10))
+    mine, ref = _pair("xnn.gnn.models.dimenet", cls_name, getattr(M, cls_name), **kw)
+    compare(mine, ref, batch(False, cutoff=4.5), rtol=1e-9, atol=1e-9)
+    compare(mine, ref, batch(True, cutoff=4.5), True, rtol=1e-9, atol=1e-9)
