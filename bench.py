@@ -30,9 +30,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 
 
 # name fragments of the kernels compiled into xnn_b200/_C.so
-OUR_KERNELS = ("conv_gather", "conv_edge", "conv_scatter", "symcon_", "edge_geom_", "p2p_allreduce",
-               "gemm_pack_kernel", "gemm_rows_kernel", "gemm_reduce_kernel", "sum_partials_kernel",
-               "radial_basis_kernel", "radial_act_kernel", "radial_dact_kernel", "nb_count", "nb_write")
+OUR_KERNELS = ("conv_gather", "conv_edge", "conv_scatter", "symcon_", "edge_geom_", "p2p_allreduce", "halo_exchange",
+               "gemm_pack_kernel", "gemm_rows_kernel", "gemm_reduce_kernel", "gemm_ws_kernel", "gemm_ws_pack_kernel",
+               "gemm_reduce_ws_kernel", "sum_partials_kernel", "radial_basis_kernel", "radial_act_kernel",
+               "radial_dact_kernel", "nb_count", "nb_write", "mp_real_kernel", "pme_spread_kernel",
+               "pme_gather_kernel")
 
 
 def parse():

@@ -117,6 +117,34 @@ def build_ops(case) -> Dict[str, tuple]:
     pos, cell, pbc, rc = case["pos"], case["cell"], case["pbc"], case["cutoff"]
     out["neighbor_list"] = (lambda: build_neighbor_list(pos, rc, cell, pbc, engine="native"),
                             8 * 3 * N + E * (2 * 8 + 3 * 8))
+    out.update(pme_ops(N))
+    return out
+
+
+def pme_ops(n_atoms: int) -> Dict[str, tuple]:
+    """The multipole PME kernels on a water box of ``n_atoms``: order-5 spreading of charges,
+    dipoles and quadrupoles onto a float32 128^3 mesh, the gather of fields and forces, and the
+    float64 real-space pair kernel (7 A, Thole-damped)."""
+    from ..ffnn import multipoles as MP
+    from ..ffnn.water import multipole_water
+    w = multipole_water(n_atoms, seed=0, device=torch.device("cuda"))
+    mesh, p = [128, 128, 128], 5
+    K = torch.tensor(mesh, dtype=torch.float64, device="cuda")
+    G = (torch.linalg.inv(w["cell"].double()) * K[None, :]).contiguous()
+    args = (w["pos"].contiguous(), G, mesh, p, 0, mesh[2], w["q"].contiguous(), w["d"].contiguous(),
+            w["Q"].reshape(-1, 9).contiguous())
+    ops = _ext.ops()
+    phi = torch.randn(mesh, dtype=torch.float32, device="cuda")
+    n, m = w["pos"].shape[0], 128 ** 3
+    site = 8 * (3 + 1 + 3 + 9)
+    out = {"pme_spread": (lambda: ops.pme_spread(*args), n * site + 4 * m),
+           "pme_gather": (lambda: ops.pme_gather(*args, phi, True, True), n * site + 4 * m + 2 * 3 * 8 * n)}
+    i, j, shift, excl = MP.multipole_pairs(w["pos"], w["cell"], 7.0, w["molecule"])
+    pol = w["pol"].contiguous()
+    q, d, Q = w["q"].contiguous(), w["d"].contiguous(), w["Q"].reshape(-1, 9).contiguous()
+    out["mp_real"] = (lambda: ops.mp_real(w["pos"], w["cell"], q, d, Q, pol, i, j, shift, excl, 0.4, 0.39, True,
+                                          True),
+                      i.shape[0] * (8 + 8 + 24 + 1) + n * site)
     return out
 
 
