@@ -240,3 +240,27 @@ def test_dimenet(cls_name, gate, ref_basis):
     mine, ref = _pair("xnn.gnn.models.dimenet", cls_name, getattr(M, cls_name), **kw)
     compare(mine, ref, batch(False, cutoff=4.5), rtol=1e-9, atol=1e-9)
     compare(mine, ref, batch(True, cutoff=4.5), True, rtol=1e-9, atol=1e-9)
+
+
+@pytest.mark.parametrize("quadruplets,direct", [(False, False), (True, False), (False, True)])
+def test_gemnet(quadruplets, direct):
+    from xnn_b200.models.gemnet import GemNet
+    kw = dict(n_features=6, n_edge_features=8, n_interactions=1, n_rbf=3, n_spherical=3, cutoff=3.5, int_cutoff=4.0,
+              n_triplet_features=4, n_quadruplet_features=4, n_rbf_features=3, n_cbf_features=3, n_sbf_features=4,
+              n_bilinear_triplet=5, n_bilinear_quadruplet=4, quadruplets=quadruplets, direct_forces=direct,
+              forces_coupled=direct, species=[1, 6, 7, 8], atomic_energies=[-1.0, -2, -3, -4])
+    mine, ref = _pair("xnn.gnn.models.gemnet", "GemNet", GemNet, **kw)
+    with torch.no_grad():
+        for fac in ref.scale_factors().values():
+            fac.scale_factor.uniform_(0.5, 1.5)
+    load_same_weights(mine, ref)
+    ref.set_use_fast(False)
+    b = batch(False, cutoff=mine.cutoff)
+    compare(mine, ref, b, rtol=1e-9, atol=1e-9)
+    if not direct:
+        compare(mine, ref, batch(True, cutoff=mine.cutoff), True, rtol=1e-9, atol=1e-9)
+    from ref_oracle import ref_graph
+    fitted, fitted_ref = mine.fit_scaling_factors([b.clone()]), ref.fit_scaling_factors([ref_graph(b)])
+    assert fitted.keys() == fitted_ref.keys()
+    for k in fitted:
+        assert abs(fitted[k] - fitted_ref[k]) < 1e-9 * abs(fitted_ref[k]), k
