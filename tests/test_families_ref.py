@@ -264,3 +264,16 @@ def test_gemnet(quadruplets, direct):
     assert fitted.keys() == fitted_ref.keys()
     for k in fitted:
         assert abs(fitted[k] - fitted_ref[k]) < 1e-9 * abs(fitted_ref[k]), k
+
+
+@pytest.mark.parametrize("influence,vector_cutoff,nb", [("both", True, True), ("keys", False, False),
+                                                        ("values", True, True), ("none", False, True)])
+def test_et(influence, vector_cutoff, nb):
+    from xnn_b200.models.et import EquivariantTransformer
+    mine, ref = _pair("xnn.trfnn.models.et", "EquivariantTransformer", EquivariantTransformer, n_features=8,
+                      n_interactions=2, n_rbf=6, cutoff=4.5, num_heads=2, distance_influence=influence,
+                      vector_cutoff=vector_cutoff, neighbor_embedding=nb, species=[1, 6, 7, 8],
+                      atomic_energies=[-1.0, -2, -3, -4])
+    ref.set_use_fast(False)
+    compare(mine, ref, batch(False, cutoff=4.5), rtol=1e-9, atol=1e-9)
+    compare(mine, ref, batch(True, cutoff=4.5), True, rtol=1e-9, atol=1e-9)

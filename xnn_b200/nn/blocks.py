@@ -103,3 +103,27 @@ class GatedMLP(nn.Module):
 
     def forward(self, x: Tensor) -> Tensor:
         return self.mlp(x) * torch.sigmoid(self.gate(x))
+
+
+class GatedEquivariantBlock(nn.Module):
+    """Scalars ``s (N, F_s)`` and vectors ``v (N, 3, F_v)`` -> gated outputs: the norms of a linear map
+    of the vectors join the scalars in an MLP whose outputs are new scalars and gates of a second
+    linear map of the vectors (PaiNN / TorchMD-Net readouts)."""
+
+    def __init__(self, n_in_s: int, n_in_v: int, n_out_s: int, n_out_v: int, n_hidden=None,
+                 scalar_activation: bool = True, n_norm=None, activation="silu"):
+        super().__init__()
+        n_hidden = n_in_s if n_hidden is None else int(n_hidden)
+        n_norm = n_out_v if n_norm is None else int(n_norm)
+        self.n_out_s, self.n_out_v, self.n_norm = n_out_s, n_out_v, n_norm
+        self.lin_v = nn.Linear(n_in_v, n_norm + n_out_v, bias=False)
+        self.net = nn.Sequential(nn.Linear(n_in_s + n_norm, n_hidden), make_activation(activation),
+                                 nn.Linear(n_hidden, n_out_s + n_out_v))
+        self.scalar_activation = scalar_activation
+        self.act = make_activation(activation)
+
+    def forward(self, s, v):
+        v1, v2 = torch.split(self.lin_v(v), [self.n_norm, self.n_out_v], dim=-1)
+        x = self.net(torch.cat([s, torch.linalg.norm(v1, dim=1)], -1))
+        s_out, gate = x[:, :self.n_out_s], x[:, self.n_out_s:]
+        return (self.act(s_out) if self.scalar_activation else s_out), gate.unsqueeze(1) * v2
