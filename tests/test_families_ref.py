@@ -158,9 +158,11 @@ def test_physnet(lr_cutoff, dispersion):
             if "k2f" in name or "output_blocks" in name:
                 p.uniform_(-0.3, 0.3)
     load_same_weights(mine, ref)
-    tol = 1e-6 if dispersion else 1e-10   # float32-rounded D3 radii in the reference's legacy tables
+    if dispersion:   # the same radii tables (the reference keeps float32 roundings of them)
+        for name in ("_d3_rcov", "_d3_r2r4", "_d3_c6ab"):
+            getattr(mine, name).copy_(getattr(ref, name))
     b = batch(False, cutoff=lr_cutoff or 5.0)
-    compare(mine, ref, b, rtol=tol, atol=tol, keys=("charges", "nh_loss"),
+    compare(mine, ref, b, rtol=1e-10, atol=1e-10, keys=("charges", "nh_loss"),
             total_charge=torch.tensor([1.0, 0.0, -2.0]))
 
 
@@ -277,3 +279,16 @@ def test_et(influence, vector_cutoff, nb):
     ref.set_use_fast(False)
     compare(mine, ref, batch(False, cutoff=4.5), rtol=1e-9, atol=1e-9)
     compare(mine, ref, batch(True, cutoff=4.5), True, rtol=1e-9, atol=1e-9)
+
+
+@pytest.mark.parametrize("elec,disp,layers", [(True, False, 3), (False, True, 2), (True, True, 4)])
+def test_bamboo(elec, disp, layers):
+    from xnn_b200.models.bamboo import BAMBOO
+    mine, ref = _pair("xnn.hybnn.models.bamboo", "BAMBOO", BAMBOO, dim=8, num_rbf=6, cutoff=5.0, n_layers=layers,
+                      num_heads=2, use_electrostatics=elec, use_dispersion=disp, disp_cutoff=5.0)
+    ref.set_use_fast(False)
+    if disp:   # the same radii tables (the reference keeps float32 roundings of them)
+        for name in ("_rcov", "_r2r4", "_c6ab"):
+            getattr(mine.dispersion, name).copy_(getattr(ref.dispersion, name))
+    compare(mine, ref, batch(False, cutoff=5.0), rtol=1e-9, atol=1e-9, keys=("charges",),
+            total_charge=torch.tensor([0.0, 1.0, -1.0]))

@@ -76,22 +76,32 @@ def _taper(r: Tensor, cutoff: float) -> Tensor:
     return torch.where(u >= 1.0, torch.ones_like(u), torch.where(u <= 0.0, torch.zeros_like(u), ramp))
 
 
+def coordination(zi: Tensor, zj: Tensor, r: Tensor, i: Tensor, n: int, cutoff: Optional[float], rcov: Tensor) -> Tensor:
+    """``CN_i = sum_j 1 / (1 + exp(-16 (R_ij / r - 1)))`` (tapered over the last bohr with a cutoff)."""
+    count = 1.0 / (1.0 + torch.exp(-_K1 * ((rcov[zi] + rcov[zj]).to(r.dtype) / r - 1.0)))
+    if cutoff is not None:
+        count = count * _taper(r, cutoff)
+    return r.new_zeros(n).index_add(0, i, count)
+
+
+def pair_c6(zi: Tensor, zj: Tensor, cni: Tensor, cnj: Tensor, c6ab: Tensor) -> Tensor:
+    """Gaussian-weighted (``exp(-4 dCN^2)``) average of the reference ``C6`` of each pair."""
+    refs = c6ab[zi, zj].to(cni.dtype)
+    c6r = refs[..., 0]
+    d2 = (refs[..., 1] - cni[:, None, None]) ** 2 + (refs[..., 2] - cnj[:, None, None]) ** 2
+    w = torch.where(c6r > 0.0, torch.exp(_K3 * d2), torch.zeros_like(d2))
+    norm = w.sum((-2, -1))
+    return torch.where(norm > 0.0, (w * c6r).sum((-2, -1)) / norm,
+                       torch.full_like(norm, -1.0e99 if norm.dtype == torch.float64 else float("-inf")))
+
+
 def pair_dispersion(Z: Tensor, r: Tensor, i: Tensor, j: Tensor, cutoff: Optional[float], s6, s8, a1, a2,
                     c6ab: Tensor, rcov: Tensor, r2r4: Tensor) -> Tensor:
     """Per-atom D3(BJ) energies (hartree) for distances ``r`` in bohr on directed edges ``i <- j``."""
     n = Z.shape[0]
     zi, zj = Z[i], Z[j]
-    count = 1.0 / (1.0 + torch.exp(-_K1 * ((rcov[zi] + rcov[zj]).to(r.dtype) / r - 1.0)))
-    if cutoff is not None:
-        count = count * _taper(r, cutoff)
-    cn = r.new_zeros(n).index_add(0, i, count)
-    refs = c6ab[zi, zj].to(r.dtype)
-    c6r = refs[..., 0]
-    d2 = (refs[..., 1] - cn[i][:, None, None]) ** 2 + (refs[..., 2] - cn[j][:, None, None]) ** 2
-    w = torch.where(c6r > 0.0, torch.exp(_K3 * d2), torch.zeros_like(d2))
-    norm = w.sum((-2, -1))
-    c6 = torch.where(norm > 0.0, (w * c6r).sum((-2, -1)) / norm,
-                     torch.full_like(norm, -1.0e99 if norm.dtype == torch.float64 else float("-inf")))
+    cn = coordination(zi, zj, r, i, n, cutoff, rcov)
+    c6 = pair_c6(zi, zj, cn[i], cn[j], c6ab)
     c8 = 3 * c6 * r2r4[zi].to(c6.dtype) * r2r4[zj].to(c6.dtype)
     r0 = a1 * torch.sqrt(c8 / c6) + a2
     r0_6 = r0 ** 6

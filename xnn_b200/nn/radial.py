@@ -123,3 +123,34 @@ def make_radial_basis(name: str, n_rbf: int, cutoff: float, trainable: bool = Fa
     if name == "smooth_bessel":
         return SmoothBesselRBF(n_rbf, cutoff)
     raise ValueError(f"unknown radial basis {name!r}; options: {RADIAL_BASES}")
+
+
+class ExponentialBernsteinRBF(nn.Module):
+    """Bernstein polynomials of ``x = exp(-gamma r)``: ``C(n-1, k) x^k (1 - x)^(n-1-k)`` (SpookyNet),
+    evaluated in log space; ``gamma = softplus(gamma_raw)`` (trainable by default)."""
+
+    def __init__(self, n_rbf: int = 16, gamma: float = 0.5 / 0.5291772109044924, trainable: bool = True,
+                 exp_weighting: bool = False):
+        super().__init__()
+        self.n_rbf, self.exp_weighting = int(n_rbf), bool(exp_weighting)
+        k = torch.arange(self.n_rbf, dtype=torch.float64)
+        n = float(self.n_rbf - 1)
+        log_binom = math.lgamma(n + 1.0) - torch.lgamma(k + 1.0) - torch.lgamma(n - k + 1.0)
+        dt = torch.get_default_dtype()
+        self.register_buffer("log_binom", log_binom.to(dt), persistent=False)
+        self.register_buffer("power_x", k.to(dt), persistent=False)
+        self.register_buffer("power_1mx", (n - k).to(dt), persistent=False)
+        raw = torch.tensor(float(gamma) + math.log(-math.expm1(-float(gamma))), dtype=dt)   # softplus^-1
+        if trainable:
+            self.gamma_raw = nn.Parameter(raw)
+        else:
+            self.register_buffer("gamma_raw", raw)
+
+    @property
+    def gamma(self) -> Tensor:
+        return nn.functional.softplus(self.gamma_raw)
+
+    def forward(self, r: Tensor) -> Tensor:
+        log_x = -nn.functional.softplus(self.gamma_raw) * r.unsqueeze(-1)
+        rbf = torch.exp(self.log_binom + self.power_x * log_x + self.power_1mx * torch.log(-torch.expm1(log_x)))
+        return rbf * torch.exp(log_x) if self.exp_weighting else rbf
