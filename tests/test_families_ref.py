@@ -292,3 +292,16 @@ def test_bamboo(elec, disp, layers):
             getattr(mine.dispersion, name).copy_(getattr(ref.dispersion, name))
     compare(mine, ref, batch(False, cutoff=5.0), rtol=1e-9, atol=1e-9, keys=("charges",),
             total_charge=torch.tensor([0.0, 1.0, -1.0]))
+
+
+@pytest.mark.parametrize("norm,blocks", [(None, 3), ("batch", 2)])
+def test_cnn3d(norm, blocks):
+    from xnn_b200.models.cnn3d import CNN3D
+    mine, ref = _pair("xnn.cnn.models.cnn3d", "CNN3D", CNN3D, species=[1, 6, 7, 8], cutoff=3.5, grid_size=7,
+                      n_features=8, n_blocks=blocks, kernel_size=3, normalization=norm,
+                      atomic_energies=[-1.0, -2, -3, -4])
+    with torch.no_grad():
+        ref.readout[-1].weight.uniform_(-0.5, 0.5)
+    load_same_weights(mine, ref)
+    ref.set_use_fast(False)
+    compare(mine, ref, batch(False, cutoff=3.5, species=[1, 6, 7, 8]), rtol=1e-9, atol=1e-9)
