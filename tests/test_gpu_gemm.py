@@ -66,3 +66,46 @@ def test_matmul_autograd_two_orders(M, K, N):
     h, = torch.autograd.grad((gX * U).sum(), W)
     hd, = torch.autograd.grad((gXd * U.double()).sum(), Wd)
     torch.testing.assert_close(h.double(), hd, rtol=1e-5, atol=1e-3)
+
+
+@pytest.mark.parametrize("M,K,N", [(5000, 8, 64), (70001, 64, 64), (333, 64, 128)])
+def test_fused_silu_epilogue(M, K, N):
+    X = torch.randn(M, K, device="cuda")
+    W = torch.randn(K, N, device="cuda") / K ** 0.5
+    Y = gemm.mm_act(X, W, 1, 1.7)
+    ref = 1.7 * torch.nn.functional.silu(X.double() @ W.double())
+    assert ((Y.double() - ref).abs().max() / ref.abs().max()) < 1e-5
+
+
+@pytest.mark.parametrize("M,K", [(5000, 8), (70001, 64), (257, 64)])
+def test_fused_tangent_pair_epilogue(M, K):
+    """``[c silu(a) | c silu'(a) a']`` from the block-diagonal product of ``[h | h']``."""
+    H = 64
+    X = torch.randn(M, 2 * K, device="cuda")
+    W = torch.randn(K, H, device="cuda") / K ** 0.5
+    Y = gemm.mm_act(X, torch.block_diag(W, W), 2, 1.3)
+    a = X[:, :K].double() @ W.double()
+    ad = X[:, K:].double() @ W.double()
+    s = torch.sigmoid(a)
+    ref = torch.cat([1.3 * a * s, 1.3 * s * (1 + a * (1 - s)) * ad], 1)
+    assert ((Y.double() - ref).abs().max() / ref.abs().max()) < 1e-5
+
+
+def test_fused_radial_network_matches_stages():
+    """The MD radial network (value and tangent, activations fused) against the staged one."""
+    from xnn_b200.models.mace import MACE
+    from xnn_b200.ops import lean_conv
+    from xnn_b200.ops.radial import RadialSpec, _eff, _forward
+    torch.manual_seed(0)
+    m = MACE(species=[1, 8], cutoff=4.5, num_channels=32, n_rbf=8, num_interactions=2, max_ell=3,
+             correlation=3, avg_num_neighbors=30.0).cuda()
+    blk, ef = m.interactions[0], m.edge_feat
+    net = blk.conv_tp_weights
+    spec = RadialSpec(net, None, ef.rbf.freqs, ef.rbf.norm, ef.cutoff, ef.envelope.p)
+    We = _eff([layer.weight for layer in net], spec)
+    r = 0.8 + 3.6 * torch.rand(50000, device="cuda")
+    R0, Rd0 = _forward(r, We, spec)[:2]
+    R1, Rd1 = lean_conv._primal_tangent(r, We, spec)
+    R2 = lean_conv._primal(r, We, spec)
+    for a, b in ((R1, R0), (Rd1, Rd0), (R2, R0)):
+        assert ((a - b).abs().max() / b.abs().max()) < 1e-5

@@ -107,11 +107,13 @@ void register_comm(pybind11::module& m) {
 // ---- tensor-core GEMM ---------------------------------------------------------------------
 cudaError_t gemm_tf32x3(int M, int N, int K, const float* X, int ldx, const float* W, int64_t sk, int64_t sn,
                         float* Bpack, float* Y, int ldy, const float* col_scale, int* status, long long spin_limit,
-                        cudaStream_t s);
+                        int act_mode, float act_c, cudaStream_t s);
 size_t gemm_rows_pack_floats(int K, int N);
 
+// act_mode 1 / 2: the epilogue activations of the warp-specialized kernel (see gemm_tc_ws.cu);
+// an undefined tensor (None) when that kernel cannot take the shape
 torch::Tensor gemm_tf32x3_op(torch::Tensor X, torch::Tensor W, c10::optional<torch::Tensor> col_scale,
-                             torch::Tensor status, int64_t spin_limit) {
+                             torch::Tensor status, int64_t spin_limit, int64_t act_mode, double act_c) {
   TORCH_CHECK(X.is_cuda() && W.is_cuda() && X.scalar_type() == torch::kFloat32 &&
               W.scalar_type() == torch::kFloat32, "gemm_tf32x3: float32 CUDA operands");
   TORCH_CHECK(X.dim() == 2 && W.dim() == 2 && X.size(1) == W.size(0), "gemm_tf32x3: shapes");
@@ -131,12 +133,20 @@ torch::Tensor gemm_tf32x3_op(torch::Tensor X, torch::Tensor W, c10::optional<tor
   auto st = at::cuda::getCurrentCUDAStream();
   cudaError_t e = gemm_tf32x3((int)M, (int)N, (int)K, X.data_ptr<float>(), (int)X.stride(0), W.data_ptr<float>(),
                               W.stride(0), W.stride(1), Bpack.data_ptr<float>(), Y.data_ptr<float>(), (int)N, cs,
-                              status.data_ptr<int>(), (long long)spin_limit, st);
+                              status.data_ptr<int>(), (long long)spin_limit, (int)act_mode, (float)act_c, st);
+  if (e == cudaErrorNotSupported && act_mode != 0) {
+    cudaGetLastError();
+    return torch::Tensor();
+  }
   TORCH_CHECK(e == cudaSuccess, "gemm_tf32x3 failed: ", cudaGetErrorString(e));
   return Y;
 }
 
-void register_gemm(pybind11::module& m) { m.def("gemm_tf32x3", &gemm_tf32x3_op); }
+void register_gemm(pybind11::module& m) {
+  namespace py = pybind11;
+  m.def("gemm_tf32x3", &gemm_tf32x3_op, py::arg("X"), py::arg("W"), py::arg("col_scale"), py::arg("status"),
+        py::arg("spin_limit"), py::arg("act_mode") = 0, py::arg("act_c") = 1.0);
+}
 
 // ---- reduction GEMM and the radial network's elementwise stages -------------------------------
 cudaError_t gemm_reduce_tf32x3(int M, int K1, int N, const float* X, int ldx, const float* D, int ldd,

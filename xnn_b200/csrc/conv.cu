@@ -20,6 +20,8 @@
 // receiver, senders through a permutation grouped by sender. Every sum accumulates in
 // registers and meets the other warps' in shared memory in a fixed order: deterministic and
 // atomic-free (except gY when the channels are split over several blocks, C > 128).
+#include <cstdlib>
+
 #include "common.cuh"
 
 template <typename T>
@@ -286,6 +288,16 @@ inline int cpl_for(int C) {
   const int c = (C + 31) / 32;
   return c > 4 ? 4 : (c < 1 ? 1 : c);
 }
+// channels per lane of the gather: XNN_B200_GATHER_CPL (1-4) overrides the default (a tuning knob;
+// fewer channels per lane means fewer registers, more resident warps and more column blocks)
+inline int gather_cpl(int C) {
+  static int forced = -1;
+  if (forced < 0) {
+    const char* v = getenv("XNN_B200_GATHER_CPL");
+    forced = (v != nullptr && v[0] >= '1' && v[0] <= '4') ? v[0] - '0' : 0;
+  }
+  return forced > 0 ? forced : cpl_for(C);
+}
 }  // namespace
 
 #define XNN_P_CPL_SWITCH(P, CPL, ...)                                        \
@@ -322,7 +334,7 @@ cudaError_t conv_gather(int N, int C, int P, const int64_t* dst_ptr, const int* 
     t.R[k] = k < nterms ? R[k] : nullptr;
     t.Y[k] = k < nterms ? Y[k] : nullptr;
   }
-  const int cpl = cpl_for(C);
+  const int cpl = gather_cpl(C);
   dim3 grid(N, (C + 32 * cpl - 1) / (32 * cpl));
   const size_t smem = (size_t)(kWPA - 1) * P * P * 32 * cpl * sizeof(T);
   XNN_P_CPL_SWITCH(P, cpl, conv_gather_kernel<T, PP, QQ, kWPA><<<grid, 32 * kWPA, smem, stream>>>(N, C, dst_ptr, src, perm, t, A));

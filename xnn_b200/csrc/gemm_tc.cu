@@ -229,7 +229,7 @@ static bool gemm_ws_enabled() {
 }
 cudaError_t gemm_tf32x3_ws(int M, int N, int K, const float* X, int ldx, const float* W, int64_t sk, int64_t sn,
                            float* Bpack, float* Y, int ldy, const float* col_scale, int* status, long long spin_limit,
-                           cudaStream_t s);
+                           int act_mode, float act_c, cudaStream_t s);
 
 // workspace for the packed W of either kernel
 size_t gemm_rows_pack_floats(int K, int N) {
@@ -240,7 +240,7 @@ size_t gemm_rows_pack_floats(int K, int N) {
 
 cudaError_t gemm_tf32x3(int M, int N, int K, const float* X, int ldx, const float* W, int64_t sk, int64_t sn,
                         float* Bpack, float* Y, int ldy, const float* col_scale, int* status, long long spin_limit,
-                        cudaStream_t s) {
+                        int act_mode, float act_c, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
   if (N < 16 || N > 512 || N % 16 != 0 || K < 1 || ldx % 4 != 0) return cudaErrorInvalidValue;
   const int n_split = (N + 255) / 256;
@@ -250,10 +250,13 @@ cudaError_t gemm_tf32x3(int M, int N, int K, const float* X, int ldx, const floa
     return cudaErrorInvalidValue;
   // the warp-specialized TMA kernel first; the staged kernel for what it does not cover
   if (gemm_ws_enabled()) {
-    cudaError_t e = gemm_tf32x3_ws(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, s);
+    cudaError_t e = gemm_tf32x3_ws(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit,
+                                   act_mode, act_c, s);
     if (e != cudaErrorNotSupported) return e;
     cudaGetLastError();
   }
+  // the fused activations exist in the warp-specialized kernel only (the caller falls back)
+  if (act_mode != 0) return cudaErrorNotSupported;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -12,9 +12,14 @@
 //               N = NS <= 256) into one of two TMEM accumulators, commits to the stage's `empty`
 //               barrier and, after the unit's last chunk, to the accumulator's `full` barrier;
 //   warps 4-11  epilogue: tcgen05.ld of the accumulator (warp w owns TMEM lanes 32 (w % 4) ..; the
-//               two warps of a lane quarter split the columns), column scale, swizzled staging in
-//               shared memory and 2D TMA stores of 32 x 16 tiles; arrive on the accumulator's
-//               `empty` barrier so the next unit can reuse it.
+//               two warps of a lane quarter split the columns), column scale, the optional
+//               activation, swizzled staging in shared memory and 2D TMA stores of 32 x 16 tiles;
+//               arrive on the accumulator's `empty` barrier so the next unit can reuse it.
+// Activations of the epilogue (a radial network layer fused with its nonlinearity):
+//   act_mode 1: y = c silu(a);
+//   act_mode 2: the columns are [a | a'] (a value and its tangent, H = N / 2 each, N <= 256) and
+//               the outputs [c silu(a) | c silu'(a) a'] -- the forward-mode layer; each epilogue
+//               warp takes matching 16-column chunks of both halves of its rows.
 // A unit of work is (row tile, column half): N > 256 is split into two halves of NS = N / 2
 // columns so that two accumulators (double buffering) fit in the 512 TMEM columns. When the
 // packed W of one column half fits in shared memory next to the stages, each CTA keeps one half
@@ -139,7 +144,7 @@ template <int KC>
 __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
     const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapY, int M, int N, int K,
     int NS, const float* __restrict__ Bpack, const float* __restrict__ col_scale, int* status,
-    long long spin_limit, int tmem_cols, uint32_t acc_stride, int resident) {
+    long long spin_limit, int tmem_cols, uint32_t acc_stride, int resident, int act_mode, float act_c) {
   using namespace tc;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // align the dynamic buffer to 1024 bytes (swizzle atoms)
@@ -298,41 +303,67 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
     // ---------------------------------------------------------------- epilogue (warps 4..11)
     const int q = warp & 3;            // TMEM lane quarter (tcgen05.ld reaches lanes 32 (warp % 4) ..)
     const int part = (warp - 4) >> 2;  // which half of the unit's columns this warp drains
-    const int cw = (NS / 2) % 16 == 0 ? NS / 2 : (part == 0 ? NS : 0);
-    const int cbeg = (NS / 2) % 16 == 0 ? part * (NS / 2) : 0;
+    // pair mode: the part takes half of the value columns and the matching tangent columns
+    const int span = act_mode == 2 ? NS / 2 : NS;
+    const int cw = (span / 2) % 16 == 0 ? span / 2 : (part == 0 ? span : 0);
+    const int cbeg = (span / 2) % 16 == 0 ? part * (span / 2) : 0;
     unsigned char* stage_buf = smem + L.staging + (uint32_t)(warp - 4) * 2 * 2048;
     long long uidx = 0;
     int nst = 0;                       // stores issued by this warp
     int tile, h;
+    // stage 16 values of this lane's row and store the 32 x 16 tile at column `col`
+    auto emit = [&](const float* v, int col, int row0) {
+      unsigned char* sb = stage_buf + (uint32_t)(nst & 1) * 2048;
+      if (nst >= 2) {
+        if (lane == 0) bulk_wait_read1();       // the store that last read this buffer is done
+        __syncwarp();
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t lin = (uint32_t)lane * 64u + (uint32_t)j * 16u;
+        const uint32_t phys = lin ^ (((lin >> 7) & 3u) << 4);
+        *reinterpret_cast<float4*>(sb + phys) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(&mapY, sb, col, row0);
+        bulk_commit();
+      }
+      ++nst;
+    };
     for (; unit_at(uidx, resident, n_sub, tiles, tile, h); ++uidx) {
       const int b = (int)(uidx & 1);
       if (!wait_or_abort(accf + b, (uint32_t)((uidx >> 1) & 1), spin_limit, abort_flag, status)) break;
       tc_fence_after();
       const uint32_t lane_base = tmem + (uint32_t)b * acc_stride + ((uint32_t)(q * 32) << 16);
-      for (int c0 = cbeg; c0 < cbeg + cw; c0 += 16, ++nst) {
+      const int row0 = tile * 128 + q * 32;
+      for (int c0 = cbeg; c0 < cbeg + cw; c0 += 16) {
         float v[16];
         tmem_ld16(lane_base + (uint32_t)c0, v);
         if (col_scale) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] *= __ldg(col_scale + h * NS + c0 + j);
         }
-        unsigned char* sb = stage_buf + (uint32_t)(nst & 1) * 2048;
-        if (nst >= 2) {
-          if (lane == 0) bulk_wait_read1();       // the store that last read this buffer is done
-          __syncwarp();
-        }
+        if (act_mode == 1) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t lin = (uint32_t)lane * 64u + (uint32_t)j * 16u;
-          const uint32_t phys = lin ^ (((lin >> 7) & 3u) << 4);
-          *reinterpret_cast<float4*>(sb + phys) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          for (int j = 0; j < 16; ++j) v[j] = act_c * v[j] / (1.0f + expf(-v[j]));
+        } else if (act_mode == 2) {
+          float t[16];
+          tmem_ld16(lane_base + (uint32_t)(span + c0), t);
+          if (col_scale) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) t[j] *= __ldg(col_scale + h * NS + span + c0 + j);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float sg = 1.0f / (1.0f + expf(-v[j]));
+            t[j] = act_c * sg * (1.0f + v[j] * (1.0f - sg)) * t[j];
+            v[j] = act_c * v[j] * sg;
+          }
+          emit(t, h * NS + span + c0, row0);
         }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&mapY, sb, h * NS + c0, tile * 128 + q * 32);
-          bulk_commit();
-        }
+        emit(v, h * NS + c0, row0);
       }
       tc_fence_before();
       mbar_arrive(acce + b);
@@ -376,7 +407,7 @@ bool encode_2d(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
 template <int KC>
 cudaError_t launch_ws(int M, int N, int K, const float* X, int ldx, const float* W, int64_t sk, int64_t sn,
                       float* Bpack, float* Y, int ldy, const float* col_scale, int* status, long long spin_limit,
-                      int sms, cudaStream_t s) {
+                      int sms, int act_mode, float act_c, cudaStream_t s) {
   const int NS = N <= 256 ? N : N / 2;
   const CUtensorMapSwizzle swA = KC == 32 ? CU_TENSOR_MAP_SWIZZLE_128B
                                           : (KC == 16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
@@ -405,7 +436,7 @@ cudaError_t launch_ws(int M, int N, int K, const float* X, int ldx, const float*
   const int tmem_cols = (int)(2 * acc_stride);
   const int grid = resident ? std::min(tiles, sms / n_sub) * n_sub : std::min(tiles * n_sub, sms);
   gemm_ws_kernel<KC><<<grid, WS_THREADS, smem, s>>>(mapA, mapY, M, N, K, NS, Bpack, col_scale, status, spin_limit,
-                                                    tmem_cols, acc_stride, resident);
+                                                    tmem_cols, acc_stride, resident, act_mode, act_c);
   return cudaGetLastError();
 }
 
@@ -427,11 +458,12 @@ size_t gemm_ws_pack_floats(int K, int N) {
 // cudaErrorNotSupported: shape or layout outside this kernel's scope (the caller falls back)
 cudaError_t gemm_tf32x3_ws(int M, int N, int K, const float* X, int ldx, const float* W, int64_t sk, int64_t sn,
                            float* Bpack, float* Y, int ldy, const float* col_scale, int* status, long long spin_limit,
-                           cudaStream_t s) {
+                           int act_mode, float act_c, cudaStream_t s) {
   if (M == 0) return cudaSuccess;
   if (N < 16 || N > 512 || N % 16 != 0 || K < 1 || K > 512) return cudaErrorNotSupported;
   const int NS = N <= 256 ? N : N / 2;
   if (NS % 16 != 0 || NS * (N / NS) != N) return cudaErrorNotSupported;
+  if (act_mode < 0 || act_mode > 2 || (act_mode == 2 && (N > 256 || N % 32 != 0))) return cudaErrorNotSupported;
   if (ldx % 4 != 0 || ldy % 4 != 0 || (reinterpret_cast<uintptr_t>(X) & 15) || (reinterpret_cast<uintptr_t>(Y) & 15) ||
       (reinterpret_cast<uintptr_t>(Bpack) & 15))
     return cudaErrorNotSupported;
@@ -439,8 +471,11 @@ cudaError_t gemm_tf32x3_ws(int M, int N, int K, const float* X, int ldx, const f
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   switch (gemm_ws_kc(K, N)) {
-    case 8: return launch_ws<8>(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, sms, s);
-    case 16: return launch_ws<16>(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, sms, s);
-    default: return launch_ws<32>(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, sms, s);
+    case 8: return launch_ws<8>(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, sms,
+                                   act_mode, act_c, s);
+    case 16: return launch_ws<16>(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, sms,
+                                   act_mode, act_c, s);
+    default: return launch_ws<32>(M, N, K, X, ldx, W, sk, sn, Bpack, Y, ldy, col_scale, status, spin_limit, sms,
+                                   act_mode, act_c, s);
   }
 }

@@ -61,6 +61,16 @@ def mm_raw(X: Tensor, W: Tensor, col_scale: Optional[Tensor] = None) -> Tensor:
     return Y * col_scale if col_scale is not None else Y
 
 
+def mm_act(X: Tensor, W: Tensor, mode: int, c: float) -> Optional[Tensor]:
+    """``X @ W`` with the activation fused into the tensor-core epilogue: ``mode`` 1 gives
+    ``c silu(XW)``; ``mode`` 2 treats the output columns as ``[a | a']`` and gives
+    ``[c silu(a) | c silu'(a) a']`` (``W`` block-diagonal over the two halves). ``None`` when the
+    kernel does not take the operands (the caller evaluates the stages separately)."""
+    if not supported(X, W):
+        return None
+    return _ext.ops().gemm_tf32x3(X, W, None, _status(X.device), SPIN_LIMIT, int(mode), float(c))
+
+
 def reduce_supported(X: Tensor, D: Tensor) -> bool:
     if not (enabled() and X.is_cuda and X.dtype == torch.float32 and D.dtype == torch.float32):
         return False

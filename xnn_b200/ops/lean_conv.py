@@ -13,7 +13,7 @@ uses the ordinary path. CUDA only.
 """
 from __future__ import annotations
 
-from typing import List, Sequence, Tuple
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 from torch import Tensor
@@ -28,14 +28,33 @@ from .radial import RadialSpec, _eff, _forward
 
 
 def _primal(r: Tensor, We: List[Tensor], spec: RadialSpec) -> Tensor:
-    """``R`` only (no tangent rows): basis, hidden SiLU layers, output layer."""
+    """``R`` only (no tangent rows): basis, hidden SiLU layers (fused into the products'
+    epilogue where the tensor-core kernel takes them), output layer."""
     E = r.shape[0]
     H = _ext.ops().radial_basis(r.contiguous(), spec.freqs.to(r.device), spec.norm, spec.rc, spec.p)[:E]
     for k in range(len(We) - 1):
-        H = F.silu(gemm.mm_raw(H.contiguous(), We[k]))
-        if spec.consts[k] != 1.0:
-            H = H * spec.consts[k]
+        Hk = gemm.mm_act(H.contiguous(), We[k], 1, spec.consts[k])
+        if Hk is None:
+            Hk = F.silu(gemm.mm_raw(H.contiguous(), We[k]))
+            if spec.consts[k] != 1.0:
+                Hk = Hk * spec.consts[k]
+        H = Hk
     return gemm.mm_raw(H.contiguous(), We[-1])
+
+
+def _primal_tangent(r: Tensor, We: List[Tensor], spec: RadialSpec) -> Optional[Tuple[Tensor, Tensor]]:
+    """``R`` and ``dR/dr``: the value and tangent columns side by side (``[h | h']``), each hidden
+    layer one product with the block-diagonal weight and the coupled activation in its epilogue."""
+    E = r.shape[0]
+    B = _ext.ops().radial_basis(r.contiguous(), spec.freqs.to(r.device), spec.norm, spec.rc, spec.p)
+    H = torch.cat([B[:E], B[E:]], 1)
+    for k in range(len(We) - 1):
+        Hk = gemm.mm_act(H, torch.block_diag(We[k], We[k]), 2, spec.consts[k])
+        if Hk is None:
+            return None
+        H = Hk
+    n = H.shape[1] // 2
+    return gemm.mm_raw(H[:, :n], We[-1]), gemm.mm_raw(H[:, n:], We[-1])
 
 
 Chunk = Tuple[Tuple[int, int], Tuple[int, int], EdgePlan]
@@ -73,7 +92,8 @@ class _LeanRadialConv(Function):
         g_r = torch.empty_like(r) if ctx.needs_input_grad[1] else None
         gY = torch.empty_like(Y) if ctx.needs_input_grad[2] else None
         for (e0, e1), (n0, n1), sub in ctx.chunks:
-            R, Rd, _, _ = _forward(r[e0:e1], We, spec)
+            fused = _primal_tangent(r[e0:e1], We, spec)
+            R, Rd = fused if fused is not None else _forward(r[e0:e1], We, spec)[:2]
             R, Rd = R.view(-1, P, C), Rd.view(-1, P, C)
             Gc = G[:, n0:n1].contiguous()
             Yc = Y[e0:e1].contiguous()
