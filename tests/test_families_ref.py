@@ -305,3 +305,29 @@ def test_cnn3d(norm, blocks):
     load_same_weights(mine, ref)
     ref.set_use_fast(False)
     compare(mine, ref, batch(False, cutoff=3.5, species=[1, 6, 7, 8]), rtol=1e-9, atol=1e-9)
+
+
+@pytest.mark.parametrize("opts,periodic", [(dict(charge_solve=True), False),
+                                           (dict(charge_solve=True, hardness="features"), True),
+                                           (dict(charge_solve=True, fragments=True), False),
+                                           (dict(method="pme", constrain_charge=True), True),
+                                           (dict(constrain_charge=True, charge_weights="learned", dielectric=2.0),
+                                            False)])
+def test_latent_ewald_options(opts, periodic):
+    from xnn_b200.models.les import LatentEwald
+    from xnn_b200.models.schnet import SchNet
+    les_ref = ref_module("xnn.common.models.les")
+    schnet_ref = ref_module("xnn.gnn.models.schnet")
+    torch.manual_seed(0)
+    kw = dict(n_features=8, n_interactions=2, n_rbf=6, cutoff=5.0)
+    ref = les_ref.LatentEwald(schnet_ref.SchNet(**kw), n_channels=2, **opts).double()
+    mine = LatentEwald(SchNet(**kw), n_channels=2, **opts).double()
+    load_same_weights(mine, ref)
+    if periodic:
+        b = batch(True, cutoff=5.0)
+        extra = {"total_charge": torch.tensor([0.0, 1.0])}
+    else:
+        b = batch(False, cutoff=5.0, species=[11, 17, 6, 8, 1, 1] if opts.get("fragments") else None)
+        extra = {"total_charge": torch.tensor([0.0, 0.0, 0.0] if opts.get("fragments") else [1.0, 0.0, -1.0])}
+    keys = ("les_charges", "energy_lr") + (("energy_charge",) if opts.get("charge_solve") else ())
+    compare(mine, ref, b, periodic, rtol=1e-8, atol=1e-8, keys=keys, **extra)

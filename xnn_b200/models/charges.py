@@ -89,3 +89,63 @@ def solve_charges(chi: Tensor, hardness: Tensor, gamma: Tensor, target: Tensor, 
     rhs = torch.cat([-chi, target.to(chi.dtype).reshape(m)]).unsqueeze(1)
     sol = torch.linalg.solve(torch.cat([top, bottom], 0), rhs)
     return sol[:n, 0], -sol[n:, 0]
+
+
+#: default ion charges (e) of the fragment constraints: alkali and alkaline-earth cations, zinc, halides
+ION_CHARGES = {"Li": 1, "Na": 1, "K": 1, "Rb": 1, "Cs": 1, "Mg": 2, "Ca": 2, "Sr": 2, "Ba": 2, "Zn": 2,
+               "F": -1, "Cl": -1, "Br": -1, "I": -1}
+
+
+def ion_charge_table(ions=None) -> Tensor:
+    from ..data.elements import ATOMIC_NUMBERS
+    table = torch.zeros(119)
+    for key, value in (ION_CHARGES if ions is None else ions).items():
+        table[key if isinstance(key, int) else ATOMIC_NUMBERS[str(key)]] = float(value)
+    return table
+
+
+def bonded_fragments(z: Tensor, edge_index: Tensor, edge_vec: Tensor, radii: Tensor, ions: Tensor,
+                     bond_factor: float = 1.2) -> Tensor:
+    """Connected components of the bond graph (``r < bond_factor (R_i + R_j)``, ions never bonded),
+    numbered by their lowest atom index in order."""
+    n = z.shape[0]
+    src, dst = edge_index[0], edge_index[1]
+    bonded = torch.linalg.norm(edge_vec, dim=-1) < bond_factor * (radii[z[src]] + radii[z[dst]])
+    is_ion = ions[z] != 0
+    keep = bonded & ~is_ion[src] & ~is_ion[dst]
+    src, dst = src[keep], dst[keep]
+    labels = torch.arange(n, device=z.device)
+    for _ in range(n):                      # min-label propagation to a fixed point
+        new = labels.scatter_reduce(0, dst, labels[src], reduce="amin", include_self=True)
+        if torch.equal(new, labels):
+            break
+        labels = new
+    roots = torch.zeros(n, dtype=torch.long, device=z.device).index_fill(0, labels, 1)
+    return (torch.cumsum(roots, 0) - 1)[labels]
+
+
+def fragment_targets(fragments: Tensor, z: Tensor, ions: Tensor, label=None, total_charge=None) -> Tensor:
+    """Net charge of every fragment: its ``fragment_charges`` label (one value per fragment) or
+    the sum of its ion charges; checked against the structure's total charge."""
+    n_frag = int(fragments.max()) + 1
+    if label is not None:
+        hi = torch.full((n_frag,), -float("inf"), dtype=label.dtype, device=label.device)
+        lo = torch.full((n_frag,), float("inf"), dtype=label.dtype, device=label.device)
+        hi = hi.scatter_reduce(0, fragments, label, reduce="amax")
+        lo = lo.scatter_reduce(0, fragments, label, reduce="amin")
+        if float((hi - lo).abs().max()) > 1e-6:
+            raise ValueError("fragment_charges differ between atoms of one fragment (the label is the charge of "
+                             "the fragment each atom belongs to; ions are fragments of their own)")
+        targets = hi
+    else:
+        targets = torch.zeros(n_frag, dtype=ions.dtype, device=fragments.device).index_add(0, fragments, ions[z])
+    if total_charge is not None and abs(float(targets.sum()) - float(total_charge)) > 1e-6:
+        raise ValueError(f"the fragment charges add up to {float(targets.sum()):g} e but the structure's "
+                         f"total_charge is {float(total_charge):g} e; label the charged fragments with "
+                         "fragment_charges, or name the ions in ion_charges")
+    return targets
+
+
+def charge_energy(chi: Tensor, hardness: Tensor, q: Tensor) -> Tensor:
+    """Per-atom ``chi q + J q^2 / 2``."""
+    return chi * q + 0.5 * hardness * q * q

@@ -15,8 +15,13 @@ enumeration of the wave vectors (leading nonzero index positive, weight 2), the 
 relative slack on the cutoff shell, the ``1e-6`` offset in the real-space denominator and the
 ``1 / (4 pi)`` normalisation, so energies of the two implementations agree to rounding.
 
-Not built: the charge-equilibration solve and fragment constraints of the reference
-(``charge_solve``, ``fragments``) and its particle-mesh variant of this sum (``method="pme"``).
+With ``charge_solve`` the head's charge channel is an electronegativity ``chi`` and the charges
+minimise ``sum chi q + J q^2 / 2 + E_lr(q)`` at the structure's net charge (one augmented solve
+per structure, the Coulomb matrix the Hessian of the long-range energy; hardness per element or
+from the features); with ``fragments`` there is one constraint per bonded fragment (ions on their
+own, charges from ``fragment_charges`` labels or the ion table). ``method="pme"`` evaluates the
+reciprocal sum on a smooth-PME mesh (order 8, oversampled twice by default): the same wave-vector
+sphere and weights, structure factors from B-spline-spread charges.
 """
 from __future__ import annotations
 
@@ -62,17 +67,34 @@ def periodic_structures(cell: Optional[Tensor], pbc: Optional[Tensor], num_graph
     return periodic
 
 
+def smooth_size(n: float) -> int:
+    """The smallest integer of at least ``n`` (and 8) with no prime factor above 5."""
+    size = max(8, int(math.ceil(n)))
+    while True:
+        rest = size
+        for prime in (2, 3, 5):
+            while rest % prime == 0:
+                rest //= prime
+        if rest == 1:
+            return size
+        size += 1
+
+
 class EwaldSummation(nn.Module):
     """Ewald energy of a per-atom latent variable ``q`` (see module notes)."""
 
     def __init__(self, dl: float = 2.0, sigma: float = 1.0, exponent: int = 1,
-                 remove_self_interaction: bool = False, atom_block: int = 4096):
+                 remove_self_interaction: bool = False, atom_block: int = 4096, method: str = "kspace",
+                 pme_order: int = 8, pme_oversample: float = 2.0):
         super().__init__()
         if exponent not in (1, 6):
             raise ValueError(f"exponent must be 1 or 6, got {exponent}")
+        if method not in ("kspace", "pme"):
+            raise ValueError(f"method must be 'kspace' or 'pme', got {method!r}")
         self.dl, self.sigma, self.exponent = float(dl), float(sigma), int(exponent)
         self.remove_self_interaction = bool(remove_self_interaction)
         self.atom_block = int(atom_block)
+        self.method, self.pme_order, self.pme_oversample = method, int(pme_order), float(pme_oversample)
 
     def kernel(self, k2: Tensor) -> Tensor:
         """``f(k)`` of the reciprocal sum for squared wave numbers ``k2``."""
@@ -120,6 +142,51 @@ class EwaldSummation(nn.Module):
             energy = energy - self.self_energy(q)
         return energy
 
+    def pme_mesh(self, cell: Tensor) -> List[int]:
+        return [smooth_size(2.0 * self.pme_oversample * float(L) / self.dl)
+                for L in torch.linalg.norm(cell.detach(), dim=1).tolist()]
+
+    def reciprocal_pme(self, pos: Tensor, q: Tensor, cell: Tensor) -> Tensor:
+        """:meth:`reciprocal` with the structure factors from a smooth-PME mesh (full FFT grid)."""
+        from ..ffnn.multipoles import bspline_moduli, spread
+        mesh = self.pme_mesh(cell)
+        axes = [torch.fft.fftfreq(k, d=1.0 / k, dtype=cell.dtype, device=cell.device) for k in mesh]
+        miller = torch.stack(torch.meshgrid(*axes, indexing="ij"), -1)
+        kvec = 2.0 * math.pi * (miller @ torch.linalg.inv(cell).t())
+        k2 = (kvec * kvec).sum(-1)
+        inside = (k2 > 0) & (k2 <= (2.0 * math.pi / self.dl) ** 2 * (1.0 + 1e-9))
+        weight = torch.where(inside, self.kernel(torch.where(inside, k2, torch.ones_like(k2))),
+                             torch.zeros_like(k2)) / cell_volume(cell)
+        B = (bspline_moduli(mesh[0], self.pme_order, cell.dtype, cell.device)[:, None, None]
+             * bspline_moduli(mesh[1], self.pme_order, cell.dtype, cell.device)[None, :, None]
+             * bspline_moduli(mesh[2], self.pme_order, cell.dtype, cell.device)[None, None, :])
+        power = 0.0
+        for c in range(q.shape[1]):
+            F = torch.fft.fftn(spread(pos, cell, q[:, c], None, None, mesh, self.pme_order))
+            power = power + F.real.square() + F.imag.square()
+        energy = (weight * B * power).sum()
+        if self.remove_self_interaction and self.exponent == 1:
+            energy = energy - self.self_energy(q)
+        return energy
+
+    def coulomb_matrix(self, pos: Tensor, cell: Optional[Tensor] = None) -> Tensor:
+        """``gamma`` with ``E_lr(q) = q^T gamma q / 2`` for one structure (exponent 1)."""
+        if self.exponent != 1:
+            raise ValueError("the charge solve needs the Coulomb kernel (exponent=1)")
+        n = pos.shape[0]
+        eye = torch.eye(n, dtype=pos.dtype, device=pos.device)
+        self_term = 2.0 / (self.sigma * (2.0 * math.pi) ** 1.5)
+        if cell is None:
+            dist = torch.linalg.norm(pos[:, None, :] - pos[None, :, :], dim=-1)
+            gamma = torch.special.erf(dist / (self.sigma * math.sqrt(2.0))) / (dist + 1e-6) / (2.0 * math.pi)
+            return gamma if self.remove_self_interaction else gamma + eye * self_term
+        _, kpts, k2 = self.wave_vectors(cell)
+        w = self.kernel(k2)
+        ph = pos @ kpts.T
+        c, s = torch.cos(ph), torch.sin(ph)
+        gamma = 4.0 / cell_volume(cell) * ((c * w) @ c.T + (s * w) @ s.T)
+        return gamma - eye * self_term if self.remove_self_interaction else gamma
+
     def realspace_single(self, pos: Tensor, q: Tensor) -> Tensor:
         if self.exponent != 1:
             raise ValueError("the real-space sum supports exponent=1 only")
@@ -157,11 +224,15 @@ class EwaldSummation(nn.Module):
         periodic = periodic_structures(cell, pbc, num_graphs, pos.device)
         if num_graphs == 1 and not bool(periodic[0]):
             return self.realspace_single(pos, q).reshape(1)
+        if num_graphs == 1:
+            recip = self.reciprocal_pme if self.method == "pme" else self.reciprocal
+            return recip(pos, q, cell[0]).reshape(1)
         molecular = ~periodic[batch]
         out = self.realspace_batch(pos[molecular], q[molecular], batch[molecular], num_graphs)
+        recip = self.reciprocal_pme if self.method == "pme" else self.reciprocal
         for b in periodic.nonzero().flatten().tolist():
             mask = batch == b
-            e = self.reciprocal(pos[mask], q[mask], cell[b]).reshape(1)
+            e = recip(pos[mask], q[mask], cell[b]).reshape(1)
             out = out.index_put((torch.tensor([b], device=out.device),), e)
         return out
 
@@ -179,11 +250,15 @@ class LatentEwald(InteratomicPotential):
                  q_add_linear: bool = True, dl: float = 2.0, sigma: float = 1.0, exponent: int = 1,
                  remove_self_interaction: bool = False, constrain_charge: bool = False,
                  charge_channel: int = 0, charge_weights: str = "uniform", charge_solve: bool = False,
-                 fragments: bool = False, method: str = "kspace", dipole_origin: str = "com",
-                 dielectric: float = 1.0, learn_dielectric: bool = False, **unsupported):
+                 hardness: str = "element", hardness_init: float = 10.0, fragments: bool = False,
+                 bond_factor: float = 1.2, ion_charges=None, method: str = "kspace", pme_order: int = 8,
+                 pme_oversample: float = 2.0, dipole_origin: str = "com", dielectric: float = 1.0,
+                 learn_dielectric: bool = False):
         super().__init__()
-        if charge_solve or fragments or method != "kspace":
-            raise NotImplementedError("LatentEwald: charge_solve, fragments and method='pme' are not built")
+        if hardness not in ("element", "features"):
+            raise ValueError(f"hardness must be 'element' or 'features', got {hardness!r}")
+        if charge_solve and exponent != 1:
+            raise ValueError("the charge solve needs the Coulomb kernel (exponent=1)")
         dim = getattr(model, "node_feature_dim", None)
         if dim is None:
             raise TypeError(f"{type(model).__name__} exposes no node_feature_dim / 'node_features'")
@@ -208,8 +283,28 @@ class LatentEwald(InteratomicPotential):
         self.charge_channel = int(charge_channel)
         self.charge_weight = nn.Linear(dim, 1) if constrain_charge and charge_weights == "learned" else None
         self.dipole_origin = dipole_origin
+        self.charge_solve, self.hardness_mode = bool(charge_solve), hardness
+        raw0 = math.log(math.expm1(float(hardness_init) / LATENT_CHARGE_PER_E ** 2))   # softplus^-1
+        self.hardness_table = self.hardness_net = None
+        if charge_solve and hardness == "element":
+            self.hardness_table = nn.Embedding(119, 1)
+            nn.init.constant_(self.hardness_table.weight, raw0)
+        elif charge_solve:
+            self.hardness_net = nn.Linear(dim, 1)
+            nn.init.zeros_(self.hardness_net.weight)
+            nn.init.constant_(self.hardness_net.bias, raw0)
+        self.fragments = bool(fragments) and self.charge_solve
+        self.bond_factor = float(bond_factor)
+        if self.fragments:
+            from .charges import ion_charge_table
+            from .dispersion import load_tables
+            radii = load_tables("d4_reference.npz")["covalent_radius_aa"]
+            self.register_buffer("covalent_radii", torch.tensor(radii, dtype=torch.get_default_dtype()),
+                                 persistent=False)
+            self.register_buffer("ion_charges", ion_charge_table(ion_charges), persistent=False)
         self.ewald = EwaldSummation(dl=dl, sigma=sigma, exponent=exponent,
-                                    remove_self_interaction=remove_self_interaction)
+                                    remove_self_interaction=remove_self_interaction, method=method,
+                                    pme_order=pme_order, pme_oversample=pme_oversample)
         log_eps = torch.tensor(math.log(float(dielectric)))
         if learn_dielectric:
             self.log_dielectric = nn.Parameter(log_eps)
@@ -258,6 +353,47 @@ class LatentEwald(InteratomicPotential):
         d = scatter_sum(charges[:, None] * (pos - origin[data.batch]), data.batch, B)
         return d * (~periodic).to(d.dtype)[:, None]
 
+    def hardness_of(self, features: Tensor, z: Tensor) -> Tensor:
+        raw = self.hardness_table(z).squeeze(1) if self.hardness_table is not None else \
+            self.hardness_net(features).squeeze(1)
+        return nn.functional.softplus(raw)
+
+    def solve_charges(self, chi: Tensor, q: Tensor, features: Tensor, data: AtomicGraph, pos: Tensor,
+                      cell: Optional[Tensor]):
+        """Charges of the charge channel from one augmented solve per structure (see module notes)."""
+        from .charges import bonded_fragments, charge_energy, fragment_targets, solve_charges
+        batch, B, z = data.batch, data.num_graphs, data.atomic_numbers
+        hardness = self.hardness_of(features, z)
+        frag_all = None
+        if self.fragments:
+            frag_all = bonded_fragments(z, data.edge_index, data.edge_vectors().to(pos.dtype),
+                                        self.covalent_radii.to(pos.dtype), self.ion_charges.to(pos.dtype),
+                                        self.bond_factor)
+        solved = torch.zeros_like(chi)
+        mus = []
+        periodic = periodic_structures(cell, data.pbc, B, pos.device)
+        for i in range(B):
+            idx = (batch == i).nonzero().flatten()
+            gamma = self.ewald.coulomb_matrix(pos[idx], cell[i] if bool(periodic[i]) else None) / \
+                self.dielectric.to(chi.dtype)
+            total = data.total_charge[i].to(chi.dtype) if data.total_charge is not None else None
+            if frag_all is None:
+                frag_i = None
+                target = total * LATENT_CHARGE_PER_E if total is not None else chi.new_zeros(())
+            else:
+                frag_i = torch.unique(frag_all[idx], return_inverse=True)[1]
+                labeled = data.fragment_charges is not None and (
+                    data.fragment_charges_mask is None or bool(data.fragment_charges_mask[i]))
+                label = data.fragment_charges[idx].to(chi.dtype) if labeled else None
+                target = fragment_targets(frag_i, z[idx], self.ion_charges.to(chi.dtype), label, total) * \
+                    LATENT_CHARGE_PER_E
+            q_i, mu_i = solve_charges(chi[idx], hardness[idx], gamma, target, frag_i)
+            solved = solved.index_copy(0, idx, q_i)
+            mus.append(mu_i)
+        q = q.clone()
+        q[:, self.charge_channel] = solved
+        return q, charge_energy(chi, hardness, solved), torch.cat(mus), hardness, frag_all
+
     def forward(self, data: AtomicGraph) -> dict:
         out = dict(self.model(data))
         feats = out["node_features"]
@@ -265,10 +401,13 @@ class LatentEwald(InteratomicPotential):
         if self.q_linear is not None:
             q = q + self.q_linear(feats)
         B = data.num_graphs
+        chi = q[:, self.charge_channel] if self.charge_solve else None
         if self.constrain_charge:
             q = self.constrain(q, feats, data.batch, B, data.total_charge)
         pos = data.pos.to(q.dtype)
         cell = data.cell.to(q.dtype) if data.cell is not None else None
+        if chi is not None:
+            q, node_qe, mu, hardness, frag = self.solve_charges(chi, q, feats, data, pos, cell)
         e_lr = self.ewald(self.screened(q), pos, data.batch, B, cell, data.pbc)
         e_sr = out["energy"]
         energy = e_sr + e_lr.to(e_sr.dtype)
@@ -278,4 +417,11 @@ class LatentEwald(InteratomicPotential):
         charges = q[:, self.charge_channel] / LATENT_CHARGE_PER_E
         out.update(energy=energy, node_energy=node_energy, energy_sr=e_sr, energy_lr=e_lr,
                    latent_charges=q, les_charges=charges, les_dipole=self.dipole(charges, pos, data, periodic))
+        if chi is not None:
+            e_q = scatter_sum(node_qe, data.batch, B)
+            out.update(energy_charge=e_q, hardness=hardness, chemical_potential=mu,
+                       energy=out["energy"] + e_q.to(out["energy"].dtype),
+                       node_energy=out["node_energy"] + node_qe.to(out["node_energy"].dtype))
+            if frag is not None:
+                out["fragments"] = frag
         return out
