@@ -10,6 +10,7 @@
 #include "neighbor_impl.h"
 
 // ---- CUDA launchers (defined in the .cu files) -------------------------------------------
+int conv_edge_blocks(int C);
 template <typename T>
 cudaError_t edge_geom_fwd(int64_t, int, const T*, int, const T*, T, T, int, T*, T*, cudaStream_t);
 template <typename T>
@@ -290,8 +291,7 @@ std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t
   check_cuda(G, "G");
   c10::cuda::CUDAGuard g(G.device());
   const int64_t D = P * P;
-  const int64_t cpl = std::min<int64_t>(4, std::max<int64_t>(1, (C + 31) / 32));
-  const bool split = (C + 32 * cpl - 1) / (32 * cpl) > 1;
+  const bool split = conv_edge_blocks((int)C) > 1;
   const bool contract = Rd.has_value() && Rd->defined();
   if (contract) check_cuda(*Rd, "Rd");
   torch::Tensor gR = (want_gR && !Ys.empty() && !contract) ? torch::empty({E, P, C}, G.options()) : torch::Tensor();

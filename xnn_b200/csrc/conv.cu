@@ -39,8 +39,7 @@ struct PairTerms {  // per term: two operands (meaning depends on the kernel)
   const T* b[2];
   int n;
 };
-
-// One block of WPA warps per receiver; warp w takes the receiver's edges j0+w, j0+w+WPA, ...
+// One block of WPA warps per receiver; warp w takes the receiver's edges j0+w, j0+w+WPA, ... two at a time
 // and the warps' partial sums meet in shared memory (fixed order: deterministic).
 template <typename T, int P, int CPL, int WPA>
 __global__ void __launch_bounds__(32 * WPA) conv_gather_kernel(
@@ -57,7 +56,45 @@ __global__ void __launch_bounds__(32 * WPA) conv_gather_kernel(
 #pragma unroll
     for (int d = 0; d < D; ++d) acc[q][d] = T(0);
   const int64_t j0 = dst_ptr[i], j1 = dst_ptr[i + 1];
-  for (int64_t j = j0 + w; j < j1; j += WPA) {
+  // two edges per warp and step: the index, Y, x and R loads of both are issued before the
+  // multiply-adds (twice the loads in flight of a one-edge loop)
+  int64_t j = j0 + w;
+  for (; j + WPA < j1; j += 2 * WPA) {
+    const int64_t ea = perm ? perm[j] : j;
+    const int64_t eb = perm ? perm[j + WPA] : j + WPA;
+    const int64_t sa = src[ea], sb = src[eb];
+#pragma unroll
+    for (int tt = 0; tt < 3; ++tt) {
+      if (tt < t.n) {
+        T ya[D], yb[D];
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+          ya[d] = __ldg(t.Y[tt] + ea * D + d);
+          yb[d] = __ldg(t.Y[tt] + eb * D + d);
+        }
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+          const int c = cbase + lane + 32 * q;
+          if (c < C) {
+            const T xa = __ldg(t.x[tt] + sa * C + c), xb = __ldg(t.x[tt] + sb * C + c);
+            T ra[P], rb[P];
+#pragma unroll
+            for (int l = 0; l < P; ++l) {
+              ra[l] = __ldg(t.R[tt] + (ea * P + l) * C + c);
+              rb[l] = __ldg(t.R[tt] + (eb * P + l) * C + c);
+            }
+#pragma unroll
+            for (int l = 0; l < P; ++l) {
+              const T pa = ra[l] * xa, pb = rb[l] * xb;
+#pragma unroll
+              for (int m = 0; m < 2 * l + 1; ++m) acc[q][l * l + m] += pa * ya[l * l + m] + pb * yb[l * l + m];
+            }
+          }
+        }
+      }
+    }
+  }
+  if (j < j1) {
     const int64_t e = perm ? perm[j] : j;
     const int64_t s = src[e];
 #pragma unroll
@@ -307,6 +344,18 @@ inline int gather_cpl(int C) {
   const int f = forced_cpl("XNN_B200_GATHER_CPL", forced);
   return f > 0 ? f : std::min(2, cpl_for(C));
 }
+// The edge kernel reduces g_r and gY over the channels; with its channels split over two column
+// blocks the two partial sums meet by atomic addition onto zeros, which is exact and
+// order-independent for two terms (a + b == b + a), so at most two blocks keep it deterministic.
+// XNN_B200_EDGE_CPL (1-4) overrides the default; values that would need more than two blocks are
+// raised until two suffice.
+inline int edge_cpl(int C) {
+  static int forced = -1;
+  const int f = forced_cpl("XNN_B200_EDGE_CPL", forced);
+  int cpl = f > 0 ? f : cpl_for(C);
+  while (cpl < 4 && (C + 32 * cpl - 1) / (32 * cpl) > 2) ++cpl;
+  return cpl;
+}
 inline int scatter_cpl(int C) {
   static int forced = -1;
   const int f = forced_cpl("XNN_B200_SCATTER_CPL", forced);
@@ -370,7 +419,7 @@ cudaError_t conv_edge(int N, int C, int P, const int64_t* dst_ptr, const int* sr
     tE.Tout[k] = k < nE ? Touts[k] : nullptr;
     tY.a[k] = k < nY ? xY[k] : nullptr; tY.b[k] = k < nY ? RY[k] : nullptr;
   }
-  const int cpl = cpl_for(C);
+  const int cpl = edge_cpl(C);
   const int gy = (C + 32 * cpl - 1) / (32 * cpl);
   dim3 grid(N, gy);
   const int atomic_gY = gy > 1 ? 1 : 0;
@@ -393,6 +442,12 @@ cudaError_t conv_scatter(int N, int C, int P, const int64_t* src_ptr, const int6
   dim3 grid(N, (C + 32 * cpl - 1) / (32 * cpl));
   XNN_P_CPL_SWITCH(P, cpl, conv_scatter_kernel<T, PP, QQ, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, src_ptr, src_perm, t, gx));
   return cudaGetLastError();
+}
+
+// column blocks of the edge kernel (its outputs g_r / gY need zero initialisation when > 1)
+int conv_edge_blocks(int C) {
+  const int cpl = edge_cpl(C);
+  return (C + 32 * cpl - 1) / (32 * cpl);
 }
 
 #define XNN_INST(T)                                                                                  \

@@ -18,6 +18,7 @@ from torch import Tensor
 from torch.autograd import Function
 
 from .. import _ext
+from .modes import MODES
 
 SPIN_LIMIT = 50_000_000
 _STATUS: Dict[torch.device, Tensor] = {}
@@ -110,7 +111,8 @@ class _MM(Function):
     def backward(ctx, G: Tensor):
         X, W = ctx.saved_tensors
         gX = matmul(G, W.t()) if ctx.needs_input_grad[0] else None
-        gW = matmul_t(X, G) if ctx.needs_input_grad[1] else None
+        # a force pass differentiates only towards the positions: no weight gradient is used
+        gW = matmul_t(X, G) if ctx.needs_input_grad[1] and not MODES.force_pass else None
         return gX, gW
 
 

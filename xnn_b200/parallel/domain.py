@@ -102,6 +102,12 @@ def _tie(x: Tensor) -> Tensor:
 
 
 # --------------------------------------------------------------------------- plan
+def _rows3(x: Tensor, m: Tensor) -> Tensor:
+    """``x @ m`` for ``x (n, 3)`` and ``m (3, 3)`` as one broadcast product and sum: a library
+    GEMM with an inner size of 3 wastes a launch configuration meant for large ``K``."""
+    return (x.unsqueeze(-1) * m.to(x.dtype)).sum(1)
+
+
 @dataclass
 class DomainPlan:
     """What one process evaluates: owned atoms, ghosts, exchanges, neighbour list.
@@ -138,6 +144,8 @@ class DomainPlan:
     remote_offsets: Optional[list] = None
     remote_send_offsets: Optional[list] = None
     max_rows: int = 0
+    #: float64 inverse of ``cell`` (reused while the cell stays the plan's)
+    inv_cell: Optional[Tensor] = None
 
     @property
     def n_owned(self) -> int:
@@ -293,7 +301,7 @@ class DomainParallel(nn.Module):
         if periodic:
             cell = cell.detach().to(device=device, dtype=torch.float64)
             inv = torch.linalg.inv(cell)
-            raw = pos @ inv
+            raw = _rows3(pos, inv)
             frac = raw - torch.floor(raw)
             widths_t = 1.0 / torch.linalg.norm(inv, dim=0)      # plane spacings of the cell
         else:
@@ -365,7 +373,7 @@ class DomainParallel(nn.Module):
             raise RuntimeError("the processes disagree on the owners of the atoms")
 
         if periodic:
-            local = torch.cat([frac[owned], frac[ghosts] + ghost_image.to(torch.float64)]) @ cell
+            local = _rows3(torch.cat([frac[owned], frac[ghosts] + ghost_image.to(torch.float64)]), cell)
             reference = frac[owned]
         else:
             local = torch.cat([pos[owned], pos[ghosts]])
@@ -404,7 +412,8 @@ class DomainParallel(nn.Module):
             cell_shifts=cell_shifts.to(device), pbc=pbc, atomic_numbers=atomic_numbers,
             total_charge=total_charge, spin_multiplicity=spin_multiplicity, reference=reference,
             cell=cell, counts=counts, order=order, need=self.need, skin=self.skin,
-            remote_offsets=remote_offsets, remote_send_offsets=remote_send_offsets, max_rows=max_rows)
+            remote_offsets=remote_offsets, remote_send_offsets=remote_send_offsets, max_rows=max_rows,
+            inv_cell=inv if periodic else None)
 
     def _cell(self, plan: DomainPlan, cell: Optional[Tensor]) -> Optional[Tensor]:
         if plan.cell is None:
@@ -424,9 +433,12 @@ class DomainParallel(nn.Module):
             moved = pos.detach().to(torch.float64) - plan.reference
         else:
             cell = cell.detach().to(torch.float64)
-            frac = pos.detach().to(torch.float64) @ torch.linalg.inv(cell) - plan.reference
-            moved = (frac - torch.round(frac)) @ cell
-            strain = float(torch.linalg.matrix_norm(torch.linalg.inv(plan.cell) @ (cell - plan.cell), ord=2))
+            same = plan.inv_cell is not None and (cell is plan.cell or bool(torch.equal(cell, plan.cell)))
+            inv = plan.inv_cell if same else torch.linalg.inv(cell)
+            frac = _rows3(pos.detach().to(torch.float64), inv) - plan.reference
+            moved = _rows3(frac - torch.round(frac), cell)
+            if not same:
+                strain = float(torch.linalg.matrix_norm(torch.linalg.inv(plan.cell) @ (cell - plan.cell), ord=2))
         largest = moved.norm(dim=-1).max() if len(moved) else moved.new_zeros(())
         if plan.world > 1:
             largest = largest.reshape(1).clone()
@@ -488,21 +500,23 @@ class DomainParallel(nn.Module):
         dtype, device = p.dtype, p.device
         strain, volume, own = None, None, p
         if cell is not None:
+            c64 = cell.detach().to(torch.float64)
+            same = plan.inv_cell is not None and (cell is plan.cell or bool(torch.equal(c64, plan.cell)))
+            inv = plan.inv_cell if same else torch.linalg.inv(c64)
             cell = cell.detach().to(dtype)
-            volume = torch.linalg.det(cell.to(torch.float64)).abs().reshape(1)
-            jumps = torch.round(p.detach().to(torch.float64) @ torch.linalg.inv(cell.to(torch.float64))
-                                - plan.reference).to(dtype)
+            volume = torch.linalg.det(c64).abs().reshape(1)
+            jumps = torch.round(_rows3(p.detach().to(torch.float64), inv) - plan.reference).to(dtype)
             if self.compute_stress:
                 strain = torch.zeros((3, 3), dtype=dtype, device=device, requires_grad=True)
                 sym = 0.5 * (strain + strain.transpose(0, 1))
                 own = own + own @ sym
                 cell = cell + cell @ sym
             # owned atoms brought back next to where the plan saw them
-            own = own - jumps @ cell
+            own = own - _rows3(jumps, cell)
         ties: List[Tensor] = []
         ghosts = self._exchange(plan, own, ties)
         if cell is not None:
-            ghosts = ghosts + plan.ghost_shifts.to(dtype) @ cell
+            ghosts = ghosts + _rows3(plan.ghost_shifts.to(dtype), cell)
         local = torch.cat([own, ghosts])
         numbers = plan.atomic_numbers[plan.index]
         if plan.n_local == 0:
@@ -514,7 +528,7 @@ class DomainParallel(nn.Module):
         with torch.no_grad():
             vec = local[edge_index[1]] - local[edge_index[0]]
             if plan.pbc is not None:
-                vec = vec + cell_shifts.to(dtype) @ cell
+                vec = vec + _rows3(cell_shifts.to(dtype), cell)
             keep = (vec * vec).sum(-1) < self.cutoff ** 2
         edge_index, cell_shifts = edge_index[:, keep], cell_shifts[keep]
         model_dtype = _model_dtype(self.model)
