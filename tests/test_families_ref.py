@@ -331,3 +331,25 @@ def test_latent_ewald_options(opts, periodic):
         extra = {"total_charge": torch.tensor([0.0, 0.0, 0.0] if opts.get("fragments") else [1.0, 0.0, -1.0])}
     keys = ("les_charges", "energy_lr") + (("energy_charge",) if opts.get("charge_solve") else ())
     compare(mine, ref, b, periodic, rtol=1e-8, atol=1e-8, keys=keys, **extra)
+
+
+@pytest.mark.parametrize("opts,periodic", [
+    (dict(), False),
+    (dict(attention="exact", n_residual=2), False),
+    (dict(lr_cutoff=6.0), True),
+    (dict(lr_cutoff=6.0, ewald=True, spin_embedding=False, exp_weighting=True), True),
+    (dict(nonlocal_interactions=False, zbl_repulsion=False, d4_dispersion=False), False),
+])
+def test_spookynet(opts, periodic):
+    from xnn_b200.models.spookynet import SpookyNet
+    mine, ref = _pair("xnn.hybnn.models.spookynet", "SpookyNet", SpookyNet, n_features=8, n_interactions=2, n_rbf=6,
+                      cutoff=4.0, seed=3, **opts)
+    ref.set_use_fast(False)
+    with torch.no_grad():   # the zero-initialised output layers and biases carry values
+        for p_ref in ref.parameters():
+            p_ref.add_(0.05 * torch.randn_like(p_ref))
+    load_same_weights(mine, ref)
+    b = batch(periodic, cutoff=6.0 if periodic else 4.0)
+    ng = 2 if periodic else 3
+    extra = {"total_charge": torch.tensor([1.0, -1.0, 0.0][:ng]), "spin_multiplicity": torch.tensor([2.0, 1.0, 3.0][:ng])}
+    compare(mine, ref, b, periodic, rtol=1e-9, atol=1e-9, keys=("charges", "dipole", "energy_dispersion"), **extra)

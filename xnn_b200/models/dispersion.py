@@ -64,14 +64,16 @@ def switching_function(r: Tensor, cutoff: float, width: float) -> Tensor:
 
 
 def gaussian_reference_weights(cn: Tensor, refcn: Tensor, valid: Tensor, wf: float,
-                               ngw: Optional[Tensor] = None, eps_norm: float = 0.0) -> Tensor:
+                               ngw: Optional[Tensor] = None, eps_norm: float = 0.0,
+                               n_gauss: Optional[int] = None) -> Tensor:
     """Normalised Gaussian weights ``(N, R)`` of the reference systems in the coordination number;
-    when every Gaussian underflows the reference(s) with the largest CN take weight one."""
+    when every Gaussian underflows the reference(s) with the largest CN take weight one.
+    ``n_gauss``: the largest entry of ``ngw`` when the caller knows it (no device read-back)."""
     d2 = (cn[:, None] - refcn) ** 2
     if ngw is None:
         gw = torch.exp(-wf * d2)
     else:
-        n_max = int(ngw.max())
+        n_max = int(ngw.max()) if n_gauss is None else int(n_gauss)
         j = torch.arange(1, n_max + 1, device=cn.device)
         g = torch.exp(-wf * j.to(cn.dtype)[None, None, :] * d2[:, :, None])
         gw = torch.where(j[None, None, :] <= ngw[:, :, None], g, 0.0).sum(-1)
