@@ -1,0 +1,138 @@
+"""Classical fixed-topology force fields against the reference framework: the ``.frc`` reader, the
+derived topology and the energies, forces and stress of the same library on the same conformers."""
+import math
+
+import pytest
+import torch
+
+from ref_oracle import ref_module
+from xnn_b200.data import collate, structure_to_graph
+from xnn_b200.models.outputs import ForceStressOutput
+
+
+@pytest.fixture(autouse=True)
+def _f64():
+    old = torch.get_default_dtype()
+    torch.set_default_dtype(torch.float64)
+    yield
+    torch.set_default_dtype(old)
+
+
+def _butane():
+    pos = [[0.0, 0.0, 0.0], [1.53, 0.0, 0.0], [2.05, 1.44, 0.0], [3.58, 1.44, 0.0], [-0.4, -0.5, 0.9],
+           [-0.4, -0.5, -0.9], [-0.4, 1.0, 0.0], [1.93, -0.52, 0.88], [1.93, -0.52, -0.88], [1.65, 1.96, -0.88],
+           [1.65, 1.96, 0.88], [3.98, 0.44, 0.0], [3.98, 1.96, 0.88], [3.98, 1.96, -0.88]]
+    z = [6, 6, 6, 6] + [1] * 10
+    types = ["opls_80", "opls_81", "opls_81", "opls_80"] + ["opls_85"] * 10
+    bonds = [(0, 1), (1, 2), (2, 3), (0, 4), (0, 5), (0, 6), (1, 7), (1, 8), (2, 9), (2, 10), (3, 11), (3, 12),
+             (3, 13)]
+    return pos, z, types, bonds
+
+
+def _ethylene(tilt=12.0):
+    d, dh, ang = 1.34, 1.08, math.radians(120.0)
+    phi = math.radians(tilt)
+    y = dh * math.sin(math.pi - ang)
+    pos = [[0.0, 0.0, 0.0], [d, 0.0, 0.0], [-dh * math.cos(math.pi - ang), y, 0], [-dh * math.cos(math.pi - ang), -y, 0],
+           [d + dh * math.cos(math.pi - ang), y * math.cos(phi), y * math.sin(phi)],
+           [d + dh * math.cos(math.pi - ang), -y, 0.0]]
+    return pos, [6, 6, 1, 1, 1, 1], ["opls_88", "opls_88"] + ["opls_89"] * 4, [(0, 1), (0, 2), (0, 3), (1, 4), (1, 5)]
+
+
+def _graphs(pos, z, cutoff, n=3, cell=None, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for k in range(n):
+        p = torch.tensor(pos) + 0.08 * torch.randn(len(pos), 3, generator=g) * (k > 0)
+        s = {"pos": p, "atomic_numbers": torch.tensor(z)}
+        if cell is not None:
+            s["cell"], s["pbc"] = torch.tensor(cell), torch.tensor([True, True, True])
+        out.append(structure_to_graph(s, cutoff))
+    return collate(out)
+
+
+def test_frc_reader_matches_reference():
+    rf = ref_module("xnn.ffnn.common.frc")
+    from pathlib import Path
+
+    from xnn_b200.ffnn import frc
+    for f in ("oplsaa", "lopls", "amber", "charmm22", "dreiding"):
+        mine, ref = frc.FrcFile(frc.DATA_DIR / f"{f}.frc"), rf.FrcFile(Path(rf.builtin_data_dir()) / f"{f}.frc")
+        assert mine.forcefields == ref.forcefields
+        for name in ref.forcefields:
+            a, b = mine.forcefield(name), ref.forcefield(name)
+            assert set(a.sections) == set(b.sections) and a.metadata == b.metadata
+            for kind, rows in b.sections.items():
+                assert set(a.sections[kind]) == set(rows)
+                for key, row in rows.items():
+                    for col, v in row.values.items():
+                        w = a.sections[kind][key].values[col]
+                        assert (math.isclose(float(w), float(v), rel_tol=1e-12, abs_tol=1e-14)
+                                if isinstance(v, float) else str(w) == str(v)), (f, kind, key, col)
+
+
+def test_units_and_nonbond_forms():
+    from xnn_b200.ffnn.frc import convert_units, nonbond_to_sigma_eps
+    assert math.isclose(convert_units(1.0, "kJ/mol/nm^2", "kcal/mol/Å^2"), 1.0 / 418.4)
+    assert math.isclose(convert_units(2.0, "(kcal/mol)**(1/12)*nm", "(kcal/mol)**(1/12)*Å"), 20.0)
+    s, e = nonbond_to_sigma_eps("A-B", 4.0 * 0.2 * 3.0 ** 12, 4.0 * 0.2 * 3.0 ** 6)
+    assert math.isclose(s, 3.0) and math.isclose(e, 0.2)
+    with pytest.raises(ValueError):
+        convert_units(1.0, "kcal/mol", "Å")
+
+
+def test_topology_derivation_matches_reference():
+    rt = ref_module("xnn.ffnn.models.topology")
+    from xnn_b200.ffnn.topology import MolecularTopology, guess_bonds
+    pos, z, types, bonds = _butane()
+    a, b = MolecularTopology.from_bonds(types, bonds), rt.MolecularTopology.from_bonds(types, bonds)
+    for f in ("bonds", "angles", "dihedrals", "exclusions", "pairs14", "pairs15"):
+        assert getattr(a, f) == getattr(b, f), f
+    assert guess_bonds(pos, z) == sorted(bonds) == rt.guess_bonds(pos, z)
+    r = a.replicate(3)
+    assert r.n_atoms == 42 and r.pairs14[-1] == tuple(x + 28 for x in a.pairs14[-1])
+
+
+@pytest.mark.parametrize("case", ["butane", "butane_switch", "ethylene", "periodic"])
+def test_opls_matches_reference(case):
+    ro = ref_module("xnn.ffnn.models.opls")
+    rt = ref_module("xnn.ffnn.models.topology")
+    from ref_oracle import ref_graph
+    from xnn_b200.ffnn.opls import OPLS
+    from xnn_b200.ffnn.topology import MolecularTopology
+    pos, z, types, bonds = _ethylene() if case == "ethylene" else _butane()
+    cell, cutoff, kw = None, 20.0, {}
+    if case == "butane_switch":
+        cutoff, kw = 4.0, {"switch_width": 1.5}
+    if case == "periodic":
+        cell, cutoff = [[9.0, 0.0, 0.0], [0.0, 8.5, 0.0], [0.0, 0.0, 9.5]], 4.0
+    mine = OPLS("oplsaa", MolecularTopology.from_bonds(types, bonds), cutoff=cutoff, **kw)
+    ref = ro.OPLS("oplsaa", rt.MolecularTopology.from_bonds(types, bonds), cutoff=cutoff, use_fast=False, **kw)
+    b = _graphs(pos, z, cutoff, cell=cell)
+    outs = ref_module("xnn.common.models.outputs")
+    periodic = cell is not None
+    o_ref = outs.ForceStressOutput(ref, compute_stress=periodic)(ref_graph(b))
+    o = ForceStressOutput(mine, compute_stress=periodic)(b.clone())
+    for k in ("energy", "forces", "e_bond", "e_angle", "e_torsion", "e_improper", "e_lj", "e_coulomb", "e_lj14",
+              "e_coulomb14") + (("stress",) if periodic else ()):
+        torch.testing.assert_close(o[k], o_ref[k], rtol=1e-10, atol=1e-10, msg=k)
+    assert float(o["e_torsion"].detach().abs().sum()) > 0
+    key = "e_improper" if case == "ethylene" else "e_lj"
+    assert float(o[key].detach().abs().sum()) > 0
+
+
+def test_opls_training_keeps_net_charge_and_library_roundtrip(tmp_path):
+    from xnn_b200.ffnn.opls import OPLS, read_opls
+    from xnn_b200.ffnn.topology import MolecularTopology
+    pos, z, types, bonds = _butane()
+    m = OPLS("oplsaa", MolecularTopology.from_bonds(types, bonds), cutoff=20.0, trainable=["charge", "bond_k"])
+    with torch.no_grad():
+        m.ff.params["charge"].add_(0.1)
+    q = m(_graphs(pos, z, 20.0, n=1))["charges"]
+    assert abs(float(q.detach().sum())) < 1e-10
+    lib = m.export_library()
+    lib.save(tmp_path / "lib.json")
+    back = read_opls(tmp_path / "lib.json")
+    e1 = m(_graphs(pos, z, 20.0, n=1))["energy"]
+    e2 = OPLS(back, MolecularTopology.from_bonds(types, bonds), cutoff=20.0)(_graphs(pos, z, 20.0, n=1))["energy"]
+    torch.testing.assert_close(e1, e2, rtol=1e-9, atol=1e-9)
