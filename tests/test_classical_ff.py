@@ -136,3 +136,37 @@ def test_opls_training_keeps_net_charge_and_library_roundtrip(tmp_path):
     e1 = m(_graphs(pos, z, 20.0, n=1))["energy"]
     e2 = OPLS(back, MolecularTopology.from_bonds(types, bonds), cutoff=20.0)(_graphs(pos, z, 20.0, n=1))["energy"]
     torch.testing.assert_close(e1, e2, rtol=1e-9, atol=1e-9)
+
+
+def _nma():
+    pos = [[0.0, 0.0, 0.0], [1.51, 0.0, 0.0], [2.13, 1.07, 0.0], [2.14, -1.19, 0.0], [3.59, -1.28, 0.0],
+           [1.60, -2.05, 0.0], [-0.38, 1.02, 0.0], [-0.38, -0.51, 0.89], [-0.38, -0.51, -0.89], [3.95, -0.76, 0.89],
+           [3.95, -0.76, -0.89], [3.95, -2.31, 0.0]]
+    z = [6, 6, 8, 7, 6, 1, 1, 1, 1, 1, 1, 1]
+    types = ["CT", "C", "O", "N", "CT", "H", "HC", "HC", "HC", "H1", "H1", "H1"]
+    bonds = [(0, 1), (1, 2), (1, 3), (3, 4), (3, 5), (0, 6), (0, 7), (0, 8), (4, 9), (4, 10), (4, 11)]
+    q = [-0.3662, 0.5972, -0.5679, -0.4157, -0.1490, 0.2719, 0.1123, 0.1123, 0.1123, 0.0976, 0.0976, 0.0976]
+    return pos, z, types, bonds, q
+
+
+@pytest.mark.parametrize("periodic", [False, True])
+def test_amber_matches_reference(periodic):
+    ra = ref_module("xnn.ffnn.models.amber")
+    rt = ref_module("xnn.ffnn.models.topology")
+    from ref_oracle import ref_graph
+    from xnn_b200.ffnn.amber import Amber
+    from xnn_b200.ffnn.topology import MolecularTopology
+    pos, z, types, bonds, q = _nma()
+    cell, cutoff = ([[10.0, 0, 0], [0, 9.0, 0], [0, 0, 9.5]], 4.0) if periodic else (None, 20.0)
+    mine = Amber("ff94", MolecularTopology.from_bonds(types, bonds, charges=q), cutoff=cutoff, switch_width=1.0)
+    ref = ra.Amber("ff94", rt.MolecularTopology.from_bonds(types, bonds, charges=q), cutoff=cutoff, switch_width=1.0,
+                   use_fast=False)
+    assert mine.impropers == ref.impropers and len(mine.impropers) == 2
+    b = _graphs(pos, z, cutoff, cell=cell)
+    outs = ref_module("xnn.common.models.outputs")
+    o_ref = outs.ForceStressOutput(ref, compute_stress=periodic)(ref_graph(b))
+    o = ForceStressOutput(mine, compute_stress=periodic)(b.clone())
+    for k in ("energy", "forces", "e_torsion", "e_improper", "e_vdw", "e_coulomb", "e_vdw14", "e_coulomb14") + \
+            (("stress",) if periodic else ()):
+        torch.testing.assert_close(o[k], o_ref[k], rtol=1e-10, atol=1e-10, msg=k)
+    assert float(o["e_improper"].detach().abs().sum()) > 0
