@@ -170,3 +170,29 @@ def test_amber_matches_reference(periodic):
             (("stress",) if periodic else ()):
         torch.testing.assert_close(o[k], o_ref[k], rtol=1e-10, atol=1e-10, msg=k)
     assert float(o["e_improper"].detach().abs().sum()) > 0
+
+
+@pytest.mark.parametrize("periodic", [False, True])
+def test_charmm_matches_reference(periodic):
+    rc = ref_module("xnn.ffnn.models.charmm")
+    rt = ref_module("xnn.ffnn.models.topology")
+    from ref_oracle import ref_graph
+    from xnn_b200.ffnn.charmm import Charmm
+    from xnn_b200.ffnn.topology import MolecularTopology
+    pos, z, _types, bonds, _q = _nma()
+    types = ["CT3", "C", "O", "NH1", "CT3", "H", "HA", "HA", "HA", "HA", "HA", "HA"]
+    q = [-0.27, 0.51, -0.51, -0.47, -0.11, 0.31, 0.09, 0.09, 0.09, 0.09, 0.09, 0.09]
+    imps = [(1, 0, 3, 2), (3, 1, 4, 5)]
+    cell, cutoff = ([[10.0, 0, 0], [0, 9.0, 0], [0, 0, 9.5]], 4.0) if periodic else (None, 20.0)
+    mine = Charmm("charmm22", MolecularTopology.from_bonds(types, bonds, charges=q, impropers=imps), cutoff=cutoff,
+                  switch_width=1.0)
+    ref = rc.Charmm("charmm22", rt.MolecularTopology.from_bonds(types, bonds, charges=q, impropers=imps),
+                    cutoff=cutoff, switch_width=1.0, use_fast=False)
+    b = _graphs(pos, z, cutoff, cell=cell)
+    outs = ref_module("xnn.common.models.outputs")
+    o_ref = outs.ForceStressOutput(ref, compute_stress=periodic)(ref_graph(b))
+    o = ForceStressOutput(mine, compute_stress=periodic)(b.clone())
+    for k in ("energy", "forces", "e_urey_bradley", "e_torsion", "e_improper", "e_vdw", "e_coulomb", "e_vdw14",
+              "e_coulomb14") + (("stress",) if periodic else ()):
+        torch.testing.assert_close(o[k], o_ref[k], rtol=1e-10, atol=1e-10, msg=k)
+    assert float(o["e_improper"].detach().abs().sum()) > 0 and float(o["e_urey_bradley"].detach().abs().sum()) > 0

@@ -338,6 +338,8 @@ class Amber(FixedTopologyPotential):
     ``e_angle``, ``e_torsion``, ``e_improper``, ``e_vdw``, ``e_coulomb``, ``e_vdw14``,
     ``e_coulomb14``, ``e_ref`` besides energies and ``charges``."""
 
+    force_field_cls = None      # AmberForceField (set below the class)
+
     def __init__(self, ffield, topology, *, cutoff: float = 10.0, switch_width: float = 0.0,
                  charges: Optional[Sequence[float]] = None, fudge_lj: Optional[float] = None,
                  fudge_qq: Optional[float] = None, trainable=(), keep_intermediates: bool = False,
@@ -349,7 +351,8 @@ class Amber(FixedTopologyPotential):
         else:
             model_groups = {g for g in trainable if g in MODEL_GROUPS}
             groups = tuple(g for g in trainable if g not in MODEL_GROUPS)
-        self.ff = ffield if isinstance(ffield, AmberForceField) else AmberForceField(ffield, trainable=groups)
+        ffc = self.force_field_cls
+        self.ff = ffield if isinstance(ffield, ffc) else ffc(ffield, trainable=groups)
         self.atom_ref = nn.Embedding(MAX_Z, 1)
         nn.init.zeros_(self.atom_ref.weight)
         self.atom_ref.weight.requires_grad_("atom_ref" in model_groups)
@@ -363,7 +366,9 @@ class Amber(FixedTopologyPotential):
         self.keep_intermediates, self.intermediates = bool(keep_intermediates), {}
         self.node_feature_dim = 1
         self.use_fast = use_fast
-        self._bind(topology if isinstance(topology, MolecularTopology) else read_topology(topology), charges)
+        top = topology if isinstance(topology, MolecularTopology) else read_topology(topology)
+        self._bind(top)
+        self._bind_charges(top, charges)
         self.species = sorted({int(z) for z in self.top_z.tolist()})
         if atomic_energies is not None:
             set_atomic_energies(self, atomic_energies)
@@ -372,7 +377,7 @@ class Amber(FixedTopologyPotential):
         self.register_buffer("charge_total", torch.tensor(float("nan") if total is None else total,
                                                           dtype=self.charge.dtype), persistent=False)
 
-    def _bind(self, top: MolecularTopology, charges) -> None:
+    def _bind(self, top: MolecularTopology) -> None:
         self.topology, ff, missing = top, self.ff, []
 
         def get(fn, *a):
@@ -414,6 +419,8 @@ class Amber(FixedTopologyPotential):
         self._buf("improper_type", it, 1)
         self._buf("pair14_index", top.pairs14, 2)
         self._buf("excl_index", sorted(set(top.exclusions) | set(top.pairs14)), 2)
+
+    def _bind_charges(self, top: MolecularTopology, charges) -> None:
         n = len(top.types)
         if charges is None:
             charges = top.charges if top.charges else [0.0] * n
@@ -500,3 +507,6 @@ class Amber(FixedTopologyPotential):
                    fudge_lj=_floaty(e, "fudge_lj"), fudge_qq=_floaty(e, "fudge_qq"),
                    trainable=_listy(e.get("trainable")) or (), constrain_charge=_constrain(e.get("constrain_charge", True)),
                    atomic_energies=e.get("atomic_energies"))
+
+
+Amber.force_field_cls = AmberForceField
