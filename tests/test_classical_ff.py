@@ -196,3 +196,46 @@ def test_charmm_matches_reference(periodic):
               "e_coulomb14") + (("stress",) if periodic else ()):
         torch.testing.assert_close(o[k], o_ref[k], rtol=1e-10, atol=1e-10, msg=k)
     assert float(o["e_improper"].detach().abs().sum()) > 0 and float(o["e_urey_bradley"].detach().abs().sum()) > 0
+
+
+def _water_dimer():
+    pos = [[0.0, 0.0, 0.0], [0.96, 0.0, 0.0], [-0.24, 0.93, 0.0], [2.9, 0.1, 0.2], [3.2, 0.9, 0.5], [3.3, -0.6, 0.6]]
+    return pos, [8, 1, 1, 8, 1, 1], ["O_3", "H__HB", "H__HB", "O_3", "H__HB", "H__HB"], [(0, 1), (0, 2), (3, 4), (3, 5)]
+
+
+def _propene():
+    pos = [[0.0, 0.0, 0.0], [1.34, 0.0, 0.0], [2.1, 1.3, 0.0], [-0.55, 0.93, 0.0], [-0.55, -0.93, 0.0],
+           [1.9, -0.93, 0.0], [3.15, 1.05, 0.1], [1.85, 1.9, 0.88], [1.9, 1.92, -0.85]]
+    return (pos, [6, 6, 6, 1, 1, 1, 1, 1, 1], ["C_2", "C_2", "C_3"] + ["H_"] * 6,
+            [(0, 1), (1, 2), (0, 3), (0, 4), (1, 5), (2, 6), (2, 7), (2, 8)])
+
+
+@pytest.mark.parametrize("case", ["propene", "propene_x6_morse", "water", "water_periodic"])
+def test_dreiding_matches_reference(case):
+    rd = ref_module("xnn.ffnn.models.dreiding")
+    rt = ref_module("xnn.ffnn.models.topology")
+    from ref_oracle import ref_graph
+    from xnn_b200.ffnn.dreiding import Dreiding
+    from xnn_b200.ffnn.topology import MolecularTopology
+    if case.startswith("water"):
+        pos, z, types, bonds = _water_dimer()
+        orders, q = [1.0] * 4, [-0.8, 0.4, 0.4, -0.8, 0.4, 0.4]
+    else:
+        pos, z, types, bonds = _propene()
+        orders, q = [2.0] + [1.0] * 7, None
+    kw = dict(bond_style="morse", angle_style="harmonic") if case == "propene_x6_morse" else {}
+    ffield = "dreiding/X6" if case == "propene_x6_morse" else "dreiding"
+    cell, cutoff = ([[8.0, 0, 0], [0, 7.5, 0], [0, 0, 7.0]], 3.5) if case == "water_periodic" else (None, 12.0)
+    mine = Dreiding(ffield, MolecularTopology.from_bonds(types, bonds, bond_orders=orders), cutoff=cutoff, charges=q, **kw)
+    ref = rd.Dreiding(ffield, rt.MolecularTopology.from_bonds(types, bonds, bond_orders=orders), cutoff=cutoff,
+                      charges=q, use_fast=False, **kw)
+    b = _graphs(pos, z, cutoff, cell=cell)
+    periodic = cell is not None
+    outs = ref_module("xnn.common.models.outputs")
+    o_ref = outs.ForceStressOutput(ref, compute_stress=periodic)(ref_graph(b))
+    o = ForceStressOutput(mine, compute_stress=periodic)(b.clone())
+    for k in ("energy", "forces", "e_bond", "e_angle", "e_torsion", "e_inversion", "e_vdw", "e_coulomb", "e_hbond") \
+            + (("stress",) if periodic else ()):
+        torch.testing.assert_close(o[k], o_ref[k], rtol=1e-10, atol=1e-10, msg=k)
+    key = "e_hbond" if case.startswith("water") else "e_torsion"
+    assert float(o[key].detach().abs().sum()) > 0
