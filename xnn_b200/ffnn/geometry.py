@@ -140,8 +140,10 @@ def half_edges(data, excl_index: Tensor, n: int, cache: dict):
 
 
 def quintic_switch(r: Tensor, cutoff: float, width: float) -> Tensor:
-    """1 below ``cutoff - width``, ``1 - x^3 (10 - 15 x + 6 x^2)`` across the last ``width``."""
+    """1 below ``cutoff - width``, ``1 - x^3 (10 - 15 x + 6 x^2)`` across the last ``width``, 0 from
+    the cutoff on (pairs of a skin list beyond the cutoff count nothing)."""
+    inside = (r < cutoff).to(r.dtype)
     if width <= 0.0:
-        return torch.ones_like(r)
+        return inside
     x = torch.clamp((r - (cutoff - width)) / width, 0.0, 1.0)
-    return 1.0 - x ** 3 * (10.0 - 15.0 * x + 6.0 * x * x)
+    return (1.0 - x ** 3 * (10.0 - 15.0 * x + 6.0 * x * x)) * inside
