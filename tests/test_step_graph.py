@@ -72,3 +72,27 @@ def test_verlet_conserves_energy():
     md.run(40)
     e1 = float(md.out["energy"]) + float(md.kinetic_energy())
     assert abs(e1 - e0) < 2e-3 * max(1.0, abs(e0))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind", ["opls", "schnet"])
+def test_step_graph_replay_on_gpu(kind):
+    dev = torch.device("cuda")
+    if kind == "opls":
+        model, pos, z = _butane_model()
+        cutoff = 4.0
+    else:
+        from xnn_b200.models.schnet import SchNet
+        torch.manual_seed(0)
+        model, cutoff = SchNet(n_features=8, n_interactions=2, n_rbf=6, cutoff=3.0), 3.0
+        pos, z = torch.rand(12, 3) * 4.0, torch.tensor([1, 6, 8] * 4)
+    model = model.to(dev)
+    sg = StepGraph(model, skin=1.0, warmup=1)
+    g = torch.Generator().manual_seed(0)
+    for k in range(5):
+        p = (pos + 0.1 * torch.randn(pos.shape, generator=g)).to(dev)
+        out, ref = sg({"pos": p, "atomic_numbers": z.to(dev)}), _direct(model, p, z.to(dev), cutoff)
+        torch.testing.assert_close(out["energy"], ref["energy"].detach(), rtol=1e-9, atol=1e-9)
+        torch.testing.assert_close(out["forces"], ref["forces"].detach(), rtol=1e-9, atol=1e-9)
+    assert sg.captures >= 1 and sg._graphed is not None
+    sg.release()
