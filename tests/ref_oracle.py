@@ -16,22 +16,55 @@ REF = os.path.join(ROOT, "baseline", "_ref")
 
 
 def _stub_e3nn():
-    """The reference's GNN base module imports ``e3nn`` (absent here) for its equivariant models
-    only; an empty stand-in lets its other models import."""
+    """The reference's equivariant models import ``e3nn`` (absent here). It is stood in for by this
+    framework's own ``xnn_b200.o3`` (the same conventions: irreps, real spherical harmonics, Wigner
+    3j, path-normalised linear and tensor-product layers, normalised MLPs), so the reference's
+    models run as oracles for the model logic; names this framework does not provide become
+    placeholder types that refuse to be used."""
     import importlib.util
     import types
     if "e3nn" in sys.modules or importlib.util.find_spec("e3nn") is not None:
         return
+    import xnn_b200.o3 as mine
+
     class _Absent:
         def __init__(self, *args, **kwargs):
             raise ImportError("e3nn is not installed")
 
-    def _attr(name):   # any name: a placeholder type that refuses to be used
+    def _attr(name):
+        if name.startswith("__"):        # module dunders (__file__, __path__, ...) stay absent
+            raise AttributeError(name)
         return type(name, (_Absent,), {})
 
+    class _Entry:
+        # the entry points e3nn's subclasses call
+        def _compiled_main_left_right(self, x, y, w):
+            return mine.TensorProduct.forward(self, x, y, w)
+
+        def _get_weights(self, w):
+            return self.weight if w is None else w
+
+    class TensorProduct(_Entry, mine.TensorProduct):
+        pass
+
+    class FullyConnectedTensorProduct(_Entry, mine.FullyConnectedTensorProduct):
+        pass
+
+    class Linear(mine.Linear):
+        def _compiled_main(self, x, w=None, b=None):
+            return mine.Linear.forward(self, x, w, b)
+
+    provided = {"o3": {k: getattr(mine, k) for k in dir(mine) if not k.startswith("_")},
+                "nn": {"FullyConnectedNet": mine.FullyConnectedNet},
+                "math": {"normalize2mom": mine.normalize2mom}}
+    provided["o3"]["TensorProduct"] = TensorProduct
+    provided["o3"]["Linear"] = Linear
+    provided["o3"]["FullyConnectedTensorProduct"] = FullyConnectedTensorProduct
     pkg = types.ModuleType("e3nn")
     for sub in ("o3", "nn", "math"):
         mod = types.ModuleType("e3nn." + sub)
+        for k, v in provided[sub].items():
+            setattr(mod, k, v)
         mod.__getattr__ = _attr
         setattr(pkg, sub, mod)
         sys.modules["e3nn." + sub] = mod

@@ -353,3 +353,23 @@ def test_spookynet(opts, periodic):
     ng = 2 if periodic else 3
     extra = {"total_charge": torch.tensor([1.0, -1.0, 0.0][:ng]), "spin_multiplicity": torch.tensor([2.0, 1.0, 3.0][:ng])}
     compare(mine, ref, b, periodic, rtol=1e-9, atol=1e-9, keys=("charges", "dipole", "energy_dispersion"), **extra)
+
+
+# the reference's e3nn-based models run on this framework's o3 (see ref_oracle): their model logic
+# against these implementations with one state dict
+@pytest.mark.parametrize("kw", [dict(), dict(l_max=1, n_layers=2, num_features=8, resnet=True)])
+@pytest.mark.parametrize("periodic", [False, True])
+def test_nequip(kw, periodic):
+    from xnn_b200.models.nequip import NequIP
+    mine, ref = _pair("xnn.gnn.models.nequip", "NequIP", NequIP, species=[1, 6, 7, 8], cutoff=4.0, **kw)
+    compare(mine, ref, batch(periodic, cutoff=4.0, species=[1, 6, 7, 8]), periodic, rtol=1e-9, atol=1e-9)
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(hidden_irreps="16x0e+16x1o", max_ell=2, correlation=2, num_interactions=2)])
+@pytest.mark.parametrize("periodic", [False, True])
+def test_mace(kw, periodic):
+    from xnn_b200.models.mace import MACE
+    mine, ref = _pair("xnn.gnn.models.mace", "MACE", MACE, species=[1, 6, 7, 8], cutoff=4.0, **kw)
+    if hasattr(ref, "set_use_fast"):
+        ref.set_use_fast(False)
+    compare(mine, ref, batch(periodic, cutoff=4.0, species=[1, 6, 7, 8]), periodic, rtol=1e-9, atol=1e-9)

@@ -204,7 +204,10 @@ class NequIP(GNNPotential):
         self.l_max = l_max
         self.node_attr_irreps = Irreps([(len(self.species), "0e")])
         self.irreps_sh = Irreps.spherical_harmonics(l_max, p=-1 if parity else 1)
-        self.rbf = BesselRBF(n_rbf, cutoff, trainable=trainable_rbf, prefactor=2.0 / cutoff)
+        # the radial basis sits in ``edge_feat`` as in the reference's shared edge featurizer
+        # (``edge_feat.rbf.freqs`` in the state dict)
+        self.edge_feat = nn.Module()
+        self.edge_feat.rbf = BesselRBF(n_rbf, cutoff, trainable=trainable_rbf, prefactor=2.0 / cutoff)
         self.envelope = PolynomialCutoff(cutoff, p=num_polynomial_cutoff)
         ns = nonlinearity_scalars or {"e": "silu", "o": "tanh"}
         ng = nonlinearity_gates or {"e": "silu", "o": "tanh"}
@@ -232,6 +235,16 @@ class NequIP(GNNPotential):
             self.atom_scale[torch.tensor(self.species)] = sc
         if atomic_energies is not None:
             self.set_atomic_energies(atomic_energies)
+
+    @property
+    def rbf(self) -> nn.Module:
+        return self.edge_feat.rbf
+
+    def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
+        old = prefix + "rbf.freqs"          # the earlier top-level name
+        if old in state_dict:
+            state_dict[prefix + "edge_feat.rbf.freqs"] = state_dict.pop(old)
+        super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
 
     def node_features_energy(self, atomic_numbers: Tensor, edge_index: Tensor, edge_vec: Tensor):
         node_attrs = self.node_attr(atomic_numbers)
