@@ -373,3 +373,19 @@ def test_mace(kw, periodic):
     if hasattr(ref, "set_use_fast"):
         ref.set_use_fast(False)
     compare(mine, ref, batch(periodic, cutoff=4.0, species=[1, 6, 7, 8]), periodic, rtol=1e-9, atol=1e-9)
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(l_max=2, num_layers=3, num_tensor_features=8, parity="o3_restricted",
+                                             avg_num_neighbors=6.0, two_body_latent=[16, 32], latent=[32],
+                                             env_embed=[16], edge_eng=[16]),
+                                dict(parity="so3", latent_resnet=False, num_tensor_features=4)])
+@pytest.mark.parametrize("periodic", [False, True])
+def test_allegro(kw, periodic):
+    from xnn_b200.models.allegro import Allegro
+    mine, ref = _pair("xnn.gnn.models.allegro", "Allegro", Allegro, species=[1, 6, 7, 8], cutoff=4.0, **kw)
+    if hasattr(ref, "set_use_fast"):
+        ref.set_use_fast(False)
+    with torch.no_grad():
+        ref._resnet_params.copy_(torch.linspace(-0.5, 0.5, ref._resnet_params.numel()))
+    load_same_weights(mine, ref)
+    compare(mine, ref, batch(periodic, cutoff=4.0, species=[1, 6, 7, 8]), periodic, rtol=1e-9, atol=1e-9)
