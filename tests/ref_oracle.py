@@ -61,6 +61,9 @@ def _stub_e3nn():
     provided["o3"]["Linear"] = Linear
     provided["o3"]["FullyConnectedTensorProduct"] = FullyConnectedTensorProduct
     pkg = types.ModuleType("e3nn")
+    _opt = {"jit_script_fx": True, "specialized_code": True, "optimize_einsums": True}
+    pkg.get_optimization_defaults = lambda: dict(_opt)
+    pkg.set_optimization_defaults = lambda **kw: _opt.update(kw)
     for sub in ("o3", "nn", "math"):
         mod = types.ModuleType("e3nn." + sub)
         for k, v in provided[sub].items():

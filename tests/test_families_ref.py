@@ -389,3 +389,21 @@ def test_allegro(kw, periodic):
         ref._resnet_params.copy_(torch.linspace(-0.5, 0.5, ref._resnet_params.numel()))
     load_same_weights(mine, ref)
     compare(mine, ref, batch(periodic, cutoff=4.0, species=[1, 6, 7, 8]), periodic, rtol=1e-9, atol=1e-9)
+
+
+_SMALL_EQUIFORMER = dict(irreps_node_embedding="16x0e+8x1e+4x2e", irreps_head="8x0e+4x1e+2x2e", num_heads=2,
+                         irreps_mlp_mid="24x0e+12x1e+6x2e", irreps_feature="32x0e", n_rbf=8, radial_hidden=[16],
+                         n_interactions=2, cutoff=4.0)
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(attention="dot_product", radial_basis="gaussian", rescale_degree=True),
+                                dict(nonlinear_message=False, radial_basis="bessel", smooth_cutoff=True),
+                                dict(irreps_node_embedding="16x0e+4x0o+4x1e+4x1o", irreps_head="8x0e+2x0o+2x1e+2x1o",
+                                     irreps_mlp_mid="24x0e+6x0o+6x1e+6x1o")])
+@pytest.mark.parametrize("periodic", [False, True])
+def test_equiformer(kw, periodic):
+    from xnn_b200.models.equiformer import Equiformer
+    mine, ref = _pair("xnn.trfnn.models.equiformer", "Equiformer", Equiformer, **{**_SMALL_EQUIFORMER, **kw})
+    if hasattr(ref, "set_use_fast"):
+        ref.set_use_fast(False)
+    compare(mine, ref, batch(periodic, cutoff=4.0), periodic, rtol=1e-9, atol=1e-9)

@@ -150,14 +150,15 @@ class Irreps(tuple):
             i += m.dim
         return out
 
-    def sort(self) -> Tuple["Irreps", Tuple[int, ...], Tuple[int, ...]]:
-        """Sorted irreps, the permutation ``p`` (old -> new position) and its inverse."""
+    def sort(self) -> "SortedIrreps":
+        """Sorted irreps, the permutation ``p`` (old -> new position) and its inverse, as a named
+        tuple ``(irreps, p, inv)``."""
         keyed = sorted((m.ir, i, m.mul) for i, m in enumerate(self))
         inv = tuple(i for _, i, _ in keyed)
         p = [0] * len(inv)
         for new, old in enumerate(inv):
             p[old] = new
-        return Irreps([(mul, ir) for ir, _, mul in keyed]), tuple(p), inv
+        return SortedIrreps(Irreps([(mul, ir) for ir, _, mul in keyed]), tuple(p), inv)
 
     def simplify(self) -> "Irreps":
         out: List[Tuple[int, Irrep]] = []
@@ -170,6 +171,14 @@ class Irreps(tuple):
 
     def __add__(self, other) -> "Irreps":  # type: ignore[override]
         return Irreps(tuple(self) + tuple(Irreps(other)))
+
+    def __mul__(self, n) -> "Irreps":  # type: ignore[override]
+        """The list repeated ``n`` times (``2 * "1x0e"`` is ``1x0e+1x0e``)."""
+        if not isinstance(n, int):
+            raise NotImplementedError("Irreps multiply only by an integer")
+        return Irreps(tuple(self) * n)
+
+    __rmul__ = __mul__
 
     def __repr__(self) -> str:
         return "+".join(repr(m) for m in self)
@@ -185,3 +194,9 @@ class Irreps(tuple):
 
     def __hash__(self) -> int:
         return tuple.__hash__(self)
+
+
+class SortedIrreps(NamedTuple):
+    irreps: Irreps
+    p: Tuple[int, ...]
+    inv: Tuple[int, ...]

@@ -115,6 +115,21 @@ class TensorProduct(nn.Module):
             cache[key] = wigner_3j(l1, l2, lo, dtype=like.dtype, device=like.device)
         return cache[key]
 
+    def weight_views(self, weight: Optional[Tensor] = None, yield_instruction: bool = False):
+        """The weights of each weighted instruction as views of shape ``(..., *path_shape)``
+        (the module's own weights by default)."""
+        if weight is None:
+            weight = self.weight
+        batch = weight.shape[:-1]
+        at = 0
+        for ins in self.instructions:
+            if not ins.has_weight:
+                continue
+            n = math.prod(ins.path_shape)
+            view = weight.narrow(-1, at, n).view(batch + tuple(ins.path_shape))
+            at += n
+            yield (ins, view) if yield_instruction else view
+
     def __repr__(self) -> str:
         return (f"TensorProduct({self.irreps_in1} x {self.irreps_in2} -> {self.irreps_out} | "
                 f"{len(self.instructions)} paths | {self.weight_numel} weights)")

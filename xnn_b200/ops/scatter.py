@@ -37,14 +37,19 @@ def structure_sum(values: Tensor, batch: Tensor, num_graphs: int) -> Tensor:
     return out.index_add(0, batch, v)
 
 
-def segment_softmax(logits: Tensor, index: Tensor, n: int) -> Tensor:
-    """Softmax of ``logits`` within the groups given by ``index`` (``n`` groups)."""
+def segment_softmax(logits: Tensor, index: Tensor, n: int, weight: Optional[Tensor] = None) -> Tensor:
+    """Softmax of ``logits`` within the groups given by ``index`` (``n`` groups). With a per-row
+    ``weight`` ``u`` (a cutoff envelope): ``u_r e^{z_r} / (1 + sum_s u_s e^{z_s})`` -- a null key of
+    logit zero lets the last row of a group fade out continuously (the Equiformers' smooth form)."""
     shape = (n,) + tuple(logits.shape[1:])
     idx = index.view((-1,) + (1,) * (logits.dim() - 1)).expand_as(logits)
-    mx = logits.new_full(shape, float("-inf")).scatter_reduce(0, idx, logits, "amax", include_self=True)
-    e = torch.exp(logits - mx.index_select(0, index))
-    s = scatter_sum(e, index, n)
-    return e / s.index_select(0, index).clamp_min(1e-30)
+    mx = logits.new_full(shape, float("-inf")).scatter_reduce(0, idx, logits.detach(), "amax", include_self=True)
+    if weight is None:
+        e = torch.exp(logits - mx.index_select(0, index))
+        return e / (scatter_sum(e, index, n) + 1e-16).index_select(0, index)
+    mx = mx.clamp(min=0.0)
+    e = torch.exp(logits - mx.index_select(0, index)) * weight.view((-1,) + (1,) * (logits.dim() - 1))
+    return e / (scatter_sum(e, index, n) + torch.exp(-mx)).index_select(0, index)
 
 
 def cell_volume(cell: Tensor) -> Tensor:
