@@ -25,10 +25,10 @@ def _butane_model(cutoff=4.0):
 
 
 def _direct(model, pos, z, cutoff, cell=None):
-    s = {"pos": pos, "atomic_numbers": z}
+    s = {"pos": pos.detach().cpu(), "atomic_numbers": z.cpu()}
     if cell is not None:
-        s["cell"], s["pbc"] = cell, torch.tensor([True, True, True])
-    return ForceStressOutput(model)(collate([structure_to_graph(s, cutoff)]))
+        s["cell"], s["pbc"] = cell.cpu(), torch.tensor([True, True, True])
+    return ForceStressOutput(model)(collate([structure_to_graph(s, cutoff)]).to(pos.device))
 
 
 @pytest.mark.parametrize("periodic", [False, True])
