@@ -170,3 +170,28 @@ def test_d4_matches_reference_for_molecules(s9):
     fa, = torch.autograd.grad(a["node_energy"].sum(), pos, retain_graph=True)
     fr, = torch.autograd.grad(r["node_energy"].sum(), pos)
     torch.testing.assert_close(fa, fr, rtol=1e-8, atol=1e-11)
+
+
+@pytest.mark.parametrize("s9", [0.0, 1.0])
+def test_d4_matches_reference_for_crystals(s9):
+    ref_d4 = _reference("xnn.common.models.d4")
+    from xnn_b200.data import collate
+    from xnn_b200.models.d4 import DFTD4
+    from xnn_b200.models.outputs import ForceStressOutput
+    xs = synthetic.triclinic_crystals(2, seed=5, labels=False)
+    for s, z in zip(xs, ([8, 1], [6, 7, 1])):
+        s["atomic_numbers"] = torch.as_tensor(z)[torch.arange(len(s["atomic_numbers"])) % len(z)]
+    cut = 7.0
+    b = collate([structure_to_graph(s, cut) for s in xs])
+    opts = dict(s9=s9, cutoff_pair=cut, cutoff_triple=5.0, cutoff_cn=cut, cutoff_eeq_cn=cut)
+    mine, theirs = DFTD4(**opts), ref_d4.DFTD4(regime="dense", **opts)
+    args = lambda pos: (b.atomic_numbers, pos, b.edge_index, pos[b.edge_index[1]] - pos[b.edge_index[0]]  # noqa: E731
+                        + b.cell_shifts.to(pos.dtype).unsqueeze(-1).mul(b.cell[b.batch[b.edge_index[0]]]).sum(1),
+                        b.batch, 2, b.cell, b.pbc, torch.tensor([0.0, 0.0]))
+    pos = b.pos.clone().requires_grad_(True)
+    a, r = mine.evaluate(*args(pos)), theirs.evaluate(*args(pos))
+    torch.testing.assert_close(a["charges"], r["charges"], rtol=1e-9, atol=1e-11)
+    torch.testing.assert_close(a["node_energy"], r["node_energy"], rtol=1e-9, atol=1e-11)
+    fa, = torch.autograd.grad(a["node_energy"].sum(), pos, retain_graph=True)
+    fr, = torch.autograd.grad(r["node_energy"].sum(), pos)
+    torch.testing.assert_close(fa, fr, rtol=1e-8, atol=1e-10)

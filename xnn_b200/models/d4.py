@@ -11,14 +11,14 @@ polarizabilities (ga = 3, gc = 2), the 23-point Casimir-Polder trapezoid grid, a
 from neutral (q = 0) polarizabilities. Reference data: the published D4 tables
 (``d4_reference.npz``, see :mod:`xnn_b200.models.dispersion`).
 
-Built: the dense regime for isolated structures (molecules; a batch of them). Not built: the
-periodic Ewald EEQ, the large-system iterative EEQ and the tail correction (a periodic structure
-raises ``NotImplementedError``).
+Built: the dense regime for isolated and periodic structures (the periodic EEQ Coulomb matrix from
+Wigner-Seitz images and Ewald sums with the dftd4 splitting rule). Not built: the large-system
+iterative EEQ and the lattice tail correction.
 """
 from __future__ import annotations
 
 import math
-from typing import Dict
+from typing import Dict, Optional
 
 import numpy as np
 import torch
@@ -37,6 +37,48 @@ FREQ = [0.000001, 0.05, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 1.0, 1.2, 1
         5.0, 7.5, 10.0]
 CP_WEIGHTS = [0.5 * ((FREQ[k] - FREQ[k - 1] if k > 0 else 0.0) + (FREQ[k + 1] - FREQ[k] if k < len(FREQ) - 1 else 0.0))
               for k in range(len(FREQ))]
+
+
+WS_TOL = 0.01          # bohr^2: images within this of the nearest count as equivalent
+EWALD_REP = 2          # +-2 real and reciprocal lattice windows of the periodic EEQ
+
+
+def _ewald_balance(alpha: float, rlen: float, dlen: float, vol: float) -> float:
+    rec = lambda g: 4.0 * math.pi * math.exp(-0.25 * g * g / (alpha * alpha)) / (vol * g * g)  # noqa: E731
+    direct = lambda r: math.erfc(alpha * r) / r  # noqa: E731
+    return (rec(4.0 * rlen) - rec(5.0 * rlen)) - (direct(2.0 * dlen) - direct(3.0 * dlen))
+
+
+def ewald_alpha(rlen: float, dlen: float, vol: float) -> float:
+    """The Ewald splitting parameter of the periodic EEQ (the dftd4 rule): the ``alpha`` at which the
+    last real-space and reciprocal-space shells of the +-2 windows carry equal weight, bracketed by
+    doubling from 1e-8 and bisected to sqrt(float32 eps); 0.25 when no bracket is found."""
+    tol = 1.4901161193847656e-08
+    alpha = 1.0e-8
+    d = _ewald_balance(alpha, rlen, dlen, vol)
+    n = 0
+    while d < -tol and n < 2000:
+        alpha *= 2.0
+        d = _ewald_balance(alpha, rlen, dlen, vol)
+        n += 1
+    if n == 0 or n >= 2000:
+        return 0.25
+    left, n = 0.5 * alpha, 0
+    while d < tol and n < 2000:
+        alpha *= 2.0
+        d = _ewald_balance(alpha, rlen, dlen, vol)
+        n += 1
+    if n >= 2000:
+        return 0.25
+    right = alpha
+    alpha = 0.5 * (left + right)
+    d, n = _ewald_balance(alpha, rlen, dlen, vol), 0
+    while abs(d) > tol and n <= 30:
+        left, right = (alpha, right) if d < 0.0 else (left, alpha)
+        alpha = 0.5 * (left + right)
+        d = _ewald_balance(alpha, rlen, dlen, vol)
+        n += 1
+    return 0.25 if n > 30 else alpha
 
 
 def _zeta(a: float, c, qref, qmod):
@@ -114,17 +156,61 @@ class DFTD4(nn.Module):
         cn_eeq = math.log(1.0 + math.exp(EEQ_CN_MAX)) - torch.log(1.0 + torch.exp(EEQ_CN_MAX - raw))
         return cn_d4, cn_eeq
 
-    def eeq_charges(self, z, pos, cn_eeq, total_charge) -> Tensor:
-        """EEQ charges of one isolated structure (positions in bohr)."""
-        n = pos.shape[0]
+    def coulomb_matrix_periodic(self, z: Tensor, pos: Tensor, cell: Tensor) -> Tensor:
+        """The EEQ Coulomb matrix of a periodic structure (bohr): for every pair the Wigner-Seitz
+        images (the nearest of the 27 neighbouring cells, ties within ``WS_TOL`` shared equally),
+        each an Ewald sum of the Gaussian-charge kernel over +-2 real and reciprocal windows; the
+        diagonal carries the hardness, the self term and the ``-2 alpha / sqrt(pi)`` correction."""
+        n, dev, dt = pos.shape[0], pos.device, pos.dtype
+        vol = torch.linalg.det(cell).abs()
+        recip = 2.0 * math.pi * torch.linalg.inv(cell).t()
+        alpha = ewald_alpha(float(torch.linalg.norm(recip, dim=1).min()), float(torch.linalg.norm(cell, dim=1).min()),
+                            float(vol))
+        one = torch.arange(-1, 2, device=dev)
+        t27 = torch.cartesian_prod(one, one, one).to(dt) @ cell
+        two = torch.arange(-EWALD_REP, EWALD_REP + 1, device=dev)
+        grid = torch.cartesian_prod(two, two, two)
+        t125 = grid.to(dt) @ cell
+        g = grid[(grid != 0).any(1)].to(dt) @ recip
+        g2 = (g * g).sum(-1)
+        g_fac = 4.0 * math.pi / vol * torch.exp(-0.25 * g2 / (alpha * alpha)) / g2
         rad2 = self.eeq_rad[z] ** 2
         gamma = torch.rsqrt(rad2[:, None] + rad2[None, :])
-        eye = torch.eye(n, dtype=torch.bool, device=pos.device)
-        dvec = pos[None, :, :] - pos[:, None, :]
-        r2 = (dvec * dvec).sum(-1)
-        r = torch.sqrt(torch.where(eye, torch.ones_like(r2), r2))
-        A = torch.where(eye, torch.zeros_like(r), torch.erf(gamma * r) / r)
-        A = A + torch.diag(self.eeq_eta[z] + math.sqrt(2.0 / math.pi) / self.eeq_rad[z])
+        d = pos[None, :, :] - pos[:, None, :]
+        d = d - torch.round(d.detach() @ torch.linalg.inv(cell.detach())) @ cell
+        d_img = d[:, :, None, :] + t27[None, None]
+        r2 = (d_img * d_img).sum(-1)
+        thr = 1.4901161193847656e-08
+        r2 = torch.where(r2 < thr, torch.full_like(r2, math.inf), r2)
+        sel = (r2 - r2.min(-1, keepdim=True).values) <= WS_TOL
+        n_img = sel.sum(-1).to(dt)
+        ii, jj, kk = torch.nonzero(sel).unbind(1)
+        vec = d_img[ii, jj, kk]
+        vt = vec[:, None, :] + t125[None]
+        r2t = (vt * vt).sum(-1)
+        keep = r2t >= thr * thr
+        rs = torch.sqrt(torch.where(keep, r2t, torch.ones_like(r2t)))
+        kern = (torch.erf(gamma[ii, jj][:, None] * rs) - torch.erf(alpha * rs)) / rs
+        a_dir = torch.where(keep, kern, torch.zeros_like(kern)).sum(-1)
+        a_rec = (torch.cos(vec @ g.t()) * g_fac[None]).sum(-1)
+        A = scatter_sum((a_dir + a_rec) / n_img[ii, jj], ii * n + jj, n * n).view(n, n)
+        return A + torch.diag(self.eeq_eta[z] + math.sqrt(2.0 / math.pi) / self.eeq_rad[z]
+                              - 2.0 * alpha / math.sqrt(math.pi))
+
+    def eeq_charges(self, z, pos, cn_eeq, total_charge, cell: Optional[Tensor] = None) -> Tensor:
+        """EEQ charges of one structure (positions and cell in bohr); ``cell`` for a periodic one."""
+        n = pos.shape[0]
+        if cell is not None:
+            A = self.coulomb_matrix_periodic(z, pos, cell)
+        else:
+            rad2 = self.eeq_rad[z] ** 2
+            gamma = torch.rsqrt(rad2[:, None] + rad2[None, :])
+            eye = torch.eye(n, dtype=torch.bool, device=pos.device)
+            dvec = pos[None, :, :] - pos[:, None, :]
+            r2 = (dvec * dvec).sum(-1)
+            r = torch.sqrt(torch.where(eye, torch.ones_like(r2), r2))
+            A = torch.where(eye, torch.zeros_like(r), torch.erf(gamma * r) / r)
+            A = A + torch.diag(self.eeq_eta[z] + math.sqrt(2.0 / math.pi) / self.eeq_rad[z])
         x = -self.eeq_chi[z] + self.eeq_kcnchi[z] * cn_eeq / torch.sqrt(cn_eeq + EEQ_CN_REG)
         ones = torch.ones((n, 1), dtype=pos.dtype, device=pos.device)
         zero = torch.zeros((1, 1), dtype=pos.dtype, device=pos.device)
@@ -174,9 +260,7 @@ class DFTD4(nn.Module):
         n = z.shape[0]
         if bool((z > MAX_Z).any()) or bool((z < 1).any()):
             raise ValueError("D4 with EEQ charges supports atomic numbers 1..103")
-        periodic = pbc.any(-1) & (cell.abs().sum((-1, -2)) > 1e-8)
-        if bool(periodic.any()):
-            raise NotImplementedError("D4 for periodic structures (Ewald EEQ) is not built; use D3")
+        periodic = (pbc.any(-1) & (cell.abs().sum((-1, -2)) > 1e-8)).tolist()
         pos_au = pos / BOHR
         vec = edge_vec / BOHR
         r = torch.linalg.norm(vec, dim=-1)
@@ -184,7 +268,8 @@ class DFTD4(nn.Module):
         q = torch.zeros_like(cn_d4)
         for b in range(num_graphs):
             m = torch.nonzero(batch == b).squeeze(1)
-            q = q.index_put((m,), self.eeq_charges(z[m], pos_au[m], cn_eeq[m], total_charge[b]))
+            q = q.index_put((m,), self.eeq_charges(z[m], pos_au[m], cn_eeq[m], total_charge[b],
+                                                   cell[b] / BOHR if periodic[b] else None))
         alpha_iw = self.dynamic_polarizabilities(z, self.gaussian_weights(z, cn_d4) * self.charge_scaling(z, q))
         in_pair = r <= self.cutoff_pair / BOHR
         e2 = self.two_body_energy(z, edge_index[:, in_pair], r[in_pair], alpha_iw, n)
