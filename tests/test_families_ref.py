@@ -407,3 +407,21 @@ def test_equiformer(kw, periodic):
     if hasattr(ref, "set_use_fast"):
         ref.set_use_fast(False)
     compare(mine, ref, batch(periodic, cutoff=4.0), periodic, rtol=1e-9, atol=1e-9)
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(normalization="batch", fields=[[4, 2, 1], [3, 2], [6]], strides=[1, 2, 1],
+                                             bandlimit="conservative", activation="relu")])
+@pytest.mark.parametrize("train", [False, True])
+def test_se3cnn(kw, train):
+    from xnn_b200.models.se3cnn import SteerableCNN
+    mine, ref = _pair("xnn.cnn.models.steerable", "SteerableCNN", SteerableCNN, species=[1, 6, 7, 8], cutoff=3.5,
+                      grid_size=9, n_features=6, n_blocks=3, l_max=2, kernel_size=3, atomic_energies=[-1.0, -2, -3, -4],
+                      **kw)
+    with torch.no_grad():
+        ref.readout[-1].weight.uniform_(-0.5, 0.5)
+    load_same_weights(mine, ref)
+    if hasattr(ref, "set_use_fast"):
+        ref.set_use_fast(False)
+    mine.train(train)
+    ref.train(train)
+    compare(mine, ref, batch(False, cutoff=3.5, species=[1, 6, 7, 8]), rtol=1e-9, atol=1e-9)

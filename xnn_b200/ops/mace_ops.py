@@ -93,7 +93,7 @@ def edge_features_torch(vec: Tensor, lmax: int, freqs: Tensor, norm: float, rc: 
                         ) -> Tuple[Tensor, Tensor]:
     """Reference formulas of :func:`edge_geometry` in PyTorch operations."""
     from ..o3 import spherical_harmonics
-    Y = spherical_harmonics(lmax, vec, normalize=True, normalization="component")
+    Y = spherical_harmonics(list(range(lmax + 1)), vec, normalize=True, normalization="component")
     r = torch.linalg.norm(vec, dim=-1)
     rcl = r.clamp(min=1e-8)[:, None]
     bessel = norm * torch.sin(freqs * rcl / rc) / rcl
