@@ -425,3 +425,21 @@ def test_se3cnn(kw, train):
     mine.train(train)
     ref.train(train)
     compare(mine, ref, batch(False, cutoff=3.5, species=[1, 6, 7, 8]), rtol=1e-9, atol=1e-9)
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(normalization=None, set_readout=[6, 4, 6], cutoff_fn="cosine", exponent=2.0)])
+@pytest.mark.parametrize("train", [False, True])
+def test_s2cnn(kw, train):
+    from xnn_b200.models.s2cnn import SphericalCNN
+    mine, ref = _pair("xnn.cnn.models.spherical", "SphericalCNN", SphericalCNN, species=[1, 6, 7, 8], cutoff=3.5,
+                      bandwidth=4, features=[3, 5], bandwidths=[4, 2], n_beta=1, n_gamma=2,
+                      atomic_energies=[-1.0, -2, -3, -4], **kw)
+    with torch.no_grad():
+        for m in (ref.readout, ref.set_readout["psi"] if ref.set_readout is not None else ref.readout):
+            m[-1].weight.uniform_(-0.5, 0.5)
+    load_same_weights(mine, ref)
+    if hasattr(ref, "set_use_fast"):
+        ref.set_use_fast(False)
+    mine.train(train)
+    ref.train(train)
+    compare(mine, ref, batch(False, cutoff=3.5, species=[1, 6, 7, 8]), rtol=1e-8, atol=1e-9)
