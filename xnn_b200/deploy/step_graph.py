@@ -104,7 +104,9 @@ class StepGraph:
 
     # ------------------------------------------------------------------------------ evaluation
     def _want_capture(self, dev) -> bool:
-        return (dev.type == "cuda") if self.capture is None else bool(self.capture)
+        if self.capture is not None:
+            return bool(self.capture)
+        return dev.type == "cuda" and bool(getattr(_core(self.model), "graph_capturable", True))
 
     def __call__(self, struct: dict) -> Dict[str, Tensor]:
         pos = struct["pos"]

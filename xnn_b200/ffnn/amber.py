@@ -376,6 +376,7 @@ class Amber(FixedTopologyPotential):
                  else (None if constrain_charge is False else float(constrain_charge)))
         self.register_buffer("charge_total", torch.tensor(float("nan") if total is None else total,
                                                           dtype=self.charge.dtype), persistent=False)
+        self._hold_total = total is not None      # a host flag: no device read per evaluation
 
     def _bind(self, top: MolecularTopology) -> None:
         self.topology, ff, missing = top, self.ff, []
@@ -436,7 +437,7 @@ class Amber(FixedTopologyPotential):
     def charges(self) -> Tensor:
         """Per-atom charges shifted uniformly onto the held total."""
         q = self.charge
-        if bool(torch.isnan(self.charge_total)):
+        if not self._hold_total:
             return q
         return q - (q.sum() - self.charge_total) / q.shape[0]
 

@@ -340,6 +340,11 @@ class Dreiding(FixedTopologyPotential):
         else:
             self.register_buffer("charge", q)
 
+    @property
+    def graph_capturable(self) -> bool:
+        # the hydrogen-bond triplets are selected from the list by their distances (data-dependent shapes)
+        return not (self.use_hbond and self.hbond_hydrogens.shape[1] > 0)
+
     def forward(self, data: AtomicGraph) -> dict:
         N, B, n = self._check_batch(data)
         P, ff = self.ff.params, self.ff

@@ -37,7 +37,8 @@ def image_shifts(vec: Tensor, lattice: Tensor, pbc: Optional[Tensor]) -> Tensor:
         shift = shift * flags
     gram = lattice @ lattice.T
     off = gram - torch.diag(torch.diagonal(gram))
-    if bool((off.abs() > ORTHOGONAL_TOL * gram.abs().amax()).any()):
+    # inside a CUDA-graph capture the 27-image search always runs (no host read of the skew test)
+    if _capturing(vec) or bool((off.abs() > ORTHOGONAL_TOL * gram.abs().amax()).any()):
         one = torch.arange(-1, 2, device=vec.device)
         offs = torch.cartesian_prod(one, one, one).to(vec.dtype)
         if flags is not None:
@@ -127,10 +128,21 @@ def excluded(i: Tensor, k: Tensor, excl_index: Tensor, n: int, b: int, cache: di
     return keys.index_select(0, at) == key
 
 
+def _capturing(t: Tensor) -> bool:
+    return t.is_cuda and torch.cuda.is_current_stream_capturing()
+
+
 def half_edges(data, excl_index: Tensor, n: int, cache: dict):
     """The neighbour list's pairs once each (``src <= dst``): ``src, dst``, the vectors, squared
-    lengths, weights (half for an atom's own image) and whether each pair is not excluded."""
+    lengths, weights (half for an atom's own image) and whether each pair is not excluded. Inside
+    a CUDA-graph capture every directed edge is kept at weight one half instead (the same sum with
+    shapes that do not depend on the data)."""
     src, dst = data.edge_index[0], data.edge_index[1]
+    if _capturing(src):
+        vec = pair_vectors(data, src, dst, None if data.cell is None else data.cell_shifts)
+        r2 = (vec * vec).sum(1)
+        half = torch.full_like(r2, 0.5)
+        return src, dst, vec, r2, half, ~excluded(src, dst, excl_index, n, data.num_graphs, cache)
     once = (src <= dst).nonzero()[:, 0]
     src, dst = src[once], dst[once]
     vec = pair_vectors(data, src, dst, None if data.cell is None else data.cell_shifts[once])

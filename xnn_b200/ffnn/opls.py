@@ -349,8 +349,13 @@ class FixedTopologyPotential(InteratomicPotential):
     topology, batch checks (conformers of that system), per-element reference energies and the
     once-per-pair nonbonded sum with exclusions and the quintic switch."""
 
+    #: whether one evaluation can be recorded as a CUDA graph (no host reads, fixed shapes)
+    graph_capturable = True
+
     def _check_batch(self, data: AtomicGraph) -> tuple:
         n = int(self.top_type.shape[0])
+        if data.pos.is_cuda and torch.cuda.is_current_stream_capturing():
+            return data.num_nodes, data.num_graphs, n          # checked when the graph was recorded
         if not bool((data.n_atoms == n).all()):
             raise ValueError(f"every structure must have the bound topology's {n} atoms (got {data.n_atoms.tolist()})")
         if not bool((data.atomic_numbers == self.top_z.repeat(data.num_graphs)).all()):
