@@ -239,3 +239,29 @@ def test_dreiding_matches_reference(case):
         torch.testing.assert_close(o[k], o_ref[k], rtol=1e-10, atol=1e-10, msg=k)
     key = "e_hbond" if case.startswith("water") else "e_torsion"
     assert float(o[key].detach().abs().sum()) > 0
+
+
+@pytest.mark.parametrize("kind", ["opls", "amber"])
+def test_lammps_input_matches_reference(kind, tmp_path):
+    rl = ref_module("xnn.ffnn.models.lammps_input")
+    rt = ref_module("xnn.ffnn.models.topology")
+    from xnn_b200.ffnn.lammps_input import lammps_input, write_lammps_input
+    from xnn_b200.ffnn.topology import MolecularTopology
+    if kind == "opls":
+        ro = ref_module("xnn.ffnn.models.opls")
+        from xnn_b200.ffnn.opls import OPLS
+        pos, z, types, bonds = _butane()
+        mine = OPLS("oplsaa", MolecularTopology.from_bonds(types, bonds), cutoff=9.0)
+        ref = ro.OPLS("oplsaa", rt.MolecularTopology.from_bonds(types, bonds), cutoff=9.0, use_fast=False)
+        cell = None
+    else:
+        ra = ref_module("xnn.ffnn.models.amber")
+        from xnn_b200.ffnn.amber import Amber
+        pos, z, types, bonds, q = _nma()
+        mine = Amber("ff94", MolecularTopology.from_bonds(types, bonds, charges=q), cutoff=4.0)
+        ref = ra.Amber("ff94", rt.MolecularTopology.from_bonds(types, bonds, charges=q), cutoff=4.0, use_fast=False)
+        cell = [[10.0, 0, 0], [0, 9.0, 0], [0, 0, 9.5]]
+    data, cmds, off = lammps_input(mine, torch.tensor(pos), cell)
+    rdata, rcmds, roff, _files = rl.lammps_input(ref, torch.tensor(pos), cell)
+    assert data == rdata and cmds == rcmds and off == roff
+    assert write_lammps_input(mine, torch.tensor(pos), cell, tmp_path).read_text().count("_coeff") > 5
