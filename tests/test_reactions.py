@@ -29,3 +29,19 @@ def test_reaction_losses_match_reference():
         assert [s["name"] for s in sub_a.structures] == [s["name"] for s in sub_b.structures]
         torch.testing.assert_close(sub_a.stoichiometry(), sub_b.stoichiometry())
     assert sum(len(x) for x in ReactionSet.from_gmtkn55(data).batches(2)) == 3
+
+
+def test_trainer_with_reaction_term(tmp_path):
+    from xnn_b200.config import from_dict
+    from xnn_b200.data import AtomicDataset
+    from xnn_b200.train import Trainer
+    from xnn_b200.train.reactions import ReactionSet
+    cfg = from_dict({"model": {"name": "schnet", "cutoff": 4.0, "n_features": 8, "n_interactions": 1, "n_rbf": 6},
+                     "optim": {"epochs": 2, "lr": 1e-3, "reaction_weight": 0.5, "reaction_batch_size": 2},
+                     "data": {"batch_size": 4}, "output_dir": str(tmp_path), "device": "cpu",
+                     "trainer": {"loggers": []}})
+    ds = AtomicDataset(synthetic.organic_molecules(12, seed=4), 4.0)
+    rs = ReactionSet.from_gmtkn55(_data())
+    tr = Trainer(cfg, ds, reactions=rs, val_reactions=rs)
+    metrics = tr.fit()
+    assert "val/reaction_mae" in metrics and metrics["val/reaction_mae"] > 0

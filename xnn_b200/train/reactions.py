@@ -123,8 +123,11 @@ class ReactionSet:
     def species_energies(self, model: torch.nn.Module, cutoff: float, batch_size: int = 32,
                          device: Optional[torch.device] = None) -> Tensor:
         gs, out = self.graphs(cutoff), []
+        p = next(model.parameters(), None)
         for s in range(0, len(gs), batch_size):
             b = collate(gs[s:s + batch_size])
+            if p is not None and b.pos.dtype != p.dtype:
+                b.compute_dtype = p.dtype          # float64 geometry driving the model's dtype
             out.append(model(b.to(device) if device is not None else b)["energy"].reshape(-1))
         return torch.cat(out) if out else torch.zeros(0, dtype=torch.float64)
 

@@ -87,7 +87,8 @@ class _Subset(torch.utils.data.Dataset):
 
 class Trainer:
     def __init__(self, cfg, train, val=None, test=None, model: Optional[nn.Module] = None,
-                 replay_set=None, callbacks: Optional[list] = None, loggers: Optional[list] = None):
+                 replay_set=None, callbacks: Optional[list] = None, loggers: Optional[list] = None,
+                 reactions=None, val_reactions=None):
         self.cfg = cfg
         dev_req = cfg.device
         self.device = D.init_process_group(None if dev_req == "auto" else dev_req)
@@ -137,6 +138,7 @@ class Trainer:
         from .loggers import make_loggers
         self.loggers = loggers if loggers is not None else (make_loggers(cfg) if D.is_main() else [])
         self._graphed: Optional[GraphedStep] = None
+        self._setup_reactions(reactions, val_reactions)
         self._padder: Optional[PaddedCollate] = None
         self.epoch = 0
         self.global_step = 0
@@ -170,6 +172,39 @@ class Trainer:
             train = _Subset(train, parts[-1])
         return train, val, test
 
+    # ------------------------------------------------------------------ reactions
+    def _setup_reactions(self, reactions, val_reactions) -> None:
+        """Reaction sets (``xnn_b200.train.reactions.ReactionSet``): with ``optim.reaction_weight > 0``
+        each step adds the loss of ``optim.reaction_batch_size`` reactions, drawn in turn from a
+        shuffled order; ``val_reactions`` are scored at every validation."""
+        o = self.cfg.optim
+        self.reactions, self.val_reactions, self._reaction_batches = reactions, val_reactions, None
+        if o.reaction_weight > 0:
+            if reactions is None or len(reactions) == 0:
+                raise ValueError("optim.reaction_weight > 0 needs reactions (a ReactionSet)")
+            if self.use_graphs or self.world > 1:
+                raise ValueError("the reaction-energy term runs in ordinary single-process steps "
+                                 "(trainer.cuda_graph off, one process)")
+            if o.reaction_batch_size < 1:
+                raise ValueError(f"optim.reaction_batch_size must be positive, got {o.reaction_batch_size}")
+
+    def _next_reactions(self):
+        if self._reaction_batches is None:
+            def endless():
+                epoch = 0
+                while True:
+                    yield from self.reactions.batches(self.cfg.optim.reaction_batch_size, True, self.cfg.seed + epoch)
+                    epoch += 1
+            self._reaction_batches = endless()
+        return next(self._reaction_batches)
+
+    def _reaction_loss(self, rs) -> Tensor:
+        o = self.cfg.optim
+        base = self.module.model
+        e = rs.species_energies(base, float(self.cfg.model.cutoff), device=self.device)
+        delta = o.huber_delta if o.huber_delta_reactions is None else o.huber_delta_reactions
+        return rs.loss(e, delta)
+
     # ------------------------------------------------------------------ step
     def _loss(self, batch: AtomicGraph):
         o = self.cfg.optim
@@ -181,6 +216,10 @@ class Trainer:
                                    huber_delta=o.huber_delta, huber_delta_energy=o.huber_delta_energy,
                                    huber_delta_forces=o.huber_delta_forces,
                                    huber_delta_stress=o.huber_delta_stress)
+        if o.reaction_weight > 0 and self.module.training and self.reactions is not None and not self.use_graphs:
+            r = self._reaction_loss(self._next_reactions())
+            loss = loss + o.reaction_weight * r.to(loss.dtype)
+            logs = dict(logs, reaction=r.detach())
         return loss, logs, out
 
     def _train_step_impl(self, batch: AtomicGraph):
@@ -301,6 +340,14 @@ class Trainer:
         D.all_reduce_sum(vec)
         vals = vec.tolist()
         res = {f"{prefix}/loss": vals[0] / max(vals[1], 1.0)}
+        if prefix == "val" and self.val_reactions is not None and len(self.val_reactions):
+            with torch.no_grad():
+                e = self.val_reactions.species_energies(self.module.model, float(self.cfg.model.cutoff),
+                                                        device=self.device)
+                err = self.val_reactions.errors(e)
+                res["val/reaction_mae"] = float(err.abs().mean())
+                res["val/reaction_rmse"] = float(err.pow(2).mean().sqrt())
+                res["val/reaction_mse"] = float(self.val_reactions.loss(e))
         got = dict(zip(keys, vals[2:]))
         for q in ("energy", "forces", "stress"):
             if f"{q}_n" in got and got[f"{q}_n"] > 0:
