@@ -443,3 +443,25 @@ def test_s2cnn(kw, train):
     mine.train(train)
     ref.train(train)
     compare(mine, ref, batch(False, cutoff=3.5, species=[1, 6, 7, 8]), rtol=1e-8, atol=1e-9)
+
+
+_SMALL_EQV2 = dict(n_features=8, n_interactions=2, cutoff=4.0, n_rbf=8, l_max=2, m_max=2, num_heads=2,
+                   attn_hidden_channels=6, attn_alpha_channels=4, attn_value_channels=3, ffn_hidden_channels=8,
+                   edge_channels=8, grid_resolution=8, species=[1, 6, 7, 8], atomic_energies=[-1.0, -2, -3, -4])
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(activation="gate", norm_type="layer_norm", use_grid_mlp=False),
+                                dict(l_max=3, m_max=1, activation="s2", norm_type="rms_norm_sh", grid_resolution=None,
+                                     use_m_share_rad=True, use_attn_renorm=False),
+                                dict(share_atom_edge_embedding=True, smooth_cutoff=True, activation="sep_s2",
+                                     use_grid_mlp=False),
+                                dict(direct_forces=True, m_max=1)])
+@pytest.mark.parametrize("periodic", [False, True])
+def test_equiformer_v2(kw, periodic):
+    from xnn_b200.models.equiformer_v2 import EquiformerV2
+    cfg = {**_SMALL_EQV2, **kw}
+    mine, ref = _pair("xnn.trfnn.models.equiformer_v2", "EquiformerV2", EquiformerV2, **cfg)
+    if hasattr(ref, "set_use_fast"):
+        ref.set_use_fast(False)
+    compare(mine, ref, batch(periodic and not cfg.get("direct_forces"), cutoff=4.0, species=[1, 6, 7, 8]),
+            periodic and not cfg.get("direct_forces"), rtol=1e-9, atol=1e-9)

@@ -4,10 +4,11 @@ equivariant models on e3nn, ``src/xnn/gnn/models/blocks.py``)."""
 from ._fcnet import FullyConnectedNet, normalize2mom
 from ._irreps import Irrep, Irreps, MulIr
 from ._linear import Linear
+from ._s2grid import FromS2Grid, ToS2Grid
 from ._sh import SphericalHarmonics, spherical_harmonics
 from ._tp import FullyConnectedTensorProduct, Instruction, TensorProduct
 from ._wigner import su2_clebsch_gordan, wigner_3j
 
 __all__ = ["FullyConnectedNet", "FullyConnectedTensorProduct", "Instruction", "Irrep", "Irreps",
-           "Linear", "MulIr", "SphericalHarmonics", "TensorProduct", "normalize2mom",
+           "FromS2Grid", "Linear", "MulIr", "SphericalHarmonics", "TensorProduct", "ToS2Grid", "normalize2mom",
            "spherical_harmonics", "su2_clebsch_gordan", "wigner_3j"]
