@@ -265,3 +265,41 @@ def test_lammps_input_matches_reference(kind, tmp_path):
     rdata, rcmds, roff, _files = rl.lammps_input(ref, torch.tensor(pos), cell)
     assert data == rdata and cmds == rcmds and off == roff
     assert write_lammps_input(mine, torch.tensor(pos), cell, tmp_path).read_text().count("_coeff") > 5
+
+
+@pytest.mark.parametrize("case", ["charmm", "dreiding_water", "dreiding_x6_morse"])
+def test_lammps_input_charmm_dreiding(case, tmp_path):
+    rl = ref_module("xnn.ffnn.models.lammps_input")
+    rt = ref_module("xnn.ffnn.models.topology")
+    from xnn_b200.ffnn.lammps_input import lammps_input, write_lammps_input
+    from xnn_b200.ffnn.topology import MolecularTopology
+    if case == "charmm":
+        rc = ref_module("xnn.ffnn.models.charmm")
+        from xnn_b200.ffnn.charmm import Charmm
+        pos, z, _types, bonds, _q = _nma()
+        types = ["CT3", "C", "O", "NH1", "CT3", "H", "HA", "HA", "HA", "HA", "HA", "HA"]
+        q = [-0.27, 0.51, -0.51, -0.47, -0.11, 0.31, 0.09, 0.09, 0.09, 0.09, 0.09, 0.09]
+        imps = [(1, 0, 3, 2), (3, 1, 4, 5)]
+        mine = Charmm("charmm22", MolecularTopology.from_bonds(types, bonds, charges=q, impropers=imps), cutoff=8.0)
+        ref = rc.Charmm("charmm22", rt.MolecularTopology.from_bonds(types, bonds, charges=q, impropers=imps),
+                        cutoff=8.0, use_fast=False)
+        cell = None
+    else:
+        rd = ref_module("xnn.ffnn.models.dreiding")
+        from xnn_b200.ffnn.dreiding import Dreiding
+        if case == "dreiding_water":
+            pos, z, types, bonds = _water_dimer()
+            orders, q, kw, ffield = [1.0] * 4, [-0.8, 0.4, 0.4, -0.8, 0.4, 0.4], {}, "dreiding"
+            cell = [[8.0, 0, 0], [0, 7.5, 0], [0, 0, 7.0]]
+        else:
+            pos, z, types, bonds = _propene()
+            orders, q, ffield = [2.0] + [1.0] * 7, None, "dreiding/X6"
+            kw, cell = dict(bond_style="morse", angle_style="harmonic"), None
+        mine = Dreiding(ffield, MolecularTopology.from_bonds(types, bonds, bond_orders=orders), cutoff=3.5, charges=q,
+                        **kw)
+        ref = rd.Dreiding(ffield, rt.MolecularTopology.from_bonds(types, bonds, bond_orders=orders), cutoff=3.5,
+                          charges=q, use_fast=False, **kw)
+    data, cmds, off = lammps_input(mine, torch.tensor(pos), cell)
+    rdata, rcmds, roff, _files = rl.lammps_input(ref, torch.tensor(pos), cell)
+    assert data == rdata and cmds == rcmds and off == roff
+    assert write_lammps_input(mine, torch.tensor(pos), cell, tmp_path).read_text().count("_coeff") > 3

@@ -56,8 +56,10 @@ __global__ void __launch_bounds__(32 * WPA) conv_gather_kernel(
 #pragma unroll
     for (int d = 0; d < D; ++d) acc[q][d] = T(0);
   const int64_t j0 = dst_ptr[i], j1 = dst_ptr[i + 1];
-  // two edges per warp and step: the index, Y, x and R loads of both are issued before the
-  // multiply-adds (twice the loads in flight of a one-edge loop)
+  // Two edges per warp and step, all their loads issued before the multiply-adds. The
+  // edge's D harmonics are the same for every lane: one coalesced load fills lanes 0..D-1
+  // (edge a) and D..2D-1 (edge b), and shuffles broadcast them (registers for acc, not copies
+  // of Y: the occupancy that hides the gather latency).
   int64_t j = j0 + w;
   for (; j + WPA < j1; j += 2 * WPA) {
     const int64_t ea = perm ? perm[j] : j;
@@ -66,31 +68,29 @@ __global__ void __launch_bounds__(32 * WPA) conv_gather_kernel(
 #pragma unroll
     for (int tt = 0; tt < 3; ++tt) {
       if (tt < t.n) {
-        T ya[D], yb[D];
-#pragma unroll
-        for (int d = 0; d < D; ++d) {
-          ya[d] = __ldg(t.Y[tt] + ea * D + d);
-          yb[d] = __ldg(t.Y[tt] + eb * D + d);
-        }
+        const T yv = lane < 2 * D ? __ldg(t.Y[tt] + (lane < D ? ea * D + lane : eb * D + (lane - D))) : T(0);
+        T pa[CPL][P], pb[CPL][P];
 #pragma unroll
         for (int q = 0; q < CPL; ++q) {
           const int c = cbase + lane + 32 * q;
-          if (c < C) {
-            const T xa = __ldg(t.x[tt] + sa * C + c), xb = __ldg(t.x[tt] + sb * C + c);
-            T ra[P], rb[P];
+          const bool in = c < C;
+          const T xa = in ? __ldg(t.x[tt] + sa * C + c) : T(0);
+          const T xb = in ? __ldg(t.x[tt] + sb * C + c) : T(0);
 #pragma unroll
-            for (int l = 0; l < P; ++l) {
-              ra[l] = __ldg(t.R[tt] + (ea * P + l) * C + c);
-              rb[l] = __ldg(t.R[tt] + (eb * P + l) * C + c);
-            }
-#pragma unroll
-            for (int l = 0; l < P; ++l) {
-              const T pa = ra[l] * xa, pb = rb[l] * xb;
-#pragma unroll
-              for (int m = 0; m < 2 * l + 1; ++m) acc[q][l * l + m] += pa * ya[l * l + m] + pb * yb[l * l + m];
-            }
+          for (int l = 0; l < P; ++l) {
+            pa[q][l] = in ? __ldg(t.R[tt] + (ea * P + l) * C + c) * xa : T(0);
+            pb[q][l] = in ? __ldg(t.R[tt] + (eb * P + l) * C + c) * xb : T(0);
           }
         }
+#pragma unroll
+        for (int l = 0; l < P; ++l)
+#pragma unroll
+          for (int m = 0; m < 2 * l + 1; ++m) {
+            const T ya = __shfl_sync(0xffffffffu, yv, l * l + m);
+            const T yb = __shfl_sync(0xffffffffu, yv, D + l * l + m);
+#pragma unroll
+            for (int q = 0; q < CPL; ++q) acc[q][l * l + m] += pa[q][l] * ya + pb[q][l] * yb;
+          }
       }
     }
   }
@@ -100,22 +100,24 @@ __global__ void __launch_bounds__(32 * WPA) conv_gather_kernel(
 #pragma unroll
     for (int tt = 0; tt < 3; ++tt) {
       if (tt < t.n) {
-        T y[D];
-#pragma unroll
-        for (int d = 0; d < D; ++d) y[d] = __ldg(t.Y[tt] + e * D + d);
+        const T yv = lane < D ? __ldg(t.Y[tt] + e * D + lane) : T(0);
+        T pr[CPL][P];
 #pragma unroll
         for (int q = 0; q < CPL; ++q) {
           const int c = cbase + lane + 32 * q;
-          if (c < C) {
-            const T xv = __ldg(t.x[tt] + s * C + c);
+          const bool in = c < C;
+          const T xv = in ? __ldg(t.x[tt] + s * C + c) : T(0);
 #pragma unroll
-            for (int l = 0; l < P; ++l) {
-              const T r = __ldg(t.R[tt] + (e * P + l) * C + c) * xv;
-#pragma unroll
-              for (int m = 0; m < 2 * l + 1; ++m) acc[q][l * l + m] += r * y[l * l + m];
-            }
-          }
+          for (int l = 0; l < P; ++l) pr[q][l] = in ? __ldg(t.R[tt] + (e * P + l) * C + c) * xv : T(0);
         }
+#pragma unroll
+        for (int l = 0; l < P; ++l)
+#pragma unroll
+          for (int m = 0; m < 2 * l + 1; ++m) {
+            const T y = __shfl_sync(0xffffffffu, yv, l * l + m);
+#pragma unroll
+            for (int q = 0; q < CPL; ++q) acc[q][l * l + m] += pr[q][l] * y;
+          }
       }
     }
   }

@@ -4,7 +4,12 @@ trained parameters) can be run or cross-checked in LAMMPS (``units real``, ``ato
 OPLS: ``pair_style lj/cut/coul/cut`` with geometric mixing, harmonic bonds and angles, ``dihedral_style
 opls`` (the series constants ``V0``, which LAMMPS drops, are returned as an energy offset) and
 ``improper_style cvff``; AMBER: arithmetic mixing, ``dihedral_style fourier`` with each torsion's
-terms and phases, ``improper_style cvff``. Charges are rescaled so that LAMMPS's Coulomb constant
+terms and phases, ``improper_style cvff``; CHARMM: ``lj/charmm/coul/charmm`` with the pair table (NBFIX and own 1-4
+values) written per type pair, Urey-Bradley terms in ``angle_style charmm``, ``dihedral_style
+charmm`` carrying the 1-4 pairs (weight ``1/count`` for a pair closing several dihedrals), harmonic
+impropers; DREIDING: ``lj/cut`` or ``buck`` (exp-6), Morse or harmonic bonds from the bond orders,
+``cosine/squared`` angles (``cosine`` at linear centres), ``dihedral_style harmonic``,
+``improper_style umbrella`` and ``hbond/dreiding/lj`` overlaid for hydrogen bonds. Charges are rescaled so that LAMMPS's Coulomb constant
 (332.06371) reproduces the model's. Bonded types are deduplicated by their parameters. The file
 layout and command set follow the reference (``src/xnn/ffnn/models/lammps_input.py``); cells must be
 orthorhombic, a cluster gets a shrink-wrapped box.
@@ -142,11 +147,177 @@ def _amber(model, pos, bounds, boundary):
     return data, cmds, 0.0
 
 
+def _charmm(model, pos, bounds, boundary):
+    from .charmm import KCAL_TO_EV
+    ev = 1.0 / KCAL_TO_EV
+    ff, top = model.ff, model.topology
+    P = {k: v.detach().double().cpu() for k, v in ff.params.items()}
+    used = list(dict.fromkeys(top.types))
+    at_id = {t: i + 1 for i, t in enumerate(used)}
+    ti = {t: ff.type_index(t) for t in used}
+    q = model.charges.detach().double().cpu().numpy() * math.sqrt(float(model.coulomb_constant) / LAMMPS_COULOMB)
+    rmin, eps, rmin14, eps14 = (x.detach().double().cpu() for x in ff.pair_tables())
+    sec = {s: [] for _, s in _SECTIONS}
+    tb, ta, td, tm = {}, {}, {}, {}
+    for m, (i, j) in enumerate(top.bonds):
+        k = int(model.bond_type[m])
+        sec["Bonds"].append((tb.setdefault((_r(P["bond_k"][k] * ev), _r(P["bond_r0"][k])), len(tb) + 1), i + 1, j + 1))
+    ub = {(int(model.ub_index[0, m]), int(model.ub_index[1, m])):
+          (_r(P["ub_k"][int(model.ub_type[m])] * ev), _r(P["ub_s0"][int(model.ub_type[m])]))
+          for m in range(model.ub_index.shape[1])}
+    for m, (i, j, k) in enumerate(top.angles):
+        t = int(model.angle_type[m])
+        key = (_r(P["angle_k"][t] * ev), _r(P["angle_theta0"][t] / _DEG)) + ub.get((i, k), (0.0, 0.0))
+        sec["Angles"].append((ta.setdefault(key, len(ta) + 1), i + 1, j + 1, k + 1))
+    # dihedral_style charmm also carries the 1-4 pairs: a pair shared by several dihedrals gets
+    # weight 1/count on each, pairs that are not 1-4 (rings) weight 0
+    p14 = set(map(tuple, top.pairs14))
+    share: dict = {}
+    for i, _, _, l in top.dihedrals:
+        share[(min(i, l), max(i, l))] = share.get((min(i, l), max(i, l)), 0) + 1
+    for m, (i, j, k, l) in enumerate(top.dihedrals):
+        t, pair = int(model.dihedral_type[m]), (min(i, l), max(i, l))
+        w14 = 1.0 / share[pair] if pair in p14 else 0.0
+        for s in range(P["dihedral_k"].shape[1]):
+            if float(ff.dihedral_mask[t, s]) == 0.0:
+                continue
+            phase = int(round(math.degrees(math.atan2(float(ff.dihedral_sin[t, s]), float(ff.dihedral_cos[t, s]))))) % 360
+            key = (_r(P["dihedral_k"][t, s] * ev), int(ff.dihedral_n[t, s]), phase, w14 if s == 0 else 0.0)
+            sec["Dihedrals"].append((td.setdefault(key, len(td) + 1), i + 1, j + 1, k + 1, l + 1))
+    for m, (i, j, k, l) in enumerate(model.impropers):
+        t = int(model.improper_type[m])
+        key = (_r(P["improper_k"][t] * ev), _r(math.degrees(math.atan2(float(ff.improper_sin[t]), float(ff.improper_cos[t])))))
+        sec["Impropers"].append((tm.setdefault(key, len(tm) + 1), i + 1, j + 1, k + 1, l + 1))
+    counts = {"Bonds": len(tb), "Angles": len(ta), "Dihedrals": len(td), "Impropers": len(tm)}
+    data = _data("xnn CHARMM", pos, bounds, {at_id[t]: float(ff.type_mass[ti[t]]) for t in used},
+                 [at_id[t] for t in top.types], q, sec, counts)
+    rc = float(model.cutoff)
+    cmds = ["units real", "atom_style full", f"boundary {boundary}",
+            f"pair_style lj/charmm/coul/charmm {rc - 1e-6!r} {rc!r}", "special_bonds charmm"]
+    cmds += _styles(sec, {"bond": "harmonic", "angle": "charmm", "dihedral": "charmm", "improper": "harmonic"})
+    cmds.append("read_data DATAFILE")
+    root = 2.0 ** (1.0 / 6.0)
+    for a in used:
+        for b in used:
+            if at_id[a] <= at_id[b]:
+                x, y = ti[a], ti[b]
+                cmds.append(f"pair_coeff {at_id[a]} {at_id[b]} {float(eps[x, y]) * ev:.15g} {float(rmin[x, y]) / root:.15g} "
+                            f"{float(eps14[x, y]) * ev:.15g} {float(rmin14[x, y]) / root:.15g}")
+    cmds += [f"bond_coeff {i} {k[0]:.15g} {k[1]:.15g}" for k, i in tb.items()]
+    cmds += [f"angle_coeff {i} {k[0]:.15g} {k[1]:.15g} {k[2]:.15g} {k[3]:.15g}" for k, i in ta.items()]
+    cmds += [f"dihedral_coeff {i} {k[0]:.15g} {k[1]} {k[2]} {k[3]:.15g}" for k, i in td.items()]
+    cmds += [f"improper_coeff {i} {k[0]:.15g} {k[1]:.15g}" for k, i in tm.items()]
+    return data, cmds, 0.0
+
+
+def _dreiding_pair(ff, P, ia: int, ib: int, ev: float) -> str:
+    if ff.form == "x6":
+        # exp-6 as LAMMPS buck: A exp(-r / rho) - C / r^6, per-type A and C combined geometrically
+        zeta = [max(float(P["x6_zeta"][x]), 6.0 + 1e-6) for x in (ia, ib)]
+        r0 = [float(P["vdw_r0"][x]) for x in (ia, ib)]
+        d0 = [float(P["vdw_d0"][x]) * ev for x in (ia, ib)]
+        A = [d0[m] * 6.0 / (zeta[m] - 6.0) * math.exp(zeta[m]) for m in (0, 1)]
+        C = [d0[m] * zeta[m] / (zeta[m] - 6.0) * r0[m] ** 6 for m in (0, 1)]
+        rho = 1.0 / (0.5 * (zeta[0] / r0[0] + zeta[1] / r0[1]))
+        return f"{math.sqrt(A[0] * A[1]):.14g} {rho:.14g} {math.sqrt(C[0] * C[1]):.14g}"
+    d0 = math.sqrt(float(P["vdw_d0"][ia] * P["vdw_d0"][ib])) * ev
+    ra, rb = float(P["vdw_r0"][ia]), float(P["vdw_r0"][ib])
+    r0 = math.sqrt(ra * rb) if ff.combination == "geometric" else 0.5 * (ra + rb)
+    return f"{d0:.14g} {r0 / 2.0 ** (1.0 / 6.0):.14g}"
+
+
+def _dreiding(model, pos, bounds, boundary):
+    from .dreiding import KCAL_TO_EV, KE
+    ev = 1.0 / KCAL_TO_EV
+    ff, top = model.ff, model.topology
+    P = {k: v.detach().double().cpu() for k, v in ff.params.items()}
+    n, cutoff = len(top.types), float(model.cutoff)
+    used = list(dict.fromkeys(top.types))
+    at_id = {t: i + 1 for i, t in enumerate(used)}
+    ti = {t: ff.type_index(t) for t in used}
+    orders = list(top.bond_orders) or [1.0] * len(top.bonds)
+    sec = {s: [] for _, s in _SECTIONS}
+    tb, ta, td, tm = {}, {}, {}, {}
+    morse = model.bond_style == "morse"
+    for (i, j), o in zip(top.bonds, orders):
+        r0 = float(P["radius"][ti[top.types[i]]] + P["radius"][ti[top.types[j]]]) - ff.delta
+        k_n = o * float(P["bond_k"])
+        if morse:
+            d_n = o * float(P["bond_d"])
+            key = (_r(d_n * ev), _r(math.sqrt(k_n / (2.0 * d_n))), _r(r0))
+        else:
+            key = (_r(0.5 * k_n * ev), _r(r0))
+        sec["Bonds"].append((tb.setdefault(key, len(tb) + 1), i + 1, j + 1))
+    ka = float(P["angle_k"]) * ev
+    for m, (i, j, k) in enumerate(top.angles):
+        th0 = float(P["theta0"][ti[top.types[j]]])
+        key = (("cosine", _r(ka), 0.0) if bool(model.angle_linear[m])
+               else ("cosine/squared", _r(0.5 * ka / math.sin(th0) ** 2), _r(th0 / _DEG)))
+        sec["Angles"].append((ta.setdefault(key, len(ta) + 1), i + 1, j + 1, k + 1))
+    for m in range(model.dihedral_index.shape[1]):
+        i, j, k, l = (int(x) for x in model.dihedral_index[:, m])
+        rule = int(model.dihedral_rule[m])
+        v = float(model.dihedral_weight[m]) * float(P["torsion_v"][rule]) * ev
+        key = (_r(0.5 * v), -int(ff.rule_sign[rule]), int(ff.rule_n[rule]))
+        sec["Dihedrals"].append((td.setdefault(key, len(td) + 1), i + 1, j + 1, k + 1, l + 1))
+    for m in range(model.inversion_index.shape[1]):
+        c, a, b, d = (int(x) for x in model.inversion_index[:, m])
+        x = ti[top.types[c]]
+        key = (_r(float(P["oop_k"][x]) * ev / 3.0), _r(float(P["oop_psi0"][x]) / _DEG))
+        sec["Impropers"].append((tm.setdefault(key, len(tm) + 1), c + 1, a + 1, b + 1, d + 1))
+    q = (model.charge.detach().double().cpu().numpy() * math.sqrt(KE * ev / LAMMPS_COULOMB) if model.has_coulomb
+         else np.zeros(n))
+    counts = {"Bonds": len(tb), "Angles": len(ta), "Dihedrals": len(td), "Impropers": len(tm)}
+    data = _data("xnn DREIDING", pos, bounds, {at_id[t]: float(ff.type_mass[ti[t]]) or 1.0 for t in used},
+                 [at_id[t] for t in top.types], q, sec, counts)
+    hyd = model.hbond_hydrogens.cpu()
+    hb = model.use_hbond and bool((hyd >= 0).any())
+    base = f"{'buck' if ff.form == 'x6' else 'lj/cut'}{'/coul/cut' if model.has_coulomb else ''} {cutoff!r}"
+    hb_ang = math.acos(model.hbond_cos) / _DEG
+    cmds = ["units real", "atom_style full", f"boundary {boundary}", "special_bonds lj/coul 0.0 0.0 1.0",
+            (f"pair_style hybrid/overlay {base} hbond/dreiding/lj 4 {model.hbond_cutoff!r} {model.hbond_cutoff!r} "
+             f"{hb_ang!r}") if hb else f"pair_style {base}"]
+    if tb:
+        cmds.append(f"bond_style {'morse' if morse else 'harmonic'}")
+    styles = sorted({k[0] for k in ta})
+    if ta:
+        cmds.append(f"angle_style hybrid {' '.join(styles)}" if len(styles) > 1 else f"angle_style {styles[0]}")
+    if td:
+        cmds.append("dihedral_style harmonic")
+    if tm:
+        cmds.append("improper_style umbrella")
+    cmds.append("read_data DATAFILE")
+    sub = f"{base.split()[0]} " if hb else ""
+    for a in used:
+        for b in used:
+            if at_id[a] <= at_id[b]:
+                cmds.append(f"pair_coeff {at_id[a]} {at_id[b]} {sub}{_dreiding_pair(ff, P, ti[a], ti[b], ev)}")
+    if hb:
+        donors = {top.types[d] for d in range(n) if int(hyd[d, 0]) >= 0}
+        hydrogens = {top.types[int(h)] for h in hyd[hyd >= 0]}
+        acceptors = {top.types[a] for a in range(n) if bool(model.hbond_acceptor[a])}
+        for d in sorted(donors):
+            for a in sorted(acceptors):
+                for h in sorted(hydrogens):
+                    cmds.append(f"pair_coeff {min(at_id[d], at_id[a])} {max(at_id[d], at_id[a])} hbond/dreiding/lj "
+                                f"{at_id[h]} i {float(P['hbond_d0']) * ev:.14g} {float(P['hbond_r0']):.14g} 4 "
+                                f"{model.hbond_cutoff!r} {model.hbond_cutoff!r} {hb_ang!r}")
+    cmds += [f"bond_coeff {t} " + " ".join(str(v) for v in k) for k, t in tb.items()]
+    multi = len(styles) > 1
+    for k, t in ta.items():
+        args = f"{k[1]} {k[2]}" if k[0] == "cosine/squared" else f"{k[1]}"
+        cmds.append(f"angle_coeff {t} {k[0] + ' ' if multi else ''}{args}")
+    cmds += [f"dihedral_coeff {t} {k[0]} {k[1]} {k[2]}" for k, t in td.items()]
+    cmds += [f"improper_coeff {t} {k[0]} {k[1]}" for k, t in tm.items()]
+    return data, cmds, 0.0
+
+
 def lammps_input(model, pos, cell=None):
     """``(data file text, commands, energy offset in kcal/mol)`` of an OPLS or AMBER model at ``pos``
     (``read_data DATAFILE`` names the data file in the commands)."""
     from .amber import Amber
     from .charmm import Charmm
+    from .dreiding import Dreiding
     from .opls import OPLS
     model = getattr(model, "model", model)
     pos = np.asarray(pos.detach().cpu() if hasattr(pos, "detach") else pos, float).reshape(-1, 3)
@@ -156,9 +327,13 @@ def lammps_input(model, pos, cell=None):
     pos, bounds, boundary = _box(pos, cell, float(model.cutoff))
     if isinstance(model, OPLS):
         return _opls(model, pos, bounds, boundary)
-    if isinstance(model, Amber) and not isinstance(model, Charmm):
+    if isinstance(model, Charmm):
+        return _charmm(model, pos, bounds, boundary)
+    if isinstance(model, Amber):
         return _amber(model, pos, bounds, boundary)
-    raise TypeError(f"no LAMMPS input writer for {type(model).__name__} (OPLS and AMBER are written)")
+    if isinstance(model, Dreiding):
+        return _dreiding(model, pos, bounds, boundary)
+    raise TypeError(f"no LAMMPS input writer for {type(model).__name__} (OPLS, AMBER, CHARMM and DREIDING are written)")
 
 
 def write_lammps_input(model, pos, cell=None, directory: Union[str, Path] = ".", name: str = "system") -> Path:
