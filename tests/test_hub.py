@@ -68,3 +68,43 @@ def test_synthetic_and_file_builders(tmp_path):
     back = load_dataset("file", path=str(path))
     assert len(back) == 5
     np.testing.assert_allclose(np.asarray(back[2]["pos"]), np.asarray(items[2]["pos"]), atol=1e-6)
+
+
+def _qm9_xyz(index, symbols, coords, props):
+    lines = [f"{len(symbols)}", "gdb " + str(index) + "\t" + "\t".join(repr(p) for p in props)]
+    lines += [f"{s}\t" + "\t".join(c) + "\t0.0" for s, c in zip(symbols, coords)]
+    return "\n".join(lines + ["freq", "SMILES", "InChI"]) + "\n"
+
+
+def test_qm9_reader(tmp_path, monkeypatch):
+    import io
+    import tarfile
+
+    from xnn_b200.data.hub import qm9
+    root = tmp_path / "qm9" / "raw"
+    root.mkdir(parents=True)
+    props = [[1.0 * k + p for p in range(15)] for k in range(4)]
+    mols = {1: (["C", "H", "H", "H", "H"], [["0.0", "0.0", "0.0"], ["1.09", "0", "0"], ["-0.36", "1.03", "0"],
+                                            ["-0.36", "-0.5", "0.9"], ["-0.36", "-0.5", "-0.9"]]),
+            2: (["O", "H", "H"], [["0", "0", "0"], ["0.96", "0", "0"], ["-2.4*^-1", "0.93", "0"]]),
+            3: (["N", "H", "H", "H"], [["0", "0", "0"], ["1.0", "0", "0"], ["0", "1.0", "0"], ["0", "0", "1.0"]]),
+            4: (["F", "H"], [["0", "0", "0"], ["0.92", "0", "0"]])}
+    with tarfile.open(root / "dsgdb9nsd.xyz.tar.bz2", "w:bz2") as tar:
+        for k in (3, 1, 4, 2):                     # archive order is not index order
+            data = _qm9_xyz(k, *mols[k], props[k - 1]).encode()
+            info = tarfile.TarInfo(f"dsgdb9nsd_{k:06d}.xyz")
+            info.size = len(data)
+            tar.addfile(info, io.BytesIO(data))
+    (root / "uncharacterized.txt").write_text("header\n   4   x\n")
+    monkeypatch.setattr(qm9, "XYZ_ARCHIVE", (qm9.XYZ_ARCHIVE[0], None))
+    monkeypatch.setattr(qm9, "UNCHARACTERIZED", (qm9.UNCHARACTERIZED[0], None))
+    monkeypatch.setenv("XNN_B200_OFFLINE", "1")
+    every = load_dataset("qm9", split="all", cache_dir=tmp_path, return_info=True)
+    assert [s["info"]["index"] for s in every] == [1, 2, 3]          # molecule 4 is uncharacterized
+    assert every[1]["atomic_numbers"].tolist() == [8, 1, 1] and abs(every[1]["pos"][2, 0] + 0.24) < 1e-12
+    hartree = 27.211386245988
+    assert abs(every[0]["energy"] - (0 + 10) * hartree) < 1e-9       # U0 column, eV
+    assert abs(every[0]["info"]["mu"] - 3.0) < 1e-12                 # not an energy: unscaled
+    s = load_dataset("qm9", cache_dir=tmp_path, n_train=2, n_val=1, label="gap", units="hartree")
+    assert [len(s[k]) for k in ("train", "val", "test")] == [2, 1, 0]
+    assert abs(qm9.atomic_energies("U0")[1] + 0.500273 * hartree) < 1e-9
