@@ -108,3 +108,36 @@ def test_qm9_reader(tmp_path, monkeypatch):
     s = load_dataset("qm9", cache_dir=tmp_path, n_train=2, n_val=1, label="gap", units="hartree")
     assert [len(s[k]) for k in ("train", "val", "test")] == [2, 1, 0]
     assert abs(qm9.atomic_energies("U0")[1] + 0.500273 * hartree) < 1e-9
+
+
+def test_gmtkn55_reader(tmp_path, monkeypatch):
+    import zipfile
+
+    from xnn_b200.data.hub import gmtkn55
+    from xnn_b200.train.reactions import ReactionSet
+    arc = tmp_path / "gmtkn55" / "raw" / "GMTKN55-v2.zip"
+    arc.parent.mkdir(parents=True)
+    top = "GMTKN55-commit/"
+    files = {"W4-11/.res": "# comment\n$tmer h2 h x -1 2 $w 109.49\n$tmer h2o h2 o x -1 1 1 $w 232.97 0 1\n",
+             "W4-11/h2/struc.xyz": "2\n\nH 0 0 0\nH 0 0 0.74\n",
+             "W4-11/h/struc.xyz": "1\n\nH 0 0 0\n", "W4-11/h/.UHF": "1\n",
+             "W4-11/o/struc.xyz": "1\n\nO 0 0 0\n", "W4-11/o/.UHF": "2\n",
+             "W4-11/h2o/struc.xyz": "3\n\nO 0 0 0\nH 0.96 0 0\nH -0.24 0.93 0\n",
+             "BH76/.resRC": "$tmer h{2,2o} x 1 -1 $w 1.5\n",
+             "BH76/h2o/struc.xyz": "3\n\nO 0 0 0\nH 0.96 0 0\nH -0.24 0.93 0\n",
+             "BH76/h2/struc.xyz": "2\n\nH 0 0 0\nH 0 0 0.74\n", "BH76/h2/.CHRG": "0\n",
+             "W4-11/h2o/PBEh-3c/orca.out": "FINAL SINGLE POINT ENERGY   -76.25\n"}
+    with zipfile.ZipFile(arc, "w") as zf:
+        for name, text in files.items():
+            zf.writestr(top + name, text)
+    monkeypatch.setattr(gmtkn55, "VERSIONS", {"v2": ("commit", None)})
+    monkeypatch.setenv("XNN_B200_OFFLINE", "1")
+    data = load_dataset("gmtkn55", cache_dir=tmp_path, subsets=["w4-11", "BH76RC"])
+    assert [r["species"] for r in data["reactions"]] == [["h2", "h"], ["h2o", "h2", "o"], ["h2", "h2o"]]
+    assert data["reactions"][2]["subset"] == "BH76RC" and data["reactions"][1]["reference"] == 232.97
+    w = {(s["subset"], s["name"]): s for s in data["structures"]}
+    assert w[("W4-11", "o")]["spin_multiplicity"] == 3.0 and abs(w[("W4-11", "h2o")]["pbeh3c_energy"] + 76.25 * 27.211386245988) < 1e-6
+    closed = load_dataset("gmtkn55", cache_dir=tmp_path, subsets="W4-11", closed_shell=True, split="reactions")
+    assert closed == []                                                  # both need an open-shell atom
+    rs = ReactionSet.from_gmtkn55(data)
+    assert len(rs) == 3 and rs.stoichiometry().shape == (3, len(data["structures"]))
