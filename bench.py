@@ -23,6 +23,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 
@@ -273,7 +274,7 @@ def main():
                   "scheduler": "none"},
         "data": {"batch_size": B, "val_fraction": 0.0},
         "trainer": {"cuda_graph": not args.no_graph, "grad_sync": args.grad_sync, "loggers": []},
-        "device": "cuda", "seed": 1234, "output_dir": os.path.join(ROOT, "gpurun_out", "bench_run"),
+        "device": "cuda", "seed": 1234, "output_dir": tempfile.mkdtemp(prefix="xnn_b200_bench_"),
     })
     trainer = Trainer(cfg, ds, val=[], test=[])
     dev = trainer.device

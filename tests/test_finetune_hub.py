@@ -106,3 +106,31 @@ def test_portable_checkpoint_round_trip(tmp_path):
     torch.save({"model": model.state_dict(), "cfg": cfg.to_dict()}, tmp_path / "best.pt")
     d2 = save_pretrained(tmp_path / "best.pt", tmp_path / "from-trainer")
     torch.testing.assert_close(from_pretrained(d2)(b.clone())["energy"], ref["energy"], rtol=1e-12, atol=1e-12)
+
+
+def test_reference_layout_directory_loads(tmp_path):
+    """A model directory as the reference writes it: ``model.pt`` holds ``{"model": state_dict}``
+    (and a bare state dict, as hand-written directories may hold, loads too)."""
+    import yaml
+
+    from xnn_b200.hub import from_pretrained, load_checkpoint
+    torch.manual_seed(3)
+    cfg = _cfg()
+    model = ForceStressOutput(prepare_model(cfg))
+    b = _batch(2, seed=6)
+    ref = model(b.clone())
+    for wrapped in (True, False):
+        d = tmp_path / f"ref-layout-{wrapped}"
+        d.mkdir()
+        sd = {k: v.detach().cpu() for k, v in model.state_dict().items()}
+        torch.save({"model": sd} if wrapped else sd, d / "model.pt")
+        (d / "config.yaml").write_text(yaml.safe_dump(cfg.to_dict()))
+        ck = load_checkpoint(d)
+        assert set(ck.state_dict) == set(sd)
+        got = from_pretrained(d)(b.clone())
+        torch.testing.assert_close(got["energy"], ref["energy"], rtol=1e-12, atol=1e-12)
+    # and what this package writes carries the same wrapping
+    from xnn_b200.hub import save_pretrained
+    out = save_pretrained(model, tmp_path / "ours", config=cfg)
+    raw = torch.load(out / "model.pt", weights_only=True)
+    assert set(raw) == {"model"} and set(raw["model"]) == set(model.state_dict())

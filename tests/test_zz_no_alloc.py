@@ -12,6 +12,7 @@ from xnn_b200 import _ext
 pytestmark = pytest.mark.gpu
 
 ERR_SCRATCH = -1
+ERR_SHAPE = -2
 SCRATCH_FLOATS = 2 * 1024 * 1024
 
 
@@ -98,3 +99,19 @@ def test_noalloc_rejects_oversized_scratch():
     assert b"scratch" in lib.xnn_gemm_reduce_noalloc_error_string(rc)
     torch.cuda.synchronize()
     assert bool((out == 3.0).all())  # nothing was launched
+
+
+def test_noalloc_rejects_unsupported_widths():
+    lib = _lib()
+    dev = torch.device("cuda:0")
+    X = torch.zeros(1024, 64, device=dev)
+    # above 256 columns the product runs as two halves that must each be a multiple of 16
+    for N in (272, 8, 528):
+        D = torch.zeros(1024, N, device=dev)
+        out = torch.full((64, N), 3.0, device=dev)
+        rc = lib.xnn_gemm_reduce_tf32x3_noalloc(1024, 64, N, X.data_ptr(), 64, D.data_ptr(), N, 0, 1.0,
+                                                out.data_ptr(), None)
+        assert rc == ERR_SHAPE, (N, rc)
+        assert b"multiple of 32" in lib.xnn_gemm_reduce_noalloc_error_string(rc)
+        torch.cuda.synchronize()
+        assert bool((out == 3.0).all())

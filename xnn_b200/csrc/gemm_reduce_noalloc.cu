@@ -112,7 +112,8 @@ extern "C" const char* xnn_gemm_reduce_noalloc_error_string(int code) {
     case XNN_NOALLOC_ERR_SCRATCH:
       return "partial blocks (ctas * K1 * N floats) exceed the fixed scratch array of 2097152 floats; "
              "pass a larger rows_per_cta or 0 to choose one that fits";
-    case XNN_NOALLOC_ERR_SHAPE: return "K1 must be in [1, 128] and N a multiple of 16 in [16, 512]";
+    case XNN_NOALLOC_ERR_SHAPE:
+      return "K1 must be in [1, 128] and N a multiple of 16 in [16, 256] or a multiple of 32 in [288, 512]";
     case XNN_NOALLOC_ERR_LAYOUT:
       return "ldx and ldd must be multiples of 4 floats and X, D 16-byte aligned";
     case XNN_NOALLOC_ERR_ROWS: return "rows_per_cta must be 0 (automatic) or a positive multiple of 32";

@@ -26,7 +26,7 @@
 //
 // What must start at zero: nothing the caller passes. The scratch array needs no clearing
 // (each call overwrites every partial block it later reads); `out` is fully written. The
-// device status word starts at zero when the module loads and is set to 2 when a kernel's
+// device status word starts at zero when the module loads and is set to a non-zero code when a kernel's
 // bounded wait on the tensor cores gave up; it stays set until cleared.
 #pragma once
 
@@ -41,7 +41,9 @@ extern "C" {
 // Return codes: 0 on success, a positive cudaError_t value when the CUDA runtime failed,
 // or one of these negative codes (nothing was launched).
 #define XNN_NOALLOC_ERR_SCRATCH (-1)  // ctas * K1 * N floats exceed the scratch array
-#define XNN_NOALLOC_ERR_SHAPE (-2)    // K1 not in [1, 128], N not a multiple of 16 in [16, 512]
+#define XNN_NOALLOC_ERR_SHAPE (-2)    // K1 not in [1, 128], or N neither a multiple of 16 in [16, 256]
+                                      // nor a multiple of 32 in [288, 512] (wider N runs as two
+                                      // halves, each a multiple of 16)
 #define XNN_NOALLOC_ERR_LAYOUT (-3)   // ldx or ldd not a multiple of 4, or X / D not 16-byte aligned
 #define XNN_NOALLOC_ERR_ROWS (-4)     // rows_per_cta negative or not a multiple of 32
 

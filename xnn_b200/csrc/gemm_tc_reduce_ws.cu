@@ -118,8 +118,9 @@ __global__ void __launch_bounds__(RS_THREADS, 1) gemm_reduce_ws_kernel(
 
   if (warp == 0) {
     if (lane == 0) {
-      int last_s = -1, c = 0;
-      for (; c < n_chunks && !*abort_flag; ++c) {
+      int issued[RS_STAGES];             // loads issued into each stage (its `full` phases)
+      for (int s = 0; s < RS_STAGES; ++s) issued[s] = 0;
+      for (int c = 0; c < n_chunks && !*abort_flag; ++c) {
         const int s = c % RS_STAGES;
         if (c >= RS_STAGES &&
             !wait_or_abort(empty + s, (uint32_t)(((c / RS_STAGES) - 1) & 1), spin_limit, abort_flag, status))
@@ -130,9 +131,13 @@ __global__ void __launch_bounds__(RS_THREADS, 1) gemm_reduce_ws_kernel(
         tma_load_2d(st + L.raw_x, &mapX, 0, row, full + s);
         for (int bx = 0; bx < nbox; ++bx)
           tma_load_2d(st + L.raw_d + (uint32_t)bx * KC * NB * 4, &mapD, bx * NB, row, full + s);
-        last_s = s;
+        ++issued[s];
       }
-      if (*abort_flag && last_s >= 0) mbar_wait(full + last_s, (uint32_t)(((c - 1) / RS_STAGES) & 1), spin_limit);
+      // after an abort, the last load issued into every stage lands before the CTA leaves (the
+      // earlier ones were consumed, so they completed)
+      if (*abort_flag)
+        for (int s = 0; s < RS_STAGES; ++s)
+          if (issued[s] > 0 && !mbar_wait(full + s, (uint32_t)((issued[s] - 1) & 1), spin_limit)) atomicExch(status, 6);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -159,7 +164,12 @@ __global__ void __launch_bounds__(RS_THREADS, 1) gemm_reduce_ws_kernel(
         }
         commit_to(empty + s);
       }
+      // the MMAs issued complete before TMEM is freed, also when the converters gave up
       commit_to(fin);
+      if (!mbar_wait(fin, 0, spin_limit)) {
+        atomicExch(status, 5);
+        mbar_wait(fin, 0, 16 * spin_limit);
+      }
     }
   } else {
     // ---------------------------------------------------------------- converters (warps 2..5)

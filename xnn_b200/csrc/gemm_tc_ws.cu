@@ -28,8 +28,11 @@
 // consecutive units overlap.
 //
 // Every wait is bounded (`spin_limit` polls); a role that gives up records code 4 in `status` and
-// raises a shared abort flag that makes the other roles leave their loops; the MMA warp then waits
-// (bounded) for its issued MMAs before TMEM is freed. Loads never use cluster multicast.
+// raises a shared abort flag that makes the other roles leave their loops. Before the CTA exits,
+// the producer waits (bounded) for the last load it issued into every stage, the epilogue for its
+// stores, and the MMA warp for its issued MMAs, so nothing lands in shared memory or TMEM after
+// they are released (code 5: the MMA drain gave up once; 6: a load drain gave up). Loads never use
+// cluster multicast.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -196,7 +199,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
       long long it = 0;
-      int last_s = -1;
+      long long issued[WS_STAGES];     // loads issued into each stage (its `full` phases)
+      for (int s = 0; s < WS_STAGES; ++s) issued[s] = 0;
       int tile, h;
       if (resident) {
         // this CTA's column half of W, every K chunk, once
@@ -217,12 +221,16 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
           tma_load_2d(st, &mapA, c * KC, tile * 128, full + s);
           if (!resident)
             bulk_g2s(st + 3 * A_BYTES, Bpack + ((int64_t)h * n_chunks + c) * 2 * NS * KC, W_BYTES, full + s);
-          last_s = s;
+          ++issued[s];
         }
       }
-      if (resident && *abort_flag) mbar_wait(wfull, 0, spin_limit);
-      // after an abort, let the last copies land before the CTA leaves
-      if (*abort_flag && last_s >= 0) mbar_wait(full + last_s, (uint32_t)(((it - 1) / WS_STAGES) & 1), spin_limit);
+      if (*abort_flag) {
+        // after an abort every copy in flight lands before the CTA leaves: the resident W and, in
+        // each stage, the last load issued (its earlier loads were consumed, so they completed)
+        if (resident && !mbar_wait(wfull, 0, spin_limit)) atomicExch(status, 6);
+        for (int s = 0; s < WS_STAGES; ++s)
+          if (issued[s] > 0 && !mbar_wait(full + s, (uint32_t)((issued[s] - 1) & 1), spin_limit)) atomicExch(status, 6);
+      }
     }
   } else if (warp == 2 || warp == 3) {
     // ---------------------------------------------------------------- converter
@@ -295,9 +303,13 @@ __global__ void __launch_bounds__(WS_THREADS, 1) gemm_ws_kernel(
         }
         if (go) commit_to(accf + b);
       }
-      // all issued MMAs complete before TMEM is released
+      // all issued MMAs complete before TMEM is released; a wait that gives up is recorded and
+      // retried once with a longer bound, since freeing TMEM under running MMAs is undefined
       commit_to(fin);
-      mbar_wait(fin, 0, spin_limit);
+      if (!mbar_wait(fin, 0, spin_limit)) {
+        atomicExch(status, 5);
+        mbar_wait(fin, 0, 16 * spin_limit);
+      }
     }
   } else {
     // ---------------------------------------------------------------- epilogue (warps 4..11)

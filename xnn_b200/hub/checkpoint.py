@@ -80,7 +80,10 @@ def load_checkpoint(path: Union[str, Path]) -> Checkpoint:
     if p.is_dir():
         card = ModelCard.read(p / CARD_FILE) if (p / CARD_FILE).exists() else None
         cfg = read_config(p / CONFIG_FILE) if (p / CONFIG_FILE).exists() else None
-        sd = torch.load(p / WEIGHTS_FILE, map_location="cpu", weights_only=True)
+        state = torch.load(p / WEIGHTS_FILE, map_location="cpu", weights_only=True)
+        # the directory's weights file holds {"model": state_dict}; older or hand-written
+        # directories may hold the bare state dict
+        sd = state["model"] if isinstance(state, dict) and isinstance(state.get("model"), dict) else state
         return Checkpoint(cfg, sd, card, p)
     obj = torch.load(p, map_location="cpu", weights_only=False)
     if isinstance(obj, dict) and "model" in obj and isinstance(obj["model"], dict):
@@ -112,7 +115,7 @@ def save_pretrained(model: Union[nn.Module, str, Path], path: Union[str, Path], 
         sd = wrapped_state_dict(model)
     if config is None:
         raise ValueError("save_pretrained needs the model's config to rebuild it")
-    torch.save(sd, out / WEIGHTS_FILE)
+    torch.save({"model": dict(sd)}, out / WEIGHTS_FILE)
     write_config(config, out / CONFIG_FILE)
     cfg = _as_config(config_to_dict(config))
     card = card or ModelCard()

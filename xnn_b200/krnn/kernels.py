@@ -1,65 +1,88 @@
-"""The Matern kernel of half-integer order ``n + 1/2`` (``n >= 2``) in the form the
-gradient-domain fit needs: ``k(r) = exp(-a r) P(r)`` with ``a = sqrt(2n + 1) / sigma`` and
-``P(r) = sum_k (n + k)! / (2n)! C(n, k) (2 a r)^(n - k)``, ``g = -k'(r) / r`` and ``t = g'(r) / r``,
-each ``exp(-a r)`` times a polynomial (reference ``src/xnn/krnn/kernels.py``). The gradient of
-``k(|x - y|)`` with respect to ``x`` is ``-g (x - y)``; the mixed second derivative is
-``g I + t d d^T``."""
+"""Half-integer Matern kernels as radial functions, with the derivatives a gradient-domain fit uses.
+
+For order ``nu = n + 1/2`` and length scale ``sigma`` (Rasmussen & Williams, eq. 4.16; Chmiela
+et al., Sci. Adv. 3, e1603015, 2017, eq. 3):
+
+    k(r) = exp(-a r) P(r),   a = sqrt(2 nu) / sigma,
+    P(r) = sum_{i=0..n} C(n, i) (n + i)! / (2n)! (2 a r)^(n - i).
+
+Force fits differentiate ``k(|x - y|)`` twice in the coordinates, which needs
+
+    g(r) = -k'(r) / r        and        t(r) = g'(r) / r.
+
+Both are ``exp(-a r)`` times a polynomial: with ``k' = exp(-a r) (P' - a P)`` the numerator of
+``g`` is ``a P - P'``, whose constant term is zero because ``k`` is flat at the origin; the
+numerator of ``t`` is ``Q' - a Q`` for ``Q = (a P - P') / r``, again without a constant term
+when ``n >= 2``. The polynomials are built once with :class:`numpy.polynomial.Polynomial`
+arithmetic and evaluated by Horner's rule on tensors. Gradient of ``k(|x - y|)`` in ``x``:
+``-g(r) (x - y)``; mixed second derivative: ``g I + t d d^T`` with ``d = x - y``.
+"""
 from __future__ import annotations
 
 import math
 from typing import List
 
+import numpy as np
 import torch
+from numpy.polynomial import Polynomial
 from torch import Tensor
 
 
-def _polyval(coef: List[float], r: Tensor) -> Tensor:
-    out = torch.full_like(r, coef[-1])
-    for c in reversed(coef[:-1]):
-        out = out * r + c
-    return out
+def _horner(coef: List[float], r: Tensor) -> Tensor:
+    acc = torch.zeros_like(r) + coef[-1]
+    for c in coef[-2::-1]:
+        acc = torch.addcmul(torch.full_like(r, c), acc, r)
+    return acc
 
 
-def _derivative(coef: List[float]) -> List[float]:
-    return [k * c for k, c in enumerate(coef)][1:] or [0.0]
+def _over_r(poly: Polynomial) -> Polynomial:
+    """``poly / r`` for a polynomial whose value at 0 vanishes (its rounding residue is dropped)."""
+    c = poly.coef
+    return Polynomial(c[1:] if c.size > 1 else np.zeros(1))
 
 
 class Matern:
+    """Matern kernel of order ``n + 1/2`` (``n >= 2``) with length scale ``sigma``."""
+
     def __init__(self, sigma: float, n: int = 2):
         self.sigma, self.n = float(sigma), int(n)
         if self.n < 2:
             raise ValueError("the gradient-domain kernel needs a Matern order of at least 5/2 (n >= 2)")
-        a = math.sqrt(2 * self.n + 1) / self.sigma
+        n, a = self.n, math.sqrt(2 * self.n + 1) / self.sigma
         self.a = a
-        f = math.factorial
-        p = [0.0] * (self.n + 1)
-        for k in range(self.n + 1):
-            p[self.n - k] = f(self.n + k) / f(2 * self.n) * math.comb(self.n, k) * (2 * a) ** (self.n - k)
-        self.p = p
-        q = [a * c for c in p]                      # -k' = exp(-ar) (a P - P')
-        for k, c in enumerate(_derivative(p)):
-            q[k] -= c
-        self.q = q[1:] or [0.0]                     # divided by r (the constant term vanishes)
-        t = [-a * c for c in self.q] + [0.0]        # g' = exp(-ar) (Q' - a Q)
-        for k, c in enumerate(_derivative(self.q)):
-            t[k] += c
-        self.t = t[1:] or [0.0]
+        # P(r): the coefficient of r^(n - i) is C(n, i) (n + i)! / (2n)! (2a)^(n - i)
+        coef = np.zeros(n + 1)
+        for i in range(n + 1):
+            coef[n - i] = math.comb(n, i) * math.factorial(n + i) / math.factorial(2 * n) * (2.0 * a) ** (n - i)
+        P = Polynomial(coef)
+        Q = _over_r(a * P - P.deriv())
+        T = _over_r(Q.deriv() - a * Q)
+        self.p, self.q, self.t = (list(map(float, x.coef)) for x in (P, Q, T))
+
+    def _exp(self, r: Tensor) -> Tensor:
+        return torch.exp(-self.a * r)
 
     def k(self, r: Tensor) -> Tensor:
-        return torch.exp(-self.a * r) * _polyval(self.p, r)
+        """``k(r)``."""
+        return self._exp(r) * _horner(self.p, r)
 
     def g(self, r: Tensor) -> Tensor:
-        return torch.exp(-self.a * r) * _polyval(self.q, r)
+        """``-k'(r) / r``."""
+        return self._exp(r) * _horner(self.q, r)
 
     def t_of(self, r: Tensor) -> Tensor:
-        return torch.exp(-self.a * r) * _polyval(self.t, r)
+        """``g'(r) / r``."""
+        return self._exp(r) * _horner(self.t, r)
 
     def g_and_t(self, r: Tensor):
-        e = torch.exp(-self.a * r)
-        return e * _polyval(self.q, r), e * _polyval(self.t, r)
+        """``g(r)`` and ``t(r)`` sharing one exponential."""
+        e = self._exp(r)
+        return e * _horner(self.q, r), e * _horner(self.t, r)
 
 
 def safe_norm(x: Tensor) -> Tensor:
-    s = (x * x).sum(-1)
-    pos = s > 0
-    return torch.where(pos, torch.sqrt(torch.where(pos, s, torch.ones_like(s))), torch.zeros_like(s))
+    """Length over the last axis whose derivative is 0 (not NaN) at the origin; exact for the
+    kernels above, whose radial functions are flat at ``r = 0``."""
+    sq = x.pow(2).sum(-1)
+    nz = sq > 0
+    return torch.sqrt(torch.where(nz, sq, torch.ones_like(sq))) * nz.to(sq.dtype)

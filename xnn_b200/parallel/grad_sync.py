@@ -75,6 +75,15 @@ class GradSync:
         dist.all_reduce(self.flat, op=dist.ReduceOp.SUM)
         self.flat.mul_(1.0 / self.world)
 
+    def check(self) -> None:
+        """Raise if a fused all-reduce gave up waiting for a peer.
+
+        The kernel reports a timeout in a host-mapped status word, so this read costs no device
+        synchronisation; it sees the kernels that have finished by the time it runs. After a
+        timeout the ranks hold differently reduced gradients, so training must not go on."""
+        if self._p2p is not None:
+            self._p2p.check()
+
     def close(self) -> None:
         if self._p2p is not None:
             self._p2p.close()

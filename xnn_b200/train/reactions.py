@@ -1,15 +1,24 @@
-"""Reaction-energy training (GMTKN55-style): a reaction is a stoichiometric combination of species
-energies, ``dE_r = sum_s nu_rs E_s``; its squared error against a reference (optionally Huber,
-optionally scaled per reaction as in WTMAD-2) trains the model alongside the per-structure terms.
+"""Reaction-energy training (GMTKN55-style benchmarks).
 
-Records and conventions follow the reference (``src/xnn/common/train/reactions.py``): structures
-``{"name", "subset"?, "pos", "atomic_numbers", ...}``, reactions ``{"species", "stoichiometry",
-"reference", "subset"?, "weight"?, "scale"?}``, species looked up by ``(subset, name)`` then by name,
-references in eV, kcal/mol or hartree.
+A reaction ``r`` combines species energies with stoichiometric coefficients,
+``dE_r = sum_s nu_rs E_s``. Its error against a reference value (optionally Huber-clipped and
+optionally multiplied by a per-reaction factor, which is how the WTMAD-2 weighting enters) is a
+loss term trained next to the per-structure energy and force terms.
+
+Storage: the coefficients are kept as coordinate triples ``(reaction, species, nu)`` rather than
+a dense reaction x species matrix, so a batch of reactions evaluates with one ``index_add`` over
+its terms and drawing a batch only renumbers the species that batch touches. The dense matrix
+is still available (:meth:`ReactionSet.stoichiometry`) for callers that want it.
+
+Record formats are the reference's (``src/xnn/common/train/reactions.py``): structures are
+dictionaries ``{"name", "subset"?, "pos", "atomic_numbers", ...}``; reactions are
+``{"species", "stoichiometry", "reference", "subset"?, "weight"?, "scale"?, "index"?}``; a
+species name is looked up inside the reaction's subset first and then without a subset;
+references are in eV, kcal/mol or hartree.
 """
 from __future__ import annotations
 
-from typing import Iterator, Mapping, Optional, Sequence
+from typing import Dict, Iterator, List, Mapping, Optional, Sequence, Tuple
 
 import numpy as np
 import torch
@@ -24,7 +33,18 @@ UNITS = {"ev": 1.0, "kcal/mol": KCAL_MOL_TO_EV, "hartree": HARTREE_TO_EV}
 
 
 def reaction_energies(species_energy: Tensor, stoichiometry: Tensor) -> Tensor:
-    return stoichiometry.to(species_energy.dtype) @ species_energy
+    """``dE = nu @ E`` for a dense ``(reactions, species)`` coefficient matrix."""
+    return torch.mv(stoichiometry.to(species_energy.dtype), species_energy)
+
+
+def _reduce(err: Tensor, weight: Optional[Tensor], scale: Optional[Tensor], huber_delta: float) -> Tensor:
+    if scale is not None:
+        err = err * scale.to(err.dtype)
+    per = _sq(err, huber_delta)
+    if weight is None:
+        return per.mean()
+    w = weight.to(per.dtype)
+    return torch.dot(w, per) / w.sum()
 
 
 def reaction_energy_loss(species_energy: Tensor, stoichiometry: Tensor, reference: Tensor,
@@ -32,82 +52,93 @@ def reaction_energy_loss(species_energy: Tensor, stoichiometry: Tensor, referenc
                          huber_delta: float = 0.0) -> Tensor:
     """Weighted mean of the squared (or Huber) errors of the reaction energies."""
     err = reaction_energies(species_energy, stoichiometry) - reference.to(species_energy.dtype)
-    if scale is not None:
-        err = err * scale.to(err.dtype)
-    sq = _sq(err, huber_delta)
-    if weight is None:
-        return sq.mean()
-    w = weight.to(sq.dtype)
-    return (w * sq).sum() / w.sum()
+    return _reduce(err, weight, scale, huber_delta)
 
 
 class ReactionSet:
-    """Structures and the reactions over them."""
+    """Structures and the reactions defined over them."""
 
     def __init__(self, structures: Sequence[Mapping], reactions: Sequence[Mapping], units: str = "eV"):
-        if units.lower() not in UNITS:
+        factor = UNITS.get(units.lower())
+        if factor is None:
             raise ValueError(f"units must be one of 'eV', 'kcal/mol', 'hartree', got {units!r}")
-        f = UNITS[units.lower()]
         self.structures = list(structures)
-        where = {(s.get("subset"), s["name"]): k for k, s in enumerate(self.structures)}
-        self.members, ref, wts, scl, self.labels = [], [], [], [], []
-        for k, r in enumerate(reactions):
-            sub = r.get("subset")
-            try:
-                idx = [where[(sub, nm)] if (sub, nm) in where else where[(None, nm)] for nm in r["species"]]
-            except KeyError as exc:
-                raise KeyError(f"reaction {k}: no structure for species {exc.args[0]!r}") from None
-            if len(idx) != len(r["stoichiometry"]):
-                raise ValueError(f"reaction {k}: {len(idx)} species but {len(r['stoichiometry'])} coefficients")
-            self.members.append((idx, [float(c) for c in r["stoichiometry"]]))
-            ref.append(f * float(r["reference"]))
-            wts.append(float(r.get("weight", 1.0)))
-            scl.append(float(r.get("scale", 1.0)))
-            self.labels.append((sub, r.get("index", k)))
-        self.reference = torch.tensor(ref, dtype=torch.float64)
-        self.weight = torch.tensor(wts, dtype=torch.float64)
-        self.scale = torch.tensor(scl, dtype=torch.float64)
-        self._graphs: dict = {}
+        lookup: Dict[Tuple[Optional[str], str], int] = {}
+        for k, s in enumerate(self.structures):
+            lookup.setdefault((s.get("subset"), s["name"]), k)
+        rows: List[int] = []
+        cols: List[int] = []
+        nus: List[float] = []
+        values = np.zeros((len(reactions), 3))          # reference (eV), weight, scale
+        self.labels = []
+        for k, rec in enumerate(reactions):
+            names, coefs = list(rec["species"]), list(rec["stoichiometry"])
+            if len(names) != len(coefs):
+                raise ValueError(f"reaction {k}: {len(names)} species but {len(coefs)} coefficients")
+            sub = rec.get("subset")
+            for name, nu in zip(names, coefs):
+                s = lookup.get((sub, name), lookup.get((None, name)))
+                if s is None:
+                    raise KeyError(f"reaction {k}: no structure for species {name!r}")
+                rows.append(k)
+                cols.append(s)
+                nus.append(float(nu))
+            values[k] = (factor * float(rec["reference"]), float(rec.get("weight", 1.0)),
+                         float(rec.get("scale", 1.0)))
+            self.labels.append((sub, rec.get("index", k)))
+        self._set_terms(torch.tensor(rows, dtype=torch.long), torch.tensor(cols, dtype=torch.long),
+                        torch.tensor(nus, dtype=torch.float64))
+        v = torch.from_numpy(values)
+        self.reference, self.weight, self.scale = v[:, 0].clone(), v[:, 1].clone(), v[:, 2].clone()
+        self._graphs: Dict[float, list] = {}
+
+    def _set_terms(self, rows: Tensor, cols: Tensor, nu: Tensor) -> None:
+        self.term_reaction, self.term_species, self.term_nu = rows, cols, nu
 
     @classmethod
     def from_gmtkn55(cls, data: Mapping, wtmad2: bool = False, scale: float = 56.84) -> "ReactionSet":
-        """GMTKN55-style records (kcal/mol); ``wtmad2`` scales each reaction by ``scale / <|dE|>`` of
-        its subset (the WTMAD-2 weighting)."""
+        """GMTKN55-style records (kcal/mol). With ``wtmad2`` every reaction is multiplied by
+        ``scale / mean |dE_ref|`` of its subset, the WTMAD-2 weighting."""
         recs = [dict(r) for r in data["reactions"]]
         if wtmad2:
-            sums: dict = {}
+            by_subset: Dict[str, List[float]] = {}
             for r in recs:
-                n, s = sums.get(r["subset"], (0, 0.0))
-                sums[r["subset"]] = (n + 1, s + abs(float(r["reference"])))
+                by_subset.setdefault(r["subset"], []).append(abs(float(r["reference"])))
+            mean_abs = {k: float(np.mean(v)) for k, v in by_subset.items()}
             for r in recs:
-                n, s = sums[r["subset"]]
-                r["scale"] = scale / (s / n)
+                r["scale"] = scale / mean_abs[r["subset"]]
         return cls(data["structures"], recs, units="kcal/mol")
 
     def __len__(self) -> int:
-        return len(self.members)
+        return int(self.reference.shape[0])
 
     def subset(self, reactions: Sequence[int]) -> "ReactionSet":
-        out = ReactionSet.__new__(ReactionSet)
-        keep: dict = {}
-        out.members = []
-        for r in reactions:
-            idx, coef = self.members[int(r)]
-            out.members.append(([keep.setdefault(i, len(keep)) for i in idx], list(coef)))
-        order = sorted(keep, key=keep.get)
-        out.structures = [self.structures[i] for i in order]
+        """The given reactions over only the species they use (numbered by first use)."""
         sel = torch.as_tensor([int(r) for r in reactions], dtype=torch.long)
+        # terms of the selected reactions, in selection order, keeping each reaction's term order
+        pos_of = torch.full((len(self),), -1, dtype=torch.long)
+        pos_of[sel] = torch.arange(sel.numel())
+        new_row = pos_of[self.term_reaction]
+        keep = new_row >= 0
+        order = torch.argsort(new_row[keep] * (self.term_reaction.numel() + 1)
+                              + torch.arange(self.term_reaction.numel())[keep])
+        rows, cols, nu = new_row[keep][order], self.term_species[keep][order], self.term_nu[keep][order]
+        used, first = np.unique(cols.numpy(), return_index=True)
+        by_first = used[np.argsort(first)]                  # species in order of first use
+        renum = torch.full((len(self.structures),), -1, dtype=torch.long)
+        renum[torch.from_numpy(by_first)] = torch.arange(len(by_first))
+        out = ReactionSet.__new__(ReactionSet)
+        out.structures = [self.structures[i] for i in by_first.tolist()]
+        out._set_terms(rows, renum[cols], nu)
         out.reference, out.weight, out.scale = self.reference[sel], self.weight[sel], self.scale[sel]
-        out.labels = [self.labels[int(r)] for r in reactions]
-        out._graphs = {k: [g[i] for i in order] for k, g in self._graphs.items()}
+        out.labels = [self.labels[i] for i in sel.tolist()]
+        out._graphs = {k: [g[i] for i in by_first.tolist()] for k, g in self._graphs.items()}
         return out
 
     def stoichiometry(self) -> Tensor:
-        out = torch.zeros(len(self.members), len(self.structures), dtype=torch.float64)
-        for r, (idx, coef) in enumerate(self.members):
-            for i, c in zip(idx, coef):
-                out[r, i] += c
-        return out
+        """Dense ``(reactions, species)`` coefficients (repeated species add up)."""
+        out = torch.zeros(len(self), len(self.structures), dtype=torch.float64)
+        return out.index_put_((self.term_reaction, self.term_species), self.term_nu, accumulate=True)
 
     def graphs(self, cutoff: float) -> list:
         key = float(cutoff)
@@ -116,26 +147,36 @@ class ReactionSet:
         return self._graphs[key]
 
     def batches(self, size: int, shuffle: bool = True, seed: int = 0) -> Iterator["ReactionSet"]:
-        order = np.random.default_rng(seed).permutation(len(self)) if shuffle else np.arange(len(self))
-        for s in range(0, len(order), size):
-            yield self.subset(order[s:s + size].tolist())
+        idx = np.arange(len(self))
+        if shuffle:
+            idx = np.random.default_rng(seed).permutation(idx)
+        for start in range(0, len(idx), size):
+            yield self.subset(idx[start:start + size].tolist())
 
     def species_energies(self, model: torch.nn.Module, cutoff: float, batch_size: int = 32,
                          device: Optional[torch.device] = None) -> Tensor:
-        gs, out = self.graphs(cutoff), []
+        """Model energy of every structure of the set, in order."""
+        gs = self.graphs(cutoff)
+        if not gs:
+            return torch.zeros(0, dtype=torch.float64)
         p = next(model.parameters(), None)
+        parts = []
         for s in range(0, len(gs), batch_size):
             b = collate(gs[s:s + batch_size])
             if p is not None and b.pos.dtype != p.dtype:
                 b.compute_dtype = p.dtype          # float64 geometry driving the model's dtype
-            out.append(model(b.to(device) if device is not None else b)["energy"].reshape(-1))
-        return torch.cat(out) if out else torch.zeros(0, dtype=torch.float64)
+            if device is not None:
+                b = b.to(device)
+            parts.append(model(b)["energy"].reshape(-1))
+        return torch.cat(parts)
+
+    def errors(self, species_energy: Tensor) -> Tensor:
+        """``dE_model - dE_ref`` per reaction, by summing the coefficient terms."""
+        dev, dt = species_energy.device, species_energy.dtype
+        terms = self.term_nu.to(dev, dt) * species_energy.index_select(0, self.term_species.to(dev))
+        dE = torch.zeros(len(self), dtype=dt, device=dev).index_add_(0, self.term_reaction.to(dev), terms)
+        return dE - self.reference.to(dev, dt)
 
     def loss(self, species_energy: Tensor, huber_delta: float = 0.0) -> Tensor:
         dev = species_energy.device
-        return reaction_energy_loss(species_energy, self.stoichiometry().to(dev), self.reference.to(dev),
-                                    self.weight.to(dev), self.scale.to(dev), huber_delta)
-
-    def errors(self, species_energy: Tensor) -> Tensor:
-        dev = species_energy.device
-        return reaction_energies(species_energy, self.stoichiometry().to(dev)) - self.reference.to(dev)
+        return _reduce(self.errors(species_energy), self.weight.to(dev), self.scale.to(dev), huber_delta)

@@ -285,6 +285,9 @@ class Trainer:
         else:
             out = self._train_step_impl(batch.to(self.device, non_blocking=True))
         self.global_step += 1
+        # a fused all-reduce that timed out left the ranks with different gradients: stop here
+        # (host-mapped status, no synchronisation; it reports the steps finished so far)
+        self.grad_sync.check()
         return out
 
     # ------------------------------------------------------------------ data
@@ -369,7 +372,9 @@ class Trainer:
                 cb.on_train_batch_end(self, loss)
         t = torch.stack([loss_sum, torch.tensor(float(n), dtype=torch.float64, device=self.device)])
         D.all_reduce_sum(t)
-        return {"train/loss": float(t[0] / t[1].clamp_min(1.0))}
+        out = {"train/loss": float(t[0] / t[1].clamp_min(1.0))}
+        self.grad_sync.check()         # every step of the epoch has finished (synchronised above)
+        return out
 
     def fit(self) -> Dict[str, float]:
         from .callbacks import ModelCheckpoint

@@ -1,0 +1,124 @@
+"""Tracing helpers: named regions and per-kernel time tables.
+
+* :func:`region` names a stretch of host code. Under ``torch.profiler`` it appears as a
+  ``record_function`` range, and with ``XNN_B200_NVTX=1`` (or inside
+  ``torch.autograd.profiler.emit_nvtx``) it also pushes an NVTX range for external
+  timeline tools. Outside both it costs one dictionary lookup. The reference wraps its PME and
+  induction stages the same way (``src/xnn/ffnn/models/amoeba_ewald.py:67-80``).
+* :func:`kernel_table` runs a callable under ``torch.profiler`` and returns every GPU kernel it
+  launched with its count and summed device time, plus the share of device time and launches
+  that belong to this package's own kernels (those compiled into ``xnn_b200/_C.so``).
+
+``python -m xnn_b200.utils.profiling`` prints that table for one eager MACE training step of the
+benchmark configuration (64 organic molecules, 96 channels).
+"""
+from __future__ import annotations
+
+import argparse
+import contextlib
+import os
+from collections import defaultdict
+from typing import Callable, Dict, List
+
+import torch
+
+_NVTX = os.environ.get("XNN_B200_NVTX", "0") == "1"
+
+#: name fragments of the kernels compiled into ``xnn_b200/_C.so``
+OWN_KERNELS = ("conv_gather", "conv_edge", "conv_scatter", "symcon_", "edge_geom_", "p2p_allreduce",
+               "halo_exchange", "gemm_pack_kernel", "gemm_rows_kernel", "gemm_reduce_kernel", "gemm_ws_kernel",
+               "gemm_ws_pack_kernel", "gemm_reduce_ws_kernel", "sum_partials_kernel", "radial_basis_kernel",
+               "radial_act_kernel", "radial_dact_kernel", "nb_count", "nb_write", "mp_real_kernel",
+               "pme_spread_kernel", "pme_gather_kernel", "xnn_", "nl_", "mace_", "tn_", "pme_", "halo_",
+               "adam_", "grad_", "seg_", "dd_", "fft_", "eeq_", "atm_", "amoeba_", "reax_", "sqm_")
+
+
+def is_own_kernel(name: str) -> bool:
+    return any(k in name for k in OWN_KERNELS)
+
+
+@contextlib.contextmanager
+def region(name: str):
+    """A named range for profilers (record_function; NVTX when enabled)."""
+    nvtx = _NVTX and torch.cuda.is_available()
+    if nvtx:
+        torch.cuda.nvtx.range_push(name)
+    try:
+        with torch.profiler.record_function(name):
+            yield
+    finally:
+        if nvtx:
+            torch.cuda.nvtx.range_pop()
+
+
+def kernel_table(fn: Callable[[], object], warmup: int = 1) -> Dict[str, object]:
+    """GPU kernels launched by one call of ``fn`` (after ``warmup`` untimed calls)."""
+    from torch.profiler import ProfilerActivity, profile
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    count: Dict[str, int] = defaultdict(int)
+    us: Dict[str, float] = defaultdict(float)
+    for e in prof.events():
+        if e.device_type.name != "CUDA":
+            continue
+        count[e.name] += 1
+        us[e.name] += float(getattr(e, "device_time", 0.0) or getattr(e, "cuda_time", 0.0) or 0.0)
+    rows: List[Dict[str, object]] = [
+        {"kernel": k, "launches": count[k], "us": round(us[k], 2), "own": is_own_kernel(k)} for k in count]
+    rows.sort(key=lambda r: -float(r["us"]))
+    tot_us = sum(float(r["us"]) for r in rows)
+    own_us = sum(float(r["us"]) for r in rows if r["own"])
+    tot_n = sum(int(r["launches"]) for r in rows)
+    own_n = sum(int(r["launches"]) for r in rows if r["own"])
+    return {"rows": rows, "device_us": round(tot_us, 1), "launches": tot_n, "own_launches": own_n,
+            "own_time_share": round(own_us / tot_us, 4) if tot_us else None}
+
+
+def _mace_step(batch: int):
+    import tempfile
+
+    from ..config import from_dict
+    from ..data import AtomicDataset, synthetic
+    from ..train import Trainer
+    mols = synthetic.organic_molecules(batch, seed=1000)
+    ds = AtomicDataset(mols, 4.5, precompute=True)
+    graphs = [ds[i] for i in range(len(ds))]
+    avg = sum(g.num_edges for g in graphs) / sum(g.num_nodes for g in graphs)
+    cfg = from_dict({
+        "model": {"name": "mace", "cutoff": 4.5, "n_features": 96, "n_interactions": 2, "n_rbf": 8,
+                  "extra": {"species": [1, 6, 7, 8, 9, 16, 17], "max_ell": 3, "max_L": 0, "correlation": 3,
+                            "avg_num_neighbors": avg}},
+        "optim": {"lr": 1e-3, "energy_weight": 1.0, "force_weight": 10.0, "epochs": 1, "scheduler": "none"},
+        "data": {"batch_size": batch, "val_fraction": 0.0},
+        "trainer": {"cuda_graph": False, "loggers": []},
+        "device": "cuda", "seed": 1234, "output_dir": tempfile.mkdtemp(prefix="xnn_b200_prof_"),
+    })
+    tr = Trainer(cfg, ds, val=[], test=[])
+    cap = tr.capacity_for_batches([graphs])
+    b = tr.make_padder(*cap)(graphs).to(tr.device)
+    return lambda: tr._train_step_impl(b)
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--top", type=int, default=40)
+    ap.add_argument("--json", default=None, help="also write the table as JSON to this path")
+    a = ap.parse_args(argv)
+    tab = kernel_table(_mace_step(a.batch), warmup=3)
+    print(f"launches {tab['launches']} (own {tab['own_launches']}), device time {tab['device_us']} us, "
+          f"own-kernel share {tab['own_time_share']}")
+    for r in tab["rows"][:a.top]:
+        print(f"{r['us']:10.1f} us {r['launches']:5d}  {'*' if r['own'] else ' '} {r['kernel'][:120]}")
+    if a.json:
+        import json
+        with open(a.json, "w") as f:
+            json.dump(tab, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()
