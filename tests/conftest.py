@@ -12,6 +12,13 @@ if ROOT not in sys.path:
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200) and the built extension")
     config.addinivalue_line("markers", "slow: long-running test")
+    # the e3nn stand-in goes in before any test can import the reference package: a reference
+    # module imported without it would record e3nn as missing for the rest of the process
+    tests_dir = os.path.dirname(os.path.abspath(__file__))
+    if tests_dir not in sys.path:
+        sys.path.insert(0, tests_dir)
+    from ref_oracle import _stub_e3nn
+    _stub_e3nn()
 
 
 def pytest_collection_modifyitems(config, items):

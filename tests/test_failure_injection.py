@@ -82,3 +82,29 @@ def test_rank_that_leaves_between_steps_makes_the_next_collective_raise(tmp_path
     out = run_ranks(_leaving_rank, 2, str(tmp_path), timeout=300)
     assert out[1] == "left"
     assert out[0].startswith("raised"), out[0]
+
+
+def _corrupt_plan(rank, world):
+    from xnn_b200.data import structure_to_graph
+    from xnn_b200.models.mace import MACE
+    from xnn_b200.parallel import domain
+    torch.set_default_dtype(torch.float64)
+    if rank == 1:
+        real = domain._ghost_counts
+        domain._ghost_counts = lambda owner, w: real(owner, w) + torch.nn.functional.one_hot(  # noqa: E731
+            torch.tensor(0), w).to(owner.device)                     # one ghost too many from rank 0
+    torch.manual_seed(0)
+    m = MACE(species=[1, 8], cutoff=3.0, num_channels=8, n_rbf=6, num_interactions=2, max_ell=2,
+             correlation=2, avg_num_neighbors=8.0).double()
+    g = structure_to_graph(synthetic.water_box(162, seed=0), 3.0)
+    dp = domain.DomainParallel(m, skin=0.3)
+    try:
+        dp.plan(g)
+    except domain.PlanError as exc:
+        return f"raised: {exc}"
+    return "no error"
+
+
+def test_corrupted_ghost_count_makes_every_rank_raise():
+    out = run_ranks(_corrupt_plan, 2, timeout=300)
+    assert all(o.startswith("raised") for o in out), out

@@ -115,6 +115,9 @@ class TrainerConfig:
     cuda_graph: bool = False
     grad_sync: str = "auto"        # auto / nccl / p2p: how data-parallel gradients are reduced
     graph_headroom: float = 0.05   # padding headroom of a captured step
+    #: the hand-written MACE step (energies, forces, loss and gradients without autograd):
+    #: "auto" on CUDA when the model and loss are covered, True / False to force it on / off
+    fused_step: Any = False
 
 
 @dataclass

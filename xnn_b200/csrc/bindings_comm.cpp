@@ -90,9 +90,11 @@ void register_gemm(pybind11::module& m);
 void register_radial(pybind11::module& m);
 void register_halo(pybind11::module& m);
 void register_ffnn(pybind11::module& m);
+void register_node(pybind11::module& m);
 
 void register_comm(pybind11::module& m) {
   register_gemm(m);
+  register_node(m);
   register_radial(m);
   register_halo(m);
   register_ffnn(m);

@@ -1,0 +1,259 @@
+// Python bindings of the node-level tcgen05 products (node_gemm.cu): problem tables built from
+// lists of tensors, launched on the current stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <algorithm>
+#include <vector>
+
+#define NM_MAX_PROBS 24
+#define NR_MAX_PROBS 16
+
+struct NodeMMProb {
+  const float* X[2];
+  int ldx[2];
+  int kx[2];
+  float* Y;
+  int ldy;
+  const float* Wp;
+  const int* perm;
+  const int* seg;
+  int rows;
+  int N;
+  int accumulate;
+  int tile0;
+};
+struct NodeMMArgs {
+  NodeMMProb p[NM_MAX_PROBS];
+  int n;
+  int* status;
+  long long spin_limit;
+};
+struct NodeRedProb {
+  const float* X[2];
+  int ldx[2];
+  const float* D[2];
+  int ldd[2];
+  int rows[2];
+  const int* perm;
+  const int* seg;
+  int K1, N;
+  float scale;
+  float* out;
+  float* partial;
+  unsigned int* counter;
+  int ctas, rows_per_cta, cta0;
+};
+struct NodeRedArgs {
+  NodeRedProb p[NR_MAX_PROBS];
+  int n;
+  int* status;
+  long long spin_limit;
+};
+struct PackJob {
+  const float* W;
+  int64_t sk, sn;
+  int K, N;
+  float* out;
+};
+struct PackArgs {
+  PackJob j[48];
+  int n;
+};
+
+cudaError_t node_mm_launch(NodeMMArgs& args, int total_tiles, int max_n, cudaStream_t s);
+cudaError_t node_mmT_launch(NodeRedArgs& args, int total_ctas, int max_k1, int max_n, cudaStream_t s);
+cudaError_t node_pack_launch(PackArgs& args, cudaStream_t s);
+size_t node_pack_floats(int K, int N);
+cudaError_t species_sort_launch(int n, int n_el, const int64_t* z, int* perm, int* seg, cudaStream_t s);
+
+namespace {
+
+void need_f32(const torch::Tensor& t, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32, what, ": float32 CUDA tensor expected");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1 && t.stride(0) % 4 == 0, what, ": rows contiguous, row stride % 4");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, what, ": 16-byte aligned");
+}
+
+const int* opt_i32(const c10::optional<torch::Tensor>& t, const char* what) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt32, what, ": int32 CUDA tensor expected");
+  return t->data_ptr<int>();
+}
+
+// Y[i] (+)= [X0 | X1][i] @ W for every problem i (one launch). Wp: packed by node_pack for the
+// concatenated K; perm / seg: optional int32 row permutation and two-entry segment.
+void node_mm(std::vector<torch::Tensor> X0, std::vector<c10::optional<torch::Tensor>> X1,
+             std::vector<torch::Tensor> Y, std::vector<torch::Tensor> Wp,
+             std::vector<c10::optional<torch::Tensor>> perm, std::vector<c10::optional<torch::Tensor>> seg,
+             std::vector<int64_t> rows, std::vector<bool> accumulate, torch::Tensor status, int64_t spin_limit) {
+  const size_t n = X0.size();
+  TORCH_CHECK(n >= 1 && n <= NM_MAX_PROBS, "node_mm: 1..", NM_MAX_PROBS, " problems");
+  TORCH_CHECK(X1.size() == n && Y.size() == n && Wp.size() == n && perm.size() == n && seg.size() == n &&
+                  rows.size() == n && accumulate.size() == n, "node_mm: list lengths");
+  c10::cuda::CUDAGuard guard(X0[0].device());
+  NodeMMArgs a;
+  a.n = (int)n;
+  a.status = status.data_ptr<int>();
+  a.spin_limit = spin_limit;
+  int tiles = 0, max_n = 16;
+  for (size_t i = 0; i < n; ++i) {
+    NodeMMProb& p = a.p[i];
+    need_f32(X0[i], "X0");
+    need_f32(Y[i], "Y");
+    p.X[0] = X0[i].data_ptr<float>();
+    p.ldx[0] = (int)X0[i].stride(0);
+    p.kx[0] = (int)X0[i].size(1);
+    p.X[1] = nullptr;
+    p.ldx[1] = 0;
+    p.kx[1] = 0;
+    if (X1[i].has_value() && X1[i]->defined()) {
+      need_f32(*X1[i], "X1");
+      p.X[1] = X1[i]->data_ptr<float>();
+      p.ldx[1] = (int)X1[i]->stride(0);
+      p.kx[1] = (int)X1[i]->size(1);
+    }
+    TORCH_CHECK(p.kx[0] % 4 == 0 && p.kx[1] % 4 == 0, "node_mm: K of every source a multiple of 4");
+    p.Y = Y[i].data_ptr<float>();
+    p.ldy = (int)Y[i].stride(0);
+    p.N = (int)Y[i].size(1);
+    TORCH_CHECK(p.N % 16 == 0 && p.N >= 16 && p.N <= 128, "node_mm: N a multiple of 16 in [16, 128]");
+    const int K = p.kx[0] + p.kx[1];
+    TORCH_CHECK(Wp[i].is_cuda() && Wp[i].scalar_type() == torch::kFloat32 &&
+                    (size_t)Wp[i].numel() >= node_pack_floats(K, p.N), "node_mm: packed weight too small");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(Wp[i].data_ptr()) % 16 == 0, "node_mm: packed weight alignment");
+    p.Wp = Wp[i].data_ptr<float>();
+    p.perm = opt_i32(perm[i], "perm");
+    p.seg = opt_i32(seg[i], "seg");
+    p.rows = (int)rows[i];
+    p.accumulate = accumulate[i] ? 1 : 0;
+    p.tile0 = tiles;
+    tiles += std::max<int>(1, (p.rows + 127) / 128);
+    max_n = std::max(max_n, p.N);
+  }
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaError_t e = node_mm_launch(a, tiles, max_n, st);
+  TORCH_CHECK(e == cudaSuccess, "node_mm: ", cudaGetErrorString(e));
+}
+
+// out[i] = scale[i] * (X0^T D0 + X1^T D1) over the rows (one launch, deterministic split-K).
+void node_mmT(std::vector<torch::Tensor> X0, std::vector<torch::Tensor> D0,
+              std::vector<c10::optional<torch::Tensor>> X1, std::vector<c10::optional<torch::Tensor>> D1,
+              std::vector<c10::optional<torch::Tensor>> perm, std::vector<c10::optional<torch::Tensor>> seg,
+              std::vector<int64_t> rows0, std::vector<int64_t> rows1, std::vector<torch::Tensor> out,
+              std::vector<double> scale, torch::Tensor counters, torch::Tensor status, int64_t spin_limit) {
+  const size_t n = X0.size();
+  TORCH_CHECK(n >= 1 && n <= NR_MAX_PROBS, "node_mmT: 1..", NR_MAX_PROBS, " problems");
+  TORCH_CHECK(D0.size() == n && X1.size() == n && D1.size() == n && perm.size() == n && seg.size() == n &&
+                  rows0.size() == n && rows1.size() == n && out.size() == n && scale.size() == n,
+              "node_mmT: list lengths");
+  TORCH_CHECK(counters.scalar_type() == torch::kInt32 && counters.numel() >= (int64_t)n, "node_mmT: counters");
+  c10::cuda::CUDAGuard guard(X0[0].device());
+  NodeRedArgs a;
+  a.n = (int)n;
+  a.status = status.data_ptr<int>();
+  a.spin_limit = spin_limit;
+  int ctas = 0, max_k1 = 16, max_n = 16;
+  int64_t partial_floats = 0;
+  std::vector<int64_t> poff(n);
+  for (size_t i = 0; i < n; ++i) {
+    NodeRedProb& p = a.p[i];
+    need_f32(X0[i], "X0");
+    need_f32(D0[i], "D0");
+    p.X[0] = X0[i].data_ptr<float>();
+    p.ldx[0] = (int)X0[i].stride(0);
+    p.D[0] = D0[i].data_ptr<float>();
+    p.ldd[0] = (int)D0[i].stride(0);
+    p.rows[0] = (int)rows0[i];
+    p.X[1] = p.X[0];
+    p.D[1] = p.D[0];
+    p.ldx[1] = p.ldx[0];
+    p.ldd[1] = p.ldd[0];
+    p.rows[1] = 0;
+    if (X1[i].has_value() && X1[i]->defined()) {
+      TORCH_CHECK(D1[i].has_value() && D1[i]->defined(), "node_mmT: X1 without D1");
+      need_f32(*X1[i], "X1");
+      need_f32(*D1[i], "D1");
+      p.X[1] = X1[i]->data_ptr<float>();
+      p.ldx[1] = (int)X1[i]->stride(0);
+      p.D[1] = D1[i]->data_ptr<float>();
+      p.ldd[1] = (int)D1[i]->stride(0);
+      p.rows[1] = (int)rows1[i];
+    }
+    p.K1 = (int)X0[i].size(1);
+    p.N = (int)D0[i].size(1);
+    TORCH_CHECK(p.K1 % 4 == 0 && p.K1 >= 4 && p.K1 <= 128, "node_mmT: K1 a multiple of 4 in [4, 128]");
+    TORCH_CHECK(p.N % 16 == 0 && p.N >= 16 && p.N <= 256, "node_mmT: N a multiple of 16 in [16, 256]");
+    TORCH_CHECK(out[i].is_cuda() && out[i].is_contiguous() && out[i].numel() == (int64_t)p.K1 * p.N,
+                "node_mmT: out must be a contiguous K1 x N tensor");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(out[i].data_ptr()) % 16 == 0, "node_mmT: out must be 16-byte aligned");
+    p.out = out[i].data_ptr<float>();
+    p.scale = (float)scale[i];
+    p.perm = opt_i32(perm[i], "perm");
+    p.seg = opt_i32(seg[i], "seg");
+    // CTAs per problem: about one per 512 rows (a segment's rows are only known on the device,
+    // where they are split evenly over these CTAs; `rows` is then the caller's size hint)
+    const int total = p.rows[0] + p.rows[1];
+    p.ctas = std::max(1, std::min(64, (total + 511) / 512));
+    p.rows_per_cta = 0;
+    p.cta0 = ctas;
+    p.counter = reinterpret_cast<unsigned int*>(counters.data_ptr<int>() + i);
+    poff[i] = partial_floats;
+    partial_floats += (int64_t)p.ctas * p.K1 * p.N;
+    ctas += p.ctas;
+    max_k1 = std::max(max_k1, p.K1);
+    max_n = std::max(max_n, p.N);
+  }
+  auto partial = torch::empty({partial_floats}, X0[0].options());
+  for (size_t i = 0; i < n; ++i) a.p[i].partial = partial.data_ptr<float>() + poff[i];
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaError_t e = node_mmT_launch(a, ctas, max_k1, max_n, st);
+  TORCH_CHECK(e == cudaSuccess, "node_mmT: ", cudaGetErrorString(e));
+}
+
+// Packs every W (K x N, any strides) into its operand layout; returns the packed tensors.
+std::vector<torch::Tensor> node_pack(std::vector<torch::Tensor> Ws) {
+  const size_t n = Ws.size();
+  TORCH_CHECK(n >= 1 && n <= 48, "node_pack: 1..48 matrices");
+  c10::cuda::CUDAGuard guard(Ws[0].device());
+  PackArgs a;
+  a.n = (int)n;
+  std::vector<torch::Tensor> out;
+  for (size_t i = 0; i < n; ++i) {
+    const auto& W = Ws[i];
+    TORCH_CHECK(W.is_cuda() && W.scalar_type() == torch::kFloat32 && W.dim() == 2, "node_pack: float32 CUDA matrix");
+    const int K = (int)W.size(0), N = (int)W.size(1);
+    TORCH_CHECK(N % 16 == 0 && K % 4 == 0, "node_pack: K a multiple of 4, N of 16");
+    auto o = torch::empty({(int64_t)node_pack_floats(K, N)}, W.options());
+    a.j[i] = PackJob{W.data_ptr<float>(), W.stride(0), W.stride(1), K, N, o.data_ptr<float>()};
+    out.push_back(o);
+  }
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaError_t e = node_pack_launch(a, st);
+  TORCH_CHECK(e == cudaSuccess, "node_pack: ", cudaGetErrorString(e));
+  return out;
+}
+
+// (perm, seg): atoms grouped by element index, stable; seg[k] .. seg[k + 1] holds element k
+std::vector<torch::Tensor> species_sort(torch::Tensor z, int64_t n_el) {
+  TORCH_CHECK(z.is_cuda() && z.scalar_type() == torch::kInt64 && z.is_contiguous(), "species_sort: int64 z");
+  c10::cuda::CUDAGuard guard(z.device());
+  auto opt = z.options().dtype(torch::kInt32);
+  auto perm = torch::empty({z.numel()}, opt);
+  auto seg = torch::empty({n_el + 1}, opt);
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaError_t e = species_sort_launch((int)z.numel(), (int)n_el, z.data_ptr<int64_t>(), perm.data_ptr<int>(),
+                                      seg.data_ptr<int>(), st);
+  TORCH_CHECK(e == cudaSuccess, "species_sort: ", cudaGetErrorString(e));
+  return {perm, seg};
+}
+
+}  // namespace
+
+void register_node(pybind11::module& m) {
+  m.def("node_mm", &node_mm);
+  m.def("node_mmT", &node_mmT);
+  m.def("node_pack", &node_pack);
+  m.def("species_sort", &species_sort);
+}

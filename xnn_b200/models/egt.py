@@ -9,25 +9,33 @@ Feature tables, layer structure and parameter names follow the reference
 """
 from __future__ import annotations
 
-import math
 from typing import Optional
 
 import torch
 from torch import Tensor, nn
+from torch.nn import functional as F
 
 from ..nn.blocks import MLP, make_activation
-from ..ops.scatter import scatter_sum
 
 N_ELEMENTS, MAX_DEGREE, MAX_FORMAL_CHARGE, MAX_RING = 86, 6, 2, 8
 N_BOND_RING, N_BOND_ORDER = 2, 4
 
 
 def class_mean(x: Tensor, cls: Tensor) -> Tensor:
-    """Each row replaced by the mean of the rows of its class."""
+    """Every row replaced by the average of the rows that share its class label."""
     n = x.shape[0]
-    total = scatter_sum(x, cls, n)
-    count = scatter_sum(torch.ones_like(cls, dtype=x.dtype), cls, n)
-    return (total / count.clamp(min=1.0).unsqueeze(-1)).index_select(0, cls)
+    sums = x.new_zeros((n,) + tuple(x.shape[1:])).index_add_(0, cls, x)
+    sizes = torch.bincount(cls, minlength=n).clamp_min(1).to(x.dtype)
+    return (sums / sizes.view(-1, *([1] * (x.dim() - 1)))).index_select(0, cls)
+
+
+def _segment_softmax(logits: Tensor, seg: Tensor, n: int) -> Tensor:
+    """Softmax of ``logits (E, H)`` within each group of rows sharing ``seg`` (max-shifted)."""
+    top = logits.new_full((n, logits.shape[1]), float("-inf"))
+    top = top.index_reduce_(0, seg, logits.detach(), "amax")
+    ex = torch.exp(logits - top.index_select(0, seg))
+    den = ex.new_zeros((n, ex.shape[1])).index_add_(0, seg, ex)
+    return ex / den.index_select(0, seg)
 
 
 def _mlp(n_in: int, hidden: int, n_out: int, layers: int, activation, activate_last: bool = False) -> MLP:
@@ -53,12 +61,16 @@ class GraphEmbedding(nn.Module):
         self.node_dim, self.edge_dim = int(node_mlp[1]), int(edge_mlp[1])
 
     def forward(self, node_features: Tensor, edge_features: Tensor, atom_class: Tensor, edge_class: Tensor):
-        f = node_features
-        charge = torch.clamp(f[:, 2] + MAX_FORMAL_CHARGE, 0, 2 * MAX_FORMAL_CHARGE)
-        x = torch.cat([self.element(f[:, 0]), self.degree(f[:, 1]), self.formal_charge(charge),
-                       self.ring_degree(f[:, 3]), self.min_ring(f[:, 4])], -1)
-        e = torch.cat([self.bond_ring(edge_features[:, 0]), self.bond_order(edge_features[:, 1])], -1)
-        return class_mean(self.node_mlp(x), atom_class), class_mean(self.edge_mlp(e), edge_class)
+        # column c of the integer feature table goes through table c; the formal charge is shifted
+        # into the table's range and clipped
+        cols = node_features.unbind(-1)
+        shifted = (cols[2] + MAX_FORMAL_CHARGE).clamp(0, 2 * MAX_FORMAL_CHARGE)
+        atom_tables = (self.element, self.degree, self.formal_charge, self.ring_degree, self.min_ring)
+        atom_cols = (cols[0], cols[1], shifted, cols[3], cols[4])
+        atoms = torch.cat([tab(c) for tab, c in zip(atom_tables, atom_cols)], dim=-1)
+        bcols = edge_features.unbind(-1)
+        bonds = torch.cat([self.bond_ring(bcols[0]), self.bond_order(bcols[1])], dim=-1)
+        return class_mean(self.node_mlp(atoms), atom_class), class_mean(self.edge_mlp(bonds), edge_class)
 
 
 class EGTLayer(nn.Module):
@@ -80,24 +92,28 @@ class EGTLayer(nn.Module):
         self.ffn = _mlp(dim, ffn[0], dim, ffn[1], activation)
         self.edge_ffn = _mlp(dim, ffn[0], dim, ffn[1], activation)
 
+    def _qkv(self, h: Tensor):
+        """Query, key and value heads from one matrix product over the stacked projections."""
+        w = torch.cat([self.query.weight, self.key.weight, self.value.weight], 0)
+        b = torch.cat([self.query.bias, self.key.bias, self.value.bias], 0)
+        return F.linear(h, w, b).view(h.shape[0], 3, self.heads, self.head_dim).unbind(1)
+
     def forward(self, x: Tensor, e: Tensor, src: Tensor, dst: Tensor):
-        n, H, C = x.shape[0], self.heads, self.head_dim
-        h = self.norm1(x)
-        q, k, v = self.query(h).view(n, H, C), self.key(h).view(n, H, C), self.value(h).view(n, H, C)
-        g = self.edge_norm1(e)
-        gate = torch.sigmoid(self.gate(g))
-        logits = (q.index_select(0, dst) * k.index_select(0, src)).sum(-1) / math.sqrt(C) + self.edge_bias(g)
-        peak = torch.full((n, H), float("-inf"), dtype=logits.dtype, device=logits.device)
-        peak = peak.scatter_reduce(0, dst.unsqueeze(-1).expand(-1, H), logits.detach(), "amax")
-        w = torch.exp(logits - peak.index_select(0, dst))
-        w = w / scatter_sum(w, dst, n).index_select(0, dst)
+        n = x.shape[0]
+        q, k, v = self._qkv(self.norm1(x))
+        ge = self.edge_norm1(e)
+        # per edge and head: scaled dot product of the receiver's query with the sender's key,
+        # biased by the edge channels; the same logits later feed back into the edges
+        logits = torch.einsum("ehc,ehc->eh", q[dst], k[src]) * self.head_dim ** -0.5 + self.edge_bias(ge)
+        att = _segment_softmax(logits, dst, n) * torch.sigmoid(self.gate(ge))
         if self.scale_by_degree:
-            w = w * scatter_sum(torch.ones_like(dst, dtype=w.dtype), dst, n).index_select(0, dst).unsqueeze(-1)
-        msg = v.index_select(0, src) * (gate * w).unsqueeze(-1)
-        x = self.proj(scatter_sum(msg, dst, n).reshape(n, H * C)) + x
-        x = self.ffn(self.norm2(x)) + x
+            att = att * torch.bincount(dst, minlength=n).to(att.dtype)[dst, None]
+        agg = x.new_zeros((n, self.heads, self.head_dim)).index_add_(0, dst, v[src] * att[..., None])
+        x = x + self.proj(agg.flatten(1))
+        x = x + self.ffn(self.norm2(x))
         e = e + self.edge_proj(logits)
-        return x, self.edge_ffn(self.edge_norm2(e)) + e
+        e = e + self.edge_ffn(self.edge_norm2(e))
+        return x, e
 
 
 class MolecularGraphTransformer(nn.Module):
@@ -133,18 +149,20 @@ class MolecularGraphTransformer(nn.Module):
                 edge_class: Tensor):
         x, e = self.embedding(node_features, edge_features, atom_class, edge_class)
         e = self.edge_in(e)
-        src, dst = edge_index[0], edge_index[1]
-        outs, last = [], len(self.layers) - 1
-        for i, layer in enumerate(self.layers):
+        src, dst = edge_index.unbind(0)
+        history = []
+        n_layers = len(self.layers)
+        for depth, layer in enumerate(self.layers, start=1):
             x, e = layer(x, e, src, dst)
-            if i < last or self.jumping_knowledge is not None:
+            # the activation follows every layer but the last, and the last too when an output
+            # head (jumping knowledge) comes after it
+            if depth < n_layers or self.jumping_knowledge is not None:
                 x = self.act(x)
-            outs.append(x)
-        if self.jumping_knowledge == "cat":
-            x = self.out(torch.cat(outs, -1))
-        elif self.jumping_knowledge == "last":
-            x = self.out(x)
+            history.append(x)
+        if self.out is not None:
+            x = self.out(torch.cat(history, -1) if self.jumping_knowledge == "cat" else x)
         e = self.edge_out(e)
-        m = e.shape[0] // 2
-        e = (0.5 * (e[0::2] + e[1::2])).unsqueeze(1).expand(m, 2, e.shape[1]).reshape(2 * m, e.shape[1])
+        # both directions of a bond (consecutive rows) carry the average of the two
+        pairs = e.view(-1, 2, e.shape[-1])
+        e = pairs.mean(1, keepdim=True).expand_as(pairs).reshape(e.shape)
         return x, e

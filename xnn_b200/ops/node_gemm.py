@@ -1,0 +1,173 @@
+"""Batched node-level products of the MACE training step (``csrc/node_gemm.cu``).
+
+A problem table goes to one kernel launch:
+
+* :class:`MM` -- ``Y[rows] (+)= [X0 | X1][rows] @ W``; rows optionally gathered / scattered
+  through ``perm`` and restricted to the segment ``seg = (start, end)`` of the permuted row
+  space (device tensor, e.g. the atoms of one element);
+* :class:`MMT` -- ``out = scale * (X0^T D0 + X1^T D1)`` summed over the rows (same row
+  options), split over CTAs with a deterministic in-kernel sum of the partial blocks.
+
+Weights are packed once per step (:func:`pack`) into the MMA operand layout. On the CPU (and
+for shapes the kernel does not take) the same problems evaluate with PyTorch, which is what the
+tests compare against.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import torch
+from torch import Tensor
+
+from .. import _ext
+
+SPIN_LIMIT = 50_000_000
+_STATE: Dict[torch.device, Dict[str, Tensor]] = {}
+
+
+def _state(dev: torch.device) -> Dict[str, Tensor]:
+    st = _STATE.get(dev)
+    if st is None:
+        st = {"status": torch.zeros(1, dtype=torch.int32, device=dev),
+              "counters": torch.zeros(64, dtype=torch.int32, device=dev)}
+        _STATE[dev] = st
+    return st
+
+
+def status(dev: torch.device) -> int:
+    """Non-zero when a node product on ``dev`` gave up waiting (reading it synchronises)."""
+    st = _STATE.get(dev)
+    return 0 if st is None else int(st["status"].item())
+
+
+def kernels(t: Tensor) -> bool:
+    return t.is_cuda and t.dtype == torch.float32 and _ext.cuda_available()
+
+
+@dataclass
+class MM:
+    X0: Tensor
+    W: Tensor                      # (K0 + K1, N) unpacked (the CPU path and shape checks)
+    Y: Tensor
+    Wp: Optional[Tensor] = None    # packed W (CUDA)
+    X1: Optional[Tensor] = None
+    perm: Optional[Tensor] = None  # int32 (CUDA) / int64 (CPU) permutation of the rows
+    seg: Optional[Tensor] = None   # two-entry tensor: the problem's rows [seg[0], seg[1])
+    rows: Optional[int] = None     # row count (default: X0 rows); with seg an upper bound
+    accumulate: bool = False
+
+
+@dataclass
+class MMT:
+    X0: Tensor
+    D0: Tensor
+    out: Tensor
+    X1: Optional[Tensor] = None
+    D1: Optional[Tensor] = None
+    perm: Optional[Tensor] = None
+    seg: Optional[Tensor] = None
+    rows0: Optional[int] = None
+    rows1: Optional[int] = None
+    scale: float = 1.0
+
+
+def pack(Ws: Sequence[Tensor]) -> List[Tensor]:
+    """Packed operand copies of the float32 CUDA matrices ``Ws`` (one launch)."""
+    out: List[Tensor] = []
+    Ws = list(Ws)
+    for i in range(0, len(Ws), 48):
+        out += _ext.ops().node_pack(Ws[i:i + 48])
+    return out
+
+
+def _rows_of(p_rows: Optional[int], X: Tensor, seg: Optional[Tensor], perm: Optional[Tensor]) -> Tensor:
+    n = X.shape[0] if p_rows is None else int(p_rows)
+    if seg is not None:
+        s = seg.tolist()
+        idx = torch.arange(int(s[0]), int(s[1]), device=X.device)
+    else:
+        idx = torch.arange(n, device=X.device)
+    return perm.long()[idx] if perm is not None else idx
+
+
+def _mm_torch(p: MM) -> None:
+    idx = _rows_of(p.rows, p.X0, p.seg, p.perm)
+    x = p.X0.index_select(0, idx)
+    if p.X1 is not None:
+        x = torch.cat([x, p.X1.index_select(0, idx)], 1)
+    y = x @ p.W.to(x.dtype)
+    if p.accumulate:
+        p.Y.index_add_(0, idx, y)
+    else:
+        p.Y.index_copy_(0, idx, y)
+
+
+def _mmt_torch(p: MMT) -> None:
+    idx = _rows_of(p.rows0, p.X0, p.seg, p.perm)
+    g = p.X0.index_select(0, idx).t() @ p.D0.index_select(0, idx)
+    if p.X1 is not None:
+        idx1 = _rows_of(p.rows1, p.X1, p.seg, p.perm)
+        g = g + p.X1.index_select(0, idx1).t() @ p.D1.index_select(0, idx1)
+    p.out.copy_((p.scale * g).view_as(p.out))
+
+
+def _mm_ok(p: MM) -> bool:
+    N = p.Y.shape[1]
+    K = p.X0.shape[1] + (0 if p.X1 is None else p.X1.shape[1])
+    return (kernels(p.X0) and p.Wp is not None and 16 <= N <= 128 and N % 16 == 0 and p.X0.shape[1] % 4 == 0
+            and (p.X1 is None or p.X1.shape[1] % 4 == 0) and K == p.W.shape[0])
+
+
+def _mmt_ok(p: MMT) -> bool:
+    K1, N = p.X0.shape[1], p.D0.shape[1]
+    return kernels(p.X0) and K1 % 4 == 0 and 4 <= K1 <= 128 and N % 16 == 0 and 16 <= N <= 256
+
+
+def mm(problems: Sequence[MM]) -> None:
+    """Run every row product (one kernel launch for those the kernel takes)."""
+    fast = [p for p in problems if _mm_ok(p)]
+    for p in problems:
+        if not _mm_ok(p):
+            _mm_torch(p)
+    if not fast:
+        return
+    st = _state(fast[0].X0.device)
+    for i in range(0, len(fast), 24):
+        chunk = fast[i:i + 24]
+        _ext.ops().node_mm([p.X0 for p in chunk], [p.X1 for p in chunk], [p.Y for p in chunk],
+                           [p.Wp for p in chunk], [p.perm for p in chunk], [p.seg for p in chunk],
+                           [int(p.X0.shape[0] if p.rows is None else p.rows) for p in chunk],
+                           [bool(p.accumulate) for p in chunk], st["status"], SPIN_LIMIT)
+
+
+def mmT(problems: Sequence[MMT]) -> None:
+    """Run every reduction (one kernel launch for those the kernel takes)."""
+    fast = [p for p in problems if _mmt_ok(p)]
+    for p in problems:
+        if not _mmt_ok(p):
+            _mmt_torch(p)
+    if not fast:
+        return
+    st = _state(fast[0].X0.device)
+    for i in range(0, len(fast), 16):
+        chunk = fast[i:i + 16]
+        _ext.ops().node_mmT([p.X0 for p in chunk], [p.D0 for p in chunk], [p.X1 for p in chunk],
+                            [p.D1 for p in chunk], [p.perm for p in chunk], [p.seg for p in chunk],
+                            [int(p.X0.shape[0] if p.rows0 is None else p.rows0) for p in chunk],
+                            [int(0 if p.X1 is None else (p.X1.shape[0] if p.rows1 is None else p.rows1))
+                             for p in chunk],
+                            [p.out for p in chunk], [float(p.scale) for p in chunk], st["counters"],
+                            st["status"], SPIN_LIMIT)
+
+
+def species_sort(z: Tensor, n_el: int):
+    """``(perm, seg)``: atoms grouped by element index (stable), element ``k`` at
+    ``perm[seg[k]:seg[k + 1]]``; int32 on CUDA."""
+    if z.is_cuda and _ext.cuda_available():
+        return _ext.ops().species_sort(z.contiguous(), int(n_el))
+    perm = torch.argsort(z, stable=True)
+    counts = torch.bincount(z, minlength=n_el)
+    seg = torch.zeros(n_el + 1, dtype=torch.long, device=z.device)
+    seg[1:] = torch.cumsum(counts, 0)
+    return perm, seg

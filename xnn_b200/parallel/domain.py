@@ -1,28 +1,44 @@
 """Spatial domain decomposition: one large structure evaluated by several processes.
 
-Behaviour follows the reference's ``DomainParallel`` (``src/xnn/common/deploy/domain.py:266-719``):
-the box (a periodic cell, or the bounding box of a molecule) is cut into a grid of sub-domains,
-one per process; a process owns the atoms whose fractional coordinates fall in its sub-domain
-and evaluates them together with a shell of ghost atoms, keeping only the energies of its owned
-atoms. The shell is one cutoff thick with ghost features refreshed from their owners before
-every layer that reads neighbours (``halo="layer"``), or the whole receptive field with no
-exchange inside the model (``halo="field"``). Ghost positions come from their owners through
-the same exchange, so the derivative of a process's energy with respect to its ghosts flows back
-to their owners: each process ends with the forces on its own atoms, and only the energy and
-virial are summed. A plan is built with a ``skin`` and stays valid while atoms moved less than
-the skin allows (``holds``), so an MD loop rebuilds it only occasionally (``reshard``).
+The behaviour is that of the reference's ``DomainParallel``
+(``src/xnn/common/deploy/domain.py:266-719``): the box (a periodic cell, or the bounding box of
+a molecule) is cut into a grid of sub-domains, one per process. A process owns the atoms whose
+fractional coordinates fall in its sub-domain and evaluates them together with a shell of
+ghosts, keeping the energies of its owned atoms only. The shell is one cutoff thick with ghost
+features refreshed from their owners before every layer that reads neighbours
+(``halo="layer"``), or the whole receptive field with no exchange inside the model
+(``halo="field"``). Ghost positions come from their owners through the same exchange, so the
+derivative of a process's energy with respect to its ghosts flows back to the owners: each
+process ends with the forces on its own atoms, and only energy and virial are summed. A plan is
+built with a ``skin`` and stays valid while the atoms moved less than the skin allows
+(:meth:`DomainParallel.holds`), so an MD loop rebuilds it only now and then
+(:meth:`DomainParallel.reshard`).
 
-Device-side design: plans are built where the positions live (the native CUDA cell list on a
-GPU), ghost rows move either through ``all_to_all_single`` of the process group (NCCL, or Gloo
-on the CPU) or, with ``exchange="p2p"``, through one kernel per direction that packs the rows
-and stores them straight into the receiving GPUs' ghost buffers over NVLink
-(:mod:`xnn_b200.parallel.halo`).
+How a plan is built here:
+
+* ownership: the sub-domain cell of every atom's fractional coordinates (row-major rank order);
+* ghosts: for every atom and every cut axis, the integer image range ``k`` with
+  ``lo <= f + k < hi`` (the slab widened by the shell) is computed directly, and the atom's
+  images are the mixed-radix enumeration of the per-axis ranges -- no fixed image window, so
+  cells thinner than the shell need no special case;
+* the handshake: one exchange of ghost counts, one of the requested atom ids and one of a small
+  table per peer (where my rows start in its ghost list, where its rows start in my send list,
+  my largest row count) -- the last replaces a separate reduction for the buffer size;
+* validation is collective: every consistency check (counts against lists, requested atoms
+  against ownership) is agreed by a reduction before anyone raises, so a rank that finds a
+  problem makes every rank raise instead of leaving the others waiting in the next collective;
+* the local neighbour list is built with the box periodic along the uncut axes only (open
+  along the cut ones, where the ghosts are explicit images).
+
+Ghost rows move through ``all_to_all_single`` of the process group (NCCL, or Gloo on the CPU)
+or, with ``exchange="p2p"``, through one kernel per direction that stores the rows straight
+into the receiving GPUs' buffers over NVLink (:mod:`xnn_b200.parallel.halo`).
 """
 from __future__ import annotations
 
 import math
 from dataclasses import dataclass
-from typing import List, Optional, Sequence
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
@@ -40,81 +56,91 @@ HALOS = ("auto", "layer", "field")
 EXCHANGES = ("collective", "p2p")
 
 
-def _process(group) -> tuple:
+class PlanError(RuntimeError):
+    """The processes built inconsistent plans (raised on every process together)."""
+
+
+def _process(group) -> Tuple[int, int]:
     if dist.is_available() and dist.is_initialized():
         return dist.get_rank(group), dist.get_world_size(group)
     return 0, 1
 
 
-# --------------------------------------------------------------------------- collectives
-class _AllToAllRows(Function):
-    """Rows ``x[send_rows]`` sent to every process; the rows received, concatenated by source.
+def _agree(ok: bool, world: int, group, device) -> bool:
+    """Whether ``ok`` holds on every process (a MIN reduction; every process calls it)."""
+    if world == 1:
+        return ok
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    return bool(flag.item())
 
-    The backward sends the gradient rows back to their owners and accumulates them into the
-    owned rows they were copied from.
-    """
+
+# --------------------------------------------------------------------------- collectives
+class _RowExchange(Function):
+    """Ghost rows from their owners (``x[send_rows]`` to every process, received by source);
+    the backward returns the ghost cotangents to the owners and adds them to the owned rows."""
 
     @staticmethod
     def forward(ctx, x: Tensor, plan: "DomainPlan", group, exchanger):
-        ctx.plan, ctx.group, ctx.exchanger, ctx.n = plan, group, exchanger, x.shape[0]
+        ctx.plan, ctx.group, ctx.exchanger, ctx.rows = plan, group, exchanger, x.shape[0]
         if exchanger is not None:
             return exchanger.forward(x, plan)
-        send = x.index_select(0, plan.send_rows).contiguous()
-        out = send.new_empty((plan.n_ghost,) + tuple(send.shape[1:]))
-        dist.all_to_all_single(out, send, plan.recv_counts, plan.send_counts, group=group)
-        return out
+        outgoing = x.index_select(0, plan.send_rows).contiguous()
+        incoming = outgoing.new_empty((plan.n_ghost,) + tuple(outgoing.shape[1:]))
+        dist.all_to_all_single(incoming, outgoing, plan.recv_counts, plan.send_counts, group=group)
+        return incoming
 
     @staticmethod
     def backward(ctx, g: Tensor):
         plan = ctx.plan
         if ctx.exchanger is not None:
-            return ctx.exchanger.backward(g.contiguous(), plan, ctx.n), None, None, None
-        back = g.new_empty((int(plan.send_rows.shape[0]),) + tuple(g.shape[1:]))
-        dist.all_to_all_single(back, g.contiguous(), plan.send_counts, plan.recv_counts, group=ctx.group)
-        gx = g.new_zeros((ctx.n,) + tuple(g.shape[1:]))
-        gx.index_add_(0, plan.send_rows, back)
-        return gx, None, None, None
+            return ctx.exchanger.backward(g.contiguous(), plan, ctx.rows), None, None, None
+        returned = g.new_empty((plan.send_rows.shape[0],) + tuple(g.shape[1:]))
+        dist.all_to_all_single(returned, g.contiguous(), plan.send_counts, plan.recv_counts, group=ctx.group)
+        grad = g.new_zeros((ctx.rows,) + tuple(g.shape[1:]))
+        return grad.index_add_(0, plan.send_rows, returned), None, None, None
 
 
-class _AllReduceSum(Function):
+class _SumOverRanks(Function):
     @staticmethod
     def forward(ctx, x: Tensor, group):
         ctx.group = group
-        y = x.clone()
-        dist.all_reduce(y, group=group)
-        return y
+        total = x.clone()
+        dist.all_reduce(total, group=group)
+        return total
 
     @staticmethod
     def backward(ctx, g: Tensor):
-        g = g.clone()
-        dist.all_reduce(g, group=ctx.group)
-        return g, None
+        total = g.clone()
+        dist.all_reduce(total, group=ctx.group)
+        return total, None
 
 
-def _tie(x: Tensor) -> Tensor:
-    """An exact float64 zero that depends on ``x``.
+def _order_link(x: Tensor) -> Tensor:
+    """An exact float64 zero that depends on ``x`` (an empty slice of it, summed).
 
-    Each collective of an evaluation adds the tie of the previous collective's output to its
-    input, and the energy adds the ties of all of them, so the backward pass of every process
-    runs the adjoint collectives in exactly the reverse order of the forward ones whatever the
-    shape of its own graph (the same device of the reference, ``domain.py:255-263``)."""
-    return x.reshape(-1)[:0].sum(dtype=torch.float64)
+    Adding the link of the previous collective's output to the next collective's input (and the
+    links of all of them to the energy) chains the collectives in the autograd graph, so every
+    process runs the adjoint collectives in the reverse order of the forward ones whatever the
+    shape of its own graph."""
+    return x.reshape(-1).narrow(0, 0, 0).sum(dtype=torch.float64)
+
+
+def _apply3(rows: Tensor, m: Tensor) -> Tensor:
+    """``rows @ m`` for ``rows (n, 3)`` and a 3 x 3 ``m``, as three scaled rows summed (a library
+    GEMM with an inner size of 3 runs a launch configuration meant for large matrices)."""
+    m = m.to(rows.dtype)
+    return rows[:, 0:1] * m[0] + rows[:, 1:2] * m[1] + rows[:, 2:3] * m[2]
 
 
 # --------------------------------------------------------------------------- plan
-def _rows3(x: Tensor, m: Tensor) -> Tensor:
-    """``x @ m`` for ``x (n, 3)`` and ``m (3, 3)`` as one broadcast product and sum: a library
-    GEMM with an inner size of 3 wastes a launch configuration meant for large ``K``."""
-    return (x.unsqueeze(-1) * m.to(x.dtype)).sum(1)
-
-
 @dataclass
 class DomainPlan:
     """What one process evaluates: owned atoms, ghosts, exchanges, neighbour list.
 
-    Field names and meanings are those of the reference's ``DomainPlan``
-    (``domain.py:109-204``) so MD drivers written against it port unchanged. Local atoms are the
-    owned atoms (ascending atom index) followed by the ghosts (grouped by owner).
+    Field names and meanings are the reference's ``DomainPlan`` (``domain.py:109-204``), so MD
+    drivers written against it port unchanged. Local atoms are the owned atoms (ascending atom
+    index) followed by the ghosts (grouped by owner).
     """
 
     grid: tuple
@@ -172,25 +198,22 @@ class DomainPlan:
 def choose_grid(n_domains: int, widths: Sequence[float], halo: float) -> tuple:
     """The factorisation ``gx * gy * gz = n_domains`` that evaluates the fewest ghosts.
 
-    Cutting an axis of width ``w`` into ``g`` slabs adds a shell ``halo`` thick on both sides
-    of each slab, multiplying the evaluated volume by ``1 + 2 halo g / w``; the grid with the
-    smallest product is returned (ties keep the first in lexicographic order).
-    """
-    best, best_cost = None, math.inf
-    for gx in range(1, n_domains + 1):
-        if n_domains % gx:
-            continue
-        rest = n_domains // gx
-        for gy in range(1, rest + 1):
-            if rest % gy:
-                continue
-            grid = (gx, gy, rest // gy)
-            cost = 1.0
-            for g, w in zip(grid, widths):
-                if g > 1:
-                    cost *= 1.0 + 2.0 * halo * g / max(float(w), 1e-12)
-            if cost < best_cost - 1e-12:
-                best, best_cost = grid, cost
+    Cutting an axis of width ``w`` into ``g`` slabs adds a shell ``halo`` thick on both sides of
+    each slab, multiplying the evaluated volume by ``1 + 2 halo g / w``; the grid with the
+    smallest product wins (ties keep the first in lexicographic order)."""
+    def cost(grid):
+        c = 1.0
+        for g, w in zip(grid, widths):
+            if g > 1:
+                c *= 1.0 + 2.0 * halo * g / max(float(w), 1e-12)
+        return c
+
+    grids = [(a, b, n_domains // (a * b)) for a in range(1, n_domains + 1) if n_domains % a == 0
+             for b in range(1, n_domains // a + 1) if (n_domains // a) % b == 0]
+    best = grids[0]
+    for g in grids[1:]:
+        if cost(g) < cost(best) - 1e-12:
+            best = g
     return best
 
 
@@ -201,33 +224,63 @@ def _model_dtype(model: nn.Module) -> Optional[torch.dtype]:
     return None
 
 
-class _Hooks:
-    """The object the model's ``refresh_ghosts`` / ``whole_structure_sum`` calls go to."""
-
-    def __init__(self, dp: "DomainParallel", plan: DomainPlan, ties: List[Tensor]):
-        self.dp, self.plan, self.ties = dp, plan, ties
-
-    def refresh(self, x: Tensor) -> Tensor:
-        plan = self.plan
-        rows = max(plan.n_local, 1)
-        if not self.dp.layer:
-            return x
-        if x.shape[0] != rows:
-            raise ValueError(f"refresh_ghosts got {x.shape[0]} rows for {rows} local atoms")
-        fresh = self.dp._exchange(plan, x[:plan.n_owned], self.ties)
-        return torch.cat([x[:plan.n_owned], fresh, x[plan.n_local:]])
-
-    def whole_sum(self, values: Tensor, batch: Tensor, num_graphs: int) -> Tensor:
-        n = self.plan.n_owned
-        part = structure_sum(values[:n], batch[:n], num_graphs)
-        if self.plan.world > 1:
-            part = part + _tie(self.ties[-1]).to(part.dtype) if self.ties else part
-            part = _AllReduceSum.apply(part, self.dp.group)
-            self.ties.append(part)
-        return part
+def _frame(pos: Tensor, cell: Optional[Tensor]):
+    """Fractional coordinates in [0, 1) per axis, the slab widths and the inverse cell."""
+    if cell is not None:
+        inv = torch.linalg.inv(cell)
+        f = _apply3(pos, inv)
+        return f - torch.floor(f), 1.0 / torch.linalg.norm(inv, dim=0), inv
+    if pos.shape[0] == 0:
+        return pos.new_zeros((0, 3)), pos.new_full((3,), 1e-6), None
+    low = pos.min(0).values
+    width = pos.max(0).values - low + 1e-6
+    return (pos - low) / width, width, None
 
 
-# --------------------------------------------------------------------------- module
+def _owners(frac: Tensor, grid: Sequence[int]) -> Tensor:
+    g = torch.tensor(list(grid), device=frac.device)
+    cell = torch.floor(frac * g.to(frac.dtype)).long()
+    cell = torch.maximum(torch.minimum(cell, g - 1), torch.zeros_like(cell))
+    return (cell[:, 0] * grid[1] + cell[:, 1]) * grid[2] + cell[:, 2]
+
+
+def _halo_members(frac: Tensor, owner: Tensor, rank: int, coords, grid, widths: List[float], halo: float,
+                  periodic: bool) -> Tuple[Tensor, Tensor]:
+    """``(atom, image)`` of every ghost: atoms (and periodic images along cut axes) inside this
+    process's slab widened by ``halo``, the process's own atoms at image 0 excluded; ordered by
+    atom, then image."""
+    n, device = frac.shape[0], frac.device
+    kmin, span = [], []
+    for a in range(3):
+        if grid[a] == 1:
+            kmin.append(torch.zeros(n, dtype=torch.long, device=device))
+            span.append(torch.ones(n, dtype=torch.long, device=device))
+            continue
+        shell = halo / widths[a]
+        lo = coords[a] / grid[a] - shell
+        hi = (coords[a] + 1) / grid[a] + shell
+        f = frac[:, a]
+        k0 = torch.ceil(lo - f).long()
+        k1 = torch.ceil(hi - f).long() - 1              # lo <= f + k < hi  <=>  k0 <= k <= k1
+        if not periodic:
+            k0 = torch.clamp(k0, min=0)
+            k1 = torch.clamp(k1, max=0)
+        kmin.append(k0)
+        span.append((k1 - k0 + 1).clamp(min=0))
+    per_atom = span[0] * span[1] * span[2]
+    atom = torch.repeat_interleave(torch.arange(n, device=device), per_atom)
+    first = torch.cumsum(per_atom, 0) - per_atom
+    j = torch.arange(atom.shape[0], device=device) - first[atom]
+    s0, s1 = span[0][atom], span[1][atom]
+    image = torch.stack([kmin[0][atom] + j % s0, kmin[1][atom] + (j // s0) % s1, kmin[2][atom] + j // (s0 * s1)], 1)
+    own_copy = (owner[atom] == rank) & (image == 0).all(1)
+    return atom[~own_copy], image[~own_copy]
+
+
+def _ghost_counts(ghost_owner: Tensor, world: int) -> Tensor:
+    return torch.bincount(ghost_owner, minlength=world)
+
+
 class DomainParallel(nn.Module):
     """Evaluate one structure split over the processes of a distributed launch.
 
@@ -242,12 +295,11 @@ class DomainParallel(nn.Module):
                  receptive_field: Optional[float] = None, compute_stress: bool = True, group=None,
                  halo: str = "auto", skin: float = 0.0, exchange: str = "collective"):
         super().__init__()
-        inner = getattr(model, "model", None)
-        if inner is not None and hasattr(model, "compute_forces"):
-            model = inner
+        if hasattr(model, "compute_forces") and getattr(model, "model", None) is not None:
+            model = model.model
         if receptive_field is None:
-            field = getattr(model, "receptive_field", None)
-            receptive_field = field() if callable(field) else None
+            rf = getattr(model, "receptive_field", None)
+            receptive_field = rf() if callable(rf) else None
         if receptive_field is None:
             raise ValueError(f"{type(model).__name__} has no bounded receptive field; pass "
                              "receptive_field= to decompose it anyway")
@@ -267,7 +319,7 @@ class DomainParallel(nn.Module):
         self.layer = halo == "layer" or (halo == "auto" and refreshes)
         self.need = self.cutoff if self.layer else self.receptive_field
         self.skin = float(skin)
-        self.grid = tuple(int(g) for g in grid) if grid is not None else None
+        self.grid = None if grid is None else tuple(int(g) for g in grid)
         self.compute_stress = compute_stress
         self.group = group
         self.exchange = exchange
@@ -291,120 +343,96 @@ class DomainParallel(nn.Module):
         return self._build(data.pos, data.atomic_numbers, data.cell[0] if periodic else None,
                            data.total_charge, data.spin_multiplicity)
 
+    def _handshake(self, owned: Tensor, ghosts: Tensor, ghost_owner: Tensor, rank: int, world: int):
+        """Send lists and peer offsets; raises :class:`PlanError` on every process together."""
+        device = ghosts.device
+        recv_t = _ghost_counts(ghost_owner, world)
+        if world == 1:
+            ok = int(recv_t.sum()) == int(ghosts.shape[0])
+            send_rows = torch.searchsorted(owned, ghosts)
+            ok = ok and bool((owned[send_rows.clamp(max=max(len(owned) - 1, 0))] == ghosts).all()) \
+                if len(ghosts) else ok
+            if not ok:
+                raise PlanError("inconsistent halo plan: ghost counts or owners")
+            counts = recv_t.tolist()
+            return send_rows, counts, counts, [0], [0], int(ghosts.shape[0])
+        send_t = torch.empty_like(recv_t)
+        dist.all_to_all_single(send_t, recv_t, group=self.group)
+        consistent = int(recv_t.sum()) == int(ghosts.shape[0]) and bool((send_t >= 0).all())
+        if not _agree(consistent, world, self.group, device):
+            raise PlanError("inconsistent halo plan: a process's ghost counts do not match its ghost list")
+        send_counts, recv_counts = send_t.tolist(), recv_t.tolist()
+        requested = ghosts.new_empty(int(send_t.sum()))
+        dist.all_to_all_single(requested, ghosts, send_counts, recv_counts, group=self.group)
+        send_rows = torch.searchsorted(owned, requested)
+        mine = True
+        if len(requested):
+            mine = len(owned) > 0 and bool((owned[send_rows.clamp(max=len(owned) - 1)] == requested).all())
+        if not _agree(mine, world, self.group, device):
+            raise PlanError("inconsistent halo plan: the processes disagree on the owners of the atoms")
+        # per peer: where its rows start in my ghost list, where my rows for it start in my send
+        # list, my largest row count; received back, the first two columns are where my rows
+        # start in the peer's lists
+        table = torch.stack([torch.cumsum(recv_t, 0) - recv_t, torch.cumsum(send_t, 0) - send_t,
+                             torch.full_like(recv_t, max(len(ghosts), len(requested)))], 1).contiguous()
+        back = torch.empty_like(table)
+        dist.all_to_all_single(back, table, group=self.group)
+        return (send_rows, send_counts, recv_counts, back[:, 0].tolist(), back[:, 1].tolist(),
+                int(back[:, 2].max()))
+
+    def _local_edges(self, local: Tensor, cell: Optional[Tensor], grid, device):
+        reach = self.cutoff + self.skin + HALO_MARGIN
+        if not len(local):
+            return (torch.zeros((2, 0), dtype=torch.long, device=device),
+                    torch.zeros((0, 3), dtype=torch.long, device=device), None)
+        if cell is None:
+            ei, sh = build_neighbor_list(local, reach)
+            return ei, sh, None
+        # periodic along the uncut axes only; the cut axes carry explicit ghost images
+        uncut = torch.tensor([g == 1 for g in grid])
+        if not bool(uncut.any()):
+            ei, sh = build_neighbor_list(local, reach)
+            return ei, sh, None
+        ei, sh = build_neighbor_list(local, reach, cell, uncut)
+        return ei, sh, uncut
+
     def _build(self, positions: Tensor, atomic_numbers: Tensor, cell: Optional[Tensor],
                total_charge: Optional[Tensor], spin_multiplicity: Optional[Tensor]) -> DomainPlan:
         rank, world = _process(self.group)
         pos = positions.detach().to(torch.float64)
-        device, n = pos.device, int(pos.shape[0])
+        device = pos.device
         halo = self.need + self.skin + HALO_MARGIN
         periodic = cell is not None
         if periodic:
             cell = cell.detach().to(device=device, dtype=torch.float64)
-            inv = torch.linalg.inv(cell)
-            raw = _rows3(pos, inv)
-            frac = raw - torch.floor(raw)
-            widths_t = 1.0 / torch.linalg.norm(inv, dim=0)      # plane spacings of the cell
-        else:
-            low = pos.min(0).values if n else pos.new_zeros(3)
-            widths_t = (pos.max(0).values - low if n else pos.new_zeros(3)) + 1e-6
-            frac = (pos - low) / widths_t
-        widths = [float(w) for w in widths_t.cpu()]
+        frac, widths_t, inv = _frame(pos, cell)
+        widths = widths_t.tolist()
         grid = self.grid if self.grid is not None else choose_grid(world, widths, halo)
         if len(grid) != 3 or math.prod(grid) != world:
             raise ValueError(f"grid {tuple(grid)} does not hold {world} processes")
         coords = (rank // (grid[1] * grid[2]), (rank // grid[2]) % grid[1], rank % grid[2])
-
-        g = torch.tensor(grid, device=device)
-        cells = torch.minimum(torch.floor(frac * g).long().clamp(min=0), g - 1)
-        owner = (cells[:, 0] * grid[1] + cells[:, 1]) * grid[2] + cells[:, 2]
-        owned = (owner == rank).nonzero().flatten()
+        owner = _owners(frac, grid)
+        owned = torch.nonzero(owner == rank).flatten()
         counts = torch.bincount(owner, minlength=world).tolist()
-        order = torch.sort(owner, stable=True).indices
-
-        # ghost shell: atoms (or their periodic images along cut axes) within `halo` of the slab
-        masks, steps = [], []
-        for a in range(3):
-            if grid[a] == 1:
-                masks.append(torch.ones(n, 1, dtype=torch.bool, device=device))
-                steps.append(torch.zeros(1, dtype=torch.long, device=device))
-                continue
-            shell = halo / widths[a]
-            lo, hi = coords[a] / grid[a] - shell, (coords[a] + 1) / grid[a] + shell
-            m = math.floor(shell) + 1 if periodic else 0
-            image = torch.arange(-m, m + 1, device=device)
-            x = frac[:, a, None] + image.to(torch.float64)
-            masks.append((x >= lo) & (x < hi))
-            steps.append(image)
-        mask = masks[0][:, :, None, None] & masks[1][:, None, :, None] & masks[2][:, None, None, :]
-        atom, i0, i1, i2 = mask.nonzero(as_tuple=True)
-        image = torch.stack([steps[0][i0], steps[1][i1], steps[2][i2]], dim=1)
-        keep = ~((owner[atom] == rank) & (image == 0).all(1))
-        atom, image = atom[keep], image[keep]
-        by_owner = torch.sort(owner[atom], stable=True).indices
+        order = torch.argsort(owner, stable=True)
+        atom, image = _halo_members(frac, owner, rank, coords, grid, widths, halo, periodic)
+        by_owner = torch.argsort(owner[atom], stable=True)
         ghosts, ghost_image = atom[by_owner], image[by_owner]
-        recv_counts_t = torch.bincount(owner[ghosts], minlength=world)
-
-        remote_offsets = None
-        if world > 1:
-            # every process asks the owners of its ghosts for them
-            send_counts_t = torch.empty_like(recv_counts_t)
-            dist.all_to_all_single(send_counts_t, recv_counts_t, group=self.group)
-            send_counts = send_counts_t.tolist()
-            recv_counts = recv_counts_t.tolist()
-            requested = ghosts.new_empty(int(sum(send_counts)))
-            dist.all_to_all_single(requested, ghosts, send_counts, recv_counts, group=self.group)
-            # where this process's rows start inside every receiver's ghost list, and where its
-            # ghosts start inside every owner's send list
-            starts = torch.stack([torch.cumsum(recv_counts_t, 0) - recv_counts_t,
-                                  torch.cumsum(send_counts_t, 0) - send_counts_t], 1).contiguous()
-            remote = torch.empty_like(starts)
-            dist.all_to_all_single(remote, starts, group=self.group)
-            remote_offsets, remote_send_offsets = remote[:, 0].tolist(), remote[:, 1].tolist()
-            most = torch.tensor([max(len(ghosts), len(requested))], dtype=torch.long, device=device)
-            dist.all_reduce(most, op=dist.ReduceOp.MAX, group=self.group)
-            max_rows = int(most[0])
-        else:
-            send_counts, requested = recv_counts_t.tolist(), ghosts
-            recv_counts = recv_counts_t.tolist()
-            remote_offsets, remote_send_offsets, max_rows = [0], [0], len(ghosts)
-        send_rows = torch.searchsorted(owned, requested)
-        if len(requested) and not (len(owned) and bool(
-                (owned[send_rows.clamp(max=len(owned) - 1)] == requested).all())):
-            raise RuntimeError("the processes disagree on the owners of the atoms")
-
+        send_rows, send_counts, recv_counts, r_off, r_send_off, max_rows = self._handshake(
+            owned, ghosts, owner[ghosts], rank, world)
         if periodic:
-            local = _rows3(torch.cat([frac[owned], frac[ghosts] + ghost_image.to(torch.float64)]), cell)
+            local = _apply3(torch.cat([frac[owned], frac[ghosts] + ghost_image.to(torch.float64)]), cell)
             reference = frac[owned]
         else:
             local = torch.cat([pos[owned], pos[ghosts]])
             reference = pos[owned]
-        reach = self.cutoff + self.skin + HALO_MARGIN
-        native = [periodic and grid[a] == 1 for a in range(3)]
-        if not len(local):
-            edge_index = torch.zeros((2, 0), dtype=torch.long, device=device)
-            cell_shifts = torch.zeros((0, 3), dtype=torch.long, device=device)
-            pbc = torch.tensor(native) if any(native) else None
-        elif any(native):
-            # stretch the cut axes far beyond the shell so only the explicit images are
-            # neighbours along them, while the uncut axes keep the box's periodicity
-            search = cell.clone()
-            for a in range(3):
-                if not native[a]:
-                    search[a] *= 1.0 + 1.0 / grid[a] + 2.0 * (halo + reach) / widths[a]
-            edge_index, cell_shifts = build_neighbor_list(local, reach, search,
-                                                          torch.ones(3, dtype=torch.bool))
-            cut = torch.tensor([not x for x in native], device=cell_shifts.device)
-            if bool((cell_shifts[:, cut] != 0).any()):
-                raise RuntimeError("a neighbour across a cut axis was found through the box's periodicity")
-            pbc = torch.tensor(native)
-        else:
-            edge_index, cell_shifts = build_neighbor_list(local, reach)
-            pbc = None
+        edge_index, cell_shifts, pbc = self._local_edges(local, cell, grid, device)
         if self.layer:
             # ghost features are replaced by their owners' before they are read: no messages
             # into ghosts are needed
-            keep = edge_index[1] < len(owned)
-            edge_index, cell_shifts = edge_index[:, keep], cell_shifts[keep.to(cell_shifts.device)]
+            into_owned = edge_index[1] < len(owned)
+            edge_index = edge_index[:, into_owned]
+            cell_shifts = cell_shifts[into_owned.to(cell_shifts.device)]
         return DomainPlan(
             grid=tuple(grid), rank=rank, world=world, owned=owned, ghosts=ghosts,
             ghost_shifts=ghost_image if periodic else None, send_rows=send_rows,
@@ -412,63 +440,66 @@ class DomainParallel(nn.Module):
             cell_shifts=cell_shifts.to(device), pbc=pbc, atomic_numbers=atomic_numbers,
             total_charge=total_charge, spin_multiplicity=spin_multiplicity, reference=reference,
             cell=cell, counts=counts, order=order, need=self.need, skin=self.skin,
-            remote_offsets=remote_offsets, remote_send_offsets=remote_send_offsets, max_rows=max_rows,
-            inv_cell=inv if periodic else None)
+            remote_offsets=r_off, remote_send_offsets=r_send_off, max_rows=max_rows, inv_cell=inv)
 
-    def _cell(self, plan: DomainPlan, cell: Optional[Tensor]) -> Optional[Tensor]:
-        if plan.cell is None:
-            return None
-        if cell is None:
+    def _plan_cell(self, plan: DomainPlan, cell: Optional[Tensor]) -> Optional[Tensor]:
+        """The cell to evaluate with: the given one (``(3, 3)`` or ``(1, 3, 3)``), else the plan's."""
+        if plan.cell is None or cell is None:
             return plan.cell
-        return cell[0] if cell.dim() == 3 else cell
+        return cell.reshape(3, 3)
+
+    def _inverse(self, plan: DomainPlan, cell64: Tensor) -> Tuple[Tensor, bool]:
+        unchanged = plan.inv_cell is not None and (cell64 is plan.cell or bool(torch.equal(cell64, plan.cell)))
+        return (plan.inv_cell if unchanged else torch.linalg.inv(cell64)), unchanged
 
     @torch.no_grad()
     def holds(self, plan: DomainPlan, pos: Tensor, cell: Optional[Tensor] = None) -> bool:
-        """Whether the plan is valid for new owned positions (and cell): it holds while
-        ``need + 2 d <= (1 - e)(need + skin)`` with ``d`` the largest displacement since the
-        plan was built and ``e`` the relative strain of the cell. The same on every process."""
-        cell = self._cell(plan, cell)
+        """Whether the plan is still valid for new owned positions (and cell).
+
+        The ghost shell stays complete while ``need + 2 d <= (1 - e)(need + skin)`` with ``d``
+        the largest displacement since the plan was built (minimum image) and ``e`` the
+        relative strain of the cell (spectral norm of ``h0^-1 (h - h0)``); ``d`` is agreed over
+        the processes, so every process gets the same answer."""
+        cell = self._plan_cell(plan, cell)
+        p64 = pos.detach().to(torch.float64)
         strain = 0.0
         if cell is None:
-            moved = pos.detach().to(torch.float64) - plan.reference
+            moved = p64 - plan.reference
         else:
-            cell = cell.detach().to(torch.float64)
-            same = plan.inv_cell is not None and (cell is plan.cell or bool(torch.equal(cell, plan.cell)))
-            inv = plan.inv_cell if same else torch.linalg.inv(cell)
-            frac = _rows3(pos.detach().to(torch.float64), inv) - plan.reference
-            moved = _rows3(frac - torch.round(frac), cell)
-            if not same:
-                strain = float(torch.linalg.matrix_norm(torch.linalg.inv(plan.cell) @ (cell - plan.cell), ord=2))
-        largest = moved.norm(dim=-1).max() if len(moved) else moved.new_zeros(())
+            c64 = cell.detach().to(torch.float64)
+            inv, unchanged = self._inverse(plan, c64)
+            df = _apply3(p64, inv) - plan.reference
+            moved = _apply3(df - torch.round(df), c64)
+            if not unchanged:
+                strain = float(torch.linalg.matrix_norm(torch.linalg.solve(plan.cell, c64 - plan.cell), ord=2))
+        worst = moved.norm(dim=-1).max().reshape(1) if len(moved) else moved.new_zeros(1)
         if plan.world > 1:
-            largest = largest.reshape(1).clone()
-            dist.all_reduce(largest, op=dist.ReduceOp.MAX, group=self.group)
-            largest = largest[0]
-        need = plan.need
-        return need + 2.0 * float(largest) <= (1.0 - strain) * (need + plan.skin + HALO_MARGIN)
+            dist.all_reduce(worst, op=dist.ReduceOp.MAX, group=self.group)
+        budget = (1.0 - strain) * (plan.need + plan.skin + HALO_MARGIN)
+        return plan.need + 2.0 * float(worst[0]) <= budget
 
     @torch.no_grad()
     def reshard(self, plan: DomainPlan, pos: Tensor, *fields: Tensor, cell: Optional[Tensor] = None) -> tuple:
         """A new plan for the current positions, with ``pos`` and every per-atom field moved
         to the atoms' new owners. Returns ``(plan, pos, *fields)``."""
-        cell = self._cell(plan, cell)
-        whole = [self._gather(plan, x) for x in (pos,) + fields]
-        new = self._build(whole[0], plan.atomic_numbers, cell, plan.total_charge, plan.spin_multiplicity)
-        return (new,) + tuple(x[new.owned] for x in whole)
+        cell = self._plan_cell(plan, cell)
+        full = [self._gather(plan, x) for x in (pos,) + fields]
+        new = self._build(full[0], plan.atomic_numbers, cell, plan.total_charge, plan.spin_multiplicity)
+        return (new,) + tuple(x.index_select(0, new.owned) for x in full)
 
     def _gather(self, plan: DomainPlan, rows: Tensor) -> Tensor:
         """Rows of every process's owned atoms, in the atom order of the structure."""
-        whole = rows.new_empty((plan.n_atoms,) + tuple(rows.shape[1:]))
+        out = rows.new_empty((plan.n_atoms,) + tuple(rows.shape[1:]))
         if plan.world == 1:
-            whole[plan.owned] = rows
-            return whole
-        size = max(plan.counts)
-        padded = rows.new_zeros((size,) + tuple(rows.shape[1:]))
-        padded[:len(rows)] = rows
-        parts = [torch.empty_like(padded) for _ in range(plan.world)]
-        dist.all_gather(parts, padded.contiguous(), group=self.group)
-        whole[plan.order] = torch.cat([p[:c] for p, c in zip(parts, plan.counts)])
-        return whole
+            out[plan.owned] = rows
+            return out
+        width = max(plan.counts)
+        mine = rows.new_zeros((width,) + tuple(rows.shape[1:]))
+        mine[:rows.shape[0]] = rows
+        parts = [torch.empty_like(mine) for _ in range(plan.world)]
+        dist.all_gather(parts, mine.contiguous(), group=self.group)
+        out[plan.order] = torch.cat([part[:c] for part, c in zip(parts, plan.counts)])
+        return out
 
     # ---------------------------------------------------------------- exchange
     def _get_exchanger(self, plan: DomainPlan, like: Tensor):
@@ -479,14 +510,14 @@ class DomainParallel(nn.Module):
             self._exchanger = PeerHaloExchange(like.device, self.group)
         return self._exchanger
 
-    def _exchange(self, plan: DomainPlan, rows: Tensor, ties: List[Tensor]) -> Tensor:
+    def _exchange(self, plan: DomainPlan, rows: Tensor, links: List[Tensor]) -> Tensor:
         """Rows of the ghosts, sent by their owners from ``rows`` (the owned atoms)."""
         if plan.world == 1:
             return rows.index_select(0, plan.send_rows)
-        if ties:
-            rows = rows + _tie(ties[-1]).to(rows.dtype)
-        out = _AllToAllRows.apply(rows, plan, self.group, self._get_exchanger(plan, rows))
-        ties.append(out)
+        if links:
+            rows = rows + _order_link(links[-1]).to(rows.dtype)
+        out = _RowExchange.apply(rows, plan, self.group, self._get_exchanger(plan, rows))
+        links.append(out)
         return out
 
     # ---------------------------------------------------------------- evaluation
@@ -495,43 +526,41 @@ class DomainParallel(nn.Module):
         periodic structure with ``compute_stress``, the stress ``(1, 3, 3)``."""
         if pos.shape[0] != plan.n_owned:
             raise ValueError(f"{pos.shape[0]} positions for the {plan.n_owned} atoms of the plan")
-        cell = self._cell(plan, cell)
-        p = pos.detach().requires_grad_(True)
-        dtype, device = p.dtype, p.device
-        strain, volume, own = None, None, p
+        cell = self._plan_cell(plan, cell)
+        x = pos.detach().requires_grad_(True)
+        dtype, device = x.dtype, x.device
+        strain, volume, own = None, None, x
         if cell is not None:
             c64 = cell.detach().to(torch.float64)
-            same = plan.inv_cell is not None and (cell is plan.cell or bool(torch.equal(c64, plan.cell)))
-            inv = plan.inv_cell if same else torch.linalg.inv(c64)
-            cell = cell.detach().to(dtype)
+            inv, _ = self._inverse(plan, c64)
             volume = torch.linalg.det(c64).abs().reshape(1)
-            jumps = torch.round(_rows3(p.detach().to(torch.float64), inv) - plan.reference).to(dtype)
+            # whole cells each owned atom moved since the plan (to bring it back next to its ghosts)
+            wraps = torch.round(_apply3(x.detach().to(torch.float64), inv) - plan.reference).to(dtype)
+            cell = cell.detach().to(dtype)
             if self.compute_stress:
                 strain = torch.zeros((3, 3), dtype=dtype, device=device, requires_grad=True)
-                sym = 0.5 * (strain + strain.transpose(0, 1))
+                sym = 0.5 * (strain + strain.t())
                 own = own + own @ sym
                 cell = cell + cell @ sym
-            # owned atoms brought back next to where the plan saw them
-            own = own - _rows3(jumps, cell)
-        ties: List[Tensor] = []
-        ghosts = self._exchange(plan, own, ties)
+            own = own - _apply3(wraps, cell)
+        links: List[Tensor] = []
+        ghost_pos = self._exchange(plan, own, links)
         if cell is not None:
-            ghosts = ghosts + _rows3(plan.ghost_shifts.to(dtype), cell)
-        local = torch.cat([own, ghosts])
-        numbers = plan.atomic_numbers[plan.index]
+            ghost_pos = ghost_pos + _apply3(plan.ghost_shifts.to(dtype), cell)
+        local = torch.cat([own, ghost_pos])
+        numbers = plan.atomic_numbers.index_select(0, plan.index)
         if plan.n_local == 0:
             # an empty sub-domain evaluates one isolated stand-in (energy dropped) so that it
             # takes part in every exchange of the others
             local = local.new_zeros((1, 3))
             numbers = plan.atomic_numbers[:1]
-        edge_index, cell_shifts = plan.edge_index, plan.cell_shifts
         with torch.no_grad():
-            vec = local[edge_index[1]] - local[edge_index[0]]
+            d = local.index_select(0, plan.edge_index[1]) - local.index_select(0, plan.edge_index[0])
             if plan.pbc is not None:
-                vec = vec + _rows3(cell_shifts.to(dtype), cell)
-            keep = (vec * vec).sum(-1) < self.cutoff ** 2
-        edge_index, cell_shifts = edge_index[:, keep], cell_shifts[keep]
-        model_dtype = _model_dtype(self.model)
+                d = d + _apply3(plan.cell_shifts.to(dtype), cell)
+            inside = (d * d).sum(-1) < self.cutoff ** 2
+        edge_index, cell_shifts = plan.edge_index[:, inside], plan.cell_shifts[inside]
+        mdt = _model_dtype(self.model)
         n_local = int(local.shape[0])
         graph = AtomicGraph(
             pos=local, atomic_numbers=numbers, edge_index=edge_index, cell_shifts=cell_shifts,
@@ -540,44 +569,44 @@ class DomainParallel(nn.Module):
             cell=cell[None] if plan.pbc is not None else None,
             pbc=plan.pbc[None].to(device) if plan.pbc is not None else None,
             total_charge=plan.total_charge, spin_multiplicity=plan.spin_multiplicity,
-            compute_dtype=model_dtype if model_dtype is not None and model_dtype != dtype else None)
+            compute_dtype=mdt if mdt is not None and mdt != dtype else None)
         graph.edge_order = "dst"
-        with domain_hooks(_Hooks(self, plan, ties)):
+        with domain_hooks(_Hooks(self, plan, links)):
             out = self.model(graph)
         energy = out["node_energy"][:plan.n_owned].to(torch.float64).sum()
-        for t in ties:
-            energy = energy + _tie(t)
-        inputs = [p] + ([strain] if strain is not None else [])
-        grads = [None] * len(inputs)
+        for t in links:
+            energy = energy + _order_link(t)
+        wrt = [x] + ([strain] if strain is not None else [])
+        grads: List[Optional[Tensor]] = [None] * len(wrt)
         if energy.requires_grad:
             # only position / strain derivatives: the fused ops skip their weight gradients
             with force_pass():
-                grads = list(torch.autograd.grad([energy], inputs, allow_unused=True))
-        g_pos = grads[0] if grads[0] is not None else torch.zeros_like(p)
-        g_strain = (grads[1] if strain is not None and grads[1] is not None
-                    else torch.zeros((3, 3), dtype=torch.float64, device=device))
-        total = torch.cat([energy.detach().reshape(1), g_strain.to(torch.float64).reshape(9)])
+                grads = list(torch.autograd.grad([energy], wrt, allow_unused=True))
+        g_pos = grads[0] if grads[0] is not None else torch.zeros_like(x)
+        g_strain = grads[1] if strain is not None and grads[1] is not None else \
+            torch.zeros((3, 3), dtype=torch.float64, device=device)
+        summed = torch.cat([energy.detach().reshape(1), g_strain.to(torch.float64).reshape(9)])
         if plan.world > 1:
-            dist.all_reduce(total, group=self.group)
+            dist.all_reduce(summed, group=self.group)
         if self._exchanger is not None:
             self._exchanger.check()
-        result = {"energy": total[:1], "forces": -g_pos.to(dtype)}
+        result = {"energy": summed[:1], "forces": -g_pos.to(dtype)}
         if strain is not None:
-            result["stress"] = (total[1:10].view(1, 3, 3) / volume).to(dtype)
+            result["stress"] = (summed[1:].view(1, 3, 3) / volume).to(dtype)
         return result
 
     def forward(self, data: AtomicGraph) -> dict:
-        """Energy, forces (all atoms, gathered) and stress of ``data``, given on every
-        process; the plan of the previous call is reused while it holds."""
+        """Energy, forces (all atoms, gathered) and stress of ``data``, given on every process;
+        the plan of the previous call is reused while it holds."""
         periodic = data.cell is not None and data.pbc is not None and bool(data.pbc.any())
         cell = data.cell[0] if periodic else None
         plan = self._plan
-        if (plan is None or plan.n_atoms != data.num_nodes or (plan.cell is None) == periodic
-                or not torch.equal(plan.atomic_numbers, data.atomic_numbers)
-                or not self.holds(plan, data.pos[plan.owned], cell)):
+        reusable = (plan is not None and plan.n_atoms == data.num_nodes and (plan.cell is not None) == periodic
+                    and torch.equal(plan.atomic_numbers, data.atomic_numbers))
+        if not (reusable and self.holds(plan, data.pos.index_select(0, plan.owned), cell)):
             plan = self._plan = self.plan(data)
         plan.total_charge, plan.spin_multiplicity = data.total_charge, data.spin_multiplicity
-        out = self.evaluate(plan, data.pos[plan.owned], cell)
+        out = self.evaluate(plan, data.pos.index_select(0, plan.owned), cell)
         out["forces"] = self._gather(plan, out["forces"])
         return out
 
@@ -585,3 +614,30 @@ class DomainParallel(nn.Module):
         if self._exchanger is not None:
             self._exchanger.close()
             self._exchanger = None
+
+
+class _Hooks:
+    """The object the model's ``refresh_ghosts`` / ``whole_structure_sum`` calls go to."""
+
+    def __init__(self, dp: DomainParallel, plan: DomainPlan, links: List[Tensor]):
+        self.dp, self.plan, self.links = dp, plan, links
+
+    def refresh(self, x: Tensor) -> Tensor:
+        plan = self.plan
+        if not self.dp.layer:
+            return x
+        rows = max(plan.n_local, 1)
+        if x.shape[0] != rows:
+            raise ValueError(f"refresh_ghosts got {x.shape[0]} rows for {rows} local atoms")
+        fresh = self.dp._exchange(plan, x[:plan.n_owned], self.links)
+        return torch.cat([x[:plan.n_owned], fresh, x[plan.n_local:]])
+
+    def whole_sum(self, values: Tensor, batch: Tensor, num_graphs: int) -> Tensor:
+        n = self.plan.n_owned
+        part = structure_sum(values[:n], batch[:n], num_graphs)
+        if self.plan.world > 1:
+            if self.links:
+                part = part + _order_link(self.links[-1]).to(part.dtype)
+            part = _SumOverRanks.apply(part, self.dp.group)
+            self.links.append(part)
+        return part

@@ -133,6 +133,15 @@ class Trainer:
         else:
             self.scheduler = None
         self.ema = EMA(self.params, o.ema_decay) if o.ema_decay > 0 else None
+        self._fused = None
+        fs = cfg.trainer.fused_step
+        if fs is True or (fs == "auto" and self.device.type == "cuda"):
+            from . import mace_step
+            ok, why = mace_step.supports(self.module, o)
+            if ok:
+                self._fused = mace_step.MACEStep(self.module, o.energy_weight, o.force_weight)
+            elif fs is True:
+                raise ValueError(f"trainer.fused_step: {why}")
         self.train_set, self.val_set, self.test_set = self._splits(train, val, test)
         self.callbacks = list(callbacks or [])
         from .loggers import make_loggers
@@ -224,9 +233,12 @@ class Trainer:
 
     def _train_step_impl(self, batch: AtomicGraph):
         self.grad_sync.zero_()
-        loss, logs, _ = self._loss(batch)
-        with params_only():
-            loss.backward(inputs=self.params)
+        if self._fused is not None:
+            loss, logs, _ = self._fused(batch)
+        else:
+            loss, logs, _ = self._loss(batch)
+            with params_only():
+                loss.backward(inputs=self.params)
         self.grad_sync.reduce()
         if self.cfg.optim.clip_grad > 0:
             torch.nn.utils.clip_grad_norm_(self.params, self.cfg.optim.clip_grad, foreach=True)
