@@ -35,7 +35,8 @@ OUR_KERNELS = ("conv_gather", "conv_edge", "conv_scatter", "symcon_", "edge_geom
                "gemm_pack_kernel", "gemm_rows_kernel", "gemm_reduce_kernel", "gemm_ws_kernel", "gemm_ws_pack_kernel",
                "gemm_reduce_ws_kernel", "sum_partials_kernel", "radial_basis_kernel", "radial_act_kernel",
                "radial_dact_kernel", "nb_count", "nb_write", "mp_real_kernel", "pme_spread_kernel",
-               "pme_gather_kernel")
+               "pme_gather_kernel", "node_mm_kernel", "node_mmT_kernel", "node_sum_kernel", "node_pack",
+               "species_sort_kernel")
 
 
 def parse():

@@ -465,3 +465,18 @@ def test_equiformer_v2(kw, periodic):
         ref.set_use_fast(False)
     compare(mine, ref, batch(periodic and not cfg.get("direct_forces"), cutoff=4.0, species=[1, 6, 7, 8]),
             periodic and not cfg.get("direct_forces"), rtol=1e-9, atol=1e-9)
+
+
+@pytest.mark.parametrize("periodic", [False, True])
+def test_acsf_fit_scaling_matches_reference(periodic):
+    from xnn_b200.featurizers.acsf import AtomCenteredSymmetryFunctions
+    reff = ref_module("xnn.dnn.featurizers.acsf")
+    sp = [6, 8] if not periodic else [8]
+    mine = AtomCenteredSymmetryFunctions(sp, _CUTS, _functions(sp), mode="center_scale").double()
+    ref = reff.AtomCenteredSymmetryFunctions(sp, _CUTS, _functions(sp), mode="center_scale").double()
+    graphs = [batch(periodic, cutoff=5.0, species=sp, seed=s) for s in (2, 5)]
+    mine.fit_scaling([g.clone() for g in graphs])
+    from ref_oracle import ref_graph
+    ref.fit_scaling([ref_graph(g) for g in graphs])
+    for name in ("stat_min", "stat_max", "stat_avg"):
+        torch.testing.assert_close(getattr(mine, name), getattr(ref, name), rtol=1e-12, atol=1e-12, msg=name)

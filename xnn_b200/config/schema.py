@@ -117,7 +117,7 @@ class TrainerConfig:
     graph_headroom: float = 0.05   # padding headroom of a captured step
     #: the hand-written MACE step (energies, forces, loss and gradients without autograd):
     #: "auto" on CUDA when the model and loss are covered, True / False to force it on / off
-    fused_step: Any = False
+    fused_step: Any = "auto"
 
 
 @dataclass

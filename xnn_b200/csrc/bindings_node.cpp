@@ -29,6 +29,7 @@ struct NodeMMArgs {
   int n;
   int* status;
   long long spin_limit;
+  unsigned long long* trace;   // optional: per CTA, globaltimer at the phase boundaries (8 slots)
 };
 struct NodeRedProb {
   const float* X[2];
@@ -50,6 +51,7 @@ struct NodeRedArgs {
   int n;
   int* status;
   long long spin_limit;
+  unsigned long long* trace;
 };
 struct PackJob {
   const float* W;
@@ -87,7 +89,8 @@ const int* opt_i32(const c10::optional<torch::Tensor>& t, const char* what) {
 void node_mm(std::vector<torch::Tensor> X0, std::vector<c10::optional<torch::Tensor>> X1,
              std::vector<torch::Tensor> Y, std::vector<torch::Tensor> Wp,
              std::vector<c10::optional<torch::Tensor>> perm, std::vector<c10::optional<torch::Tensor>> seg,
-             std::vector<int64_t> rows, std::vector<bool> accumulate, torch::Tensor status, int64_t spin_limit) {
+             std::vector<int64_t> rows, std::vector<bool> accumulate, torch::Tensor status, int64_t spin_limit,
+             c10::optional<torch::Tensor> trace) {
   const size_t n = X0.size();
   TORCH_CHECK(n >= 1 && n <= NM_MAX_PROBS, "node_mm: 1..", NM_MAX_PROBS, " problems");
   TORCH_CHECK(X1.size() == n && Y.size() == n && Wp.size() == n && perm.size() == n && seg.size() == n &&
@@ -97,6 +100,11 @@ void node_mm(std::vector<torch::Tensor> X0, std::vector<c10::optional<torch::Ten
   a.n = (int)n;
   a.status = status.data_ptr<int>();
   a.spin_limit = spin_limit;
+  a.trace = nullptr;
+  if (trace.has_value() && trace->defined()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == torch::kInt64, "node_mm: int64 trace buffer");
+    a.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
   int tiles = 0, max_n = 16;
   for (size_t i = 0; i < n; ++i) {
     NodeMMProb& p = a.p[i];
@@ -133,6 +141,7 @@ void node_mm(std::vector<torch::Tensor> X0, std::vector<c10::optional<torch::Ten
     max_n = std::max(max_n, p.N);
   }
   auto st = at::cuda::getCurrentCUDAStream();
+  if (a.trace != nullptr) TORCH_CHECK(trace->numel() >= (int64_t)tiles * 8, "node_mm: trace buffer too small");
   cudaError_t e = node_mm_launch(a, tiles, max_n, st);
   TORCH_CHECK(e == cudaSuccess, "node_mm: ", cudaGetErrorString(e));
 }
@@ -142,7 +151,8 @@ void node_mmT(std::vector<torch::Tensor> X0, std::vector<torch::Tensor> D0,
               std::vector<c10::optional<torch::Tensor>> X1, std::vector<c10::optional<torch::Tensor>> D1,
               std::vector<c10::optional<torch::Tensor>> perm, std::vector<c10::optional<torch::Tensor>> seg,
               std::vector<int64_t> rows0, std::vector<int64_t> rows1, std::vector<torch::Tensor> out,
-              std::vector<double> scale, torch::Tensor counters, torch::Tensor status, int64_t spin_limit) {
+              std::vector<double> scale, torch::Tensor counters, torch::Tensor status, int64_t spin_limit,
+              c10::optional<torch::Tensor> trace) {
   const size_t n = X0.size();
   TORCH_CHECK(n >= 1 && n <= NR_MAX_PROBS, "node_mmT: 1..", NR_MAX_PROBS, " problems");
   TORCH_CHECK(D0.size() == n && X1.size() == n && D1.size() == n && perm.size() == n && seg.size() == n &&
@@ -154,6 +164,11 @@ void node_mmT(std::vector<torch::Tensor> X0, std::vector<torch::Tensor> D0,
   a.n = (int)n;
   a.status = status.data_ptr<int>();
   a.spin_limit = spin_limit;
+  a.trace = nullptr;
+  if (trace.has_value() && trace->defined()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == torch::kInt64, "node_mmT: int64 trace buffer");
+    a.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
   int ctas = 0, max_k1 = 16, max_n = 16;
   int64_t partial_floats = 0;
   std::vector<int64_t> poff(n);
@@ -207,6 +222,7 @@ void node_mmT(std::vector<torch::Tensor> X0, std::vector<torch::Tensor> D0,
   }
   auto partial = torch::empty({partial_floats}, X0[0].options());
   for (size_t i = 0; i < n; ++i) a.p[i].partial = partial.data_ptr<float>() + poff[i];
+  if (a.trace != nullptr) TORCH_CHECK(trace->numel() >= (int64_t)ctas * 8, "node_mmT: trace buffer too small");
   auto st = at::cuda::getCurrentCUDAStream();
   cudaError_t e = node_mmT_launch(a, ctas, max_k1, max_n, st);
   TORCH_CHECK(e == cudaSuccess, "node_mmT: ", cudaGetErrorString(e));

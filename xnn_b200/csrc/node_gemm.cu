@@ -11,8 +11,8 @@
 //              (two inputs through stacked weights: Y = X1 W1 + X2 W2 in one accumulator).
 //   node_mmT : a table of weight-gradient reductions G = scale * sum_rows X^T D (up to two row
 //              sets per output: primal and tangent rows). Each problem splits its rows over CTAs;
-//              every CTA writes a partial block and the last CTA to finish (an arrival counter)
-//              sums the partials in a fixed order: one launch, deterministic.
+//              every CTA writes a partial block and a second kernel sums them in a fixed order
+//              (deterministic), for every problem of the table at once.
 //   node_pack: every weight matrix of the step packed once into the MMA operand layout.
 //   species_sort: a stable counting sort of the atoms by element (one CTA), giving the
 //              permutation and the per-element segments the grouped products use.
@@ -59,6 +59,7 @@ struct NodeMMArgs {
   int n;
   int* status;
   long long spin_limit;
+  unsigned long long* trace;   // optional: per CTA, globaltimer at the phase boundaries (8 slots)
 };
 
 struct NodeRedProb {
@@ -73,7 +74,7 @@ struct NodeRedProb {
   float scale;
   float* out;             // K1 x N row-major
   float* partial;         // ctas x K1 x N
-  unsigned int* counter;  // arrival counter, zero between launches (the last CTA resets it)
+  unsigned int* counter;  // unused (kept for the layout shared with the bindings)
   int ctas, rows_per_cta, cta0;
 };
 
@@ -82,6 +83,7 @@ struct NodeRedArgs {
   int n;
   int* status;
   long long spin_limit;
+  unsigned long long* trace;   // optional: per CTA, globaltimer at the phase boundaries (8 slots)
 };
 
 struct PackJob {
@@ -99,6 +101,12 @@ struct PackArgs {
 namespace {
 
 using namespace tc;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t canon_off(int r, int k4, int kb) {
   return (uint32_t)(r >> 3) * (uint32_t)(kb / 4) * 128u + (uint32_t)k4 * 128u + (uint32_t)(r & 7) * 16u;
@@ -122,6 +130,8 @@ __global__ void __launch_bounds__(128, 1) node_mm_kernel(const __grid_constant__
   int pi = 0;
   while (pi + 1 < a.n && (int)blockIdx.x >= a.p[pi + 1].tile0) ++pi;
   const NodeMMProb& P = a.p[pi];
+  unsigned long long* tr = (a.trace != nullptr && threadIdx.x == 0) ? a.trace + (size_t)blockIdx.x * 8 : nullptr;
+  if (tr) tr[0] = global_ns();
   int r_begin = 0, r_end = P.rows;
   if (P.seg != nullptr) {
     r_begin = P.seg[0];
@@ -157,6 +167,7 @@ __global__ void __launch_bounds__(128, 1) node_mm_kernel(const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (tr) tr[1] = global_ns();
   __shared__ int w_failed;
   if (tid == 0) w_failed = 0;
   bool ok = true;
@@ -170,33 +181,58 @@ __global__ void __launch_bounds__(128, 1) node_mm_kernel(const __grid_constant__
       mbar_arrive_expect_tx(bars, 2 * wbytes);
       bulk_copy(b_st, wblk, 2 * wbytes, bars);
     }
-    // A block: rows of X (gathered through perm), split into TF32 halves; 16-byte chunks of one
-    // row's four consecutive columns; eight consecutive threads fill eight rows of one chunk column
-    const int k4n = kbp / 4;
-    for (int q = tid; q < 128 * k4n; q += 128) {
-      const int r8 = q & 7, k4 = (q >> 3) % k4n, rg = (q >> 3) / k4n;
-      const int r = rg * 8 + r8;
-      const int kc = k0 + 4 * k4;                 // column in the concatenated K
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r < nrow && 4 * k4 < kbw) {
-        const int pr = row0 + r;
-        const int gr = P.perm ? P.perm[pr] : pr;
-        const int s = kc < P.kx[0] ? 0 : 1;
-        const int col = s == 0 ? kc : kc - P.kx[0];
-        v = __ldg(reinterpret_cast<const float4*>(P.X[s] + (int64_t)gr * P.ldx[s] + col));
+    // A block: lane (r8, kl) of warp w loads the 16-byte chunks k4 = kl, kl + 4, ... of rows
+    // 8 g + r8 for row groups g = w, w + 4, w + 8, w + 12 -- per instruction eight rows x 64
+    // contiguous bytes from global memory, 512 contiguous bytes into shared memory. All loads of a
+    // thread are independent (row indices first), then split into TF32 halves and stored.
+    {
+      const int k4n = kbp / 4;
+      const int r8 = lane & 7, kl = lane >> 3;
+      int grow[4];
+      bool live[4];
+#pragma unroll
+      for (int gi = 0; gi < 4; ++gi) {
+        const int r = (warp + 4 * gi) * 8 + r8;
+        live[gi] = r < nrow;
+        grow[gi] = live[gi] ? (P.perm ? __ldg(P.perm + row0 + r) : row0 + r) : 0;
       }
-      float4 h, l;
-      split4(v, h, l);
-      const uint32_t off = canon_off(r, k4, kbp);
-      *reinterpret_cast<float4*>(a_hi + off) = h;
-      *reinterpret_cast<float4*>(a_lo + off) = l;
+      // k4 = kl + 4 u (u < 6 covers k4n <= 24): all 24 loads of the thread issued together
+      float4 v[4][6];
+#pragma unroll
+      for (int gi = 0; gi < 4; ++gi)
+#pragma unroll
+        for (int u = 0; u < 6; ++u) {
+          const int k4 = kl + 4 * u;
+          v[gi][u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (live[gi] && k4 < k4n && 4 * k4 < kbw) {
+            const int kc = k0 + 4 * k4;
+            const int s = kc < P.kx[0] ? 0 : 1;
+            const int col = s == 0 ? kc : kc - P.kx[0];
+            v[gi][u] = __ldg(reinterpret_cast<const float4*>(P.X[s] + (int64_t)grow[gi] * P.ldx[s] + col));
+          }
+        }
+#pragma unroll
+      for (int gi = 0; gi < 4; ++gi)
+#pragma unroll
+        for (int u = 0; u < 6; ++u) {
+          const int k4 = kl + 4 * u;
+          if (k4 < k4n) {
+            float4 h, l;
+            split4(v[gi][u], h, l);
+            const uint32_t off = canon_off((warp + 4 * gi) * 8 + r8, k4, kbp);
+            *reinterpret_cast<float4*>(a_hi + off) = h;
+            *reinterpret_cast<float4*>(a_lo + off) = l;
+          }
+        }
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (tr && kb == 0) tr[2] = global_ns();
     if (tid == 0) {
       bool w_ok = mbar_wait(bars, (uint32_t)(kb & 1), a.spin_limit);
+      if (tr && kb == 0) tr[3] = global_ns();
       if (!w_ok) {
         atomicExch(a.status, 21);
         w_ok = mbar_wait(bars, (uint32_t)(kb & 1), 16 * a.spin_limit);   // the copy must land before reuse
@@ -225,45 +261,62 @@ __global__ void __launch_bounds__(128, 1) node_mm_kernel(const __grid_constant__
     }
     ok = __syncthreads_and((ok && m_ok && !w_failed) ? 1 : 0) != 0;
     tc_fence_after();
+    if (tr && kb == 0) tr[4] = global_ns();
     if (!ok) break;
     wblk += 2 * (size_t)N * kbp;
   }
   if (ok) {
-    // epilogue: warp w holds rows 32 w .. 32 w + 31 (TMEM lanes), 16 columns per load
-    const int r = warp * 32 + lane;
-    const bool live = r < nrow;
-    const int pr = row0 + r;
-    const int gr = live ? (P.perm ? P.perm[pr] : pr) : 0;
-    float* yrow = P.Y + (int64_t)gr * P.ldy;
+    // epilogue: warp w holds rows 32 w .. 32 w + 31 (TMEM lanes). Each thread parks its row in
+    // shared memory (the A buffers are free now; rows padded by 4 floats against bank
+    // conflicts), then the warp writes its rows one at a time with contiguous 16-byte stores.
+    float* stage = reinterpret_cast<float*>(a_hi) + (size_t)warp * 32 * (N + 4);
+    float* mine = stage + (size_t)lane * (N + 4);
     for (int c0 = 0; c0 < N; c0 += 16) {
       float v[16];
       tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
-      if (live) {
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) {
-          float4* dst = reinterpret_cast<float4*>(yrow + c0 + j);
-          float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          if (P.accumulate) {
-            const float4 y = *dst;
-            o.x += y.x; o.y += y.y; o.z += y.z; o.w += y.w;
-          }
-          *dst = o;
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(mine + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+    }
+    if (tr) tr[7] = global_ns();
+    // destination rows of the warp: lane i holds row 32 w + i's, broadcast below
+    const int my_r = warp * 32 + lane;
+    const int my_gr = my_r < nrow ? (P.perm ? __ldg(P.perm + row0 + my_r) : row0 + my_r) : 0;
+    __syncwarp();
+    const int n4 = N / 4;
+    for (int rr = 0; rr < 32; ++rr) {
+      const int r = warp * 32 + rr;
+      if (r >= nrow) break;                        // warp-uniform
+      const int gr = __shfl_sync(0xffffffffu, my_gr, rr);
+      float4* yrow = reinterpret_cast<float4*>(P.Y + (int64_t)gr * P.ldy);
+      const float4* src = reinterpret_cast<const float4*>(stage + (size_t)rr * (N + 4));
+      for (int c = lane; c < n4; c += 32) {
+        float4 o = src[c];
+        if (P.accumulate) {
+          const float4 y = yrow[c];
+          o.x += y.x; o.y += y.y; o.z += y.z; o.w += y.w;
         }
+        yrow[c] = o;
       }
     }
   }
+  if (tr) tr[5] = global_ns();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(tcols));
   }
+  if (tr) tr[6] = global_ns();
 }
 
 // ------------------------------------------------------------------------------------ reduction
 // G^T (N x K1) accumulates in TMEM: lanes = G columns n (D columns, up to 128 per pass), TMEM
-// columns = K1 (X columns, padded to 16); the data rows are the MMA's K. Chunks of 32 rows are
-// staged raw (coalesced 16-byte loads), then transposed and split into the canonical layout.
+// columns = K1 (X columns, padded to 16); the data rows are the MMA's K. A chunk of RC rows is
+// read straight into the transposed operand layout: a 16-byte operand piece is four consecutive
+// rows of one column, so every thread issues four scalar loads whose warp-wide pattern reads
+// whole rows (consecutive lanes, consecutive columns). Two operand stages alternate: the loads
+// and conversion of chunk g + 1 overlap the MMAs of chunk g.
 constexpr int RC = 32;      // rows per chunk
 
 __global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant__ NodeRedArgs a) {
@@ -272,6 +325,8 @@ __global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant_
   int pi = 0;
   while (pi + 1 < a.n && (int)blockIdx.x >= a.p[pi + 1].cta0) ++pi;
   const NodeRedProb& P = a.p[pi];
+  unsigned long long* tr = (a.trace != nullptr && threadIdx.x == 0) ? a.trace + (size_t)blockIdx.x * 8 : nullptr;
+  if (tr) tr[0] = global_ns();
   const int cta = (int)blockIdx.x - P.cta0;
   const int K1 = P.K1, N = P.N;
   const int K1p = (K1 + 15) / 16 * 16;            // TMEM columns / MMA N
@@ -288,16 +343,15 @@ __global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant_
   const int per = ((n0 + n1 + P.ctas - 1) / P.ctas + RC - 1) / RC * RC;
   const int lo_row = cta * per, hi_row = min(n0 + n1, lo_row + per);
 
-  // shared memory: raw X chunk (RC x K1), raw D chunk (RC x N), A = D^T hi/lo (npass x 128 x RC),
-  // B = X^T hi/lo (K1p x RC), barrier, TMEM slot
-  float* raw_x = reinterpret_cast<float*>(smem);
-  float* raw_d = raw_x + RC * 128;
-  unsigned char* a_st = reinterpret_cast<unsigned char*>(raw_d + RC * 256);
+  // shared memory: two stages of [A = D^T hi/lo (npass x 128 x RC) | B = X^T hi/lo (K1p x RC)],
+  // two MMA barriers, the row indices of two chunks, the TMEM slot
   const uint32_t A_BYTES = 128u * RC * 4u;
   const uint32_t B_BYTES = (uint32_t)K1p * RC * 4u;
-  unsigned char* b_st = a_st + 2 * A_BYTES * npass;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(b_st + 2 * B_BYTES);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  const uint32_t STAGE = 2u * A_BYTES * npass + 2u * B_BYTES;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * STAGE);
+  int* rows_sm = reinterpret_cast<int*>(bar + 2);          // [2][RC]: source row, or -1
+  unsigned char* set_sm = reinterpret_cast<unsigned char*>(rows_sm + 2 * RC);   // [2][RC]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(set_sm + 2 * RC);
   const int tcols = tmem_cols_for(npass * K1p);
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -306,91 +360,119 @@ __global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant_
   }
   if (tid == 0) {
     mbar_init(bar, 1);
+    mbar_init(bar + 1, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // A rows past N stay zero (cleared once)
-  for (int i = tid; i < (int)(2 * A_BYTES * npass / 16); i += 128)
-    reinterpret_cast<float4*>(a_st)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  // operand rows past N / K1 stay zero: clear both stages once
+  for (int i = tid; i < (int)(2 * STAGE / 16); i += 128)
+    reinterpret_cast<float4*>(smem)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  // row indices of the chunk starting at c0 into slot b (thread j < RC handles row j)
+  auto index_rows = [&](int c0, int b) {
+    if (tid < RC) {
+      const int cr = c0 + tid;
+      int row = -1, set = 0;
+      if (cr < hi_row) {
+        set = cr < n0 ? 0 : 1;
+        const int pr = r_begin + (set == 0 ? cr : cr - n0);
+        row = P.perm ? __ldg(P.perm + pr) : pr;
+      }
+      rows_sm[b * RC + tid] = row;
+      set_sm[b * RC + tid] = (unsigned char)set;
+    }
+  };
+  // operands of the chunk whose rows are in slot b, into stage b. Per pass a thread takes eight
+  // pieces of each operand (64 independent scalar loads in flight), then splits and stores them.
+  // Operand 0: A = D^T (pieces over n < N); operand 1: B = X^T (pieces over m < K1); a piece
+  // (c, k4) holds rows 4 k4 .. 4 k4 + 3 of column c, and the lanes of a warp run over c.
+  auto stage_chunk = [&](int b) {
+    unsigned char* st = smem + (size_t)b * STAGE;
+    const int* rw = rows_sm + b * RC;
+    const unsigned char* sw = set_sm + b * RC;
+    const int dpad = (N + 31) / 32 * 32, xpad = (K1 + 31) / 32 * 32;
+    const int d_items = dpad * (RC / 4), x_items = xpad * (RC / 4);
+    const int passes = (max(d_items, x_items) + 8 * 128 - 1) / (8 * 128);
+    for (int pq = 0; pq < passes; ++pq) {
+      float v[2][8][4];
+#pragma unroll
+      for (int op = 0; op < 2; ++op) {
+        const int cols = op == 0 ? N : K1;
+        const int cpad = op == 0 ? dpad : xpad;
+        const int items = op == 0 ? d_items : x_items;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int q = pq * 8 * 128 + tid + 128 * u;
+          const int c = q % cpad, k4 = q / cpad;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            v[op][u][i] = 0.f;
+            if (q < items && c < cols) {
+              const int row = rw[4 * k4 + i];
+              if (row >= 0) {
+                const int ss = sw[4 * k4 + i];
+                v[op][u][i] = op == 0 ? __ldg(P.D[ss] + (int64_t)row * P.ldd[ss] + c)
+                                      : __ldg(P.X[ss] + (int64_t)row * P.ldx[ss] + c);
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int op = 0; op < 2; ++op) {
+        const int cols = op == 0 ? N : K1;
+        const int cpad = op == 0 ? dpad : xpad;
+        const int items = op == 0 ? d_items : x_items;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int q = pq * 8 * 128 + tid + 128 * u;
+          const int c = q % cpad, k4 = q / cpad;
+          if (q < items && c < cols) {
+            float4 h, l;
+            split4(make_float4(v[op][u][0], v[op][u][1], v[op][u][2], v[op][u][3]), h, l);
+            unsigned char* base;
+            uint32_t off, half;
+            if (op == 0) {
+              base = st + (size_t)(c >> 7) * 2 * A_BYTES;
+              off = canon_off(c & 127, k4, RC);
+              half = A_BYTES;
+            } else {
+              base = st + 2 * A_BYTES * npass;
+              off = canon_off(c, k4, RC);
+              half = B_BYTES;
+            }
+            *reinterpret_cast<float4*>(base + off) = h;
+            *reinterpret_cast<float4*>(base + half + off) = l;
+          }
+        }
+      }
+    }
+  };
+
   bool ok = true;
   int g = 0;
+  if (lo_row < hi_row) index_rows(lo_row, 0);
+  __syncthreads();
+  if (tr) tr[1] = global_ns();
   for (int c0 = lo_row; c0 < hi_row; c0 += RC, ++g) {
-    const int nr = min(RC, hi_row - c0);
-    // raw rows: row c0 + j of the concatenated space -> set and source row
-    for (int q = tid; q < RC * (K1 / 4); q += 128) {
-      const int j = q / (K1 / 4), k4 = q % (K1 / 4);
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < nr) {
-        const int cr = c0 + j;
-        const int s = cr < n0 ? 0 : 1;
-        const int pr = r_begin + (s == 0 ? cr : cr - n0);
-        const int gr = P.perm ? P.perm[pr] : pr;
-        v = __ldg(reinterpret_cast<const float4*>(P.X[s] + (int64_t)gr * P.ldx[s]) + k4);
-      }
-      reinterpret_cast<float4*>(raw_x)[j * (K1 / 4) + k4] = v;
-    }
-    for (int q = tid; q < RC * (N / 4); q += 128) {
-      const int j = q / (N / 4), n4 = q % (N / 4);
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < nr) {
-        const int cr = c0 + j;
-        const int s = cr < n0 ? 0 : 1;
-        const int pr = r_begin + (s == 0 ? cr : cr - n0);
-        const int gr = P.perm ? P.perm[pr] : pr;
-        v = __ldg(reinterpret_cast<const float4*>(P.D[s] + (int64_t)gr * P.ldd[s]) + n4);
-      }
-      reinterpret_cast<float4*>(raw_d)[j * (N / 4) + n4] = v;
-    }
-    __syncthreads();
-    if (g > 0) {
-      // the previous chunk's MMAs read the operand buffers: wait before overwriting them
-      bool m_ok = mbar_wait(bar, (uint32_t)((g - 1) & 1), a.spin_limit);
+    const int b = g & 1;
+    if (g >= 2) {
+      // stage b was read by the MMAs of chunk g - 2
+      bool m_ok = mbar_wait(bar + b, (uint32_t)(((g - 2) >> 1) & 1), a.spin_limit);
       if (!m_ok) {
         atomicExch(a.status, 23);
-        m_ok = mbar_wait(bar, (uint32_t)((g - 1) & 1), 16 * a.spin_limit);
+        m_ok = mbar_wait(bar + b, (uint32_t)(((g - 2) >> 1) & 1), 16 * a.spin_limit);
       }
       ok = __syncthreads_and((ok && m_ok) ? 1 : 0) != 0;
       tc_fence_after();
       if (!ok) break;
     }
-    // A = D^T: row n (D column), k = chunk row; 16-byte chunk = rows 4 k4 .. 4 k4 + 3 of column n
-    for (int q = tid; q < npass * 128 * (RC / 4); q += 128) {
-      const int n8 = q & 7, k4 = (q >> 3) % (RC / 4), ng = (q >> 3) / (RC / 4);
-      const int n = ng * 8 + n8;                  // 0 .. npass*128-1
-      if (n >= N) continue;
-      float4 v;
-      v.x = raw_d[(4 * k4 + 0) * N + n];
-      v.y = raw_d[(4 * k4 + 1) * N + n];
-      v.z = raw_d[(4 * k4 + 2) * N + n];
-      v.w = raw_d[(4 * k4 + 3) * N + n];
-      float4 h, l;
-      split4(v, h, l);
-      const int pass = n >> 7, nl = n & 127;
-      unsigned char* base = a_st + (size_t)pass * 2 * A_BYTES;
-      const uint32_t off = canon_off(nl, k4, RC);
-      *reinterpret_cast<float4*>(base + off) = h;
-      *reinterpret_cast<float4*>(base + A_BYTES + off) = l;
-    }
-    // B = X^T: row k1 (X column), k = chunk row
-    for (int q = tid; q < K1p * (RC / 4); q += 128) {
-      const int m8 = q & 7, k4 = (q >> 3) % (RC / 4), mg = (q >> 3) / (RC / 4);
-      const int m = mg * 8 + m8;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (m < K1) {
-        v.x = raw_x[(4 * k4 + 0) * K1 + m];
-        v.y = raw_x[(4 * k4 + 1) * K1 + m];
-        v.z = raw_x[(4 * k4 + 2) * K1 + m];
-        v.w = raw_x[(4 * k4 + 3) * K1 + m];
-      }
-      float4 h, l;
-      split4(v, h, l);
-      const uint32_t off = canon_off(m, k4, RC);
-      *reinterpret_cast<float4*>(b_st + off) = h;
-      *reinterpret_cast<float4*>(b_st + B_BYTES + off) = l;
-    }
+    stage_chunk(b);
+    if (tr && g == 0) tr[2] = global_ns();
+    if (c0 + RC < hi_row) index_rows(c0 + RC, b ^ 1);
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -398,9 +480,10 @@ __global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant_
     if (tid == 0) {
       const uint32_t idesc = make_idesc_tf32(K1p, 0, 0);
       const uint32_t sbo = (RC / 4) * 128u;
-      const uint32_t bh = smem_u32(b_st), bl = bh + B_BYTES;
+      unsigned char* st = smem + (size_t)b * STAGE;
+      const uint32_t bh = smem_u32(st + 2 * A_BYTES * npass), bl = bh + B_BYTES;
       for (int pass = 0; pass < npass; ++pass) {
-        const uint32_t ah = smem_u32(a_st + (size_t)pass * 2 * A_BYTES), al = ah + A_BYTES;
+        const uint32_t ah = smem_u32(st + (size_t)pass * 2 * A_BYTES), al = ah + A_BYTES;
         const uint32_t d = tmem + (uint32_t)(pass * K1p);
         for (int s = 0; s < RC / 8; ++s) {
           const uint32_t o = (uint32_t)s * 256u;
@@ -410,18 +493,23 @@ __global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant_
           mma_tf32(d, make_desc2(al + o, 128, sbo), make_desc2(bh + o, 128, sbo), idesc, 1u);
         }
       }
-      commit_to(bar);
+      commit_to(bar + b);
     }
   }
-  if (g > 0) {
-    bool m_ok = mbar_wait(bar, (uint32_t)((g - 1) & 1), a.spin_limit);
+  if (tr) tr[3] = global_ns();
+  // the last chunk's MMAs (and, with two or more chunks, the one before) before TMEM is read
+  for (int back = 1; back <= 2 && g - back >= 0; ++back) {
+    const int gg = g - back;
+    bool m_ok = mbar_wait(bar + (gg & 1), (uint32_t)((gg >> 1) & 1), a.spin_limit);
     if (!m_ok) {
       atomicExch(a.status, 23);
-      m_ok = mbar_wait(bar, (uint32_t)((g - 1) & 1), 16 * a.spin_limit);
+      m_ok = mbar_wait(bar + (gg & 1), (uint32_t)((gg >> 1) & 1), 16 * a.spin_limit);
     }
-    ok = __syncthreads_and((ok && m_ok) ? 1 : 0) != 0;
-    tc_fence_after();
+    ok = ok && m_ok;
   }
+  ok = __syncthreads_and(ok ? 1 : 0) != 0;
+  tc_fence_after();
+  if (tr) tr[4] = global_ns();
   // partial block G[k1][n] of this CTA (zeros when it had no rows)
   float* part = P.partial + (size_t)cta * K1 * N;
   for (int pass = 0; pass < npass; ++pass) {
@@ -441,31 +529,40 @@ __global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant_
       }
     }
   }
+  if (tr) tr[5] = global_ns();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(tcols));
   }
-  // the last CTA of the problem to arrive sums the partial blocks in CTA order (deterministic)
-  __shared__ unsigned int last;
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) last = atomicAdd(P.counter, 1u) == (unsigned)(P.ctas - 1) ? 1u : 0u;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  const int tot4 = K1 * N / 4;                   // K1 % 4 == 0
+  if (tr) { tr[6] = global_ns(); tr[7] = (unsigned long long)g; }
+}
+
+// out = scale * sum over the problem's CTAs of the partial blocks, in CTA order (deterministic);
+// one thread per four output elements, every problem of the table in one launch (grid.y)
+__global__ void __launch_bounds__(256) node_sum_kernel(const __grid_constant__ NodeRedArgs a) {
+  const NodeRedProb& P = a.p[blockIdx.y];
+  const int tot4 = P.K1 * P.N / 4;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= tot4) return;
   const float4* part4 = reinterpret_cast<const float4*>(P.partial);
-  for (int i = tid; i < tot4; i += 128) {
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int c = 0; c < P.ctas; ++c) {
-      const float4 v = __ldcg(part4 + (size_t)c * tot4 + i);
-      s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  int c = 0;
+  for (; c + 4 <= P.ctas; c += 4) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = __ldcg(part4 + (size_t)(c + u) * tot4 + i);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      s.x += v[u].x; s.y += v[u].y; s.z += v[u].z; s.w += v[u].w;
     }
-    reinterpret_cast<float4*>(P.out)[i] = make_float4(P.scale * s.x, P.scale * s.y, P.scale * s.z, P.scale * s.w);
   }
-  if (tid == 0) *P.counter = 0u;                  // ready for the next launch (stream-ordered)
+  for (; c < P.ctas; ++c) {
+    const float4 v = __ldcg(part4 + (size_t)c * tot4 + i);
+    s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+  }
+  reinterpret_cast<float4*>(P.out)[i] = make_float4(P.scale * s.x, P.scale * s.y, P.scale * s.z, P.scale * s.w);
 }
 
 // ------------------------------------------------------------------------------------ packing
@@ -545,7 +642,8 @@ size_t mm_smem(int N) {
 size_t red_smem(int K1, int N) {
   const int K1p = (K1 + 15) / 16 * 16;
   const int npass = (N + 127) / 128;
-  return (size_t)RC * 128 * 4 + (size_t)RC * 256 * 4 + 2u * 128u * RC * 4u * npass + 2u * (size_t)K1p * RC * 4u + 64;
+  const size_t stage = 2u * 128u * RC * 4u * npass + 2u * (size_t)K1p * RC * 4u;
+  return 2 * stage + 16 + 2 * RC * 4 + 2 * RC + 16 + 64;
 }
 
 }  // namespace
@@ -566,6 +664,10 @@ cudaError_t node_mmT_launch(NodeRedArgs& args, int total_ctas, int max_k1, int m
   cudaError_t e = cudaFuncSetAttribute(node_mmT_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   node_mmT_kernel<<<total_ctas, 128, smem, s>>>(args);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int most4 = max_k1 * max_n / 4;
+  node_sum_kernel<<<dim3((most4 + 255) / 256, args.n), 256, 0, s>>>(args);
   return cudaGetLastError();
 }
 

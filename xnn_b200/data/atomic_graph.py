@@ -57,6 +57,10 @@ class AtomicGraph:
     # "dst" when the edges are grouped by receiver in increasing order (what the
     # neighbour lists produce and collate keeps); lets the fused kernels skip a sort
     edge_order: Optional[str] = None
+    # the edges' CSR views packed as int64 ``[dst_ptr (N+1) | src_ptr (N+1) | src_perm (E)]``,
+    # computed on the host by the padded collate so the device builds no plan per step; only
+    # valid for this graph as it is (subsets and concatenations drop it)
+    edge_plan: Optional[Tensor] = None
 
     # --- sizes -------------------------------------------------------------------
     @property
@@ -115,7 +119,7 @@ class AtomicGraph:
                   edge_index=new_node[self.edge_index[:, edge_keep]],
                   cell_shifts=self.cell_shifts[edge_keep],
                   batch=new_graph[self.batch[node_keep]], n_atoms=self.n_atoms[keep],
-                  compute_dtype=self.compute_dtype, edge_order=self.edge_order)
+                  compute_dtype=self.compute_dtype, edge_order=self.edge_order, edge_plan=None)
         for f in fields(self):
             if f.name in kw:
                 continue

@@ -114,7 +114,7 @@ def collate(graphs: Sequence[AtomicGraph]) -> AtomicGraph:
     skip = set(out) | {"cell", "pbc"} | set(_MASKED.values())
     for f in fields(AtomicGraph):
         name = f.name
-        if name in skip or name in ("compute_dtype", "edge_order"):
+        if name in skip or name in ("compute_dtype", "edge_order", "edge_plan"):
             continue
         vals = [getattr(g, name) for g in graphs]
         if all(v is None for v in vals):

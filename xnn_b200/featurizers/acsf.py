@@ -289,20 +289,23 @@ class AtomCenteredSymmetryFunctions(nn.Module):
                 raise ValueError(f"unknown scaling mode {mode!r}")
             self.mode = mode
         n_sp = len(self.species)
+        # running per-element statistics with scatter reductions over all atoms of a graph at
+        # once: minimum and maximum by scatter_reduce, sums and counts by index_add
         lo = torch.full((n_sp, self._dim), math.inf, dtype=torch.float64)
         hi = torch.full((n_sp, self._dim), -math.inf, dtype=torch.float64)
         total = torch.zeros(n_sp, self._dim, dtype=torch.float64)
         count = torch.zeros(n_sp, dtype=torch.float64)
+        z2i = self._z2i.cpu()
         for data in graphs:
             g = self.raw(data).detach().double().cpu()
-            sp = self._z2i.cpu()[data.atomic_numbers.cpu()]
-            for i in range(n_sp):
-                rows = g[sp == i]
-                if rows.shape[0]:
-                    lo[i] = torch.minimum(lo[i], rows.min(0).values)
-                    hi[i] = torch.maximum(hi[i], rows.max(0).values)
-                    total[i] += rows.sum(0)
-                    count[i] += rows.shape[0]
+            sp = z2i[data.atomic_numbers.cpu()]
+            keep = sp >= 0
+            g, sp = g[keep], sp[keep]
+            idx = sp[:, None].expand_as(g)
+            lo.scatter_reduce_(0, idx, g, "amin")
+            hi.scatter_reduce_(0, idx, g, "amax")
+            total.index_add_(0, sp, g)
+            count.index_add_(0, sp, torch.ones_like(sp, dtype=torch.float64))
         missing = [self.species[i] for i in range(n_sp) if count[i] == 0]
         if missing:
             raise ValueError(f"no atoms of elements {missing} to compute the scaling from")

@@ -104,7 +104,7 @@ class _AtomUpdate(nn.Module):
         self.lin_rbf = _Dense(n_rbf_emb, n_edge)
         self.scale_sum = ScaleFactor()
         self.dense = _Dense(n_edge, n_atom, True)
-        self.residuals = nn.ModuleList([_Residual(n_atom) for _ in range(n_residual)])
+        self.residuals = _stack(n_residual, n_atom)
 
     def forward(self, m: Tensor, rbf: Tensor, dst: Tensor, n: int):
         gated = m * self.lin_rbf(rbf)
@@ -119,7 +119,7 @@ class _ForceHead(nn.Module):
         super().__init__()
         self.scale_rbf = ScaleFactor()
         self.dense = _Dense(n_edge, n_edge, True)
-        self.residuals = nn.ModuleList([_Residual(n_edge) for _ in range(n_residual)])
+        self.residuals = _stack(n_residual, n_edge)
         self.final = _Dense(n_edge, 1, init=output_init)
 
     def forward(self, m: Tensor, gated: Tensor) -> Tensor:
@@ -160,47 +160,62 @@ def _bilinear_init_(w: Tensor) -> None:
         w.copy_(flat.t().reshape(j, fi, fo))
 
 
-class _TripletInteraction(nn.Module):
+def _stack(n: int, width: int) -> nn.ModuleList:
+    return nn.ModuleList(_Residual(width) for _ in range(n))
+
+
+class _ManyBody(nn.Module):
+    """The skeleton shared by the triplet and quadruplet interactions: an edge update gated by the
+    radial basis, a projection down to the interaction width, a bilinear contraction of the
+    basis sums, and up-projections for the edge and for its reverse (averaged)."""
+
+    first: str
+
+    def _build(self, n_edge: int, n_down: int, n_rbf_emb: int, n_bilinear_basis: int, n_bilinear: int,
+               scale_names) -> None:
+        setattr(self, self.first, _Dense(n_edge, n_edge, True))
+        self.lin_rbf = _Dense(n_rbf_emb, n_edge)
+        self.down = _Dense(n_edge, n_down, True)
+        self.bilinear = nn.Parameter(torch.empty(n_bilinear_basis, n_down, n_bilinear))
+        _bilinear_init_(self.bilinear)
+        for name in scale_names:
+            setattr(self, name, ScaleFactor())
+        self.up_ca, self.up_ac = (_Dense(n_bilinear, n_edge, True) for _ in range(2))
+
+    def _gated_down(self, m: Tensor, rbf: Tensor) -> Tensor:
+        x = getattr(self, self.first)(m)
+        return self.down(self.scale_rbf(x, x * self.lin_rbf(rbf)))
+
+    def _up(self, y: Tensor, rev: Tensor) -> Tensor:
+        return (self.up_ca(y) + self.up_ac(y).index_select(0, rev)) * _IS2
+
+
+class _TripletInteraction(_ManyBody):
+    first = "dense_ba"
+
     def __init__(self, n_edge, n_trip, n_rbf_emb, n_cbf_emb, n_bilinear):
         super().__init__()
-        self.dense_ba = _Dense(n_edge, n_edge, True)
-        self.lin_rbf = _Dense(n_rbf_emb, n_edge)
-        self.scale_rbf = ScaleFactor()
-        self.down = _Dense(n_edge, n_trip, True)
-        self.bilinear = nn.Parameter(torch.empty(n_cbf_emb, n_trip, n_bilinear))
-        _bilinear_init_(self.bilinear)
-        self.scale_cbf_sum = ScaleFactor()
-        self.up_ca, self.up_ac = _Dense(n_bilinear, n_edge, True), _Dense(n_bilinear, n_edge, True)
+        self._build(n_edge, n_trip, n_rbf_emb, n_cbf_emb, n_bilinear, ("scale_rbf", "scale_cbf_sum"))
 
     def forward(self, m, rbf, cbf_rad, sph, t_out, t_in, rev):
-        x = self.dense_ba(m)
-        x = self.scale_rbf(x, x * self.lin_rbf(rbf))
-        x = self.down(x).index_select(0, t_in)
+        x = self._gated_down(m, rbf).index_select(0, t_in)
         y = self.scale_cbf_sum(x, _mix(_basis_sums(x, sph, t_out, m.shape[0]), cbf_rad, self.bilinear))
-        return (self.up_ca(y) + self.up_ac(y)[rev]) * _IS2
+        return self._up(y, rev)
 
 
-class _QuadrupletInteraction(nn.Module):
+class _QuadrupletInteraction(_ManyBody):
+    first = "dense_db"
+
     def __init__(self, n_edge, n_quad, n_rbf_emb, n_cbf_emb, n_sbf_emb, n_bilinear):
         super().__init__()
-        self.dense_db = _Dense(n_edge, n_edge, True)
-        self.lin_rbf = _Dense(n_rbf_emb, n_edge)
-        self.scale_rbf = ScaleFactor()
-        self.down = _Dense(n_edge, n_quad, True)
+        self._build(n_edge, n_quad, n_rbf_emb, n_sbf_emb, n_bilinear, ("scale_rbf", "scale_cbf", "scale_sbf_sum"))
         self.lin_cbf = _Dense(n_cbf_emb, n_quad)
-        self.scale_cbf = ScaleFactor()
-        self.bilinear = nn.Parameter(torch.empty(n_sbf_emb, n_quad, n_bilinear))
-        _bilinear_init_(self.bilinear)
-        self.scale_sbf_sum = ScaleFactor()
-        self.up_ca, self.up_ac = _Dense(n_bilinear, n_edge, True), _Dense(n_bilinear, n_edge, True)
 
     def forward(self, m, rbf, cbf, sbf_rad, sph, intm_db, q_out, q_intm, rev):
-        x = self.dense_db(m)
-        x = self.scale_rbf(x, x * self.lin_rbf(rbf))
-        x = self.down(x).index_select(0, intm_db)
+        x = self._gated_down(m, rbf).index_select(0, intm_db)
         x = self.scale_cbf(x, x * self.lin_cbf(cbf)).index_select(0, q_intm)
         y = self.scale_sbf_sum(x, _mix(_basis_sums(x, sph, q_out, m.shape[0]), sbf_rad, self.bilinear))
-        return (self.up_ca(y) + self.up_ac(y)[rev]) * _IS2
+        return self._up(y, rev)
 
 
 class _Interaction(nn.Module):
@@ -211,11 +226,10 @@ class _Interaction(nn.Module):
         self.quad = (_QuadrupletInteraction(n_edge, n_quad, n_rbf_emb, n_cbf_emb, n_sbf_emb, n_bil_quad)
                      if quadruplets else None)
         self.trip = _TripletInteraction(n_edge, n_trip, n_rbf_emb, n_cbf_emb, n_bil_trip)
-        self.before_skip = nn.ModuleList([_Residual(n_edge) for _ in range(n_before)])
-        self.after_skip = nn.ModuleList([_Residual(n_edge) for _ in range(n_after)])
+        self.before_skip, self.after_skip = _stack(n_before, n_edge), _stack(n_after, n_edge)
         self.atom_update = _AtomUpdate(n_atom, n_edge, n_rbf_emb, n_atom_residual)
         self.concat = _EdgeEmbedding(n_atom, n_edge, n_edge)
-        self.residual_m = nn.ModuleList([_Residual(n_edge) for _ in range(n_concat)])
+        self.residual_m = _stack(n_concat, n_edge)
 
     def forward(self, h, m, src, dst, rev, g3, g4, rbf_h):
         x_skip = self.dense_ca(m)

@@ -114,50 +114,46 @@ class HDNNP(DescriptorPotential):
         self.screening = None if screening is None else dict(screening)
         self.ewald_accuracy = float(ewald_accuracy)
         self.coulomb_constant = float(coulomb_constant)
-        if generation < 3:
-            self.register_buffer("gaussian_widths", torch.zeros(119), persistent=False)
-        if generation < 4:
-            self.register_buffer("chi_scale", torch.tensor(1.0), persistent=False)
-            self.register_buffer("hardness_scale", torch.tensor(1.0), persistent=False)
-            self.register_buffer("charge_input_shift", torch.zeros(119), persistent=False)
-            self.register_buffer("charge_input_factor", torch.ones(119), persistent=False)
-        if not (generation == 4 and hardness == "element"):
-            self.register_buffer("_hardness_index", torch.zeros(119, dtype=torch.long), persistent=False)
-            self.hardness_act = nn.Identity()
+        gen4 = generation == 4
+        if gen4 and hardness not in ("element", "network"):
+            raise ValueError(f"hardness must be 'element' or 'network', got {hardness!r}")
+        # buffers by generation: name -> (value, saved in the state dict); the ones a generation
+        # does not use exist as inert defaults outside the state dict
+        q_feat = charge_featurizer if charge_featurizer is not None else featurizer
+        q_dims = getattr(q_feat, "n_features", None) or q_feat.output_dim
+        sigma = torch.zeros(119)
         if generation >= 3:
-            feat = charge_featurizer if charge_featurizer is not None else featurizer
-            dims = getattr(feat, "n_features", None) or feat.output_dim
-            self.charge_nets = ElementNetworks(species, dims, hidden if charge_hidden is None else charge_hidden,
-                                               activation if charge_activation is None else charge_activation)
             widths = (default_gaussian_widths(species) if gaussian_widths is None
                       else _per_species(gaussian_widths, species, "gaussian_widths"))
-            sigma = torch.zeros(119)
-            for z, w in zip(species, widths):
-                sigma[z] = w
-            self.register_buffer("gaussian_widths", sigma)
-            self.cutoff = max(self.cutoff, feat.cutoff, float(self.screening["r_cut"]) if self.screening else 0.0)
-        if generation == 4:
-            self.register_buffer("chi_scale", torch.tensor(float(chi_scale)))
-            self.register_buffer("hardness_scale", torch.tensor(float(hardness_scale)))
-            if hardness == "element":
-                init = ([float(hardness_init)] * len(species) if isinstance(hardness_init, (int, float))
-                        else _per_species(hardness_init, species, "hardness_init"))
-                self.hardness_raw = nn.Parameter(torch.tensor(init))
-                self.hardness_act = make_activation(hardness_activation)
-                z2i = torch.full((119,), -1, dtype=torch.long)
-                for i, z in enumerate(species):
-                    z2i[z] = i
-                self.register_buffer("_hardness_index", z2i, persistent=False)
-            elif hardness == "network":
-                feat = charge_featurizer if charge_featurizer is not None else featurizer
-                dims = getattr(feat, "n_features", None) or feat.output_dim
-                self.hardness_nets = ElementNetworks(
-                    species, dims, hidden if hardness_hidden is None else hardness_hidden,
-                    activation if hardness_activation_nn is None else hardness_activation_nn)
-            else:
-                raise ValueError(f"hardness must be 'element' or 'network', got {hardness!r}")
-            self.register_buffer("charge_input_shift", torch.zeros(119))
-            self.register_buffer("charge_input_factor", torch.ones(119))
+            sigma[torch.tensor(species)] = torch.tensor(widths, dtype=sigma.dtype)
+        slot = torch.zeros(119, dtype=torch.long)
+        if gen4 and hardness == "element":
+            slot.fill_(-1)
+            slot[torch.tensor(species)] = torch.arange(len(species))
+        buffers = {
+            "gaussian_widths": (sigma, generation >= 3),
+            "chi_scale": (torch.tensor(float(chi_scale) if gen4 else 1.0), gen4),
+            "hardness_scale": (torch.tensor(float(hardness_scale) if gen4 else 1.0), gen4),
+            "charge_input_shift": (torch.zeros(119), gen4),
+            "charge_input_factor": (torch.ones(119), gen4),
+            "_hardness_index": (slot, False),
+        }
+        for name, (value, saved) in buffers.items():
+            self.register_buffer(name, value, persistent=saved)
+        self.hardness_act = nn.Identity()
+        if generation >= 3:
+            self.charge_nets = ElementNetworks(species, q_dims, hidden if charge_hidden is None else charge_hidden,
+                                               activation if charge_activation is None else charge_activation)
+            self.cutoff = max(self.cutoff, q_feat.cutoff, float(self.screening["r_cut"]) if self.screening else 0.0)
+        if gen4 and hardness == "element":
+            init = ([float(hardness_init)] * len(species) if isinstance(hardness_init, (int, float))
+                    else _per_species(hardness_init, species, "hardness_init"))
+            self.hardness_raw = nn.Parameter(torch.tensor(init))
+            self.hardness_act = make_activation(hardness_activation)
+        elif gen4:
+            self.hardness_nets = ElementNetworks(
+                species, q_dims, hidden if hardness_hidden is None else hardness_hidden,
+                activation if hardness_activation_nn is None else hardness_activation_nn)
 
     # ------------------------------------------------------------------ electrostatics
     def coulomb_matrices(self, data: AtomicGraph, dtype) -> list:

@@ -421,7 +421,9 @@ class MACE(GNNPotential):
         plan = None
         if data.edge_order == "dst" and self._fast_active(edge_vec):
             from ..ops.mace_ops import EdgePlan
-            plan = EdgePlan.build(data.edge_index, data.num_nodes, assume_dst_sorted=True)
+            plan = (EdgePlan.from_packed(data.edge_index, data.num_nodes, data.edge_plan)
+                    if data.edge_plan is not None else
+                    EdgePlan.build(data.edge_index, data.num_nodes, assume_dst_sorted=True))
         feats, node_energy = self.node_features_energy(data.atomic_numbers, data.edge_index,
                                                        edge_vec, plan)
         return {"node_energy": node_energy, "energy": self.aggregate_energy(node_energy, data),

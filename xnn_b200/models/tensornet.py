@@ -15,6 +15,7 @@ from typing import Optional, Tuple
 
 import torch
 from torch import Tensor, nn
+from torch.nn import functional as F
 
 from ..data import AtomicGraph
 from ..nn import CosineCutoff, make_radial_basis
@@ -210,23 +211,26 @@ class TensorNet(InteratomicPotential):
     def receptive_field(self) -> float:
         return max(1, self.n_interactions) * self.cutoff
 
+    def _pairs(self, n_atoms: int, edge_index: Tensor, edge_vec: Tensor):
+        """``(src, dst, length, direction)`` of the edges, followed (with ``self_pairs``) by one
+        zero-length loop per atom, which carries the atom's own embedding into the messages."""
+        length = edge_vec.norm(dim=-1)
+        direction = edge_vec / length.clamp(min=1e-12)[:, None]
+        src, dst = edge_index.unbind(0)
+        if not self.self_pairs:
+            return src, dst, length, direction
+        ids = torch.arange(n_atoms, dtype=edge_index.dtype, device=edge_index.device)
+        return (torch.cat((src, ids)), torch.cat((dst, ids)), F.pad(length, (0, n_atoms)),
+                F.pad(direction, (0, 0, 0, n_atoms)))
+
     def tensors(self, atomic_numbers: Tensor, edge_index: Tensor, edge_vec: Tensor, total_charge: Tensor) -> Tensor:
-        r = torch.linalg.norm(edge_vec, dim=-1)
-        unit = edge_vec / r.clamp(min=1e-12).unsqueeze(-1)
-        src, dst = edge_index[0], edge_index[1]
-        if self.self_pairs:
-            n = atomic_numbers.shape[0]
-            loops = torch.arange(n, dtype=edge_index.dtype, device=edge_index.device)
-            src = torch.cat([src, loops])
-            dst = torch.cat([dst, loops])
-            r = torch.cat([r, r.new_zeros((n,))])
-            unit = torch.cat([unit, unit.new_zeros((n, 3))])
-        cut = self.cutoff_fn(r)
-        rbf = self.rbf(r)
-        X = self.tensor_embedding(atomic_numbers, src, dst, cut, unit, rbf)
+        """Per-atom 3 x 3 tensor features after the embedding and every interaction."""
+        src, dst, length, direction = self._pairs(atomic_numbers.shape[0], edge_index, edge_vec)
+        fc, basis = self.cutoff_fn(length), self.rbf(length)
+        feats = self.tensor_embedding(atomic_numbers, src, dst, fc, direction, basis)
         for layer in self.layers:
-            X = layer(refresh_ghosts(X), src, dst, cut, rbf, total_charge)
-        return X
+            feats = layer(refresh_ghosts(feats), src, dst, fc, basis, total_charge)
+        return feats
 
     def _features(self, X: Tensor) -> Tensor:
         scalar, skew, sym = decompose(X)

@@ -66,6 +66,16 @@ class EdgePlan:
         return self.n_src if self.n_src >= 0 else self.n_nodes
 
     @staticmethod
+    def from_packed(edge_index: Tensor, n_nodes: int, packed: Tensor) -> "EdgePlan":
+        """The plan of receiver-sorted edges from ``[dst_ptr | src_ptr | src_perm]`` computed on
+        the host (no sort on the device)."""
+        src, dst = edge_index[0], edge_index[1]
+        E = int(src.shape[0])
+        n1 = n_nodes + 1
+        return EdgePlan(n_nodes, E, src.to(torch.int32), dst.to(torch.int32), src, dst, packed[:n1],
+                        None, packed[n1:2 * n1], packed[2 * n1:2 * n1 + E])
+
+    @staticmethod
     def build(edge_index: Tensor, n_nodes: int, assume_dst_sorted: Optional[bool] = None,
               n_src: Optional[int] = None) -> "EdgePlan":
         src, dst = edge_index[0], edge_index[1]

@@ -6,7 +6,8 @@ A problem table goes to one kernel launch:
   through ``perm`` and restricted to the segment ``seg = (start, end)`` of the permuted row
   space (device tensor, e.g. the atoms of one element);
 * :class:`MMT` -- ``out = scale * (X0^T D0 + X1^T D1)`` summed over the rows (same row
-  options), split over CTAs with a deterministic in-kernel sum of the partial blocks.
+  options), split over CTAs whose partial blocks a second kernel sums in a fixed order
+  (deterministic).
 
 Weights are packed once per step (:func:`pack`) into the MMA operand layout. On the CPU (and
 for shapes the kernel does not take) the same problems evaluate with PyTorch, which is what the
@@ -124,8 +125,9 @@ def _mmt_ok(p: MMT) -> bool:
     return kernels(p.X0) and K1 % 4 == 0 and 4 <= K1 <= 128 and N % 16 == 0 and 16 <= N <= 256
 
 
-def mm(problems: Sequence[MM]) -> None:
-    """Run every row product (one kernel launch for those the kernel takes)."""
+def mm(problems: Sequence[MM], trace: Optional[Tensor] = None) -> None:
+    """Run every row product (one kernel launch for those the kernel takes). ``trace`` (int64,
+    8 slots per CTA) receives each CTA's phase timestamps in nanoseconds (diagnostics)."""
     fast = [p for p in problems if _mm_ok(p)]
     for p in problems:
         if not _mm_ok(p):
@@ -138,11 +140,12 @@ def mm(problems: Sequence[MM]) -> None:
         _ext.ops().node_mm([p.X0 for p in chunk], [p.X1 for p in chunk], [p.Y for p in chunk],
                            [p.Wp for p in chunk], [p.perm for p in chunk], [p.seg for p in chunk],
                            [int(p.X0.shape[0] if p.rows is None else p.rows) for p in chunk],
-                           [bool(p.accumulate) for p in chunk], st["status"], SPIN_LIMIT)
+                           [bool(p.accumulate) for p in chunk], st["status"], SPIN_LIMIT, trace)
 
 
-def mmT(problems: Sequence[MMT]) -> None:
-    """Run every reduction (one kernel launch for those the kernel takes)."""
+def mmT(problems: Sequence[MMT], trace: Optional[Tensor] = None) -> None:
+    """Run every reduction (one kernel launch for those the kernel takes); ``trace`` as in
+    :func:`mm`."""
     fast = [p for p in problems if _mmt_ok(p)]
     for p in problems:
         if not _mmt_ok(p):
@@ -158,7 +161,7 @@ def mmT(problems: Sequence[MMT]) -> None:
                             [int(0 if p.X1 is None else (p.X1.shape[0] if p.rows1 is None else p.rows1))
                              for p in chunk],
                             [p.out for p in chunk], [float(p.scale) for p in chunk], st["counters"],
-                            st["status"], SPIN_LIMIT)
+                            st["status"], SPIN_LIMIT, trace)
 
 
 def species_sort(z: Tensor, n_el: int):

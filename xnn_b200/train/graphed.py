@@ -92,7 +92,7 @@ def pad_graph(b: AtomicGraph, max_atoms: int, max_edges: int, max_graphs: int, c
              "charges": "charges_mask", "properties": "properties_mask"}
     for f in fields(AtomicGraph):
         name = f.name
-        if name in kw or name in ("cell", "pbc") or name.endswith("_mask"):
+        if name in kw or name in ("cell", "pbc", "edge_plan") or name.endswith("_mask"):
             continue
         v = getattr(b, name)
         if not isinstance(v, Tensor):
@@ -104,7 +104,21 @@ def pad_graph(b: AtomicGraph, max_atoms: int, max_edges: int, max_graphs: int, c
             kw[masks[name]] = torch.cat([m if m is not None else ones_b, zeros_nb])
     afw = b.atom_force_weight if b.atom_force_weight is not None else b.pos.new_ones(n)
     kw["atom_force_weight"] = torch.cat([afw, afw.new_zeros(na)])
+    kw["edge_plan"] = packed_edge_plan(kw["edge_index"], max_atoms)
     return AtomicGraph(**kw)
+
+
+def packed_edge_plan(edge_index: Tensor, n_nodes: int) -> Tensor:
+    """``[dst_ptr | src_ptr | src_perm]`` (int64) of receiver-sorted edges, on the host."""
+    import numpy as np
+    ei = edge_index.detach().cpu().numpy()
+    src, dst = ei[0], ei[1]
+    dst_ptr = np.zeros(n_nodes + 1, dtype=np.int64)
+    np.cumsum(np.bincount(dst, minlength=n_nodes), out=dst_ptr[1:])
+    src_ptr = np.zeros(n_nodes + 1, dtype=np.int64)
+    np.cumsum(np.bincount(src, minlength=n_nodes), out=src_ptr[1:])
+    src_perm = np.argsort(src, kind="stable").astype(np.int64)
+    return torch.from_numpy(np.concatenate([dst_ptr, src_ptr, src_perm])).to(edge_index.device)
 
 
 def copy_graph_(dst: AtomicGraph, src: AtomicGraph) -> None:

@@ -248,8 +248,7 @@ class _Ops:
 # ----------------------------------------------------------------------------- weights
 @dataclass
 class _Weights:
-    """Effective matrices of one step, built from the parameters with autograd on (so that
-    their cotangents back-propagate to the raw parameters through the scalings and views)."""
+    """Effective matrices of one step (scaled views of the parameters, detached)."""
 
     emb: Tensor                      # (n_el, C)
     up: List[Tensor]                 # (C, C)
@@ -264,35 +263,121 @@ class _Weights:
     ro_w2: Tensor                    # (H, 1)
     ro_c: float                      # SiLU normalisation constant
 
-    def tensors(self) -> List[Tensor]:
-        out = [self.emb] + self.up + self.sc + [w for ws in self.radial for w in ws] + \
-            [w for ws in self.lin for w in ws] + self.sym + self.prod + self.ro_lin + [self.ro_w1, self.ro_w2]
+
+@dataclass
+class _Entry:
+    """One effective matrix: ``view(param) * scalar`` (times ``col`` per column when given)."""
+
+    param: torch.nn.Parameter
+    offset: int
+    shape: Tuple[int, ...]
+    permute: Optional[Tuple[int, ...]]
+    scalar: float
+    col: Optional[Tensor] = None
+
+    def view(self, t: Tensor) -> Tensor:
+        v = t.reshape(-1).narrow(0, self.offset, math.prod(self.shape)).view(self.shape)
+        return v.permute(*self.permute) if self.permute is not None else v
+
+
+class _WeightMap:
+    """The effective matrices of a MACE model as scaled views of its parameters.
+
+    Every matrix the step multiplies with is a parameter (or a slice of one) times a constant --
+    the e3nn path normalisations, ``1 / avg_num_neighbors``, the radial layers' factors and the
+    tensor-product path coefficients per column. So the step builds them with one multi-tensor
+    multiply and returns their gradients the same way (scaled and added into the parameters'
+    gradient buffers), with no autograd graph over the weights."""
+
+    def __init__(self, m, like: Tensor):
+        from ..models.mace_fast import _conv_path_scale
+        from ..o3 import wigner_3j
+        n_el = len(m.species)
+        ef = m.edge_feat
+        self.order: Dict[str, object] = {}
+
+        def lin_entries(lin, extra: float = 1.0) -> List[_Entry]:
+            out, off = [], 0
+            for ins in lin.instructions:
+                shp = tuple(int(x) for x in ins.path_shape)
+                out.append(_Entry(lin.weight, off, shp, None, float(ins.path_weight) * extra))
+                off += math.prod(shp)
+            return out
+
+        def species_entry(tp) -> _Entry:
+            ins = tp.instructions[0]
+            c_in, ne, c_out = (int(x) for x in ins.path_shape)
+            l = tp.irreps_out[ins.i_out].ir.l
+            cg = float(wigner_3j(l, 0, l, dtype=torch.float64)[0, 0, 0])
+            return _Entry(tp.weight, 0, (c_in, ne, c_out), (1, 0, 2), float(ins.path_weight) * cg)
+
+        self.emb = lin_entries(m.node_embedding)[0]
+        self.up, self.sc, self.radial, self.spec, self.lin, self.sym, self.prod = [], [], [], [], [], [], []
+        for blk, pr in zip(m.interactions, m.products):
+            self.up.append(lin_entries(blk.linear_up)[0])
+            self.sc.append(species_entry(blk.skip_tp))
+            spec = RAD.RadialSpec(blk.conv_tp_weights, _conv_path_scale(blk, like), ef.rbf.freqs, ef.rbf.norm,
+                                  ef.cutoff, ef.envelope.p)
+            self.spec.append(spec)
+            layers = [layer.weight for layer in blk.conv_tp_weights]
+            rad = [_Entry(w, 0, tuple(w.shape), None, f) for w, f in zip(layers, spec.factors)]
+            rad[-1].col = spec.col_scale
+            self.radial.append(rad)
+            self.lin.append(lin_entries(blk.linear, 1.0 / float(blk.avg_num_neighbors)))
+            con = pr.symmetric_contractions.contractions[0]
+            self.sym.append([_Entry(w, 0, tuple(w.shape), None, 1.0) for w in con.weights])
+            self.prod.append(lin_entries(pr.linear)[0])
+        self.ro_lin = [lin_entries(ro.linear)[0] for ro in m.readouts[:-1]]
+        last = m.readouts[-1]
+        self.w1 = lin_entries(last.linear_1)[0]
+        self.w2 = lin_entries(last.linear_2)[0]
+        act = last.non_linearity.act
+        self.c = 1.0 if act._is_id else float(act.cst)
+
+    def _flat(self) -> List[_Entry]:
+        out = [self.emb] + self.up + self.sc + [e for es in self.radial for e in es] + \
+            [e for es in self.lin for e in es] + [e for es in self.sym for e in es] + self.prod + self.ro_lin + \
+            [self.w1, self.w2]
         return out
 
+    def build(self) -> _Weights:
+        ents = self._flat()
+        views = [e.view(e.param.detach()) for e in ents]
+        scaled = torch._foreach_mul(views, [e.scalar for e in ents])
+        eff = {}
+        for e, v in zip(ents, scaled):
+            eff[id(e)] = v * e.col.to(v) if e.col is not None else v
+        g = lambda e: eff[id(e)]  # noqa: E731
+        return _Weights(g(self.emb), [g(e) for e in self.up], [g(e) for e in self.sc],
+                        [[g(e) for e in es] for es in self.radial], self.spec,
+                        [[g(e) for e in es] for es in self.lin],
+                        [torch.cat([g(e) for e in es], dim=1) for es in self.sym],
+                        [g(e) for e in self.prod], [g(e) for e in self.ro_lin], g(self.w1), g(self.w2), self.c)
 
-def _effective_weights(m, like: Tensor) -> _Weights:
-    from ..models.mace_fast import _conv_path_scale, _linear_blocks, _species_weights
-    n_el = len(m.species)
-    ef = m.edge_feat
-    up, sc, radial, spec, lin, sym, prod, ro_lin = [], [], [], [], [], [], [], []
-    for blk, pr in zip(m.interactions, m.products):
-        up.append(_linear_blocks(blk.linear_up)[0])
-        sc.append(_species_weights(blk.skip_tp, n_el))
-        s = RAD.RadialSpec(blk.conv_tp_weights, _conv_path_scale(blk, like), ef.rbf.freqs, ef.rbf.norm,
-                           ef.cutoff, ef.envelope.p)
-        spec.append(s)
-        radial.append(RAD._eff([layer.weight for layer in blk.conv_tp_weights], s))
-        lin.append([w / blk.avg_num_neighbors for w in _linear_blocks(blk.linear)])
-        con = pr.symmetric_contractions.contractions[0]
-        sym.append(torch.cat(list(con.weights), dim=1))
-        prod.append(_linear_blocks(pr.linear)[0])
-    for ro in m.readouts[:-1]:
-        ro_lin.append(_linear_blocks(ro.linear)[0])
-    last = m.readouts[-1]
-    act = last.non_linearity.act
-    c = 1.0 if act._is_id else float(act.cst)
-    return _Weights(_linear_blocks(m.node_embedding)[0], up, sc, radial, spec, lin, sym, prod, ro_lin,
-                    _linear_blocks(last.linear_1)[0], _linear_blocks(last.linear_2)[0], c)
+    def add_grads(self, grads: Dict[str, object]) -> None:
+        """Add the effective-matrix gradients (same structure as :class:`_Weights`) to the
+        parameters' ``.grad`` (created as zeros where missing)."""
+        pairs: List[Tuple[_Entry, Tensor]] = [(self.emb, grads["emb"])]
+        pairs += list(zip(self.up, grads["up"])) + list(zip(self.sc, grads["sc"]))
+        for es, gs in zip(self.radial, grads["radial"]):
+            pairs += list(zip(es, gs))
+        for es, gs in zip(self.lin, grads["lin"]):
+            pairs += list(zip(es, gs))
+        for es, gsym in zip(self.sym, grads["sym"]):
+            k0 = 0
+            for e in es:
+                k = e.shape[1]
+                pairs.append((e, gsym[:, k0:k0 + k]))
+                k0 += k
+        pairs += list(zip(self.prod, grads["prod"])) + list(zip(self.ro_lin, grads["ro_lin"]))
+        pairs += [(self.w1, grads["w1"]), (self.w2, grads["w2"])]
+        live = [(e, g) for e, g in pairs if e.param.requires_grad]
+        for e, _ in live:
+            if e.param.grad is None:
+                e.param.grad = torch.zeros_like(e.param)
+        gs = [g * e.col.to(g) if e.col is not None else g for e, g in live]
+        gs = torch._foreach_mul(gs, [e.scalar for e, _ in live])
+        torch._foreach_add_([e.view(e.param.grad) for e, _ in live], gs)
 
 
 # ----------------------------------------------------------------------------- the step
@@ -333,6 +418,7 @@ class MACEStep:
         # constants read once (a captured step may not read device memory from the host)
         self.scale = float(self.m.scale_shift.scale)
         self.shift = float(self.m.scale_shift.shift)
+        self._maps: Dict[tuple, _WeightMap] = {}
 
     def __call__(self, b) -> Tuple[Tensor, Dict[str, Tensor], Dict[str, Tensor]]:
         m = self.m
@@ -342,14 +428,20 @@ class MACEStep:
         vec = b.edge_vectors().detach()
         dev, dt = vec.device, vec.dtype
         ops = _Ops(vec.is_cuda, m.max_ell, self.corr, m.edge_feat)
-        with torch.enable_grad():
-            Wt = _effective_weights(m, vec)
+        key = (vec.device, vec.dtype)
+        if self._maps.get(key) is None:
+            self._maps[key] = _WeightMap(m, vec)
+        wmap = self._maps[key]
+        Wt = wmap.build()
         n_el, C, T = len(m.species), m.num_features, len(m.interactions)
         P, D = ops.P, ops.D
         N, E = b.num_nodes, vec.shape[0]
         Z = b.atomic_numbers
         z = m.z_to_index[Z].clamp(min=0)
-        plan = K.EdgePlan.build(b.edge_index, N, assume_dst_sorted=b.edge_order == "dst")
+        if b.edge_plan is not None and b.edge_order == "dst":
+            plan = K.EdgePlan.from_packed(b.edge_index, N, b.edge_plan)
+        else:
+            plan = K.EdgePlan.build(b.edge_index, N, assume_dst_sorted=b.edge_order == "dst")
         scale, shift = self.scale, self.shift
         perm, seg = NG.species_sort(z, n_el)
         emb = Wt.emb.detach()
@@ -546,12 +638,9 @@ class MACEStep:
         NG.mmT(red)
         g_emb = torch.zeros_like(emb).index_add_(0, z, hb[0])
 
-        # effective-weight cotangents back to the parameters
-        grads = [g_emb] + g_up + g_sc + [g for gs in g_rad for g in gs] + [g for gs in g_lin for g in gs] + \
-            g_sym + g_prod + g_rol + [gw1, gw2]
-        pairs = [(w, g_) for w, g_ in zip(Wt.tensors(), grads) if w.requires_grad]
-        if pairs:
-            torch.autograd.backward([w for w, _ in pairs], [g_ for _, g_ in pairs])
+        # effective-matrix gradients back to the parameters
+        wmap.add_grads({"emb": g_emb, "up": g_up, "sc": g_sc, "radial": g_rad, "lin": g_lin, "sym": g_sym,
+                        "prod": g_prod, "ro_lin": g_rol, "w1": gw1, "w2": gw2})
         ar = m.atom_ref.weight
         if ar.requires_grad and self.we > 0:
             gar = torch.zeros_like(ar).index_add_(0, Z, a_s.to(ar.dtype).index_select(0, b.batch)[:, None])

@@ -30,7 +30,8 @@ OWN_KERNELS = ("conv_gather", "conv_edge", "conv_scatter", "symcon_", "edge_geom
                "gemm_ws_pack_kernel", "gemm_reduce_ws_kernel", "sum_partials_kernel", "radial_basis_kernel",
                "radial_act_kernel", "radial_dact_kernel", "nb_count", "nb_write", "mp_real_kernel",
                "pme_spread_kernel", "pme_gather_kernel", "xnn_", "nl_", "mace_", "tn_", "pme_", "halo_",
-               "adam_", "grad_", "seg_", "dd_", "fft_", "eeq_", "atm_", "amoeba_", "reax_", "sqm_")
+               "adam_", "grad_", "seg_", "dd_", "fft_", "eeq_", "atm_", "amoeba_", "reax_", "sqm_", "node_",
+               "species_sort")
 
 
 def is_own_kernel(name: str) -> bool:
