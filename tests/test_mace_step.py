@@ -13,10 +13,10 @@ from xnn_b200.train import mace_step
 from xnn_b200.train.losses import weighted_loss
 
 
-def _setup(dtype, device, channels=8, seed=0, n_struct=3):
+def _setup(dtype, device, channels=8, seed=0, n_struct=3, max_ell=3, correlation=3):
     torch.manual_seed(seed)
     model = MACE(species=[1, 6, 7, 8, 9, 16, 17], cutoff=4.5, num_channels=channels, n_rbf=8, num_interactions=2,
-                 max_ell=3, correlation=3, avg_num_neighbors=9.0).to(device=device, dtype=dtype)
+                 max_ell=max_ell, correlation=correlation, avg_num_neighbors=9.0).to(device=device, dtype=dtype)
     # non-trivial readouts, self-connections and reference energies
     with torch.no_grad():
         for p in model.parameters():
@@ -99,3 +99,15 @@ def test_step_matches_autograd_gpu_float64():
 def test_step_matches_autograd_gpu_float32_bench_width():
     # the benchmarked width (96 channels, l <= 3, correlation 3): fp32 parity at 1e-3 relative
     _gpu_compare(torch.float32, 96, 1e-3)
+
+
+@pytest.mark.parametrize("max_ell,correlation", [(2, 2), (1, 3)])
+def test_step_matches_autograd_other_degrees(max_ell, correlation):
+    pot, b = _setup(torch.float64, "cpu", max_ell=max_ell, correlation=correlation)
+    pot.model.set_use_fast(True)
+    l0, f0, g0 = _autograd(pot, b, 1.0, 10.0)
+    l1, f1, g1 = _engine(pot, b, 1.0, 10.0)
+    torch.testing.assert_close(l1, l0, rtol=1e-10, atol=1e-12)
+    for name in g0:
+        err = (g1[name] - g0[name]).abs().max() / g0[name].abs().max().clamp_min(1e-12)
+        assert err < 1e-8, (name, float(err))

@@ -5,6 +5,7 @@
 #include <torch/extension.h>
 
 #include <algorithm>
+#include <cmath>
 #include <vector>
 
 #define NM_MAX_PROBS 24
@@ -69,6 +70,11 @@ cudaError_t node_mmT_launch(NodeRedArgs& args, int total_ctas, int max_k1, int m
 cudaError_t node_pack_launch(PackArgs& args, cudaStream_t s);
 size_t node_pack_floats(int K, int N);
 cudaError_t species_sort_launch(int n, int n_el, const int64_t* z, int* perm, int* seg, cudaStream_t s);
+template <typename T>
+cudaError_t mace_dual_reverse(int N, int C, int P, int64_t E, const int64_t* dst_ptr, const int* src,
+                              const int64_t* src_ptr, const int64_t* src_perm, const T* G, const T* Gd, const T* Y,
+                              const T* Yd, const T* rdot, const T* u, const T* ud, const T* R, const T* Rd, T* Rbar,
+                              T* Rdbar, T* T14, T* T2, T* ub, T* ubd, cudaStream_t s);
 
 namespace {
 
@@ -207,10 +213,10 @@ void node_mmT(std::vector<torch::Tensor> X0, std::vector<torch::Tensor> D0,
     p.scale = (float)scale[i];
     p.perm = opt_i32(perm[i], "perm");
     p.seg = opt_i32(seg[i], "seg");
-    // CTAs per problem: about one per 512 rows (a segment's rows are only known on the device,
+    // CTAs per problem: about one per 256 rows (a segment's rows are only known on the device,
     // where they are split evenly over these CTAs; `rows` is then the caller's size hint)
     const int total = p.rows[0] + p.rows[1];
-    p.ctas = std::max(1, std::min(64, (total + 511) / 512));
+    p.ctas = std::max(1, std::min(96, (total + 255) / 256));
     p.rows_per_cta = 0;
     p.cta0 = ctas;
     p.counter = reinterpret_cast<unsigned int*>(counters.data_ptr<int>() + i);
@@ -265,9 +271,51 @@ std::vector<torch::Tensor> species_sort(torch::Tensor z, int64_t n_el) {
   return {perm, seg};
 }
 
+// Fused reverse of the tangent-carrying convolution (mace_dual.cu): returns
+// (R_bar, R'_bar, u_bar, u_dot_bar or undefined); edges grouped by receiver (no permutation).
+std::vector<torch::Tensor> mace_dual_reverse_op(torch::Tensor dst_ptr, torch::Tensor src, torch::Tensor src_ptr,
+                                                torch::Tensor src_perm, torch::Tensor G, torch::Tensor Gd,
+                                                torch::Tensor Y, torch::Tensor Yd, torch::Tensor rdot,
+                                                torch::Tensor u, c10::optional<torch::Tensor> ud, torch::Tensor R,
+                                                torch::Tensor Rd) {
+  TORCH_CHECK(G.is_cuda() && G.dim() == 3 && G.is_contiguous() && Gd.is_contiguous(), "mace_dual_reverse: G (D, N, C)");
+  TORCH_CHECK(src.scalar_type() == torch::kInt32 && dst_ptr.scalar_type() == torch::kInt64 &&
+                  src_ptr.scalar_type() == torch::kInt64 && src_perm.scalar_type() == torch::kInt64,
+              "mace_dual_reverse: index dtypes");
+  const int64_t D = G.size(0), N = G.size(1), C = G.size(2);
+  const int P = (int)std::lround(std::sqrt((double)D));
+  TORCH_CHECK(P * P == D && P >= 1 && P <= 4, "mace_dual_reverse: D must be (lmax + 1)^2 with lmax <= 3");
+  const int64_t E = Y.size(0);
+  TORCH_CHECK(R.is_contiguous() && Rd.is_contiguous() && R.numel() == E * P * C && Rd.numel() == E * P * C,
+              "mace_dual_reverse: R, R' (E, P, C)");
+  TORCH_CHECK(Y.is_contiguous() && Yd.is_contiguous() && rdot.is_contiguous() && u.is_contiguous(),
+              "mace_dual_reverse: contiguous inputs");
+  c10::cuda::CUDAGuard guard(G.device());
+  auto Rbar = torch::empty({E, P, C}, G.options());
+  auto Rdbar = torch::empty({E, P, C}, G.options());
+  auto T14 = torch::empty({E, P, C}, G.options());
+  auto T2 = torch::empty({E, P, C}, G.options());
+  auto ub = torch::empty({N, C}, G.options());
+  const bool with_ud = ud.has_value() && ud->defined();
+  torch::Tensor ubd = with_ud ? torch::empty({N, C}, G.options()) : torch::Tensor();
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(G.scalar_type(), "mace_dual_reverse", [&] {
+    cudaError_t e = mace_dual_reverse<scalar_t>(
+        (int)N, (int)C, P, E, dst_ptr.data_ptr<int64_t>(), src.data_ptr<int>(), src_ptr.data_ptr<int64_t>(),
+        src_perm.data_ptr<int64_t>(), G.data_ptr<scalar_t>(), Gd.data_ptr<scalar_t>(), Y.data_ptr<scalar_t>(),
+        Yd.data_ptr<scalar_t>(), rdot.data_ptr<scalar_t>(), u.data_ptr<scalar_t>(),
+        with_ud ? ud->data_ptr<scalar_t>() : nullptr, R.data_ptr<scalar_t>(), Rd.data_ptr<scalar_t>(),
+        Rbar.data_ptr<scalar_t>(), Rdbar.data_ptr<scalar_t>(), T14.data_ptr<scalar_t>(), T2.data_ptr<scalar_t>(),
+        ub.data_ptr<scalar_t>(), with_ud ? ubd.data_ptr<scalar_t>() : nullptr, st);
+    TORCH_CHECK(e == cudaSuccess, "mace_dual_reverse: ", cudaGetErrorString(e));
+  });
+  return {Rbar, Rdbar, ub, ubd};
+}
+
 }  // namespace
 
 void register_node(pybind11::module& m) {
+  m.def("mace_dual_reverse", &mace_dual_reverse_op);
   m.def("node_mm", &node_mm);
   m.def("node_mmT", &node_mmT);
   m.def("node_pack", &node_pack);

@@ -1,0 +1,193 @@
+// Reverse sweep of the MACE convolution in the tangent-carrying training step, fused.
+//
+// The forward pair (A, A_dot) of the convolution in the training step is
+//   A     = conv(u, R, Y)
+//   A_dot = conv(u_dot, R, Y) + conv(u, R', r_dot Y) + conv(u, R, Y_dot)
+// with conv(x, R, Y)[lm, d, c] = sum_{e into d} R[e, l, c] x[s, c] Y[e, lm]. Its reverse for the
+// cotangent pair (G, G_dot) = (A_bar, A_dot_bar) needs, per edge e = (s -> d),
+//   T1 = sum_m G[lm, d] Y[e, lm],  T2 = sum_m G_dot[lm, d] Y[e, lm],  T4 = sum_m G_dot[lm, d] Y_dot[e, lm]
+//   R_bar  = u[s] (T1 + T4) + u_dot[s] T2          (cotangent of R)
+//   R'_bar = u[s] r_dot T2                          (cotangent of R' = dR/dr)
+// and, per sender s,
+//   u_bar[s]     = sum_{e out of s} sum_l R (T1 + T4) + r_dot R' T2
+//   u_dot_bar[s] = sum_{e out of s} sum_l R T2.
+// dual_edge_kernel (one block per receiver, lanes over channels, warps over its edges) writes
+// R_bar, R'_bar, T14 = T1 + T4 and T2 in one pass; dual_scatter_kernel (one block per sender,
+// edges through the sender permutation) forms both sender sums from R, R', T14, T2 and r_dot in
+// one pass. Deterministic: every sum is a fixed-order register accumulation or a fixed-order
+// reduction over the block's warps.
+#include "common.cuh"
+
+namespace {
+
+template <typename T, int P, int CPL, int WPA>
+__global__ void __launch_bounds__(32 * WPA) dual_edge_kernel(
+    int N, int C, const int64_t* __restrict__ dst_ptr, const int* __restrict__ src, const T* __restrict__ G,
+    const T* __restrict__ Gd, const T* __restrict__ Y, const T* __restrict__ Yd, const T* __restrict__ rdot,
+    const T* __restrict__ u, const T* __restrict__ ud, T* __restrict__ Rbar, T* __restrict__ Rdbar,
+    T* __restrict__ T14, T* __restrict__ T2out) {
+  constexpr int D = P * P;
+  const int i = blockIdx.x;
+  const int w = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cbase = blockIdx.y * 32 * CPL;
+  T g[CPL][D], gd[CPL][D];
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) {
+    const int c = cbase + lane + 32 * q;
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      g[q][d] = c < C ? __ldg(G + ((int64_t)d * N + i) * C + c) : T(0);
+      gd[q][d] = c < C ? __ldg(Gd + ((int64_t)d * N + i) * C + c) : T(0);
+    }
+  }
+  const int64_t j0 = dst_ptr[i], j1 = dst_ptr[i + 1];
+  for (int64_t e = j0 + w; e < j1; e += WPA) {
+    const int64_t s = src[e];
+    T y[D], yd[D];
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      y[d] = __ldg(Y + e * D + d);
+      yd[d] = __ldg(Yd + e * D + d);
+    }
+    const T rd = __ldg(rdot + e);
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c = cbase + lane + 32 * q;
+      if (c >= C) continue;
+      const T us = __ldg(u + s * C + c);
+      const T uds = ud ? __ldg(ud + s * C + c) : T(0);
+#pragma unroll
+      for (int l = 0; l < P; ++l) {
+        T t1 = T(0), t2 = T(0), t4 = T(0);
+#pragma unroll
+        for (int m = 0; m < 2 * l + 1; ++m) {
+          const int k = l * l + m;
+          t1 += g[q][k] * y[k];
+          t2 += gd[q][k] * y[k];
+          t4 += gd[q][k] * yd[k];
+        }
+        const int64_t o = (e * P + l) * C + c;
+        const T t14 = t1 + t4;
+        Rbar[o] = us * t14 + uds * t2;
+        Rdbar[o] = us * rd * t2;
+        T14[o] = t14;
+        T2out[o] = t2;
+      }
+    }
+  }
+}
+
+template <typename T, int P, int CPL, int WPA>
+__global__ void __launch_bounds__(32 * WPA) dual_scatter_kernel(
+    int N, int C, const int64_t* __restrict__ src_ptr, const int64_t* __restrict__ src_perm, const T* __restrict__ R,
+    const T* __restrict__ Rd, const T* __restrict__ T14, const T* __restrict__ T2, const T* __restrict__ rdot,
+    T* __restrict__ ub, T* __restrict__ ubd) {
+  const int s = blockIdx.x;
+  const int w = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cbase = blockIdx.y * 32 * CPL;
+  T acc[CPL], accd[CPL];
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) acc[q] = accd[q] = T(0);
+  const int64_t j0 = src_ptr[s], j1 = src_ptr[s + 1];
+  for (int64_t j = j0 + w; j < j1; j += WPA) {
+    const int64_t e = src_perm[j];
+    const T rd = __ldg(rdot + e);
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c = cbase + lane + 32 * q;
+      if (c >= C) continue;
+#pragma unroll
+      for (int l = 0; l < P; ++l) {
+        const int64_t o = (e * P + l) * C + c;
+        const T r = __ldg(R + o), t2 = __ldg(T2 + o);
+        acc[q] += r * __ldg(T14 + o) + rd * __ldg(Rd + o) * t2;
+        accd[q] += r * t2;
+      }
+    }
+  }
+  __shared__ T red[2][WPA][32 * CPL];
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) {
+    red[0][w][q * 32 + lane] = acc[q];
+    red[1][w][q * 32 + lane] = accd[q];
+  }
+  __syncthreads();
+  if (w != 0) return;
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) {
+    T v = red[0][0][q * 32 + lane], vd = red[1][0][q * 32 + lane];
+#pragma unroll
+    for (int ww = 1; ww < WPA; ++ww) {
+      v += red[0][ww][q * 32 + lane];
+      vd += red[1][ww][q * 32 + lane];
+    }
+    const int c = cbase + lane + 32 * q;
+    if (c < C) {
+      ub[(int64_t)s * C + c] = v;
+      if (ubd) ubd[(int64_t)s * C + c] = vd;
+    }
+  }
+}
+
+constexpr int kDualWPA = 4;
+
+template <typename T, int P>
+cudaError_t launch_dual(int N, int C, int64_t E, const int64_t* dst_ptr, const int* src, const int64_t* src_ptr,
+                        const int64_t* src_perm, const T* G, const T* Gd, const T* Y, const T* Yd, const T* rdot,
+                        const T* u, const T* ud, const T* R, const T* Rd, T* Rbar, T* Rdbar, T* T14, T* T2, T* ub,
+                        T* ubd, cudaStream_t s) {
+  if (N == 0) return cudaSuccess;
+  const int cpl = C <= 32 ? 1 : (C <= 64 ? 2 : (C <= 96 ? 3 : 4));
+  const dim3 grid(N, (C + 32 * cpl - 1) / (32 * cpl));
+  const dim3 block(32 * kDualWPA);
+#define XNN_DUAL(CPLV)                                                                                      \
+  dual_edge_kernel<T, P, CPLV, kDualWPA><<<grid, block, 0, s>>>(N, C, dst_ptr, src, G, Gd, Y, Yd, rdot, u, ud, \
+                                                               Rbar, Rdbar, T14, T2);                       \
+  {                                                                                                         \
+    const cudaError_t e_ = cudaGetLastError();                                                              \
+    if (e_ != cudaSuccess) return e_;                                                                       \
+  }                                                                                                         \
+  dual_scatter_kernel<T, P, CPLV, kDualWPA><<<grid, block, 0, s>>>(N, C, src_ptr, src_perm, R, Rd, T14, T2,   \
+                                                                  rdot, ub, ubd);
+  switch (cpl) {
+    case 1: XNN_DUAL(1); break;
+    case 2: XNN_DUAL(2); break;
+    case 3: XNN_DUAL(3); break;
+    default: XNN_DUAL(4); break;
+  }
+#undef XNN_DUAL
+  (void)E;
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+template <typename T>
+cudaError_t mace_dual_reverse(int N, int C, int P, int64_t E, const int64_t* dst_ptr, const int* src,
+                              const int64_t* src_ptr, const int64_t* src_perm, const T* G, const T* Gd, const T* Y,
+                              const T* Yd, const T* rdot, const T* u, const T* ud, const T* R, const T* Rd, T* Rbar,
+                              T* Rdbar, T* T14, T* T2, T* ub, T* ubd, cudaStream_t s) {
+  switch (P) {
+    case 1: return launch_dual<T, 1>(N, C, E, dst_ptr, src, src_ptr, src_perm, G, Gd, Y, Yd, rdot, u, ud, R, Rd,
+                                     Rbar, Rdbar, T14, T2, ub, ubd, s);
+    case 2: return launch_dual<T, 2>(N, C, E, dst_ptr, src, src_ptr, src_perm, G, Gd, Y, Yd, rdot, u, ud, R, Rd,
+                                     Rbar, Rdbar, T14, T2, ub, ubd, s);
+    case 3: return launch_dual<T, 3>(N, C, E, dst_ptr, src, src_ptr, src_perm, G, Gd, Y, Yd, rdot, u, ud, R, Rd,
+                                     Rbar, Rdbar, T14, T2, ub, ubd, s);
+    case 4: return launch_dual<T, 4>(N, C, E, dst_ptr, src, src_ptr, src_perm, G, Gd, Y, Yd, rdot, u, ud, R, Rd,
+                                     Rbar, Rdbar, T14, T2, ub, ubd, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+template cudaError_t mace_dual_reverse<float>(int, int, int, int64_t, const int64_t*, const int*, const int64_t*,
+                                              const int64_t*, const float*, const float*, const float*, const float*,
+                                              const float*, const float*, const float*, const float*, const float*,
+                                              float*, float*, float*, float*, float*, float*, cudaStream_t);
+template cudaError_t mace_dual_reverse<double>(int, int, int, int64_t, const int64_t*, const int*, const int64_t*,
+                                               const int64_t*, const double*, const double*, const double*,
+                                               const double*, const double*, const double*, const double*,
+                                               const double*, const double*, double*, double*, double*, double*,
+                                               double*, double*, cudaStream_t);

@@ -124,7 +124,9 @@ __device__ __forceinline__ int tmem_cols_for(int n) {
 }
 
 // ------------------------------------------------------------------------------------ row product
-__global__ void __launch_bounds__(128, 1) node_mm_kernel(const __grid_constant__ NodeMMArgs a) {
+constexpr int MT = 256;     // threads of the row-product kernel (8 warps)
+
+__global__ void __launch_bounds__(MT, 1) node_mm_kernel(const __grid_constant__ NodeMMArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int pi = 0;
@@ -182,24 +184,24 @@ __global__ void __launch_bounds__(128, 1) node_mm_kernel(const __grid_constant__
       bulk_copy(b_st, wblk, 2 * wbytes, bars);
     }
     // A block: lane (r8, kl) of warp w loads the 16-byte chunks k4 = kl, kl + 4, ... of rows
-    // 8 g + r8 for row groups g = w, w + 4, w + 8, w + 12 -- per instruction eight rows x 64
-    // contiguous bytes from global memory, 512 contiguous bytes into shared memory. All loads of a
-    // thread are independent (row indices first), then split into TF32 halves and stored.
+    // 8 g + r8 for row groups g = w, w + 8 -- per instruction eight rows x 64 contiguous bytes
+    // from global memory, 512 contiguous bytes into shared memory. All loads of a thread are
+    // independent (row indices first) and issued together, then split and stored.
     {
       const int k4n = kbp / 4;
       const int r8 = lane & 7, kl = lane >> 3;
-      int grow[4];
-      bool live[4];
+      int grow[2];
+      bool live[2];
 #pragma unroll
-      for (int gi = 0; gi < 4; ++gi) {
-        const int r = (warp + 4 * gi) * 8 + r8;
+      for (int gi = 0; gi < 2; ++gi) {
+        const int r = (warp + 8 * gi) * 8 + r8;
         live[gi] = r < nrow;
         grow[gi] = live[gi] ? (P.perm ? __ldg(P.perm + row0 + r) : row0 + r) : 0;
       }
-      // k4 = kl + 4 u (u < 6 covers k4n <= 24): all 24 loads of the thread issued together
-      float4 v[4][6];
+      // k4 = kl + 4 u (u < 6 covers k4n <= 24)
+      float4 v[2][6];
 #pragma unroll
-      for (int gi = 0; gi < 4; ++gi)
+      for (int gi = 0; gi < 2; ++gi)
 #pragma unroll
         for (int u = 0; u < 6; ++u) {
           const int k4 = kl + 4 * u;
@@ -212,14 +214,14 @@ __global__ void __launch_bounds__(128, 1) node_mm_kernel(const __grid_constant__
           }
         }
 #pragma unroll
-      for (int gi = 0; gi < 4; ++gi)
+      for (int gi = 0; gi < 2; ++gi)
 #pragma unroll
         for (int u = 0; u < 6; ++u) {
           const int k4 = kl + 4 * u;
           if (k4 < k4n) {
             float4 h, l;
             split4(v[gi][u], h, l);
-            const uint32_t off = canon_off((warp + 4 * gi) * 8 + r8, k4, kbp);
+            const uint32_t off = canon_off((warp + 8 * gi) * 8 + r8, k4, kbp);
             *reinterpret_cast<float4*>(a_hi + off) = h;
             *reinterpret_cast<float4*>(a_lo + off) = l;
           }
@@ -266,30 +268,32 @@ __global__ void __launch_bounds__(128, 1) node_mm_kernel(const __grid_constant__
     wblk += 2 * (size_t)N * kbp;
   }
   if (ok) {
-    // epilogue: warp w holds rows 32 w .. 32 w + 31 (TMEM lanes). Each thread parks its row in
-    // shared memory (the A buffers are free now; rows padded by 4 floats against bank
-    // conflicts), then the warp writes its rows one at a time with contiguous 16-byte stores.
-    float* stage = reinterpret_cast<float*>(a_hi) + (size_t)warp * 32 * (N + 4);
-    float* mine = stage + (size_t)lane * (N + 4);
-    for (int c0 = 0; c0 < N; c0 += 16) {
+    // epilogue: TMEM lane quarter q = w % 4 holds rows 32 q .. 32 q + 31; warps w and w + 4 read
+    // alternate 16-column pieces of those rows and park them in shared memory (the A buffers are
+    // free now; rows padded by 4 floats against bank conflicts). After a block barrier every warp
+    // writes 16 whole rows with contiguous 16-byte stores.
+    const int q = warp & 3, wg = warp >> 2;
+    float* stage = reinterpret_cast<float*>(a_hi);
+    float* mine = stage + (size_t)(q * 32 + lane) * (N + 4);
+    for (int c0 = wg * 16; c0 < N; c0 += 32) {
       float v[16];
-      tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+      tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
 #pragma unroll
       for (int j = 0; j < 16; j += 4)
         *reinterpret_cast<float4*>(mine + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
     }
     if (tr) tr[7] = global_ns();
-    // destination rows of the warp: lane i holds row 32 w + i's, broadcast below
-    const int my_r = warp * 32 + lane;
+    // destination rows: lane i holds the index of row 16 w + i (i < 16), broadcast below
+    const int my_r = warp * 16 + (lane & 15);
     const int my_gr = my_r < nrow ? (P.perm ? __ldg(P.perm + row0 + my_r) : row0 + my_r) : 0;
-    __syncwarp();
+    __syncthreads();
     const int n4 = N / 4;
-    for (int rr = 0; rr < 32; ++rr) {
-      const int r = warp * 32 + rr;
+    for (int rr = 0; rr < 16; ++rr) {
+      const int r = warp * 16 + rr;
       if (r >= nrow) break;                        // warp-uniform
       const int gr = __shfl_sync(0xffffffffu, my_gr, rr);
       float4* yrow = reinterpret_cast<float4*>(P.Y + (int64_t)gr * P.ldy);
-      const float4* src = reinterpret_cast<const float4*>(stage + (size_t)rr * (N + 4));
+      const float4* src = reinterpret_cast<const float4*>(stage + (size_t)r * (N + 4));
       for (int c = lane; c < n4; c += 32) {
         float4 o = src[c];
         if (P.accumulate) {
@@ -319,7 +323,9 @@ __global__ void __launch_bounds__(128, 1) node_mm_kernel(const __grid_constant__
 // and conversion of chunk g + 1 overlap the MMAs of chunk g.
 constexpr int RC = 32;      // rows per chunk
 
-__global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant__ NodeRedArgs a) {
+constexpr int RT = 256;     // threads of the reduction kernel (8 warps)
+
+__global__ void __launch_bounds__(RT, 1) node_mmT_kernel(const __grid_constant__ NodeRedArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int pi = 0;
@@ -364,7 +370,7 @@ __global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant_
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // operand rows past N / K1 stay zero: clear both stages once
-  for (int i = tid; i < (int)(2 * STAGE / 16); i += 128)
+  for (int i = tid; i < (int)(2 * STAGE / 16); i += RT)
     reinterpret_cast<float4*>(smem)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   tc_fence_before();
   __syncthreads();
@@ -385,69 +391,61 @@ __global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant_
       set_sm[b * RC + tid] = (unsigned char)set;
     }
   };
-  // operands of the chunk whose rows are in slot b, into stage b. Per pass a thread takes eight
-  // pieces of each operand (64 independent scalar loads in flight), then splits and stores them.
-  // Operand 0: A = D^T (pieces over n < N); operand 1: B = X^T (pieces over m < K1); a piece
-  // (c, k4) holds rows 4 k4 .. 4 k4 + 3 of column c, and the lanes of a warp run over c.
+  // operands of the chunk whose rows are in slot b, into stage b. A piece (c, k4) of an operand
+  // holds rows 4 k4 .. 4 k4 + 3 of column c. Items are (column block of 32, k4): warp w takes
+  // items w, w + 8, ... of both operands, its lanes the 32 columns of the block (coalesced row
+  // loads); all loads of a warp's items are issued before any is used.
   auto stage_chunk = [&](int b) {
     unsigned char* st = smem + (size_t)b * STAGE;
     const int* rw = rows_sm + b * RC;
     const unsigned char* sw = set_sm + b * RC;
-    const int dpad = (N + 31) / 32 * 32, xpad = (K1 + 31) / 32 * 32;
-    const int d_items = dpad * (RC / 4), x_items = xpad * (RC / 4);
-    const int passes = (max(d_items, x_items) + 8 * 128 - 1) / (8 * 128);
-    for (int pq = 0; pq < passes; ++pq) {
-      float v[2][8][4];
+    const int dblk = (N + 31) / 32, xblk = (K1 + 31) / 32;          // <= 8 and <= 4
+    const int d_items = dblk * (RC / 4), x_items = xblk * (RC / 4);   // <= 64 and <= 32
+    constexpr int MAXI = (8 + 4) * (RC / 4) / 8;                       // items per warp (both operands)
+    float v[MAXI][4];
 #pragma unroll
-      for (int op = 0; op < 2; ++op) {
-        const int cols = op == 0 ? N : K1;
-        const int cpad = op == 0 ? dpad : xpad;
-        const int items = op == 0 ? d_items : x_items;
+    for (int t = 0; t < MAXI; ++t) {
+      const int it = warp + 8 * t;                 // over d items, then x items
+      const bool is_d = it < d_items;
+      const int local = is_d ? it : it - d_items;
+      const bool real = is_d || local < x_items;
+      const int blk = local >> 3, k4 = local & 7;  // RC / 4 == 8
+      const int c = blk * 32 + lane;
+      const int cols = is_d ? N : K1;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int q = pq * 8 * 128 + tid + 128 * u;
-          const int c = q % cpad, k4 = q / cpad;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            v[op][u][i] = 0.f;
-            if (q < items && c < cols) {
-              const int row = rw[4 * k4 + i];
-              if (row >= 0) {
-                const int ss = sw[4 * k4 + i];
-                v[op][u][i] = op == 0 ? __ldg(P.D[ss] + (int64_t)row * P.ldd[ss] + c)
-                                      : __ldg(P.X[ss] + (int64_t)row * P.ldx[ss] + c);
-              }
-            }
+      for (int i = 0; i < 4; ++i) {
+        v[t][i] = 0.f;
+        if (real && c < cols) {
+          const int row = rw[4 * k4 + i];
+          if (row >= 0) {
+            const int ss = sw[4 * k4 + i];
+            v[t][i] = is_d ? __ldg(P.D[ss] + (int64_t)row * P.ldd[ss] + c)
+                           : __ldg(P.X[ss] + (int64_t)row * P.ldx[ss] + c);
           }
         }
       }
+    }
 #pragma unroll
-      for (int op = 0; op < 2; ++op) {
-        const int cols = op == 0 ? N : K1;
-        const int cpad = op == 0 ? dpad : xpad;
-        const int items = op == 0 ? d_items : x_items;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int q = pq * 8 * 128 + tid + 128 * u;
-          const int c = q % cpad, k4 = q / cpad;
-          if (q < items && c < cols) {
-            float4 h, l;
-            split4(make_float4(v[op][u][0], v[op][u][1], v[op][u][2], v[op][u][3]), h, l);
-            unsigned char* base;
-            uint32_t off, half;
-            if (op == 0) {
-              base = st + (size_t)(c >> 7) * 2 * A_BYTES;
-              off = canon_off(c & 127, k4, RC);
-              half = A_BYTES;
-            } else {
-              base = st + 2 * A_BYTES * npass;
-              off = canon_off(c, k4, RC);
-              half = B_BYTES;
-            }
-            *reinterpret_cast<float4*>(base + off) = h;
-            *reinterpret_cast<float4*>(base + half + off) = l;
-          }
-        }
+    for (int t = 0; t < MAXI; ++t) {
+      const int it = warp + 8 * t;
+      const bool is_d = it < d_items;
+      const int local = is_d ? it : it - d_items;
+      if (!is_d && local >= x_items) continue;
+      const int blk = local >> 3, k4 = local & 7;
+      const int c = blk * 32 + lane;
+      if (c >= (is_d ? N : K1)) continue;
+      float4 h, l;
+      split4(make_float4(v[t][0], v[t][1], v[t][2], v[t][3]), h, l);
+      if (is_d) {
+        unsigned char* base = st + (size_t)(c >> 7) * 2 * A_BYTES;
+        const uint32_t off = canon_off(c & 127, k4, RC);
+        *reinterpret_cast<float4*>(base + off) = h;
+        *reinterpret_cast<float4*>(base + A_BYTES + off) = l;
+      } else {
+        unsigned char* bst = st + 2 * A_BYTES * npass;
+        const uint32_t off = canon_off(c, k4, RC);
+        *reinterpret_cast<float4*>(bst + off) = h;
+        *reinterpret_cast<float4*>(bst + B_BYTES + off) = l;
       }
     }
   };
@@ -510,14 +508,15 @@ __global__ void __launch_bounds__(128, 1) node_mmT_kernel(const __grid_constant_
   ok = __syncthreads_and(ok ? 1 : 0) != 0;
   tc_fence_after();
   if (tr) tr[4] = global_ns();
-  // partial block G[k1][n] of this CTA (zeros when it had no rows)
+  // partial block G[k1][n] of this CTA (zeros when it had no rows); warps w and w + 4 share a
+  // TMEM lane quarter and take alternate 16-column pieces
   float* part = P.partial + (size_t)cta * K1 * N;
   for (int pass = 0; pass < npass; ++pass) {
-    const int n = pass * 128 + warp * 32 + lane;  // TMEM lane = D column
-    for (int c0 = 0; c0 < K1p; c0 += 16) {
+    const int n = pass * 128 + (warp & 3) * 32 + lane;  // TMEM lane = D column
+    for (int c0 = (warp >> 2) * 16; c0 < K1p; c0 += 32) {
       float v[16];
       if (g > 0 && ok) {
-        tmem_ld16(tmem + (uint32_t)(pass * K1p + c0) + ((uint32_t)(warp * 32) << 16), v);
+        tmem_ld16(tmem + (uint32_t)(pass * K1p + c0) + ((uint32_t)((warp & 3) * 32) << 16), v);
       } else {
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = 0.f;
@@ -654,7 +653,7 @@ cudaError_t node_mm_launch(NodeMMArgs& args, int total_tiles, int max_n, cudaStr
   const size_t smem = mm_smem(max_n);
   cudaError_t e = cudaFuncSetAttribute(node_mm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  node_mm_kernel<<<total_tiles, 128, smem, s>>>(args);
+  node_mm_kernel<<<total_tiles, MT, smem, s>>>(args);
   return cudaGetLastError();
 }
 
@@ -663,7 +662,7 @@ cudaError_t node_mmT_launch(NodeRedArgs& args, int total_ctas, int max_k1, int m
   const size_t smem = red_smem(max_k1, max_n);
   cudaError_t e = cudaFuncSetAttribute(node_mmT_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  node_mmT_kernel<<<total_ctas, 128, smem, s>>>(args);
+  node_mmT_kernel<<<total_ctas, RT, smem, s>>>(args);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const int most4 = max_k1 * max_n / 4;

@@ -92,12 +92,23 @@ class P2PAllReduce:
         shard = numel // self.world
         self.nblocks = nblocks or max(1, min(32, (shard + 4095) // 4096))
 
-    def all_reduce_mean_(self, flat: Optional[torch.Tensor] = None) -> None:
-        """Average the buffer over the ranks in place (``flat`` must be :attr:`buffer`)."""
+    def all_reduce_mean_(self, flat: Optional[torch.Tensor] = None, offset: int = 0,
+                         numel: Optional[int] = None) -> None:
+        """Average ``numel`` elements from ``offset`` of the buffer over the ranks, in place
+        (``flat``, when given, must be :attr:`buffer`). A range must be a multiple of
+        ``4 * world`` elements long and start on a multiple of 64 elements; every rank reduces
+        the same ranges in the same order."""
         if flat is not None and flat.data_ptr() != self.buffer.data_ptr():
             raise ValueError("P2PAllReduce reduces its own peer-mapped buffer")
-        _ext.ops().p2p_allreduce(self.buf_ptrs, self.flag_ptrs, self.epochs, self.status_addr,
-                                 self.world, self.rank, self.numel, 1.0 / self.world, self.nblocks,
+        n = self.numel - offset if numel is None else int(numel)
+        if offset < 0 or n < 0 or offset + n > self.numel or n % (4 * self.world) or offset % 64:
+            raise ValueError(f"range [{offset}, {offset + n}) is not a reducible range of {self.numel} elements")
+        if n == 0:
+            return
+        shift = 4 * int(offset)
+        nb = self.nblocks if numel is None else max(1, min(self.nblocks, (n // self.world + 4095) // 4096))
+        _ext.ops().p2p_allreduce([p + shift for p in self.buf_ptrs], self.flag_ptrs, self.epochs,
+                                 self.status_addr, self.world, self.rank, n, 1.0 / self.world, nb,
                                  SPIN_LIMIT, self.emulate)
 
     def status(self) -> int:

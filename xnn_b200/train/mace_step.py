@@ -41,7 +41,7 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
-from typing import Dict, List, Optional, Tuple
+from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
 from torch import Tensor
@@ -196,6 +196,26 @@ class _Ops:
                 part = x.index_select(0, plan.src)[:, None, :] * T
                 gR = part if gR is None else gR + part
         return gR, Ts
+
+    def dual_reverse(self, plan: K.EdgePlan, G: Tensor, Gd: Tensor, Y: Tensor, Yd: Tensor, rdot: Tensor,
+                     u: Tensor, ud: Optional[Tensor], R: Tensor, Rd: Tensor):
+        """Reverse of the tangent-carrying convolution for cotangents ``(G, G_dot)``:
+        ``(R_bar, R'_bar, u_bar, u_dot_bar)`` (the last ``None`` without ``u_dot``), see
+        ``csrc/mace_dual.cu``."""
+        if self.cuda and plan.dst_perm is None:
+            Rb, Rdb, ub, ubd = K._C().mace_dual_reverse(plan.dst_ptr, plan.src32, plan.src_ptr, plan.src_perm,
+                                                         G.contiguous(), Gd.contiguous(), Y.contiguous(),
+                                                         Yd.contiguous(), rdot.contiguous(), u.contiguous(),
+                                                         None if ud is None else ud.contiguous(), R.contiguous(),
+                                                         Rd.contiguous())
+            return Rb, Rdb, ub, (ubd if ud is not None else None)
+        gR_a, (T1,) = self.edge_terms(plan, G, [Y], [u])
+        gR_b, (T2, T4) = self.edge_terms(plan, Gd, [Y, Yd], [ud, u])
+        T2r = T2 * rdot[:, None, None]
+        Rdbar = u.index_select(0, plan.src)[:, None, :] * T2r
+        ub = self.scatter(plan, [(R, T1 + T4), (Rd, T2r)])
+        ubd = self.scatter(plan, [(R, T2)]) if ud is not None else None
+        return gR_a + gR_b, Rdbar, ub, ubd
 
     # ---------------------------------------------------------------- symmetric contraction
     def symcon(self, A: Tensor, z: Tensor, W: Tensor) -> Tensor:
@@ -354,24 +374,27 @@ class _WeightMap:
                         [torch.cat([g(e) for e in es], dim=1) for es in self.sym],
                         [g(e) for e in self.prod], [g(e) for e in self.ro_lin], g(self.w1), g(self.w2), self.c)
 
-    def add_grads(self, grads: Dict[str, object]) -> None:
-        """Add the effective-matrix gradients (same structure as :class:`_Weights`) to the
-        parameters' ``.grad`` (created as zeros where missing)."""
-        pairs: List[Tuple[_Entry, Tensor]] = [(self.emb, grads["emb"])]
-        pairs += list(zip(self.up, grads["up"])) + list(zip(self.sc, grads["sc"]))
-        for es, gs in zip(self.radial, grads["radial"]):
-            pairs += list(zip(es, gs))
-        for es, gs in zip(self.lin, grads["lin"]):
-            pairs += list(zip(es, gs))
-        for es, gsym in zip(self.sym, grads["sym"]):
-            k0 = 0
-            for e in es:
-                k = e.shape[1]
-                pairs.append((e, gsym[:, k0:k0 + k]))
-                k0 += k
-        pairs += list(zip(self.prod, grads["prod"])) + list(zip(self.ro_lin, grads["ro_lin"]))
-        pairs += [(self.w1, grads["w1"]), (self.w2, grads["w2"])]
+    def interaction_pairs(self, t: int, up, sc, radial, lin, sym, prod, ro=None) -> List[Tuple[_Entry, Tensor]]:
+        """(entry, gradient) pairs of interaction ``t`` (its block, product and readout)."""
+        pairs: List[Tuple[_Entry, Tensor]] = [(self.up[t], up), (self.sc[t], sc), (self.prod[t], prod)]
+        pairs += list(zip(self.radial[t], radial)) + list(zip(self.lin[t], lin))
+        k0 = 0
+        for e in self.sym[t]:
+            k = e.shape[1]
+            pairs.append((e, sym[:, k0:k0 + k]))
+            k0 += k
+        if t < len(self.ro_lin):
+            pairs.append((self.ro_lin[t], ro))
+        else:
+            pairs += [(self.w1, ro[0]), (self.w2, ro[1])]
+        return pairs
+
+    def add_grads(self, pairs: Sequence[Tuple[_Entry, Tensor]]) -> None:
+        """Add effective-matrix gradients to the parameters' ``.grad`` (created as zeros where
+        missing): scaled back by each entry's constants, one multi-tensor add."""
         live = [(e, g) for e, g in pairs if e.param.requires_grad]
+        if not live:
+            return
         for e, _ in live:
             if e.param.grad is None:
                 e.param.grad = torch.zeros_like(e.param)
@@ -420,7 +443,21 @@ class MACEStep:
         self.shift = float(self.m.scale_shift.shift)
         self._maps: Dict[tuple, _WeightMap] = {}
 
-    def __call__(self, b) -> Tuple[Tensor, Dict[str, Tensor], Dict[str, Tensor]]:
+    def bucket_params(self) -> List[List[torch.nn.Parameter]]:
+        """Parameter groups in the order the reverse sweep finishes them: interaction ``T - 1``
+        (block, product, readout) first, down to interaction 0; every other parameter (node
+        embedding, reference energies) is final only at the end."""
+        m = self.m
+        groups = []
+        for t in range(len(m.interactions) - 1, -1, -1):
+            mods = (m.interactions[t], m.products[t], m.readouts[t])
+            groups.append([p for mod in mods for p in mod.parameters()])
+        return groups
+
+    def __call__(self, b, bucket_hook: Optional[Callable[[int], None]] = None
+                 ) -> Tuple[Tensor, Dict[str, Tensor], Dict[str, Tensor]]:
+        """``bucket_hook(i)`` is called as soon as the gradients of group ``i`` of
+        :meth:`bucket_params` are final (a data-parallel reduction may start there)."""
         m = self.m
         mdt = m.atom_ref.weight.dtype
         if b.compute_dtype is None and b.pos.dtype != mdt:
@@ -502,7 +539,7 @@ class MACEStep:
             NG.mm([NG.MM(h[t], up[t], u[t], Pk["up"][t])] + sc_problems(t, h[t], hn))
             A.append(ops.gather(plan, [(u[t], Rs[t], Y)]))
             A2.append(torch.empty_like(A[t]))
-            NG.mm(_per_degree_problems(A[t], A2[t], lin[t], Pk["lin"][4 * t:4 * t + 4]))
+            NG.mm(_per_degree_problems(A[t], A2[t], lin[t], Pk["lin"][P * t:P * t + P]))
             Bs.append(ops.symcon(A2[t], z, symw[t]))
             NG.mm([NG.MM(Bs[t], prod[t], hn, Pk["prod"][t], accumulate=True)])
             h.append(hn)
@@ -530,7 +567,7 @@ class MACEStep:
             NG.mm([NG.MM(hb[t + 1], prod[t].t(), Bb, Pk["prodT"][t])])
             A2b = ops.symcon_vjp(A2[t], z, symw[t], Bb)
             Ab = torch.empty_like(A2b)
-            NG.mm(_per_degree_problems(A2b, Ab, [w.t() for w in lin[t]], Pk["linT"][4 * t:4 * t + 4]))
+            NG.mm(_per_degree_problems(A2b, Ab, [w.t() for w in lin[t]], Pk["linT"][P * t:P * t + P]))
             gr_t, gY_t, T1 = ops.edge_force(plan, Ab, Y, u[t], Rs[t], Rds[t])
             g_r = gr_t if g_r is None else g_r + gr_t
             gY = gY_t if gY is None else gY + gY_t
@@ -565,7 +602,7 @@ class MACEStep:
                 terms.insert(0, (ud[t], Rs[t], Y))
             Ad.append(ops.gather(plan, terms))
             A2d.append(torch.empty_like(Ad[t]))
-            NG.mm(_per_degree_problems(Ad[t], A2d[t], lin[t], Pk["lin"][4 * t:4 * t + 4]))
+            NG.mm(_per_degree_problems(Ad[t], A2d[t], lin[t], Pk["lin"][P * t:P * t + P]))
             Bd.append(ops.symcon_jvp(A2[t], z, symw[t], A2d[t]))
             NG.mm([NG.MM(Bd[t], prod[t], hdn, Pk["prod"][t], accumulate=t > 0)])
             hd.append(hdn)
@@ -583,7 +620,7 @@ class MACEStep:
         qbar = c_ro * (f1 * pb + f2 * qd * pbd)
         qbard = c_ro * f1 * pbd
         gw1 = torch.empty(w1.shape, dtype=w1.dtype, device=w1.device)
-        red = [NG.MMT(h[T], qbar, gw1, X1=hd[T], D1=qbard)]
+        red = [NG.MMT(h[T], qbar, gw1, X1=hd[T], D1=qbard)]     # reductions of the current interaction
         hb = [None] * (T + 1)
         hbd = [None] * (T + 1)
         hb[T], hbd[T] = empty_nc(), empty_nc()
@@ -613,18 +650,14 @@ class MACEStep:
                                   X1=Ad[t][sl].reshape(-1, C), D1=A2bd[sl].reshape(-1, C)))
             Ab, Abd = torch.empty_like(A2b), torch.empty_like(A2bd)
             linT = [w.t() for w in lin[t]]
-            NG.mm(_per_degree_problems(A2b, Ab, linT, Pk["linT"][4 * t:4 * t + 4])
-                  + _per_degree_problems(A2bd, Abd, linT, Pk["linT"][4 * t:4 * t + 4]))
-            # convolution: T1 = tee(Ab, Y), T2 = tee(Abd, Y), T4 = tee(Abd, Y_dot)
-            gR_a, (T1,) = ops.edge_terms(plan, Ab, [Y], [u[t]])
-            gR_b, (T2, T4) = ops.edge_terms(plan, Abd, [Y, Ydot], [ud[t] if t > 0 else None, u[t]])
-            Rbar = gR_a + gR_b
-            T2r = T2 * rdot[:, None, None]
-            Rdbar = u[t].index_select(0, src)[:, None, :] * T2r
+            NG.mm(_per_degree_problems(A2b, Ab, linT, Pk["linT"][P * t:P * t + P])
+                  + _per_degree_problems(A2bd, Abd, linT, Pk["linT"][P * t:P * t + P]))
+            Rbar, Rdbar, ub, ubd = ops.dual_reverse(plan, Ab, Abd, Y, Ydot, rdot, u[t], ud[t] if t > 0 else None,
+                                                    Rs[t], Rds[t])
+            if ubd is None:
+                ubd = torch.zeros_like(ub)
             g_rad[t] = RAD._reverse(E, radial_w[t], Wt.spec[t], acts[t], H0s[t],
                                     Rbar.reshape(E, P * C), Rdbar.reshape(E, P * C))
-            ub = ops.scatter(plan, [(Rs[t], T1 + T4), (Rds[t], T2r)])
-            ubd = ops.scatter(plan, [(Rs[t], T2)]) if t > 0 else torch.zeros_like(ub)
             red.append(NG.MMT(h[t], ub, g_up[t], X1=hd[t], D1=ubd))
             red += [NG.MMT(h[t], Hb, g_sc[t][k], X1=hd[t], D1=Hbd, perm=perm, seg=seg[k:k + 2], rows0=N, rows1=N)
                     for k in range(n_el)]
@@ -635,12 +668,15 @@ class MACEStep:
             if t > 0:
                 probs += rev_problems(t, ubd, Hbd, hbd[t])
             NG.mm(probs)
-        NG.mmT(red)
+            # interaction t is done: its weight gradients, then its bucket may be reduced
+            NG.mmT(red)
+            red = []
+            ro = (gw1, gw2) if t == T - 1 else g_rol[t]
+            wmap.add_grads(wmap.interaction_pairs(t, g_up[t], g_sc[t], g_rad[t], g_lin[t], g_sym[t], g_prod[t], ro))
+            if bucket_hook is not None:
+                bucket_hook(T - 1 - t)
         g_emb = torch.zeros_like(emb).index_add_(0, z, hb[0])
-
-        # effective-matrix gradients back to the parameters
-        wmap.add_grads({"emb": g_emb, "up": g_up, "sc": g_sc, "radial": g_rad, "lin": g_lin, "sym": g_sym,
-                        "prod": g_prod, "ro_lin": g_rol, "w1": gw1, "w2": gw2})
+        wmap.add_grads([(wmap.emb, g_emb)])
         ar = m.atom_ref.weight
         if ar.requires_grad and self.we > 0:
             gar = torch.zeros_like(ar).index_add_(0, Z, a_s.to(ar.dtype).index_select(0, b.batch)[:, None])

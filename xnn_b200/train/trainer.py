@@ -104,7 +104,8 @@ class Trainer:
         backend = cfg.trainer.grad_sync
         if backend == "auto":
             backend = "nccl"
-        self.grad_sync = GradSync(self.params, backend=backend if self.world > 1 else "none")
+        self._grad_backend = backend if self.world > 1 else "none"
+        self.grad_sync = GradSync(self.params, backend=self._grad_backend)
         # same starting weights on every rank
         if self.world > 1:
             with torch.no_grad():
@@ -140,6 +141,10 @@ class Trainer:
             ok, why = mace_step.supports(self.module, o)
             if ok:
                 self._fused = mace_step.MACEStep(self.module, o.energy_weight, o.force_weight)
+                # the flat gradient buffer in the step's bucket order (interaction by interaction)
+                self.grad_sync.close()
+                self.grad_sync = GradSync(self.params, backend=self._grad_backend,
+                                          buckets=self._fused.bucket_params())
             elif fs is True:
                 raise ValueError(f"trainer.fused_step: {why}")
         self.train_set, self.val_set, self.test_set = self._splits(train, val, test)
@@ -234,7 +239,7 @@ class Trainer:
     def _train_step_impl(self, batch: AtomicGraph):
         self.grad_sync.zero_()
         if self._fused is not None:
-            loss, logs, _ = self._fused(batch)
+            loss, logs, _ = self._fused(batch, bucket_hook=self.grad_sync.bucket_ready)
         else:
             loss, logs, _ = self._loss(batch)
             with params_only():
