@@ -30,15 +30,6 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
 
-# name fragments of the kernels compiled into xnn_b200/_C.so
-OUR_KERNELS = ("conv_gather", "conv_edge", "conv_scatter", "symcon_", "edge_geom_", "p2p_allreduce", "halo_exchange",
-               "gemm_pack_kernel", "gemm_rows_kernel", "gemm_reduce_kernel", "gemm_ws_kernel", "gemm_ws_pack_kernel",
-               "gemm_reduce_ws_kernel", "sum_partials_kernel", "radial_basis_kernel", "radial_act_kernel",
-               "radial_dact_kernel", "nb_count", "nb_write", "mp_real_kernel", "pme_spread_kernel",
-               "pme_gather_kernel", "node_mm_kernel", "node_mmT_kernel", "node_sum_kernel", "node_pack",
-               "species_sort_kernel")
-
-
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -48,7 +39,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=64, help="structures per GPU per step")
     ap.add_argument("--pool", type=int, default=8, help="distinct batches per rank, cycled")
     ap.add_argument("--no-graph", action="store_true", help="eager steps instead of one CUDA graph")
-    ap.add_argument("--grad-sync", default="nccl", choices=["nccl", "p2p"])
+    ap.add_argument("--grad-sync", default="p2p", choices=["nccl", "p2p"])
     ap.add_argument("--dtype", default="float32")
     ap.add_argument("--md-atoms", type=int, default=1_000_000, help="atoms of the MD water box (0: skip MD)")
     ap.add_argument("--md-steps", type=int, default=10)
@@ -58,6 +49,11 @@ def parse():
     ap.add_argument("--pme-atoms", type=int, default=100_000, help="atoms of the config-5 water box (0: skip)")
     ap.add_argument("--pme-steps", type=int, default=3)
     ap.add_argument("--pme-exchange", default="collective", choices=["collective", "p2p"])
+    ap.add_argument("--tn-batch", type=int, default=32, help="config-3 crystals per GPU per step (0: skip)")
+    ap.add_argument("--tn-steps", type=int, default=10)
+    ap.add_argument("--tn-pool", type=int, default=4)
+    ap.add_argument("--solve-atoms", type=int, default=100_000,
+                    help="atoms of the config-5 induction-solve comparison on one GPU (0: skip)")
     return ap.parse_args()
 
 
@@ -107,6 +103,163 @@ def pme_measure(args, dev, world, rank):
                        "box": "water density (0.1 atoms/A^3): 100.4 A for 100,000 atoms"},
             "e2e": {"value": round(1e3 / wall_ms, 3), "unit": "evaluations/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 8}}
+
+
+def _device_time(step, batches, warmup, steps, world):
+    """Mean device time of ``steps`` calls of ``step`` (CUDA events on the launching stream, after
+    ``warmup`` untimed calls, barrier + synchronize on both sides, max over ranks), in ms."""
+    import torch
+    import torch.distributed as dist
+    for i in range(max(3, warmup)):
+        step(batches[i % len(batches)])
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(steps):
+        step(batches[i % len(batches)])
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / steps], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t[0])
+
+
+TN_CONFIG = {"model": {"name": "tensornet", "cutoff": 5.0, "n_features": 64, "n_interactions": 2, "n_rbf": 32,
+                       "extra": {"n_elements": 90}},
+             "optim": {"lr": 1e-3, "energy_weight": 1.0, "force_weight": 10.0, "stress_weight": 1.0, "epochs": 1,
+                       "scheduler": "none"},
+             "data": {"val_fraction": 0.0, "test_fraction": 0.0},
+             "device": "cuda", "seed": 1234}
+
+
+def tensornet_measure(args, impl, world, rank):
+    """Config 3: TensorNet (MatPES-shaped: 2 layers, 64 channels, 32 RBF, 5 A, 89 elements) training on
+    32 periodic triclinic crystals of 8-200 atoms per GPU, energy + force + stress loss, through the
+    trainer of the package named by ``impl`` (each arm its own stock training step)."""
+    import copy
+
+    import torch
+
+    from xnn_b200.data import synthetic          # structure generator only (plain numpy / torch)
+    B = args.tn_batch
+    structs = synthetic.triclinic_crystals(B * args.tn_pool, seed=3000 + rank)
+    cfgd = copy.deepcopy(TN_CONFIG)
+    cfgd["data"]["batch_size"] = B
+    cfgd["output_dir"] = tempfile.mkdtemp(prefix="xnn_b200_bench_tn_")
+    if impl == "reference":
+        from xnn.common.config.loaders import from_dict as ref_from_dict
+        from xnn.common.data.dataset import AtomicDataset as RefDataset
+        from xnn.common.data.dataset import collate as ref_collate
+        from xnn.common.train.trainer import Trainer as RefTrainer
+        ds = RefDataset(structs, 5.0)
+        trainer = RefTrainer(ref_from_dict(cfgd), ds)
+        batches = [ref_collate([ds[k] for k in range(j * B, (j + 1) * B)]).to(trainer.device)
+                   for j in range(args.tn_pool)]
+
+        def step(b):
+            trainer._step(b, True)            # the reference's training step (fit() runs it per batch)
+    else:
+        from xnn_b200.config import from_dict
+        from xnn_b200.data import AtomicDataset, collate
+        from xnn_b200.train import Trainer
+        cfgd["trainer"] = {"loggers": [], "grad_sync": args.grad_sync, "cuda_graph": False}
+        ds = AtomicDataset(structs, 5.0, precompute=True)
+        trainer = Trainer(from_dict(cfgd), ds, val=[], test=[])
+        batches = [collate([ds[k] for k in range(j * B, (j + 1) * B)]).to(trainer.device)
+                   for j in range(args.tn_pool)]
+
+        def step(b):
+            trainer.train_step(b)
+    ms = _device_time(step, batches, args.warmup, args.tn_steps, world)
+    n_atoms = sum(int(b.num_nodes) for b in batches) / len(batches)
+    out = {"metric": "TensorNet train structures/s", "value": round(world * B / (ms / 1e3), 2),
+           "unit": "structures/s", "ms_per_step": round(ms, 3), "steps": args.tn_steps, "warmup": max(3, args.warmup),
+           "config": {"model": "TensorNet MatPES-shaped: 2 layers, 64 ch, 32 RBF, 5.0 A, 89 elements",
+                      "global_batch": world * B, "avg_atoms_per_batch": round(n_atoms, 1),
+                      "loss": "energy 1 + forces 10 + stress 1", "dtype": "fp32",
+                      "data": "synthetic triclinic crystals 8-200 atoms, Morse labels with virial stress"}}
+    if hasattr(trainer, "close"):
+        trainer.close()
+    return out
+
+
+def solve_measure(args, impl):
+    """Config 5's hot loop on one GPU: the induced dipoles of the 100,000-atom water box,
+    ``(1/alpha - T) mu = F`` solved by preconditioned CG to 1e-5 D, ``T`` the Ewald dipole field
+    (real space within 7 A, Thole-damped, a = 0.39, pairs of one molecule excluded; PME 128^3,
+    order 5, alpha 0.4; self term). The right-hand side ``F`` is a seeded random field, identical
+    for both arms. Timed: pair search, operator setup and the whole solve, each arm on its own
+    code (the reference: ``unique_pairs``, the Ewald and Thole ladders, ``MeshPlan`` and ``_pcg``)."""
+    import torch
+
+    from xnn_b200.ffnn.water import multipole_water    # the box: positions, molecules, polarizabilities
+    dev = torch.device("cuda", torch.cuda.current_device())
+    w = multipole_water(args.solve_atoms, seed=0, device=dev)
+    pos, cell, pol, mol = w["pos"], w["cell"], w["pol"], w["molecule"]
+    n = pos.shape[0]
+    g = torch.Generator(device="cpu").manual_seed(5)
+    F = (0.05 * torch.randn(n, 3, generator=g, dtype=torch.float64)).to(dev)
+    alpha, thole, cutoff, tol = 0.4, 0.39, 7.0, 1e-5
+    if impl == "reference":
+        from xnn.common.data.neighborlist import unique_pairs
+        from xnn.ffnn.models.amoeba import _pcg, coulomb_ladder, mutual_field_real, thole_ladder
+        from xnn.ffnn.models.amoeba_ewald import MeshPlan, ewald_ladder, self_field_coefficient
+        pbc = torch.ones(3, dtype=torch.bool, device=dev)
+
+        def run():
+            i, k, sh = unique_pairs(pos, cutoff, cell, pbc)
+            r = pos[k] - pos[i] + sh.to(pos.dtype) @ cell
+            R = r.norm(dim=-1)
+            De = ewald_ladder(R, torch.full_like(R, alpha), 2)
+            th = torch.full_like(R, thole)
+            Dt = thole_ladder(R, pol[i], pol[k], th, th, 2)
+            Dc = coulomb_ladder(R, 2)
+            same = mol[i] == mol[k]
+            D1 = De[1] + torch.where(same, -Dc[1], Dt[1] - Dc[1])
+            D2 = De[2] + torch.where(same, -Dc[2], Dt[2] - Dc[2])
+            ik, ki = torch.cat([i, k]), torch.cat([k, i])
+            plan = MeshPlan(pos, cell[None], torch.zeros(n, dtype=torch.long, device=dev), [128] * 3, 5)
+            coef = float(self_field_coefficient(alpha))
+
+            def field_of(v, guard=None):
+                _, dphi, _ = plan.potential(None, v, None, alpha, hessian=False)
+                return mutual_field_real(v, r, D1, D2, ik, ki, n) - dphi + coef * v
+
+            mu, iters = _pcg(F, pol, field_of, torch.ones(n, dtype=torch.bool, device=dev), tol, 100)[:2]
+            return mu, iters
+    else:
+        from xnn_b200.ffnn import multipoles as MP
+        setup = MP.EwaldSetup(alpha=alpha, cutoff=cutoff, mesh=(128, 128, 128), order=5, fft_dtype=torch.float32)
+        mod = MP.PolarizableMultipoles(setup, tol_debye=tol, max_iter=100, thole=thole)
+
+        def run():
+            pairs = mod.pairs(pos, cell, mol)
+            mu, iters, _ = mod.solve(pos, cell, pairs, F, pol)
+            return mu, iters
+    with torch.no_grad():
+        mu, iters = run()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        steps = 3
+        for _ in range(steps):
+            mu, iters = run()
+        b.record()
+        torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    return {"metric": "induced-dipole solves/s (100k-atom water box, PME 128^3)", "value": round(1e3 / ms, 3),
+            "unit": "solves/s", "ms_per_solve": round(ms, 2), "iterations": int(iters), "steps": steps, "warmup": 1,
+            "mu_rms_debye": float((mu * mu).sum(-1).mean().sqrt()) * 4.80320427,
+            "config": {"atoms": n, "mesh": [128, 128, 128], "order": 5, "alpha": alpha, "cutoff_A": cutoff,
+                       "thole": thole, "tol_debye": tol,
+                       "precision": "fp64 real space, fp32 FFT" if impl != "reference" else
+                       "fp64 throughout (the reference mesh follows the positions' dtype)",
+                       "convergence": "rms preconditioned residual" if impl != "reference" else
+                       "rms dipole change per iteration"}}
 
 
 def md_measure(args, dev, world, rank):
@@ -220,13 +373,22 @@ class ClockSampler:
 
 
 def reference_arm(args):
-    """Run the unmodified reference through its own API, or say why it cannot run."""
+    """Run the unmodified reference through its own API, or say why it cannot.
+
+    The headline model (MACE) needs ``e3nn``, which is absent offline, so the headline arm prints
+    ``unavailable``; the same line carries the configs the reference can run on this box: TensorNet
+    training (config 3) and the induced-dipole solve of config 5 (one GPU: the reference PME has no
+    multi-GPU path)."""
     ref = os.path.join(ROOT, "baseline", "_ref")
     reason = None
+    extra = {}
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if not os.path.isdir(os.path.join(ref, "xnn")):
         reason = "reference not installed under baseline/_ref"
     else:
         sys.path.insert(0, ref)
+        sys.path.insert(1, ROOT)
         try:
             import xnn.gnn.models.mace  # noqa: F401
         except ModuleNotFoundError as exc:
@@ -234,11 +396,30 @@ def reference_arm(args):
                       "offline wheelhouse (no network); the reference cannot build the benchmarked model")
         except Exception as exc:  # pragma: no cover
             reason = f"reference import failed: {exc!r}"
+        import torch
+        if torch.cuda.is_available():
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+            if args.tn_batch > 0:
+                try:
+                    extra["tensornet"] = tensornet_measure(args, "reference", world, rank)
+                except Exception as exc:  # pragma: no cover
+                    extra["tensornet"] = {"unavailable": f"reference TensorNet run failed: {exc!r}"[:300]}
+            if args.solve_atoms > 0:
+                if world == 1:
+                    try:
+                        extra["solve"] = solve_measure(args, "reference")
+                    except Exception as exc:  # pragma: no cover
+                        extra["solve"] = {"unavailable": f"reference solve failed: {exc!r}"[:300]}
+                else:
+                    extra["solve"] = {"unavailable": "the reference PME runs on one GPU only"}
     if reason is None:
         reason = "reference MACE importable but its arm is not wired"
-    rank = int(os.environ.get("RANK", "0"))
     if rank == 0:
-        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+        print(json.dumps({"impl": "reference", "unavailable": reason, **extra}), flush=True)
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():
@@ -315,7 +496,8 @@ def main():
             torch.cuda.synchronize(dev)
         trainer.use_graphs = saved
         names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
-        ours = [n for n in names if any(k in n for k in OUR_KERNELS)]
+        from xnn_b200.utils.profiling import is_own_kernel
+        ours = [n for n in names if is_own_kernel(n)]
         launches = len(ours)
         all_kernels = len(names)
     except Exception as exc:  # pragma: no cover
@@ -373,6 +555,14 @@ def main():
         with ClockSampler(torch.cuda.current_device()) as pme_clocks:
             pme = pme_measure(args, dev, world, rank)
         pme["clocks"] = pme_clocks.summary()
+    tn = None
+    if args.tn_batch > 0:
+        torch.cuda.empty_cache()
+        tn = tensornet_measure(args, "xnn_b200", world, rank)
+    solve = None
+    if args.solve_atoms > 0 and world == 1:
+        torch.cuda.empty_cache()
+        solve = solve_measure(args, "xnn_b200")
     if rank == 0:
         line = {
             "metric": "MACE train structures/s", "value": round(value, 2), "unit": "structures/s",
@@ -396,6 +586,8 @@ def main():
             "loss_finite": finite,
             "md": md,
             "pme": pme,
+            "tensornet": tn,
+            "solve": solve,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

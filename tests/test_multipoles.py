@@ -144,3 +144,59 @@ def test_slab_decomposed_mesh_matches_single_process(world):
         torch.testing.assert_close(o["energy"], ref["energy"], rtol=1e-9, atol=1e-9)
         torch.testing.assert_close(o["forces"], ref["forces"], rtol=1e-7, atol=1e-8)
         torch.testing.assert_close(o["mu"], ref["induced_dipoles"], rtol=1e-7, atol=1e-9)
+
+
+@pytest.mark.parametrize("damped", [True, False])
+def test_dipole_operator_matches_energy_gradient(damped):
+    """The direct dipole operator of the induction solve against ``-dE/d(mu)`` of the energy
+    with dipoles only (Thole-damped and undamped)."""
+    pos, cell, q, d, Q = _system(n=21, seed=4)
+    mol = torch.arange(21) // 3
+    pol = 0.6 + 0.6 * torch.rand(21, generator=torch.Generator().manual_seed(5))
+    mod = M.PolarizableMultipoles(M.EwaldSetup(alpha=0.45, cutoff=5.0, mesh=(24, 24, 24), order=5,
+                                               fft_dtype=torch.float64))
+    pairs = mod.pairs(pos, cell, mol)
+    damp = pol if damped else None
+    v = 0.2 * torch.randn(21, 3, generator=torch.Generator().manual_seed(6))
+    ref = mod.dipole_field(pos, cell, pairs, v, pol=damp) / M.KE      # eV / (e A) -> Coulomb units
+    got = M.DipoleOperator(mod, pos, cell, pairs, damp)(v)
+    torch.testing.assert_close(got, ref, rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.gpu
+def test_dipole_operator_kernels_match_cpu():
+    pos, cell, q, d, Q = _system(n=300, L=20.0, seed=7)
+    mol = torch.arange(300) // 3
+    pol = 0.6 + 0.6 * torch.rand(300, generator=torch.Generator().manual_seed(8))
+    v = 0.2 * torch.randn(300, 3, generator=torch.Generator().manual_seed(9))
+    setup = M.EwaldSetup(alpha=0.4, cutoff=7.0, mesh=(32, 32, 32), order=5, fft_dtype=torch.float64)
+    mod = M.PolarizableMultipoles(setup)
+    pairs = mod.pairs(pos, cell, mol)
+    ref = M.DipoleOperator(mod, pos, cell, pairs, pol)(v)
+    dev = torch.device("cuda")
+    modg = M.PolarizableMultipoles(setup)
+    pg = tuple(t.to(dev) for t in pairs)
+    op = M.DipoleOperator(modg, pos.to(dev), cell.to(dev), pg, pol.to(dev))
+    assert op.kernel, "the dipole pair kernels did not load"
+    got = op(v.to(dev)).cpu()
+    torch.testing.assert_close(got, ref, rtol=1e-9, atol=1e-11)
+
+
+@pytest.mark.gpu
+def test_direct_reciprocal_field_matches_energy_gradient():
+    """The reciprocal dipole field by spread / FFT / gather (no graph) against the gradient of the
+    reciprocal energy on the same float32 mesh."""
+    dev = torch.device("cuda")
+    pos, cell, q, d, Q = _system(n=500, L=22.0, seed=11)
+    pos, cell = pos.to(dev), cell.to(dev)
+    v = (0.2 * torch.randn(500, 3, generator=torch.Generator().manual_seed(12), dtype=torch.float64)).to(dev)
+    mod = M.PolarizableMultipoles(M.EwaldSetup(alpha=0.4, cutoff=7.0, mesh=(40, 40, 40), order=5,
+                                               fft_dtype=torch.float32))
+    pairs = mod.pairs(pos, cell, None)
+    op = M.DipoleOperator(mod, pos, cell, pairs, None)
+    assert op._direct_setup()
+    got = op.recip(v)
+    vv = v.clone().requires_grad_(True)
+    e = mod.recip(pos, cell, v.new_zeros(500), vv, v.new_zeros(500, 3, 3))
+    (g,) = torch.autograd.grad(e, vv)
+    torch.testing.assert_close(got, -g, rtol=1e-4, atol=1e-6 * float(g.abs().max()))

@@ -403,9 +403,11 @@ std::vector<torch::Tensor> symcon_bwd2_op(torch::Tensor A, torch::Tensor z, torc
 }  // namespace
 
 void register_comm(pybind11::module& m);
+void register_tensornet(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_comm(m);
+  register_tensornet(m);
   m.attr("HAS_CUDA") = true;
   m.def("neighbor_list", &neighbor_list, "cell-list neighbour search (CUDA or OpenMP)");
   m.def("edge_geometry_fwd", &edge_geometry_fwd);

@@ -16,6 +16,12 @@ cudaError_t pme_gather_launch(int64_t n, int p, const double* pos, const double*
                               int nz, const double* q, const double* d, const double* Q, const float* phi, double* gd,
                               double* gpos, cudaStream_t s);
 
+cudaError_t dipole_pairs(int64_t P, const double* pos, const double* cell, const int64_t* pi, const int64_t* pj,
+                         const int64_t* shift, const bool* excluded, const double* pol, double alpha, double thole,
+                         double* v, double* b1, double* b2, cudaStream_t s);
+cudaError_t dipole_matvec(int64_t P, const int64_t* pi, const int64_t* pj, const double* v, const double* b1,
+                          const double* b2, const double* d, double* field, cudaStream_t s);
+
 namespace {
 
 void need(const torch::Tensor& t, torch::ScalarType st, const char* name) {
@@ -87,10 +93,53 @@ std::vector<torch::Tensor> pme_gather_op(torch::Tensor pos, torch::Tensor G, std
   return {gd, gp};
 }
 
+// (v (P, 3), B1 (P,), B2 (P,)) of the real-space dipole-dipole operator; thole <= 0: undamped
+std::vector<torch::Tensor> dipole_pairs_op(torch::Tensor pos, torch::Tensor cell, torch::Tensor I, torch::Tensor J,
+                                           torch::Tensor S, torch::Tensor excl, torch::Tensor pol, double alpha,
+                                           double thole) {
+  need(pos, torch::kFloat64, "pos");
+  need(cell, torch::kFloat64, "cell");
+  need(I, torch::kInt64, "I");
+  need(J, torch::kInt64, "J");
+  need(S, torch::kInt64, "S");
+  need(excl, torch::kBool, "excluded");
+  need(pol, torch::kFloat64, "pol");
+  c10::cuda::CUDAGuard g(pos.device());
+  const int64_t P = I.numel();
+  auto v = torch::empty({P, 3}, pos.options());
+  auto b1 = torch::empty({P}, pos.options());
+  auto b2 = torch::empty({P}, pos.options());
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaError_t e = dipole_pairs(P, pos.data_ptr<double>(), cell.data_ptr<double>(), I.data_ptr<int64_t>(),
+                               J.data_ptr<int64_t>(), S.data_ptr<int64_t>(), excl.data_ptr<bool>(),
+                               pol.data_ptr<double>(), alpha, thole, v.data_ptr<double>(), b1.data_ptr<double>(),
+                               b2.data_ptr<double>(), st);
+  TORCH_CHECK(e == cudaSuccess, "dipole_pairs: ", cudaGetErrorString(e));
+  return {v, b1, b2};
+}
+
+// field (n, 3) of the dipoles d through the precomputed pair operator
+torch::Tensor dipole_matvec_op(torch::Tensor I, torch::Tensor J, torch::Tensor v, torch::Tensor b1, torch::Tensor b2,
+                               torch::Tensor d) {
+  need(d, torch::kFloat64, "d");
+  need(v, torch::kFloat64, "v");
+  c10::cuda::CUDAGuard g(d.device());
+  auto field = torch::zeros_like(d);
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaError_t e = dipole_matvec(I.numel(), I.data_ptr<int64_t>(), J.data_ptr<int64_t>(), v.data_ptr<double>(),
+                                b1.data_ptr<double>(), b2.data_ptr<double>(), d.data_ptr<double>(),
+                                field.data_ptr<double>(), st);
+  TORCH_CHECK(e == cudaSuccess, "dipole_matvec: ", cudaGetErrorString(e));
+  return field;
+}
+
 }  // namespace
+
 
 void register_ffnn(pybind11::module& m) {
   m.def("mp_real", &mp_real_op);
+  m.def("dipole_pairs", &dipole_pairs_op);
+  m.def("dipole_matvec", &dipole_matvec_op);
   m.def("pme_spread", &pme_spread_op);
   m.def("pme_gather", &pme_gather_op);
 }

@@ -59,6 +59,9 @@ struct PackJob {
   int64_t sk, sn;
   int K, N;
   float* out;
+  const float* W2;
+  int64_t sk2, sn2;
+  int K1;
 };
 struct PackArgs {
   PackJob j[48];
@@ -75,6 +78,13 @@ cudaError_t mace_dual_reverse(int N, int C, int P, int64_t E, const int64_t* dst
                               const int64_t* src_ptr, const int64_t* src_perm, const T* G, const T* Gd, const T* Y,
                               const T* Yd, const T* rdot, const T* u, const T* ud, const T* R, const T* Rd, T* Rbar,
                               T* Rdbar, T* T14, T* T2, T* ub, T* ubd, cudaStream_t s);
+
+template <typename T, typename TO>
+cudaError_t edge_forces(int N, const int64_t* dst_ptr, const int64_t* dst_perm, const int64_t* src_ptr,
+                        const int64_t* src_perm, const T* v, TO* F, cudaStream_t s);
+template <typename T>
+cudaError_t segment_rows_sum(int groups, int cols, const int* perm, const int* seg, const T* X, T* out,
+                             cudaStream_t s);
 
 namespace {
 
@@ -235,9 +245,12 @@ void node_mmT(std::vector<torch::Tensor> X0, std::vector<torch::Tensor> D0,
 }
 
 // Packs every W (K x N, any strides) into its operand layout; returns the packed tensors.
-std::vector<torch::Tensor> node_pack(std::vector<torch::Tensor> Ws) {
+// Packed tf32 hi/lo operand copies of the matrices Ws[i], each stacked above Ws2[i] when that is
+// given (same column count): one launch, any strides.
+std::vector<torch::Tensor> node_pack(std::vector<torch::Tensor> Ws, std::vector<c10::optional<torch::Tensor>> Ws2) {
   const size_t n = Ws.size();
   TORCH_CHECK(n >= 1 && n <= 48, "node_pack: 1..48 matrices");
+  TORCH_CHECK(Ws2.empty() || Ws2.size() == n, "node_pack: Ws2 empty or one entry per matrix");
   c10::cuda::CUDAGuard guard(Ws[0].device());
   PackArgs a;
   a.n = (int)n;
@@ -245,10 +258,23 @@ std::vector<torch::Tensor> node_pack(std::vector<torch::Tensor> Ws) {
   for (size_t i = 0; i < n; ++i) {
     const auto& W = Ws[i];
     TORCH_CHECK(W.is_cuda() && W.scalar_type() == torch::kFloat32 && W.dim() == 2, "node_pack: float32 CUDA matrix");
-    const int K = (int)W.size(0), N = (int)W.size(1);
+    const int K1 = (int)W.size(0), N = (int)W.size(1);
+    const bool two = !Ws2.empty() && Ws2[i].has_value() && Ws2[i]->defined();
+    int K = K1;
+    const float* w2 = nullptr;
+    int64_t sk2 = 0, sn2 = 0;
+    if (two) {
+      const auto& B = *Ws2[i];
+      TORCH_CHECK(B.is_cuda() && B.scalar_type() == torch::kFloat32 && B.dim() == 2 && B.size(1) == N,
+                  "node_pack: the stacked matrix must be float32 CUDA with the same columns");
+      K += (int)B.size(0);
+      w2 = B.data_ptr<float>();
+      sk2 = B.stride(0);
+      sn2 = B.stride(1);
+    }
     TORCH_CHECK(N % 16 == 0 && K % 4 == 0, "node_pack: K a multiple of 4, N of 16");
     auto o = torch::empty({(int64_t)node_pack_floats(K, N)}, W.options());
-    a.j[i] = PackJob{W.data_ptr<float>(), W.stride(0), W.stride(1), K, N, o.data_ptr<float>()};
+    a.j[i] = PackJob{W.data_ptr<float>(), W.stride(0), W.stride(1), K, N, o.data_ptr<float>(), w2, sk2, sn2, K1};
     out.push_back(o);
   }
   auto st = at::cuda::getCurrentCUDAStream();
@@ -314,7 +340,61 @@ std::vector<torch::Tensor> mace_dual_reverse_op(torch::Tensor dst_ptr, torch::Te
 
 }  // namespace
 
+// F (N, 3) in out_dtype: F_i = sum over edges leaving i of v - sum over edges entering i of v
+torch::Tensor edge_forces_op(torch::Tensor dst_ptr, c10::optional<torch::Tensor> dst_perm, torch::Tensor src_ptr,
+                             torch::Tensor src_perm, torch::Tensor v, torch::ScalarType out_dtype) {
+  TORCH_CHECK(v.is_cuda() && v.is_contiguous() && v.dim() == 2 && v.size(1) == 3, "edge_forces: v (E, 3) CUDA");
+  for (const auto* t : {&dst_ptr, &src_ptr, &src_perm})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt64 && t->is_contiguous(), "edge_forces: int64 plan");
+  const bool perm = dst_perm.has_value() && dst_perm->defined();
+  c10::cuda::CUDAGuard guard(v.device());
+  const int N = (int)dst_ptr.numel() - 1;
+  auto F = torch::empty({N, 3}, v.options().dtype(out_dtype));
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int64_t* dp = perm ? dst_perm->data_ptr<int64_t>() : nullptr;
+  cudaError_t e;
+  if (v.scalar_type() == torch::kFloat32 && out_dtype == torch::kFloat64)
+    e = edge_forces<float, double>(N, dst_ptr.data_ptr<int64_t>(), dp, src_ptr.data_ptr<int64_t>(),
+                                   src_perm.data_ptr<int64_t>(), v.data_ptr<float>(), F.data_ptr<double>(), st);
+  else if (v.scalar_type() == torch::kFloat32 && out_dtype == torch::kFloat32)
+    e = edge_forces<float, float>(N, dst_ptr.data_ptr<int64_t>(), dp, src_ptr.data_ptr<int64_t>(),
+                                  src_perm.data_ptr<int64_t>(), v.data_ptr<float>(), F.data_ptr<float>(), st);
+  else {
+    TORCH_CHECK(v.scalar_type() == torch::kFloat64 && out_dtype == torch::kFloat64, "edge_forces: dtypes");
+    e = edge_forces<double, double>(N, dst_ptr.data_ptr<int64_t>(), dp, src_ptr.data_ptr<int64_t>(),
+                                    src_perm.data_ptr<int64_t>(), v.data_ptr<double>(), F.data_ptr<double>(), st);
+  }
+  TORCH_CHECK(e == cudaSuccess, "edge_forces: ", cudaGetErrorString(e));
+  return F;
+}
+
+// out (groups, ...) = per-group sums of the rows of X (N, ...) through (perm, seg) of species_sort
+torch::Tensor segment_rows_sum_op(torch::Tensor X, torch::Tensor perm, torch::Tensor seg) {
+  TORCH_CHECK(X.is_cuda() && X.is_contiguous() && X.dim() >= 1, "segment_rows_sum: contiguous CUDA X");
+  TORCH_CHECK(perm.scalar_type() == torch::kInt32 && seg.scalar_type() == torch::kInt32, "segment_rows_sum: int32");
+  c10::cuda::CUDAGuard guard(X.device());
+  const int groups = (int)seg.numel() - 1;
+  auto shape = X.sizes().vec();
+  shape[0] = groups;
+  auto out = torch::empty(shape, X.options());
+  const int cols = (int)(X.numel() / std::max<int64_t>(1, X.size(0)));
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaError_t e;
+  if (X.scalar_type() == torch::kFloat64)
+    e = segment_rows_sum<double>(groups, cols, perm.data_ptr<int>(), seg.data_ptr<int>(), X.data_ptr<double>(),
+                                 out.data_ptr<double>(), st);
+  else {
+    TORCH_CHECK(X.scalar_type() == torch::kFloat32, "segment_rows_sum: float32 or float64");
+    e = segment_rows_sum<float>(groups, cols, perm.data_ptr<int>(), seg.data_ptr<int>(), X.data_ptr<float>(),
+                                out.data_ptr<float>(), st);
+  }
+  TORCH_CHECK(e == cudaSuccess, "segment_rows_sum: ", cudaGetErrorString(e));
+  return out;
+}
+
 void register_node(pybind11::module& m) {
+  m.def("edge_forces", &edge_forces_op);
+  m.def("segment_rows_sum", &segment_rows_sum_op);
   m.def("mace_dual_reverse", &mace_dual_reverse_op);
   m.def("node_mm", &node_mm);
   m.def("node_mmT", &node_mmT);

@@ -182,6 +182,68 @@ cudaError_t mace_dual_reverse(int N, int C, int P, int64_t E, const int64_t* dst
   }
 }
 
+// ------------------------------------------------------------------------------------ node sums
+// Forces from per-edge vectors v_e = dE/d(r_dst - r_src):  F_i = sum_{e: src=i} v_e - sum_{e: dst=i} v_e,
+// one thread per atom through both CSR orderings (fixed order, no atomics), accumulated in TO.
+template <typename T, typename TO>
+__global__ void edge_forces_kernel(int N, const int64_t* __restrict__ dst_ptr, const int64_t* __restrict__ dst_perm,
+                                   const int64_t* __restrict__ src_ptr, const int64_t* __restrict__ src_perm,
+                                   const T* __restrict__ v, TO* __restrict__ F) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  TO f[3] = {TO(0), TO(0), TO(0)};
+  for (int64_t j = src_ptr[i]; j < src_ptr[i + 1]; ++j) {
+    const int64_t e = src_perm[j];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) f[c] += (TO)v[3 * e + c];
+  }
+  for (int64_t j = dst_ptr[i]; j < dst_ptr[i + 1]; ++j) {
+    const int64_t e = dst_perm ? dst_perm[j] : j;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) f[c] -= (TO)v[3 * e + c];
+  }
+#pragma unroll
+  for (int c = 0; c < 3; ++c) F[3 * i + c] = f[c];
+}
+
+// Per-group row sums: out[k, :] = sum_{r in seg[k] .. seg[k+1]} X[perm[r], :] (atoms grouped by
+// element: the gradients of per-element tables). Block (k, column tile of 256), rows in order.
+template <typename T>
+__global__ void segment_rows_sum_kernel(int cols, const int* __restrict__ perm, const int* __restrict__ seg,
+                                        const T* __restrict__ X, T* __restrict__ out) {
+  const int k = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= cols) return;
+  T acc = T(0);
+  for (int r = seg[k]; r < seg[k + 1]; ++r) acc += X[(int64_t)perm[r] * cols + c];
+  out[(int64_t)k * cols + c] = acc;
+}
+
+template <typename T, typename TO>
+cudaError_t edge_forces(int N, const int64_t* dst_ptr, const int64_t* dst_perm, const int64_t* src_ptr,
+                        const int64_t* src_perm, const T* v, TO* F, cudaStream_t s) {
+  if (N == 0) return cudaSuccess;
+  edge_forces_kernel<T, TO><<<(N + 127) / 128, 128, 0, s>>>(N, dst_ptr, dst_perm, src_ptr, src_perm, v, F);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t segment_rows_sum(int groups, int cols, const int* perm, const int* seg, const T* X, T* out,
+                             cudaStream_t s) {
+  if (groups == 0 || cols == 0) return cudaSuccess;
+  segment_rows_sum_kernel<T><<<dim3((cols + 255) / 256, groups), 256, 0, s>>>(cols, perm, seg, X, out);
+  return cudaGetLastError();
+}
+
+template cudaError_t edge_forces<float, double>(int, const int64_t*, const int64_t*, const int64_t*, const int64_t*,
+                                                const float*, double*, cudaStream_t);
+template cudaError_t edge_forces<float, float>(int, const int64_t*, const int64_t*, const int64_t*, const int64_t*,
+                                               const float*, float*, cudaStream_t);
+template cudaError_t edge_forces<double, double>(int, const int64_t*, const int64_t*, const int64_t*,
+                                                 const int64_t*, const double*, double*, cudaStream_t);
+template cudaError_t segment_rows_sum<float>(int, int, const int*, const int*, const float*, float*, cudaStream_t);
+template cudaError_t segment_rows_sum<double>(int, int, const int*, const int*, const double*, double*, cudaStream_t);
+
 template cudaError_t mace_dual_reverse<float>(int, int, int, int64_t, const int64_t*, const int*, const int64_t*,
                                               const int64_t*, const float*, const float*, const float*, const float*,
                                               const float*, const float*, const float*, const float*, const float*,

@@ -87,10 +87,13 @@ struct NodeRedArgs {
 };
 
 struct PackJob {
-  const float* W;         // K x N with strides (sk, sn)
+  const float* W;         // rows 0 .. K1 - 1 of the K x N matrix, strides (sk, sn)
   int64_t sk, sn;
   int K, N;
   float* out;             // K blocks of NM_KB: [hi | lo], each N x kbp canonical
+  const float* W2;        // rows K1 .. K - 1 (a second matrix stacked below), strides (sk2, sn2)
+  int64_t sk2, sn2;
+  int K1;
 };
 
 struct PackArgs {
@@ -579,7 +582,7 @@ __global__ void node_pack_kernel(const __grid_constant__ PackArgs a) {
     const int kbw = min(NM_KB, J.K - kb * NM_KB);
     const int kbp = (kbw + 7) / 8 * 8;
     float hi, lo;
-    split_tf32(J.W[k * J.sk + n * J.sn], hi, lo);
+    split_tf32(k < J.K1 ? J.W[k * J.sk + n * J.sn] : J.W2[(k - J.K1) * J.sk2 + n * J.sn2], hi, lo);
     const uint32_t off = ((uint32_t)(n >> 3) * (uint32_t)(kbp / 4) * 128u + (uint32_t)(kl >> 2) * 128u +
                           (uint32_t)(n & 7) * 16u + (uint32_t)(kl & 3) * 4u) / 4u;
     J.out[base + off] = hi;

@@ -370,6 +370,110 @@ def multipole_pairs(pos: Tensor, cell: Tensor, cutoff: float, molecule: Optional
     return i.to(pos.device), j.to(pos.device), s.to(pos.device), excluded.to(pos.device)
 
 
+# ----------------------------------------------------------------------------- dipole operator
+class DipoleOperator:
+    """``T v``: the field (Coulomb units) that a set of dipoles ``v`` produces at every site, with
+    the induction's Thole damping (``pol`` given) -- the matrix of the induced-dipole solve,
+    applied without an energy graph.
+
+    * real space: per pair ``-[B_1 v_j - B_2 (v_j . r) r]`` (and symmetrically), ``B_1, B_2`` of the
+      screened (or, within a molecule, ``-erf``) kernel formed once (``csrc/pme_induce.cu``);
+    * reciprocal space: the dipoles spread on the mesh, the FFT convolution, and the gather of
+      ``-dE/dv`` (the spreading kernel's adjoint);
+    * self term: ``4 a^3 / (3 sqrt(pi)) v``.
+
+    With the work split over processes each returns its share, summed over the group."""
+
+    def __init__(self, mod: "PolarizableMultipoles", pos: Tensor, cell: Tensor, pairs, pol: Optional[Tensor]):
+        self.mod = mod
+        self.pos, self.cell = pos.detach(), cell.detach()
+        i, j, sh, ex = pairs
+        self.i, self.j = i, j
+        s = mod.setup
+        a = s.alpha
+        self.self_coef = 4.0 * a ** 3 / (3.0 * math.sqrt(math.pi)) if mod.rank == 0 else 0.0
+        self.kernel = pos.is_cuda and pos.dtype == torch.float64 and _kernel_ok()
+        th = mod.thole if pol is not None else None
+        pw = (pol if pol is not None else torch.ones(pos.shape[0], dtype=pos.dtype, device=pos.device)).detach()
+        if self.kernel:
+            from .. import _ext
+            self.v, self.b1, self.b2 = _ext.ops().dipole_pairs(
+                self.pos.contiguous(), self.cell.contiguous(), i.contiguous(), j.contiguous(), sh.contiguous(),
+                ex.contiguous(), pw.contiguous(), float(a), float(th) if th is not None else -1.0)
+        else:
+            v = self.pos[j] - self.pos[i] + _shift_vec(sh, self.cell)
+            r = torch.linalg.norm(v, dim=-1)
+            Bc = _bn(r, a, "erfc", 2)
+            b1, b2 = Bc[1], Bc[2]
+            if th is not None:
+                u = r / (pw[i] * pw[j]) ** (1.0 / 6.0)
+                au3 = th * u * u * u
+                e = torch.exp(-au3)
+                r3 = r * r * r
+                b1 = b1 - e / r3                               # (1 - lambda_3) / r^3
+                b2 = b2 - 3.0 * (1.0 + au3) * e / (r3 * r * r)  # 3 (1 - lambda_5) / r^5
+            Be = _bn(r, a, "neg_erf", 2)
+            self.v = v
+            self.b1 = torch.where(ex, Be[1], b1)
+            self.b2 = torch.where(ex, Be[2], b2)
+
+    def real(self, d: Tensor) -> Tensor:
+        if self.kernel:
+            from .. import _ext
+            return _ext.ops().dipole_matvec(self.i, self.j, self.v, self.b1, self.b2, d.contiguous())
+        v, b1, b2 = self.v, self.b1[:, None], self.b2[:, None]
+        dj, di = d[self.j], d[self.i]
+        fi = -(b1 * dj - b2 * (dj * v).sum(-1, keepdim=True) * v)
+        fj = -(b1 * di - b2 * (di * v).sum(-1, keepdim=True) * v)
+        return torch.zeros_like(d).index_add_(0, self.i, fi).index_add_(0, self.j, fj)
+
+    def _direct_setup(self) -> bool:
+        """The reciprocal field without an energy graph: one process, CUDA float64 sites and a
+        float32 mesh (the spreading and gather kernels)."""
+        s = self.mod.setup
+        ok = (self.kernel and self.mod.mesh_backend is None and s.fft_dtype == torch.float32 and s.order <= 8)
+        if ok and not hasattr(self, "_G"):
+            K = torch.tensor(s.mesh, dtype=torch.float64, device=self.pos.device)
+            self._G = (torch.linalg.inv(self.cell.double()) * K[None, :]).contiguous()
+            K3 = s.mesh[2]
+            w = torch.full((K3 // 2 + 1,), 2.0, dtype=torch.float32, device=self.pos.device)
+            w[0] = 1.0
+            if K3 % 2 == 0:
+                w[-1] = 1.0
+            # the influence function without the half-spectrum doubling (irfftn restores the
+            # conjugate half), times the mesh size (the unnormalised inverse transform)
+            self._infl = self.mod._influence(self.cell) / w * float(math.prod(s.mesh))
+        return ok
+
+    def recip(self, d: Tensor) -> Tensor:
+        if self._direct_setup():
+            # field = -dE/dd with E = 1/2 sum_m infl(m) |F(m)|^2: spread d, transform, weigh,
+            # transform back to the mesh potential dE/dgrid, gather its stencil derivatives
+            from .. import _ext
+            s = self.mod.setup
+            C = _ext.ops()
+            pos = self.pos.contiguous()
+            dd = d.contiguous()
+            K3 = s.mesh[2]
+            grid = C.pme_spread(pos, self._G, list(s.mesh), s.order, 0, K3, None, dd, None)
+            phi = torch.fft.irfftn(torch.fft.rfftn(grid) * self._infl, s=list(s.mesh))
+            gd, _ = C.pme_gather(pos, self._G, list(s.mesh), s.order, 0, K3, None, dd, None, phi.contiguous(),
+                                 True, False)
+            return -gd
+        n = d.shape[0]
+        dd = d.detach().clone().requires_grad_(True)
+        with torch.enable_grad():
+            e = self.mod.recip(self.pos, self.cell, d.new_zeros(n), dd, d.new_zeros(n, 3, 3))
+            (g,) = torch.autograd.grad(e, dd)
+        return -g
+
+    def __call__(self, d: Tensor) -> Tensor:
+        out = self.real(d) + self.recip(d)
+        if self.self_coef:
+            out = out + self.self_coef * d
+        return self.mod._sum(out)
+
+
 # ----------------------------------------------------------------------------- module
 @dataclass
 class EwaldSetup:
@@ -471,34 +575,51 @@ class PolarizableMultipoles(nn.Module):
             (g,) = torch.autograd.grad(e, vv)
         return -self._sum(g)
 
-    def induce(self, pos, cell, pairs, q, d, Q, pol, mu0: Optional[Tensor] = None):
-        """Induced dipoles by Jacobi-preconditioned CG on ``(alpha^-1 - T) mu = F_perm``."""
+    def induce(self, pos, cell, pairs, q, d, Q, pol, mu0: Optional[Tensor] = None, check_every: int = 4):
+        """Induced dipoles by Jacobi-preconditioned CG on ``(alpha^-1 - T) mu = F_perm``.
+
+        ``T`` is applied directly (:class:`DipoleOperator`): the real-space pair couplings are
+        formed once, the reciprocal part is one spread, FFT and gather of the dipoles. The
+        convergence test runs on the device every iteration -- a converged solve freezes (zero
+        steps), so the result is the one of stopping there -- and is read back every
+        ``check_every`` iterations only."""
         damp = pol if self.thole is not None else None
         F = self.field(pos, cell, pairs, q, d, Q, pol=damp) / KE        # fields in e / A^2 (Coulomb units)
+        return self.solve(pos, cell, pairs, F, pol, mu0, check_every)
+
+    def solve(self, pos, cell, pairs, F, pol, mu0: Optional[Tensor] = None, check_every: int = 4):
+        """The CG iterations of :meth:`induce` for a given permanent field ``F`` (Coulomb units)."""
+        damp = pol if self.thole is not None else None
         inv_a = 1.0 / pol[:, None]
+        T = DipoleOperator(self, pos, cell, pairs, damp)
 
         def A(v):
-            return inv_a * v - self.dipole_field(pos, cell, pairs, v, pol=damp) / KE
+            return inv_a * v - T(v)
 
         mu = pol[:, None] * F if mu0 is None else mu0.detach().clone()
         r = F - A(mu)
         z = pol[:, None] * r
         p_ = z.clone()
         rz = (r * z).sum()
+        done = torch.zeros((), dtype=torch.bool, device=pos.device)
+        iters = torch.zeros((), dtype=torch.long, device=pos.device)
+        err = torch.sqrt(((pol[:, None] * r) ** 2).sum(-1).mean())
         it = 0
         for it in range(1, self.max_iter + 1):
             Ap = A(p_)
-            step = rz / (p_ * Ap).sum()
+            step = torch.where(done, torch.zeros_like(rz), rz / (p_ * Ap).sum())
             mu = mu + step * p_
             r = r - step * Ap
             z = pol[:, None] * r
-            err = torch.sqrt(((pol[:, None] * r) ** 2).sum(-1).mean())
-            if float(err) < self.tol:
-                break
+            err = torch.where(done, err, torch.sqrt(((pol[:, None] * r) ** 2).sum(-1).mean()))
+            iters = torch.where(done, iters, torch.full_like(iters, it))
+            done = done | (err < self.tol)
             rz_new = (r * z).sum()
-            p_ = z + (rz_new / rz) * p_
-            rz = rz_new
-        return mu.detach(), it, float(err)
+            p_ = torch.where(done, p_, z + (rz_new / rz) * p_)
+            rz = torch.where(done, rz, rz_new)
+            if it % check_every == 0 and bool(done):
+                break
+        return mu.detach(), int(iters), float(err)
 
     def forward(self, pos: Tensor, cell: Tensor, q: Tensor, d: Tensor, Q: Tensor, pol: Tensor,
                 molecule: Optional[Tensor] = None, compute_forces: bool = True,

@@ -228,10 +228,6 @@ class NonLinearReadout(nn.Module):
         return self.linear_2(self.non_linearity(self.linear_1(x)))
 
 
-# covalent radii (A) by atomic number, Cordero et al. 2008 (index 0 unused)
-
-
-
 class ZBLPairRepulsion(nn.Module):
     """Ziegler-Biersack-Littmark screened Coulomb repulsion tapered at the covalent-radii sum."""
 

@@ -21,6 +21,7 @@ from ..data import AtomicGraph
 from ..nn import CosineCutoff, make_radial_basis
 from ..nn.blocks import GatedMLP, make_activation
 from ..ops.scatter import refresh_ghosts, scatter_sum
+from ..ops.tensornet_ops import TensorPlan, messages, sym_from_compact, to_compact
 from .base import InteratomicPotential
 from .registry import register_model
 
@@ -112,7 +113,7 @@ class Interaction(nn.Module):
                                              nn.Linear(2 * n_features, 3 * n_features)])
         self.linears_tensor = nn.ModuleList([nn.Linear(n_features, n_features, bias=False) for _ in range(6)])
 
-    def forward(self, X: Tensor, src: Tensor, dst: Tensor, cut: Tensor, rbf: Tensor, q: Tensor) -> Tensor:
+    def forward(self, X: Tensor, plan: TensorPlan, cut: Tensor, rbf: Tensor, q: Tensor) -> Tensor:
         n, F = X.shape[0], self.n_features
         f = rbf
         for lin in self.linears_scalar:
@@ -124,11 +125,10 @@ class Interaction(nn.Module):
         skew = self.linears_tensor[1](skew)
         sym = self.linears_tensor[2](sym)
         Y = compose(scalar, skew, sym)
-        vector = axial_vector(skew)
-        m_scalar = scatter_sum(filters[:, 0] * scalar.index_select(0, src), dst, n)
-        m_vector = scatter_sum(filters[:, 1].unsqueeze(1) * vector.index_select(0, src), dst, n)
-        m_sym = scatter_sum(filters[:, 2][:, None, None, :] * sym.index_select(0, src), dst, n)
-        msg = compose(m_scalar, skew_tensor(m_vector), m_sym)
+        # the neighbours' parts, each weighed by its filter, summed onto the centres in one pass
+        # over compact rows (scalar, axial vector, six symmetric entries)
+        m = messages(filters, to_compact(scalar, axial_vector(skew), sym), plan)
+        msg = compose(m[:, 0], skew_tensor(m[:, 1:4]), sym_from_compact(m[:, 4:]))
         cs = (1.0 + 0.1 * q)[:, None, None, None]
         C = cs * (tensor_matmul(Y, msg) + tensor_matmul(msg, Y)) if self.o3 else 2.0 * tensor_matmul(Y, msg)
         scalar, skew, sym = decompose(C)
@@ -228,8 +228,9 @@ class TensorNet(InteratomicPotential):
         src, dst, length, direction = self._pairs(atomic_numbers.shape[0], edge_index, edge_vec)
         fc, basis = self.cutoff_fn(length), self.rbf(length)
         feats = self.tensor_embedding(atomic_numbers, src, dst, fc, direction, basis)
+        plan = TensorPlan.build(src, dst, atomic_numbers.shape[0])
         for layer in self.layers:
-            feats = layer(refresh_ghosts(feats), src, dst, fc, basis, total_charge)
+            feats = layer(refresh_ghosts(feats), plan, fc, basis, total_charge)
         return feats
 
     def _features(self, X: Tensor) -> Tensor:

@@ -49,7 +49,7 @@ def kernels(t: Tensor) -> bool:
 @dataclass
 class MM:
     X0: Tensor
-    W: Tensor                      # (K0 + K1, N) unpacked (the CPU path and shape checks)
+    W: object                      # (K0 + K1, N) unpacked, or a pair (upper, lower) of row blocks
     Y: Tensor
     Wp: Optional[Tensor] = None    # packed W (CUDA)
     X1: Optional[Tensor] = None
@@ -73,12 +73,16 @@ class MMT:
     scale: float = 1.0
 
 
-def pack(Ws: Sequence[Tensor]) -> List[Tensor]:
-    """Packed operand copies of the float32 CUDA matrices ``Ws`` (one launch)."""
+def pack(Ws: Sequence) -> List[Tensor]:
+    """Packed operand copies of the float32 CUDA matrices ``Ws`` (one launch per 48; any strides,
+    so transposed views need no copy). An entry ``(A, B)`` packs ``A`` stacked above ``B``."""
     out: List[Tensor] = []
     Ws = list(Ws)
     for i in range(0, len(Ws), 48):
-        out += _ext.ops().node_pack(Ws[i:i + 48])
+        chunk = Ws[i:i + 48]
+        top = [w[0] if isinstance(w, tuple) else w for w in chunk]
+        low = [w[1] if isinstance(w, tuple) else None for w in chunk]
+        out += _ext.ops().node_pack(top, low)
     return out
 
 
@@ -97,7 +101,8 @@ def _mm_torch(p: MM) -> None:
     x = p.X0.index_select(0, idx)
     if p.X1 is not None:
         x = torch.cat([x, p.X1.index_select(0, idx)], 1)
-    y = x @ p.W.to(x.dtype)
+    W = torch.cat(p.W, 0) if isinstance(p.W, tuple) else p.W
+    y = x @ W.to(x.dtype)
     if p.accumulate:
         p.Y.index_add_(0, idx, y)
     else:
@@ -117,7 +122,11 @@ def _mm_ok(p: MM) -> bool:
     N = p.Y.shape[1]
     K = p.X0.shape[1] + (0 if p.X1 is None else p.X1.shape[1])
     return (kernels(p.X0) and p.Wp is not None and 16 <= N <= 128 and N % 16 == 0 and p.X0.shape[1] % 4 == 0
-            and (p.X1 is None or p.X1.shape[1] % 4 == 0) and K == p.W.shape[0])
+            and (p.X1 is None or p.X1.shape[1] % 4 == 0) and K == _w_rows(p.W))
+
+
+def _w_rows(W) -> int:
+    return sum(int(w.shape[0]) for w in W) if isinstance(W, tuple) else int(W.shape[0])
 
 
 def _mmt_ok(p: MMT) -> bool:
@@ -174,3 +183,21 @@ def species_sort(z: Tensor, n_el: int):
     seg = torch.zeros(n_el + 1, dtype=torch.long, device=z.device)
     seg[1:] = torch.cumsum(counts, 0)
     return perm, seg
+
+
+def segment_sum(X: Tensor, perm: Tensor, seg: Tensor, z: Tensor, groups: int) -> Tensor:
+    """Row sums of ``X`` per group: ``out[k] = sum_{i: z_i = k} X[i]`` (``perm, seg`` from
+    :func:`species_sort` of ``z``); one fixed-order kernel on CUDA."""
+    if X.is_cuda and X.dtype in (torch.float32, torch.float64) and _ext.cuda_available():
+        return _ext.ops().segment_rows_sum(X.contiguous(), perm, seg)
+    return X.new_zeros((groups,) + tuple(X.shape[1:])).index_add_(0, z, X)
+
+
+def edge_forces(plan, v: Tensor, out_dtype: torch.dtype) -> Tensor:
+    """``F_i = sum_{e: src=i} v_e - sum_{e: dst=i} v_e`` for per-edge vectors ``v (E, 3)`` through the
+    plan's CSR orderings (one fixed-order kernel on CUDA), in ``out_dtype``."""
+    if v.is_cuda and _ext.cuda_available():
+        return _ext.ops().edge_forces(plan.dst_ptr, plan.dst_perm, plan.src_ptr, plan.src_perm, v.contiguous(),
+                                      out_dtype)
+    F = torch.zeros(plan.n_nodes, 3, dtype=v.dtype, device=v.device)
+    return F.index_add_(0, plan.src, v).index_add_(0, plan.dst, -v).to(out_dtype)

@@ -60,7 +60,7 @@ class PeerBuffer:
 
 class P2PAllReduce:
     def __init__(self, numel: int, dtype: torch.dtype, device: torch.device, nblocks: Optional[int] = None,
-                 group=None, emulate_world: int = 0):
+                 group=None, emulate_world: int = 0, spin_limit: int = SPIN_LIMIT):
         if dtype != torch.float32:
             raise NotImplementedError("the fused all-reduce reduces float32 gradients")
         C = _ext.ops()
@@ -91,6 +91,7 @@ class P2PAllReduce:
         self.status_addr = int(addr.item())
         shard = numel // self.world
         self.nblocks = nblocks or max(1, min(32, (shard + 4095) // 4096))
+        self.spin_limit = int(spin_limit)
 
     def all_reduce_mean_(self, flat: Optional[torch.Tensor] = None, offset: int = 0,
                          numel: Optional[int] = None) -> None:
@@ -109,7 +110,7 @@ class P2PAllReduce:
         nb = self.nblocks if numel is None else max(1, min(self.nblocks, (n // self.world + 4095) // 4096))
         _ext.ops().p2p_allreduce([p + shift for p in self.buf_ptrs], self.flag_ptrs, self.epochs,
                                  self.status_addr, self.world, self.rank, n, 1.0 / self.world, nb,
-                                 SPIN_LIMIT, self.emulate)
+                                 self.spin_limit, self.emulate)
 
     def status(self) -> int:
         return int(self.status_host[0].item())

@@ -295,8 +295,12 @@ class _Entry:
     scalar: float
     col: Optional[Tensor] = None
 
+    def base(self, t: Tensor) -> Tensor:
+        """The entry's block of ``t`` (a parameter or its gradient) in the parameter's layout."""
+        return t.reshape(-1).narrow(0, self.offset, math.prod(self.shape)).view(self.shape)
+
     def view(self, t: Tensor) -> Tensor:
-        v = t.reshape(-1).narrow(0, self.offset, math.prod(self.shape)).view(self.shape)
+        v = self.base(t)
         return v.permute(*self.permute) if self.permute is not None else v
 
 
@@ -362,10 +366,13 @@ class _WeightMap:
 
     def build(self) -> _Weights:
         ents = self._flat()
-        views = [e.view(e.param.detach()) for e in ents]
-        scaled = torch._foreach_mul(views, [e.scalar for e in ents])
+        # one multi-tensor multiply over blocks in the parameters' own (contiguous) layout; the
+        # permutations are views of its outputs
+        scaled = torch._foreach_mul([e.base(e.param.detach()) for e in ents], [e.scalar for e in ents])
         eff = {}
         for e, v in zip(ents, scaled):
+            if e.permute is not None:
+                v = v.permute(*e.permute)
             eff[id(e)] = v * e.col.to(v) if e.col is not None else v
         g = lambda e: eff[id(e)]  # noqa: E731
         return _Weights(g(self.emb), [g(e) for e in self.up], [g(e) for e in self.sc],
@@ -395,12 +402,19 @@ class _WeightMap:
         live = [(e, g) for e, g in pairs if e.param.requires_grad]
         if not live:
             return
-        for e, _ in live:
+        src, dst = [], []
+        for e, g in live:
             if e.param.grad is None:
                 e.param.grad = torch.zeros_like(e.param)
-        gs = [g * e.col.to(g) if e.col is not None else g for e, g in live]
-        gs = torch._foreach_mul(gs, [e.scalar for e, _ in live])
-        torch._foreach_add_([e.view(e.param.grad) for e, _ in live], gs)
+            if e.col is not None:
+                g = g * e.col.to(g)
+            if e.permute is not None:
+                g = g.permute(*[e.permute.index(k) for k in range(len(e.permute))])
+            # both lists contiguous in the parameters' layout, so the multi-tensor kernels take
+            # them all in one launch each (mixed strides send every tensor to its own launch)
+            src.append(g.contiguous())
+            dst.append(e.base(e.param.grad))
+        torch._foreach_add_(dst, torch._foreach_mul(src, [e.scalar for e, _ in live]))
 
 
 # ----------------------------------------------------------------------------- the step
@@ -496,7 +510,7 @@ class MACEStep:
         for t in range(T):
             mats["up"].append(up[t])
             mats["sc"] += [scw[t][k] for k in range(n_el)]
-            mats["rev"] += [torch.cat([up[t].t(), scw[t][k].t()], 0) for k in range(n_el)]
+            mats["rev"] += [(up[t].t(), scw[t][k].t()) for k in range(n_el)]     # stacked rows, packed as is
             mats["lin"] += lin[t]
             mats["linT"] += [w.t() for w in lin[t]]
             mats["prod"].append(prod[t])
@@ -504,7 +518,7 @@ class MACEStep:
         mats["w1"], mats["w1T"] = [w1], [w1.t()]
         Pk: Dict[str, List[Optional[Tensor]]] = {}
         if NG.kernels(vec):
-            flat = [w.contiguous() for key in mats for w in mats[key]]
+            flat = [w for key in mats for w in mats[key]]                  # any strides: the pack reads them
             packed = iter(NG.pack(flat))
             Pk = {key: [next(packed) for _ in mats[key]] for key in mats}
         else:
@@ -578,8 +592,7 @@ class MACEStep:
         vbar = ops.geometry_vjp(vec, gY) + g_r[:, None] * rhat
         fdt = b.pos.dtype
         src, dst = plan.src, plan.dst
-        forces = (torch.zeros(N, 3, dtype=dt, device=dev).index_add_(0, src, vbar)
-                  .index_add_(0, dst, -vbar)).to(fdt)
+        forces = NG.edge_forces(plan, vbar, fdt)
 
         # ---------------------------------------------------------------- 3. loss
         loss, logs, a_s, g = self._loss(b, energy, forces)
@@ -643,7 +656,7 @@ class MACEStep:
             Bb, Bbd = empty_nc(), empty_nc()
             NG.mm([NG.MM(Hb, prod[t].t(), Bb, Pk["prodT"][t]), NG.MM(Hbd, prod[t].t(), Bbd, Pk["prodT"][t])])
             A2b, A2bd, gWa = ops.symcon_dual_reverse(A2[t], z, symw[t], A2d[t], Bb, Bbd)
-            g_sym[t] = torch.zeros_like(symw[t]).index_add_(0, z, gWa)
+            g_sym[t] = NG.segment_sum(gWa, perm, seg, z, n_el)
             for l in range(P):
                 sl = slice(l * l, (l + 1) * (l + 1))
                 red.append(NG.MMT(A[t][sl].reshape(-1, C), A2b[sl].reshape(-1, C), g_lin[t][l],
@@ -675,7 +688,7 @@ class MACEStep:
             wmap.add_grads(wmap.interaction_pairs(t, g_up[t], g_sc[t], g_rad[t], g_lin[t], g_sym[t], g_prod[t], ro))
             if bucket_hook is not None:
                 bucket_hook(T - 1 - t)
-        g_emb = torch.zeros_like(emb).index_add_(0, z, hb[0])
+        g_emb = NG.segment_sum(hb[0], perm, seg, z, n_el)
         wmap.add_grads([(wmap.emb, g_emb)])
         ar = m.atom_ref.weight
         if ar.requires_grad and self.we > 0:

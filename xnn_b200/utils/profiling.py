@@ -9,8 +9,9 @@
   launched with its count and summed device time, plus the share of device time and launches
   that belong to this package's own kernels (those compiled into ``xnn_b200/_C.so``).
 
-``python -m xnn_b200.utils.profiling`` prints that table for one eager MACE training step of the
-benchmark configuration (64 organic molecules, 96 channels).
+``python -m xnn_b200.utils.profiling [--model tensornet]`` prints that table for one eager training
+step of the benchmark configuration (MACE: 64 organic molecules, 96 channels; TensorNet: 32
+crystals, 64 channels, energy + force + stress loss).
 """
 from __future__ import annotations
 
@@ -31,7 +32,7 @@ OWN_KERNELS = ("conv_gather", "conv_edge", "conv_scatter", "symcon_", "edge_geom
                "radial_act_kernel", "radial_dact_kernel", "nb_count", "nb_write", "mp_real_kernel",
                "pme_spread_kernel", "pme_gather_kernel", "xnn_", "nl_", "mace_", "tn_", "pme_", "halo_",
                "adam_", "grad_", "seg_", "dd_", "fft_", "eeq_", "atm_", "amoeba_", "reax_", "sqm_", "node_",
-               "species_sort")
+               "species_sort", "dual_edge_kernel", "dual_scatter_kernel", "dipole_pairs", "dipole_matvec")
 
 
 def is_own_kernel(name: str) -> bool:
@@ -104,13 +105,40 @@ def _mace_step(batch: int):
     return lambda: tr._train_step_impl(b)
 
 
+def _tensornet_step(batch: int):
+    import tempfile
+
+    from ..config import from_dict
+    from ..data import AtomicDataset, collate, synthetic
+    from ..train import Trainer
+    structs = synthetic.triclinic_crystals(batch, seed=3000)
+    ds = AtomicDataset(structs, 5.0, precompute=True)
+    cfg = from_dict({
+        "model": {"name": "tensornet", "cutoff": 5.0, "n_features": 64, "n_interactions": 2, "n_rbf": 32,
+                  "extra": {"n_elements": 90}},
+        "optim": {"lr": 1e-3, "energy_weight": 1.0, "force_weight": 10.0, "stress_weight": 1.0, "epochs": 1,
+                  "scheduler": "none"},
+        "data": {"batch_size": batch, "val_fraction": 0.0},
+        "trainer": {"cuda_graph": False, "loggers": []},
+        "device": "cuda", "seed": 1234, "output_dir": tempfile.mkdtemp(prefix="xnn_b200_prof_"),
+    })
+    tr = Trainer(cfg, ds, val=[], test=[])
+    b = collate([ds[i] for i in range(len(ds))]).to(tr.device)
+    return lambda: tr.train_step(b)
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--model", default="mace", choices=["mace", "tensornet"])
+    ap.add_argument("--batch", type=int, default=None, help="structures per step (64 MACE, 32 TensorNet)")
     ap.add_argument("--top", type=int, default=40)
     ap.add_argument("--json", default=None, help="also write the table as JSON to this path")
     a = ap.parse_args(argv)
-    tab = kernel_table(_mace_step(a.batch), warmup=3)
+    if a.model == "mace":
+        fn = _mace_step(a.batch or 64)
+    else:
+        fn = _tensornet_step(a.batch or 32)
+    tab = kernel_table(fn, warmup=3)
     print(f"launches {tab['launches']} (own {tab['own_launches']}), device time {tab['device_us']} us, "
           f"own-kernel share {tab['own_time_share']}")
     for r in tab["rows"][:a.top]:
