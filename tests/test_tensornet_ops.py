@@ -44,6 +44,48 @@ def test_second_order_gradients():
         assert torch.autograd.gradgradcheck(f, inp)
 
 
+def test_embedding_forms_and_second_order():
+    plan, a, x, y, src, dst = _case(n=6, E=15, F=3, seed=2)
+    geo = T.geometry_rows(torch.nn.functional.normalize(torch.randn(15, 3, dtype=torch.float64), dim=-1))
+    grp = torch.tensor(T.GROUP)
+    out = T.embedding(a, geo, plan)
+    want = torch.zeros_like(out)
+    for p in range(15):
+        want[dst[p]] += a[p, grp] * geo[p][:, None]
+    torch.testing.assert_close(out, want)
+    plan, a, x, y, _, _ = _case(n=4, E=6, F=2, seed=5)
+    geo = torch.randn(6, 10, dtype=torch.float64)
+    for fn, args in ((T._Em.apply, (a, geo)), (T._Ea.apply, (y, geo)), (T._Eg.apply, (a, y))):
+        inp = tuple(t.clone().requires_grad_(True) for t in args)
+        f = lambda u, v: fn(u, v, plan)  # noqa: E731
+        assert torch.autograd.gradcheck(f, inp)
+        assert torch.autograd.gradgradcheck(f, inp)
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_matmul3_and_its_derivatives(ta, tb):
+    g = torch.Generator().manual_seed(7)
+    A = torch.randn(3, 3, 3, 2, generator=g, dtype=torch.float64, requires_grad=True)
+    B = torch.randn(3, 3, 3, 2, generator=g, dtype=torch.float64, requires_grad=True)
+    a = A.permute(0, 3, 1, 2)
+    b = B.permute(0, 3, 1, 2)
+    want = (a.transpose(-1, -2) if ta else a) @ (b.transpose(-1, -2) if tb else b)
+    torch.testing.assert_close(T.matmul3(A, B, ta, tb), want.permute(0, 2, 3, 1))
+    f = lambda u, v: T.matmul3(u, v, ta, tb)  # noqa: E731
+    assert torch.autograd.gradcheck(f, (A, B))
+    assert torch.autograd.gradgradcheck(f, (A, B))
+
+
+@pytest.mark.gpu
+def test_matmul3_kernel_matches_cpu():
+    g = torch.Generator().manual_seed(8)
+    for ta, tb in ((False, False), (True, False), (False, True), (True, True)):
+        A = torch.randn(50, 3, 3, 64, generator=g)
+        B = torch.randn(50, 3, 3, 64, generator=g)
+        torch.testing.assert_close(T.matmul3(A.cuda(), B.cuda(), ta, tb).cpu(), T.matmul3(A, B, ta, tb),
+                                   rtol=1e-5, atol=1e-5)
+
+
 def test_compact_round_trip():
     s = torch.randn(4, 3, 3, 2, dtype=torch.float64)
     sym = 0.5 * (s + s.transpose(1, 2))
@@ -70,5 +112,23 @@ def test_kernels_match_cpu(dtype, F, tol):
         torch.testing.assert_close(v.cpu(), u.detach(), rtol=tol, atol=tol)
     hc = torch.autograd.grad(lc, (ac, xc, yc))
     hg = torch.autograd.grad(lg, (ag, xg, yg))
+    for u, v in zip(hc, hg):
+        torch.testing.assert_close(v.cpu(), u, rtol=tol * 10, atol=tol * 10)
+    # the embedding forms through the same pattern (geometry rows carry the force path)
+    geo = T.geometry_rows(torch.nn.functional.normalize(torch.randn(9000, 3, dtype=dtype), dim=-1))
+    gc = geo.clone().requires_grad_(True)
+    gg = geo.cuda().requires_grad_(True)
+    ac2, ag2 = a.clone().requires_grad_(True), a.cuda().requires_grad_(True)
+
+    def chain_e(aa, ge, yy, plan):
+        m = T.embedding(aa, ge, plan)
+        (ga, gq) = torch.autograd.grad((m * yy).sum(), (aa, ge), create_graph=True)
+        return m, ga, gq, (ga * ga).sum() + (gq * gq).sum()
+    outc = chain_e(ac2, gc, y, plan_c)
+    outg = chain_e(ag2, gg, y.cuda(), plan_g)
+    for u, v in zip(outc[:3], outg[:3]):
+        torch.testing.assert_close(v.detach().cpu(), u.detach(), rtol=tol, atol=tol)
+    hc = torch.autograd.grad(outc[3], (ac2, gc))
+    hg = torch.autograd.grad(outg[3], (ag2, gg))
     for u, v in zip(hc, hg):
         torch.testing.assert_close(v.cpu(), u, rtol=tol * 10, atol=tol * 10)

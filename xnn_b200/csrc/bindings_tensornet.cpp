@@ -10,6 +10,17 @@ template <typename T>
 cudaError_t tn_edge_dot(int64_t E, int F, const int64_t* dst, const int64_t* src, const T* y, const T* x, T* out,
                         cudaStream_t s);
 
+template <typename T>
+cudaError_t tn_embed(int N, int F, const int64_t* ptr, const int64_t* order, const T* a, const T* geo, T* out,
+                     cudaStream_t s);
+template <typename T>
+cudaError_t tn_embed_da(int64_t E, int F, const int64_t* dst, const T* y, const T* geo, T* out, cudaStream_t s);
+template <typename T>
+cudaError_t tn_embed_dg(int64_t E, int F, const int64_t* dst, const T* a, const T* y, T* out, cudaStream_t s);
+
+template <typename T>
+cudaError_t tn_mm3(int64_t N, int F, bool ta, bool tb, const T* A, const T* B, T* C, cudaStream_t s);
+
 namespace {
 
 void check(const torch::Tensor& t, const char* name, torch::ScalarType st) {
@@ -74,9 +85,107 @@ torch::Tensor tn_edge_dot_op(torch::Tensor dst, torch::Tensor src, torch::Tensor
   return out;
 }
 
+#define XNN_TN_DISPATCH(T_, CALL_F, CALL_D)                                              \
+  cudaError_t e;                                                                       \
+  if ((T_) == torch::kFloat64) {                                                       \
+    e = CALL_D;                                                                        \
+  } else {                                                                             \
+    TORCH_CHECK((T_) == torch::kFloat32, "tensornet: float32 or float64");             \
+    e = CALL_F;                                                                        \
+  }
+
+// out[n, c] = sum_{j in ptr[n]..ptr[n+1]} a[order[j], g(c)] * geo[order[j], c]
+torch::Tensor tn_embed_op(torch::Tensor ptr, torch::Tensor order, torch::Tensor a, torch::Tensor geo) {
+  const c10::cuda::CUDAGuard guard(a.device());
+  check(ptr, "ptr", torch::kInt64);
+  check(a, "a", a.scalar_type());
+  check(geo, "geo", a.scalar_type());
+  TORCH_CHECK(a.dim() == 3 && a.size(1) == 3 && geo.dim() == 2 && geo.size(1) == 10 && geo.size(0) == a.size(0),
+              "tensornet embed: a (E, 3, F), geo (E, 10)");
+  const bool ord = order.numel() > 0;
+  if (ord) check(order, "order", torch::kInt64);
+  const int64_t N = ptr.numel() - 1;
+  const int F = (int)a.size(2);
+  auto out = torch::empty({N, 10, F}, a.options());
+  auto s = at::cuda::getCurrentCUDAStream();
+  const int64_t* o = ord ? order.data_ptr<int64_t>() : nullptr;
+  XNN_TN_DISPATCH(a.scalar_type(),
+                  tn_embed<float>((int)N, F, ptr.data_ptr<int64_t>(), o, a.data_ptr<float>(), geo.data_ptr<float>(),
+                                  out.data_ptr<float>(), s),
+                  tn_embed<double>((int)N, F, ptr.data_ptr<int64_t>(), o, a.data_ptr<double>(),
+                                   geo.data_ptr<double>(), out.data_ptr<double>(), s))
+  TORCH_CHECK(e == cudaSuccess, "tn_embed: ", cudaGetErrorString(e));
+  return out;
+}
+
+// out[e, g] = sum_{c in g} y[dst[e], c] * geo[e, c]
+torch::Tensor tn_embed_da_op(torch::Tensor dst, torch::Tensor y, torch::Tensor geo) {
+  const c10::cuda::CUDAGuard guard(y.device());
+  check(dst, "dst", torch::kInt64);
+  check(y, "y", y.scalar_type());
+  check(geo, "geo", y.scalar_type());
+  TORCH_CHECK(y.dim() == 3 && y.size(1) == 10 && geo.dim() == 2 && geo.size(1) == 10 && geo.size(0) == dst.numel(),
+              "tensornet embed_da: y (n, 10, F), geo (E, 10)");
+  const int64_t E = dst.numel();
+  const int F = (int)y.size(2);
+  auto out = torch::empty({E, 3, F}, y.options());
+  auto s = at::cuda::getCurrentCUDAStream();
+  XNN_TN_DISPATCH(y.scalar_type(),
+                  tn_embed_da<float>(E, F, dst.data_ptr<int64_t>(), y.data_ptr<float>(), geo.data_ptr<float>(),
+                                     out.data_ptr<float>(), s),
+                  tn_embed_da<double>(E, F, dst.data_ptr<int64_t>(), y.data_ptr<double>(), geo.data_ptr<double>(),
+                                      out.data_ptr<double>(), s))
+  TORCH_CHECK(e == cudaSuccess, "tn_embed_da: ", cudaGetErrorString(e));
+  return out;
+}
+
+// out[e, c] = sum_f a[e, g(c), f] * y[dst[e], c, f]
+torch::Tensor tn_embed_dg_op(torch::Tensor dst, torch::Tensor a, torch::Tensor y) {
+  const c10::cuda::CUDAGuard guard(y.device());
+  check(dst, "dst", torch::kInt64);
+  check(a, "a", y.scalar_type());
+  check(y, "y", y.scalar_type());
+  TORCH_CHECK(a.dim() == 3 && a.size(1) == 3 && y.dim() == 3 && y.size(1) == 10 && a.size(2) == y.size(2) &&
+                  a.size(0) == dst.numel(),
+              "tensornet embed_dg: a (E, 3, F), y (n, 10, F)");
+  const int64_t E = dst.numel();
+  const int F = (int)y.size(2);
+  auto out = torch::empty({E, 10}, y.options());
+  auto s = at::cuda::getCurrentCUDAStream();
+  XNN_TN_DISPATCH(y.scalar_type(),
+                  tn_embed_dg<float>(E, F, dst.data_ptr<int64_t>(), a.data_ptr<float>(), y.data_ptr<float>(),
+                                     out.data_ptr<float>(), s),
+                  tn_embed_dg<double>(E, F, dst.data_ptr<int64_t>(), a.data_ptr<double>(), y.data_ptr<double>(),
+                                      out.data_ptr<double>(), s))
+  TORCH_CHECK(e == cudaSuccess, "tn_embed_dg: ", cudaGetErrorString(e));
+  return out;
+}
+// C = op(A) op(B) per atom and channel, (N, 3, 3, F)
+torch::Tensor tn_mm3_op(torch::Tensor A, torch::Tensor B, bool ta, bool tb) {
+  const c10::cuda::CUDAGuard guard(A.device());
+  check(A, "A", A.scalar_type());
+  check(B, "B", A.scalar_type());
+  TORCH_CHECK(A.dim() == 4 && A.size(1) == 3 && A.size(2) == 3 && A.sizes() == B.sizes(),
+              "tensornet mm3: A, B (N, 3, 3, F)");
+  auto C = torch::empty_like(A);
+  const int64_t N = A.size(0);
+  const int F = (int)A.size(3);
+  auto s = at::cuda::getCurrentCUDAStream();
+  XNN_TN_DISPATCH(A.scalar_type(),
+                  tn_mm3<float>(N, F, ta, tb, A.data_ptr<float>(), B.data_ptr<float>(), C.data_ptr<float>(), s),
+                  tn_mm3<double>(N, F, ta, tb, A.data_ptr<double>(), B.data_ptr<double>(), C.data_ptr<double>(), s))
+  TORCH_CHECK(e == cudaSuccess, "tn_mm3: ", cudaGetErrorString(e));
+  return C;
+}
+#undef XNN_TN_DISPATCH
+
 }  // namespace
 
 void register_tensornet(pybind11::module& m) {
   m.def("tn_gather", &tn_gather_op);
   m.def("tn_edge_dot", &tn_edge_dot_op);
+  m.def("tn_embed", &tn_embed_op);
+  m.def("tn_embed_da", &tn_embed_da_op);
+  m.def("tn_embed_dg", &tn_embed_dg_op);
+  m.def("tn_mm3", &tn_mm3_op);
 }

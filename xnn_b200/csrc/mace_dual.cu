@@ -207,16 +207,28 @@ __global__ void edge_forces_kernel(int N, const int64_t* __restrict__ dst_ptr, c
 }
 
 // Per-group row sums: out[k, :] = sum_{r in seg[k] .. seg[k+1]} X[perm[r], :] (atoms grouped by
-// element: the gradients of per-element tables). Block (k, column tile of 256), rows in order.
+// element: the gradients of per-element tables). Block (32-column tile, group k): lanes over the
+// columns (coalesced), the 8 warps over the group's rows in a fixed interleave, then a fixed-order
+// sum of the warps' partials.
 template <typename T>
-__global__ void segment_rows_sum_kernel(int cols, const int* __restrict__ perm, const int* __restrict__ seg,
-                                        const T* __restrict__ X, T* __restrict__ out) {
+__global__ void __launch_bounds__(256) segment_rows_sum_kernel(int cols, const int* __restrict__ perm,
+                                                               const int* __restrict__ seg, const T* __restrict__ X,
+                                                               T* __restrict__ out) {
+  __shared__ T part[8][32];
   const int k = blockIdx.y;
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lane;
   T acc = T(0);
-  for (int r = seg[k]; r < seg[k + 1]; ++r) acc += X[(int64_t)perm[r] * cols + c];
-  out[(int64_t)k * cols + c] = acc;
+  if (c < cols)
+    for (int r = seg[k] + w; r < seg[k + 1]; r += 8) acc += X[(int64_t)perm[r] * cols + c];
+  part[w][lane] = acc;
+  __syncthreads();
+  if (w == 0 && c < cols) {
+    T v = part[0][lane];
+#pragma unroll
+    for (int q = 1; q < 8; ++q) v += part[q][lane];
+    out[(int64_t)k * cols + c] = v;
+  }
 }
 
 template <typename T, typename TO>
@@ -231,7 +243,7 @@ template <typename T>
 cudaError_t segment_rows_sum(int groups, int cols, const int* perm, const int* seg, const T* X, T* out,
                              cudaStream_t s) {
   if (groups == 0 || cols == 0) return cudaSuccess;
-  segment_rows_sum_kernel<T><<<dim3((cols + 255) / 256, groups), 256, 0, s>>>(cols, perm, seg, X, out);
+  segment_rows_sum_kernel<T><<<dim3((cols + 31) / 32, groups), 256, 0, s>>>(cols, perm, seg, X, out);
   return cudaGetLastError();
 }
 

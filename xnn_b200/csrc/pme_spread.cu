@@ -6,54 +6,14 @@
 // G[b][a] = du_a/dr_b). The adjoint kernel reads a mesh potential phi and returns, per site,
 // dE/dd = G (sum phi dW/du) and dE/dr = G (sum phi d(L W)/du) (third spline derivatives for the
 // quadrupoles). Only planes z0 <= k_3 < z0 + nz are touched (a z-slab of a distributed mesh).
-// Spreading accumulates with float atomics (one thread per site and (x, y) stencil column);
-// the gather is one thread per site (no atomics).
+// Spreading accumulates with float atomics (one thread per site and (x, y) stencil column); the
+// gather is one warp per site, lanes over the stencil columns, with a warp reduction (no
+// atomics). Both are instantiated for spline orders 4-6 so the spline rows stay in registers.
 #include <cuda_runtime.h>
 
 #include <cstdint>
 
 namespace {
-
-constexpr int PMAX = 8;
-
-// M_n(t + j) for j = 0..p-1 (zero where j >= n), by the cardinal B-spline recursion
-__device__ __forceinline__ void spline_row(double t, int n, int p, double* out) {
-  if (n == 1) {                      // the unit box: M_1(t + j) = 1 for j == 0
-    for (int j = 0; j < p; ++j) out[j] = j == 0 ? 1.0 : 0.0;
-    return;
-  }
-  double w[PMAX];
-  w[0] = t;
-  w[1] = 1.0 - t;
-  for (int m = 3; m <= n; ++m) {
-    double nw[PMAX];
-    for (int j = 0; j < m; ++j) {
-      double v = 0.0;
-      if (j < m - 1) v += (t + j) / (m - 1) * w[j];
-      if (j >= 1) v += (m - t - j) / (m - 1) * w[j - 1];
-      nw[j] = v;
-    }
-    for (int j = 0; j < m; ++j) w[j] = nw[j];
-  }
-  for (int j = 0; j < p; ++j) out[j] = j < n ? w[j] : 0.0;
-}
-
-// values and the first `nd` derivatives of M_p(t + j): derivatives are finite differences of
-// lower-order splines, M_p^(k)(x) = sum_i (-1)^i C(k, i) M_{p-k}(x - i)
-__device__ __forceinline__ void spline_derivs(double t, int p, int nd, double th[4][PMAX]) {
-  for (int k = 0; k <= nd; ++k) {
-    double low[PMAX];
-    spline_row(t, p - k, p, low);
-    for (int j = 0; j < p; ++j) {
-      double v = 0.0, c = 1.0;
-      for (int i = 0; i <= k; ++i) {
-        if (j - i >= 0) v += ((i & 1) ? -c : c) * low[j - i];
-        c = c * (k - i) / (i + 1);
-      }
-      th[k][j] = v;
-    }
-  }
-}
 
 struct Site {
   double t[3];
@@ -95,101 +55,189 @@ __device__ __forceinline__ void site_multipoles(int64_t i, const double* d, cons
     }
 }
 
-__global__ void pme_spread_kernel(int64_t n, int p, const double* __restrict__ pos, const double* __restrict__ G,
-                                  int K1, int K2, int K3, int z0, int nz, const double* __restrict__ q,
-                                  const double* __restrict__ d, const double* __restrict__ Q,
-                                  float* __restrict__ grid) {
+// ---------------------------------------------------------------- order-templated forms
+// M_n(t + j), j = 0..P-1 (zero where j >= n), n <= P, every loop unrolled so the rows stay in
+// registers.
+template <int P>
+__device__ __forceinline__ void spline_row_t(double t, int n, double out[P]) {
+  double w[P];
+#pragma unroll
+  for (int j = 0; j < P; ++j) w[j] = 0.0;
+  w[0] = 1.0;                                  // M_1
+#pragma unroll
+  for (int m = 2; m <= P; ++m) {
+    if (m <= n) {
+      double nw[P];
+#pragma unroll
+      for (int j = 0; j < P; ++j) {
+        double v = 0.0;
+        if (j < m - 1) v += (t + j) / (m - 1) * w[j];
+        if (j >= 1 && j < m) v += (m - t - j) / (m - 1) * w[j - 1];
+        nw[j] = v;
+      }
+#pragma unroll
+      for (int j = 0; j < P; ++j) w[j] = nw[j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < P; ++j) out[j] = j < n ? w[j] : 0.0;
+}
+
+// th[k][j] = k-th derivative of M_P at t + j, k = 0..ND
+template <int P, int ND>
+__device__ __forceinline__ void spline_derivs_t(double t, double th[ND + 1][P]) {
+#pragma unroll
+  for (int k = 0; k <= ND; ++k) {
+    double low[P];
+    spline_row_t<P>(t, P - k, low);
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      double v = 0.0, c = 1.0;
+#pragma unroll
+      for (int i = 0; i <= k; ++i) {
+        if (j - i >= 0) v += ((i & 1) ? -c : c) * low[j - i];
+        c = c * (k - i) / (i + 1);
+      }
+      th[k][j] = v;
+    }
+  }
+}
+
+// the entry j of a register row (unrolled select: no local-memory indexing)
+template <int P>
+__device__ __forceinline__ double pick(const double row[P], int j) {
+  double v = row[0];
+#pragma unroll
+  for (int q = 1; q < P; ++q) v = j == q ? row[q] : v;
+  return v;
+}
+
+// Spreading: one thread per site and (x, y) stencil column, the column's P planes in registers.
+template <int P, int ND>
+__global__ void __launch_bounds__(256) pme_spread_kernel(int64_t n, const double* __restrict__ pos,
+                                                         const double* __restrict__ G, int K1, int K2, int K3, int z0,
+                                                         int nz, const double* __restrict__ q,
+                                                         const double* __restrict__ d, const double* __restrict__ Q,
+                                                         float* __restrict__ grid) {
   const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int64_t i = tid / (p * p);
+  const int64_t i = tid / (P * P);
   if (i >= n) return;
-  const int jx = (int)(tid % (p * p)) / p, jy = (int)(tid % p);
+  const int col = (int)(tid - i * (P * P));
+  const int jx = col / P, jy = col - jx * P;
   const int K[3] = {K1, K2, K3};
   const Site s = site_of(pos, i, G, K);
-  double th[3][4][PMAX];
-  for (int a = 0; a < 3; ++a) spline_derivs(s.t[a], p, Q ? 2 : (d ? 1 : 0), th[a]);
+  double tx[ND + 1][P], ty[ND + 1][P], tz[ND + 1][P];
+  spline_derivs_t<P, ND>(s.t[0], tx);
+  spline_derivs_t<P, ND>(s.t[1], ty);
+  spline_derivs_t<P, ND>(s.t[2], tz);
+  double ax[ND + 1], ay[ND + 1];
+#pragma unroll
+  for (int k = 0; k <= ND; ++k) {
+    ax[k] = pick<P>(tx[k], jx);
+    ay[k] = pick<P>(ty[k], jy);
+  }
   double du[3], Qu[9];
   site_multipoles(i, d, Q, G, du, Qu);
   const double qi = q ? q[i] : 0.0;
   const int kx = wrap(s.base[0] - jx, K1), ky = wrap(s.base[1] - jy, K2);
-  for (int jz = 0; jz < p; ++jz) {
-    const int kz = wrap(s.base[2] - jz, K3);
-    const int zl = kz - z0;
+  float* col_ptr = grid + ((int64_t)kx * K2 + ky) * nz;
+#pragma unroll
+  for (int jz = 0; jz < P; ++jz) {
+    const int zl = wrap(s.base[2] - jz, K3) - z0;
     if (zl < 0 || zl >= nz) continue;
-    const double w0x = th[0][0][jx], w0y = th[1][0][jy], w0z = th[2][0][jz];
-    double v = qi * w0x * w0y * w0z;
-    if (d) {
-      v += du[0] * th[0][1][jx] * w0y * w0z + du[1] * w0x * th[1][1][jy] * w0z + du[2] * w0x * w0y * th[2][1][jz];
-    }
-    if (Q) {
+    double v = qi * ax[0] * ay[0] * tz[0][jz];
+    if (ND >= 1 && d)
+      v += du[0] * ax[ND >= 1 ? 1 : 0] * ay[0] * tz[0][jz] + du[1] * ax[0] * ay[ND >= 1 ? 1 : 0] * tz[0][jz] +
+           du[2] * ax[0] * ay[0] * tz[ND >= 1 ? 1 : 0][jz];
+    if (ND >= 2 && Q) {
+#pragma unroll
       for (int a = 0; a < 3; ++a)
+#pragma unroll
         for (int c = 0; c < 3; ++c) {
-          int o[3] = {0, 0, 0};
-          o[a] += 1;
-          o[c] += 1;
-          v += (Qu[3 * a + c] / 3.0) * th[0][o[0]][jx] * th[1][o[1]][jy] * th[2][o[2]][jz];
+          const int ox = (a == 0) + (c == 0), oy = (a == 1) + (c == 1), oz = (a == 2) + (c == 2);
+          v += (Qu[3 * a + c] / 3.0) * ax[ox < ND ? ox : ND] * ay[oy < ND ? oy : ND] * tz[oz < ND ? oz : ND][jz];
         }
     }
-    atomicAdd(grid + ((int64_t)kx * K2 + ky) * nz + zl, (float)v);
+    atomicAdd(col_ptr + zl, (float)v);
   }
 }
 
-__global__ void pme_gather_kernel(int64_t n, int p, const double* __restrict__ pos, const double* __restrict__ G,
-                                  int K1, int K2, int K3, int z0, int nz, const double* __restrict__ q,
-                                  const double* __restrict__ d, const double* __restrict__ Q,
-                                  const float* __restrict__ phi, double* __restrict__ gd, double* __restrict__ gpos) {
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+// Gather (the spreading's adjoint): one warp per site, lanes over the P x P columns, each lane's
+// P planes in registers, then a fixed-order warp reduction of the six sums.
+template <int P, int ND>
+__global__ void __launch_bounds__(256) pme_gather_kernel(int64_t n, const double* __restrict__ pos,
+                                                         const double* __restrict__ G, int K1, int K2, int K3, int z0,
+                                                         int nz, const double* __restrict__ q,
+                                                         const double* __restrict__ d, const double* __restrict__ Q,
+                                                         const float* __restrict__ phi, double* __restrict__ gd,
+                                                         double* __restrict__ gpos) {
+  const int64_t i = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   if (i >= n) return;
   const int K[3] = {K1, K2, K3};
   const Site s = site_of(pos, i, G, K);
-  const int nd = gpos ? (Q ? 3 : (d ? 2 : 1)) : 1;
-  double th[3][4][PMAX];
-  for (int a = 0; a < 3; ++a) spline_derivs(s.t[a], p, nd, th[a]);
-  double du[3], Qu[9];
-  site_multipoles(i, d, Q, G, du, Qu);
-  const double qi = q ? q[i] : 0.0;
   double P1[3] = {0, 0, 0};      // sum phi dW/du_a
   double Fu[3] = {0, 0, 0};      // sum phi d(L W)/du_a
-  for (int jx = 0; jx < p; ++jx) {
-    const int kx = wrap(s.base[0] - jx, K1);
-    for (int jy = 0; jy < p; ++jy) {
-      const int ky = wrap(s.base[1] - jy, K2);
-      for (int jz = 0; jz < p; ++jz) {
-        const int kz = wrap(s.base[2] - jz, K3);
-        const int zl = kz - z0;
-        if (zl < 0 || zl >= nz) continue;
-        const double f = (double)phi[((int64_t)kx * K2 + ky) * nz + zl];
-        // derivative of W of multi-order (ox, oy, oz) along the axes
-        auto W = [&](int ox, int oy, int oz) { return th[0][ox][jx] * th[1][oy][jy] * th[2][oz][jz]; };
-        P1[0] += f * W(1, 0, 0);
-        P1[1] += f * W(0, 1, 0);
-        P1[2] += f * W(0, 0, 1);
-        if (gpos) {
-          for (int a = 0; a < 3; ++a) {
-            int o[3] = {0, 0, 0};
-            o[a] = 1;
-            double lw = qi * W(o[0], o[1], o[2]);
-            if (d) {
-              for (int b = 0; b < 3; ++b) {
-                int ob[3] = {o[0], o[1], o[2]};
-                ob[b] += 1;
-                lw += du[b] * W(ob[0], ob[1], ob[2]);
-              }
-            }
-            if (Q) {
-              for (int b = 0; b < 3; ++b)
-                for (int c = 0; c < 3; ++c) {
-                  int oc[3] = {o[0], o[1], o[2]};
-                  oc[b] += 1;
-                  oc[c] += 1;
-                  lw += (Qu[3 * b + c] / 3.0) * W(oc[0], oc[1], oc[2]);
-                }
-            }
-            Fu[a] += f * lw;
+  if (lane < P * P) {
+    const int jx = lane / P, jy = lane - (lane / P) * P;
+    double tx[ND + 1][P], ty[ND + 1][P], tz[ND + 1][P];
+    spline_derivs_t<P, ND>(s.t[0], tx);
+    spline_derivs_t<P, ND>(s.t[1], ty);
+    spline_derivs_t<P, ND>(s.t[2], tz);
+    double ax[ND + 1], ay[ND + 1];
+#pragma unroll
+    for (int k = 0; k <= ND; ++k) {
+      ax[k] = pick<P>(tx[k], jx);
+      ay[k] = pick<P>(ty[k], jy);
+    }
+    double du[3], Qu[9];
+    site_multipoles(i, d, Q, G, du, Qu);
+    const double qi = q ? q[i] : 0.0;
+    const int kx = wrap(s.base[0] - jx, K1), ky = wrap(s.base[1] - jy, K2);
+    const float* col_ptr = phi + ((int64_t)kx * K2 + ky) * nz;
+#pragma unroll
+    for (int jz = 0; jz < P; ++jz) {
+      const int zl = wrap(s.base[2] - jz, K3) - z0;
+      if (zl < 0 || zl >= nz) continue;
+      const double f = (double)__ldg(col_ptr + zl);
+      // derivative of W of multi-order (ox, oy, oz)
+      auto W = [&](int ox, int oy, int oz) {
+        return ax[ox < ND ? ox : ND] * ay[oy < ND ? oy : ND] * tz[oz < ND ? oz : ND][jz];
+      };
+      P1[0] += f * W(1, 0, 0);
+      P1[1] += f * W(0, 1, 0);
+      P1[2] += f * W(0, 0, 1);
+      if (gpos) {
+#pragma unroll
+        for (int a = 0; a < 3; ++a) {
+          const int o0 = a == 0, o1 = a == 1, o2 = a == 2;
+          double lw = qi * W(o0, o1, o2);
+          if (d) {
+#pragma unroll
+            for (int b = 0; b < 3; ++b) lw += du[b] * W(o0 + (b == 0), o1 + (b == 1), o2 + (b == 2));
           }
+          if (Q) {
+#pragma unroll
+            for (int b = 0; b < 3; ++b)
+#pragma unroll
+              for (int c = 0; c < 3; ++c)
+                lw += (Qu[3 * b + c] / 3.0) *
+                      W(o0 + (b == 0) + (c == 0), o1 + (b == 1) + (c == 1), o2 + (b == 2) + (c == 2));
+          }
+          Fu[a] += f * lw;
         }
       }
     }
   }
+#pragma unroll
+  for (int a = 0; a < 3; ++a) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      P1[a] += __shfl_xor_sync(0xffffffffu, P1[a], off);
+      Fu[a] += __shfl_xor_sync(0xffffffffu, Fu[a], off);
+    }
+  }
+  if (lane != 0) return;
   // back to Cartesian: dE/dr_b = sum_a G[b][a] dE/du_a
   for (int b = 0; b < 3; ++b) {
     if (gd) gd[3 * i + b] = G[b * 3 + 0] * P1[0] + G[b * 3 + 1] * P1[1] + G[b * 3 + 2] * P1[2];
@@ -199,22 +247,49 @@ __global__ void pme_gather_kernel(int64_t n, int p, const double* __restrict__ p
 
 }  // namespace
 
+template <int P>
+cudaError_t spread_p(int64_t n, const double* pos, const double* G, int K1, int K2, int K3, int z0, int nz,
+                     const double* q, const double* d, const double* Q, float* grid, cudaStream_t s) {
+  const unsigned blocks = (unsigned)((n * P * P + 255) / 256);
+  if (Q) pme_spread_kernel<P, 2><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, grid);
+  else if (d) pme_spread_kernel<P, 1><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, grid);
+  else pme_spread_kernel<P, 0><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, grid);
+  return cudaGetLastError();
+}
+
+template <int P>
+cudaError_t gather_p(int64_t n, const double* pos, const double* G, int K1, int K2, int K3, int z0, int nz,
+                     const double* q, const double* d, const double* Q, const float* phi, double* gd, double* gpos,
+                     cudaStream_t s) {
+  const unsigned blocks = (unsigned)((n + 7) / 8);          // 8 sites (warps) per block
+  if (gpos && Q)
+    pme_gather_kernel<P, 3><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd, gpos);
+  else if (gpos && d)
+    pme_gather_kernel<P, 2><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd, gpos);
+  else
+    pme_gather_kernel<P, 1><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd, gpos);
+  return cudaGetLastError();
+}
+
 cudaError_t pme_spread_launch(int64_t n, int p, const double* pos, const double* G, int K1, int K2, int K3, int z0,
                               int nz, const double* q, const double* d, const double* Q, float* grid, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  if (p < 2 || p > PMAX) return cudaErrorInvalidValue;
-  const int64_t threads = n * p * p;
-  pme_spread_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(n, p, pos, G, K1, K2, K3, z0, nz, q, d, Q,
-                                                                       grid);
-  return cudaGetLastError();
+  switch (p) {
+    case 4: return spread_p<4>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, grid, s);
+    case 5: return spread_p<5>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, grid, s);
+    case 6: return spread_p<6>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t pme_gather_launch(int64_t n, int p, const double* pos, const double* G, int K1, int K2, int K3, int z0,
                               int nz, const double* q, const double* d, const double* Q, const float* phi, double* gd,
                               double* gpos, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  if (p < 2 || p > PMAX) return cudaErrorInvalidValue;
-  pme_gather_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(n, p, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd,
-                                                                gpos);
-  return cudaGetLastError();
+  switch (p) {
+    case 4: return gather_p<4>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd, gpos, s);
+    case 5: return gather_p<5>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd, gpos, s);
+    case 6: return gather_p<6>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd, gpos, s);
+    default: return cudaErrorInvalidValue;
+  }
 }

@@ -143,7 +143,7 @@ def spread(pos: Tensor, cell: Tensor, q: Optional[Tensor], d: Optional[Tensor], 
     of the third axis, ``(K1, K2, z1 - z0)``). For a float32 mesh of float64 CUDA sites the
     spreading kernel runs (its adjoint differentiates positions and dipoles)."""
     n = pos.shape[0]
-    if (out_dtype == torch.float32 and pos.is_cuda and pos.dtype == torch.float64 and p <= 8 and _kernel_ok()
+    if (out_dtype == torch.float32 and pos.is_cuda and pos.dtype == torch.float64 and 4 <= p <= 6 and _kernel_ok()
             and hasattr(__import__("xnn_b200._ext", fromlist=["ops"]).ops(), "pme_spread")):
         if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (q, Q, cell)):
             raise NotImplementedError("the spreading kernel differentiates positions and dipoles only")
@@ -431,7 +431,7 @@ class DipoleOperator:
         """The reciprocal field without an energy graph: one process, CUDA float64 sites and a
         float32 mesh (the spreading and gather kernels)."""
         s = self.mod.setup
-        ok = (self.kernel and self.mod.mesh_backend is None and s.fft_dtype == torch.float32 and s.order <= 8)
+        ok = (self.kernel and self.mod.mesh_backend is None and s.fft_dtype == torch.float32 and 4 <= s.order <= 6)
         if ok and not hasattr(self, "_G"):
             K = torch.tensor(s.mesh, dtype=torch.float64, device=self.pos.device)
             self._G = (torch.linalg.inv(self.cell.double()) * K[None, :]).contiguous()

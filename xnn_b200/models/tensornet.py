@@ -20,8 +20,10 @@ from torch.nn import functional as F
 from ..data import AtomicGraph
 from ..nn import CosineCutoff, make_radial_basis
 from ..nn.blocks import GatedMLP, make_activation
+from ..ops import gemm
 from ..ops.scatter import refresh_ghosts, scatter_sum
-from ..ops.tensornet_ops import TensorPlan, messages, sym_from_compact, to_compact
+from ..ops.tensornet_ops import (TensorPlan, embedding, geometry_rows, matmul3, messages, sym_from_compact,
+                                 to_compact)
 from .base import InteratomicPotential
 from .registry import register_model
 
@@ -58,7 +60,8 @@ def frobenius(t: Tensor) -> Tensor:
 
 
 def tensor_matmul(a: Tensor, b: Tensor) -> Tensor:
-    return (a.unsqueeze(3) * b.unsqueeze(1)).sum(2)
+    """Per atom and channel 3x3 products (one kernel on CUDA, differentiable to any order)."""
+    return matmul3(a, b)
 
 
 class TensorEmbedding(nn.Module):
@@ -76,16 +79,24 @@ class TensorEmbedding(nn.Module):
                                              nn.Linear(2 * n_features, 3 * n_features)])
         self.init_norm = nn.LayerNorm(n_features)
 
-    def forward(self, z: Tensor, src: Tensor, dst: Tensor, cut: Tensor, unit: Tensor, rbf: Tensor) -> Tensor:
-        n = z.shape[0]
+    def forward(self, z: Tensor, src: Tensor, dst: Tensor, cut: Tensor, unit: Tensor, rbf: Tensor,
+                plan: Optional[TensorPlan] = None) -> Tensor:
+        n, nf = z.shape[0], self.n_features
+        if plan is None:
+            plan = TensorPlan.build(src, dst, n)
         emb = self.emb(z)
-        pair = self.emb2(torch.cat([emb.index_select(0, dst), emb.index_select(0, src)], -1))
+        # emb2 on [emb_i | emb_j] splits into two per-atom products gathered to the pairs
+        w_i, w_j = self.emb2.weight[:, :nf], self.emb2.weight[:, nf:]
+        pair = (emb @ w_i.t()).index_select(0, dst) + F.linear(emb, w_j, self.emb2.bias).index_select(0, src)
         w = cut.unsqueeze(-1) * pair
-        scalar = scatter_sum(w * self.distance_proj1(rbf), dst, n)
-        vector = scatter_sum((w * self.distance_proj2(rbf)).unsqueeze(1) * unit.unsqueeze(-1), dst, n)
-        outer = unit.unsqueeze(2) * unit.unsqueeze(1)
-        full = scatter_sum((w * self.distance_proj3(rbf))[:, None, None, :] * outer.unsqueeze(-1), dst, n)
-        skew = skew_tensor(vector)
+        # the three radial projections as one product
+        proj = gemm.matmul(rbf, torch.cat([self.distance_proj1.weight, self.distance_proj2.weight,
+                                           self.distance_proj3.weight], 0).t()) + torch.cat(
+            [self.distance_proj1.bias, self.distance_proj2.bias, self.distance_proj3.bias])
+        a = w.unsqueeze(1) * proj.view(-1, 3, nf)
+        rows = embedding(a, geometry_rows(unit), plan)
+        scalar, skew = rows[:, 0], skew_tensor(rows[:, 1:4])
+        full = sym_from_compact(rows[:, 4:])
         eye = torch.eye(3, dtype=full.dtype, device=full.device)
         sym = full - full.diagonal(dim1=1, dim2=2).mean(-1)[:, None, None, :] * eye[None, :, :, None]
         norm = self.init_norm(frobenius(compose(scalar, skew, sym)))
@@ -96,6 +107,12 @@ class TensorEmbedding(nn.Module):
         skew = _mix(self.linears_tensor[1], skew) * norm[:, 1, None, None, :]
         sym = _mix(self.linears_tensor[2], sym) * norm[:, 2, None, None, :]
         return compose(scalar, skew, sym)
+
+
+def _edge_linear(x: Tensor, lin: nn.Linear) -> Tensor:
+    """``lin(x)`` for per-pair rows: the tensor-core product (3xTF32, float32 accuracy) when the
+    rows are many, differentiable to any order."""
+    return gemm.matmul(x, lin.weight.t()) + lin.bias
 
 
 def _mix(lin: nn.Linear, t: Tensor) -> Tensor:
@@ -117,7 +134,7 @@ class Interaction(nn.Module):
         n, F = X.shape[0], self.n_features
         f = rbf
         for lin in self.linears_scalar:
-            f = self.act(lin(f))
+            f = self.act(_edge_linear(f, lin))
         filters = (f * cut.unsqueeze(-1)).reshape(-1, 3, F)
         X = X / (frobenius(X) + 1.0)[:, None, None, :]
         scalar, skew, sym = decompose(X)
@@ -227,8 +244,8 @@ class TensorNet(InteratomicPotential):
         """Per-atom 3 x 3 tensor features after the embedding and every interaction."""
         src, dst, length, direction = self._pairs(atomic_numbers.shape[0], edge_index, edge_vec)
         fc, basis = self.cutoff_fn(length), self.rbf(length)
-        feats = self.tensor_embedding(atomic_numbers, src, dst, fc, direction, basis)
         plan = TensorPlan.build(src, dst, atomic_numbers.shape[0])
+        feats = self.tensor_embedding(atomic_numbers, src, dst, fc, direction, basis, plan)
         for layer in self.layers:
             feats = layer(refresh_ghosts(feats), plan, fc, basis, total_charge)
         return feats

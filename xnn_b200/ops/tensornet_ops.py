@@ -17,8 +17,10 @@ and its two adjoints are of the same kind:
 ``d M / d a = D``, ``d M / d x = M^T``, ``d M^T / d a = D`` (roles swapped), ``d M^T / d y = M``,
 ``d D / d y = M``, ``d D / d x = M^T``: three autograd functions whose backward passes call each
 other differentiate to any order, each on one sm_100a kernel (``csrc/tensornet.cu``) with
-nothing pair-sized beyond the filters and their gradients. On the CPU the same functions run
-their PyTorch formulas.
+nothing pair-sized beyond the filters and their gradients. The embedding is the same kind of
+sum with per-pair geometry rows ``geo = [1, u, u u^T]`` in place of the neighbour's features
+(``Em``, with adjoints ``Ea`` in the pair parts and ``Eg`` in the geometry). On the CPU the same
+functions run their PyTorch formulas.
 """
 from __future__ import annotations
 
@@ -142,6 +144,79 @@ class _D(torch.autograd.Function):
         return dy, dx, None
 
 
+class _Em(torch.autograd.Function):
+    """Embedding sum onto the receivers: ``out[i, c] = sum_{p -> i} a[p, g(c)] geo[p, c]``."""
+
+    @staticmethod
+    def forward(ctx, a: Tensor, geo: Tensor, plan: TensorPlan):
+        ctx.save_for_backward(a, geo)
+        ctx.plan = plan
+        if _kernels(a):
+            return _ext.ops().tn_embed(plan.dst_ptr, plan.dst_order, a.contiguous(), geo.contiguous())
+        out = a.new_zeros(plan.n, 10, a.shape[-1])
+        return out.index_add_(0, plan.dst, _expand(a) * geo.unsqueeze(-1))
+
+    @staticmethod
+    def backward(ctx, g: Tensor):
+        a, geo = ctx.saved_tensors
+        plan = ctx.plan
+        da = _Ea.apply(g, geo, plan) if ctx.needs_input_grad[0] else None
+        dgeo = _Eg.apply(a, g, plan) if ctx.needs_input_grad[1] else None
+        return da, dgeo, None
+
+
+class _Ea(torch.autograd.Function):
+    """``out[p, g] = sum_{c in g} y[dst, c] geo[p, c]`` (the adjoint of the embedding in ``a``)."""
+
+    @staticmethod
+    def forward(ctx, y: Tensor, geo: Tensor, plan: TensorPlan):
+        ctx.save_for_backward(y, geo)
+        ctx.plan = plan
+        if _kernels(y):
+            return _ext.ops().tn_embed_da(plan.dst, y.contiguous(), geo.contiguous())
+        return _reduce(y.index_select(0, plan.dst) * geo.unsqueeze(-1))
+
+    @staticmethod
+    def backward(ctx, h: Tensor):
+        y, geo = ctx.saved_tensors
+        plan = ctx.plan
+        dy = _Em.apply(h, geo, plan) if ctx.needs_input_grad[0] else None
+        dgeo = _Eg.apply(h, y, plan) if ctx.needs_input_grad[1] else None
+        return dy, dgeo, None
+
+
+class _Eg(torch.autograd.Function):
+    """``out[p, c] = sum_f a[p, g(c), f] y[dst, c, f]`` (the adjoint of the embedding in ``geo``)."""
+
+    @staticmethod
+    def forward(ctx, a: Tensor, y: Tensor, plan: TensorPlan):
+        ctx.save_for_backward(a, y)
+        ctx.plan = plan
+        if _kernels(a):
+            return _ext.ops().tn_embed_dg(plan.dst, a.contiguous(), y.contiguous())
+        return (_expand(a) * y.index_select(0, plan.dst)).sum(-1)
+
+    @staticmethod
+    def backward(ctx, k: Tensor):
+        a, y = ctx.saved_tensors
+        plan = ctx.plan
+        da = _Ea.apply(y, k, plan) if ctx.needs_input_grad[0] else None
+        dy = _Em.apply(a, k, plan) if ctx.needs_input_grad[1] else None
+        return da, dy, None
+
+
+def embedding(a: Tensor, geo: Tensor, plan: TensorPlan) -> Tensor:
+    """``Em(a, geo)``: pair parts ``a (E, 3, F)`` weighing the geometry rows ``geo (E, 10)``
+    (:func:`geometry_rows`) -> compact rows ``(n, 10, F)``."""
+    return _Em.apply(a, geo, plan)
+
+
+def geometry_rows(u: Tensor) -> Tensor:
+    """``[1, u_x, u_y, u_z, u_x u_x, u_x u_y, u_x u_z, u_y u_y, u_y u_z, u_z u_z]`` per pair."""
+    x, y, z = u.unbind(-1)
+    return torch.stack([torch.ones_like(x), x, y, z, x * x, x * y, x * z, y * y, y * z, z * z], -1)
+
+
 def messages(a: Tensor, x: Tensor, plan: TensorPlan) -> Tensor:
     """``M(a, x)``: filters ``a (E, 3, F)``, compact features ``x (n, 10, F)`` -> ``(n, 10, F)``."""
     return _M.apply(a, x, plan)
@@ -157,3 +232,34 @@ def sym_from_compact(s6: Tensor) -> Tensor:
     """Six distinct entries ``(n, 6, F)`` -> the full symmetric matrices ``(n, 3, 3, F)``."""
     xx, xy, xz, yy, yz, zz = s6.unbind(1)
     return torch.stack([xx, xy, xz, xy, yy, yz, xz, yz, zz], 1).reshape(s6.shape[0], 3, 3, s6.shape[2])
+
+
+class _MM3(torch.autograd.Function):
+    """``C = op(A) op(B)`` per atom and channel on ``(n, 3, 3, F)`` tensors (``op`` a transpose when
+    its flag is set); the backward products are of the same kind, so any order differentiates."""
+
+    @staticmethod
+    def forward(ctx, A: Tensor, B: Tensor, ta: bool, tb: bool):
+        ctx.save_for_backward(A, B)
+        ctx.t = (ta, tb)
+        if _kernels(A) and A.dtype == B.dtype:
+            return _ext.ops().tn_mm3(A.contiguous(), B.contiguous(), bool(ta), bool(tb))
+        a = A.transpose(1, 2) if ta else A
+        b = B.transpose(1, 2) if tb else B
+        return torch.einsum("nikf,nkjf->nijf", a, b)
+
+    @staticmethod
+    def backward(ctx, g: Tensor):
+        A, B = ctx.saved_tensors
+        ta, tb = ctx.t
+        dA = dB = None
+        if ctx.needs_input_grad[0]:
+            dA = _MM3.apply(g, B, False, not tb) if not ta else _MM3.apply(B, g, tb, True)
+        if ctx.needs_input_grad[1]:
+            dB = _MM3.apply(A, g, not ta, False) if not tb else _MM3.apply(g, A, True, ta)
+        return dA, dB, None, None
+
+
+def matmul3(A: Tensor, B: Tensor, ta: bool = False, tb: bool = False) -> Tensor:
+    """Per atom and channel 3x3 matrix products of ``(n, 3, 3, F)`` tensors."""
+    return _MM3.apply(A, B, ta, tb)

@@ -9,9 +9,11 @@
   launched with its count and summed device time, plus the share of device time and launches
   that belong to this package's own kernels (those compiled into ``xnn_b200/_C.so``).
 
-``python -m xnn_b200.utils.profiling [--model tensornet]`` prints that table for one eager training
-step of the benchmark configuration (MACE: 64 organic molecules, 96 channels; TensorNet: 32
-crystals, 64 channels, energy + force + stress loss).
+``python -m xnn_b200.utils.profiling [--model tensornet|pme]`` prints that table for one eager
+training step of the benchmark configuration (MACE: 64 organic molecules, 96 channels;
+TensorNet: 32 crystals, 64 channels, energy + force + stress loss) or one evaluation of the
+polarizable-multipole PME workload (``--batch`` atoms, 100,000 by default) or one step of the
+domain-decomposed MD of a water box (``--model md``, ``--batch`` atoms, 1,000,000 by default).
 """
 from __future__ import annotations
 
@@ -32,7 +34,8 @@ OWN_KERNELS = ("conv_gather", "conv_edge", "conv_scatter", "symcon_", "edge_geom
                "radial_act_kernel", "radial_dact_kernel", "nb_count", "nb_write", "mp_real_kernel",
                "pme_spread_kernel", "pme_gather_kernel", "xnn_", "nl_", "mace_", "tn_", "pme_", "halo_",
                "adam_", "grad_", "seg_", "dd_", "fft_", "eeq_", "atm_", "amoeba_", "reax_", "sqm_", "node_",
-               "species_sort", "dual_edge_kernel", "dual_scatter_kernel", "dipole_pairs", "dipole_matvec")
+               "species_sort", "dual_edge_kernel", "dual_scatter_kernel", "dipole_pairs", "dipole_matvec",
+               "segment_rows_sum", "edge_forces_kernel")
 
 
 def is_own_kernel(name: str) -> bool:
@@ -127,17 +130,53 @@ def _tensornet_step(batch: int):
     return lambda: tr.train_step(b)
 
 
+def _pme_eval(atoms: int):
+    from ..ffnn import multipoles as MP
+    from ..ffnn.water import multipole_water
+    dev = torch.device("cuda", torch.cuda.current_device())
+    w = multipole_water(atoms, seed=0, device=dev)
+    setup = MP.EwaldSetup(alpha=0.4, cutoff=7.0, mesh=(128, 128, 128), order=5, fft_dtype=torch.float32)
+    mod = MP.PolarizableMultipoles(setup, tol_debye=1e-5, max_iter=100)
+    return lambda: mod(w["pos"], w["cell"], w["q"], w["d"], w["Q"], w["pol"], w["molecule"])
+
+
+def _md_step(atoms: int, chunk: int = 4_000_000):
+    from ..data import synthetic
+    from ..data.atomic_graph import AtomicGraph
+    from ..deploy.md import VelocityVerlet
+    from ..models.mace import MACE
+    from ..parallel.domain import DomainParallel
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(4321)
+    model = MACE(species=[1, 6, 7, 8, 9, 16, 17], cutoff=4.5, num_channels=96, n_rbf=8, num_interactions=2,
+                 max_ell=3, correlation=3, avg_num_neighbors=38.0).to(dev).eval()
+    model.edge_chunk = chunk
+    s = synthetic.water_box(atoms, seed=0)
+    n = int(s["pos"].shape[0])
+    g = AtomicGraph(pos=s["pos"].to(dev), atomic_numbers=s["atomic_numbers"].to(dev),
+                    edge_index=torch.zeros(2, 0, dtype=torch.long, device=dev),
+                    cell_shifts=torch.zeros(0, 3, dtype=torch.long, device=dev),
+                    batch=torch.zeros(n, dtype=torch.long, device=dev), n_atoms=torch.tensor([n], device=dev),
+                    cell=s["cell"][None].to(dev), pbc=s["pbc"][None].to(dev))
+    md = VelocityVerlet(DomainParallel(model, skin=1.0), g, dt_fs=0.5, temperature_k=300.0, seed=7)
+    return lambda: md.step()
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--model", default="mace", choices=["mace", "tensornet"])
+    ap.add_argument("--model", default="mace", choices=["mace", "tensornet", "pme", "md"])
     ap.add_argument("--batch", type=int, default=None, help="structures per step (64 MACE, 32 TensorNet)")
     ap.add_argument("--top", type=int, default=40)
     ap.add_argument("--json", default=None, help="also write the table as JSON to this path")
     a = ap.parse_args(argv)
     if a.model == "mace":
         fn = _mace_step(a.batch or 64)
-    else:
+    elif a.model == "tensornet":
         fn = _tensornet_step(a.batch or 32)
+    elif a.model == "pme":
+        fn = _pme_eval(a.batch or 100_000)
+    else:
+        fn = _md_step(a.batch or 1_000_000)
     tab = kernel_table(fn, warmup=3)
     print(f"launches {tab['launches']} (own {tab['own_launches']}), device time {tab['device_us']} us, "
           f"own-kernel share {tab['own_time_share']}")
