@@ -1,6 +1,6 @@
 """Configuration dataclasses and their loaders."""
 from .schema import (Config, DataConfig, IgnoredOptionWarning, ModelConfig, OptimConfig,
-                     TrainerConfig, from_argparse, from_dict, from_yaml)
+                     TrainerConfig, apply_overrides, from_argparse, from_dict, from_hydra, from_yaml)
 
 __all__ = ["Config", "DataConfig", "IgnoredOptionWarning", "ModelConfig", "OptimConfig",
-           "TrainerConfig", "from_argparse", "from_dict", "from_yaml"]
+           "TrainerConfig", "apply_overrides", "from_argparse", "from_dict", "from_hydra", "from_yaml"]

@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import ast
 import copy
+import os
 import warnings
 from dataclasses import asdict, dataclass, field, fields, is_dataclass
 from typing import Any, Dict, List, Optional
@@ -207,6 +208,20 @@ def from_dict(d: Dict[str, Any], overrides: Optional[Dict[str, Any]] = None) -> 
     model = d.get("model", {})
     if isinstance(model, str):
         d["model"] = {"name": model}
+    elif isinstance(model, dict):
+        # a model option that is not a core field is a family option (model.extra), as in the
+        # family config files; upstream spellings of the core fields are translated first
+        core = {f.name for f in fields(ModelConfig)}
+        mod_keys = {"r_max": "cutoff", "num_channels": "n_features", "num_interactions": "n_interactions",
+                    "num_radial_basis": "n_rbf", "num_bessel": "n_rbf"}
+        folded = {}
+        for k in list(model):
+            if k in mod_keys and mod_keys[k] not in model:
+                model[mod_keys[k]] = model.pop(k)
+            elif k not in core:
+                folded[k] = model.pop(k)
+        if folded:
+            model["extra"] = {**folded, **dict(model.get("extra") or {})}
     cfg = _build(Config, d, "")
     if cfg.model.name == "mace":
         base = _default_mace_extra()
@@ -216,10 +231,38 @@ def from_dict(d: Dict[str, Any], overrides: Optional[Dict[str, Any]] = None) -> 
     return cfg
 
 
+def _compose_defaults(d: Dict[str, Any], base_dir: str) -> Dict[str, Any]:
+    """Hydra-style ``defaults``: ``[{model: schnet}, {data: default}, _self_]`` reads
+    ``<dir>/model/schnet.yaml`` and ``<dir>/data/default.yaml`` into those sections; the file's
+    own keys win when ``_self_`` comes last (the default), the groups' when it comes first."""
+    import yaml
+    defaults = d.pop("defaults", None)
+    if not defaults:
+        return d
+    self_last = not (defaults and defaults[0] == "_self_")
+    groups: Dict[str, Any] = {}
+    for item in defaults:
+        if item == "_self_" or not isinstance(item, dict):
+            continue
+        for group, name in item.items():
+            with open(os.path.join(base_dir, str(group), f"{name}.yaml")) as f:
+                groups[str(group)] = yaml.safe_load(f) or {}
+    for group, body in groups.items():
+        mine = d.get(group)
+        if isinstance(mine, dict) and isinstance(body, dict):
+            d[group] = {**body, **mine} if self_last else {**mine, **body}
+        elif mine is None or not self_last:
+            d[group] = body
+    return d
+
+
 def from_yaml(path: str, overrides: Optional[Dict[str, Any]] = None) -> Config:
+    """A run config from a YAML file; a ``defaults`` list composes group files from the same
+    directory tree (the shipped ``configs/`` layout: ``model/<family>.yaml``, ``data/*.yaml``)."""
     import yaml
     with open(path) as f:
         d = yaml.safe_load(f) or {}
+    d = _compose_defaults(d, os.path.dirname(os.path.abspath(path)))
     return from_dict(d, overrides)
 
 
@@ -232,3 +275,40 @@ def from_argparse(args) -> Config:
     if getattr(args, "config", None):
         return from_yaml(args.config, overrides)
     return from_dict({}, overrides)
+
+
+def _plain(node):
+    """A nested plain container of a mapping / sequence tree (OmegaConf nodes included)."""
+    if isinstance(node, (str, bytes, int, float, bool)) or node is None:
+        return node
+    if hasattr(node, "items"):
+        return {str(k): _plain(v) for k, v in node.items()}
+    if isinstance(node, (list, tuple)) or (hasattr(node, "__iter__") and hasattr(node, "__len__")):
+        return [_plain(v) for v in node]
+    return node
+
+
+def from_hydra(dict_config) -> Config:
+    """A :class:`Config` from a Hydra / OmegaConf ``DictConfig`` (interpolations resolved when
+    OmegaConf is installed; any mapping otherwise), through :func:`from_dict`. Parity:
+    ``src/xnn/common/config/loaders.py:182``."""
+    try:
+        from omegaconf import OmegaConf
+        container = OmegaConf.to_container(dict_config, resolve=True)
+    except (ModuleNotFoundError, ValueError):
+        container = _plain(dict_config)
+    return from_dict(container)
+
+
+def apply_overrides(cfg: Config, overrides) -> Config:
+    """Apply ``"a.b=c"`` dotted overrides (values parsed as Python literals, else strings) and
+    return the new config; an entry without ``=`` is ignored with an
+    :class:`IgnoredOptionWarning`. The same syntax as ``--set`` on the command line."""
+    parsed = {}
+    for item in overrides or []:
+        if "=" not in item:
+            warnings.warn(f"override {item!r} has no '='", IgnoredOptionWarning, stacklevel=2)
+            continue
+        k, _, v = item.partition("=")
+        parsed[k.strip()] = _coerce(v.strip())
+    return from_dict(cfg.to_dict(), parsed)

@@ -22,6 +22,9 @@ cudaError_t dipole_pairs(int64_t P, const double* pos, const double* cell, const
 cudaError_t dipole_matvec(int64_t P, const int64_t* pi, const int64_t* pj, const double* v, const double* b1,
                           const double* b2, const double* d, double* field, cudaStream_t s);
 
+cudaError_t dipole_csr_matvec(int64_t n, const int64_t* ptr, const int* partner, const double* v, const double* b1,
+                              const double* b2, const double* d, double* field, cudaStream_t s);
+
 namespace {
 
 void need(const torch::Tensor& t, torch::ScalarType st, const char* name) {
@@ -133,6 +136,25 @@ torch::Tensor dipole_matvec_op(torch::Tensor I, torch::Tensor J, torch::Tensor v
   return field;
 }
 
+// field (n, 3) of dipoles d from receiver-ordered pair entries (ptr (n + 1), partner, v, b1, b2)
+torch::Tensor dipole_csr_matvec_op(torch::Tensor ptr, torch::Tensor partner, torch::Tensor v, torch::Tensor b1,
+                                   torch::Tensor b2, torch::Tensor d) {
+  need(v, torch::kFloat64, "v"); need(b1, torch::kFloat64, "b1"); need(b2, torch::kFloat64, "b2");
+  need(d, torch::kFloat64, "d");
+  TORCH_CHECK(ptr.is_cuda() && ptr.scalar_type() == torch::kInt64 && ptr.is_contiguous(), "dipole_csr_matvec: ptr");
+  TORCH_CHECK(partner.is_cuda() && partner.scalar_type() == torch::kInt32 && partner.is_contiguous(),
+              "dipole_csr_matvec: int32 partner");
+  c10::cuda::CUDAGuard g(d.device());
+  const int64_t n = ptr.numel() - 1;
+  TORCH_CHECK(d.numel() == 3 * n, "dipole_csr_matvec: d (n, 3)");
+  auto field = torch::empty({n, 3}, d.options());
+  cudaError_t err = dipole_csr_matvec(n, ptr.data_ptr<int64_t>(), partner.data_ptr<int>(), v.data_ptr<double>(),
+                                      b1.data_ptr<double>(), b2.data_ptr<double>(), d.data_ptr<double>(),
+                                      field.data_ptr<double>(), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(err == cudaSuccess, "dipole_csr_matvec: ", cudaGetErrorString(err));
+  return field;
+}
+
 }  // namespace
 
 
@@ -140,6 +162,7 @@ void register_ffnn(pybind11::module& m) {
   m.def("mp_real", &mp_real_op);
   m.def("dipole_pairs", &dipole_pairs_op);
   m.def("dipole_matvec", &dipole_matvec_op);
+  m.def("dipole_csr_matvec", &dipole_csr_matvec_op);
   m.def("pme_spread", &pme_spread_op);
   m.def("pme_gather", &pme_gather_op);
 }

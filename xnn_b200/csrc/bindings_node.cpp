@@ -317,8 +317,10 @@ std::vector<torch::Tensor> mace_dual_reverse_op(torch::Tensor dst_ptr, torch::Te
   TORCH_CHECK(Y.is_contiguous() && Yd.is_contiguous() && rdot.is_contiguous() && u.is_contiguous(),
               "mace_dual_reverse: contiguous inputs");
   c10::cuda::CUDAGuard guard(G.device());
-  auto Rbar = torch::empty({E, P, C}, G.options());
-  auto Rdbar = torch::empty({E, P, C}, G.options());
+  // R_bar and R'_bar stacked in one buffer (the radial reverse takes them as one (2E, P*C) matrix)
+  auto RR = torch::empty({2 * E, P, C}, G.options());
+  auto Rbar = RR.narrow(0, 0, E);
+  auto Rdbar = RR.narrow(0, E, E);
   auto T14 = torch::empty({E, P, C}, G.options());
   auto T2 = torch::empty({E, P, C}, G.options());
   auto ub = torch::empty({N, C}, G.options());

@@ -20,6 +20,9 @@ cudaError_t tn_embed_dg(int64_t E, int F, const int64_t* dst, const T* a, const 
 
 template <typename T>
 cudaError_t tn_mm3(int64_t N, int F, bool ta, bool tb, const T* A, const T* B, T* C, cudaStream_t s);
+template <typename T>
+cudaError_t tn_plin(int64_t N, int F, int K, int K1, int O, int O1, const T* in1, const T* in2, const double* M,
+                    T* out1, T* out2, cudaStream_t s);
 
 namespace {
 
@@ -177,6 +180,33 @@ torch::Tensor tn_mm3_op(torch::Tensor A, torch::Tensor B, bool ta, bool tb) {
   TORCH_CHECK(e == cudaSuccess, "tn_mm3: ", cudaGetErrorString(e));
   return C;
 }
+// [out1; out2] = M [in1; in2] per atom and channel (rows of (N, K, F) tensors); in2 and out2 may
+// be empty (O1 == O, K1 == K); M (O, K) float64 on the device
+std::vector<torch::Tensor> tn_plin_op(torch::Tensor in1, c10::optional<torch::Tensor> in2, torch::Tensor M,
+                                      int64_t O1) {
+  const c10::cuda::CUDAGuard guard(in1.device());
+  check(in1, "in1", in1.scalar_type());
+  check(M, "M", torch::kFloat64);
+  const bool two = in2.has_value() && in2->defined();
+  if (two) check(*in2, "in2", in1.scalar_type());
+  TORCH_CHECK(in1.dim() == 3 && M.dim() == 2, "tensornet plin: in (N, K, F), M (O, K)");
+  const int64_t N = in1.size(0), F = in1.size(2), K1 = in1.size(1);
+  const int64_t K = K1 + (two ? in2->size(1) : 0), O = M.size(0);
+  TORCH_CHECK(M.size(1) == K && O1 >= 1 && O1 <= O, "tensornet plin: M columns / O1");
+  if (two) TORCH_CHECK(in2->size(0) == N && in2->size(2) == F, "tensornet plin: in2 shape");
+  auto out1 = torch::empty({N, O1, F}, in1.options());
+  auto out2 = O1 < O ? torch::empty({N, O - O1, F}, in1.options()) : torch::Tensor();
+  auto s = at::cuda::getCurrentCUDAStream();
+  XNN_TN_DISPATCH(in1.scalar_type(),
+                  tn_plin<float>(N, (int)F, (int)K, (int)K1, (int)O, (int)O1, in1.data_ptr<float>(),
+                                 two ? in2->data_ptr<float>() : nullptr, M.data_ptr<double>(), out1.data_ptr<float>(),
+                                 O1 < O ? out2.data_ptr<float>() : nullptr, s),
+                  tn_plin<double>(N, (int)F, (int)K, (int)K1, (int)O, (int)O1, in1.data_ptr<double>(),
+                                  two ? in2->data_ptr<double>() : nullptr, M.data_ptr<double>(),
+                                  out1.data_ptr<double>(), O1 < O ? out2.data_ptr<double>() : nullptr, s))
+  TORCH_CHECK(e == cudaSuccess, "tn_plin: ", cudaGetErrorString(e));
+  return {out1, out2};
+}
 #undef XNN_TN_DISPATCH
 
 }  // namespace
@@ -188,4 +218,5 @@ void register_tensornet(pybind11::module& m) {
   m.def("tn_embed_da", &tn_embed_da_op);
   m.def("tn_embed_dg", &tn_embed_dg_op);
   m.def("tn_mm3", &tn_mm3_op);
+  m.def("tn_plin", &tn_plin_op);
 }

@@ -11,7 +11,9 @@
 // B_n of erfc(a r)/r follow the recursion B_n = ((2n - 1) B_{n-1} + (2 a^2)^n / (a sqrt(pi))
 // exp(-a^2 r^2)) / r^2 (B_0 = erfc(a r) / r); the bare 1/r kernel has B_n = (2n - 1)!! / r^(2n+1).
 // dipole_pairs_kernel writes (v, B_1, B_2) per pair; dipole_matvec_kernel applies the operator,
-// one thread per pair, accumulating both sites' fields with float64 atomics.
+// one thread per pair, accumulating both sites' fields with float64 atomics;
+// dipole_csr_matvec_kernel applies it from a receiver-ordered copy of the pairs (each twice),
+// one warp per site and no atomics (the solve's iterations use this one).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -77,7 +79,51 @@ __global__ void dipole_matvec_kernel(int64_t P, const int64_t* __restrict__ pi, 
   atomicAdd(field + 3 * b + 2, -(B1 * az - B2 * va * vz));
 }
 
+// The same product over a receiver-ordered list of directed pair entries (every pair twice):
+// one warp per site, lanes over its entries, fixed-order warp reduction, no atomics. Entry k of
+// site a holds the partner b, the pair vector (its sign cancels) and B_1, B_2.
+__global__ void __launch_bounds__(256) dipole_csr_matvec_kernel(int64_t n, const int64_t* __restrict__ ptr,
+                                                                const int* __restrict__ partner,
+                                                                const double* __restrict__ v,
+                                                                const double* __restrict__ b1,
+                                                                const double* __restrict__ b2,
+                                                                const double* __restrict__ d,
+                                                                double* __restrict__ field) {
+  const int64_t a = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (a >= n) return;
+  double f0 = 0.0, f1 = 0.0, f2 = 0.0;
+  for (int64_t k = ptr[a] + lane; k < ptr[a + 1]; k += 32) {
+    const int b = partner[k];
+    const double vx = v[3 * k], vy = v[3 * k + 1], vz = v[3 * k + 2];
+    const double B1 = b1[k], B2 = b2[k];
+    const double dx = __ldg(d + 3 * (int64_t)b), dy = __ldg(d + 3 * (int64_t)b + 1), dz = __ldg(d + 3 * (int64_t)b + 2);
+    const double dv = dx * vx + dy * vy + dz * vz;
+    f0 -= B1 * dx - B2 * dv * vx;
+    f1 -= B1 * dy - B2 * dv * vy;
+    f2 -= B1 * dz - B2 * dv * vz;
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    f0 += __shfl_xor_sync(0xffffffffu, f0, off);
+    f1 += __shfl_xor_sync(0xffffffffu, f1, off);
+    f2 += __shfl_xor_sync(0xffffffffu, f2, off);
+  }
+  if (lane == 0) {
+    field[3 * a] = f0;
+    field[3 * a + 1] = f1;
+    field[3 * a + 2] = f2;
+  }
+}
+
 }  // namespace
+
+cudaError_t dipole_csr_matvec(int64_t n, const int64_t* ptr, const int* partner, const double* v, const double* b1,
+                              const double* b2, const double* d, double* field, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  dipole_csr_matvec_kernel<<<(unsigned)((n + 7) / 8), 256, 0, s>>>(n, ptr, partner, v, b1, b2, d, field);
+  return cudaGetLastError();
+}
 
 cudaError_t dipole_pairs(int64_t P, const double* pos, const double* cell, const int64_t* pi, const int64_t* pj,
                          const int64_t* shift, const bool* excluded, const double* pol, double alpha, double thole,

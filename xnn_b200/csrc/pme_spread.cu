@@ -6,9 +6,10 @@
 // G[b][a] = du_a/dr_b). The adjoint kernel reads a mesh potential phi and returns, per site,
 // dE/dd = G (sum phi dW/du) and dE/dr = G (sum phi d(L W)/du) (third spline derivatives for the
 // quadrupoles). Only planes z0 <= k_3 < z0 + nz are touched (a z-slab of a distributed mesh).
-// Spreading accumulates with float atomics (one thread per site and (x, y) stencil column); the
-// gather is one warp per site, lanes over the stencil columns, with a warp reduction (no
-// atomics). Both are instantiated for spline orders 4-6 so the spline rows stay in registers.
+// Both run one warp per site: three lanes evaluate the spline rows of the three axes once and
+// share them through shared memory, then each lane owns one (x, y) stencil column. Spreading
+// accumulates with float atomics; the gather ends in a fixed-order warp reduction (no atomics).
+// Both are instantiated for spline orders 4-6 so the rows stay in registers.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -103,38 +104,48 @@ __device__ __forceinline__ void spline_derivs_t(double t, double th[ND + 1][P]) 
   }
 }
 
-// the entry j of a register row (unrolled select: no local-memory indexing)
-template <int P>
-__device__ __forceinline__ double pick(const double row[P], int j) {
-  double v = row[0];
+// One warp per site (8 sites per 256-thread block): lanes 0-2 evaluate the spline rows of the
+// three axes once and share them through shared memory; lane c < P*P then owns the (x, y) stencil
+// column (c / P, c % P) and its P planes.
+template <int P, int ND>
+struct SiteSplines {
+  double th[3][ND + 1][P];
+};
+
+template <int P, int ND>
+__device__ __forceinline__ void share_splines(const Site& s, int lane, SiteSplines<P, ND>& sh) {
+  if (lane < 3) {
+    double th[ND + 1][P];
+    const double t = lane == 0 ? s.t[0] : (lane == 1 ? s.t[1] : s.t[2]);   // no indexed local array
+    spline_derivs_t<P, ND>(t, th);
 #pragma unroll
-  for (int q = 1; q < P; ++q) v = j == q ? row[q] : v;
-  return v;
+    for (int k = 0; k <= ND; ++k)
+#pragma unroll
+      for (int j = 0; j < P; ++j) sh.th[lane][k][j] = th[k][j];
+  }
+  __syncwarp();
 }
 
-// Spreading: one thread per site and (x, y) stencil column, the column's P planes in registers.
 template <int P, int ND>
 __global__ void __launch_bounds__(256) pme_spread_kernel(int64_t n, const double* __restrict__ pos,
                                                          const double* __restrict__ G, int K1, int K2, int K3, int z0,
                                                          int nz, const double* __restrict__ q,
                                                          const double* __restrict__ d, const double* __restrict__ Q,
                                                          float* __restrict__ grid) {
-  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int64_t i = tid / (P * P);
+  __shared__ SiteSplines<P, ND> sh[8];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = blockIdx.x * (int64_t)8 + w;
   if (i >= n) return;
-  const int col = (int)(tid - i * (P * P));
-  const int jx = col / P, jy = col - jx * P;
   const int K[3] = {K1, K2, K3};
   const Site s = site_of(pos, i, G, K);
-  double tx[ND + 1][P], ty[ND + 1][P], tz[ND + 1][P];
-  spline_derivs_t<P, ND>(s.t[0], tx);
-  spline_derivs_t<P, ND>(s.t[1], ty);
-  spline_derivs_t<P, ND>(s.t[2], tz);
+  share_splines<P, ND>(s, lane, sh[w]);
+  if (lane >= P * P) return;
+  const int jx = lane / P, jy = lane - jx * P;
   double ax[ND + 1], ay[ND + 1];
 #pragma unroll
   for (int k = 0; k <= ND; ++k) {
-    ax[k] = pick<P>(tx[k], jx);
-    ay[k] = pick<P>(ty[k], jy);
+    ax[k] = sh[w].th[0][k][jx];
+    ay[k] = sh[w].th[1][k][jy];
   }
   double du[3], Qu[9];
   site_multipoles(i, d, Q, G, du, Qu);
@@ -145,25 +156,27 @@ __global__ void __launch_bounds__(256) pme_spread_kernel(int64_t n, const double
   for (int jz = 0; jz < P; ++jz) {
     const int zl = wrap(s.base[2] - jz, K3) - z0;
     if (zl < 0 || zl >= nz) continue;
-    double v = qi * ax[0] * ay[0] * tz[0][jz];
+    double tz[ND + 1];
+#pragma unroll
+    for (int k = 0; k <= ND; ++k) tz[k] = sh[w].th[2][k][jz];
+    double v = qi * ax[0] * ay[0] * tz[0];
     if (ND >= 1 && d)
-      v += du[0] * ax[ND >= 1 ? 1 : 0] * ay[0] * tz[0][jz] + du[1] * ax[0] * ay[ND >= 1 ? 1 : 0] * tz[0][jz] +
-           du[2] * ax[0] * ay[0] * tz[ND >= 1 ? 1 : 0][jz];
+      v += du[0] * ax[ND >= 1 ? 1 : 0] * ay[0] * tz[0] + du[1] * ax[0] * ay[ND >= 1 ? 1 : 0] * tz[0] +
+           du[2] * ax[0] * ay[0] * tz[ND >= 1 ? 1 : 0];
     if (ND >= 2 && Q) {
 #pragma unroll
       for (int a = 0; a < 3; ++a)
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
           const int ox = (a == 0) + (c == 0), oy = (a == 1) + (c == 1), oz = (a == 2) + (c == 2);
-          v += (Qu[3 * a + c] / 3.0) * ax[ox < ND ? ox : ND] * ay[oy < ND ? oy : ND] * tz[oz < ND ? oz : ND][jz];
+          v += (Qu[3 * a + c] / 3.0) * ax[ox < ND ? ox : ND] * ay[oy < ND ? oy : ND] * tz[oz < ND ? oz : ND];
         }
     }
     atomicAdd(col_ptr + zl, (float)v);
   }
 }
 
-// Gather (the spreading's adjoint): one warp per site, lanes over the P x P columns, each lane's
-// P planes in registers, then a fixed-order warp reduction of the six sums.
+// Gather (the spreading's adjoint): same layout, then a fixed-order warp reduction of the six sums.
 template <int P, int ND>
 __global__ void __launch_bounds__(256) pme_gather_kernel(int64_t n, const double* __restrict__ pos,
                                                          const double* __restrict__ G, int K1, int K2, int K3, int z0,
@@ -171,24 +184,22 @@ __global__ void __launch_bounds__(256) pme_gather_kernel(int64_t n, const double
                                                          const double* __restrict__ d, const double* __restrict__ Q,
                                                          const float* __restrict__ phi, double* __restrict__ gd,
                                                          double* __restrict__ gpos) {
-  const int64_t i = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+  __shared__ SiteSplines<P, ND> sh[8];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = blockIdx.x * (int64_t)8 + w;
   if (i >= n) return;
   const int K[3] = {K1, K2, K3};
   const Site s = site_of(pos, i, G, K);
+  share_splines<P, ND>(s, lane, sh[w]);
   double P1[3] = {0, 0, 0};      // sum phi dW/du_a
   double Fu[3] = {0, 0, 0};      // sum phi d(L W)/du_a
   if (lane < P * P) {
     const int jx = lane / P, jy = lane - (lane / P) * P;
-    double tx[ND + 1][P], ty[ND + 1][P], tz[ND + 1][P];
-    spline_derivs_t<P, ND>(s.t[0], tx);
-    spline_derivs_t<P, ND>(s.t[1], ty);
-    spline_derivs_t<P, ND>(s.t[2], tz);
     double ax[ND + 1], ay[ND + 1];
 #pragma unroll
     for (int k = 0; k <= ND; ++k) {
-      ax[k] = pick<P>(tx[k], jx);
-      ay[k] = pick<P>(ty[k], jy);
+      ax[k] = sh[w].th[0][k][jx];
+      ay[k] = sh[w].th[1][k][jy];
     }
     double du[3], Qu[9];
     site_multipoles(i, d, Q, G, du, Qu);
@@ -200,9 +211,12 @@ __global__ void __launch_bounds__(256) pme_gather_kernel(int64_t n, const double
       const int zl = wrap(s.base[2] - jz, K3) - z0;
       if (zl < 0 || zl >= nz) continue;
       const double f = (double)__ldg(col_ptr + zl);
+      double tz[ND + 1];
+#pragma unroll
+      for (int k = 0; k <= ND; ++k) tz[k] = sh[w].th[2][k][jz];
       // derivative of W of multi-order (ox, oy, oz)
       auto W = [&](int ox, int oy, int oz) {
-        return ax[ox < ND ? ox : ND] * ay[oy < ND ? oy : ND] * tz[oz < ND ? oz : ND][jz];
+        return ax[ox < ND ? ox : ND] * ay[oy < ND ? oy : ND] * tz[oz < ND ? oz : ND];
       };
       P1[0] += f * W(1, 0, 0);
       P1[1] += f * W(0, 1, 0);
@@ -250,7 +264,7 @@ __global__ void __launch_bounds__(256) pme_gather_kernel(int64_t n, const double
 template <int P>
 cudaError_t spread_p(int64_t n, const double* pos, const double* G, int K1, int K2, int K3, int z0, int nz,
                      const double* q, const double* d, const double* Q, float* grid, cudaStream_t s) {
-  const unsigned blocks = (unsigned)((n * P * P + 255) / 256);
+  const unsigned blocks = (unsigned)((n + 7) / 8);          // 8 sites (warps) per block
   if (Q) pme_spread_kernel<P, 2><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, grid);
   else if (d) pme_spread_kernel<P, 1><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, grid);
   else pme_spread_kernel<P, 0><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, grid);

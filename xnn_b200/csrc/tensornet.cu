@@ -233,6 +233,34 @@ __global__ void __launch_bounds__(256) tn_mm3_kernel(int64_t NF, int F, const T*
     }
 }
 
+// Constant linear maps per atom and channel: [out1; out2][o] = sum_k M[o][k] [in1; in2][k] with
+// in1 (N, K1, F), in2 (N, K - K1, F) (absent when K1 == K), out1 (N, O1, F), out2 (N, O - O1, F);
+// M (O x K, float64 host-built, converted to T) in shared memory. One thread per (atom, channel).
+template <typename T, int K, int O>
+__global__ void __launch_bounds__(256) tn_plin_kernel(int64_t NF, int F, int K1, int O1, const T* __restrict__ in1,
+                                                      const T* __restrict__ in2, const double* __restrict__ M,
+                                                      T* __restrict__ out1, T* __restrict__ out2) {
+  __shared__ T m[O * K];
+  for (int t = threadIdx.x; t < O * K; t += blockDim.x) m[t] = (T)M[t];
+  __syncthreads();
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= NF) return;
+  const int64_t n = t / F;
+  const int f = (int)(t - n * F);
+  T x[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+    x[k] = k < K1 ? __ldg(in1 + (n * K1 + k) * F + f) : __ldg(in2 + (n * (K - K1) + (k - K1)) * F + f);
+#pragma unroll
+  for (int o = 0; o < O; ++o) {
+    T acc = T(0);
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc += m[o * K + k] * x[k];
+    if (o < O1) out1[(n * O1 + o) * F + f] = acc;
+    else out2[(n * (O - O1) + (o - O1)) * F + f] = acc;
+  }
+}
+
 inline int cpl_of(int F) { return F <= 32 ? 1 : (F <= 64 ? 2 : (F <= 96 ? 3 : 4)); }
 
 }  // namespace
@@ -323,6 +351,31 @@ cudaError_t tn_mm3(int64_t N, int F, bool ta, bool tb, const T* A, const T* B, T
 }
 template cudaError_t tn_mm3<float>(int64_t, int, bool, bool, const float*, const float*, float*, cudaStream_t);
 template cudaError_t tn_mm3<double>(int64_t, int, bool, bool, const double*, const double*, double*, cudaStream_t);
+
+template <typename T>
+cudaError_t tn_plin(int64_t N, int F, int K, int K1, int O, int O1, const T* in1, const T* in2, const double* M,
+                    T* out1, T* out2, cudaStream_t s) {
+  const int64_t NF = N * F;
+  if (NF == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((NF + 255) / 256);
+#define XNN_PLIN(KK, OO)                                                                                 \
+  if (K == KK && O == OO) {                                                                              \
+    tn_plin_kernel<T, KK, OO><<<grid, 256, 0, s>>>(NF, F, K1, O1, in1, in2, M, out1, out2);             \
+    return cudaGetLastError();                                                                           \
+  }
+  XNN_PLIN(27, 19)
+  XNN_PLIN(19, 27)
+  XNN_PLIN(10, 9)
+  XNN_PLIN(9, 10)
+  XNN_PLIN(27, 9)
+  XNN_PLIN(9, 27)
+#undef XNN_PLIN
+  return cudaErrorInvalidValue;
+}
+template cudaError_t tn_plin<float>(int64_t, int, int, int, int, int, const float*, const float*, const double*,
+                                    float*, float*, cudaStream_t);
+template cudaError_t tn_plin<double>(int64_t, int, int, int, int, int, const double*, const double*, const double*,
+                                     double*, double*, cudaStream_t);
 
 #define XNN_TN_EMBED(T)                                                                                          \
   template cudaError_t tn_embed<T>(int, int, const int64_t*, const int64_t*, const T*, const T*, T*, cudaStream_t); \

@@ -417,10 +417,26 @@ class DipoleOperator:
             self.b1 = torch.where(ex, Be[1], b1)
             self.b2 = torch.where(ex, Be[2], b2)
 
+    def _csr(self):
+        """The pairs twice, ordered by receiving site (built once per solve): the warp-per-site
+        product needs no atomics."""
+        if not hasattr(self, "_rows"):
+            n = self.pos.shape[0]
+            recv = torch.cat([self.i, self.j])
+            order = torch.sort(recv, stable=True)[1]
+            pair = order % self.i.shape[0]
+            ptr = torch.zeros(n + 1, dtype=torch.long, device=recv.device)
+            ptr[1:] = torch.cumsum(torch.bincount(recv, minlength=n), 0)
+            partner = torch.cat([self.j, self.i]).index_select(0, order).to(torch.int32)
+            self._rows = (ptr, partner, self.v.index_select(0, pair).contiguous(),
+                          self.b1.index_select(0, pair).contiguous(), self.b2.index_select(0, pair).contiguous())
+        return self._rows
+
     def real(self, d: Tensor) -> Tensor:
         if self.kernel:
             from .. import _ext
-            return _ext.ops().dipole_matvec(self.i, self.j, self.v, self.b1, self.b2, d.contiguous())
+            ptr, partner, v, b1, b2 = self._csr()
+            return _ext.ops().dipole_csr_matvec(ptr, partner, v, b1, b2, d.contiguous())
         v, b1, b2 = self.v, self.b1[:, None], self.b2[:, None]
         dj, di = d[self.j], d[self.i]
         fi = -(b1 * dj - b2 * (dj * v).sum(-1, keepdim=True) * v)

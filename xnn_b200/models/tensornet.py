@@ -8,6 +8,13 @@ interaction normalises ``X``, mixes its parts, sums messages ``f_ij (I_j, A_j, S
 pairs included), forms ``C = YM + MY`` (O(3)) or ``2 YM`` (SO(3)), mixes again and updates
 ``X <- X + dX + dX^2``; the readout takes ``(|I|^2, |A|^2, |S|^2)`` through a LayerNorm and a
 linear layer, then an MLP. Edge vectors are ``pos[i] - pos[j]`` (receiver minus sender).
+
+Evaluation plan (same numbers as the part-by-part formulas): the three channel linears of a
+tensor's parts commute with the split into parts, so they run as one tensor-core product over
+all nine entries, and the split / recombination is one constant per-entry linear map
+(:class:`~xnn_b200.ops.tensornet_ops.LinearMap`); messages and the embedding sum onto the atoms
+in one kernel each over compact rows, and the per-atom 3x3 products are one kernel
+(``csrc/tensornet.cu``). Every piece differentiates to any order (force and stress training).
 """
 from __future__ import annotations
 
@@ -21,25 +28,14 @@ from ..data import AtomicGraph
 from ..nn import CosineCutoff, make_radial_basis
 from ..nn.blocks import GatedMLP, make_activation
 from ..ops import gemm
-from ..ops.scatter import refresh_ghosts, scatter_sum
-from ..ops.tensornet_ops import (TensorPlan, embedding, geometry_rows, matmul3, messages, sym_from_compact,
-                                 to_compact)
+from ..ops.scatter import refresh_ghosts
+from ..ops.tensornet_ops import (EMBEDDING_FULL, FULL_FROM_COMPACT, RECOMPOSE, Y_AND_COMPACT, TensorPlan,
+                                 embedding, geometry_rows, matmul3, messages)
 from .base import InteratomicPotential
 from .registry import register_model
 
 _READOUTS = ("mlp", "gated")
 _GROUPS = ("O(3)", "SO(3)")
-
-
-def skew_tensor(v: Tensor) -> Tensor:
-    """``(N, 3, F)`` axial vectors to ``(N, 3, 3, F)`` skew matrices."""
-    z = torch.zeros_like(v[:, 0])
-    x, y, w = v[:, 0], v[:, 1], v[:, 2]
-    return torch.stack([z, -w, y, w, z, -x, -y, x, z], 1).reshape(v.shape[0], 3, 3, v.shape[2])
-
-
-def axial_vector(t: Tensor) -> Tensor:
-    return 0.5 * torch.stack([t[:, 2, 1] - t[:, 1, 2], t[:, 0, 2] - t[:, 2, 0], t[:, 1, 0] - t[:, 0, 1]], 1)
 
 
 def decompose(t: Tensor) -> Tuple[Tensor, Tensor, Tensor]:
@@ -48,11 +44,6 @@ def decompose(t: Tensor) -> Tuple[Tensor, Tensor, Tensor]:
     eye = torch.eye(3, dtype=t.dtype, device=t.device)
     sym = t - skew - scalar[:, None, None, :] * eye[None, :, :, None]
     return scalar, skew, sym
-
-
-def compose(scalar: Tensor, skew: Tensor, sym: Tensor) -> Tensor:
-    eye = torch.eye(3, dtype=skew.dtype, device=skew.device)
-    return scalar[:, None, None, :] * eye[None, :, :, None] + skew + sym
 
 
 def frobenius(t: Tensor) -> Tensor:
@@ -95,29 +86,30 @@ class TensorEmbedding(nn.Module):
             [self.distance_proj1.bias, self.distance_proj2.bias, self.distance_proj3.bias])
         a = w.unsqueeze(1) * proj.view(-1, 3, nf)
         rows = embedding(a, geometry_rows(unit), plan)
-        scalar, skew = rows[:, 0], skew_tensor(rows[:, 1:4])
-        full = sym_from_compact(rows[:, 4:])
-        eye = torch.eye(3, dtype=full.dtype, device=full.device)
-        sym = full - full.diagonal(dim1=1, dim2=2).mean(-1)[:, None, None, :] * eye[None, :, :, None]
-        norm = self.init_norm(frobenius(compose(scalar, skew, sym)))
+        X = EMBEDDING_FULL(rows).view(n, 3, 3, nf)          # scalar 1 + skew(v) + traceless sym
+        norm = self.init_norm(frobenius(X))
         for lin in self.linears_scalar:
             norm = self.act(lin(norm))
-        norm = norm.reshape(n, 3, self.n_features)
-        scalar = self.linears_tensor[0](scalar) * norm[:, 0]
-        skew = _mix(self.linears_tensor[1], skew) * norm[:, 1, None, None, :]
-        sym = _mix(self.linears_tensor[2], sym) * norm[:, 2, None, None, :]
-        return compose(scalar, skew, sym)
+        # the part linears commute with the split into parts: one product for all three, the
+        # norm factors per part, then the parts recombined
+        G = _tensor_products(X, self.linears_tensor[0], self.linears_tensor[1], self.linears_tensor[2])
+        G = G.view(n, 9, 3, nf) * norm.view(n, 1, 3, nf)
+        return RECOMPOSE(G.reshape(n, 27, nf)).view(n, 3, 3, nf)
+
+
+def _tensor_products(X: Tensor, l0: nn.Linear, l1: nn.Linear, l2: nn.Linear) -> Tensor:
+    """``[X W_0^T | X W_1^T | X W_2^T]`` over every matrix entry of ``X (n, 3, 3, F)``: one product
+    on the tensor cores for the three channel linears (bias-free), as ``(n, 27, F)`` rows
+    ``entry * 3 + part``."""
+    n, nf = X.shape[0], X.shape[-1]
+    W = torch.cat([l0.weight, l1.weight, l2.weight], 0).t()
+    return gemm.matmul(X.reshape(n * 9, nf), W).view(n, 27, nf)
 
 
 def _edge_linear(x: Tensor, lin: nn.Linear) -> Tensor:
     """``lin(x)`` for per-pair rows: the tensor-core product (3xTF32, float32 accuracy) when the
     rows are many, differentiable to any order."""
     return gemm.matmul(x, lin.weight.t()) + lin.bias
-
-
-def _mix(lin: nn.Linear, t: Tensor) -> Tensor:
-    """A channel-mixing linear map on ``(N, 3, 3, F)`` tensors (acts on the last axis)."""
-    return lin(t)
 
 
 class Interaction(nn.Module):
@@ -137,23 +129,14 @@ class Interaction(nn.Module):
             f = self.act(_edge_linear(f, lin))
         filters = (f * cut.unsqueeze(-1)).reshape(-1, 3, F)
         X = X / (frobenius(X) + 1.0)[:, None, None, :]
-        scalar, skew, sym = decompose(X)
-        scalar = self.linears_tensor[0](scalar)
-        skew = self.linears_tensor[1](skew)
-        sym = self.linears_tensor[2](sym)
-        Y = compose(scalar, skew, sym)
-        # the neighbours' parts, each weighed by its filter, summed onto the centres in one pass
-        # over compact rows (scalar, axial vector, six symmetric entries)
-        m = messages(filters, to_compact(scalar, axial_vector(skew), sym), plan)
-        msg = compose(m[:, 0], skew_tensor(m[:, 1:4]), sym_from_compact(m[:, 4:]))
+        # channel linears of the parts as one product, then Y and the compact rows of its parts
+        Y, rows = Y_AND_COMPACT(_tensor_products(X, *self.linears_tensor[:3]))
+        Y = Y.view(n, 3, 3, F)
+        msg = FULL_FROM_COMPACT(messages(filters, rows, plan)).view(n, 3, 3, F)
         cs = (1.0 + 0.1 * q)[:, None, None, None]
         C = cs * (tensor_matmul(Y, msg) + tensor_matmul(msg, Y)) if self.o3 else 2.0 * tensor_matmul(Y, msg)
-        scalar, skew, sym = decompose(C)
-        norm = frobenius(C) + 1.0
-        scalar = self.linears_tensor[3](scalar / norm)
-        skew = self.linears_tensor[4](skew / norm[:, None, None, :])
-        sym = self.linears_tensor[5](sym / norm[:, None, None, :])
-        dX = compose(scalar, skew, sym)
+        C = C / (frobenius(C) + 1.0)[:, None, None, :]
+        dX = RECOMPOSE(_tensor_products(C, *self.linears_tensor[3:])).view(n, 3, 3, F)
         return X + dX + cs * tensor_matmul(dX, dX)
 
 

@@ -147,6 +147,9 @@ def _reverse(E: int, We: List[Tensor], spec: RadialSpec, acts: List[Tensor], H0:
     primal = dRd is None
     if primal:
         D = dR
+    elif (dR is not None and dR.is_contiguous() and dRd.is_contiguous() and dR.shape == dRd.shape
+          and dRd.data_ptr() == dR.data_ptr() + dR.numel() * dR.element_size()):
+        D = dR.as_strided((2 * dR.shape[0],) + tuple(dR.shape[1:]), dR.stride())   # adjacent: no copy
     else:
         D = torch.cat([dR if dR is not None else torch.zeros_like(dRd), dRd], 0)
     grads: List[Optional[Tensor]] = [None] * len(We)

@@ -25,6 +25,7 @@ functions run their PyTorch formulas.
 from __future__ import annotations
 
 from dataclasses import dataclass
+from typing import Optional
 
 import torch
 from torch import Tensor
@@ -263,3 +264,130 @@ class _MM3(torch.autograd.Function):
 def matmul3(A: Tensor, B: Tensor, ta: bool = False, tb: bool = False) -> Tensor:
     """Per atom and channel 3x3 matrix products of ``(n, 3, 3, F)`` tensors."""
     return _MM3.apply(A, B, ta, tb)
+
+
+class _PLin(torch.autograd.Function):
+    """``[out1; out2] = M [in1; in2]`` per atom and channel (rows of ``(n, K, F)`` tensors, ``M``
+    a constant ``(O, K)`` float64 matrix; ``out2`` only when ``O1 < O``, ``in2`` optional). Linear,
+    so its backward is the same map with ``M^T`` and every order differentiates."""
+
+    @staticmethod
+    def forward(ctx, in1: Tensor, in2, M: Tensor, MT: Tensor, O1: int):
+        ctx.K1 = in1.shape[1]
+        ctx.O1 = O1
+        ctx.two_in = in2 is not None
+        ctx.mats = (M, MT)
+        if _kernels(in1):
+            o1, o2 = _ext.ops().tn_plin(in1.contiguous(), None if in2 is None else in2.contiguous(),
+                                        M.to(in1.device), int(O1))
+        else:
+            x = in1 if in2 is None else torch.cat([in1, in2], 1)
+            out = torch.einsum("ok,nkf->nof", M.to(x.dtype), x)
+            o1, o2 = out[:, :O1].contiguous(), out[:, O1:].contiguous()
+        if O1 == M.shape[0]:
+            return o1
+        return o1, o2
+
+    @staticmethod
+    def backward(ctx, *gs):
+        M, MT = ctx.mats
+        g1 = gs[0]
+        g2 = gs[1] if len(gs) > 1 else None
+        res = _PLin.apply(g1, g2, MT, M, ctx.K1)
+        if ctx.two_in:
+            d1, d2 = res
+        else:
+            d1, d2 = res, None
+        return d1, d2, None, None, None
+
+
+class LinearMap:
+    """A constant per-atom, per-channel linear map of component rows (kernel ``tn_plin``)."""
+
+    def __init__(self, M: Tensor, O1: Optional[int] = None):
+        self.M = M.to(torch.float64).contiguous()
+        self.MT = self.M.t().contiguous()
+        self.O1 = int(M.shape[0] if O1 is None else O1)
+        self._dev = {}
+
+    def _on(self, dev):
+        key = str(dev)
+        if key not in self._dev:
+            self._dev[key] = (self.M.to(dev), self.MT.to(dev))
+        return self._dev[key]
+
+    def __call__(self, in1: Tensor, in2: Optional[Tensor] = None):
+        M, MT = self._on(in1.device)
+        return _PLin.apply(in1, in2, M, MT, self.O1)
+
+
+def _trace3(t: Tensor) -> Tensor:
+    return (t[:, 0, 0] + t[:, 1, 1] + t[:, 2, 2]) / 3.0
+
+
+def _matrix_of(fn, k_in: int) -> Tensor:
+    """The matrix of a linear map of component rows, read off from the basis vectors."""
+    eye = torch.eye(k_in, dtype=torch.float64)
+    cols = [fn(eye[r].view(1, k_in, 1)).reshape(-1) for r in range(k_in)]
+    return torch.stack(cols, 1)
+
+
+def _parts(T: Tensor):
+    """Scalar, skew and traceless symmetric parts of ``(1, 3, 3, 1)`` matrices."""
+    skew = 0.5 * (T - T.transpose(1, 2))
+    s = _trace3(T)
+    sym = 0.5 * (T + T.transpose(1, 2)) - s[:, None, None] * torch.eye(3, dtype=T.dtype)[None, :, :, None]
+    return s, skew, sym
+
+
+def _compose(s: Tensor, skew: Tensor, sym: Tensor) -> Tensor:
+    return s[:, None, None] * torch.eye(3, dtype=skew.dtype)[None, :, :, None] + skew + sym
+
+
+def _axial(t: Tensor) -> Tensor:
+    return 0.5 * torch.stack([t[:, 2, 1] - t[:, 1, 2], t[:, 0, 2] - t[:, 2, 0], t[:, 1, 0] - t[:, 0, 1]], 1)
+
+
+def _three_parts(x: Tensor):
+    """``(1, 27, 1)`` rows ``k * 3 + j`` (matrix entry ``k``, product ``j``) -> the scalar part of
+    product 0, the skew part of product 1 and the traceless symmetric part of product 2."""
+    G = x.view(1, 9, 3, 1)
+    s = _parts(G[:, :, 0].reshape(1, 3, 3, 1))[0]
+    skew = _parts(G[:, :, 1].reshape(1, 3, 3, 1))[1]
+    sym = _parts(G[:, :, 2].reshape(1, 3, 3, 1))[2]
+    return s, skew, sym
+
+
+def _y_and_compact(x: Tensor) -> Tensor:
+    s, skew, sym = _three_parts(x)
+    Y = _compose(s, skew, sym).reshape(1, 9, 1)
+    c = torch.cat([s.unsqueeze(1), _axial(skew), torch.stack([sym[:, 0, 0], sym[:, 0, 1], sym[:, 0, 2],
+                                                              sym[:, 1, 1], sym[:, 1, 2], sym[:, 2, 2]], 1)], 1)
+    return torch.cat([Y, c], 1)
+
+
+def _full_from_compact(x: Tensor) -> Tensor:
+    m = x.view(1, 10, 1)
+    v = m[:, 1:4]
+    z = torch.zeros_like(v[:, 0])
+    skew = torch.stack([z, -v[:, 2], v[:, 1], v[:, 2], z, -v[:, 0], -v[:, 1], v[:, 0], z], 1).reshape(1, 3, 3, 1)
+    return _compose(m[:, 0], skew, sym_from_compact(m[:, 4:10])).reshape(1, 9, 1)
+
+
+#: (Y | compact rows) of the three channel products of a normalised tensor (27 -> 9 + 10)
+Y_AND_COMPACT = LinearMap(_matrix_of(_y_and_compact, 27), O1=9)
+#: full 3x3 rows of compact rows (10 -> 9)
+FULL_FROM_COMPACT = LinearMap(_matrix_of(_full_from_compact, 10))
+#: scalar / skew / traceless symmetric parts of three products, recomposed (27 -> 9)
+RECOMPOSE = LinearMap(_matrix_of(lambda x: _compose(*_three_parts(x)).reshape(1, 9, 1), 27))
+
+
+def _embedding_full(x: Tensor) -> Tensor:
+    m = x.view(1, 10, 1)
+    full = _full_from_compact(x).view(1, 3, 3, 1)
+    sym = sym_from_compact(m[:, 4:10])
+    return (full - (_trace3(sym))[:, None, None] * torch.eye(3, dtype=x.dtype)[None, :, :, None]).reshape(1, 9, 1)
+
+
+#: the embedding's tensors from its summed rows: scalar, skew of the vector, traceless symmetric (10 -> 9)
+EMBEDDING_FULL = LinearMap(_matrix_of(_embedding_full, 10))

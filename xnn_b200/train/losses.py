@@ -44,7 +44,9 @@ def weighted_loss(pred: Dict[str, Tensor], data: AtomicGraph, energy_weight: flo
                   huber_delta_energy: Optional[float] = None,
                   huber_delta_forces: Optional[float] = None,
                   huber_delta_stress: Optional[float] = None,
-                  counts: Optional[dict] = None) -> Tuple[Tensor, Dict[str, Tensor]]:
+                  counts: Optional[dict] = None, parts: Optional[dict] = None) -> Tuple[Tensor, Dict[str, Tensor]]:
+    """Weighted sum of the loss terms; ``parts``, when given, receives every weighted term under
+    its :data:`LOSS_TERMS` name (the input of :class:`UncertaintyWeights`)."""
     logs: Dict[str, Tensor] = {}
     total = None
     dev = data.pos.device
@@ -54,6 +56,8 @@ def weighted_loss(pred: Dict[str, Tensor], data: AtomicGraph, energy_weight: flo
         logs[key] = term.detach()
         if counts is not None:
             counts[key] = (den.detach(), w)
+        if parts is not None:
+            parts[_PART_NAME[key]] = term * w
         total = term * w if total is None else total + term * w
 
     sw = data.weight
@@ -109,6 +113,40 @@ def weighted_loss(pred: Dict[str, Tensor], data: AtomicGraph, energy_weight: flo
     if total is None:
         total = torch.zeros((), device=dev, dtype=torch.float64)
     return total, logs
+
+
+#: the weighted loss terms by name, with the config weight that switches each on
+LOSS_TERMS = {"energy_mse": "energy_weight", "force_mse": "force_weight", "stress_mse": "stress_weight",
+              "dipole_mse": "dipole_weight", "polarizability_mse": "polarizability_weight",
+              "charge_mse": "charge_weight", "property_mse": "property_weight"}
+_PART_NAME = {"energy": "energy_mse", "forces": "force_mse", "stress": "stress_mse", "dipole": "dipole_mse",
+              "polarizability": "polarizability_mse", "charges": "charge_mse", "properties": "property_mse"}
+
+
+class UncertaintyWeights(torch.nn.Module):
+    """Learned balance of the loss terms (Kendall, Gal & Cipolla, CVPR 2018, homoscedastic task
+    uncertainty): term ``L_k`` (already times its config weight) contributes
+    ``exp(-2 s_k) L_k / 2 + s_k`` with a trainable ``s_k = log sigma_k`` starting at 0; a term
+    without an ``s_k`` adds unchanged. Parity: ``src/xnn/common/train/losses.py:529-585``
+    (``optim.loss_weighting: uncertainty``)."""
+
+    def __init__(self, names):
+        super().__init__()
+        self.log_sigma = torch.nn.ParameterDict({n: torch.nn.Parameter(torch.zeros(())) for n in names})
+
+    def forward(self, parts: Dict[str, Tensor]) -> Tensor:
+        out = None
+        for name, term in parts.items():
+            if name in self.log_sigma:
+                ls = self.log_sigma[name].to(term.dtype)
+                term = 0.5 * torch.exp(-2.0 * ls) * term + ls
+            out = term if out is None else out + term
+        if out is None:
+            return next(iter(self.log_sigma.values())).new_zeros(())
+        return out
+
+    def sigmas(self) -> Dict[str, float]:
+        return {n: float(torch.exp(p.detach())) for n, p in self.log_sigma.items()}
 
 
 def error_metrics(pred: Dict[str, Tensor], data: AtomicGraph) -> Dict[str, Tensor]:

@@ -134,9 +134,13 @@ class Trainer:
         else:
             self.scheduler = None
         self.ema = EMA(self.params, o.ema_decay) if o.ema_decay > 0 else None
+        self.loss_weights = self._make_loss_weights(o)
         self._fused = None
         fs = cfg.trainer.fused_step
-        if fs is True or (fs == "auto" and self.device.type == "cuda"):
+        if self.loss_weights is not None and fs is True:
+            raise ValueError("trainer.fused_step computes fixed-weight losses; optim.loss_weighting: uncertainty "
+                             "runs in the ordinary step")
+        if self.loss_weights is None and (fs is True or (fs == "auto" and self.device.type == "cuda")):
             from . import mace_step
             ok, why = mace_step.supports(self.module, o)
             if ok:
@@ -160,6 +164,28 @@ class Trainer:
         self.history: List[Dict[str, float]] = []
 
     # ------------------------------------------------------------------ setup
+    def _make_loss_weights(self, o):
+        """:class:`UncertaintyWeights` over the active loss terms (``optim.loss_weighting:
+        uncertainty``, ordinary single-head steps), their ``log sigma`` in the optimizer without
+        weight decay; ``None`` for fixed weights."""
+        if o.loss_weighting not in ("fixed", "uncertainty"):
+            raise ValueError(f"optim.loss_weighting must be 'fixed' or 'uncertainty', got {o.loss_weighting!r}")
+        if o.loss_weighting == "fixed":
+            return None
+        if self.use_graphs:
+            raise ValueError("optim.loss_weighting: uncertainty does not run in captured steps (trainer.cuda_graph)")
+        from .losses import LOSS_TERMS, UncertaintyWeights
+        names = [n for n, w in LOSS_TERMS.items() if getattr(o, w, 0.0) > 0]
+        if not names:
+            raise ValueError("optim.loss_weighting: uncertainty needs a loss term with a positive weight")
+        uw = UncertaintyWeights(names).to(self.device, self.params[0].dtype)
+        if self.world > 1:
+            with torch.no_grad():
+                for p in uw.parameters():
+                    torch.distributed.broadcast(p, 0)
+        self.optimizer.add_param_group({"params": list(uw.parameters()), "weight_decay": 0.0})
+        return uw
+
     def _freeze(self):
         import fnmatch
         o = self.cfg.optim
@@ -223,13 +249,18 @@ class Trainer:
     def _loss(self, batch: AtomicGraph):
         o = self.cfg.optim
         out = self.module(batch)
+        learned = self.loss_weights is not None and self.module.training
+        parts = {} if learned else None
         loss, logs = weighted_loss(out, batch, o.energy_weight, o.force_weight, o.stress_weight,
                                    dipole_weight=o.dipole_weight,
                                    polarizability_weight=o.polarizability_weight,
                                    charge_weight=o.charge_weight, property_weight=o.property_weight,
                                    huber_delta=o.huber_delta, huber_delta_energy=o.huber_delta_energy,
                                    huber_delta_forces=o.huber_delta_forces,
-                                   huber_delta_stress=o.huber_delta_stress)
+                                   huber_delta_stress=o.huber_delta_stress, parts=parts)
+        if learned:
+            loss = self.loss_weights(parts)
+            logs = dict(logs, **{f"sigma_{k}": torch.exp(p.detach()) for k, p in self.loss_weights.log_sigma.items()})
         if o.reaction_weight > 0 and self.module.training and self.reactions is not None and not self.use_graphs:
             r = self._reaction_loss(self._next_reactions())
             loss = loss + o.reaction_weight * r.to(loss.dtype)
@@ -238,13 +269,22 @@ class Trainer:
 
     def _train_step_impl(self, batch: AtomicGraph):
         self.grad_sync.zero_()
+        if self.loss_weights is not None:
+            for p in self.loss_weights.parameters():
+                p.grad = None
         if self._fused is not None:
             loss, logs, _ = self._fused(batch, bucket_hook=self.grad_sync.bucket_ready)
         else:
             loss, logs, _ = self._loss(batch)
             with params_only():
-                loss.backward(inputs=self.params)
+                inputs = self.params if self.loss_weights is None else self.params + list(
+                    self.loss_weights.parameters())
+                loss.backward(inputs=inputs)
         self.grad_sync.reduce()
+        if self.loss_weights is not None and self.world > 1:
+            for p in self.loss_weights.parameters():
+                torch.distributed.all_reduce(p.grad)
+                p.grad.mul_(1.0 / self.world)
         if self.cfg.optim.clip_grad > 0:
             torch.nn.utils.clip_grad_norm_(self.params, self.cfg.optim.clip_grad, foreach=True)
         self.optimizer.step()
@@ -447,7 +487,10 @@ class Trainer:
     def save(self, path: str) -> None:
         if D.is_main():
             os.makedirs(os.path.dirname(os.path.abspath(path)), exist_ok=True)
-            torch.save({"model": self.state_dict_for_save(), "cfg": self.cfg.to_dict()}, path)
+            state = {"model": self.state_dict_for_save(), "cfg": self.cfg.to_dict()}
+            if self.loss_weights is not None:
+                state["loss_sigmas"] = self.loss_weights.sigmas()
+            torch.save(state, path)
         D.barrier()
 
     def close(self) -> None:
