@@ -1,8 +1,8 @@
-"""Model hub: portable checkpoints, local registry of named models, ``from_pretrained``.
+"""Model hub: portable checkpoints, a registry of named models, downloads, ``from_pretrained``.
 
-This build has no network access, so named models resolve to local directories: entries of
-``$XNN_B200_HUB`` (a directory of portable model directories, one per name) or names
-registered with :func:`register_pretrained`.
+A source is a local checkpoint path, a registered name (entries of ``$XNN_B200_HUB``, a directory
+of portable model directories, one per name, or names given to :func:`register_pretrained`), or a
+URL / Zenodo DOI, downloaded once into the model cache (:mod:`xnn_b200.hub.fetch`).
 """
 from __future__ import annotations
 
@@ -15,12 +15,14 @@ from torch import nn
 from .card import CARD_FILE, CONFIG_FILE, WEIGHTS_FILE, ModelCard
 from .checkpoint import (Checkpoint, build_potential, config_to_dict, load_checkpoint, read_config,
                          save_pretrained, write_config)
+from .fetch import fetch_model, is_remote, model_cache_dir
 
 _REGISTRY: Dict[str, Path] = {}
 
 
 def register_pretrained(name: str, path: Union[str, Path]) -> None:
-    _REGISTRY[name] = Path(path)
+    """Name a local model directory / checkpoint, or a URL / DOI fetched on first use."""
+    _REGISTRY[name] = path if is_remote(path) else Path(path)
 
 
 def list_pretrained() -> Dict[str, Path]:
@@ -33,26 +35,32 @@ def list_pretrained() -> Dict[str, Path]:
     return out
 
 
-def resolve(source: Union[str, Path]) -> Path:
-    p = Path(source)
+def resolve(source: Union[str, Path], cache_dir: Optional[Union[str, Path]] = None) -> Path:
+    if is_remote(source):
+        return fetch_model(source, cache_dir=cache_dir)
+    p = Path(source).expanduser()
     if p.exists():
         return p
     known = list_pretrained()
     if str(source) in known:
-        return known[str(source)]
-    raise FileNotFoundError(f"{source!r} is neither a checkpoint path nor a registered model "
-                            f"(known: {sorted(known)}); downloads are not available in this build")
+        v = known[str(source)]
+        return fetch_model(str(v), cache_dir=cache_dir) if is_remote(v) else Path(v)
+    raise FileNotFoundError(f"{source!r} is neither a checkpoint path, a URL / DOI nor a registered model "
+                            f"(known: {sorted(known)})")
 
 
-def from_pretrained(source: Union[str, Path], wrap: bool = True, dtype=None) -> nn.Module:
-    """The model of a checkpoint path or registered name; ``wrap`` keeps the force/stress wrapper."""
-    ck = load_checkpoint(resolve(source))
+def from_pretrained(source: Union[str, Path], wrap: bool = True, dtype=None,
+                    cache_dir: Optional[Union[str, Path]] = None) -> nn.Module:
+    """The model of a checkpoint path, registered name, URL or Zenodo DOI; ``wrap`` keeps the
+    force/stress wrapper."""
+    ck = load_checkpoint(resolve(source, cache_dir=cache_dir))
     if ck.config is None:
         raise ValueError(f"{source}: a bare state dict carries no config; use build_potential(config, sd)")
     pot = build_potential(ck.config, ck.state_dict, dtype=dtype)
     return pot if wrap else pot.model
 
 
-__all__ = ["Checkpoint", "ModelCard", "build_potential", "config_to_dict", "from_pretrained", "list_pretrained",
+__all__ = ["Checkpoint", "ModelCard", "build_potential", "config_to_dict", "fetch_model", "from_pretrained",
+           "is_remote", "list_pretrained", "model_cache_dir",
            "load_checkpoint", "read_config", "register_pretrained", "resolve", "save_pretrained", "write_config",
            "CARD_FILE", "CONFIG_FILE", "WEIGHTS_FILE"]
