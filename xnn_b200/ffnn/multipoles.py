@@ -194,6 +194,27 @@ def spread(pos: Tensor, cell: Tensor, q: Optional[Tensor], d: Optional[Tensor], 
     return grid.view(K1, K2, nz)
 
 
+def gather_dipole_gradient(pos: Tensor, cell: Tensor, d: Tensor, mesh: List[int], p: int,
+                           z_range: Tuple[int, int], phi: Tensor) -> Tensor:
+    """``dE/dd`` of the spread dipoles for a mesh potential ``phi = dE/dgrid`` on the planes
+    ``z_range`` (the spreading's adjoint): the gather kernel on CUDA (float64 sites, float32 mesh),
+    autograd through the spreading formulas otherwise."""
+    z0, z1 = z_range
+    if (pos.is_cuda and pos.dtype == torch.float64 and phi.dtype == torch.float32 and 4 <= p <= 6
+            and _kernel_ok()):
+        from .. import _ext
+        K = torch.tensor(mesh, dtype=torch.float64, device=pos.device)
+        G = (torch.linalg.inv(cell.detach().double()) * K[None, :]).contiguous()
+        gd, _ = _ext.ops().pme_gather(pos.detach().contiguous(), G, list(mesh), int(p), int(z0), int(z1 - z0),
+                                      None, d.detach().contiguous(), None, phi.contiguous(), True, False)
+        return gd
+    dd = d.detach().clone().requires_grad_(True)
+    with torch.enable_grad():
+        grid = spread(pos.detach(), cell.detach(), None, dd, None, list(mesh), p, z_range=z_range)
+        (g,) = torch.autograd.grad((grid * phi.to(grid.dtype)).sum(), dd)
+    return g
+
+
 def influence(cell: Tensor, mesh: List[int], alpha: float, p: int, dtype, device) -> Tensor:
     """``exp(-pi^2 m^2 / alpha^2) / (pi V m^2) B(m)`` on the rfft half-spectrum ``(K1, K2, K3//2+1)``,
     zero at ``m = 0`` and doubled where the half spectrum stands for two conjugate terms."""
@@ -462,6 +483,9 @@ class DipoleOperator:
         return ok
 
     def recip(self, d: Tensor) -> Tensor:
+        backend = self.mod.mesh_backend
+        if backend is not None and hasattr(backend, "dipole_field"):
+            return backend.dipole_field(self.pos, self.cell, d, self.mod.setup)
         if self._direct_setup():
             # field = -dE/dd with E = 1/2 sum_m infl(m) |F(m)|^2: spread d, transform, weigh,
             # transform back to the mesh potential dE/dgrid, gather its stencil derivatives

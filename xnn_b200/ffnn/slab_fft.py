@@ -191,6 +191,49 @@ class SlabFFT:
         infl = self.influence(cell, setup.alpha, p, setup.fft_dtype)
         return (0.5 * (infl * (F.real * F.real + F.imag * F.imag)).sum()).to(pos.dtype)
 
+    def _slab_sites(self, pos: Tensor, cell: Tensor, p: int) -> Tensor:
+        """Indices of the sites whose stencil (planes base - p + 1 .. base) reaches this slab."""
+        K3 = self.mesh[2]
+        z0, z1 = self.z[self.rank]
+        with torch.no_grad():
+            uz = (pos.detach() @ torch.linalg.inv(cell.detach()))[:, 2] * K3
+            base = torch.floor(uz).long()
+            return torch.nonzero(((base - z0) % K3) < (z1 - z0) + p - 1).flatten()
+
+    def dipole_field(self, pos: Tensor, cell: Tensor, d: Tensor, setup) -> Tensor:
+        """This process's share of the reciprocal field ``-dE/dd`` of dipoles ``d`` (Coulomb
+        units, ``(n, 3)``; the caller sums the shares), without an energy graph: spread onto this
+        slab, forward transform and transpose, influence, the inverse pipeline (the adjoint of the
+        forward one) back to the slab's mesh potential ``dE/dgrid``, and the gather of its stencil
+        derivatives at the sites that reach the slab."""
+        from .multipoles import gather_dipole_gradient
+        K1, K2, K3 = self.mesh
+        p = setup.order
+        z0, z1 = self.z[self.rank]
+        keep = self._slab_sites(pos, cell, p) if self.world > 1 else None
+        pk = pos if keep is None else pos.index_select(0, keep)
+        dk = d if keep is None else d.index_select(0, keep)
+        planes = spread(pk, cell, None, dk, None, self.mesh, p, z_range=(z0, z1),
+                        out_dtype=setup.fft_dtype).to(setup.fft_dtype)
+        F = torch.fft.fft(torch.fft.rfft(planes, dim=0), dim=1)
+        F = torch.fft.fft(self._to_lines(F), dim=2)
+        infl = self.influence(cell, setup.alpha, p, setup.fft_dtype)
+        x0, x1 = self.x[self.rank]
+        w = torch.full((x1 - x0,), 2.0, dtype=infl.dtype, device=infl.device)
+        f1 = torch.arange(x0, x1, device=infl.device)
+        w[f1 == 0] = 1.0
+        if K1 % 2 == 0:
+            w[f1 == K1 // 2] = 1.0
+        # the unweighted influence (the inverse real transform restores the conjugate half) times
+        # the mesh size (the unnormalised inverse)
+        G = torch.fft.ifft(F * (infl / w[:, None, None] * float(K1 * K2 * K3)), dim=2)
+        G = torch.fft.ifft(self._to_planes(G.contiguous()), dim=1)
+        phi = torch.fft.irfft(G, n=K1, dim=0).contiguous()
+        gk = gather_dipole_gradient(pk, cell, dk, self.mesh, p, (z0, z1), phi)
+        if keep is None:
+            return -gk
+        return torch.zeros_like(d).index_add_(0, keep, -gk)
+
     def close(self) -> None:
         if self._peer is not None:
             self._peer.close()
