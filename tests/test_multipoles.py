@@ -200,3 +200,28 @@ def test_direct_reciprocal_field_matches_energy_gradient():
     e = mod.recip(pos, cell, v.new_zeros(500), vv, v.new_zeros(500, 3, 3))
     (g,) = torch.autograd.grad(e, vv)
     torch.testing.assert_close(got, -g, rtol=1e-4, atol=1e-6 * float(g.abs().max()))
+
+
+def test_pairs_split_over_receiver_ranges():
+    """Receiver-range searches give disjoint pair sets whose union is the full set, and each
+    range holds a share close to its atoms' share."""
+    pos, cell, q, d, Q = _system(n=60, L=12.0, seed=9)
+    mol = torch.arange(60) // 3
+    full = M.multipole_pairs(pos, cell, 5.0, mol)
+
+    def keyset(pairs):
+        i, j, s, ex = pairs
+        out = set()
+        for a, b, sh, e in zip(i.tolist(), j.tolist(), s.tolist(), ex.tolist()):
+            if (a, b) > (b, a) or (a == b and tuple(sh) < (0, 0, 0)):
+                a, b, sh = b, a, [-x for x in sh]
+            out.add((min(a, b), max(a, b), tuple(sh) if a <= b else tuple(-x for x in sh), e))
+        return out
+
+    ref = keyset(full)
+    parts = [M.multipole_pairs(pos, cell, 5.0, mol, receivers=r) for r in ((0, 20), (20, 41), (41, 60))]
+    sets = [keyset(p) for p in parts]
+    assert sum(len(x) for x in sets) == len(ref)
+    assert set().union(*sets) == ref
+    for x in sets:
+        assert 0.2 * len(ref) < len(x) < 0.5 * len(ref)

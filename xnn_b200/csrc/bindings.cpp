@@ -59,7 +59,8 @@ const T* ptr_or_null(const c10::optional<torch::Tensor>& t) {
 
 // ---- neighbour list ------------------------------------------------------------------
 std::vector<torch::Tensor> neighbor_list(torch::Tensor pos, torch::Tensor cell, std::vector<int64_t> reps,
-                                         std::vector<int64_t> pbc, double cutoff, bool self_interaction) {
+                                         std::vector<int64_t> pbc, double cutoff, bool self_interaction,
+                                         int64_t r0, int64_t r1) {
   TORCH_CHECK(pos.dim() == 2 && pos.size(1) == 3 && pos.scalar_type() == torch::kFloat64,
               "pos must be (N, 3) float64");
   pos = pos.contiguous();
@@ -137,8 +138,14 @@ std::vector<torch::Tensor> neighbor_list(torch::Tensor pos, torch::Tensor cell, 
   prm.cutoff2 = cutoff * cutoff;
   prm.self_interaction = self_interaction ? 1 : 0;
   prm.N = N;
+  // receivers r0 .. r1 - 1 (r1 < 0: to the end)
+  if (r1 < 0 || r1 > N) r1 = N;
+  TORCH_CHECK(r0 >= 0 && r0 <= r1, "neighbor_list: receiver range");
+  prm.r0 = r0;
+  prm.M = r1 - r0;
+  const int64_t M = prm.M;
 
-  auto counts = torch::empty({N}, lopt);
+  auto counts = torch::empty({M}, lopt);
   if (pos.is_cuda()) {
     c10::cuda::CUDAGuard g(pos.device());
     auto st = at::cuda::getCurrentCUDAStream();
@@ -146,10 +153,10 @@ std::vector<torch::Tensor> neighbor_list(torch::Tensor pos, torch::Tensor cell, 
   } else {
     int64_t* cp = counts.data_ptr<int64_t>();
 #pragma omp parallel for schedule(dynamic, 64)
-    for (int64_t i = 0; i < N; ++i) {
+    for (int64_t t = 0; t < M; ++t) {
       int64_t n = 0;
-      nb_visit(prm, i, [&](int64_t, int64_t, int64_t, int64_t) { ++n; });
-      cp[i] = n;
+      nb_visit(prm, r0 + t, [&](int64_t, int64_t, int64_t, int64_t) { ++n; });
+      cp[t] = n;
     }
   }
   auto offsets = torch::cumsum(counts, 0) - counts;
@@ -170,8 +177,9 @@ std::vector<torch::Tensor> neighbor_list(torch::Tensor pos, torch::Tensor cell, 
       int64_t* dp = dst.data_ptr<int64_t>();
       int64_t* hp = shifts.data_ptr<int64_t>();
 #pragma omp parallel for schedule(dynamic, 64)
-      for (int64_t i = 0; i < N; ++i) {
-        int64_t o = op[i];
+      for (int64_t t = 0; t < M; ++t) {
+        const int64_t i = r0 + t;
+        int64_t o = op[t];
         nb_visit(prm, i, [&](int64_t j, int64_t s0, int64_t s1, int64_t s2) {
           sp[o] = j; dp[o] = i;
           hp[3 * o] = -s0; hp[3 * o + 1] = -s1; hp[3 * o + 2] = -s2;
@@ -409,7 +417,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_comm(m);
   register_tensornet(m);
   m.attr("HAS_CUDA") = true;
-  m.def("neighbor_list", &neighbor_list, "cell-list neighbour search (CUDA or OpenMP)");
+  m.def("neighbor_list", &neighbor_list, "cell-list neighbour search (CUDA or OpenMP)", pybind11::arg("pos"),
+        pybind11::arg("cell"), pybind11::arg("reps"), pybind11::arg("pbc"), pybind11::arg("cutoff"),
+        pybind11::arg("self_interaction"), pybind11::arg("r0") = 0, pybind11::arg("r1") = -1);
   m.def("edge_geometry_fwd", &edge_geometry_fwd);
   m.def("edge_geometry_bwd", &edge_geometry_bwd);
   m.def("edge_geometry_jvp", &edge_geometry_jvp);

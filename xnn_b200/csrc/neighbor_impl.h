@@ -29,6 +29,8 @@ struct NbParams {
   double cutoff2;
   int self_interaction;
   int64_t N;
+  int64_t r0;                 // receivers r0 .. r0 + M - 1 are searched (all atoms are candidates)
+  int64_t M;
 };
 
 // Visits every candidate pair of receiver i; fn(j, s0, s1, s2) for pairs inside the cutoff.

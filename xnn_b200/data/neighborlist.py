@@ -91,13 +91,16 @@ def _brute_force(pos: Tensor, cutoff: float, cell: Optional[Tensor], pbc: Option
 
 def build_neighbor_list(pos: Tensor, cutoff: float, cell: Optional[Tensor] = None,
                         pbc: Optional[Tensor] = None, self_interaction: bool = False,
-                        engine: str = "auto") -> Tuple[Tensor, Tensor]:
+                        engine: str = "auto", receivers: Optional[Tuple[int, int]] = None) -> Tuple[Tensor, Tensor]:
     """``(edge_index (2, E), cell_shifts (E, 3))`` of one structure (see module notes).
 
     Parameters
     ----------
     engine : {"auto", "native", "torch"}
         ``"auto"`` takes the native cell list when the extension is loaded.
+    receivers : (int, int), optional
+        Only edges into atoms ``r0 <= i < r1`` (every atom stays a candidate sender): one
+        process's share of a list split over processes.
     """
     if cell is not None and cell.dim() == 3:
         cell = cell[0]
@@ -110,14 +113,18 @@ def build_neighbor_list(pos: Tensor, cutoff: float, cell: Optional[Tensor] = Non
         from .. import _ext
         if _ext.available() or engine == "native":
             return _native(pos, cutoff, cell if periodic else None, pbc if periodic else None,
-                           self_interaction)
+                           self_interaction, receivers)
     ei, sh = _brute_force(pos, cutoff, cell if periodic else None, pbc if periodic else None,
                           self_interaction)
-    return _sort_edges(ei, sh, pos.shape[0])
+    ei, sh = _sort_edges(ei, sh, pos.shape[0])
+    if receivers is not None:
+        keep = (ei[1] >= receivers[0]) & (ei[1] < receivers[1])
+        ei, sh = ei[:, keep], sh[keep]
+    return ei, sh
 
 
 def _native(pos: Tensor, cutoff: float, cell: Optional[Tensor], pbc: Optional[Tensor],
-            self_interaction: bool) -> Tuple[Tensor, Tensor]:
+            self_interaction: bool, receivers: Optional[Tuple[int, int]] = None) -> Tuple[Tensor, Tensor]:
     from .. import _ext
     C = _ext.ops()
     p64 = pos.detach().to(torch.float64).contiguous()
@@ -131,8 +138,9 @@ def _native(pos: Tensor, cutoff: float, cell: Optional[Tensor], pbc: Optional[Te
         reps = torch.zeros(3, dtype=torch.long)
         cell64 = torch.zeros(3, 3, dtype=torch.float64, device=p64.device)
         pbc_t = torch.zeros(3, dtype=torch.long)
+    r0, r1 = (0, -1) if receivers is None else (int(receivers[0]), int(receivers[1]))
     src, dst, shifts = C.neighbor_list(p64, cell64, [int(r) for r in reps], [int(b) for b in pbc_t],
-                                       float(cutoff), bool(self_interaction))
+                                       float(cutoff), bool(self_interaction), r0, r1)
     if offsets is not None:
         shifts = shifts + offsets[src] - offsets[dst]
     return torch.stack([src, dst]), shifts

@@ -369,16 +369,24 @@ def background_energy(q: Tensor, cell: Tensor, alpha: float) -> Tensor:
 
 
 # ----------------------------------------------------------------------------- pair list
-def multipole_pairs(pos: Tensor, cell: Tensor, cutoff: float, molecule: Optional[Tensor]):
-    """Unique pairs within ``cutoff`` (``i < j`` or ``i == j`` in a nonzero image counted once),
-    their shifts, and which pairs belong to one molecule (excluded)."""
+def multipole_pairs(pos: Tensor, cell: Tensor, cutoff: float, molecule: Optional[Tensor],
+                    receivers: Optional[Tuple[int, int]] = None):
+    """Unique pairs within ``cutoff`` (every unordered pair, and an atom with a nonzero image of
+    itself, once), their shifts, and which pairs belong to one molecule (excluded).
+
+    Of the two directed edges of a pair the one kept is ``src < dst`` when ``src + dst`` is odd
+    and ``src > dst`` when it is even (an image of itself: the positive shift), so the pairs kept
+    by a receiving atom are about half of its neighbours whatever its index. With ``receivers``
+    only edges into those atoms are searched: processes that split the atoms into ranges get
+    disjoint, balanced shares of the pairs from their own searches."""
     from ..data.neighborlist import build_neighbor_list
     ei, sh = build_neighbor_list(pos.detach().double(), cutoff, cell.detach().double(),
-                                 torch.ones(3, dtype=torch.bool))
+                                 torch.ones(3, dtype=torch.bool), receivers=receivers)
     src, dst = ei[0], ei[1]
     # edge vector pos[dst] - pos[src] + sh @ cell; keep each unordered pair once
-    key = (src < dst) | ((src == dst) & ((sh[:, 0] > 0) | ((sh[:, 0] == 0) & ((sh[:, 1] > 0) | (
-        (sh[:, 1] == 0) & (sh[:, 2] > 0))))))
+    odd = ((src + dst) % 2) == 1
+    positive = (sh[:, 0] > 0) | ((sh[:, 0] == 0) & ((sh[:, 1] > 0) | ((sh[:, 1] == 0) & (sh[:, 2] > 0))))
+    key = torch.where(src == dst, positive, torch.where(odd, src < dst, src > dst))
     i, j, s = src[key], dst[key], sh[key]
     if molecule is None:
         excluded = torch.zeros_like(i, dtype=torch.bool)
@@ -551,11 +559,15 @@ class PolarizableMultipoles(nn.Module):
         return t
 
     def pairs(self, pos, cell, molecule):
-        i, j, s, ex = multipole_pairs(pos, cell, self.setup.cutoff, molecule)
+        """This process's pairs: with the work split, the pairs received by its range of atoms
+        (its own neighbour search, no replicated list)."""
+        recv = None
         if self.world > 1:
-            sl = slice(self.rank, None, self.world)
-            i, j, s, ex = i[sl], j[sl], s[sl], ex[sl]
-        return i, j, s, ex
+            n = pos.shape[0]
+            base, extra = divmod(n, self.world)
+            r0 = self.rank * base + min(self.rank, extra)
+            recv = (r0, r0 + base + (1 if self.rank < extra else 0))
+        return multipole_pairs(pos, cell, self.setup.cutoff, molecule, receivers=recv)
 
     def _influence(self, cell: Tensor) -> Tensor:
         s = self.setup
