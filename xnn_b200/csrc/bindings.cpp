@@ -412,10 +412,12 @@ std::vector<torch::Tensor> symcon_bwd2_op(torch::Tensor A, torch::Tensor z, torc
 
 void register_comm(pybind11::module& m);
 void register_tensornet(pybind11::module& m);
+void register_d3(pybind11::module& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_comm(m);
   register_tensornet(m);
+  register_d3(m);
   m.attr("HAS_CUDA") = true;
   m.def("neighbor_list", &neighbor_list, "cell-list neighbour search (CUDA or OpenMP)", pybind11::arg("pos"),
         pybind11::arg("cell"), pybind11::arg("reps"), pybind11::arg("pbc"), pybind11::arg("cutoff"),

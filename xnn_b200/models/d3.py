@@ -33,6 +33,31 @@ PARAMS_ZERO = {"pbe0": dict(s8=0.928, rs6=1.287), "pbe": dict(s8=0.722, rs6=1.21
                "b3lyp": dict(s8=1.703, rs6=1.261)}
 
 
+class _TwoBodyKernel(torch.autograd.Function):
+    """The two-body energy per atom on the native passes (``csrc/d3.cu``, OpenMP twin on the
+    CPU) with analytic edge gradients. The backward scales them by the incoming gradient of the
+    receiving atom, which is exact when that gradient is the same on both ends of every edge
+    (energies of whole structures, the forces / stress / energy-loss case); first derivatives
+    only."""
+
+    @staticmethod
+    def forward(ctx, vec, z, plan, tables, damping, prm):
+        r = torch.linalg.norm(vec, dim=-1).contiguous()
+        from .. import _ext
+        e_atom, cn, g, w = _ext.ops().d3_two_body(z, plan.dst_ptr, plan.dst_perm if plan.dst_perm is not None
+                                               else z.new_zeros(0), plan.src, plan.dst, r, vec.contiguous(),
+                                               *tables, damping, prm, True)
+        ctx.save_for_backward(g, plan.dst)
+        ctx.mark_non_differentiable(cn, w)
+        return e_atom, cn, w
+
+    @staticmethod
+    @torch.autograd.function.once_differentiable
+    def backward(ctx, ge, gcn, gw):
+        g, dst = ctx.saved_tensors
+        return g * ge.index_select(0, dst)[:, None], None, None, None, None, None
+
+
 class DFTD3(nn.Module):
     """The D3 energy of one or several structures from a neighbour list (see module notes)."""
 
@@ -123,6 +148,33 @@ class DFTD3(nn.Module):
         sw = switching_function(r, self.cutoff_pair / BOHR, self.switch_width_pair / BOHR)
         return scatter_sum(-0.5 * c6 * sw * (self.s6 * t6 + self.s8 * rr * t8), dst, n)
 
+    # ------------------------------------------------------------------ native two-body path
+    def kernels_usable(self, edge_vec: Tensor) -> bool:
+        """The native passes take the two-body term: rational or zero damping, no three-body term,
+        fixed parameters, evaluation mode (first derivatives), ``use_kernels`` not switched off."""
+        from .. import _ext
+        return (getattr(self, "use_kernels", True) and not self.training and self.damping in ("bj", "zero")
+                and not any(isinstance(getattr(self, k), nn.Parameter) for k in ("s6", "s8", "a1", "a2"))
+                and float(self.s9) == 0.0 and _ext.available() and hasattr(_ext.ops(), "d3_two_body"))
+
+    def _tables(self, device):
+        key = str(device)
+        cache = self.__dict__.setdefault("_table_cache", {})
+        if key not in cache:
+            f = lambda t: t.detach().to(device=device, dtype=torch.float64).contiguous()  # noqa: E731
+            cache[key] = (f(self.rcov), f(self.r4r2), f(self.rvdw), self.nref.to(device).contiguous(),
+                          f(self.refcn), f(self.c6ref))
+        return cache[key]
+
+    def _two_body_kernel(self, z: Tensor, edge_index: Tensor, vec: Tensor):
+        from ..ops.mace_ops import EdgePlan
+        n = z.shape[0]
+        plan = EdgePlan.build(edge_index, n)
+        prm = [float(self.s6), float(self.s8), float(self.a1), float(self.a2), float(self.rs6), float(self.rs8),
+               float(self.alp), KCN, WF, self.cutoff_cn / BOHR, self.cutoff_pair / BOHR, self.switch_width_pair / BOHR]
+        return _TwoBodyKernel.apply(vec.to(torch.float64), z.contiguous(), plan, self._tables(z.device),
+                                    0 if self.damping == "bj" else 1, prm)
+
     # ------------------------------------------------------------------ evaluation
     def evaluate(self, atomic_numbers: Tensor, pos: Tensor, edge_index: Tensor, edge_vec: Tensor, batch: Tensor,
                  num_graphs: int, cell: Tensor, pbc: Tensor, total_charge: Tensor) -> Dict[str, Tensor]:
@@ -133,6 +185,16 @@ class DFTD3(nn.Module):
         if bool((z > MAX_Z).any()) or bool((z < 1).any()):
             raise ValueError("D3 reference data cover atomic numbers 1..103")
         vec = edge_vec / BOHR
+        if self.kernels_usable(edge_vec):
+            e2, cn, w = self._two_body_kernel(z, edge_index, vec)
+            c6_self = torch.einsum("na,abn,nb->n", w, self._tables(z.device)[5][:, :, z, z], w)
+            e2, cn, c6_self = (t.to(edge_vec.dtype) for t in (e2, cn, c6_self))
+            empty = torch.zeros((0, 0), dtype=edge_vec.dtype, device=edge_vec.device)
+            return {"node_energy": e2 * HARTREE,
+                    "energy_2body": structure_sum(e2, batch, num_graphs) * HARTREE,
+                    "energy_3body": torch.zeros(num_graphs, dtype=e2.dtype, device=e2.device),
+                    "coordination_numbers": cn, "c6_matrix": empty,
+                    "node_features": torch.stack([cn, c6_self], 1)}
         r = torch.linalg.norm(vec, dim=-1)
         cn = self.coordination_numbers(z, edge_index, r, n)
         w = self.reference_weights(z, cn)
