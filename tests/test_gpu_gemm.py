@@ -109,3 +109,16 @@ def test_fused_radial_network_matches_stages():
     R2 = lean_conv._primal(r, We, spec)
     for a, b in ((R1, R0), (Rd1, Rd0), (R2, R0)):
         assert ((a - b).abs().max() / b.abs().max()) < 1e-5
+
+
+def test_reduction_with_wide_left_operand_swaps():
+    """``X^T D`` with ``X`` wider than the reduction kernel takes runs as ``(D^T X)^T``."""
+    g = torch.Generator(device="cuda").manual_seed(3)
+    X = torch.randn(40000, 192, device="cuda", generator=g)
+    D = torch.randn(40000, 64, device="cuda", generator=g)
+    want = (X.double().t() @ D.double()).float()
+    got = gemm.mm_t_raw(X, D)
+    assert got.shape == (192, 64)
+    torch.testing.assert_close(got, want, rtol=2e-5, atol=2e-3)
+    got2 = gemm.matmul_t(X, D)
+    torch.testing.assert_close(got2, want, rtol=2e-5, atol=2e-3)

@@ -91,9 +91,12 @@ def rows_per_cta(M: int, target_ctas: int = 296) -> int:
 
 
 def mm_t_raw(X: Tensor, D: Tensor) -> Tensor:
-    """``X^T @ D`` summed over the rows, without autograd (tensor cores, deterministic split-K)."""
+    """``X^T @ D`` summed over the rows, without autograd (tensor cores, deterministic split-K;
+    ``(D^T X)^T`` when only the swapped operands fit the kernel)."""
     if reduce_supported(X, D):
         return _ext.ops().gemm_reduce_tf32x3(X, D, rows_per_cta(X.shape[0]), 1.0, _status(X.device), SPIN_LIMIT)
+    if reduce_supported(D, X):
+        return _ext.ops().gemm_reduce_tf32x3(D, X, rows_per_cta(D.shape[0]), 1.0, _status(D.device), SPIN_LIMIT).t()
     return X.t() @ D
 
 
@@ -170,6 +173,11 @@ def matmul(X: Tensor, W: Tensor) -> Tensor:
 
 def matmul_t(X: Tensor, D: Tensor) -> Tensor:
     """``X^T @ D`` summed over the rows of ``X (M, K1)`` and ``D (M, N)``."""
-    if not _tc_ok(X, D) or not reduce_supported(X.contiguous(), D.contiguous()):
+    if not _tc_ok(X, D):
         return X.t() @ D
-    return _MMT.apply(X, D)
+    Xc, Dc = X.contiguous(), D.contiguous()
+    if reduce_supported(Xc, Dc):
+        return _MMT.apply(X, D)
+    if reduce_supported(Dc, Xc):
+        return _MMT.apply(D, X).t()
+    return X.t() @ D
