@@ -145,6 +145,16 @@ def pme_ops(n_atoms: int) -> Dict[str, tuple]:
     out["mp_real"] = (lambda: ops.mp_real(w["pos"], w["cell"], q, d, Q, pol, i, j, shift, excl, 0.4, 0.39, True,
                                           True),
                       i.shape[0] * (8 + 8 + 24 + 1) + n * site)
+    # one induction iteration's pieces: the dipole field product over receiver-ordered pair entries
+    # (int32 partner, 3 + 2 float64 per entry, each pair twice) and the dipole-only spread / gather
+    mod = MP.PolarizableMultipoles(MP.EwaldSetup(alpha=0.4, cutoff=7.0, mesh=(128, 128, 128), order=5))
+    T = MP.DipoleOperator(mod, w["pos"], w["cell"], (i, j, shift, excl), pol)
+    rows = T._csr()
+    out["dipole_csr_matvec"] = (lambda: T.real(d), 2 * i.shape[0] * (4 + 5 * 8) + n * 8 * (3 + 3) + 8 * (n + 1))
+    dargs = args[:6] + (None, d, None)
+    out["pme_spread_dipoles"] = (lambda: ops.pme_spread(*dargs), n * (8 * 6) + 4 * m)
+    out["pme_gather_dipoles"] = (lambda: ops.pme_gather(*dargs, phi, True, False), n * (8 * 6 + 8 * 3) + 4 * m)
+    del rows
     return out
 
 

@@ -56,13 +56,15 @@ def region(name: str):
             torch.cuda.nvtx.range_pop()
 
 
-def kernel_table(fn: Callable[[], object], warmup: int = 1) -> Dict[str, object]:
-    """GPU kernels launched by one call of ``fn`` (after ``warmup`` untimed calls)."""
+def kernel_table(fn: Callable[[], object], warmup: int = 1, ops: bool = False) -> Dict[str, object]:
+    """GPU kernels launched by one call of ``fn`` (after ``warmup`` untimed calls); with ``ops``
+    also the host operators that launched device work, by count (``"ops"``)."""
     from torch.profiler import ProfilerActivity, profile
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+    acts = [ProfilerActivity.CUDA] + ([ProfilerActivity.CPU] if ops else [])
+    with profile(activities=acts) as prof:
         fn()
         torch.cuda.synchronize()
     count: Dict[str, int] = defaultdict(int)
@@ -79,8 +81,13 @@ def kernel_table(fn: Callable[[], object], warmup: int = 1) -> Dict[str, object]
     own_us = sum(float(r["us"]) for r in rows if r["own"])
     tot_n = sum(int(r["launches"]) for r in rows)
     own_n = sum(int(r["launches"]) for r in rows if r["own"])
-    return {"rows": rows, "device_us": round(tot_us, 1), "launches": tot_n, "own_launches": own_n,
-            "own_time_share": round(own_us / tot_us, 4) if tot_us else None}
+    out = {"rows": rows, "device_us": round(tot_us, 1), "launches": tot_n, "own_launches": own_n,
+           "own_time_share": round(own_us / tot_us, 4) if tot_us else None}
+    if ops:
+        avg = [k for k in prof.key_averages() if getattr(k, "self_device_time_total", 0) > 0]
+        avg.sort(key=lambda k: -k.count)
+        out["ops"] = [{"op": k.key, "calls": k.count, "us": round(float(k.self_device_time_total), 1)} for k in avg]
+    return out
 
 
 def _mace_step(batch: int):
@@ -168,6 +175,7 @@ def main(argv=None) -> None:
     ap.add_argument("--batch", type=int, default=None, help="structures per step (64 MACE, 32 TensorNet)")
     ap.add_argument("--top", type=int, default=40)
     ap.add_argument("--json", default=None, help="also write the table as JSON to this path")
+    ap.add_argument("--ops", action="store_true", help="also list the host operators that launched device work")
     a = ap.parse_args(argv)
     if a.model == "mace":
         fn = _mace_step(a.batch or 64)
@@ -177,11 +185,15 @@ def main(argv=None) -> None:
         fn = _pme_eval(a.batch or 100_000)
     else:
         fn = _md_step(a.batch or 1_000_000)
-    tab = kernel_table(fn, warmup=3)
+    tab = kernel_table(fn, warmup=3, ops=a.ops)
     print(f"launches {tab['launches']} (own {tab['own_launches']}), device time {tab['device_us']} us, "
           f"own-kernel share {tab['own_time_share']}")
     for r in tab["rows"][:a.top]:
         print(f"{r['us']:10.1f} us {r['launches']:5d}  {'*' if r['own'] else ' '} {r['kernel'][:120]}")
+    if a.ops:
+        print("host operators launching device work (calls, device us):")
+        for r in tab["ops"][:a.top]:
+            print(f"{r['calls']:6d} {r['us']:10.1f} us  {r['op'][:100]}")
     if a.json:
         import json
         with open(a.json, "w") as f:
