@@ -111,3 +111,27 @@ def test_step_matches_autograd_other_degrees(max_ell, correlation):
     for name in g0:
         err = (g1[name] - g0[name]).abs().max() / g0[name].abs().max().clamp_min(1e-12)
         assert err < 1e-8, (name, float(err))
+
+
+@pytest.mark.gpu
+def test_fused_loss_kernel_matches_formulas(monkeypatch):
+    """The one-kernel loss (both terms, sums, cotangents) against the PyTorch formulas, on a padded
+    batch (structure masks and per-atom force weights)."""
+    import xnn_b200.ops.mace_ops as K
+    from xnn_b200.train.graphed import pad_graph
+    pot, b = _setup(torch.float32, "cuda", channels=8, n_struct=5)
+    b = pad_graph(b, b.num_nodes + 12, b.num_edges + 40, b.num_graphs + 2, 4.5)
+    b.weight = torch.linspace(0.5, 1.5, b.num_graphs, dtype=torch.float64, device="cuda")
+    step = mace_step.MACEStep(pot, 1.0, 10.0)
+    g0 = torch.Generator(device="cuda").manual_seed(3)
+    energy = torch.randn(b.num_graphs, device="cuda", generator=g0)
+    forces = torch.randn(b.num_nodes, 3, device="cuda", dtype=torch.float64, generator=g0)
+    assert hasattr(K._C(), "mace_loss")
+    l1, logs1, a1, f1 = step._loss(b, energy, forces)
+    monkeypatch.setattr(K, "_C", lambda: object())        # no kernel: the PyTorch formulas
+    l0, logs0, a0, f0 = step._loss(b, energy, forces)
+    torch.testing.assert_close(l1, l0, rtol=1e-12, atol=1e-14)
+    torch.testing.assert_close(a1.to(a0.dtype), a0, rtol=1e-10, atol=1e-14)
+    torch.testing.assert_close(f1, f0, rtol=1e-10, atol=1e-14)
+    for k in logs0:
+        torch.testing.assert_close(logs1[k], logs0[k], rtol=1e-12, atol=1e-14)

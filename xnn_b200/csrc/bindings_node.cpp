@@ -86,6 +86,12 @@ template <typename T>
 cudaError_t segment_rows_sum(int groups, int cols, const int* perm, const int* seg, const T* X, T* out,
                              cudaStream_t s);
 
+template <typename TF>
+cudaError_t mace_loss(int B, int N, const double* energy, const double* eref, const int64_t* n_atoms, const double* sw,
+                      const double* ew, const bool* em, const TF* forces, const double* fref, const int64_t* batch,
+                      const double* fw, const bool* fm, const double* afw, double we, double wf, double* out,
+                      double* a, TF* g, cudaStream_t s);
+
 namespace {
 
 void need_f32(const torch::Tensor& t, const char* what) {
@@ -394,7 +400,53 @@ torch::Tensor segment_rows_sum_op(torch::Tensor X, torch::Tensor perm, torch::Te
   return out;
 }
 
+// (out (3,) = [loss, energy term, force term], a (B,), g (N, 3)) of the step's loss; optional
+// float64 / bool weight and mask arrays (None: absent); eref / fref None switch a term off
+std::vector<torch::Tensor> mace_loss_op(torch::Tensor energy, c10::optional<torch::Tensor> eref, torch::Tensor n_atoms,
+                                        c10::optional<torch::Tensor> sw, c10::optional<torch::Tensor> ew,
+                                        c10::optional<torch::Tensor> em, torch::Tensor forces,
+                                        c10::optional<torch::Tensor> fref, torch::Tensor batch,
+                                        c10::optional<torch::Tensor> fw, c10::optional<torch::Tensor> fm,
+                                        c10::optional<torch::Tensor> afw, double we, double wf) {
+  auto d64 = [](const c10::optional<torch::Tensor>& t, const char* what) -> const double* {
+    if (!t.has_value() || !t->defined()) return nullptr;
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat64 && t->is_contiguous(), "mace_loss: ", what,
+                " float64 contiguous");
+    return t->data_ptr<double>();
+  };
+  auto b8 = [](const c10::optional<torch::Tensor>& t, const char* what) -> const bool* {
+    if (!t.has_value() || !t->defined()) return nullptr;
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kBool && t->is_contiguous(), "mace_loss: ", what, " bool");
+    return t->data_ptr<bool>();
+  };
+  TORCH_CHECK(energy.scalar_type() == torch::kFloat64 && energy.is_contiguous(), "mace_loss: float64 energy");
+  TORCH_CHECK(n_atoms.scalar_type() == torch::kInt64 && batch.scalar_type() == torch::kInt64, "mace_loss: int64");
+  TORCH_CHECK(forces.is_contiguous() && forces.dim() == 2 && forces.size(1) == 3, "mace_loss: forces (N, 3)");
+  c10::cuda::CUDAGuard guard(energy.device());
+  const int B = (int)energy.numel(), N = (int)forces.size(0);
+  auto out = torch::empty({3}, energy.options());
+  auto a = torch::empty({B}, energy.options());
+  auto g = torch::empty_like(forces);
+  auto st = at::cuda::getCurrentCUDAStream();
+  cudaError_t e;
+  if (forces.scalar_type() == torch::kFloat64)
+    e = mace_loss<double>(B, N, energy.data_ptr<double>(), d64(eref, "eref"), n_atoms.data_ptr<int64_t>(),
+                          d64(sw, "sw"), d64(ew, "ew"), b8(em, "em"), forces.data_ptr<double>(), d64(fref, "fref"),
+                          batch.data_ptr<int64_t>(), d64(fw, "fw"), b8(fm, "fm"), d64(afw, "afw"), we, wf,
+                          out.data_ptr<double>(), a.data_ptr<double>(), g.data_ptr<double>(), st);
+  else {
+    TORCH_CHECK(forces.scalar_type() == torch::kFloat32, "mace_loss: float32 or float64 forces");
+    e = mace_loss<float>(B, N, energy.data_ptr<double>(), d64(eref, "eref"), n_atoms.data_ptr<int64_t>(),
+                         d64(sw, "sw"), d64(ew, "ew"), b8(em, "em"), forces.data_ptr<float>(), d64(fref, "fref"),
+                         batch.data_ptr<int64_t>(), d64(fw, "fw"), b8(fm, "fm"), d64(afw, "afw"), we, wf,
+                         out.data_ptr<double>(), a.data_ptr<double>(), g.data_ptr<float>(), st);
+  }
+  TORCH_CHECK(e == cudaSuccess, "mace_loss: ", cudaGetErrorString(e));
+  return {out, a, g};
+}
+
 void register_node(pybind11::module& m) {
+  m.def("mace_loss", &mace_loss_op);
   m.def("edge_forces", &edge_forces_op);
   m.def("segment_rows_sum", &segment_rows_sum_op);
   m.def("mace_dual_reverse", &mace_dual_reverse_op);

@@ -247,6 +247,109 @@ cudaError_t segment_rows_sum(int groups, int cols, const int* perm, const int* s
   return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------------------------ loss
+// The energy / force loss of the training step and its cotangents in one CTA (batches hold a few
+// thousand atoms): per-structure weights w_s = weight * energy_weight * energy_mask (each optional),
+// per-atom force weights wa_i = (weight * force_weight * forces_mask)[batch_i] * atom_force_weight_i;
+// L = we sum w_s r_s^2 / sum w_s + wf sum wa_i |dF_i|^2 / 3 / sum wa_i with r_s = (E_s - E_ref) / n_s;
+// a_s = dL/dE_s, g_i = dL/dF_i. Fixed-order strided sums and a fixed tree: deterministic.
+template <typename TF>
+__global__ void __launch_bounds__(1024) mace_loss_kernel(
+    int B, int N, const double* __restrict__ energy, const double* __restrict__ eref,
+    const int64_t* __restrict__ n_atoms, const double* __restrict__ sw, const double* __restrict__ ew,
+    const bool* __restrict__ em, const TF* __restrict__ forces, const double* __restrict__ fref,
+    const int64_t* __restrict__ batch, const double* __restrict__ fw, const bool* __restrict__ fm,
+    const double* __restrict__ afw, double we, double wf, double* __restrict__ out, double* __restrict__ a,
+    TF* __restrict__ g) {
+  __shared__ double red[4][32];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  auto w_energy = [&](int s) {
+    double w = sw ? sw[s] : 1.0;
+    if (ew) w *= ew[s];
+    if (em) w *= em[s] ? 1.0 : 0.0;
+    return w;
+  };
+  auto w_force = [&](int i) {
+    const int64_t s = batch[i];
+    double w = sw ? sw[s] : 1.0;
+    if (fw) w *= fw[s];
+    if (fm) w *= fm[s] ? 1.0 : 0.0;
+    if (afw) w *= afw[i];
+    return w;
+  };
+  double v[4] = {0.0, 0.0, 0.0, 0.0};     // sum w_s, sum w_s r^2, sum wa, sum wa sq
+  if (eref)
+    for (int s = t; s < B; s += blockDim.x) {
+      const double r = (energy[s] - eref[s]) / (double)n_atoms[s];
+      const double w = w_energy(s);
+      v[0] += w;
+      v[1] += w * r * r;
+    }
+  if (fref)
+    for (int i = t; i < N; i += blockDim.x) {
+      double sq = 0.0;
+      for (int c = 0; c < 3; ++c) {
+        const double d = (double)forces[3 * i + c] - fref[3 * i + c];
+        sq += d * d;
+      }
+      const double w = w_force(i);
+      v[2] += w;
+      v[3] += w * sq / 3.0;
+    }
+  for (int k = 0; k < 4; ++k) {
+    for (int off = 16; off > 0; off >>= 1) v[k] += __shfl_xor_sync(0xffffffffu, v[k], off);
+    if (lane == 0) red[k][warp] = v[k];
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    for (int k = 0; k < 4; ++k) {
+      double x = lane < nw ? red[k][lane] : 0.0;
+      for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+      if (lane == 0) red[k][0] = x;
+    }
+  }
+  __syncthreads();
+  const double den_e = fmax(red[0][0], 1e-12), den_f = fmax(red[2][0], 1e-12);
+  const double e_term = red[1][0] / den_e, f_term = red[3][0] / den_f;
+  if (t == 0) {
+    out[1] = eref ? e_term : 0.0;
+    out[2] = fref ? f_term : 0.0;
+    out[0] = (eref ? we * e_term : 0.0) + (fref ? wf * f_term : 0.0);
+  }
+  for (int s = t; s < B; s += blockDim.x) {
+    if (eref) {
+      const double n = (double)n_atoms[s];
+      a[s] = 2.0 * we * w_energy(s) * (energy[s] - eref[s]) / n / n / den_e;
+    } else {
+      a[s] = 0.0;
+    }
+  }
+  for (int i = t; i < N; i += blockDim.x) {
+    const double c = fref ? (2.0 * wf / 3.0) * w_force(i) / den_f : 0.0;
+    for (int k = 0; k < 3; ++k)
+      g[3 * i + k] = fref ? (TF)(c * ((double)forces[3 * i + k] - fref[3 * i + k])) : TF(0);
+  }
+}
+
+template <typename TF>
+cudaError_t mace_loss(int B, int N, const double* energy, const double* eref, const int64_t* n_atoms, const double* sw,
+                      const double* ew, const bool* em, const TF* forces, const double* fref, const int64_t* batch,
+                      const double* fw, const bool* fm, const double* afw, double we, double wf, double* out,
+                      double* a, TF* g, cudaStream_t s) {
+  mace_loss_kernel<TF><<<1, 1024, 0, s>>>(B, N, energy, eref, n_atoms, sw, ew, em, forces, fref, batch, fw, fm, afw,
+                                          we, wf, out, a, g);
+  return cudaGetLastError();
+}
+template cudaError_t mace_loss<float>(int, int, const double*, const double*, const int64_t*, const double*,
+                                      const double*, const bool*, const float*, const double*, const int64_t*,
+                                      const double*, const bool*, const double*, double, double, double*, double*,
+                                      float*, cudaStream_t);
+template cudaError_t mace_loss<double>(int, int, const double*, const double*, const int64_t*, const double*,
+                                       const double*, const bool*, const double*, const double*, const int64_t*,
+                                       const double*, const bool*, const double*, double, double, double*, double*,
+                                       double*, cudaStream_t);
+
 template cudaError_t edge_forces<float, double>(int, const int64_t*, const int64_t*, const int64_t*, const int64_t*,
                                                 const float*, double*, cudaStream_t);
 template cudaError_t edge_forces<float, float>(int, const int64_t*, const int64_t*, const int64_t*, const int64_t*,

@@ -705,6 +705,21 @@ class MACEStep:
         """Energy and force terms of ``weighted_loss`` and their cotangents ``a = dL/dE``,
         ``g = dL/dF``."""
         logs: Dict[str, Tensor] = {}
+        has_e, has_f = self.we > 0 and b.energy is not None, self.wf > 0 and b.forces is not None
+        if energy.is_cuda and forces.dtype in (torch.float32, torch.float64) and hasattr(K._C(), "mace_loss"):
+            # one kernel: both terms, their sums and the cotangents
+            f64 = lambda t: None if t is None else t.to(torch.float64).contiguous()  # noqa: E731
+            msk = lambda t: None if t is None else t.to(torch.bool).contiguous()  # noqa: E731
+            out, a, g = K._C().mace_loss(
+                energy.to(torch.float64).contiguous(), f64(b.energy) if has_e else None, b.n_atoms.long().contiguous(),
+                f64(b.weight), f64(b.energy_weight), msk(b.energy_mask), forces.contiguous(),
+                f64(b.forces) if has_f else None, b.batch.long().contiguous(), f64(b.force_weight),
+                msk(b.forces_mask), f64(b.atom_force_weight), float(self.we), float(self.wf))
+            if has_e:
+                logs["energy"] = out[1]
+            if has_f:
+                logs["forces"] = out[2]
+            return out[0], logs, a, g
         total = torch.zeros((), dtype=torch.float64, device=energy.device)
         a = torch.zeros_like(energy)
         g = torch.zeros_like(forces)
