@@ -5,6 +5,7 @@
   ``synthetic:<organic|crystals|water>:<count>``) and run ``Trainer(cfg, data).fit()``; under
   ``torchrun`` every process joins the data-parallel run;
 * ``benchmark --model M --data FILE [--format json|csv|md] [--out FILE]``: error metrics;
+  ``benchmark --suite FILE [--models A,B | --shard I/N | --parallel [K] | --merge]``: several models;
 * ``export --model M --format lammps|torchscript --out FILE``;
 * ``mdi --model M --mdi "<MDI options>"``: serve the model as an MDI engine;
 * ``models``: registered architectures and locally registered pretrained models.
@@ -55,8 +56,28 @@ def cmd_train(args) -> int:
 
 
 def cmd_benchmark(args) -> int:
+    if args.suite:
+        from ..benchmark import suite as S
+        if args.parallel is not None:
+            rows = S.run_parallel(args.suite, args.parallel)
+        else:
+            cfg = S.load_suite(args.suite)
+            if args.device:
+                cfg["device"] = args.device
+            if args.merge:
+                rows = S.merge_parts(cfg)
+            else:
+                entries = S.select_entries(cfg, args.models, args.shard)
+                rows = S.score(cfg, entries)
+                S.write_part(cfg, rows, entries)
+                if args.models is None and args.shard is None:
+                    S.write_table(cfg, rows)
+        print(json.dumps(rows, indent=1))
+        return 0
+    if not args.model or not args.data:
+        raise SystemExit("benchmark needs --model and --data, or --suite")
     from ..benchmark import format_report, run_benchmark
-    report = run_benchmark(args.model, args.data, args.batch_size, args.device, args.format, args.out)
+    report = run_benchmark(args.model, args.data, args.batch_size, args.device or "cpu", args.format, args.out)
     print(format_report(report, args.format))
     return 0
 
@@ -97,10 +118,16 @@ def build_parser() -> argparse.ArgumentParser:
     t.add_argument("--set", action="append", default=[])
     t.set_defaults(fn=cmd_train)
     b = sub.add_parser("benchmark")
-    b.add_argument("--model", required=True)
-    b.add_argument("--data", required=True)
+    b.add_argument("--model")
+    b.add_argument("--data")
+    b.add_argument("--suite", help="a suite YAML of several models (see xnn_b200.benchmark.suite)")
+    b.add_argument("--models", help="suite: labels or positions to score, comma separated")
+    b.add_argument("--shard", help="suite: I/N (every N-th model from I) or 'slurm'")
+    b.add_argument("--parallel", type=int, nargs="?", const=0, default=None,
+                   help="suite: one worker per model, this many at once (default: one per visible GPU)")
+    b.add_argument("--merge", action="store_true", help="suite: assemble the part files into the table")
     b.add_argument("--batch-size", type=int, default=16)
-    b.add_argument("--device", default="cpu")
+    b.add_argument("--device", default=None)
     b.add_argument("--format", default="json", choices=["json", "csv", "md"])
     b.add_argument("--out")
     b.set_defaults(fn=cmd_benchmark)
