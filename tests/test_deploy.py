@@ -133,3 +133,36 @@ def test_mdi_engine_protocol():
     assert abs(comm.sent[0][0] * HARTREE - float(ref["energy"].sum().detach())) < 1e-9
     np.testing.assert_allclose(np.array(comm.sent[1]).reshape(-1, 3) * HARTREE / BOHR,
                                ref["forces"].detach().numpy(), rtol=1e-8, atol=1e-9)
+
+
+def test_mdi_engine_cell_charge_stress_and_stats():
+    from xnn_b200.deploy.mdi_engine import MDIEngine
+    from xnn_b200.models.dispersion import BOHR, HARTREE
+    m = _model()
+    s = synthetic.triclinic_crystals(1, seed=3, n_min=10, n_max=14, z_max=17, labels=False)[0]
+    n = s["pos"].shape[0]
+
+    class Comm:
+        def __init__(self, script):
+            self.script, self.sent = list(script), []
+
+        def recv_command(self):
+            return self.script.pop(0)
+
+        def recv(self, count, kind):
+            return self.script.pop(0)
+
+        def send(self, values, kind):
+            self.sent.append(list(values))
+
+    comm = Comm([">NATOMS", [n], ">ELEMENTS", s["atomic_numbers"].tolist(), ">TOTCHARGE", [0.0],
+                 ">CELL", (s["cell"] / BOHR).reshape(-1).tolist(), ">COORDS", (s["pos"] / BOHR).reshape(-1).tolist(),
+                 "SCF", "<ENERGY", "<STRESS", "<CELL", "EXIT"])
+    eng = MDIEngine(m)
+    eng.serve(comm)
+    ref = ForceStressOutput(m, compute_stress=True)(structure_to_graph(s, 4.5))
+    assert abs(comm.sent[0][0] * HARTREE - float(ref["energy"].sum().detach())) < 1e-9
+    np.testing.assert_allclose(-np.array(comm.sent[1]).reshape(3, 3) * HARTREE / BOHR ** 3,
+                               ref["stress"][0].detach().numpy(), rtol=1e-7, atol=1e-10)
+    np.testing.assert_allclose(np.array(comm.sent[2]).reshape(3, 3) * BOHR, s["cell"].numpy(), rtol=1e-12)
+    assert eng.stats()["evaluations"] == 1
