@@ -114,6 +114,22 @@ def test_neighbor_list_cuda_matches_cpu():
         assert torch.equal(ka, kb)
 
 
+def test_neighbor_list_warp_kernel_matches_thread_kernel(monkeypatch):
+    """The warp-per-receiver search gives the thread-per-receiver kernel's edges in the same order
+    (and a receiver range its share)."""
+    from xnn_b200.data.neighborlist import build_neighbor_list
+    for s in synthetic.triclinic_crystals(2, seed=7, labels=False) + [synthetic.water_box(6000)]:
+        args = (s["pos"].cuda(), 5.0, s["cell"].cuda(), s["pbc"])
+        a = build_neighbor_list(*args, engine="native")
+        r = build_neighbor_list(*args, engine="native", receivers=(7, s["pos"].shape[0] // 2))
+        monkeypatch.setenv("XNN_B200_NB_THREAD", "1")
+        b = build_neighbor_list(*args, engine="native")
+        rb = build_neighbor_list(*args, engine="native", receivers=(7, s["pos"].shape[0] // 2))
+        monkeypatch.delenv("XNN_B200_NB_THREAD")
+        assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+        assert torch.equal(r[0], rb[0]) and torch.equal(r[1], rb[1])
+
+
 def test_schnet_cfconv_kernel_matches_torch_path():
     from xnn_b200.models import ForceStressOutput
     from xnn_b200.models.schnet import SchNet

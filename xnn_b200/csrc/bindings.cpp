@@ -4,6 +4,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+
 #include <cmath>
 #include <vector>
 
@@ -35,6 +37,10 @@ template <typename T>
 cudaError_t symcon_bwd2(int, int, int, int, const T*, const int64_t*, const T*, const T*, const T*,
                         const T*, T*, T*, T*, cudaStream_t);
 int symcon_num_invariants(int lmax, int corr);
+cudaError_t nb_count_warp_cuda(const NbParams& p, const double* pos_sorted, int64_t* counts, cudaStream_t s);
+cudaError_t nb_write_warp_cuda(const NbParams& p, const double* pos_sorted, const int64_t* offsets, int64_t* src,
+                               int64_t* dst, int64_t* shifts, cudaStream_t s);
+
 cudaError_t nb_count_cuda(const NbParams& p, int64_t* counts, cudaStream_t s);
 cudaError_t nb_write_cuda(const NbParams& p, const int64_t* offsets, int64_t* src, int64_t* dst,
                           int64_t* shifts, cudaStream_t s);
@@ -146,10 +152,17 @@ std::vector<torch::Tensor> neighbor_list(torch::Tensor pos, torch::Tensor cell, 
   const int64_t M = prm.M;
 
   auto counts = torch::empty({M}, lopt);
+  // the warp-per-receiver kernels read the candidates' positions in cell order
+  torch::Tensor pos_sorted;
+  const bool warp = pos.is_cuda() && std::getenv("XNN_B200_NB_THREAD") == nullptr;
+  if (warp) pos_sorted = p.index_select(0, sorted).contiguous();
   if (pos.is_cuda()) {
     c10::cuda::CUDAGuard g(pos.device());
     auto st = at::cuda::getCurrentCUDAStream();
-    XNN_CUDA_OK(nb_count_cuda(prm, counts.data_ptr<int64_t>(), st));
+    if (warp)
+      XNN_CUDA_OK(nb_count_warp_cuda(prm, pos_sorted.data_ptr<double>(), counts.data_ptr<int64_t>(), st));
+    else
+      XNN_CUDA_OK(nb_count_cuda(prm, counts.data_ptr<int64_t>(), st));
   } else {
     int64_t* cp = counts.data_ptr<int64_t>();
 #pragma omp parallel for schedule(dynamic, 64)
@@ -169,8 +182,12 @@ std::vector<torch::Tensor> neighbor_list(torch::Tensor pos, torch::Tensor cell, 
     if (pos.is_cuda()) {
       c10::cuda::CUDAGuard g(pos.device());
       auto st = at::cuda::getCurrentCUDAStream();
-      XNN_CUDA_OK(nb_write_cuda(prm, offsets.data_ptr<int64_t>(), src.data_ptr<int64_t>(),
-                                dst.data_ptr<int64_t>(), shifts.data_ptr<int64_t>(), st));
+      if (warp)
+        XNN_CUDA_OK(nb_write_warp_cuda(prm, pos_sorted.data_ptr<double>(), offsets.data_ptr<int64_t>(),
+                                       src.data_ptr<int64_t>(), dst.data_ptr<int64_t>(), shifts.data_ptr<int64_t>(), st));
+      else
+        XNN_CUDA_OK(nb_write_cuda(prm, offsets.data_ptr<int64_t>(), src.data_ptr<int64_t>(),
+                                  dst.data_ptr<int64_t>(), shifts.data_ptr<int64_t>(), st));
     } else {
       const int64_t* op = offsets.data_ptr<int64_t>();
       int64_t* sp = src.data_ptr<int64_t>();
