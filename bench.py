@@ -495,7 +495,8 @@ def main():
             trainer._train_step_impl(dev_batches[0])
             torch.cuda.synchronize(dev)
         trainer.use_graphs = saved
-        names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+        names = [e.name for e in prof.events()
+                 if e.device_type.name == "CUDA" and not getattr(e, "is_user_annotation", False)]
         from xnn_b200.utils.profiling import is_own_kernel
         ours = [n for n in names if is_own_kernel(n)]
         launches = len(ours)

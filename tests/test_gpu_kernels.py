@@ -141,3 +141,46 @@ def test_schnet_cfconv_kernel_matches_torch_path():
     o_ref = ForceStressOutput(m.set_use_fast(False))(g.clone())
     torch.testing.assert_close(o_fast["energy"], o_ref["energy"], rtol=1e-10, atol=1e-10)
     torch.testing.assert_close(o_fast["forces"], o_ref["forces"], rtol=1e-9, atol=1e-10)
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-10), (torch.float32, 1e-4)])
+@pytest.mark.parametrize("C", [96, 160])
+def test_sender_rows_match_scatter(dtype, tol, C):
+    """Per-edge sender terms of the edge kernel, summed per sender, equal the scatter kernel's sums."""
+    g = _graph()
+    ei = g.edge_index.to("cuda")
+    N, E, P = g.num_nodes, g.num_edges, 4
+    plan = K.EdgePlan.build(ei, N)
+    ops = _ext.ops()
+    G = torch.randn(P * P, N, C, dtype=dtype, device="cuda")
+    x = torch.randn(N, C, dtype=dtype, device="cuda")
+    R = torch.randn(E, P, C, dtype=dtype, device="cuda")
+    Rd = torch.randn(E, P, C, dtype=dtype, device="cuda")
+    Y = torch.randn(E, P * P, dtype=dtype, device="cuda")
+    g_r, gY, T1, _, _ = ops.conv_edge(N, C, P, E, plan.dst_ptr, plan.src32, plan.dst_perm, G, [Y], [x], [True],
+                                      True, [x], [R], Rd)
+    ref = ops.conv_scatter(plan.n_senders, C, P, plan.src_ptr, plan.src_perm, [R], [T1])
+    g_r2, gY2, _, _, v = ops.conv_edge(N, C, P, E, plan.dst_ptr, plan.src32, plan.dst_perm, G, [Y], [x], [False],
+                                       True, [x], [R], Rd, R)
+    got = ops.conv_sender_sum(plan.n_senders, plan.src_ptr, plan.src_perm, v)
+    torch.testing.assert_close(got, ref, rtol=tol, atol=tol)
+    torch.testing.assert_close(g_r2, g_r, rtol=tol, atol=tol)
+    torch.testing.assert_close(gY2, gY, rtol=tol, atol=tol)
+
+
+def test_lean_chunks_match_single_pass():
+    """The chunked force pass (radial network recomputed per chunk) against the unchunked one."""
+    from xnn_b200.models import ForceStressOutput
+    from xnn_b200.models.mace import MACE
+    torch.manual_seed(0)
+    m = MACE(species=[1, 6, 7, 8], cutoff=4.5, num_channels=32, max_ell=3, correlation=3, num_interactions=2,
+             hidden_irreps="32x0e").double().cuda().eval().set_use_fast(True)
+    f = ForceStressOutput(m)
+    b = _graph(n=5, seed=3).to("cuda")
+    b.pos = b.pos.double()
+    m.edge_chunk = None
+    o1 = f(b.clone())
+    m.edge_chunk = 301
+    o2 = f(b.clone())
+    torch.testing.assert_close(o2["energy"], o1["energy"], rtol=1e-11, atol=1e-11)
+    torch.testing.assert_close(o2["forces"], o1["forces"], rtol=1e-10, atol=1e-10)

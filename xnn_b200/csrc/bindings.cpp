@@ -25,7 +25,9 @@ cudaError_t conv_gather(int, int, int, const int64_t*, const int*, const int64_t
 template <typename T>
 cudaError_t conv_edge(int, int, int, const int64_t*, const int*, const int64_t*, const T*, int,
                       const T* const*, const T* const*, T* const*, int, const T* const*, const T* const*, T*, T*,
-                      const T*, T*, cudaStream_t);
+                      const T*, T*, const T*, T*, cudaStream_t);
+template <typename T>
+cudaError_t conv_sender_sum(int, int, const int64_t*, const int64_t*, const T*, T*, cudaStream_t);
 template <typename T>
 cudaError_t conv_scatter(int, int, int, const int64_t*, const int64_t*, int, const T* const*, const T* const*,
                          T*, cudaStream_t);
@@ -301,14 +303,15 @@ torch::Tensor conv_gather_op(int64_t N, int64_t C, int64_t P, torch::Tensor dst_
   return A;
 }
 
-// Returns [gR, gY, T_0, T_1] (undefined where not requested). Ys: 0-2 Y terms; xs: per Y term
-// an x for gR or an undefined tensor; want_T: per Y term whether T_t is written; want_gR.
+// Returns [gR, gY, T_0, T_1, gxe] (undefined where not requested). Ys: 0-2 Y terms; xs: per Y term
+// an x for gR or an undefined tensor; want_T: per Y term whether T_t is written; want_gR. With Rx
+// (E, P, C): gxe[e, c] = sum_l T_0[e, l, c] Rx[e, l, c] (E, C), the edge's term of the sender cotangent.
 std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t E, torch::Tensor dst_ptr,
                                         torch::Tensor src, c10::optional<torch::Tensor> perm, torch::Tensor G,
                                         std::vector<torch::Tensor> Ys, std::vector<c10::optional<torch::Tensor>> xs,
                                         std::vector<bool> want_T, bool want_gR,
                                         std::vector<torch::Tensor> xY, std::vector<torch::Tensor> RY,
-                                        c10::optional<torch::Tensor> Rd) {
+                                        c10::optional<torch::Tensor> Rd, c10::optional<torch::Tensor> Rx) {
   // with Rd (E, P, C): the first output is g_r[e] = sum_{l,c} gR[e,l,c] Rd[e,l,c] (E,) instead of gR
   TORCH_CHECK(Ys.size() == xs.size() && Ys.size() == want_T.size() && Ys.size() <= 2,
               "conv_edge: 0-2 Y terms with matching x / want_T");
@@ -328,6 +331,12 @@ std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t
   std::vector<torch::Tensor> Ts(2);
   for (size_t k = 0; k < Ys.size(); ++k)
     if (want_T[k]) Ts[k] = torch::empty({E, P, C}, G.options());
+  const bool sender = Rx.has_value() && Rx->defined();
+  if (sender) {
+    check_cuda(*Rx, "Rx");
+    TORCH_CHECK(!Ys.empty() && Rx->is_contiguous() && Rx->numel() == E * P * C, "conv_edge: Rx (E, P, C)");
+  }
+  torch::Tensor gxe = sender ? torch::empty({E, C}, G.options()) : torch::Tensor();
   auto st = at::cuda::getCurrentCUDAStream();
   AT_DISPATCH_FLOATING_TYPES(G.scalar_type(), "conv_edge", [&] {
     auto pY = ptrs<scalar_t>(Ys, "Y");
@@ -351,9 +360,29 @@ std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t
                                     gR.defined() ? gR.data_ptr<scalar_t>() : nullptr,
                                     gY.defined() ? gY.data_ptr<scalar_t>() : nullptr,
                                     contract ? Rd->data_ptr<scalar_t>() : nullptr,
-                                    g_r.defined() ? g_r.data_ptr<scalar_t>() : nullptr, st));
+                                    g_r.defined() ? g_r.data_ptr<scalar_t>() : nullptr,
+                                    sender ? Rx->data_ptr<scalar_t>() : nullptr,
+                                    sender ? gxe.data_ptr<scalar_t>() : nullptr, st));
   });
-  return {contract ? g_r : gR, gY, Ts[0], Ts[1]};
+  return {contract ? g_r : gR, gY, Ts[0], Ts[1], gxe};
+}
+
+// gx[s] = sum over the edges out of s of v[e] (v (E, C), the gxe rows of conv_edge)
+torch::Tensor conv_sender_sum_op(int64_t N, torch::Tensor src_ptr, torch::Tensor src_perm, torch::Tensor v) {
+  check_cuda(v, "v");
+  TORCH_CHECK(v.dim() == 2 && v.is_contiguous(), "conv_sender_sum: v (E, C) contiguous");
+  TORCH_CHECK(src_ptr.scalar_type() == torch::kLong && src_perm.scalar_type() == torch::kLong &&
+                  src_ptr.numel() == N + 1 && src_perm.numel() == v.size(0),
+              "conv_sender_sum: int64 src_ptr (N + 1) and src_perm (E)");
+  c10::cuda::CUDAGuard g(v.device());
+  auto gx = torch::empty({N, v.size(1)}, v.options());
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(v.scalar_type(), "conv_sender_sum", [&] {
+    XNN_CUDA_OK(conv_sender_sum<scalar_t>((int)N, (int)v.size(1), src_ptr.data_ptr<int64_t>(),
+                                          src_perm.data_ptr<int64_t>(), v.data_ptr<scalar_t>(),
+                                          gx.data_ptr<scalar_t>(), st));
+  });
+  return gx;
 }
 
 torch::Tensor conv_scatter_op(int64_t N, int64_t C, int64_t P, torch::Tensor src_ptr, torch::Tensor src_perm,
@@ -446,7 +475,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv_edge", &conv_edge_op, pybind11::arg("N"), pybind11::arg("C"), pybind11::arg("P"), pybind11::arg("E"),
         pybind11::arg("dst_ptr"), pybind11::arg("src"), pybind11::arg("perm"), pybind11::arg("G"), pybind11::arg("Ys"),
         pybind11::arg("xs"), pybind11::arg("want_T"), pybind11::arg("want_gR"), pybind11::arg("xY"),
-        pybind11::arg("RY"), pybind11::arg("Rd") = pybind11::none());
+        pybind11::arg("RY"), pybind11::arg("Rd") = pybind11::none(), pybind11::arg("Rx") = pybind11::none());
+  m.def("conv_sender_sum", &conv_sender_sum_op);
   m.def("conv_scatter", &conv_scatter_op);
   m.def("symcon_fwd", &symcon_fwd_op);
   m.def("symcon_bwd", &symcon_bwd_op);

@@ -168,7 +168,8 @@ template <typename T, int P, int CPL, int WPA>
 __global__ void __launch_bounds__(32 * WPA) conv_edge_kernel(
     int N, int C, const int64_t* __restrict__ dst_ptr, const int* __restrict__ src,
     const int64_t* __restrict__ perm, const T* __restrict__ G, EdgeTerms<T> tE, PairTerms<T> tY,
-    T* __restrict__ gR, T* __restrict__ gY, int atomic_gY, const T* __restrict__ Rd, T* __restrict__ g_r) {
+    T* __restrict__ gR, T* __restrict__ gY, int atomic_gY, const T* __restrict__ Rd, T* __restrict__ g_r,
+    const T* __restrict__ Rx, T* __restrict__ gxe) {
   constexpr int D = P * P;
   const int i = blockIdx.x;
   const int w = threadIdx.x >> 5;
@@ -187,10 +188,13 @@ __global__ void __launch_bounds__(32 * WPA) conv_edge_kernel(
     const int64_t s = src[e];
     if (tE.n > 0) {
       T out[CPL][P];
+      T sx[CPL];  // this edge's share of the sender cotangent: sum_l T_0[e,l,c] Rx[e,l,c]
 #pragma unroll
-      for (int q = 0; q < CPL; ++q)
+      for (int q = 0; q < CPL; ++q) {
+        sx[q] = T(0);
 #pragma unroll
         for (int l = 0; l < P; ++l) out[q][l] = T(0);
+      }
 #pragma unroll
       for (int tt = 0; tt < 2; ++tt) {
         if (tt < tE.n) {
@@ -208,10 +212,18 @@ __global__ void __launch_bounds__(32 * WPA) conv_edge_kernel(
 #pragma unroll
                 for (int m = 0; m < 2 * l + 1; ++m) sm += g[q][l * l + m] * y[l * l + m];
                 if (tE.Tout[tt]) tE.Tout[tt][(e * P + l) * C + c] = sm;
+                if (tt == 0 && gxe != nullptr) sx[q] += sm * __ldg(Rx + (e * P + l) * C + c);
                 out[q][l] += xv * sm;
               }
             }
           }
+        }
+      }
+      if (gxe != nullptr) {
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+          const int c = cbase + lane + 32 * q;
+          if (c < C) gxe[e * C + c] = sx[q];
         }
       }
       if (gR != nullptr) {
@@ -322,6 +334,43 @@ __global__ void __launch_bounds__(32 * WPA) conv_scatter_kernel(
   }
 }
 
+// gx[s, c] = sum over the edges out of s of v[e, c] (rows of conv_edge_kernel's gxe), edges via
+// the sender permutation; the warps' partial sums meet in shared memory in a fixed order.
+template <typename T, int CPL, int WPA>
+__global__ void __launch_bounds__(32 * WPA) conv_sender_sum_kernel(
+    int N, int C, const int64_t* __restrict__ src_ptr, const int64_t* __restrict__ src_perm,
+    const T* __restrict__ v, T* __restrict__ gx) {
+  const int s = blockIdx.x;
+  const int w = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cbase = blockIdx.y * 32 * CPL;
+  T acc[CPL];
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) acc[q] = T(0);
+  const int64_t j0 = src_ptr[s], j1 = src_ptr[s + 1];
+  for (int64_t j = j0 + w; j < j1; j += WPA) {
+    const int64_t e = src_perm[j];
+#pragma unroll
+    for (int q = 0; q < CPL; ++q) {
+      const int c = cbase + lane + 32 * q;
+      if (c < C) acc[q] += __ldg(v + e * C + c);
+    }
+  }
+  __shared__ T red[WPA][32 * CPL];
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) red[w][q * 32 + lane] = acc[q];
+  __syncthreads();
+  if (w != 0) return;
+#pragma unroll
+  for (int q = 0; q < CPL; ++q) {
+    T t = red[0][q * 32 + lane];
+#pragma unroll
+    for (int ww = 1; ww < WPA; ++ww) t += red[ww][q * 32 + lane];
+    const int c = cbase + lane + 32 * q;
+    if (c < C) gx[(int64_t)s * C + c] = t;
+  }
+}
+
 namespace {
 constexpr int kWPA = 4;  // warps per atom
 inline int cpl_for(int C) {
@@ -410,9 +459,10 @@ template <typename T>
 cudaError_t conv_edge(int N, int C, int P, const int64_t* dst_ptr, const int* src, const int64_t* perm,
                       const T* G, int nE, const T* const* Ys, const T* const* xs, T* const* Touts,
                       int nY, const T* const* xY, const T* const* RY, T* gR, T* gY, const T* Rd, T* g_r,
-                      cudaStream_t stream) {
+                      const T* Rx, T* gxe, cudaStream_t stream) {
   if (N == 0) return cudaSuccess;
   if (nE < 0 || nE > 2 || nY < 0 || nY > 2) return cudaErrorInvalidValue;
+  if (gxe != nullptr && (nE < 1 || Rx == nullptr)) return cudaErrorInvalidValue;
   EdgeTerms<T> tE;
   PairTerms<T> tY;
   tE.n = nE; tY.n = nY;
@@ -425,7 +475,7 @@ cudaError_t conv_edge(int N, int C, int P, const int64_t* dst_ptr, const int* sr
   const int gy = (C + 32 * cpl - 1) / (32 * cpl);
   dim3 grid(N, gy);
   const int atomic_gY = gy > 1 ? 1 : 0;
-  XNN_P_CPL_SWITCH(P, cpl, conv_edge_kernel<T, PP, QQ, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, dst_ptr, src, perm, G, tE, tY, gR, gY, atomic_gY, Rd, g_r));
+  XNN_P_CPL_SWITCH(P, cpl, conv_edge_kernel<T, PP, QQ, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, dst_ptr, src, perm, G, tE, tY, gR, gY, atomic_gY, Rd, g_r, Rx, gxe));
   return cudaGetLastError();
 }
 
@@ -446,6 +496,21 @@ cudaError_t conv_scatter(int N, int C, int P, const int64_t* src_ptr, const int6
   return cudaGetLastError();
 }
 
+template <typename T>
+cudaError_t conv_sender_sum(int N, int C, const int64_t* src_ptr, const int64_t* src_perm, const T* v, T* gx,
+                            cudaStream_t stream) {
+  if (N == 0) return cudaSuccess;
+  const int cpl = scatter_cpl(C);
+  dim3 grid(N, (C + 32 * cpl - 1) / (32 * cpl));
+  switch (cpl) {
+    case 1: conv_sender_sum_kernel<T, 1, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
+    case 2: conv_sender_sum_kernel<T, 2, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
+    case 3: conv_sender_sum_kernel<T, 3, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
+    default: conv_sender_sum_kernel<T, 4, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
+  }
+  return cudaGetLastError();
+}
+
 // column blocks of the edge kernel (its outputs g_r / gY need zero initialisation when > 1)
 int conv_edge_blocks(int C) {
   const int cpl = edge_cpl(C);
@@ -458,7 +523,9 @@ int conv_edge_blocks(int C) {
                                       cudaStream_t);                                                  \
   template cudaError_t conv_edge<T>(int, int, int, const int64_t*, const int*, const int64_t*,       \
                                     const T*, int, const T* const*, const T* const*, T* const*, int,  \
-                                    const T* const*, const T* const*, T*, T*, const T*, T*, cudaStream_t);          \
+                                    const T* const*, const T* const*, T*, T*, const T*, T*, const T*, T*, \
+                                    cudaStream_t);                                                    \
+  template cudaError_t conv_sender_sum<T>(int, int, const int64_t*, const int64_t*, const T*, T*, cudaStream_t); \
   template cudaError_t conv_scatter<T>(int, int, int, const int64_t*, const int64_t*, int,           \
                                        const T* const*, const T* const*, T*, cudaStream_t);
 XNN_INST(float)

@@ -25,6 +25,7 @@ from torch.nn import Parameter, ParameterDict
 
 from ..data import AtomicGraph
 from ..data.elements import ATOMIC_NUMBERS, SYMBOLS
+from ..models.fast import resolve_use_fast
 from ..models.registry import register_model
 from ..ops.scatter import scatter_sum
 from .frc import read_forcefield
@@ -365,7 +366,7 @@ class Amber(FixedTopologyPotential):
         self.fudge_qq = self.ff.fudge_qq if fudge_qq is None else float(fudge_qq)
         self.keep_intermediates, self.intermediates = bool(keep_intermediates), {}
         self.node_feature_dim = 1
-        self.use_fast = use_fast
+        self.use_fast = resolve_use_fast(use_fast)
         top = topology if isinstance(topology, MolecularTopology) else read_topology(topology)
         self._bind(top)
         self._bind_charges(top, charges)

@@ -25,6 +25,7 @@ from torch.nn import Parameter, ParameterDict
 
 from ..data import AtomicGraph
 from ..data.elements import ATOMIC_NUMBERS
+from ..models.fast import resolve_use_fast
 from ..models.registry import register_model
 from ..ops.scatter import scatter_sum
 from .frc import read_forcefield
@@ -265,7 +266,7 @@ class Dreiding(FixedTopologyPotential):
         self.hbond_cos = math.cos(float(hbond_angle) * DEG)
         self.keep_intermediates, self.intermediates = bool(keep_intermediates), {}
         self.node_feature_dim = 1
-        self.use_fast = use_fast
+        self.use_fast = resolve_use_fast(use_fast)
         self._bind(topology if isinstance(topology, MolecularTopology) else read_topology(topology), charges)
         self.species = sorted({int(z) for z in self.top_z.tolist()})
 

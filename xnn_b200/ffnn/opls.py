@@ -26,6 +26,7 @@ from torch.nn import Parameter, ParameterDict
 from ..data import AtomicGraph
 from ..data.elements import ATOMIC_NUMBERS
 from ..models.base import InteratomicPotential
+from ..models.fast import resolve_use_fast
 from ..models.registry import register_model
 from ..ops.scatter import scatter_sum
 from .frc import WILDCARD as FRC_WILDCARD
@@ -373,6 +374,13 @@ class FixedTopologyPotential(InteratomicPotential):
     def masses(self) -> Tensor:
         return self.ff.type_mass[self.top_type]
 
+    def set_use_fast(self, use_fast) -> "FixedTopologyPotential":
+        """Accepted for the common model interface; the bonded and nonbonded terms here have one
+        formulation (index-gather PyTorch ops, capturable in a CUDA graph), so the mode changes
+        nothing numerically."""
+        self.use_fast = resolve_use_fast(use_fast)
+        return self
+
 
 @register_model("opls")
 class OPLS(FixedTopologyPotential):
@@ -400,7 +408,7 @@ class OPLS(FixedTopologyPotential):
         self.keep_intermediates = bool(keep_intermediates)
         self.intermediates: dict = {}
         self.node_feature_dim = 1
-        self.use_fast = use_fast
+        self.use_fast = resolve_use_fast(use_fast)
         self._bind(topology if isinstance(topology, MolecularTopology) else read_topology(topology))
         self.species = sorted({int(z) for z in self.top_z.tolist()})
         if atomic_energies is not None:

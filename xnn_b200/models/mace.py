@@ -39,6 +39,7 @@ from ..o3 import (FullyConnectedNet, FullyConnectedTensorProduct, Irreps, Linear
                   SphericalHarmonics, TensorProduct, normalize2mom)
 from ..ops.scatter import refresh_ghosts, scatter_sum
 from .base import GNNPotential
+from .fast import AutoPolicy, choose, resolve_use_fast
 from .mace_blocks import (ReshapeIrreps, SymmetricContraction, hidden_irreps,
                           tp_out_irreps_with_instructions)
 from .registry import register_model
@@ -344,10 +345,12 @@ class MACE(GNNPotential):
         self.__dict__["_fast_cache"] = None
 
     # --- fast-path selection -----------------------------------------------------
+    #: ``"auto"``: the fused path on any CUDA input the architecture allows (measured faster from
+    #: the smallest benchmark batches on)
+    AUTO_POLICY = AutoPolicy()
+
     def set_use_fast(self, use_fast) -> "MACE":
-        if use_fast not in (True, False, "auto"):
-            raise ValueError("use_fast must be True, False or 'auto'")
-        self.use_fast = use_fast
+        self.use_fast = resolve_use_fast(use_fast)
         return self
 
     def fast_eligible(self) -> bool:
@@ -367,13 +370,10 @@ class MACE(GNNPotential):
         return True
 
     def _fast_active(self, like: Tensor) -> bool:
-        if self.use_fast is False or not self.fast_eligible():
-            return False
-        if like.dtype not in (torch.float32, torch.float64):
-            return False
+        covered = self.fast_eligible() and like.dtype in (torch.float32, torch.float64)
         if self.use_fast is True:
-            return True
-        return like.is_cuda
+            return covered          # the PyTorch twin of the fused path also runs on the CPU
+        return choose(self.use_fast, covered, self.AUTO_POLICY, like.device, like.dtype, int(like.shape[0]))
 
     # --- energies ----------------------------------------------------------------
     def node_features_energy(self, atomic_numbers: Tensor, edge_index: Tensor, edge_vec: Tensor,

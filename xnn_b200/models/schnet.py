@@ -21,6 +21,7 @@ from ..nn.cutoff import CosineCutoff
 from ..nn.radial import make_radial_basis
 from ..ops.scatter import scatter_sum
 from .base import InteratomicPotential
+from .fast import AutoPolicy, choose, resolve_use_fast
 from .registry import register_model
 
 MAX_Z = 100
@@ -116,8 +117,11 @@ class SchNet(InteratomicPotential):
             self.set_atomic_energies(species, atomic_energies)
         self.use_fast = "auto"
 
+    #: ``"auto"``: the CSR segment sums on any CUDA input with receiver-sorted edges
+    AUTO_POLICY = AutoPolicy()
+
     def set_use_fast(self, use_fast) -> "SchNet":
-        self.use_fast = use_fast
+        self.use_fast = resolve_use_fast(use_fast)
         return self
 
     def set_atomic_energies(self, species, values) -> None:
@@ -146,7 +150,8 @@ class SchNet(InteratomicPotential):
     def forward(self, data: AtomicGraph) -> Dict[str, Tensor]:
         edge_vec = data.edge_vectors()
         plan = None
-        if self.use_fast is not False and edge_vec.is_cuda and data.edge_order == "dst":
+        if choose(self.use_fast, edge_vec.is_cuda and data.edge_order == "dst", self.AUTO_POLICY, edge_vec.device,
+                  edge_vec.dtype, data.num_edges):
             from ..ops.mace_ops import EdgePlan
             plan = EdgePlan.build(data.edge_index, data.num_nodes, assume_dst_sorted=True)
         x, node_energy = self.node_features_energy(data.atomic_numbers, data.edge_index, edge_vec, plan)

@@ -30,8 +30,9 @@ from ..nn.blocks import GatedMLP, make_activation
 from ..ops import gemm
 from ..ops.scatter import refresh_ghosts
 from ..ops.tensornet_ops import (EMBEDDING_FULL, FULL_FROM_COMPACT, RECOMPOSE, Y_AND_COMPACT, TensorPlan,
-                                 embedding, geometry_rows, matmul3, messages)
+                                 embedding, geometry_rows, kernels_enabled, matmul3, messages)
 from .base import InteratomicPotential
+from .fast import AutoPolicy, choose, resolve_use_fast
 from .registry import register_model
 
 _READOUTS = ("mlp", "gated")
@@ -174,6 +175,7 @@ class TensorNet(InteratomicPotential):
         self.linear = nn.Linear(3 * n_features, n_features)
         self.act = make_activation(activation)
         self.self_pairs = bool(self_pairs)
+        self.use_fast = "auto"
         self.activate_features = readout == "mlp"
         n_in = n_features + self.readout_extra_inputs
         if readout_hidden is None:
@@ -198,6 +200,15 @@ class TensorNet(InteratomicPotential):
             if species is None:
                 raise ValueError("species is required to map atomic_energies")
             self.set_atomic_energies(species, atomic_energies)
+
+    #: ``"auto"``: the kernels on any CUDA input (faster from the smallest batches measured on)
+    AUTO_POLICY = AutoPolicy()
+
+    def set_use_fast(self, use_fast) -> "TensorNet":
+        """``False``: the message sums, embeddings and 3 x 3 products run their PyTorch formulas
+        also on the GPU; ``True`` / ``"auto"``: the sm_100a kernels on CUDA inputs."""
+        self.use_fast = resolve_use_fast(use_fast)
+        return self
 
     def set_atomic_energies(self, species, values) -> None:
         with torch.no_grad():
@@ -228,9 +239,13 @@ class TensorNet(InteratomicPotential):
         src, dst, length, direction = self._pairs(atomic_numbers.shape[0], edge_index, edge_vec)
         fc, basis = self.cutoff_fn(length), self.rbf(length)
         plan = TensorPlan.build(src, dst, atomic_numbers.shape[0])
-        feats = self.tensor_embedding(atomic_numbers, src, dst, fc, direction, basis, plan)
-        for layer in self.layers:
-            feats = layer(refresh_ghosts(feats), plan, fc, basis, total_charge)
+        covered = edge_vec.dtype in (torch.float32, torch.float64) and self.n_features <= 128
+        fast = choose(getattr(self, "use_fast", "auto"), covered, self.AUTO_POLICY, edge_vec.device,
+                      edge_vec.dtype, int(src.shape[0]))
+        with kernels_enabled(fast):
+            feats = self.tensor_embedding(atomic_numbers, src, dst, fc, direction, basis, plan)
+            for layer in self.layers:
+                feats = layer(refresh_ghosts(feats), plan, fc, basis, total_charge)
         return feats
 
     def _features(self, X: Tensor) -> Tensor:

@@ -5,7 +5,8 @@ edge chunks; the per-edge tensors of the radial network (``R``, its tangent ``dR
 hidden activations, several kB per edge) exist for one chunk at a time and are never saved.
 The backward recomputes ``R`` and ``dR/dr`` chunk by chunk (the forward-mode network of
 :mod:`xnn_b200.ops.radial`) and forms, per chunk, the edge cotangents ``g_r = sum gR dR/dr`` and
-``gY`` and the sender cotangent ``gx``. Saved state is ``x``, ``r`` and ``Y``: O(E) floats
+``gY`` and each edge's term of the sender cotangent (an ``(E, C)`` row, summed per sender by a
+second kernel), so no ``(E, P, C)`` tensor besides ``R`` and ``dR/dr`` is written. Saved state is ``x``, ``r`` and ``Y``: O(E) floats
 instead of O(E * P * C).
 
 First derivatives only (forces, stress, MD); parameter gradients are not formed, so training
@@ -98,16 +99,18 @@ class _LeanRadialConv(Function):
             Gc = G[:, n0:n1].contiguous()
             Yc = Y[e0:e1].contiguous()
             want_y = gY is not None
-            # the edge kernel contracts gR with dR/dr itself: g_r without the (E, P, C) gR tensor
-            g_rc, gYc, T1, _ = K.conv_edge(n1 - n0, C, P, e1 - e0, sub.dst_ptr, sub.src32, None, Gc, [Yc], [xc],
-                                           [gx is not None], g_r is not None, [xc] if want_y else [],
-                                           [R] if want_y else [], Rd.contiguous())
+            # the edge kernel contracts gR with dR/dr itself (g_r without the (E, P, C) gR tensor)
+            # and writes each edge's (E, C) term of the sender cotangent, summed per sender after
+            g_rc, gYc, _, _, gxe = K.conv_edge(n1 - n0, C, P, e1 - e0, sub.dst_ptr, sub.src32, None, Gc, [Yc],
+                                               [xc], [False], g_r is not None, [xc] if want_y else [],
+                                               [R] if want_y else [], Rd.contiguous(),
+                                               R.contiguous() if gx is not None else None)
             if g_r is not None:
                 g_r[e0:e1] = g_rc
             if want_y:
                 gY[e0:e1] = gYc
             if gx is not None:
-                gx += K.conv_scatter(N_src, C, P, sub.src_ptr, sub.src_perm, [R], [T1])
+                gx += K.conv_sender_sum(N_src, sub.src_ptr, sub.src_perm, gxe)
         return (gx, g_r, gY, None, None, None) + (None,) * len(Ws)
 
 

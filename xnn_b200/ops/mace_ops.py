@@ -229,7 +229,7 @@ class _ConvVJP(Function):
         N, C, P = plan.n_nodes, x.shape[1], R.shape[1]
         G = G.contiguous()
         K = _C()
-        gR, gY, T1, _ = K.conv_edge(N, C, P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm, G,
+        gR, gY, T1, _, _ = K.conv_edge(N, C, P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm, G,
                                     [Y], [x if nR else None], [True], bool(nR),
                                     [x] if nY else [], [R] if nY else [])
         gx = K.conv_scatter(plan.n_senders, C, P, plan.src_ptr, plan.src_perm, [R], [T1]) if nx else None
@@ -272,7 +272,7 @@ class _ConvVJP(Function):
                     xY.append(tx); RY.append(tR)
         T2 = None
         if Ys or xY:
-            a, b, t0, t1 = K.conv_edge(N, C, P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm, G,
+            a, b, t0, t1, _ = K.conv_edge(N, C, P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm, G,
                                        Ys, xs, wT, bool(nR) and any(v is not None for v in xs), xY, RY)
             cR = a if (nR and any(v is not None for v in xs)) else None
             cY = b if xY else None

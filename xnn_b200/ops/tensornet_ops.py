@@ -20,10 +20,15 @@ other differentiate to any order, each on one sm_100a kernel (``csrc/tensornet.c
 nothing pair-sized beyond the filters and their gradients. The embedding is the same kind of
 sum with per-pair geometry rows ``geo = [1, u, u u^T]`` in place of the neighbour's features
 (``Em``, with adjoints ``Ea`` in the pair parts and ``Eg`` in the geometry). On the CPU the same
-functions run their PyTorch formulas.
+functions run their PyTorch formulas, and so do they on the GPU inside :func:`kernels_enabled`
+``(False)`` (the model's ``use_fast=False``); each function's backward pass takes the forward
+pass's choice.
 """
 from __future__ import annotations
 
+import contextlib
+import functools
+import threading
 from dataclasses import dataclass
 from typing import Optional
 
@@ -33,6 +38,39 @@ from torch import Tensor
 from .. import _ext
 
 GROUP = (0, 1, 1, 1, 2, 2, 2, 2, 2, 2)
+
+_MODE = threading.local()
+
+
+def _allowed() -> bool:
+    return getattr(_MODE, "on", True)
+
+
+@contextlib.contextmanager
+def kernels_enabled(on: bool):
+    """Within the block the functions here use their kernels (``True``) or formulas (``False``)."""
+    prev = _allowed()
+    _MODE.on = bool(on)
+    try:
+        yield
+    finally:
+        _MODE.on = prev
+
+
+def _records_mode(fwd):
+    @functools.wraps(fwd)
+    def run(ctx, *args):
+        ctx.kernels_on = _allowed()
+        return fwd(ctx, *args)
+    return run
+
+
+def _keeps_mode(bwd):
+    @functools.wraps(bwd)
+    def run(ctx, *grads):
+        with kernels_enabled(ctx.kernels_on):
+            return bwd(ctx, *grads)
+    return run
 
 
 @dataclass
@@ -63,7 +101,7 @@ class TensorPlan:
 
 
 def _kernels(t: Tensor) -> bool:
-    if not t.is_cuda or t.dtype not in (torch.float32, torch.float64) or t.shape[-1] > 128:
+    if not _allowed() or not t.is_cuda or t.dtype not in (torch.float32, torch.float64) or t.shape[-1] > 128:
         return False
     if not hasattr(_ext.ops(), "tn_gather"):
         raise RuntimeError("xnn_b200 extension without the TensorNet kernels: rebuild it (xnn_b200.build)")
@@ -89,6 +127,7 @@ class _M(torch.autograd.Function):
     """Message sum onto the receivers."""
 
     @staticmethod
+    @_records_mode
     def forward(ctx, a: Tensor, x: Tensor, plan: TensorPlan):
         ctx.save_for_backward(a, x)
         ctx.plan = plan
@@ -97,6 +136,7 @@ class _M(torch.autograd.Function):
         return _gather_sum(a, x, plan.dst, plan.src, plan.n)
 
     @staticmethod
+    @_keeps_mode
     def backward(ctx, g: Tensor):
         a, x = ctx.saved_tensors
         plan = ctx.plan
@@ -109,6 +149,7 @@ class _MT(torch.autograd.Function):
     """Adjoint sum onto the senders: ``out[j] = sum_{j -> i} a (.) y[i]``."""
 
     @staticmethod
+    @_records_mode
     def forward(ctx, a: Tensor, y: Tensor, plan: TensorPlan):
         ctx.save_for_backward(a, y)
         ctx.plan = plan
@@ -117,6 +158,7 @@ class _MT(torch.autograd.Function):
         return _gather_sum(a, y, plan.src, plan.dst, plan.n)
 
     @staticmethod
+    @_keeps_mode
     def backward(ctx, k: Tensor):
         a, y = ctx.saved_tensors
         plan = ctx.plan
@@ -129,6 +171,7 @@ class _D(torch.autograd.Function):
     """Per-pair group sums ``out[p, g] = sum_{c in g} y[dst, c] x[src, c]``."""
 
     @staticmethod
+    @_records_mode
     def forward(ctx, y: Tensor, x: Tensor, plan: TensorPlan):
         ctx.save_for_backward(y, x)
         ctx.plan = plan
@@ -137,6 +180,7 @@ class _D(torch.autograd.Function):
         return _reduce(y.index_select(0, plan.dst) * x.index_select(0, plan.src))
 
     @staticmethod
+    @_keeps_mode
     def backward(ctx, h: Tensor):
         y, x = ctx.saved_tensors
         plan = ctx.plan
@@ -149,6 +193,7 @@ class _Em(torch.autograd.Function):
     """Embedding sum onto the receivers: ``out[i, c] = sum_{p -> i} a[p, g(c)] geo[p, c]``."""
 
     @staticmethod
+    @_records_mode
     def forward(ctx, a: Tensor, geo: Tensor, plan: TensorPlan):
         ctx.save_for_backward(a, geo)
         ctx.plan = plan
@@ -158,6 +203,7 @@ class _Em(torch.autograd.Function):
         return out.index_add_(0, plan.dst, _expand(a) * geo.unsqueeze(-1))
 
     @staticmethod
+    @_keeps_mode
     def backward(ctx, g: Tensor):
         a, geo = ctx.saved_tensors
         plan = ctx.plan
@@ -170,6 +216,7 @@ class _Ea(torch.autograd.Function):
     """``out[p, g] = sum_{c in g} y[dst, c] geo[p, c]`` (the adjoint of the embedding in ``a``)."""
 
     @staticmethod
+    @_records_mode
     def forward(ctx, y: Tensor, geo: Tensor, plan: TensorPlan):
         ctx.save_for_backward(y, geo)
         ctx.plan = plan
@@ -178,6 +225,7 @@ class _Ea(torch.autograd.Function):
         return _reduce(y.index_select(0, plan.dst) * geo.unsqueeze(-1))
 
     @staticmethod
+    @_keeps_mode
     def backward(ctx, h: Tensor):
         y, geo = ctx.saved_tensors
         plan = ctx.plan
@@ -190,6 +238,7 @@ class _Eg(torch.autograd.Function):
     """``out[p, c] = sum_f a[p, g(c), f] y[dst, c, f]`` (the adjoint of the embedding in ``geo``)."""
 
     @staticmethod
+    @_records_mode
     def forward(ctx, a: Tensor, y: Tensor, plan: TensorPlan):
         ctx.save_for_backward(a, y)
         ctx.plan = plan
@@ -198,6 +247,7 @@ class _Eg(torch.autograd.Function):
         return (_expand(a) * y.index_select(0, plan.dst)).sum(-1)
 
     @staticmethod
+    @_keeps_mode
     def backward(ctx, k: Tensor):
         a, y = ctx.saved_tensors
         plan = ctx.plan
@@ -240,6 +290,7 @@ class _MM3(torch.autograd.Function):
     its flag is set); the backward products are of the same kind, so any order differentiates."""
 
     @staticmethod
+    @_records_mode
     def forward(ctx, A: Tensor, B: Tensor, ta: bool, tb: bool):
         ctx.save_for_backward(A, B)
         ctx.t = (ta, tb)
@@ -250,6 +301,7 @@ class _MM3(torch.autograd.Function):
         return torch.einsum("nikf,nkjf->nijf", a, b)
 
     @staticmethod
+    @_keeps_mode
     def backward(ctx, g: Tensor):
         A, B = ctx.saved_tensors
         ta, tb = ctx.t
@@ -272,6 +324,7 @@ class _PLin(torch.autograd.Function):
     so its backward is the same map with ``M^T`` and every order differentiates."""
 
     @staticmethod
+    @_records_mode
     def forward(ctx, in1: Tensor, in2, M: Tensor, MT: Tensor, O1: int):
         ctx.K1 = in1.shape[1]
         ctx.O1 = O1
@@ -289,6 +342,7 @@ class _PLin(torch.autograd.Function):
         return o1, o2
 
     @staticmethod
+    @_keeps_mode
     def backward(ctx, *gs):
         M, MT = ctx.mats
         g1 = gs[0]

@@ -165,26 +165,32 @@ class _Ops:
         acc = sum((a * b).sum(1) for a, b in pairs)
         return torch.zeros(plan.n_senders, acc.shape[1], dtype=acc.dtype, device=acc.device).index_add_(0, plan.src, acc)
 
-    def edge_force(self, plan: K.EdgePlan, G: Tensor, Y: Tensor, u: Tensor, R: Tensor, Rd: Tensor):
-        """Force pass of one convolution with cotangent ``G``: ``(r_bar, Y_bar, T)`` where
-        ``r_bar[e] = sum u[s] T R'``, ``Y_bar[e, lm] = sum_c G R u[s]`` and ``T = tee(G, Y)``."""
+    def edge_force(self, plan: K.EdgePlan, G: Tensor, Y: Tensor, u: Tensor, R: Tensor, Rd: Tensor,
+                   sender: bool = True):
+        """Force pass of one convolution with cotangent ``G``: ``(r_bar, Y_bar, u_bar)`` where
+        ``r_bar[e] = sum u[s] T R'``, ``Y_bar[e, lm] = sum_c G R u[s]`` and (with ``sender``)
+        ``u_bar[s] = sum_{e out of s} sum_l T R`` with ``T = tee(G, Y)``; each edge's term of
+        ``u_bar`` is an ``(E, C)`` row of the edge kernel, summed per sender."""
         if self.cuda:
             N, C = plan.n_nodes, u.shape[1]
-            g_r, gY, T, _ = K._C().conv_edge(N, C, self.P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm,
-                                             G.contiguous(), [Y], [u], [True], True, [u], [R], Rd.contiguous())
-            return g_r, gY, T
+            g_r, gY, _, _, v = K._C().conv_edge(N, C, self.P, plan.n_edges, plan.dst_ptr, plan.src32,
+                                                plan.dst_perm, G.contiguous(), [Y], [u], [False], True, [u], [R],
+                                                Rd.contiguous(), R.contiguous() if sender else None)
+            ub = K._C().conv_sender_sum(plan.n_senders, plan.src_ptr, plan.src_perm, v) if sender else None
+            return g_r, gY, ub
         T = self.tee(plan, G, Y)
         us = u.index_select(0, plan.src)[:, None, :]
         g_r = (us * T * Rd).sum((1, 2))
         Gd = G.index_select(1, plan.dst)                       # (D, E, C)
         gY = (Gd * (R[:, self.lidx.to(R.device), :] * us).transpose(0, 1)).sum(-1).t()
-        return g_r, gY, T
+        ub = self.scatter(plan, [(R, T)]) if sender else None
+        return g_r, gY, ub
 
     def edge_terms(self, plan: K.EdgePlan, G: Tensor, Ys, xs) -> Tuple[Optional[Tensor], List[Tensor]]:
         """``gR = sum_k x_k[s] * tee(G, Y_k)`` and every ``tee(G, Y_k)``."""
         if self.cuda:
             N, C = plan.n_nodes, G.shape[2]
-            gR, _, T0, T1 = K._C().conv_edge(N, C, self.P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm,
+            gR, _, T0, T1, _ = K._C().conv_edge(N, C, self.P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm,
                                              G.contiguous(), [y.contiguous() for y in Ys],
                                              [x.contiguous() if x is not None else None for x in xs],
                                              [True] * len(Ys), any(x is not None for x in xs), [], [], None)
@@ -582,11 +588,10 @@ class MACEStep:
             A2b = ops.symcon_vjp(A2[t], z, symw[t], Bb)
             Ab = torch.empty_like(A2b)
             NG.mm(_per_degree_problems(A2b, Ab, [w.t() for w in lin[t]], Pk["linT"][P * t:P * t + P]))
-            gr_t, gY_t, T1 = ops.edge_force(plan, Ab, Y, u[t], Rs[t], Rds[t])
+            gr_t, gY_t, ub = ops.edge_force(plan, Ab, Y, u[t], Rs[t], Rds[t], sender=t > 0)
             g_r = gr_t if g_r is None else g_r + gr_t
             gY = gY_t if gY is None else gY + gY_t
             if t > 0:
-                ub = ops.scatter(plan, [(Rs[t], T1)])
                 NG.mm(rev_problems(t, ub, hb[t + 1], hb[t]))
         rhat = vec / r.clamp_min(1e-30)[:, None]
         vbar = ops.geometry_vjp(vec, gY) + g_r[:, None] * rhat

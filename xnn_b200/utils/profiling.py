@@ -19,27 +19,49 @@ from __future__ import annotations
 
 import argparse
 import contextlib
+import functools
 import os
+import re
 from collections import defaultdict
+from pathlib import Path
 from typing import Callable, Dict, List
 
 import torch
 
 _NVTX = os.environ.get("XNN_B200_NVTX", "0") == "1"
 
-#: name fragments of the kernels compiled into ``xnn_b200/_C.so``
-OWN_KERNELS = ("conv_gather", "conv_edge", "conv_scatter", "symcon_", "edge_geom_", "p2p_allreduce",
-               "halo_exchange", "gemm_pack_kernel", "gemm_rows_kernel", "gemm_reduce_kernel", "gemm_ws_kernel",
-               "gemm_ws_pack_kernel", "gemm_reduce_ws_kernel", "sum_partials_kernel", "radial_basis_kernel",
-               "radial_act_kernel", "radial_dact_kernel", "nb_count", "nb_write", "mp_real_kernel",
-               "pme_spread_kernel", "pme_gather_kernel", "xnn_", "nl_", "mace_", "tn_", "pme_", "halo_",
-               "adam_", "grad_", "seg_", "dd_", "fft_", "eeq_", "atm_", "amoeba_", "reax_", "sqm_", "node_",
-               "species_sort", "dual_edge_kernel", "dual_scatter_kernel", "dipole_pairs", "dipole_matvec",
-               "segment_rows_sum", "edge_forces_kernel")
+_GLOBAL = re.compile(r"__global__\s+(?:__launch_bounds__\s*\([^)]*\)\s*)?(?:static\s+)?void\s+"
+                     r"(?:__launch_bounds__\s*\([^)]*\)\s*)?(\w+)\s*\(")
+
+
+@functools.lru_cache(maxsize=1)
+def own_kernel_names() -> frozenset:
+    """Names of the ``__global__`` functions in this package's CUDA sources (``csrc``)."""
+    root = Path(__file__).resolve().parents[1] / "csrc"
+    names = set()
+    for f in sorted(root.rglob("*")):
+        if f.suffix in (".cu", ".cuh", ".h"):
+            names.update(_GLOBAL.findall(f.read_text(errors="replace")))
+    return frozenset(names)
+
+
+def kernel_base_name(name: str) -> str:
+    """``void (anonymous namespace)::gemm_ws_kernel<32>(CUtensorMap_st, ...)`` -> ``gemm_ws_kernel``."""
+    out, level = [], 0
+    for ch in name:                       # drop template arguments (they may hold parentheses)
+        if ch == "<":
+            level += 1
+        elif ch == ">":
+            level -= 1
+        elif level == 0:
+            out.append(ch)
+    flat = "".join(out).replace("(anonymous namespace)::", "").split("(", 1)[0].strip()
+    return flat.split()[-1].split("::")[-1] if flat else ""
 
 
 def is_own_kernel(name: str) -> bool:
-    return any(k in name for k in OWN_KERNELS)
+    """Whether a profiler kernel name is one of this package's kernels."""
+    return kernel_base_name(name) in own_kernel_names()
 
 
 @contextlib.contextmanager
@@ -70,8 +92,8 @@ def kernel_table(fn: Callable[[], object], warmup: int = 1, ops: bool = False) -
     count: Dict[str, int] = defaultdict(int)
     us: Dict[str, float] = defaultdict(float)
     for e in prof.events():
-        if e.device_type.name != "CUDA":
-            continue
+        if e.device_type.name != "CUDA" or getattr(e, "is_user_annotation", False):
+            continue                    # a record_function range spans kernels counted on their own
         count[e.name] += 1
         us[e.name] += float(getattr(e, "device_time", 0.0) or getattr(e, "cuda_time", 0.0) or 0.0)
     rows: List[Dict[str, object]] = [
