@@ -168,6 +168,36 @@ def test_sender_rows_match_scatter(dtype, tol, C):
     torch.testing.assert_close(gY2, gY, rtol=tol, atol=tol)
 
 
+@pytest.mark.parametrize("dtype,tol", [(torch.float64, 1e-10), (torch.float32, 1e-4)])
+@pytest.mark.parametrize("P,C", [(4, 96), (3, 40), (4, 160), (2, 128)])
+def test_force_kernel_matches_formulas(dtype, tol, P, C):
+    """The force-pass kernel (g_r, gY, sender terms) against the PyTorch formulas, fp64 reference."""
+    g = _graph()
+    ei = g.edge_index
+    ei = ei[:, torch.argsort(ei[1], stable=True)].to("cuda")
+    N, E = g.num_nodes, ei.shape[1]
+    plan = K.EdgePlan.build(ei, N, assume_dst_sorted=True)
+    assert plan.dst_perm is None
+    G = torch.randn(P * P, N, C, dtype=torch.float64, device="cuda")
+    x = torch.randn(N, C, dtype=torch.float64, device="cuda")
+    R = torch.randn(E, P, C, dtype=torch.float64, device="cuda")
+    Rd = torch.randn(E, P, C, dtype=torch.float64, device="cuda")
+    Y = torch.randn(E, P * P, dtype=torch.float64, device="cuda")
+    src, dst = ei[0], ei[1]
+    lidx = torch.tensor([l for l in range(P) for _ in range(2 * l + 1)], device="cuda")
+    Gd = G[:, dst].permute(1, 0, 2)                                   # (E, D, C)
+    T = torch.zeros(E, P, C, dtype=torch.float64, device="cuda").index_add_(1, lidx, Gd * Y[:, :, None])
+    xs = x[src]
+    ref_gr = (xs[:, None, :] * T * Rd).sum((1, 2))
+    ref_gY = (Gd * R[:, lidx, :] * xs[:, None, :]).sum(-1)
+    ref_gxe = (T * R).sum(1)
+    cast = [t.to(dtype) for t in (G, Y, x, R, Rd)]
+    g_r, gY, gxe = _ext.ops().conv_force(N, C, P, E, plan.dst_ptr, plan.src32, *cast)
+    torch.testing.assert_close(g_r.double(), ref_gr, rtol=tol, atol=tol * 10)
+    torch.testing.assert_close(gY.double(), ref_gY, rtol=tol, atol=tol * 10)
+    torch.testing.assert_close(gxe.double(), ref_gxe, rtol=tol, atol=tol * 10)
+
+
 def test_lean_chunks_match_single_pass():
     """The chunked force pass (radial network recomputed per chunk) against the unchunked one."""
     from xnn_b200.models import ForceStressOutput

@@ -135,3 +135,23 @@ def test_fused_loss_kernel_matches_formulas(monkeypatch):
     torch.testing.assert_close(f1, f0, rtol=1e-10, atol=1e-14)
     for k in logs0:
         torch.testing.assert_close(logs1[k], logs0[k], rtol=1e-12, atol=1e-14)
+
+
+@pytest.mark.gpu
+def test_grouped_species_linear_matches_all_blocks():
+    from xnn_b200.models.mace_fast import species_linear
+    from xnn_b200.ops import node_gemm as NG
+    torch.manual_seed(0)
+    N, n_el, C = 1000, 5, 96
+    z = torch.randint(0, n_el, (N,), device="cuda")
+    z[z == 3] = 2                                            # one element absent
+    Wz = torch.randn(n_el, C, C, device="cuda") / C ** 0.5
+    for lead in ((), (7,)):
+        h = torch.randn(*lead, N, C, device="cuda", requires_grad=True)
+        ref = species_linear(h, z, Wz)
+        got = NG.species_linear(h, z, Wz)
+        torch.testing.assert_close(got, ref, rtol=2e-5, atol=2e-5)
+        g = torch.randn_like(ref)
+        (dr,) = torch.autograd.grad(ref, h, g)
+        (dg,) = torch.autograd.grad(got, h, g)
+        torch.testing.assert_close(dg, dr, rtol=2e-5, atol=2e-5)

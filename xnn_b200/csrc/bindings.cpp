@@ -29,6 +29,10 @@ cudaError_t conv_edge(int, int, int, const int64_t*, const int*, const int64_t*,
 template <typename T>
 cudaError_t conv_sender_sum(int, int, const int64_t*, const int64_t*, const T*, T*, cudaStream_t);
 template <typename T>
+cudaError_t conv_force(int, int, int, const int64_t*, const int*, const T*, const T*, const T*, const T*, const T*,
+                       T*, T*, T*, cudaStream_t);
+int conv_force_blocks(int C);
+template <typename T>
 cudaError_t conv_scatter(int, int, int, const int64_t*, const int64_t*, int, const T* const*, const T* const*,
                          T*, cudaStream_t);
 template <typename T>
@@ -311,7 +315,8 @@ std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t
                                         std::vector<torch::Tensor> Ys, std::vector<c10::optional<torch::Tensor>> xs,
                                         std::vector<bool> want_T, bool want_gR,
                                         std::vector<torch::Tensor> xY, std::vector<torch::Tensor> RY,
-                                        c10::optional<torch::Tensor> Rd, c10::optional<torch::Tensor> Rx) {
+                                        c10::optional<torch::Tensor> Rd, c10::optional<torch::Tensor> Rx,
+                                        c10::optional<torch::Tensor> gxe_out) {
   // with Rd (E, P, C): the first output is g_r[e] = sum_{l,c} gR[e,l,c] Rd[e,l,c] (E,) instead of gR
   TORCH_CHECK(Ys.size() == xs.size() && Ys.size() == want_T.size() && Ys.size() <= 2,
               "conv_edge: 0-2 Y terms with matching x / want_T");
@@ -336,7 +341,15 @@ std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t
     check_cuda(*Rx, "Rx");
     TORCH_CHECK(!Ys.empty() && Rx->is_contiguous() && Rx->numel() == E * P * C, "conv_edge: Rx (E, P, C)");
   }
-  torch::Tensor gxe = sender ? torch::empty({E, C}, G.options()) : torch::Tensor();
+  torch::Tensor gxe;
+  if (sender && gxe_out.has_value() && gxe_out->defined()) {
+    gxe = *gxe_out;
+    check_cuda(gxe, "gxe_out");
+    TORCH_CHECK(gxe.is_contiguous() && gxe.dim() == 2 && gxe.size(0) == E && gxe.size(1) == C &&
+                    gxe.scalar_type() == G.scalar_type(), "conv_edge: gxe_out (E, C) contiguous, G's dtype");
+  } else if (sender) {
+    gxe = torch::empty({E, C}, G.options());
+  }
   auto st = at::cuda::getCurrentCUDAStream();
   AT_DISPATCH_FLOATING_TYPES(G.scalar_type(), "conv_edge", [&] {
     auto pY = ptrs<scalar_t>(Ys, "Y");
@@ -365,6 +378,41 @@ std::vector<torch::Tensor> conv_edge_op(int64_t N, int64_t C, int64_t P, int64_t
                                     sender ? gxe.data_ptr<scalar_t>() : nullptr, st));
   });
   return {contract ? g_r : gR, gY, Ts[0], Ts[1], gxe};
+}
+
+// Force pass of one convolution over receiver-sorted edges (no permutation): returns [g_r (E),
+// gY (E, P*P), gxe (E, C)]; gxe is written into gxe_out when given.
+std::vector<torch::Tensor> conv_force_op(int64_t N, int64_t C, int64_t P, int64_t E, torch::Tensor dst_ptr,
+                                         torch::Tensor src, torch::Tensor G, torch::Tensor Y, torch::Tensor x,
+                                         torch::Tensor R, torch::Tensor Rd, c10::optional<torch::Tensor> gxe_out) {
+  for (auto* t : {&G, &Y, &x, &R, &Rd}) {
+    check_cuda(*t, "conv_force operand");
+    TORCH_CHECK(t->is_contiguous() && t->scalar_type() == G.scalar_type(), "conv_force: contiguous, one dtype");
+  }
+  TORCH_CHECK(R.numel() == E * P * C && Rd.numel() == E * P * C && Y.numel() == E * P * P && x.size(1) == C &&
+                  G.numel() == P * P * N * C && dst_ptr.numel() == N + 1 && src.numel() >= E,
+              "conv_force: shapes");
+  c10::cuda::CUDAGuard g(G.device());
+  const bool split = conv_force_blocks((int)C) > 1;
+  auto g_r = split ? torch::zeros({E}, G.options()) : torch::empty({E}, G.options());
+  auto gY = split ? torch::zeros({E, P * P}, G.options()) : torch::empty({E, P * P}, G.options());
+  torch::Tensor gxe;
+  if (gxe_out.has_value() && gxe_out->defined()) {
+    gxe = *gxe_out;
+    check_cuda(gxe, "gxe_out");
+    TORCH_CHECK(gxe.is_contiguous() && gxe.dim() == 2 && gxe.size(0) == E && gxe.size(1) == C &&
+                    gxe.scalar_type() == G.scalar_type(), "conv_force: gxe_out (E, C) contiguous, G's dtype");
+  } else {
+    gxe = torch::empty({E, C}, G.options());
+  }
+  auto st = at::cuda::getCurrentCUDAStream();
+  AT_DISPATCH_FLOATING_TYPES(G.scalar_type(), "conv_force", [&] {
+    XNN_CUDA_OK(conv_force<scalar_t>((int)N, (int)C, (int)P, dst_ptr.data_ptr<int64_t>(), src.data_ptr<int>(),
+                                     G.data_ptr<scalar_t>(), Y.data_ptr<scalar_t>(), x.data_ptr<scalar_t>(),
+                                     R.data_ptr<scalar_t>(), Rd.data_ptr<scalar_t>(), g_r.data_ptr<scalar_t>(),
+                                     gY.data_ptr<scalar_t>(), gxe.data_ptr<scalar_t>(), st));
+  });
+  return {g_r, gY, gxe};
 }
 
 // gx[s] = sum over the edges out of s of v[e] (v (E, C), the gxe rows of conv_edge)
@@ -475,8 +523,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv_edge", &conv_edge_op, pybind11::arg("N"), pybind11::arg("C"), pybind11::arg("P"), pybind11::arg("E"),
         pybind11::arg("dst_ptr"), pybind11::arg("src"), pybind11::arg("perm"), pybind11::arg("G"), pybind11::arg("Ys"),
         pybind11::arg("xs"), pybind11::arg("want_T"), pybind11::arg("want_gR"), pybind11::arg("xY"),
-        pybind11::arg("RY"), pybind11::arg("Rd") = pybind11::none(), pybind11::arg("Rx") = pybind11::none());
+        pybind11::arg("RY"), pybind11::arg("Rd") = pybind11::none(), pybind11::arg("Rx") = pybind11::none(),
+        pybind11::arg("gxe_out") = pybind11::none());
   m.def("conv_sender_sum", &conv_sender_sum_op);
+  m.def("conv_force", &conv_force_op, pybind11::arg("N"), pybind11::arg("C"), pybind11::arg("P"), pybind11::arg("E"),
+        pybind11::arg("dst_ptr"), pybind11::arg("src"), pybind11::arg("G"), pybind11::arg("Y"), pybind11::arg("x"),
+        pybind11::arg("R"), pybind11::arg("Rd"), pybind11::arg("gxe_out") = pybind11::none());
   m.def("conv_scatter", &conv_scatter_op);
   m.def("symcon_fwd", &symcon_fwd_op);
   m.def("symcon_bwd", &symcon_bwd_op);

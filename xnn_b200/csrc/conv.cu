@@ -334,40 +334,159 @@ __global__ void __launch_bounds__(32 * WPA) conv_scatter_kernel(
   }
 }
 
+// Force pass of one convolution (first derivatives only, the radial network in forward mode):
+// per edge e = (s -> d) with T[l, c] = sum_m G[lm, d, c] Y[e, lm]
+//   g_r[e]    = sum_{l,c} x[s, c] T[l, c] Rd[e, l, c]        (Rd = dR/dr of the radial network)
+//   gY[e, lm] = sum_c G[lm, d, c] R[e, l, c] x[s, c]
+//   gxe[e, c] = sum_l T[l, c] R[e, l, c]                       (the edge's term of the sender cotangent)
+// One block of WPA warps per receiver, the receiver's G staged in shared memory (registers stay
+// for the streamed rows); EPS edges per warp step with all their loads issued before the
+// arithmetic, the edges' harmonics in one coalesced load broadcast by shuffles. With the channels
+// split over two column blocks, g_r and gY meet by atomic addition onto zeros (exact for two terms).
+template <typename T, int P, int CPL, int WPA, int EPS>
+__global__ void __launch_bounds__(32 * WPA) conv_force_kernel(
+    int N, int C, const int64_t* __restrict__ dst_ptr, const int* __restrict__ src, const T* __restrict__ G,
+    const T* __restrict__ Y, const T* __restrict__ x, const T* __restrict__ R, const T* __restrict__ Rd,
+    T* __restrict__ g_r, T* __restrict__ gY, T* __restrict__ gxe, int atomic) {
+  constexpr int D = P * P;
+  constexpr int W = 32 * CPL;
+  __shared__ T gs[D * W];
+  const int i = blockIdx.x;
+  const int w = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int cbase = blockIdx.y * W;
+  for (int k = threadIdx.x; k < D * W; k += 32 * WPA) {
+    const int d = k / W, c = cbase + k % W;
+    gs[k] = c < C ? G[((int64_t)d * N + i) * C + c] : T(0);
+  }
+  __syncthreads();
+  const int64_t j0 = dst_ptr[i], j1 = dst_ptr[i + 1];
+  for (int64_t j = j0 + w; j < j1; j += EPS * WPA) {
+    int64_t e[EPS], sv[EPS];
+    bool ok[EPS];
+#pragma unroll
+    for (int u = 0; u < EPS; ++u) {
+      ok[u] = j + u * WPA < j1;
+      e[u] = ok[u] ? j + u * WPA : j;
+      sv[u] = src[e[u]];
+    }
+    T yv = T(0);
+#pragma unroll
+    for (int u = 0; u < EPS; ++u)
+      if (ok[u] && lane >= u * D && lane < (u + 1) * D) yv = __ldg(Y + e[u] * D + (lane - u * D));
+    T xs[EPS][CPL], r[EPS][CPL][P], rd[EPS][CPL][P];
+#pragma unroll
+    for (int u = 0; u < EPS; ++u)
+#pragma unroll
+      for (int q = 0; q < CPL; ++q) {
+        const int c = cbase + lane + 32 * q;
+        const bool in = c < C && ok[u];
+        xs[u][q] = in ? __ldg(x + sv[u] * C + c) : T(0);
+#pragma unroll
+        for (int l = 0; l < P; ++l) {
+          r[u][q][l] = in ? __ldg(R + (e[u] * P + l) * C + c) : T(0);
+          rd[u][q][l] = in ? __ldg(Rd + (e[u] * P + l) * C + c) : T(0);
+        }
+      }
+    T t[EPS][CPL][P];
+    T v[EPS][16];
+#pragma unroll
+    for (int u = 0; u < EPS; ++u) {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) v[u][k] = T(0);
+#pragma unroll
+      for (int q = 0; q < CPL; ++q)
+#pragma unroll
+        for (int l = 0; l < P; ++l) t[u][q][l] = T(0);
+    }
+#pragma unroll
+    for (int l = 0; l < P; ++l)
+#pragma unroll
+      for (int m = 0; m < 2 * l + 1; ++m) {
+        const int lm = l * l + m;
+        T yy[EPS];
+#pragma unroll
+        for (int u = 0; u < EPS; ++u) yy[u] = __shfl_sync(0xffffffffu, yv, u * D + lm);
+#pragma unroll
+        for (int q = 0; q < CPL; ++q) {
+          const T gv = gs[lm * W + q * 32 + lane];
+#pragma unroll
+          for (int u = 0; u < EPS; ++u) {
+            t[u][q][l] += gv * yy[u];
+            v[u][lm] += gv * r[u][q][l] * xs[u][q];
+          }
+        }
+      }
+#pragma unroll
+    for (int u = 0; u < EPS; ++u) {
+      T acc = T(0);
+#pragma unroll
+      for (int q = 0; q < CPL; ++q) {
+        T sx = T(0), sd = T(0);
+#pragma unroll
+        for (int l = 0; l < P; ++l) {
+          sx += t[u][q][l] * r[u][q][l];
+          sd += t[u][q][l] * rd[u][q][l];
+        }
+        acc += xs[u][q] * sd;
+        const int c = cbase + lane + 32 * q;
+        if (ok[u] && c < C) gxe[e[u] * C + c] = sx;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      reduce16(v[u], lane);
+      if (ok[u]) {
+        if (lane == 0) {
+          if (atomic) atomicAdd(g_r + e[u], acc);
+          else g_r[e[u]] = acc;
+        }
+        const int idx = reduce16_index(lane);
+        if ((lane & 1) == 0 && idx < D) {
+          if (atomic) atomicAdd(gY + e[u] * D + idx, v[u][0]);
+          else gY[e[u] * D + idx] = v[u][0];
+        }
+      }
+    }
+  }
+}
+
 // gx[s, c] = sum over the edges out of s of v[e, c] (rows of conv_edge_kernel's gxe), edges via
-// the sender permutation; the warps' partial sums meet in shared memory in a fixed order.
-template <typename T, int CPL, int WPA>
-__global__ void __launch_bounds__(32 * WPA) conv_sender_sum_kernel(
+// the sender permutation. One warp per sender, CPL channels per lane; four edges per step with all
+// their loads issued first (memory-level parallelism for the short, scattered rows); each lane
+// adds its edges in the permutation's order: deterministic.
+template <typename T, int CPL>
+__global__ void __launch_bounds__(256) conv_sender_sum_kernel(
     int N, int C, const int64_t* __restrict__ src_ptr, const int64_t* __restrict__ src_perm,
     const T* __restrict__ v, T* __restrict__ gx) {
-  const int s = blockIdx.x;
-  const int w = threadIdx.x >> 5;
+  const int s = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (s >= N) return;
   const int lane = threadIdx.x & 31;
   const int cbase = blockIdx.y * 32 * CPL;
   T acc[CPL];
 #pragma unroll
   for (int q = 0; q < CPL; ++q) acc[q] = T(0);
   const int64_t j0 = src_ptr[s], j1 = src_ptr[s + 1];
-  for (int64_t j = j0 + w; j < j1; j += WPA) {
-    const int64_t e = src_perm[j];
+  for (int64_t j = j0; j < j1; j += 4) {
+    int64_t e[4];
 #pragma unroll
-    for (int q = 0; q < CPL; ++q) {
-      const int c = cbase + lane + 32 * q;
-      if (c < C) acc[q] += __ldg(v + e * C + c);
-    }
+    for (int u = 0; u < 4; ++u) e[u] = j + u < j1 ? __ldg(src_perm + j + u) : -1;
+    T val[4][CPL];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int q = 0; q < CPL; ++q) {
+        const int c = cbase + lane + 32 * q;
+        val[u][q] = (e[u] >= 0 && c < C) ? __ldg(v + e[u] * C + c) : T(0);
+      }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int q = 0; q < CPL; ++q) acc[q] += val[u][q];
   }
-  __shared__ T red[WPA][32 * CPL];
-#pragma unroll
-  for (int q = 0; q < CPL; ++q) red[w][q * 32 + lane] = acc[q];
-  __syncthreads();
-  if (w != 0) return;
 #pragma unroll
   for (int q = 0; q < CPL; ++q) {
-    T t = red[0][q * 32 + lane];
-#pragma unroll
-    for (int ww = 1; ww < WPA; ++ww) t += red[ww][q * 32 + lane];
     const int c = cbase + lane + 32 * q;
-    if (c < C) gx[(int64_t)s * C + c] = t;
+    if (c < C) gx[(int64_t)s * C + c] = acc[q];
   }
 }
 
@@ -500,13 +619,53 @@ template <typename T>
 cudaError_t conv_sender_sum(int N, int C, const int64_t* src_ptr, const int64_t* src_perm, const T* v, T* gx,
                             cudaStream_t stream) {
   if (N == 0) return cudaSuccess;
-  const int cpl = scatter_cpl(C);
-  dim3 grid(N, (C + 32 * cpl - 1) / (32 * cpl));
+  const int cpl = std::min(4, std::max(1, (C + 31) / 32));
+  dim3 grid((N + 7) / 8, (C + 32 * cpl - 1) / (32 * cpl));
   switch (cpl) {
-    case 1: conv_sender_sum_kernel<T, 1, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
-    case 2: conv_sender_sum_kernel<T, 2, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
-    case 3: conv_sender_sum_kernel<T, 3, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
-    default: conv_sender_sum_kernel<T, 4, kWPA><<<grid, 32 * kWPA, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
+    case 1: conv_sender_sum_kernel<T, 1><<<grid, 256, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
+    case 2: conv_sender_sum_kernel<T, 2><<<grid, 256, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
+    case 3: conv_sender_sum_kernel<T, 3><<<grid, 256, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
+    default: conv_sender_sum_kernel<T, 4><<<grid, 256, 0, stream>>>(N, C, src_ptr, src_perm, v, gx); break;
+  }
+  return cudaGetLastError();
+}
+
+inline int force_cpl(int C) {
+  static int forced = -1;
+  const int f = forced_cpl("XNN_B200_FORCE_CPL", forced);
+  int cpl = f > 0 ? f : std::min(2, cpl_for(C));
+  while (cpl < 4 && (C + 32 * cpl - 1) / (32 * cpl) > 2) ++cpl;
+  return cpl;
+}
+inline int force_eps() {
+  static int cache = -1;
+  if (cache < 0) {
+    const char* v = getenv("XNN_B200_FORCE_EPS");
+    cache = (v != nullptr && v[0] == '1') ? 1 : 2;
+  }
+  return cache;
+}
+
+// column blocks of the force kernel (g_r / gY need zero initialisation when > 1)
+int conv_force_blocks(int C) {
+  const int cpl = force_cpl(C);
+  return (C + 32 * cpl - 1) / (32 * cpl);
+}
+
+template <typename T>
+cudaError_t conv_force(int N, int C, int P, const int64_t* dst_ptr, const int* src, const T* G, const T* Y,
+                       const T* x, const T* R, const T* Rd, T* g_r, T* gY, T* gxe, cudaStream_t stream) {
+  if (N == 0) return cudaSuccess;
+  const int cpl = force_cpl(C);
+  const int gy = (C + 32 * cpl - 1) / (32 * cpl);
+  dim3 grid(N, gy);
+  const int atomic = gy > 1 ? 1 : 0;
+  if (force_eps() == 1) {
+    XNN_P_CPL_SWITCH(P, cpl, conv_force_kernel<T, PP, QQ, kWPA, 1><<<grid, 32 * kWPA, 0, stream>>>(
+        N, C, dst_ptr, src, G, Y, x, R, Rd, g_r, gY, gxe, atomic));
+  } else {
+    XNN_P_CPL_SWITCH(P, cpl, conv_force_kernel<T, PP, QQ, kWPA, 2><<<grid, 32 * kWPA, 0, stream>>>(
+        N, C, dst_ptr, src, G, Y, x, R, Rd, g_r, gY, gxe, atomic));
   }
   return cudaGetLastError();
 }
@@ -526,6 +685,8 @@ int conv_edge_blocks(int C) {
                                     const T* const*, const T* const*, T*, T*, const T*, T*, const T*, T*, \
                                     cudaStream_t);                                                    \
   template cudaError_t conv_sender_sum<T>(int, int, const int64_t*, const int64_t*, const T*, T*, cudaStream_t); \
+  template cudaError_t conv_force<T>(int, int, int, const int64_t*, const int*, const T*, const T*, const T*,    \
+                                     const T*, const T*, T*, T*, T*, cudaStream_t);                              \
   template cudaError_t conv_scatter<T>(int, int, int, const int64_t*, const int64_t*, int,           \
                                        const T* const*, const T* const*, T*, cudaStream_t);
 XNN_INST(float)

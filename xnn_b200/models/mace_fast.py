@@ -24,6 +24,7 @@ from torch.utils.checkpoint import checkpoint
 
 from ..ops import gemm
 from ..ops import mace_ops as K
+from ..ops import node_gemm as NG
 from ..ops.lean_conv import lean_radial_conv
 from ..ops.radial import radial_network
 from ..ops.scatter import refresh_ghosts
@@ -47,8 +48,13 @@ def _species_weights(tp, n_el: int, block: int = 0) -> Tensor:
     return (w * (ins.path_weight * cg)).permute(1, 0, 2)
 
 
-def species_linear(h: Tensor, z: Tensor, Wz: Tensor) -> Tensor:
-    """``out[i] = h[i] @ Wz[z_i]`` for ``h (..., N, C_in)`` and ``Wz (n_el, C_in, C_out)``."""
+def species_linear(h: Tensor, z: Tensor, Wz: Tensor, grouped: bool = False) -> Tensor:
+    """``out[i] = h[i] @ Wz[z_i]`` for ``h (..., N, C_in)`` and ``Wz (n_el, C_in, C_out)``. With
+    ``grouped`` (evaluation: constant weights) the rows of each element are multiplied by that
+    element's matrix only, in one grouped tensor-core launch; otherwise by all matrices, keeping
+    the matching block (differentiable in the weights)."""
+    if grouped and NG.grouped_species_ok(h, Wz):
+        return NG.species_linear(h, z, Wz)
     n_el, c_in, c_out = Wz.shape
     full = gemm.matmul(h, Wz.permute(1, 0, 2).reshape(c_in, n_el * c_out))   # (..., N, n_el*C_out)
     full = full.view(*h.shape[:-1], n_el, c_out)
@@ -147,6 +153,7 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
         if not model.training else None
     n_el = len(model.species)
     C = model.num_features
+    grouped = not model.training
     emb = model.node_embedding
     h = _linear_blocks(emb)[0].index_select(0, z)                       # (N, C)
     inter = torch.zeros_like(e0)
@@ -154,13 +161,13 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
     for t, (blk, prod, readout) in enumerate(zip(model.interactions, model.products, model.readouts)):
         if t > 0:
             h = refresh_ghosts(h)
-        sc = species_linear(h, z, _species_weights(blk.skip_tp, n_el)) if blk.residual else None
+        sc = species_linear(h, z, _species_weights(blk.skip_tp, n_el), grouped) if blk.residual else None
         h_up = gemm.matmul(h, _linear_blocks(blk.linear_up)[0])
         if chunks is None:
             A = _messages(h_up, r, Y, plan, blk, ef, P, C)               # (D, N, C)
         elif h_up.is_cuda:
             A = lean_radial_conv(h_up, r, Y, chunks, blk.conv_tp_weights, _conv_path_scale(blk, r),
-                                 ef.rbf.freqs, ef.rbf.norm, ef.cutoff, ef.envelope.p, P)
+                                 ef.rbf.freqs, ef.rbf.norm, ef.cutoff, ef.envelope.p, P, plan)
         else:
             A = torch.cat([checkpoint(_messages, h_up, r[e0:e1], Y[e0:e1], sub, blk, ef, P, C,
                                       use_reentrant=False) for (e0, e1), _, sub in chunks], dim=1)
@@ -173,7 +180,8 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
         if not blk.residual:
             outs = []
             for l in range(P):
-                outs.append(species_linear(A2[l * l:(l + 1) * (l + 1)], z, _species_weights(blk.skip_tp, n_el, l)))
+                outs.append(species_linear(A2[l * l:(l + 1) * (l + 1)], z, _species_weights(blk.skip_tp, n_el, l),
+                                           grouped))
             A2 = torch.cat(outs, 0) if P > 1 else outs[0]
         sym = prod.symmetric_contractions.contractions[0]
         W = torch.cat(list(sym.weights), dim=1)                         # (n_el, K, C)

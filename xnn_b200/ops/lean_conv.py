@@ -64,7 +64,7 @@ Chunk = Tuple[Tuple[int, int], Tuple[int, int], EdgePlan]
 class _LeanRadialConv(Function):
     @staticmethod
     def forward(ctx, x: Tensor, r: Tensor, Y: Tensor, chunks: Sequence[Chunk], spec: RadialSpec, P: int,
-                *Ws: Tensor) -> Tensor:
+                plan: Optional[EdgePlan], *Ws: Tensor) -> Tensor:
         C = x.shape[1]
         N = chunks[-1][1][1]
         K = _ext.ops()
@@ -75,7 +75,7 @@ class _LeanRadialConv(Function):
             R = _primal(r[e0:e1], We, spec).view(-1, P, C)
             A[:, n0:n1] = K.conv_gather(n1 - n0, C, P, sub.dst_ptr, sub.src32, None, [xc], [R],
                                         [Y[e0:e1].contiguous()])
-        ctx.chunks, ctx.spec, ctx.P = chunks, spec, P
+        ctx.chunks, ctx.spec, ctx.P, ctx.plan = chunks, spec, P, plan
         ctx.save_for_backward(x, r, Y, *Ws)
         return A
 
@@ -89,34 +89,44 @@ class _LeanRadialConv(Function):
         K = _ext.ops()
         We = _eff(Ws, spec)
         xc = x.contiguous()
-        gx = torch.zeros_like(xc) if ctx.needs_input_grad[0] else None
+        want_x = ctx.needs_input_grad[0]
+        gx = None
         g_r = torch.empty_like(r) if ctx.needs_input_grad[1] else None
         gY = torch.empty_like(Y) if ctx.needs_input_grad[2] else None
+        # the edges' sender terms of every chunk in one (E, C) buffer, summed per sender once over
+        # the whole graph's sender ordering; per chunk when that buffer does not fit
+        plan = ctx.plan
+        E = r.shape[0]
+        whole = want_x and plan is not None and 2 * E * C * x.element_size() < torch.cuda.mem_get_info(x.device)[0]
+        gxe_all = x.new_empty((E, C)) if whole else None
+        if want_x and not whole:
+            gx = torch.zeros_like(xc)
         for (e0, e1), (n0, n1), sub in ctx.chunks:
             fused = _primal_tangent(r[e0:e1], We, spec)
             R, Rd = fused if fused is not None else _forward(r[e0:e1], We, spec)[:2]
             R, Rd = R.view(-1, P, C), Rd.view(-1, P, C)
             Gc = G[:, n0:n1].contiguous()
             Yc = Y[e0:e1].contiguous()
-            want_y = gY is not None
-            # the edge kernel contracts gR with dR/dr itself (g_r without the (E, P, C) gR tensor)
+            # the force kernel contracts gR with dR/dr itself (g_r without the (E, P, C) gR tensor)
             # and writes each edge's (E, C) term of the sender cotangent, summed per sender after
-            g_rc, gYc, _, _, gxe = K.conv_edge(n1 - n0, C, P, e1 - e0, sub.dst_ptr, sub.src32, None, Gc, [Yc],
-                                               [xc], [False], g_r is not None, [xc] if want_y else [],
-                                               [R] if want_y else [], Rd.contiguous(),
-                                               R.contiguous() if gx is not None else None)
+            g_rc, gYc, gxe = K.conv_force(n1 - n0, C, P, e1 - e0, sub.dst_ptr, sub.src32, Gc, Yc, xc,
+                                          R.contiguous(), Rd.contiguous(), gxe_all[e0:e1] if whole else None)
             if g_r is not None:
                 g_r[e0:e1] = g_rc
-            if want_y:
+            if gY is not None:
                 gY[e0:e1] = gYc
-            if gx is not None:
+            if want_x and not whole:
                 gx += K.conv_sender_sum(N_src, sub.src_ptr, sub.src_perm, gxe)
-        return (gx, g_r, gY, None, None, None) + (None,) * len(Ws)
+        if whole:
+            gx = K.conv_sender_sum(N_src, plan.src_ptr, plan.src_perm, gxe_all)
+        return (gx, g_r, gY, None, None, None, None) + (None,) * len(Ws)
 
 
 def lean_radial_conv(x: Tensor, r: Tensor, Y: Tensor, chunks: Sequence[Chunk], net, col_scale: Tensor,
-                     freqs: Tensor, norm: float, rc: float, p: int, P: int) -> Tensor:
-    """``A (P*P, N, C)`` of the MACE message pass with the radial network ``net`` (see module notes)."""
+                     freqs: Tensor, norm: float, rc: float, p: int, P: int,
+                     plan: Optional[EdgePlan] = None) -> Tensor:
+    """``A (P*P, N, C)`` of the MACE message pass with the radial network ``net`` (see module notes);
+    ``plan``: the whole graph's edge plan (sender ordering of the chunks' edges taken together)."""
     spec = RadialSpec(net, col_scale, freqs, norm, rc, p)
     Ws = [layer.weight for layer in net]
-    return _LeanRadialConv.apply(x, r, Y, chunks, spec, P, *Ws)
+    return _LeanRadialConv.apply(x, r, Y, chunks, spec, P, plan, *Ws)

@@ -201,3 +201,73 @@ def edge_forces(plan, v: Tensor, out_dtype: torch.dtype) -> Tensor:
                                       out_dtype)
     F = torch.zeros(plan.n_nodes, 3, dtype=v.dtype, device=v.device)
     return F.index_add_(0, plan.src, v).index_add_(0, plan.dst, -v).to(out_dtype)
+
+
+def _grouped_rows(z: Tensor, n_el: int, lead: int):
+    """Row permutation and element segments of ``lead`` stacked copies of the atoms: element
+    ``k``'s rows (every copy) are ``perm[lead * seg[k]:lead * seg[k + 1]]``; plus the host counts."""
+    perm, seg = species_sort(z, n_el)
+    N = z.shape[0]
+    seg64 = seg.long()
+    segs = (seg64 * lead).to(torch.int32)
+    if lead == 1:
+        return perm, segs, seg64.cpu()
+    q = torch.arange(lead * N, device=z.device)
+    k = torch.searchsorted(segs[1:].long(), q, right=True)
+    s, c = seg64[k], (seg64[k + 1] - seg64[k]).clamp_min(1)
+    local = q - lead * s
+    full = (local // c) * N + perm.long()[s + local % c]
+    return full.to(torch.int32), segs, seg64.cpu()
+
+
+def _grouped_product(X: Tensor, Ws: Sequence[Tensor], perm: Tensor, segs: Tensor, counts: Tensor,
+                     lead: int) -> Tensor:
+    Y = torch.empty(X.shape[0], Ws[0].shape[1], dtype=X.dtype, device=X.device)
+    packed = pack(list(Ws))
+    probs = []
+    for k, W in enumerate(Ws):
+        rows = lead * int(counts[k + 1] - counts[k])
+        if rows > 0:
+            probs.append(MM(X, W, Y, packed[k], perm=perm, seg=segs[k:k + 2], rows=rows))
+    mm(probs)
+    return Y
+
+
+class _SpeciesLinear(torch.autograd.Function):
+    """``Y = X @ W[z]`` per row, rows grouped by element; the backward is the same product with
+    the transposed matrices (differentiable again). The weights are constants here."""
+
+    @staticmethod
+    def forward(ctx, X: Tensor, Wz: Tensor, perm: Tensor, segs: Tensor, counts: Tensor, lead: int):
+        ctx.save_for_backward(Wz, perm, segs)
+        ctx.counts, ctx.lead = counts, lead
+        return _grouped_product(X, list(Wz.unbind(0)), perm, segs, counts, lead)
+
+    @staticmethod
+    def backward(ctx, g: Tensor):
+        Wz, perm, segs = ctx.saved_tensors
+        dX = _SpeciesLinear.apply(g.contiguous(), Wz.transpose(1, 2), perm, segs, ctx.counts, ctx.lead)
+        return dX, None, None, None, None, None
+
+
+def grouped_species_ok(h: Tensor, Wz: Tensor) -> bool:
+    """Whether :func:`species_linear` takes the grouped kernel for these operands."""
+    c_in, c_out = int(Wz.shape[1]), int(Wz.shape[2])
+    ok = lambda n: 16 <= n <= 128 and n % 16 == 0
+    return (kernels(h) and Wz.dtype == torch.float32 and ok(c_in) and ok(c_out) and h.shape[-1] == c_in
+            and not torch.cuda.is_current_stream_capturing())      # it reads the element counts
+
+
+def species_linear(h: Tensor, z: Tensor, Wz: Tensor) -> Tensor:
+    """``out[..., i, :] = h[..., i, :] @ Wz[z_i]`` for ``h (..., N, C_in)`` with constant
+    ``Wz (n_el, C_in, C_out)``: the rows of every element in one grouped tcgen05 launch (each row
+    multiplied by its own element's matrix only). Float32 CUDA; reads the element counts once."""
+    n_el, c_in, c_out = Wz.shape
+    lead = 1
+    for d in h.shape[:-2]:
+        lead *= int(d)
+    perm, segs, counts = _grouped_rows(z, n_el, lead)
+    X = h.reshape(-1, c_in)
+    X = X if X.is_contiguous() else X.contiguous()
+    out = _SpeciesLinear.apply(X, Wz.detach().contiguous(), perm, segs, counts, lead)
+    return out.view(*h.shape[:-1], c_out)

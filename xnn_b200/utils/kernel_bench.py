@@ -95,6 +95,16 @@ def build_ops(case) -> Dict[str, tuple]:
                         f * (P * P * N * C + E * P * P + N * C + 2 * E * P * C))
     out["conv_scatter"] = (lambda: ops.conv_scatter(N, C, P, plan.src_ptr, plan.src_perm, [R], [T1]),
                            f * (2 * E * P * C + N * C))
+    Rd = torch.randn(E, P, C, device="cuda")
+    # force pass (MD): reads R, Rd, Y, x[src], G once per receiver; writes g_r, gY, the (E, C) sender terms
+    out["conv_force"] = (lambda: ops.conv_force(N, C, P, E, plan.dst_ptr, plan.src32, G, Y, x, R, Rd),
+                         f * (2 * E * P * C + E * P * P + E * C + P * P * N * C + E + E * P * P + E * C))
+    out["conv_edge_force"] = (lambda: ops.conv_edge(N, C, P, E, plan.dst_ptr, plan.src32, None, G, [Y], [x], [False],
+                                                    True, [x], [R], Rd, R),
+                              f * (2 * E * P * C + E * P * P + E * C + P * P * N * C + E + E * P * P + E * C))
+    gxe = torch.randn(E, C, device="cuda")
+    out["conv_sender_sum"] = (lambda: ops.conv_sender_sum(N, plan.src_ptr, plan.src_perm, gxe),
+                              f * (E * C + N * C) + 8 * E)
     H = 64
     Hr = torch.randn(2 * E, H, device="cuda")
     W2 = torch.randn(H, P * C, device="cuda")

@@ -78,15 +78,17 @@ def region(name: str):
             torch.cuda.nvtx.range_pop()
 
 
-def kernel_table(fn: Callable[[], object], warmup: int = 1, ops: bool = False) -> Dict[str, object]:
+def kernel_table(fn: Callable[[], object], warmup: int = 1, ops: bool = False,
+                 stacks: int = 0) -> Dict[str, object]:
     """GPU kernels launched by one call of ``fn`` (after ``warmup`` untimed calls); with ``ops``
-    also the host operators that launched device work, by count (``"ops"``)."""
+    also the host operators that launched device work, by count (``"ops"``); with ``stacks`` the
+    Python call sites (``stacks`` frames deep) of the host operators with the most device time."""
     from torch.profiler import ProfilerActivity, profile
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    acts = [ProfilerActivity.CUDA] + ([ProfilerActivity.CPU] if ops else [])
-    with profile(activities=acts) as prof:
+    acts = [ProfilerActivity.CUDA] + ([ProfilerActivity.CPU] if (ops or stacks) else [])
+    with profile(activities=acts, with_stack=bool(stacks)) as prof:
         fn()
         torch.cuda.synchronize()
     count: Dict[str, int] = defaultdict(int)
@@ -109,6 +111,12 @@ def kernel_table(fn: Callable[[], object], warmup: int = 1, ops: bool = False) -
         avg = [k for k in prof.key_averages() if getattr(k, "self_device_time_total", 0) > 0]
         avg.sort(key=lambda k: -k.count)
         out["ops"] = [{"op": k.key, "calls": k.count, "us": round(float(k.self_device_time_total), 1)} for k in avg]
+    if stacks:
+        avg = [k for k in prof.key_averages(group_by_stack_n=stacks)
+               if getattr(k, "self_device_time_total", 0) > 0 and k.key.startswith("aten::")]
+        avg.sort(key=lambda k: -float(k.self_device_time_total))
+        out["sites"] = [{"op": k.key, "calls": k.count, "us": round(float(k.self_device_time_total), 1),
+                         "stack": [f for f in (k.stack or []) if "torch/" not in f][:stacks]} for k in avg]
     return out
 
 
@@ -198,6 +206,8 @@ def main(argv=None) -> None:
     ap.add_argument("--top", type=int, default=40)
     ap.add_argument("--json", default=None, help="also write the table as JSON to this path")
     ap.add_argument("--ops", action="store_true", help="also list the host operators that launched device work")
+    ap.add_argument("--stacks", type=int, default=0, help="also list the call sites (this many frames) of the "
+                                                          "ATen operators with the most device time")
     a = ap.parse_args(argv)
     if a.model == "mace":
         fn = _mace_step(a.batch or 64)
@@ -207,7 +217,7 @@ def main(argv=None) -> None:
         fn = _pme_eval(a.batch or 100_000)
     else:
         fn = _md_step(a.batch or 1_000_000)
-    tab = kernel_table(fn, warmup=3, ops=a.ops)
+    tab = kernel_table(fn, warmup=3, ops=a.ops, stacks=a.stacks)
     print(f"launches {tab['launches']} (own {tab['own_launches']}), device time {tab['device_us']} us, "
           f"own-kernel share {tab['own_time_share']}")
     for r in tab["rows"][:a.top]:
@@ -216,6 +226,10 @@ def main(argv=None) -> None:
         print("host operators launching device work (calls, device us):")
         for r in tab["ops"][:a.top]:
             print(f"{r['calls']:6d} {r['us']:10.1f} us  {r['op'][:100]}")
+    if a.stacks:
+        print("ATen call sites by device time (calls, device us, frames):")
+        for r in tab["sites"][:a.top]:
+            print(f"{r['calls']:6d} {r['us']:10.1f} us  {r['op']}  <- " + " <- ".join(r["stack"]))
     if a.json:
         import json
         with open(a.json, "w") as f:
