@@ -172,16 +172,15 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
             A = torch.cat([checkpoint(_messages, h_up, r[e0:e1], Y[e0:e1], sub, blk, ef, P, C,
                                       use_reentrant=False) for (e0, e1), _, sub in chunks], dim=1)
         mats = _linear_blocks(blk.linear)
-        parts = []
-        for l in range(P):
-            blk_l = A[l * l:(l + 1) * (l + 1)]
-            parts.append(gemm.matmul(blk_l, mats[l] / blk.avg_num_neighbors))
+        # per-degree blocks as one split (its adjoint is one concatenation; slices would each
+        # add a full-size zero-filled gradient)
+        degrees = [2 * l + 1 for l in range(P)]
+        parts = [gemm.matmul(blk_l, mats[l] / blk.avg_num_neighbors)
+                 for l, blk_l in enumerate(A.split(degrees, 0))]
         A2 = torch.cat(parts, 0) if P > 1 else parts[0]
         if not blk.residual:
-            outs = []
-            for l in range(P):
-                outs.append(species_linear(A2[l * l:(l + 1) * (l + 1)], z, _species_weights(blk.skip_tp, n_el, l),
-                                           grouped))
+            outs = [species_linear(blk_l, z, _species_weights(blk.skip_tp, n_el, l), grouped)
+                    for l, blk_l in enumerate(A2.split(degrees, 0))]
             A2 = torch.cat(outs, 0) if P > 1 else outs[0]
         sym = prod.symmetric_contractions.contractions[0]
         W = torch.cat(list(sym.weights), dim=1)                         # (n_el, K, C)
