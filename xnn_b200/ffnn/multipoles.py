@@ -141,12 +141,12 @@ def spread(pos: Tensor, cell: Tensor, q: Optional[Tensor], d: Optional[Tensor], 
            out_dtype: Optional[torch.dtype] = None) -> Tensor:
     """Mesh of ``sum_i L_i W_i`` (``(K1, K2, K3)``; with ``z_range`` only planes ``[z0, z1)``
     of the third axis, ``(K1, K2, z1 - z0)``). For a float32 mesh of float64 CUDA sites the
-    spreading kernel runs (its adjoint differentiates positions and dipoles)."""
+    spreading kernel runs (its adjoint differentiates positions and dipoles; derivatives in the
+    charges, quadrupoles or cell take the tensor formulas)."""
     n = pos.shape[0]
+    others = torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (q, Q, cell))
     if (out_dtype == torch.float32 and pos.is_cuda and pos.dtype == torch.float64 and 4 <= p <= 6 and _kernel_ok()
-            and hasattr(__import__("xnn_b200._ext", fromlist=["ops"]).ops(), "pme_spread")):
-        if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (q, Q, cell)):
-            raise NotImplementedError("the spreading kernel differentiates positions and dipoles only")
+            and not others and hasattr(__import__("xnn_b200._ext", fromlist=["ops"]).ops(), "pme_spread")):
         z0, z1 = z_range if z_range is not None else (0, mesh[2])
         return _SpreadKernel.apply(pos, d, cell, q, Q, list(mesh), p, z0, z1 - z0)
     K1, K2, K3 = mesh
@@ -336,9 +336,10 @@ def real_energy(pos: Tensor, cell: Tensor, i: Tensor, j: Tensor, shift: Tensor, 
     pairs contribute ``-erf`` (their reciprocal share removed); with ``thole`` the dipole,
     dipole-dipole and dipole-quadrupole kernels are Thole-damped. On CUDA (float64) the pair
     kernel evaluates it (differentiable in positions and dipoles)."""
-    if pos.is_cuda and pos.dtype == torch.float64 and _kernel_ok():
-        if (q.requires_grad or Q.requires_grad or cell.requires_grad) and torch.is_grad_enabled():
-            raise NotImplementedError("the real-space pair kernel differentiates positions and dipoles only")
+    # the pair kernel differentiates positions and dipoles; derivatives in the charges, the
+    # quadrupoles (frame torques) or the cell (stress) take the tensor formulas below
+    others = torch.is_grad_enabled() and (q.requires_grad or Q.requires_grad or cell.requires_grad)
+    if pos.is_cuda and pos.dtype == torch.float64 and _kernel_ok() and not others:
         pw = pol if pol is not None else torch.ones_like(q)
         return _RealKernel.apply(pos, d, cell, q, Q.reshape(-1, 9), pw, i, j, shift, excluded, alpha, thole)
     e = pos.new_zeros(())
@@ -355,6 +356,26 @@ def real_energy(pos: Tensor, cell: Tensor, i: Tensor, j: Tensor, shift: Tensor, 
         B = [torch.where(ex, y, x) for x, y in zip(Bc, Be)]
         e = e + pair_energy(v, q[a], d[a], Q[a], q[b], d[b], Q[b], B).sum()
     return e
+
+
+def intra_dipole_energy(pos: Tensor, cell: Tensor, pairs, mu: Tensor, pol: Tensor, thole: Optional[float]) -> Tensor:
+    """Dipole-dipole energy (Coulomb units) of the excluded (intramolecular) pairs with the bare,
+    Thole-damped kernel: added to a sum in which those pairs contribute nothing, it makes the
+    induced dipoles of a molecule interact in full."""
+    i, j, sh, ex = pairs
+    if not bool(ex.any()):
+        return pos.new_zeros(())
+    a, b, s_ = i[ex], j[ex], sh[ex]
+    v = pos[b] - pos[a] + _shift_vec(s_, cell)
+    r = torch.linalg.norm(v, dim=-1)
+    r2 = r * r
+    B = [1.0 / r, 1.0 / (r2 * r), 3.0 / (r2 * r2 * r), 15.0 / (r2 * r2 * r2 * r), 105.0 / (r2 * r2 * r2 * r2 * r)]
+    if thole is not None:
+        u = r / (pol[a] * pol[b]) ** (1.0 / 6.0)
+        B = thole_damp(B, r, thole * u * u * u)
+    z = mu.new_zeros(a.shape[0])
+    z3 = mu.new_zeros(a.shape[0], 3, 3)
+    return pair_energy(v, z, mu[a], z3, z, mu[b], z3, B).sum()
 
 
 def self_energy(q: Tensor, d: Tensor, Q: Tensor, alpha: float) -> Tensor:
@@ -536,11 +557,14 @@ class PolarizableMultipoles(nn.Module):
     """Energy, forces and induced dipoles of a periodic polarizable multipole system."""
 
     def __init__(self, setup: EwaldSetup = EwaldSetup(), tol_debye: float = 1e-5, max_iter: int = 100,
-                 mesh_backend=None, group=None, thole: Optional[float] = 0.39):
+                 mesh_backend=None, group=None, thole: Optional[float] = 0.39, mutual_intra: bool = False):
         """``mesh_backend``: a :class:`~xnn_b200.ffnn.slab_fft.SlabFFT` to split the mesh over the
         processes of ``group`` (the real-space pairs are split too, and fields, energies and
-        forces summed); ``None`` evaluates everything here."""
+        forces summed); ``None`` evaluates everything here. ``mutual_intra``: the induced dipoles
+        of one molecule interact with each other (Thole-damped, AMOEBA's mutual scale 1), while
+        every interaction of the permanent multipoles within a molecule stays excluded."""
         super().__init__()
+        self.mutual_intra = bool(mutual_intra)
         self.setup = setup
         self.tol = float(tol_debye) * DEBYE
         self.max_iter = int(max_iter)
@@ -605,6 +629,8 @@ class PolarizableMultipoles(nn.Module):
                           - real_energy(pos, cell, i, j, sh, ex, q, d, Q, s.alpha, pol=pol, thole=self.thole))
         if self.rank == 0:
             u = u + KE * 0.5 * ((mu * mu).sum(-1) / pol).sum()
+        if self.mutual_intra:
+            u = u + KE * intra_dipole_energy(pos, cell, pairs, mu, pol, self.thole)
         return u
 
     def field(self, pos, cell, pairs, q, d, Q, pol: Optional[Tensor] = None) -> Tensor:
@@ -643,6 +669,8 @@ class PolarizableMultipoles(nn.Module):
         """The CG iterations of :meth:`induce` for a given permanent field ``F`` (Coulomb units)."""
         damp = pol if self.thole is not None else None
         inv_a = 1.0 / pol[:, None]
+        if self.mutual_intra:              # intramolecular dipole pairs as ordinary damped pairs
+            pairs = (pairs[0], pairs[1], pairs[2], torch.zeros_like(pairs[3]))
         T = DipoleOperator(self, pos, cell, pairs, damp)
 
         def A(v):
