@@ -155,3 +155,25 @@ def test_grouped_species_linear_matches_all_blocks():
         (dr,) = torch.autograd.grad(ref, h, g)
         (dg,) = torch.autograd.grad(got, h, g)
         torch.testing.assert_close(dg, dr, rtol=2e-5, atol=2e-5)
+
+
+@pytest.mark.gpu
+def test_grouped_species_linear_blocks():
+    from xnn_b200.models.mace_fast import species_linear
+    from xnn_b200.ops import node_gemm as NG
+    torch.manual_seed(1)
+    N, n_el, C = 777, 4, 96
+    z = torch.randint(0, n_el, (N,), device="cuda")
+    sizes = [1, 3, 5, 7]
+    Ws = [torch.randn(n_el, C, C, device="cuda") / C ** 0.5 for _ in sizes]
+    h = torch.randn(16, N, C, device="cuda", requires_grad=True)
+    ref = torch.cat([species_linear(b, z, W) for b, W in zip(h.split(sizes, 0), Ws)], 0)
+    got = NG.species_linear_blocks(h, z, Ws, sizes)
+    torch.testing.assert_close(got, ref, rtol=2e-5, atol=2e-5)
+    g = torch.randn_like(ref)
+    torch.testing.assert_close(torch.autograd.grad(got, h, g)[0], torch.autograd.grad(ref, h, g)[0],
+                               rtol=2e-5, atol=2e-5)
+    # the library sort path of large systems gives the same grouping as the kernel
+    zz = torch.randint(0, n_el, (100_000,), device="cuda")
+    p, s = NG.species_sort(zz, n_el)
+    assert torch.equal(zz[p.long()], torch.sort(zz, stable=True).values) and int(s[-1]) == 100_000

@@ -179,9 +179,12 @@ def fast_node_features_energy(model, atomic_numbers: Tensor, edge_index: Tensor,
                  for l, blk_l in enumerate(A.split(degrees, 0))]
         A2 = torch.cat(parts, 0) if P > 1 else parts[0]
         if not blk.residual:
-            outs = [species_linear(blk_l, z, _species_weights(blk.skip_tp, n_el, l), grouped)
-                    for l, blk_l in enumerate(A2.split(degrees, 0))]
-            A2 = torch.cat(outs, 0) if P > 1 else outs[0]
+            Wl = [_species_weights(blk.skip_tp, n_el, l) for l in range(P)]
+            if grouped and NG.grouped_species_ok(A2, Wl[0]):
+                A2 = NG.species_linear_blocks(A2, z, Wl, degrees)       # every degree in one launch
+            else:
+                outs = [species_linear(blk_l, z, Wl[l], grouped) for l, blk_l in enumerate(A2.split(degrees, 0))]
+                A2 = torch.cat(outs, 0) if P > 1 else outs[0]
         sym = prod.symmetric_contractions.contractions[0]
         W = torch.cat(list(sym.weights), dim=1)                         # (n_el, K, C)
         B = K.symmetric_contraction(A2, W, z, lmax, sym.correlation)

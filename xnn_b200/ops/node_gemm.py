@@ -16,7 +16,7 @@ tests compare against.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Dict, List, Optional, Sequence
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 from torch import Tensor
@@ -24,6 +24,8 @@ from torch import Tensor
 from .. import _ext
 
 SPIN_LIMIT = 50_000_000
+#: atoms up to which the one-CTA species sort kernel is used (it serves the training batches)
+SORT_KERNEL_MAX = 65536
 _STATE: Dict[torch.device, Dict[str, Tensor]] = {}
 
 
@@ -176,8 +178,13 @@ def mmT(problems: Sequence[MMT], trace: Optional[Tensor] = None) -> None:
 def species_sort(z: Tensor, n_el: int):
     """``(perm, seg)``: atoms grouped by element index (stable), element ``k`` at
     ``perm[seg[k]:seg[k + 1]]``; int32 on CUDA."""
-    if z.is_cuda and _ext.cuda_available():
+    if z.is_cuda and _ext.cuda_available() and z.numel() <= SORT_KERNEL_MAX:
         return _ext.ops().species_sort(z.contiguous(), int(n_el))
+    if z.is_cuda:                  # large systems: the library's radix sort (the kernel is one CTA)
+        perm = torch.argsort(z, stable=True).to(torch.int32)
+        seg = torch.zeros(n_el + 1, dtype=torch.int32, device=z.device)
+        seg[1:] = torch.cumsum(torch.bincount(z, minlength=n_el), 0).to(torch.int32)
+        return perm, seg
     perm = torch.argsort(z, stable=True)
     counts = torch.bincount(z, minlength=n_el)
     seg = torch.zeros(n_el + 1, dtype=torch.long, device=z.device)
@@ -256,6 +263,68 @@ def grouped_species_ok(h: Tensor, Wz: Tensor) -> bool:
     ok = lambda n: 16 <= n <= 128 and n % 16 == 0
     return (kernels(h) and Wz.dtype == torch.float32 and ok(c_in) and ok(c_out) and h.shape[-1] == c_in
             and not torch.cuda.is_current_stream_capturing())      # it reads the element counts
+
+
+class _SpeciesLinearBlocks(torch.autograd.Function):
+    """``Y = X @ W_l[z]`` for rows of ``lead`` stacked components split into per-degree blocks of
+    ``sizes`` components each (one matrix per element and block); the weights are constants."""
+
+    @staticmethod
+    def forward(ctx, X: Tensor, Ws: Tensor, perm: Tensor, segs: Tensor, counts: Tensor, sizes: Tuple[int, ...]):
+        ctx.save_for_backward(Ws, perm, segs)
+        ctx.counts, ctx.sizes = counts, sizes
+        return _blocks_product(X, Ws, perm, segs, counts, sizes)
+
+    @staticmethod
+    def backward(ctx, g: Tensor):
+        Ws, perm, segs = ctx.saved_tensors
+        dX = _SpeciesLinearBlocks.apply(g.contiguous(), Ws.transpose(-1, -2), perm, segs, ctx.counts, ctx.sizes)
+        return dX, None, None, None, None, None
+
+
+def _blocks_product(X: Tensor, Ws: Tensor, perm: Tensor, segs: Tensor, counts: Tensor, sizes) -> Tensor:
+    """``Ws (blocks, n_el, C_in, C_out)``; element ``k``'s rows are component-major, so block
+    ``b`` of element ``k`` is a contiguous segment of the permuted rows."""
+    nb, n_el = Ws.shape[0], Ws.shape[1]
+    lead = sum(sizes)
+    Y = torch.empty(X.shape[0], Ws.shape[3], dtype=X.dtype, device=X.device)
+    packed = pack([Ws[b, k] for b in range(nb) for k in range(n_el)])
+    # segment bounds of (element, block) on the device: lead * seg[k] + first component * count
+    seg = segs.long() // lead
+    cnt = seg[1:] - seg[:-1]
+    first = [0]
+    for sz in sizes[:-1]:
+        first.append(first[-1] + sz)
+    bounds = []
+    probs = []
+    for b, sz in enumerate(sizes):
+        lo = segs.long()[:-1] + first[b] * cnt
+        hi = lo + sz * cnt
+        bounds.append(torch.stack([lo, hi], 1).to(torch.int32))
+    bounds = torch.stack(bounds, 0).contiguous()                 # (blocks, n_el, 2)
+    for b, sz in enumerate(sizes):
+        for k in range(n_el):
+            rows = sz * int(counts[k + 1] - counts[k])
+            if rows > 0:
+                probs.append(MM(X, Ws[b, k], Y, packed[b * n_el + k], perm=perm, seg=bounds[b, k], rows=rows))
+    mm(probs)
+    return Y
+
+
+def species_linear_blocks(h: Tensor, z: Tensor, Ws: Sequence[Tensor], sizes: Sequence[int]) -> Tensor:
+    """``out[d, i] = h[d, i] @ W_b[z_i]`` for ``h (D, N, C_in)`` whose components ``d`` form blocks
+    of ``sizes`` (e.g. ``1, 3, 5, 7`` per degree) and ``Ws[b] (n_el, C_in, C_out)``: every
+    (element, block) product in one grouped launch. Float32 CUDA, constant weights."""
+    sizes = tuple(int(x) for x in sizes)
+    lead = sum(sizes)
+    assert h.shape[0] == lead, "h must stack the blocks' components along its first dimension"
+    n_el = int(Ws[0].shape[0])
+    perm, segs, counts = _grouped_rows(z, n_el, lead)
+    X = h.reshape(-1, h.shape[-1])
+    X = X if X.is_contiguous() else X.contiguous()
+    W = torch.stack([w.detach() for w in Ws], 0).contiguous()
+    out = _SpeciesLinearBlocks.apply(X, W, perm, segs, counts, sizes)
+    return out.view(*h.shape[:-1], W.shape[-1])
 
 
 def species_linear(h: Tensor, z: Tensor, Wz: Tensor) -> Tensor:
