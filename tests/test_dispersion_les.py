@@ -195,3 +195,34 @@ def test_d4_matches_reference_for_crystals(s9):
     fa, = torch.autograd.grad(a["node_energy"].sum(), pos, retain_graph=True)
     fr, = torch.autograd.grad(r["node_energy"].sum(), pos)
     torch.testing.assert_close(fa, fr, rtol=1e-8, atol=1e-10)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("width", [0.0, 2.0])
+def test_d4_three_body_kernel_matches_formulas(width):
+    """The ATM kernel (energies per atom, forces, C6-factor gradients) against the tensor formulas."""
+    _reference("xnn.common.models.d4")                      # the D4 reference tables
+    from xnn_b200.data import collate
+    from xnn_b200.models.d4 import DFTD4
+    xs = synthetic.triclinic_crystals(2, seed=5, labels=False)
+    cut = 7.0
+    b = collate([structure_to_graph(s, cut) for s in xs]).to("cuda")
+    opts = dict(s9=1.0, cutoff_pair=cut, cutoff_triple=6.0, cutoff_cn=cut, cutoff_eeq_cn=cut,
+                switch_width_triple=width)
+    m = DFTD4(**opts).to("cuda")
+
+    def run(kernels):
+        m.use_kernels = kernels
+        pos = b.pos.clone().requires_grad_(True)
+        vec = pos[b.edge_index[1]] - pos[b.edge_index[0]] + b.cell_shifts.to(pos.dtype).unsqueeze(-1).mul(
+            b.cell[b.batch[b.edge_index[0]]]).sum(1)
+        out = m.evaluate(b.atomic_numbers, pos, b.edge_index, vec, b.batch, 2, b.cell, b.pbc,
+                         torch.zeros(2, device="cuda"))
+        f, = torch.autograd.grad(out["energy_3body"].sum(), pos)
+        return out, f
+
+    a, fa = run(True)
+    r, fr = run(False)
+    torch.testing.assert_close(a["energy_3body"], r["energy_3body"], rtol=1e-11, atol=1e-13)
+    torch.testing.assert_close(a["node_energy"], r["node_energy"], rtol=1e-10, atol=1e-12)
+    torch.testing.assert_close(fa, fr, rtol=1e-9, atol=1e-12)

@@ -11,6 +11,13 @@ cudaError_t d3_two_body_cuda(int64_t n, int64_t E, const int64_t* ptr, const int
                              const D3Params& p, double* cn, double* w, double* dw, double* e_atom, double* dedcn,
                              double* deps_dr, double* g, cudaStream_t s);
 
+cudaError_t atm_cuda(int n, const int64_t* ptr, const int64_t* nbr, const double* vec, const int64_t* z,
+                     const double* fa, const double* fb, const double* c6e, const double* r0, int K, int nz,
+                     double s9, double alp3, double cutoff, double width, const double* go, double* e_atom,
+                     double* g_vec, double* g_c6, cudaStream_t s);
+cudaError_t coulomb_matvec_cuda(int n, const double* pos, const double* rad, const double* v, int nrhs, double* out,
+                                cudaStream_t s);
+
 namespace {
 
 // (e_atom, cn, g, w): per-atom energies (hartree), coordination numbers, the edge gradients
@@ -119,6 +126,61 @@ std::vector<torch::Tensor> d3_two_body_op(torch::Tensor z, torch::Tensor ptr, to
   return {e_atom, cn, g, w};
 }
 
+
+
+// Axilrod-Teller-Muto energies per centre (go undefined) or, with go (per-centre upstream
+// gradients, equal within a structure), the edge gradients [g_vec (E, 3), g_c6 (E)]. Edges grouped by
+// centre through ptr (no permutation); nbr the other atom of each edge; vectors and cutoff in bohr.
+std::vector<torch::Tensor> atm_op(torch::Tensor ptr, torch::Tensor nbr, torch::Tensor vec, torch::Tensor z,
+                                  torch::Tensor fa, torch::Tensor fb, torch::Tensor c6e, torch::Tensor r0, double s9,
+                                  double alp3, double cutoff, double width, c10::optional<torch::Tensor> go) {
+  for (const auto* t : {&ptr, &nbr, &z})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kInt64 && t->is_contiguous(), "atm: int64 CUDA indices");
+  for (const auto* t : {&vec, &fa, &fb, &c6e, &r0})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat64 && t->is_contiguous(), "atm: float64 CUDA arrays");
+  const int64_t n = z.numel(), E = nbr.numel();
+  TORCH_CHECK(ptr.numel() == n + 1 && vec.numel() == 3 * E && c6e.numel() == E && fa.sizes() == fb.sizes() &&
+                  fa.size(0) == n && r0.dim() == 2 && r0.size(0) == r0.size(1), "atm: shapes");
+  c10::cuda::CUDAGuard g(vec.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const bool grad = go.has_value() && go->defined();
+  auto e = torch::zeros({n}, vec.options());
+  torch::Tensor gv, g6;
+  if (grad) {
+    TORCH_CHECK(go->scalar_type() == torch::kFloat64 && go->numel() == n && go->is_contiguous(), "atm: go (n,)");
+    gv = torch::zeros({E, 3}, vec.options());
+    g6 = torch::zeros({E}, vec.options());
+  }
+  cudaError_t err = atm_cuda((int)n, ptr.data_ptr<int64_t>(), nbr.data_ptr<int64_t>(), vec.data_ptr<double>(),
+                             z.data_ptr<int64_t>(), fa.data_ptr<double>(), fb.data_ptr<double>(), c6e.data_ptr<double>(),
+                             r0.data_ptr<double>(), (int)fa.size(1), (int)r0.size(0), s9, alp3, cutoff, width,
+                             grad ? go->data_ptr<double>() : nullptr, e.data_ptr<double>(),
+                             grad ? gv.data_ptr<double>() : nullptr, grad ? g6.data_ptr<double>() : nullptr, st);
+  TORCH_CHECK(err == cudaSuccess, "atm: ", cudaGetErrorString(err));
+  if (grad) return {gv, g6};
+  return {e};
+}
+
+// y = A v for the EEQ Coulomb matrix of a molecule without its diagonal (erf-screened 1 / r,
+// radii a_i): v (n, k), k = 1 or 2; positions in bohr.
+torch::Tensor coulomb_matvec_op(torch::Tensor pos, torch::Tensor rad, torch::Tensor v) {
+  for (const auto* t : {&pos, &rad, &v})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat64 && t->is_contiguous(), "coulomb: float64 CUDA");
+  const int64_t n = rad.numel();
+  TORCH_CHECK(pos.numel() == 3 * n && v.size(0) == n && (v.dim() == 1 || v.size(1) <= 2), "coulomb: shapes");
+  c10::cuda::CUDAGuard g(pos.device());
+  auto out = torch::empty_like(v);
+  const int k = v.dim() == 1 ? 1 : (int)v.size(1);
+  cudaError_t err = coulomb_matvec_cuda((int)n, pos.data_ptr<double>(), rad.data_ptr<double>(), v.data_ptr<double>(), k,
+                                        out.data_ptr<double>(), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(err == cudaSuccess, "coulomb: ", cudaGetErrorString(err));
+  return out;
+}
+
 }  // namespace
 
-void register_d3(pybind11::module& m) { m.def("d3_two_body", &d3_two_body_op); }
+void register_d3(pybind11::module& m) {
+  m.def("d3_two_body", &d3_two_body_op);
+  m.def("atm", &atm_op);
+  m.def("coulomb_matvec", &coulomb_matvec_op);
+}

@@ -25,8 +25,9 @@ import torch
 from torch import Tensor, nn
 
 from ..ops.scatter import scatter_sum, structure_sum
-from .dispersion import (BOHR, HARTREE, DispersionCorrection, evaluate_on_graph, gaussian_reference_weights,
-                         load_tables, options_from_extra, switching_function, three_body_energy)
+from .dispersion import (BOHR, HARTREE, DispersionCorrection, atm_kernel_ok, evaluate_on_graph,
+                         gaussian_reference_weights, load_tables, options_from_extra, switching_function,
+                         three_body_energy, three_body_energy_factored)
 from .registry import register_model
 
 KCN, K4, K5, K6 = 7.5, 4.10451, 19.08857, 2.0 * 11.28174 ** 2
@@ -102,6 +103,8 @@ class DFTD4(nn.Module):
         self.cutoff = max(self.cutoff_pair, self.cutoff_triple, self.cutoff_cn, self.cutoff_eeq_cn)
         self.switch_width_pair, self.switch_width_triple = float(switch_width_pair), float(switch_width_triple)
         self.n_features = 3
+        #: the three-body term on the CUDA kernel (float64 CUDA inputs); False: the tensor formulas
+        self.use_kernels = True
         dt = torch.get_default_dtype()
         for name, v in [("s6", s6), ("s8", s8), ("a1", a1), ("a2", a2), ("s9", s9)]:
             t = torch.tensor(float(v), dtype=dt)
@@ -277,10 +280,16 @@ class DFTD4(nn.Module):
         if bool(self.s9 != 0.0):
             w0 = self.gaussian_weights(z, cn_d4) * self.charge_scaling(z, torch.zeros_like(q))
             a0 = self.dynamic_polarizabilities(z, w0)
-            c6_0 = (3.0 / math.pi) * (a0 * self.cp_weights) @ a0.t()
             m3 = r <= self.cutoff_triple / BOHR
-            e3 = three_body_energy(z, edge_index[:, m3], vec[m3], r[m3], c6_0, self.pair_radius_table(), self.s9,
-                                   self.alp / 3.0, self.cutoff_triple / BOHR, self.switch_width_triple / BOHR, n)
+            if atm_kernel_ok(vec) and self.use_kernels:
+                # C6 factors per atom (no n x n matrix): C6_ij = (3/pi) sum_w cp_w a_i(w) a_j(w)
+                e3 = three_body_energy_factored(z, edge_index[:, m3], vec[m3], (3.0 / math.pi) * a0 * self.cp_weights,
+                                                a0, self.pair_radius_table(), float(self.s9), self.alp / 3.0,
+                                                self.cutoff_triple / BOHR, self.switch_width_triple / BOHR, batch)
+            else:
+                c6_0 = (3.0 / math.pi) * (a0 * self.cp_weights) @ a0.t()
+                e3 = three_body_energy(z, edge_index[:, m3], vec[m3], r[m3], c6_0, self.pair_radius_table(), self.s9,
+                                       self.alp / 3.0, self.cutoff_triple / BOHR, self.switch_width_triple / BOHR, n)
         return {"node_energy": (e2 + e3) * HARTREE,
                 "energy_2body": structure_sum(e2, batch, num_graphs) * HARTREE,
                 "energy_3body": structure_sum(e3, batch, num_graphs) * HARTREE,

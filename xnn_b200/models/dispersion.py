@@ -125,6 +125,61 @@ def three_body_energy(z: Tensor, edge_index: Tensor, edge_vec: Tensor, r: Tensor
     return out
 
 
+def atm_kernel_ok(vec: Tensor) -> bool:
+    """Whether the three-body kernel (``csrc/dispersion.cu``) takes these edges."""
+    if not (vec.is_cuda and vec.dtype == torch.float64):
+        return False
+    from .. import _ext
+    return _ext.cuda_available() and hasattr(_ext.ops(), "atm")
+
+
+class _ATMKernel(torch.autograd.Function):
+    """Per-centre ATM energies from the kernel; the backward pass gives the edge-vector and C6-factor
+    gradients for upstream gradients equal within each structure (a structure's energy)."""
+
+    @staticmethod
+    def forward(ctx, vec, fa, fb, ptr, center, nbr, z, r0, s9, alp3, cutoff, width, batch):
+        from .. import _ext
+        c6e = (fa.index_select(0, center) * fb.index_select(0, nbr)).sum(-1).contiguous()
+        (e,) = _ext.ops().atm(ptr, nbr, vec.contiguous(), z, fa.contiguous(), fb.contiguous(), c6e, r0,
+                              float(s9), float(alp3), float(cutoff), float(width), None)
+        ctx.save_for_backward(vec, fa, fb, ptr, center, nbr, z, r0, c6e, batch)
+        ctx.prm = (float(s9), float(alp3), float(cutoff), float(width))
+        return e
+
+    @staticmethod
+    def backward(ctx, ge):
+        from .. import _ext
+        vec, fa, fb, ptr, center, nbr, z, r0, c6e, batch = ctx.saved_tensors
+        ge = ge.contiguous().to(torch.float64)
+        first = torch.zeros(int(batch.max()) + 1 if batch.numel() else 1, dtype=ge.dtype, device=ge.device)
+        first = first.index_reduce_(0, batch, ge, "amax", include_self=False)
+        if not torch.equal(first.index_select(0, batch), ge):
+            raise NotImplementedError("the three-body kernel differentiates a structure's total energy "
+                                      "(equal upstream gradients for the atoms of a structure)")
+        gv, g6 = _ext.ops().atm(ptr, nbr, vec.contiguous(), z, fa.contiguous(), fb.contiguous(), c6e, r0,
+                                *ctx.prm, ge)
+        g_fa = torch.zeros_like(fa).index_add_(0, center, g6[:, None] * fb.index_select(0, nbr))
+        g_fb = torch.zeros_like(fb).index_add_(0, nbr, g6[:, None] * fa.index_select(0, center))
+        return (gv, g_fa, g_fb) + (None,) * 10
+
+
+def three_body_energy_factored(z: Tensor, edge_index: Tensor, edge_vec: Tensor, fa: Tensor, fb: Tensor,
+                               r0_table: Tensor, s9: float, alp3: float, cutoff: float, width: float,
+                               batch: Tensor) -> Tensor:
+    """:func:`three_body_energy` with ``C6_ij = fa_i . fb_j`` (D4's Casimir-Polder sums) on the
+    kernel: one block per centre walking every pair of its edges (no triplet list in memory)."""
+    n = z.shape[0]
+    src, dst = edge_index
+    order = torch.argsort(dst, stable=True)
+    center, nbr = dst[order].contiguous(), src[order].contiguous()
+    vec = edge_vec.index_select(0, order)
+    ptr = torch.zeros(n + 1, dtype=torch.long, device=z.device)
+    ptr[1:] = torch.cumsum(torch.bincount(dst, minlength=n), 0)
+    return _ATMKernel.apply(vec, fa, fb, ptr, center, nbr, z.contiguous(), r0_table.contiguous(), s9, alp3, cutoff,
+                            width, batch)
+
+
 def evaluate_on_graph(term: nn.Module, data: AtomicGraph) -> Dict[str, Tensor]:
     """Run ``term.evaluate`` on a (batched) graph; adds ``"energy"`` ``(B,)``."""
     b = data.num_graphs
