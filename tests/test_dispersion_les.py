@@ -226,3 +226,30 @@ def test_d4_three_body_kernel_matches_formulas(width):
     torch.testing.assert_close(a["energy_3body"], r["energy_3body"], rtol=1e-11, atol=1e-13)
     torch.testing.assert_close(a["node_energy"], r["node_energy"], rtol=1e-10, atol=1e-12)
     torch.testing.assert_close(fa, fr, rtol=1e-9, atol=1e-12)
+
+
+@pytest.mark.gpu
+def test_d4_matrix_free_eeq_matches_dense():
+    """Matrix-free EEQ (all-pairs product kernel, implicit derivatives) against the dense solve."""
+    _reference("xnn.common.models.d4")
+    from xnn_b200.models.d4 import DFTD4
+    m = DFTD4(s9=0.0).to("cuda")
+    s = synthetic.organic_molecules(1, seed=9, labels=False)[0]
+    z = s["atomic_numbers"].to("cuda")
+    gen = torch.Generator().manual_seed(0)
+    pos0 = (s["pos"].double() / 0.529177210903).to("cuda")
+    cn = torch.rand(z.shape[0], generator=gen, dtype=torch.float64).to("cuda") * 3.0
+    w = torch.randn(z.shape[0], generator=gen, dtype=torch.float64).to("cuda")
+    out = {}
+    for dense_max in (10 ** 9, 0):
+        m.eeq_dense_max = dense_max
+        pos = pos0.clone().requires_grad_(True)
+        c = cn.clone().requires_grad_(True)
+        q = m.eeq_charges(z, pos, c, torch.tensor(0.5, dtype=torch.float64))
+        gp, gc = torch.autograd.grad((q * w).sum(), (pos, c))
+        out[dense_max] = (q.detach(), gp, gc)
+    (qa, pa, ca), (qb, pb, cb) = out[10 ** 9], out[0]
+    torch.testing.assert_close(qb, qa, rtol=1e-9, atol=1e-11)
+    assert abs(float(qb.sum()) - 0.5) < 1e-10
+    torch.testing.assert_close(pb, pa, rtol=1e-8, atol=1e-10)
+    torch.testing.assert_close(cb, ca, rtol=1e-8, atol=1e-10)

@@ -17,6 +17,8 @@ cudaError_t atm_cuda(int n, const int64_t* ptr, const int64_t* nbr, const double
                      double* g_vec, double* g_c6, cudaStream_t s);
 cudaError_t coulomb_matvec_cuda(int n, const double* pos, const double* rad, const double* v, int nrhs, double* out,
                                 cudaStream_t s);
+cudaError_t coulomb_bilinear_grad_cuda(int n, const double* pos, const double* rad, const double* a, const double* b,
+                                       double* out, cudaStream_t s);
 
 namespace {
 
@@ -177,9 +179,25 @@ torch::Tensor coulomb_matvec_op(torch::Tensor pos, torch::Tensor rad, torch::Ten
   return out;
 }
 
+// d/dpos of sum_{i != j} a_i b_j erf(r_ij / sqrt(a_i^2 + a_j^2)) / r_ij, (n, 3)
+torch::Tensor coulomb_bilinear_grad_op(torch::Tensor pos, torch::Tensor rad, torch::Tensor a, torch::Tensor b) {
+  for (const auto* t : {&pos, &rad, &a, &b})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == torch::kFloat64 && t->is_contiguous(), "coulomb: float64 CUDA");
+  const int64_t n = rad.numel();
+  TORCH_CHECK(pos.numel() == 3 * n && a.numel() == n && b.numel() == n, "coulomb: shapes");
+  c10::cuda::CUDAGuard g(pos.device());
+  auto out = torch::empty({n, 3}, pos.options());
+  cudaError_t err = coulomb_bilinear_grad_cuda((int)n, pos.data_ptr<double>(), rad.data_ptr<double>(), a.data_ptr<double>(),
+                                               b.data_ptr<double>(), out.data_ptr<double>(),
+                                               at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(err == cudaSuccess, "coulomb: ", cudaGetErrorString(err));
+  return out;
+}
+
 }  // namespace
 
 void register_d3(pybind11::module& m) {
+  m.def("coulomb_bilinear_grad", &coulomb_bilinear_grad_op);
   m.def("d3_two_body", &d3_two_body_op);
   m.def("atm", &atm_op);
   m.def("coulomb_matvec", &coulomb_matvec_op);

@@ -190,7 +190,72 @@ __global__ void __launch_bounds__(CT) coulomb_matvec_kernel(int n, const double*
   }
 }
 
+// g_i = sum_{j != i} (a_i b_j + a_j b_i) K'(r_ij) (r_i - r_j) / r_ij with K(r) = erf(g r) / r: the
+// position gradient of the bilinear form sum_{i != j} a_i b_j K(r_ij) (implicit differentiation of
+// the EEQ solve).
+__global__ void __launch_bounds__(CT) coulomb_bilinear_grad_kernel(int n, const double* __restrict__ pos,
+                                                                    const double* __restrict__ rad,
+                                                                    const double* __restrict__ a,
+                                                                    const double* __restrict__ b,
+                                                                    double* __restrict__ out) {
+  __shared__ double sp[CT][3];
+  __shared__ double sr[CT];
+  __shared__ double sa[CT], sb[CT];
+  const int i = blockIdx.x * CT + threadIdx.x;
+  double xi = 0, yi = 0, zi = 0, ai2 = 0, ai = 0, bi = 0;
+  if (i < n) {
+    xi = pos[3 * i];
+    yi = pos[3 * i + 1];
+    zi = pos[3 * i + 2];
+    ai2 = rad[i] * rad[i];
+    ai = a[i];
+    bi = b[i];
+  }
+  double gx = 0.0, gy = 0.0, gz = 0.0;
+  const double two_over_sqrt_pi = 1.1283791670955126;
+  for (int t0 = 0; t0 < n; t0 += CT) {
+    const int j = t0 + threadIdx.x;
+    if (j < n) {
+      sp[threadIdx.x][0] = pos[3 * j];
+      sp[threadIdx.x][1] = pos[3 * j + 1];
+      sp[threadIdx.x][2] = pos[3 * j + 2];
+      sr[threadIdx.x] = rad[j];
+      sa[threadIdx.x] = a[j];
+      sb[threadIdx.x] = b[j];
+    }
+    __syncthreads();
+    const int m = min(CT, n - t0);
+    if (i < n) {
+      for (int q = 0; q < m; ++q) {
+        if (t0 + q == i) continue;
+        const double dx = xi - sp[q][0], dy = yi - sp[q][1], dz = zi - sp[q][2];
+        const double r2 = dx * dx + dy * dy + dz * dz;
+        const double r = sqrt(r2);
+        const double g = rsqrt(ai2 + sr[q] * sr[q]);
+        const double dk = (two_over_sqrt_pi * g * exp(-g * g * r2) * r - erf(g * r)) / r2;   // K'(r)
+        const double w = (ai * sb[q] + sa[q] * bi) * dk / r;
+        gx += w * dx;
+        gy += w * dy;
+        gz += w * dz;
+      }
+    }
+    __syncthreads();
+  }
+  if (i < n) {
+    out[3 * i] = gx;
+    out[3 * i + 1] = gy;
+    out[3 * i + 2] = gz;
+  }
+}
+
 }  // namespace
+
+cudaError_t coulomb_bilinear_grad_cuda(int n, const double* pos, const double* rad, const double* a, const double* b,
+                                       double* out, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  coulomb_bilinear_grad_kernel<<<(n + CT - 1) / CT, CT, 0, s>>>(n, pos, rad, a, b, out);
+  return cudaGetLastError();
+}
 
 cudaError_t atm_cuda(int n, const int64_t* ptr, const int64_t* nbr, const double* vec, const int64_t* z,
                      const double* fa, const double* fb, const double* c6e, const double* r0, int K, int nz,

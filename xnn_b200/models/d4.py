@@ -89,6 +89,72 @@ def _zeta(a: float, c, qref, qmod):
     return np.where(qmod < 0.0, np.exp(a), s)
 
 
+def _matrix_free_ok(pos: Tensor) -> bool:
+    if not (pos.is_cuda and pos.dtype == torch.float64):
+        return False
+    from .. import _ext
+    return _ext.cuda_available() and hasattr(_ext.ops(), "coulomb_matvec")
+
+
+def _cg2(apply, rhs: Tensor, diag: Tensor, tol: float, max_iter: int) -> Tensor:
+    """Jacobi-preconditioned conjugate gradients on the columns of ``rhs (n, k)`` together."""
+    x = rhs / diag[:, None]
+    r = rhs - apply(x)
+    z = r / diag[:, None]
+    p = z.clone()
+    rz = (r * z).sum(0)
+    bnorm = rhs.norm(dim=0).clamp_min(1e-300)
+    for _ in range(max_iter):
+        Ap = apply(p)
+        alpha = rz / (p * Ap).sum(0)
+        x = x + alpha * p
+        r = r - alpha * Ap
+        if bool(((r.norm(dim=0) / bnorm) < tol).all()):
+            break
+        z = r / diag[:, None]
+        rz_new = (r * z).sum(0)
+        p = z + (rz_new / rz) * p
+        rz = rz_new
+    return x
+
+
+class _EEQMatrixFree(torch.autograd.Function):
+    """EEQ charges of a molecule from ``A q = x - lambda 1``, ``sum q = Q`` (``A`` the erf-screened
+    Coulomb matrix plus the diagonal hardness) without forming ``A``: the product is the all-pairs
+    kernel ``coulomb_matvec``; the two solves ``A s = x`` and ``A u = 1`` run together and
+    ``q = s - (sum s - Q) / sum u * u``. The backward pass solves the adjoint the same way and
+    differentiates the matrix through ``coulomb_bilinear_grad`` (implicit differentiation)."""
+
+    @staticmethod
+    def forward(ctx, pos, x, rad, diag, Q, tol, max_iter):
+        from .. import _ext
+        C = _ext.ops()
+        posc = pos.detach().contiguous()
+
+        def apply(v):
+            return C.coulomb_matvec(posc, rad, v.contiguous()) + diag[:, None] * v
+        rhs = torch.stack([x.detach(), torch.ones_like(x)], 1)
+        su = _cg2(apply, rhs, diag, tol, max_iter)
+        s, u = su[:, 0], su[:, 1]
+        q = s - ((s.sum() - Q) / u.sum()) * u
+        ctx.save_for_backward(posc, rad, diag, q, u)
+        ctx.tol, ctx.max_iter = tol, max_iter
+        return q
+
+    @staticmethod
+    def backward(ctx, g):
+        from .. import _ext
+        C = _ext.ops()
+        posc, rad, diag, q, u = ctx.saved_tensors
+
+        def apply(v):
+            return C.coulomb_matvec(posc, rad, v.contiguous()) + diag[:, None] * v
+        sg = _cg2(apply, g.contiguous()[:, None], diag, ctx.tol, ctx.max_iter)[:, 0]
+        mu = sg - (sg.sum() / u.sum()) * u                     # the constrained adjoint (sum mu = 0)
+        g_pos = -C.coulomb_bilinear_grad(posc, rad, mu.contiguous(), q.contiguous())
+        return g_pos, mu, None, None, None, None, None
+
+
 class DFTD4(nn.Module):
     def __init__(self, s6: float = 1.0, s8: float = 1.20065498, a1: float = 0.40085597, a2: float = 5.02928789,
                  s9: float = 1.0, alp: float = 16.0, ga: float = 3.0, gc: float = 2.0, wf: float = 6.0,
@@ -105,6 +171,9 @@ class DFTD4(nn.Module):
         self.n_features = 3
         #: the three-body term on the CUDA kernel (float64 CUDA inputs); False: the tensor formulas
         self.use_kernels = True
+        #: molecules with more atoms solve EEQ without forming the matrix (CUDA float64), to this
+        #: relative residual
+        self.eeq_dense_max, self.eeq_tol, self.eeq_max_iter = 2000, 1e-12, 500
         dt = torch.get_default_dtype()
         for name, v in [("s6", s6), ("s8", s8), ("a1", a1), ("a2", a2), ("s9", s9)]:
             t = torch.tensor(float(v), dtype=dt)
@@ -201,8 +270,15 @@ class DFTD4(nn.Module):
                               - 2.0 * alpha / math.sqrt(math.pi))
 
     def eeq_charges(self, z, pos, cn_eeq, total_charge, cell: Optional[Tensor] = None) -> Tensor:
-        """EEQ charges of one structure (positions and cell in bohr); ``cell`` for a periodic one."""
+        """EEQ charges of one structure (positions and cell in bohr); ``cell`` for a periodic one.
+        Molecules above :attr:`eeq_dense_max` atoms on a CUDA float64 device take the matrix-free
+        solve (:class:`_EEQMatrixFree`)."""
         n = pos.shape[0]
+        if cell is None and n > self.eeq_dense_max and _matrix_free_ok(pos):
+            x = -self.eeq_chi[z] + self.eeq_kcnchi[z] * cn_eeq / torch.sqrt(cn_eeq + EEQ_CN_REG)
+            rad = self.eeq_rad[z].contiguous()
+            diag = (self.eeq_eta[z] + math.sqrt(2.0 / math.pi) / self.eeq_rad[z]).contiguous()
+            return _EEQMatrixFree.apply(pos, x, rad, diag, float(total_charge), self.eeq_tol, self.eeq_max_iter)
         if cell is not None:
             A = self.coulomb_matrix_periodic(z, pos, cell)
         else:
