@@ -152,12 +152,12 @@ class LennardJonesChargeHead(nn.Module):
 
 
 class Member(nn.Module):
-    def __init__(self, graph: dict, bonded: dict, nonbonded: dict):
+    def __init__(self, graph: dict, bonded: dict, nonbonded: dict, head=None):
         super().__init__()
         self.graph = MolecularGraphTransformer(**graph)
         nd, ed = self.graph.node_dim, self.graph.edge_dim
         self.bonded = BondedHead(nd, ed, **bonded)
-        self.nonbonded = LennardJonesChargeHead(nd, ed, **nonbonded)
+        self.nonbonded = (head or LennardJonesChargeHead)(nd, ed, **nonbonded)
 
     def forward(self, g: dict) -> Dict[str, Tensor]:
         x, e = self.graph(g["features"], g["edge_features"], g["edge_index"], g["atom_class"], g["edge_class"])
@@ -207,6 +207,10 @@ class ByteFF(InteratomicPotential):
     system, ``(graph index, atom indices)`` (the system's atom order may interleave molecules). Or
     call :meth:`bind` with the system's atomic numbers and bonds."""
 
+    #: the nonbonded head of every member and its default options
+    head = LennardJonesChargeHead
+    nonbonded_defaults = dict(pre=(512, 512, 4), out=(256, 3), tanh_output=20.0)
+
     def __init__(self, graphs: Optional[Sequence[MolecularGraph]] = None, species=None, *, graph: Optional[dict] = None,
                  bonded: Optional[dict] = None, nonbonded: Optional[dict] = None, members: int = 1,
                  supported_elements: Sequence[int] = (1, 6, 7, 8, 9, 15, 16, 17, 35, 53),
@@ -216,9 +220,9 @@ class ByteFF(InteratomicPotential):
         self.graph_options = {**GRAPH_DEFAULTS, **(graph or {})}
         self.bonded_options = {**dict(pre=(256, 256, 3), out=(256, 4), tanh_output=20.0, form="harmonic"),
                                **(bonded or {})}
-        self.nonbonded_options = {**dict(pre=(512, 512, 4), out=(256, 3), tanh_output=20.0), **(nonbonded or {})}
-        self.members = nn.ModuleList(Member(self.graph_options, self.bonded_options, self.nonbonded_options)
-                                     for _ in range(int(members)))
+        self.nonbonded_options = {**self.nonbonded_defaults, **(nonbonded or {})}
+        self.members = nn.ModuleList(Member(self.graph_options, self.bonded_options, self.nonbonded_options,
+                                            self.head) for _ in range(int(members)))
         self.supported_elements = tuple(int(z) for z in supported_elements)
         self.coulomb_constant, self.fudge_qq, self.fudge_lj = float(coulomb_constant), float(fudge_qq), float(fudge_lj)
         self.all_pairs = cutoff is None
