@@ -52,6 +52,7 @@ def parse():
     ap.add_argument("--tn-batch", type=int, default=32, help="config-3 crystals per GPU per step (0: skip)")
     ap.add_argument("--tn-steps", type=int, default=10)
     ap.add_argument("--tn-pool", type=int, default=4)
+    ap.add_argument("--nq-steps", type=int, default=20, help="config-1 NequIP CPU training steps (0: skip)")
     ap.add_argument("--solve-atoms", type=int, default=100_000,
                     help="atoms of the config-5 induction-solve comparison on one GPU (0: skip)")
     return ap.parse_args()
@@ -185,6 +186,46 @@ def tensornet_measure(args, impl, world, rank):
     if hasattr(trainer, "close"):
         trainer.close()
     return out
+
+
+NQ_CONFIG = {"model": {"name": "nequip", "cutoff": 5.0, "n_features": 32, "n_interactions": 3, "n_rbf": 8,
+                       "extra": {"species": [1, 6, 8], "lmax": 2}},
+             "optim": {"lr": 1e-2, "energy_weight": 1.0, "force_weight": 100.0, "epochs": 1, "scheduler": "none"},
+             "data": {"val_fraction": 0.0, "test_fraction": 0.0, "batch_size": 5},
+             "device": "cpu", "seed": 1234}
+
+
+def nequip_cpu_measure(args):
+    """Config 1 on the CPU: NequIP (species H, C, O; l_max 2; 3 layers; 32 channels; 8 Bessel; 5 A)
+    trained on the 250 seeded 21-atom molecules in batches of 5, energy + force MSE (force weight 100),
+    one process (wall clock: no device). Timed: ``--nq-steps`` training steps after warm-up."""
+    import torch
+
+    from xnn_b200.config import from_dict
+    from xnn_b200.data import AtomicDataset, collate, synthetic
+    from xnn_b200.train import Trainer
+    structs = synthetic.small_organic(250, seed=0)
+    cfgd = {k: (dict(v) if isinstance(v, dict) else v) for k, v in NQ_CONFIG.items()}
+    cfgd["output_dir"] = tempfile.mkdtemp(prefix="xnn_b200_bench_nq_")
+    cfgd["trainer"] = {"loggers": [], "cuda_graph": False}
+    ds = AtomicDataset(structs, 5.0, precompute=True)
+    trainer = Trainer(from_dict(cfgd), ds, val=[], test=[])
+    B = 5
+    batches = [collate([ds[k] for k in range(j * B, (j + 1) * B)]) for j in range(len(structs) // B)]
+    for j in range(max(3, args.warmup)):
+        trainer.train_step(batches[j % len(batches)])
+    t0 = time.perf_counter()
+    for j in range(args.nq_steps):
+        trainer.train_step(batches[j % len(batches)])
+    dt = time.perf_counter() - t0
+    if hasattr(trainer, "close"):
+        trainer.close()
+    return {"metric": "NequIP train structures/s (CPU)", "value": round(args.nq_steps * B / dt, 2),
+            "unit": "structures/s", "ms_per_step": round(1e3 * dt / args.nq_steps, 3), "steps": args.nq_steps,
+            "device": "cpu", "threads": torch.get_num_threads(),
+            "config": {"model": "NequIP small: species [1, 6, 8], l_max 2, 3 layers, 32 channels, 8 Bessel, 5.0 A",
+                       "global_batch": B, "data": "synthetic 21-atom molecules (8 H, 9 C, 4 O), Morse labels",
+                       "loss": "energy 1 + forces 100", "dtype": "fp32", "timing": "wall clock"}}
 
 
 def solve_measure(args, impl):
@@ -404,6 +445,9 @@ def reference_arm(args):
                     extra["tensornet"] = tensornet_measure(args, "reference", world, rank)
                 except Exception as exc:  # pragma: no cover
                     extra["tensornet"] = {"unavailable": f"reference TensorNet run failed: {exc!r}"[:300]}
+            if args.nq_steps > 0 and world == 1:
+                extra["nequip_cpu"] = {"unavailable": "the reference NequIP imports e3nn, which is not installed and "
+                                                      "not in the offline wheelhouse"}
             if args.solve_atoms > 0:
                 if world == 1:
                     try:
@@ -564,6 +608,9 @@ def main():
     if args.solve_atoms > 0 and world == 1:
         torch.cuda.empty_cache()
         solve = solve_measure(args, "xnn_b200")
+    nequip = None
+    if args.nq_steps > 0 and world == 1:
+        nequip = nequip_cpu_measure(args)
     if rank == 0:
         line = {
             "metric": "MACE train structures/s", "value": round(value, 2), "unit": "structures/s",
@@ -589,6 +636,7 @@ def main():
             "pme": pme,
             "tensornet": tn,
             "solve": solve,
+            "nequip_cpu": nequip,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
