@@ -7,4 +7,4 @@ MD5-checked downloads that respect ``XNN_B200_OFFLINE``, unit conversion, fixed 
 The same call shapes as the reference hub (``src/xnn/common/data/hub/base.py:20-160``).
 """
 from .base import DatasetBuilder, get_builder, list_datasets, load_dataset, register_dataset  # noqa: F401
-from . import builders, gmtkn55, qm9  # noqa: F401  (registers the builders)
+from . import builders, gmtkn55, more, qm9  # noqa: F401  (registers the builders)
