@@ -128,7 +128,47 @@ def build_ops(case) -> Dict[str, tuple]:
     out["neighbor_list"] = (lambda: build_neighbor_list(pos, rc, cell, pbc, engine="native"),
                             8 * 3 * N + E * (2 * 8 + 3 * 8))
     out.update(pme_ops(N))
+    out.update(dispersion_ops(case))
     return out
+
+
+def dispersion_ops(case) -> Dict[str, tuple]:
+    """The D4 three-body kernel on the water box (triple cutoff 6 A, 23 Casimir-Polder frequencies;
+    the byte figure is the edges' rows once: the kernel is bound by the pair walk, see ``pairs``)
+    and the EEQ Coulomb product of a 20,000-atom molecule (one right-hand side pair)."""
+    pos, cell, pbc = case["pos"], case["cell"], case["pbc"]
+    N = pos.shape[0]
+    n = min(N, 4000)
+    ei, sh = build_neighbor_list(pos[:n], 6.0, cell, pbc, engine="native")
+    order = torch.argsort(ei[1], stable=True)
+    ei, sh = ei[:, order], sh[order]
+    vec = ((pos[ei[0]] - pos[ei[1]] + sh.to(pos.dtype) @ cell) / 0.529177210903).double().contiguous()
+    ptr = torch.zeros(n + 1, dtype=torch.long, device="cuda")
+    ptr[1:] = torch.cumsum(torch.bincount(ei[1], minlength=n), 0)
+    z = torch.where(torch.arange(n, device="cuda") % 3 == 0, 8, 1).long()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    fa = 1.0 + torch.rand(n, 23, device="cuda", dtype=torch.float64, generator=g)
+    fb = fa.clone()
+    c6e = (fa[ei[1]] * fb[ei[0]]).sum(-1).contiguous()
+    r0 = 4.0 + torch.rand(104, 104, device="cuda", dtype=torch.float64, generator=g)
+    r0 = (0.5 * (r0 + r0.t())).contiguous()
+    ops = _ext.ops()
+    go = torch.ones(n, device="cuda", dtype=torch.float64)
+    E = ei.shape[1]
+    deg = torch.bincount(ei[1], minlength=n).double()
+    pairs = float((deg * (deg - 1)).sum())
+    out = {"d4_atm_energy": (lambda: ops.atm(ptr, ei[0].contiguous(), vec, z, fa, fb, c6e, r0, 1.0, 16.0 / 3.0,
+                                             6.0 / 0.529177210903, 0.0, None), 8 * (4 * E + 23 * 2 * n)),
+           "d4_atm_grad": (lambda: ops.atm(ptr, ei[0].contiguous(), vec, z, fa, fb, c6e, r0, 1.0, 16.0 / 3.0,
+                                           6.0 / 0.529177210903, 0.0, go), 8 * (8 * E + 23 * 2 * n))}
+    print(json.dumps({"op": "d4_atm", "atoms": n, "edges": E, "ordered_edge_pairs_per_call": pairs}))
+    m = 20000
+    pm = (torch.rand(m, 3, device="cuda", dtype=torch.float64, generator=g) * 60.0).contiguous()
+    rad = (1.0 + torch.rand(m, device="cuda", dtype=torch.float64, generator=g)).contiguous()
+    v = torch.randn(m, 2, device="cuda", dtype=torch.float64, generator=g).contiguous()
+    out["eeq_coulomb_matvec"] = (lambda: ops.coulomb_matvec(pm, rad, v), 8 * (4 * m + 4 * m))
+    return out
+
 
 
 def pme_ops(n_atoms: int) -> Dict[str, tuple]:
