@@ -294,7 +294,7 @@ class DFTD4(nn.Module):
         ones = torch.ones((n, 1), dtype=pos.dtype, device=pos.device)
         zero = torch.zeros((1, 1), dtype=pos.dtype, device=pos.device)
         full = torch.cat([torch.cat([A, ones], 1), torch.cat([ones.t(), zero], 1)], 0)
-        rhs = torch.cat([x, total_charge.reshape(1).to(pos.dtype)])[:, None]
+        rhs = torch.cat([x, torch.as_tensor(total_charge).reshape(1).to(device=pos.device, dtype=pos.dtype)])[:, None]
         return torch.linalg.solve(full, rhs)[:n, 0]
 
     def gaussian_weights(self, z, cn):
