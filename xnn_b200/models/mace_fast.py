@@ -133,7 +133,8 @@ def _edge_chunks(plan: K.EdgePlan, edge_index: Tensor, max_edges: Optional[int])
     for n0, n1 in bounds:
         e0, e1 = int(ptr[n0]), int(ptr[n1])
         ei = torch.stack([edge_index[0, e0:e1], edge_index[1, e0:e1] - n0])
-        out.append(((e0, e1), (n0, n1), K.EdgePlan.build(ei, n1 - n0, assume_dst_sorted=True, n_src=N)))
+        out.append(((e0, e1), (n0, n1), K.EdgePlan.build(ei, n1 - n0, assume_dst_sorted=True, n_src=N,
+                                                        senders=False)))
     return out
 
 

@@ -116,8 +116,10 @@ class _LeanRadialConv(Function):
             if gY is not None:
                 gY[e0:e1] = gYc
             if want_x and not whole:
+                sub = sub.with_senders()
                 gx += K.conv_sender_sum(N_src, sub.src_ptr, sub.src_perm, gxe)
         if whole:
+            plan = plan.with_senders()
             gx = K.conv_sender_sum(N_src, plan.src_ptr, plan.src_perm, gxe_all)
         return (gx, g_r, gY, None, None, None, None) + (None,) * len(Ws)
 

@@ -56,8 +56,8 @@ class EdgePlan:
     dst: Tensor
     dst_ptr: Tensor
     dst_perm: Optional[Tensor]
-    src_ptr: Tensor
-    src_perm: Tensor
+    src_ptr: Optional[Tensor]
+    src_perm: Optional[Tensor]
     #: number of sender rows when senders and receivers differ (an edge chunk); -1: ``n_nodes``
     n_src: int = -1
 
@@ -77,7 +77,7 @@ class EdgePlan:
 
     @staticmethod
     def build(edge_index: Tensor, n_nodes: int, assume_dst_sorted: Optional[bool] = None,
-              n_src: Optional[int] = None) -> "EdgePlan":
+              n_src: Optional[int] = None, senders: bool = True) -> "EdgePlan":
         src, dst = edge_index[0], edge_index[1]
         E = int(src.shape[0])
         dev = src.device
@@ -90,12 +90,20 @@ class EdgePlan:
             assume_dst_sorted = bool((dst[1:] >= dst[:-1]).all()) if E > 1 else True
         dst_perm = None if assume_dst_sorted else torch.argsort(dst, stable=True)
         ns = n_nodes if n_src is None else int(n_src)
-        scounts = torch.zeros(ns, dtype=torch.int64, device=dev).index_add_(0, src, one)
-        src_ptr = torch.zeros(ns + 1, dtype=torch.int64, device=dev)
-        src_ptr[1:] = torch.cumsum(scounts, 0)
-        src_perm = torch.argsort(src, stable=True)
-        return EdgePlan(n_nodes, E, src.to(torch.int32).contiguous(), dst.to(torch.int32).contiguous(),
-                        src, dst, dst_ptr, dst_perm, src_ptr, src_perm, -1 if n_src is None else ns)
+        plan = EdgePlan(n_nodes, E, src.to(torch.int32).contiguous(), dst.to(torch.int32).contiguous(),
+                        src, dst, dst_ptr, dst_perm, None, None, -1 if n_src is None else ns)
+        return plan.with_senders() if senders else plan
+
+    def with_senders(self) -> "EdgePlan":
+        """The plan with its sender ordering (``src_ptr``, ``src_perm``), formed on first use."""
+        if self.src_ptr is None:
+            ns, dev = self.n_senders, self.src.device
+            one = torch.ones(self.n_edges, dtype=torch.int64, device=dev)
+            scounts = torch.zeros(ns, dtype=torch.int64, device=dev).index_add_(0, self.src, one)
+            self.src_ptr = torch.zeros(ns + 1, dtype=torch.int64, device=dev)
+            self.src_ptr[1:] = torch.cumsum(scounts, 0)
+            self.src_perm = torch.argsort(self.src, stable=True)
+        return self
 
 
 # --------------------------------------------------------------------------- edge geometry
@@ -232,7 +240,7 @@ class _ConvVJP(Function):
         gR, gY, T1, _, _ = K.conv_edge(N, C, P, plan.n_edges, plan.dst_ptr, plan.src32, plan.dst_perm, G,
                                     [Y], [x if nR else None], [True], bool(nR),
                                     [x] if nY else [], [R] if nY else [])
-        gx = K.conv_scatter(plan.n_senders, C, P, plan.src_ptr, plan.src_perm, [R], [T1]) if nx else None
+        gx = K.conv_scatter(plan.n_senders, C, P, plan.with_senders().src_ptr, plan.src_perm, [R], [T1]) if nx else None
         ctx.save_for_backward(G, x, R, Y, T1)
         ctx.plan = plan
         ctx.set_materialize_grads(False)
@@ -285,7 +293,7 @@ class _ConvVJP(Function):
             if T2 is not None:
                 As.append(R); Bs.append(T2)
             if As:
-                cx = K.conv_scatter(plan.n_senders, C, P, plan.src_ptr, plan.src_perm, As, Bs)
+                cx = K.conv_scatter(plan.n_senders, C, P, plan.with_senders().src_ptr, plan.src_perm, As, Bs)
         return cG, cx, cR, cY, None, None
 
 
