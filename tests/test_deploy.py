@@ -166,3 +166,45 @@ def test_mdi_engine_cell_charge_stress_and_stats():
                                ref["stress"][0].detach().numpy(), rtol=1e-7, atol=1e-10)
     np.testing.assert_allclose(np.array(comm.sent[2]).reshape(3, 3) * BOHR, s["cell"].numpy(), rtol=1e-12)
     assert eng.stats()["evaluations"] == 1
+
+
+def test_openmm_ml_potential_on_a_subset(monkeypatch):
+    """MLPotential("xnn_b200") through the factory, with stand-ins for OpenMM's topology and system and
+    for openmm-torch's TorchForce: the force acts on the chosen atoms only."""
+    import sys
+    import types
+
+    from xnn_b200.deploy.openmm_ml import XNNPotentialImplFactory
+
+    class _TorchForce:
+        def __init__(self, module):
+            self.module, self.group, self.periodic = module, None, None
+
+        def setForceGroup(self, g):
+            self.group = g
+
+        def setUsesPeriodicBoundaryConditions(self, p):
+            self.periodic = p
+
+    monkeypatch.setitem(sys.modules, "openmmtorch", types.SimpleNamespace(TorchForce=_TorchForce))
+    mol = synthetic.organic_molecules(1, seed=9, labels=False)[0]
+    z = mol["atomic_numbers"].tolist()
+    water = [8, 1, 1]
+    Atom = types.SimpleNamespace
+    atoms = [Atom(element=Atom(atomic_number=int(a))) for a in water + z]
+    topology = types.SimpleNamespace(atoms=lambda: iter(atoms), getPeriodicBoxVectors=lambda: None)
+    system = types.SimpleNamespace(forces=[])
+    system.addForce = system.forces.append
+    m = _model()
+    with pytest.raises(ValueError):
+        XNNPotentialImplFactory().createImpl("xnn_b200")
+    impl = XNNPotentialImplFactory().createImpl("xnn_b200", model=m)
+    sub = list(range(3, 3 + len(z)))
+    impl.addForces(topology, system, sub, 2)
+    (force,) = system.forces
+    assert force.group == 2 and force.periodic is False
+    pos = torch.cat([torch.zeros(3, 3), mol["pos"]], 0) / 10.0
+    e_kj = force.module(pos)
+    m.set_use_fast(False)
+    e_ref = ForceStressOutput(m)(structure_to_graph(mol, 4.5))["energy"]
+    torch.testing.assert_close(e_kj / 96.48533212331002, e_ref.reshape(()), rtol=1e-10, atol=1e-10)

@@ -137,8 +137,22 @@ class OpenMMForce(nn.Module):
         return self.core(self.atomic_numbers, edge_index, vec).sum() * self.ev_to_kj
 
 
-def openmm_force(model: nn.Module, atomic_numbers, periodic: bool = False) -> torch.jit.ScriptModule:
-    """The scripted OpenMM force module (save it with ``torch.jit.save`` for ``TorchForce``)."""
+class OpenMMSubsetForce(nn.Module):
+    """An :class:`OpenMMForce` on the ``atoms`` of a larger OpenMM system (ML/MM): the model sees
+    those atoms' positions only; every other particle gets no force from it."""
+
+    def __init__(self, inner: nn.Module, atoms: Tensor):
+        super().__init__()
+        self.inner = inner
+        self.register_buffer("atoms", atoms.clone())
+
+    def forward(self, positions: Tensor, boxvectors: Optional[Tensor] = None) -> Tensor:
+        return self.inner(positions.index_select(0, self.atoms), boxvectors)
+
+
+def openmm_force(model: nn.Module, atomic_numbers, periodic: bool = False, atoms=None) -> torch.jit.ScriptModule:
+    """The scripted OpenMM force module (save it with ``torch.jit.save`` for ``TorchForce``); with
+    ``atoms`` (indices into the OpenMM system) it acts on that subset of a larger system."""
     core_model = _core_model(model)
     deactivate_fast_paths(core_model)
     dtype = next((p.dtype for p in core_model.parameters() if p.is_floating_point()), torch.get_default_dtype())
@@ -147,4 +161,10 @@ def openmm_force(model: nn.Module, atomic_numbers, periodic: bool = False) -> to
         traced = torch.jit.trace(_EnergyCore(core_model).eval(), _example(core_model, dtype, device),
                                  check_trace=False)
     z = torch.as_tensor(atomic_numbers, dtype=torch.long, device=device)
-    return torch.jit.script(OpenMMForce(traced, z, float(core_model.cutoff), periodic).eval())
+    inner = OpenMMForce(traced, z, float(core_model.cutoff), periodic).eval()
+    if atoms is not None:
+        idx = torch.as_tensor(list(atoms), dtype=torch.long, device=device)
+        if idx.numel() != z.numel():
+            raise ValueError(f"{idx.numel()} atoms for {z.numel()} atomic numbers")
+        return torch.jit.script(OpenMMSubsetForce(inner, idx).eval())
+    return torch.jit.script(inner)
