@@ -149,3 +149,15 @@ def test_periodic_box_on_gpu_matches_cpu():
         assert float(out_g[k].sum()) == pytest.approx(float(out_c[k].sum()), abs=1e-7), k
     f = -torch.autograd.grad(out_g["energy"].sum(), g2.pos)[0]
     assert torch.isfinite(f).all()
+
+
+def test_tinker_inputs_round_trip(tmp_path):
+    from xnn_b200.ffnn.amoeba_params import read_tinker_xyz, parse_prm
+    m = Amoeba.water(2)
+    xyz, key, prm = m.write_tinker_inputs(tmp_path, DIMER, cell=[[12.0, 0, 0], [0, 12.0, 0], [0, 0, 12.0]])
+    pos, types, bonds, syms, cell = read_tinker_xyz(xyz)
+    assert types == [1, 2, 2, 1, 2, 2] and syms == ["O", "H", "H", "O", "H", "H"]
+    assert bonds == [(0, 1), (0, 2), (3, 4), (3, 5)]
+    assert abs(pos - torch.tensor(DIMER).numpy()).max() < 1e-6 and abs(cell - 12.0 * torch.eye(3).numpy()).max() < 1e-6
+    assert "parameters  system.prm" in key.read_text() and "ewald" in key.read_text()
+    assert parse_prm(prm.read_text()).bonds == m.params.bonds

@@ -750,6 +750,27 @@ class Amoeba(FixedTopologyPotential):
         out.update(terms)
         return out
 
+    def write_tinker_inputs(self, directory, positions, cell=None, name: str = "system"):
+        """Tinker inputs of this system: ``<name>.xyz`` (coordinates, types, connectivity),
+        ``<name>.key`` and the parameter file ``<name>.prm`` (for the built-in water model its
+        Tinker text); returns the three paths."""
+        from pathlib import Path
+
+        from ..data.elements import SYMBOLS
+        from .amoeba_params import write_tinker_key, write_tinker_xyz
+        d = Path(directory)
+        d.mkdir(parents=True, exist_ok=True)
+        syms = [SYMBOLS[int(z)] for z in self.top_z.tolist()]
+        xyz = write_tinker_xyz(d / f"{name}.xyz", positions, self.top_type.tolist(), self.topology.bonds, syms,
+                               cell=cell)
+        prm = d / f"{name}.prm"
+        if self.params.source_text:
+            prm.write_text(self.params.source_text)
+        else:
+            raise ValueError("the parameter set has no Tinker text to write (read it from a .prm file)")
+        key = write_tinker_key(d / f"{name}.key", prm.name, cell=cell, cutoff=self.cutoff, polar_eps=self.polar_eps)
+        return xyz, key, prm
+
     @property
     def masses(self) -> Tensor:
         return torch.tensor([self.params.types[int(t)][3] for t in self.top_type.tolist()], dtype=torch.float64)

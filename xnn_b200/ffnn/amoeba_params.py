@@ -66,6 +66,8 @@ class AmoebaParameters:
     polarize: Dict[int, Tuple[float, float, Tuple[int, ...]]] = field(default_factory=dict)
     scalars: Dict[str, object] = field(default_factory=dict)
     unsupported: List[str] = field(default_factory=list)
+    #: the Tinker text the set was read from (written back by the Tinker input writer)
+    source_text: Optional[str] = None
 
     # ------------------------------------------------------------------ scalar access
     def get(self, key: str, default):
@@ -214,7 +216,10 @@ def parse_prm(text: str, name: str = "amoeba") -> AmoebaParameters:
 
 def read_prm(path: Union[str, Path]) -> AmoebaParameters:
     path = Path(path)
-    return parse_prm(path.read_text(), name=path.stem)
+    text = path.read_text()
+    p = parse_prm(text, name=path.stem)
+    p.source_text = text
+    return p
 
 
 #: AMOEBA water (Ren and Ponder 2003, Table 1): Tinker types 1 (O) and 2 (H)
@@ -288,7 +293,9 @@ polarize      2          0.496     0.390     1
 
 
 def amoeba_water_2003() -> AmoebaParameters:
-    return parse_prm(AMOEBA_WATER_2003_PRM, name="amoeba-water-2003")
+    p = parse_prm(AMOEBA_WATER_2003_PRM, name="amoeba-water-2003")
+    p.source_text = AMOEBA_WATER_2003_PRM
+    return p
 
 
 def load_parameters(source) -> AmoebaParameters:
@@ -298,3 +305,82 @@ def load_parameters(source) -> AmoebaParameters:
     if isinstance(source, str) and source.lower() in ("amoeba-water-2003", "water03", "amoeba_water_2003"):
         return amoeba_water_2003()
     return read_prm(source)
+
+
+# ----------------------------------------------------------------------------- Tinker inputs
+def write_tinker_xyz(path: Union[str, Path], positions, types, bonds, symbols, title: str = "xnn_b200",
+                     cell=None) -> Path:
+    """A Tinker ``.xyz`` file: atom count and title, the box (lengths and angles) when ``cell`` is
+    given, then per atom its index, symbol, position (A), Tinker type and bonded neighbours
+    (1-based)."""
+    import math as _m
+
+    import numpy as np
+    pos = np.asarray(positions, dtype=float)
+    n = pos.shape[0]
+    nbr = [[] for _ in range(n)]
+    for i, j in bonds:
+        nbr[int(i)].append(int(j) + 1)
+        nbr[int(j)].append(int(i) + 1)
+    lines = [f"{n:6d}  {title}"]
+    if cell is not None:
+        c = np.asarray(cell, dtype=float)
+        a, b, cc = (float(np.linalg.norm(v)) for v in c)
+        ang = lambda u, v: _m.degrees(_m.acos(float(np.dot(u, v)) / (np.linalg.norm(u) * np.linalg.norm(v))))  # noqa
+        lines.append(f"{a:12.6f}{b:12.6f}{cc:12.6f}{ang(c[1], c[2]):12.6f}{ang(c[0], c[2]):12.6f}{ang(c[0], c[1]):12.6f}")
+    for k in range(n):
+        conn = "".join(f"{x:6d}" for x in sorted(nbr[k]))
+        lines.append(f"{k + 1:6d}  {symbols[k]:<3s}{pos[k, 0]:12.6f}{pos[k, 1]:12.6f}{pos[k, 2]:12.6f}"
+                     f"{int(types[k]):6d}{conn}")
+    p = Path(path)
+    p.write_text("\n".join(lines) + "\n")
+    return p
+
+
+def read_tinker_xyz(path: Union[str, Path]):
+    """``(positions (n, 3), types, bonds, symbols, cell or None)`` of a Tinker ``.xyz`` file."""
+    import math as _m
+
+    import numpy as np
+    lines = [ln for ln in Path(path).read_text().splitlines()]
+    n = int(lines[0].split()[0])
+    body = lines[1:]
+    cell = None
+    first = body[0].split()
+    if len(first) == 6 and all(_is_float(x) for x in first):
+        a, b, c, al, be, ga = (float(x) for x in first)
+        al, be, ga = (_m.radians(x) for x in (al, be, ga))
+        cx = _m.cos(be)
+        cy = (_m.cos(al) - _m.cos(be) * _m.cos(ga)) / _m.sin(ga)
+        cell = np.array([[a, 0, 0], [b * _m.cos(ga), b * _m.sin(ga), 0],
+                         [c * cx, c * cy, c * _m.sqrt(max(0.0, 1 - cx * cx - cy * cy))]])
+        body = body[1:]
+    pos, types, syms, bonds = np.zeros((n, 3)), [], [], set()
+    for k in range(n):
+        f = body[k].split()
+        syms.append(f[1])
+        pos[k] = [float(x) for x in f[2:5]]
+        types.append(int(f[5]))
+        for j in f[6:]:
+            a, b = k, int(j) - 1
+            bonds.add((min(a, b), max(a, b)))
+    return pos, types, sorted(bonds), syms, cell
+
+
+def _is_float(x: str) -> bool:
+    try:
+        float(x)
+        return True
+    except ValueError:
+        return False
+
+
+def write_tinker_key(path: Union[str, Path], prm_name: str, cell=None, cutoff: float = 9.0,
+                     ewald_cutoff: float = 7.0, polar_eps: float = 1e-8) -> Path:
+    """A Tinker ``.key`` file naming the parameter file; Ewald and cutoffs for a periodic box."""
+    lines = [f"parameters  {prm_name}", "verbose", f"polar-eps  {polar_eps:g}"]
+    if cell is not None:
+        lines += ["ewald", f"ewald-cutoff  {ewald_cutoff:g}", f"vdw-cutoff  {cutoff:g}", "neighbor-list"]
+    p = Path(path)
+    p.write_text("\n".join(lines) + "\n")
+    return p
