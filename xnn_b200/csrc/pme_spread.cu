@@ -177,7 +177,9 @@ __global__ void __launch_bounds__(256) pme_spread_kernel(int64_t n, const double
 }
 
 // Gather (the spreading's adjoint): same layout, then a fixed-order warp reduction of the six sums.
-template <int P, int ND>
+// POS = false: the field only (no position derivatives; the induction solve's gather), which
+// drops the multipole-derivative sums and their registers at compile time.
+template <int P, int ND, bool POS = true>
 __global__ void __launch_bounds__(256) pme_gather_kernel(int64_t n, const double* __restrict__ pos,
                                                          const double* __restrict__ G, int K1, int K2, int K3, int z0,
                                                          int nz, const double* __restrict__ q,
@@ -221,7 +223,7 @@ __global__ void __launch_bounds__(256) pme_gather_kernel(int64_t n, const double
       P1[0] += f * W(1, 0, 0);
       P1[1] += f * W(0, 1, 0);
       P1[2] += f * W(0, 0, 1);
-      if (gpos) {
+      if (POS && gpos) {
 #pragma unroll
         for (int a = 0; a < 3; ++a) {
           const int o0 = a == 0, o1 = a == 1, o2 = a == 2;
@@ -248,14 +250,14 @@ __global__ void __launch_bounds__(256) pme_gather_kernel(int64_t n, const double
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       P1[a] += __shfl_xor_sync(0xffffffffu, P1[a], off);
-      Fu[a] += __shfl_xor_sync(0xffffffffu, Fu[a], off);
+      if (POS) Fu[a] += __shfl_xor_sync(0xffffffffu, Fu[a], off);
     }
   }
   if (lane != 0) return;
   // back to Cartesian: dE/dr_b = sum_a G[b][a] dE/du_a
   for (int b = 0; b < 3; ++b) {
     if (gd) gd[3 * i + b] = G[b * 3 + 0] * P1[0] + G[b * 3 + 1] * P1[1] + G[b * 3 + 2] * P1[2];
-    if (gpos) gpos[3 * i + b] = G[b * 3 + 0] * Fu[0] + G[b * 3 + 1] * Fu[1] + G[b * 3 + 2] * Fu[2];
+    if (POS && gpos) gpos[3 * i + b] = G[b * 3 + 0] * Fu[0] + G[b * 3 + 1] * Fu[1] + G[b * 3 + 2] * Fu[2];
   }
 }
 
@@ -280,8 +282,10 @@ cudaError_t gather_p(int64_t n, const double* pos, const double* G, int K1, int 
     pme_gather_kernel<P, 3><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd, gpos);
   else if (gpos && d)
     pme_gather_kernel<P, 2><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd, gpos);
-  else
+  else if (gpos)
     pme_gather_kernel<P, 1><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd, gpos);
+  else
+    pme_gather_kernel<P, 1, false><<<blocks, 256, 0, s>>>(n, pos, G, K1, K2, K3, z0, nz, q, d, Q, phi, gd, gpos);
   return cudaGetLastError();
 }
 
