@@ -169,8 +169,9 @@ class NDDO(InteratomicPotential):
     def core_core(self, za: Tensor, zb: Tensor, r: Tensor, gab: Tensor, tore_a: Tensor, tore_b: Tensor) -> Tensor:
         raise NotImplementedError
 
-    def corrections(self, z: Tensor, pos: Tensor, batch: Tensor) -> Tensor:
-        """Per-atom post-SCF corrections (kcal/mol)."""
+    def corrections(self, z: Tensor, pos: Tensor, batch: Tensor,
+                    pairs: Optional[Tuple[Tensor, Tensor]] = None) -> Tensor:
+        """Per-atom post-SCF corrections (kcal/mol); ``pairs`` are the atom pairs ``i < j`` of each structure."""
         return pos.new_zeros(z.shape[0])
 
     def parameter_set(self) -> NDDOParameters:
@@ -397,7 +398,7 @@ class NDDO(InteratomicPotential):
         e_atom = w * ((PA * (H_atom[None] + 0.5 * G_atom)).sum((-1, -2))).sum(0)
         e_pair = w * 2.0 * ((PAB * (H_pair[None] + 0.5 * G_pair)).sum((-1, -2))).sum(0)
         e_atom = e_atom.index_add(0, lay.pa, 0.5 * (e_pair + e_core)).index_add(0, lay.pb, 0.5 * (e_pair + e_core))
-        corr = self.corrections(z, pos64, batch)
+        corr = self.corrections(z, pos64, batch, (lay.pa, lay.pb))
         node_kcal = (e_atom - el["eisol"][sp]) * I.EV_TO_KCAL + self.atom_heat.to(pos.device)[z] + corr
         hof = torch.zeros(n_struct, dtype=dt, device=pos.device).index_add(0, batch, node_kcal)
         zeros = torch.zeros(n_struct, dtype=dt, device=pos.device)
@@ -461,28 +462,41 @@ def _sin2_dihedral(p: Tensor, i: int, j: int, k: int, l: int) -> Tensor:
     return 1.0 - c * c
 
 
-def amide_torsions(z: Tensor, pos: Tensor, barrier: float, batch: Optional[Tensor] = None) -> Tensor:
+def amide_torsions(z: Tensor, pos: Tensor, barrier: float, batch: Optional[Tensor] = None,
+                   pairs: Optional[Tuple[Tensor, Tensor]] = None) -> Tensor:
     """Per-atom amide torsion barrier (kcal/mol) on the nitrogen of each H-N-C=O group.
 
     A carbon with an oxygen within 1.3 A, a nitrogen within 1.6 A that has a hydrogen within 1.3 A and a
     further neighbour X within 1.7 A (neither the carbon nor that hydrogen) adds ``barrier`` times
     ``sin^2`` of the torsions O=C-N-X and O=C-N-H; each nitrogen counts once and, per carbon, the first
-    match in atom order is taken (reference ``sqmnn/models/corrections.py:368-414``)."""
+    match in atom order is taken (reference ``sqmnn/models/corrections.py:368-414``). The search runs on
+    the host over the neighbour lists within 1.7 A of the atom pairs of each structure (``pairs``, all
+    pairs ``i < j`` of a structure; built from ``batch`` when not given)."""
     out = pos.new_zeros(z.shape[0])
-    if barrier == 0.0:
+    if barrier == 0.0 or z.shape[0] < 4:
         return out
+    if pairs is None:
+        b = batch if batch is not None else torch.zeros_like(z)
+        counts = torch.zeros(int(b.max()) + 1, dtype=torch.long, device=z.device).index_add_(0, b, torch.ones_like(b))
+        pairs = _pairs_within(b, torch.cat([counts.new_zeros(1), torch.cumsum(counts, 0)]))
+    pa, pb = pairs
+    r = (pos.detach()[pb] - pos.detach()[pa]).norm(dim=-1)
+    near = r <= 1.7
     zl = z.tolist()
-    d = torch.cdist(pos.detach(), pos.detach())
-    if batch is not None:
-        d = torch.where(batch[:, None] == batch[None, :], d, torch.full_like(d, float("inf")))
-    d = d.cpu().numpy()
+    ia, ib, rr = pa[near].tolist(), pb[near].tolist(), r[near].tolist()
+    nbrs: Dict[int, List[Tuple[int, float]]] = {}
+    for a, b, d in zip(ia, ib, rr):
+        nbrs.setdefault(a, []).append((b, d))
+        nbrs.setdefault(b, []).append((a, d))
+    for v in nbrs.values():
+        v.sort()
     used = set()
-    for c in (i for i, v in enumerate(zl) if v == 6):
+    for c in sorted(a for a in nbrs if zl[a] == 6):
         hit = None
-        for o in (i for i, v in enumerate(zl) if v == 8 and d[i, c] <= 1.3):
-            for n in (i for i, v in enumerate(zl) if v == 7 and d[i, c] <= 1.6):
-                for h in (i for i, v in enumerate(zl) if v == 1 and d[n, i] <= 1.3):
-                    xs = [x for x in range(len(zl)) if x not in (n, h, c) and d[x, n] <= 1.7]
+        for o in (a for a, d in nbrs[c] if zl[a] == 8 and d <= 1.3):
+            for n in (a for a, d in nbrs[c] if zl[a] == 7 and d <= 1.6):
+                for h in (a for a, d in nbrs.get(n, []) if zl[a] == 1 and d <= 1.3):
+                    xs = [a for a, d in nbrs[n] if a not in (h, c)]
                     if xs and n not in used:
                         hit = (o, n, h, xs[0])
                         break
@@ -530,5 +544,5 @@ class PM3(NDDO):
                                             torch.zeros_like(r))
         return e + gauss
 
-    def corrections(self, z, pos, batch):
-        return amide_torsions(z, pos, self.peptide_barrier, batch)
+    def corrections(self, z, pos, batch, pairs=None):
+        return amide_torsions(z, pos, self.peptide_barrier, batch, pairs)
