@@ -80,19 +80,39 @@ __global__ void __launch_bounds__(512) p2p_allreduce_kernel(P2PArgs a) {
   long long hi = lo + a.chunk;
   const long long shard_end = (long long)(rank + 1) * a.shard;
   if (hi > shard_end) hi = shard_end;
-  for (long long i = lo + 4 * (long long)threadIdx.x; i < hi; i += 4 * (long long)blockDim.x) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  // four float4 positions per thread and step, every peer's loads issued before the sums: world x 4
+  // independent 16-byte remote loads in flight per thread (the links need megabytes in flight to fill)
+  const long long stride = 4LL * blockDim.x;
+  for (long long i0 = lo + 4LL * threadIdx.x; i0 < hi; i0 += 4 * stride) {
+    float4 acc[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int p = 0; p < XNN_MAX_RANKS; ++p) {
       if (p < a.world) {
-        const float4 v = __ldcv(reinterpret_cast<const float4*>(a.bufs[p] + i));  // no stale cache lines
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const long long i = i0 + u * stride;   // chunks are multiples of 4 floats: i < hi covers i + 3
+          if (i < hi) {
+            const float4 v = __ldcv(reinterpret_cast<const float4*>(a.bufs[p] + i));  // no stale cache lines
+            acc[u].x += v.x; acc[u].y += v.y; acc[u].z += v.z; acc[u].w += v.w;
+          }
+        }
       }
     }
-    acc.x *= a.scale; acc.y *= a.scale; acc.z *= a.scale; acc.w *= a.scale;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      acc[u].x *= a.scale; acc[u].y *= a.scale; acc[u].z *= a.scale; acc[u].w *= a.scale;
+    }
 #pragma unroll
     for (int p = 0; p < XNN_MAX_RANKS; ++p) {
-      if (p < a.world) *reinterpret_cast<float4*>(a.bufs[p] + i) = acc;
+      if (p < a.world) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const long long i = i0 + u * stride;
+          if (i < hi) *reinterpret_cast<float4*>(a.bufs[p] + i) = acc[u];
+        }
+      }
     }
   }
   if (!cta_exchange(a, rank, 1, epoch)) return;

@@ -90,7 +90,7 @@ class P2PAllReduce:
         self.status_host, addr = C.mapped_status(1)
         self.status_addr = int(addr.item())
         shard = numel // self.world
-        self.nblocks = nblocks or max(1, min(32, (shard + 4095) // 4096))
+        self.nblocks = nblocks or max(1, min(64, (shard + 4095) // 4096))
         self.spin_limit = int(spin_limit)
 
     def all_reduce_mean_(self, flat: Optional[torch.Tensor] = None, offset: int = 0,
